@@ -1,0 +1,506 @@
+"""Benchmark: selected-KV decode layer-steps/s at N=32K.
+
+One step = one Gradient-Llama-3-8B-shaped decode step over 32 layers at
+N=32768 visible tokens: per layer Q F16 [32,128] (+ its F32 copy for the
+attention), K/V F16 [32768,8,128] ~ N(0,1) with 2% heavy-hitter K rows x4 and
+K RoPE-rotated (theta 500000) by token position; layers 0-1 dense attention,
+layers 2-31 score -> select (alpha, 20% cap) -> gather -> attention.  Inputs
+are seeded synthetic data resident in HBM (4.3 GB, far larger than the 126 MB
+L2, so no flush is needed between steps).  The 32-layer step is captured once
+as a CUDA graph of C-ABI calls and replayed.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 (torchrun, one process per GPU): each rank decodes its own independent
+sequence (weak scaling, no collective on the data path); the step time is the
+max over ranks.  --impl reference times the reference HillServe CPU path
+(oracle/_ref, built from the reference sources) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+LAYERS, DENSE, N, HEADS = 32, 2, 32768, 32
+THETA = 500000.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--alpha", type=float, default=0.1)
+    ap.add_argument("--tokens", type=int, default=N)
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+
+    def summary(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        rows = [r.split(",") for r in Path(self.file.name).read_text().strip().splitlines() if r.strip()]
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for name, val in zip(names, r[5:9]):
+                    if val.strip().lower() == "active":
+                        reasons.add(name)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- our arm
+class Model:
+    """Per-layer HBM-resident inputs and the selected-KV step."""
+
+    def __init__(self, hsb, torch, tokens, layers, alpha, seed):
+        self.hsb, self.torch = hsb, torch
+        self.n, self.layers, self.alpha = tokens, layers, alpha
+        dev = torch.device("cuda")
+        lib = hsb._capi.lib()
+        s = torch.cuda.current_stream().cuda_stream
+        self.q16 = torch.empty((layers, 4096), dtype=torch.int16, device=dev)
+        self.q32 = torch.empty((layers, 4096), dtype=torch.float32, device=dev)
+        self.kc = torch.empty((layers, tokens * 1024), dtype=torch.int16, device=dev)
+        self.vc = torch.empty((layers, tokens * 1024), dtype=torch.int16, device=dev)
+        for l in range(layers):
+            ls = seed * 1000 + l
+            lib.hsb_synth_normal_f16(self.q16[l].data_ptr(), 4096, ls * 7 + 1, 1.0, s)
+            lib.hsb_synth_keys(self.kc[l].data_ptr(), tokens, 1024, ls * 7 + 2, 0.02, 4.0, 1, THETA, s)
+            lib.hsb_synth_keys(self.vc[l].data_ptr(), tokens, 1024, ls * 7 + 3, 0.0, 1.0, 0, THETA, s)
+        self.q32.copy_(self.q16.view(torch.float16).float())
+        self.count = hsb.select_kmax(tokens, 0.2)
+        self.scores = torch.empty((HEADS, tokens), dtype=torch.int16, device=dev)
+        self.ids = torch.empty((layers, HEADS, self.count), dtype=torch.int32, device=dev)
+        self.counts = torch.zeros((layers, HEADS), dtype=torch.int32, device=dev)
+        self.results = torch.zeros((layers, 4), dtype=torch.int32, device=dev)
+        self.kp = torch.empty(self.count * 4096, dtype=torch.int16, device=dev)
+        self.vp = torch.empty(self.count * 4096, dtype=torch.int16, device=dev)
+        self.out = torch.zeros((layers, HEADS, 128), dtype=torch.float32, device=dev)
+        self.ws_sel = hsb._workspace(lib.hsb_select_workspace_bytes(HEADS, tokens, tokens, self.count), dev)
+        self.ws_att = hsb._workspace(lib.hsb_attention_workspace_bytes(self.count), dev)
+        self.ws_dense = hsb._workspace(lib.hsb_attention_dense_workspace_bytes(tokens), dev)
+        nsparse = layers - DENSE
+        mk = lambda: torch.cuda.Event(enable_timing=True, external=True)  # noqa: E731
+        self.ev = [[mk() for _ in range(5)] for _ in range(nsparse)]
+        self.ev_dense = [[mk() for _ in range(2)] for _ in range(DENSE)]
+        self.lib = lib
+
+    def step(self, stream):
+        lib, P = self.lib, self.hsb._ptr
+        s = stream.cuda_stream
+        n = self.n
+        for l in range(self.layers):
+            if l < DENSE:
+                e = self.ev_dense[l]
+                e[0].record(stream)
+                rc = lib.hsb_attention_dense(P(self.q32[l]), P(self.kc[l]), P(self.vc[l]), n, 1024, P(self.out[l]),
+                                             P(self.ws_dense), self.ws_dense.numel(), s)
+                e[1].record(stream)
+                assert rc == 0, lib.hsb_last_error()
+                continue
+            e = self.ev[l - DENSE]
+            res = self.results[l]
+            e[0].record(stream)
+            rc = lib.hsb_score_v3(P(self.q16[l]), P(self.kc[l]), n, 1024, P(self.scores), s)
+            e[1].record(stream)
+            rc |= lib.hsb_select(P(self.scores), 1, HEADS, n, n, self.alpha, 0.2, 0, P(self.ids[l]), self.count,
+                                 P(self.counts[l]), P(res), P(self.ws_sel), self.ws_sel.numel(), s)
+            e[2].record(stream)
+            rc |= lib.hsb_gather_cache(P(self.ids[l]), self.count, P(res), 0, P(self.kc[l]), P(self.vc[l]), 1024, n,
+                                       self.count, 0, P(self.kp), P(self.vp), P(res[2:]), s)
+            e[3].record(stream)
+            rc |= lib.hsb_attention_packed(P(self.q32[l]), P(self.kp), P(self.vp), self.count, None, 0, P(res), 0,
+                                           P(self.out[l]), P(self.ws_att), self.ws_att.numel(), s)
+            e[4].record(stream)
+            assert rc == 0, lib.hsb_last_error()
+
+    def stage_ms(self):
+        """Per-stage durations (ms) of the last replay, averaged over layers."""
+        sc, se, ga, at, dn = [], [], [], [], []
+        for e in self.ev:
+            sc.append(e[0].elapsed_time(e[1]))
+            se.append(e[1].elapsed_time(e[2]))
+            ga.append(e[2].elapsed_time(e[3]))
+            at.append(e[3].elapsed_time(e[4]))
+        for e in self.ev_dense:
+            dn.append(e[0].elapsed_time(e[1]))
+        return {"score": float(np.mean(sc)), "select": float(np.mean(se)), "gather": float(np.mean(ga)),
+                "attention": float(np.mean(at)), "dense_attention": float(np.mean(dn)) if dn else 0.0,
+                "score_select_gather": float(np.mean(np.array(sc) + np.array(se) + np.array(ga)))}
+
+    def selection_stats(self):
+        """k per sparse layer and physical-union sizes (outside timing)."""
+        torch, hsb = self.torch, self.hsb
+        ks, unions, zero = [], [], 0
+        res = self.results.cpu().numpy()
+        for l in range(DENSE, self.layers):
+            k = int(res[l, 0])
+            code = int(res[l, 2])
+            ks.append(k)
+            if code == 70:
+                zero += 1
+            if k:
+                sizes = torch.full((HEADS,), k, dtype=torch.int32, device="cuda")
+                u = hsb.gqa_physical_union(self.ids[l], sizes, self.n)
+                unions.append(int(u.numel()))
+            else:
+                unions.append(0)
+        return ks, unions, zero
+
+
+def run_ours(args, rank, world, torch, dist):
+    import hillserve_b200 as hsb
+
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+    dev_index = torch.cuda.current_device()
+    m = Model(hsb, torch, args.tokens, args.layers, args.alpha, seed=rank)
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        m.step(stream)  # eager run: sets kernel attributes before capture
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        m.step(stream)
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dev_index) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            stop.record(stream)
+        stop.synchronize()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = start.elapsed_time(stop)
+    stages = m.stage_ms()
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    ms_per_step = ms_max / args.steps
+    layer_steps = args.layers * args.steps * world
+    value = layer_steps / (ms_max / 1e3)
+
+    # ---- end to end through the public API with host buffers
+    e2e = run_e2e(m, graph, stream, torch, args, dist)
+
+    ks, unions, zero = m.selection_stats()
+    n = args.tokens
+    mean_k = float(np.mean(ks)) if ks else 0.0
+    mean_u = float(np.mean(unions)) if unions else 0.0
+    b_score = 2048 * n + 8192 + 64 * n
+    b_select = 64 * n + 4 * 32 * mean_k
+    b_gather = 4096 * mean_u + 16384 * mean_k
+    peak, peak_kind = peaks()
+    score_gbs = b_score / (stages["score"] / 1e3) / 1e9
+    ssg_gbs = (b_score + b_select + b_gather) / (stages["score_select_gather"] / 1e3) / 1e9
+    traffic = ncu_traffic()
+
+    line = {
+        "metric": "selected-KV decode layer-steps/s at N=32K (score+select+gather HBM GB/s vs peak)",
+        "value": round(value, 1),
+        "unit": "layer-steps/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": max(args.warmup, 3),
+        "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16 in, f32 accumulate (ordered)",
+        "data": "synthetic",
+        "config": {"workload": "configs[1]: 32-layer decode step, N=32768, layers 0-1 dense, 2-31 selected-KV",
+                   "tokens": n, "layers": args.layers, "alpha": args.alpha, "cap_ratio": 0.2,
+                   "kv_bytes_per_step": 2 * 2048 * n * args.layers, "l2": "inputs 4.3 GB >> 126 MB L2, no flush",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "launch": "one CUDA graph per 32-layer step"},
+        "stages_ms": {k: round(v, 5) for k, v in stages.items()},
+        "selection": {"k_mean": mean_k, "k_min": int(min(ks)) if ks else 0, "k_max": int(max(ks)) if ks else 0,
+                      "union_mean": mean_u, "zero_selection_layers": zero,
+                      "note": "k==0 is the reference's own outcome at this alpha (it throws there); "
+                              "attention over an empty selection returns zeros"},
+        "score_select_gather": {"bytes": b_score + b_select + b_gather, "GB_s": round(ssg_gbs, 1),
+                                "frac_of_peak": round(ssg_gbs / peak, 4), "peak_GB_s": peak, "peak_kind": peak_kind},
+        "roofline": {"kernel": "score_v3_kernel", "bound": "hbm", "achieved": round(score_gbs, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(score_gbs / peak, 4), "traffic": traffic,
+                     "algorithmic_bytes_per_launch": b_score, "peak_kind": peak_kind},
+        "e2e": e2e,
+        "gpu_launches": kernel_launches_per_step(args.layers) * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(m, torch, args)
+    graph.reset()
+    return line
+
+
+def kernel_launches_per_step(layers: int) -> int:
+    # dense: 1 kernel; sparse: score, select, gather, attention
+    return DENSE * 1 + (layers - DENSE) * 4
+
+
+def run_e2e(m, graph, stream, torch, args, dist):
+    """Same step through the public API with host buffers: every step copies
+    the 32 layers' queries (F16 + F32) and the current token's K/V rows from
+    pinned host memory, runs the step, and reads back the 32 attention
+    outputs and selections."""
+    L = args.layers
+    hq16 = m.q16.cpu().pin_memory()
+    hq32 = m.q32.cpu().pin_memory()
+    hk = m.kc[:, -1024:].cpu().pin_memory()
+    hv = m.vc[:, -1024:].cpu().pin_memory()
+    hout = torch.empty_like(m.out, device="cpu").pin_memory()
+    hres = torch.empty_like(m.results, device="cpu").pin_memory()
+    h2d = hq16.numel() * 2 + hq32.numel() * 4 + hk.numel() * 2 + hv.numel() * 2
+    d2h = hout.numel() * 4 + hres.numel() * 4
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = args.steps
+
+    def one():
+        m.q16.copy_(hq16, non_blocking=True)
+        m.q32.copy_(hq32, non_blocking=True)
+        m.kc[:, -1024:].copy_(hk, non_blocking=True)
+        m.vc[:, -1024:].copy_(hv, non_blocking=True)
+        graph.replay()
+        hout.copy_(m.out, non_blocking=True)
+        hres.copy_(m.results, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            one()
+        stream.synchronize()
+        if dist:
+            dist.barrier()
+        start.record(stream)
+        for _ in range(steps):
+            one()
+        stop.record(stream)
+    stop.synchronize()
+    ms = start.elapsed_time(stop)
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    world = dist.get_world_size() if dist else 1
+    return {"value": round(L * steps * world / (float(t.item()) / 1e3), 1), "unit": "layer-steps/s",
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "note": "KV history stays resident in HBM; per step the host sends Q and the new token's K/V rows "
+                    "and reads back attention outputs + selections"}
+
+
+def ncu_traffic():
+    """DRAM bytes per scorer launch from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "score_v3_traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get("dram_bytes_per_launch_full_size")
+        except (ValueError, OSError):
+            return None
+    return None
+
+
+# ---------------------------------------------------------------- reference
+def reference_layer_times(kc, vc, q16, q32, n, alpha, threads, sparse: bool):
+    """One layer of the reference CPU path (oracle/_ref) on host arrays.
+    Returns (seconds, k)."""
+    from oracle import binding as ob
+
+    t0 = time.perf_counter()
+    if not sparse:
+        ob.attention_dense_fast(kc, vc, n, q32, threads)
+        return time.perf_counter() - t0, n
+    scorer = reference_layer_times.scorers.setdefault(threads, ob.RefScorer(threads, 0))
+    raw = scorer.score(q16, [(kc, 0, n, 1024)])
+    scaled = ob.ref_scale(raw)
+    ids, counts, k, _ = ob.ref_select(scaled, HEADS, n, n, alpha, 0.2)
+    if k:
+        sizes = np.full(HEADS, k, dtype=np.uint64)
+        physical = ob.ref_union(ids, sizes, n)
+        rows = np.empty((len(physical), 2048), dtype=np.uint16)
+        rows[:, :1024] = kc.reshape(n, 1024)[physical.astype(np.int64)]
+        rows[:, 1024:] = vc.reshape(n, 1024)[physical.astype(np.int64)]
+        count = max(32, (int(math.floor((n) * 0.2)) + 31) // 32 * 32)
+        kp, vp, mask = ob.ref_pack(ids, sizes, [n - 1], physical, rows.reshape(-1).view(np.uint8), count)
+        ob.attention_packed_fast(kp, vp, mask, count, q32, threads)
+    return time.perf_counter() - t0, k
+
+
+reference_layer_times.scorers = {}
+
+
+def host_layers(torch, tokens, layers, seed):
+    """The same seeded inputs as our arm (generated on the GPU, then held in
+    host memory for the CPU path)."""
+    import hillserve_b200 as hsb
+
+    m = Model(hsb, torch, tokens, min(layers, 4), 0.1, seed)
+    torch.cuda.synchronize()
+    out = []
+    for l in range(min(layers, 4)):
+        out.append((m.kc[l].cpu().numpy().view(np.uint16), m.vc[l].cpu().numpy().view(np.uint16),
+                    m.q16[l].cpu().numpy().view(np.uint16), m.q32[l].cpu().numpy()))
+    del m
+    torch.cuda.empty_cache()
+    return out
+
+
+def cpu_baseline(m, torch, args, sample_layers=(0, 2, 3)):
+    """Reference CPU path timed on this host's cores on a bounded sample: one
+    dense and two selected-KV layers, scaled to the 32-layer step."""
+    from oracle import binding as ob
+
+    if not ob.reference_available():
+        return {"value": None, "unit": "layer-steps/s", "cores": os.cpu_count(), "kind": "unavailable",
+                "sample": "oracle/_ref was not built (reference sources absent when built)"}
+    threads = min(128, os.cpu_count() or 1)  # FullGqaCpuScorer accepts 1..128 threads
+    n = args.tokens
+    data = {}
+    for l in sample_layers:
+        data[l] = (m.kc[l].cpu().numpy().view(np.uint16), m.vc[l].cpu().numpy().view(np.uint16),
+                   m.q16[l].cpu().numpy().view(np.uint16), m.q32[l].cpu().numpy())
+    reference_layer_times(*data[sample_layers[1]], n, args.alpha, threads, True)  # warm-up
+    dense_t = [reference_layer_times(*data[l], n, args.alpha, threads, l < DENSE)[0] for l in sample_layers
+               if l < DENSE]
+    sparse_t = [reference_layer_times(*data[l], n, args.alpha, threads, False)[0] for l in sample_layers
+                if l >= DENSE]
+    step_s = DENSE * float(np.mean(dense_t)) + (args.layers - DENSE) * float(np.mean(sparse_t))
+    return {"value": round(args.layers / step_s, 3), "unit": "layer-steps/s", "cores": threads, "kind": "reference",
+            "sample": f"1 dense + {len(sparse_t)} selected-KV layers at N={n} (reference FullGqaCpuScorer "
+                      f"x{threads} threads, select_gqa_scores, gqa_physical_union, pack_gqa_workspace; attention "
+                      f"by the oracle port, x{threads} threads), scaled to {args.layers} layers",
+            "dense_layer_s": round(float(np.mean(dense_t)), 4), "sparse_layer_s": round(float(np.mean(sparse_t)), 4)}
+
+
+def run_reference(args, rank, world, torch):
+    from oracle import binding as ob
+
+    if rank != 0:
+        return None
+    if not ob.reference_available():
+        return {"impl": "reference", "unavailable": "oracle/_ref not built: reference sources were absent at build"}
+    threads = min(128, os.cpu_count() or 1)
+    n = args.tokens
+    layers = host_layers(torch, n, args.layers, seed=0)
+    for _ in range(max(args.warmup, 3)):
+        reference_layer_times(*layers[2 % len(layers)], n, args.alpha, threads, True)
+    # Each step: the 32-layer decode step with the layers' data cycled from a
+    # 4-layer sample (2 dense + 2 selected-KV).
+    t0 = time.perf_counter()
+    ks = []
+    for _ in range(args.steps):
+        for l in range(args.layers):
+            d = layers[l % len(layers)] if l < DENSE else layers[DENSE + (l % 2)]
+            _, k = reference_layer_times(*d, n, args.alpha, threads, l >= DENSE)
+            if l >= DENSE:
+                ks.append(k)
+    secs = time.perf_counter() - t0
+    value = args.layers * args.steps / secs
+    return {"metric": "selected-KV decode layer-steps/s at N=32K (score+select+gather HBM GB/s vs peak)",
+            "value": round(value, 3), "unit": "layer-steps/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": round(secs * 1e3 / args.steps, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 in, f32 accumulate",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": "configs[1]: 32-layer decode step, N=32768, layers 0-1 dense, 2-31 selected-KV",
+                       "tokens": n, "layers": args.layers, "alpha": args.alpha, "cap_ratio": 0.2},
+            "selection": {"k_mean": float(np.mean(ks)) if ks else 0.0},
+            "cpu_baseline": {"value": round(value, 3), "unit": "layer-steps/s", "cores": threads, "kind": "reference",
+                             "sample": "full 32-layer steps, layer data cycled from 2 dense + 2 selected-KV layers"},
+            "e2e": {"value": round(value, 3), "unit": "layer-steps/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse()
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as tdist
+
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist = tdist
+    if args.impl == "reference":
+        line = run_reference(args, rank, world, torch)
+    else:
+        line = run_ours(args, rank, world, torch, dist)
+    if rank == 0 and line is not None:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,109 @@
+"""ctypes declarations of the C ABI in ``include/hsb.h``.
+
+The shared library is loaded from ``hillserve_b200/_lib/libhsb.so`` (built
+in-tree by ``hillserve_b200.build``).  There is no other implementation: if
+the library is missing every call raises, so nothing can silently run on a
+CPU path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libhsb.so"
+
+P = C.c_void_p
+SZ = C.c_size_t
+U64 = C.c_uint64
+I = C.c_int
+F = C.c_float
+
+
+class KeyView(C.Structure):
+    _fields_ = [("data", P), ("tokens", SZ), ("stride_words", SZ)]
+
+
+class DeviceStatus(C.Structure):
+    _fields_ = [("code", C.c_int32), ("index", C.c_int32)]
+
+
+class Selection(C.Structure):
+    _fields_ = [("k", C.c_uint32), ("boundary_tied_heads", C.c_uint32), ("status", DeviceStatus)]
+
+
+class LayerBuffers(C.Structure):
+    _fields_ = [
+        ("scores", P), ("ids", P), ("counts", P), ("result", P),
+        ("k_packed", P), ("v_packed", P), ("workspace", P), ("workspace_bytes", SZ),
+    ]
+
+
+# name: (restype, argtypes)
+_SIGNATURES = {
+    "hsb_abi_version": (I, []),
+    "hsb_last_error": (C.c_char_p, []),
+    "hsb_status_message": (C.c_char_p, [I]),
+    "hsb_status_check": (I, [P, P]),
+    "hsb_score_v3": (I, [P, P, SZ, SZ, P, P]),
+    "hsb_score_views": (I, [P, P, SZ, P, P]),
+    "hsb_score_pipeline_v3": (I, [P, P, C.c_uint32, P, P]),
+    "hsb_scale_scores": (I, [P, SZ, P, P]),
+    "hsb_select_workspace_bytes": (SZ, [SZ, SZ, SZ, SZ]),
+    "hsb_select": (I, [P, I, SZ, SZ, SZ, F, F, I, P, SZ, P, P, P, SZ, P]),
+    "hsb_selection_read": (I, [P, P, P]),
+    "hsb_prefetch_cover": (I, [P, SZ, SZ, F, I, P, SZ, P, P, SZ, P]),
+    "hsb_union_workspace_bytes": (SZ, [SZ]),
+    "hsb_union": (I, [P, SZ, P, SZ, SZ, P, P, P, P, SZ, P]),
+    "hsb_pack_workspace_bytes": (SZ, [U64]),
+    "hsb_pack": (I, [P, SZ, P, SZ, P, SZ, U64, P, SZ, P, SZ, SZ, P, P, P, P, P, SZ, P]),
+    "hsb_gather_map": (I, [P, SZ, P, SZ, P, SZ, P, P, P, P]),
+    "hsb_gather_cache": (I, [P, SZ, P, SZ, P, P, SZ, SZ, SZ, I, P, P, P, P]),
+    "hsb_stage_rows": (I, [P, P, P, SZ, P, P]),
+    "hsb_attention_workspace_bytes": (SZ, [SZ]),
+    "hsb_attention_packed": (I, [P, P, P, SZ, P, SZ, P, SZ, P, P, SZ, P]),
+    "hsb_attention_dense_workspace_bytes": (SZ, [SZ]),
+    "hsb_attention_dense": (I, [P, P, P, SZ, SZ, P, P, SZ, P]),
+    "hsb_rehearsal_query": (I, [P, P, U64, F, P, P, P]),
+    "hsb_layer_workspace_bytes": (SZ, [SZ, SZ]),
+    "hsb_layer_step": (I, [P, P, P, P, SZ, SZ, F, F, SZ, P, P, P]),
+    "hsb_synth_normal_f16": (I, [P, SZ, U64, F, P]),
+    "hsb_synth_normal_bf16": (I, [P, SZ, U64, F, P]),
+    "hsb_synth_keys": (I, [P, SZ, SZ, U64, F, F, I, F, P]),
+}
+
+_lib = None
+
+
+def declared_symbols() -> list[str]:
+    """Names of every entry point this binding declares (all of hsb.h)."""
+    return list(_SIGNATURES)
+
+
+def lib() -> C.CDLL:
+    """Loads libhsb.so once; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python -m hillserve_b200.build` "
+                "(the selected-KV path has no CPU fallback)")
+        handle = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+class HsbError(RuntimeError):
+    """A non-zero hsb_status; ``str()`` is the reference-worded message."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+def check(status: int) -> None:
+    if status != 0:
+        raise HsbError(status, lib().hsb_last_error().decode() or lib().hsb_status_message(status).decode())

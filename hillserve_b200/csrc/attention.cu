@@ -1,0 +1,333 @@
+// attention.cu -- stage 4: flash-decode attention.
+//
+// attention_packed_kernel: the ggml graph of runtime/gqa_delivery.cpp:19-20
+// (scores = K.q at F32, softmax(scores/sqrt(128) + mask), out = V.p) over the
+// packed layout K [slot][32][128], V [32][128][slot].  Split-K: a CTA owns
+// (query head, 256 slots), writes (max, sum, partial output) and the last CTA
+// of a head folds the partials.  Decode has one query per head and the four
+// heads of a KV group select different slots, so there is no dense
+// contraction to give the tensor cores; the kernel is a bandwidth-bound
+// GEMV pair on the CUDA cores.
+//
+// attention_dense_kernel: dense decode attention over a token-major cache
+// (the two dense layers): a CTA owns (KV head, 512 tokens) and serves the
+// four query heads of the group from one read of each K and V row.
+#include <algorithm>
+#include <cmath>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace hsb {
+namespace {
+
+constexpr int kSplit = 256;
+constexpr int kPThreads = 128;
+constexpr int kPart = kDim + 2;  // floats per partial: max, sum, out[128]
+
+struct PackedParams {
+    const float* q;
+    const uint16_t* k;
+    const uint16_t* v;
+    size_t count;
+    const float* mask;
+    size_t qpad;
+    const uint32_t* sizes;
+    size_t sizes_stride;
+    float* out;
+    float* part;        // [32][nsplit][kPart]
+    unsigned* arrive;   // [32], zeroed before launch
+    int nsplit;
+    float scale;
+};
+
+__device__ __forceinline__ float block_reduce_max128(float v, float* red) {
+    v = warp_max(v);
+    const int warp = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) red[warp] = v;
+    __syncthreads();
+    const float r = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();
+    return r;
+}
+__device__ __forceinline__ float block_reduce_sum128(float v, float* red) {
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) red[warp] = v;
+    __syncthreads();
+    const float r = (red[0] + red[1]) + (red[2] + red[3]);
+    __syncthreads();
+    return r;
+}
+
+__global__ void __launch_bounds__(kPThreads) attention_packed_kernel(const __grid_constant__ PackedParams p) {
+    __shared__ float sc[kSplit];
+    __shared__ float red[4];
+    __shared__ int last;
+    const int h = blockIdx.y, j = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    size_t n = p.count;
+    int live = p.nsplit;
+    if (!p.mask) {
+        n = std::min<size_t>(p.sizes[(size_t)h * p.sizes_stride], p.count);
+        live = (int)((n + kSplit - 1) / kSplit);
+        if (n == 0) {
+            if (j == 0) p.out[h * kDim + tid] = 0.0f;
+            return;
+        }
+    }
+    if (j >= live) return;
+    const size_t s0 = (size_t)j * kSplit, s1 = std::min(n, s0 + kSplit);
+    const int m = (int)(s1 - s0);
+
+    const float4 q4 = reinterpret_cast<const float4*>(p.q + h * kDim)[lane];
+    for (int s = warp; s < m; s += 4) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(p.k + ((s0 + s) * kHeads + h) * kDim + lane * 4);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+        float dot = a.x * q4.x + a.y * q4.y + b.x * q4.z + b.y * q4.w;
+        dot = warp_sum(dot);
+        if (lane == 0) {
+            float x = dot * p.scale;
+            if (p.mask) x += p.mask[(size_t)h * p.qpad * p.count + s0 + s];
+            sc[s] = x;
+        }
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int s = tid; s < m; s += kPThreads) mx = fmaxf(mx, sc[s]);
+    mx = block_reduce_max128(mx, red);
+    float l = 0.0f;
+    for (int s = tid; s < m; s += kPThreads) {
+        const float e = mx == -INFINITY ? 0.0f : expf(sc[s] - mx);
+        sc[s] = e;
+        l += e;
+    }
+    l = block_reduce_sum128(l, red);
+    // out[d] partial: thread d walks its V row over the split's slots.
+    const uint16_t* vrow = p.v + ((size_t)h * kDim + tid) * p.count + s0;
+    float acc = 0.0f;
+    for (int s = 0; s < m; ++s) acc = fmaf(sc[s], half_value(vrow[s]), acc);
+    float* part = p.part + ((size_t)h * p.nsplit + j) * kPart;
+    if (tid == 0) {
+        part[0] = mx;
+        part[1] = l;
+    }
+    part[2 + tid] = acc;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = atomicAdd(&p.arrive[h], 1u) == (unsigned)(live - 1);
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const float* base = p.part + (size_t)h * p.nsplit * kPart;
+    float M = -INFINITY;
+    for (int i = 0; i < live; ++i) M = fmaxf(M, __ldcg(base + i * kPart));
+    float L = 0.0f, o = 0.0f;
+    if (M != -INFINITY) {
+        for (int i = 0; i < live; ++i) {
+            const float mi = __ldcg(base + i * kPart);
+            if (mi == -INFINITY) continue;
+            const float w = expf(mi - M);
+            L = fmaf(__ldcg(base + i * kPart + 1), w, L);
+            o = fmaf(__ldcg(base + i * kPart + 2 + tid), w, o);
+        }
+    }
+    p.out[h * kDim + tid] = L > 0.0f ? o / L : 0.0f;
+}
+
+// ------------------------------------------------------------------ dense
+constexpr int kDTokens = 512;
+constexpr int kDThreads = 256;
+
+struct DenseParams {
+    const float* q;
+    const uint16_t* kc;
+    const uint16_t* vc;
+    size_t tokens, stride;
+    float* out;
+    float* part;       // [32][nsplit][kPart]
+    unsigned* arrive;  // [8]
+    int nsplit;
+    float scale;
+};
+
+__global__ void __launch_bounds__(kDThreads) attention_dense_kernel(const __grid_constant__ DenseParams p) {
+    __shared__ float4 qs[kDim];         // [c] -> 4 heads of the group
+    __shared__ float sc[kGroup][kDTokens];
+    __shared__ float red[8][kGroup];
+    __shared__ float stat[2][kGroup];   // max, sum
+    __shared__ float accs[4][kGroup][kDim];
+    __shared__ int last;
+    const int kh = blockIdx.y, j = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int i = tid; i < kDim * kGroup; i += kDThreads) {
+        const int c = i >> 2, g = i & 3;
+        reinterpret_cast<float*>(qs)[i] = p.q[(kh * kGroup + g) * kDim + c];
+    }
+    __syncthreads();
+    const size_t t0 = (size_t)j * kDTokens;
+    const int m = (int)std::min<size_t>(kDTokens, p.tokens - t0);
+    // Scores: two tokens per thread, four heads per token.
+    for (int t = tid; t < m; t += kDThreads) {
+        const uint4* row = reinterpret_cast<const uint4*>(p.kc + (t0 + t) * p.stride + kh * kDim);
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll 4
+        for (int c8 = 0; c8 < 16; ++c8) {
+            const uint4 w = row[c8];
+            const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const float2 kv = __half22float2(*reinterpret_cast<const __half2*>(&words[jj]));
+                const float4 qa = qs[c8 * 8 + 2 * jj], qb = qs[c8 * 8 + 2 * jj + 1];
+                a0 = fmaf(qa.x, kv.x, a0); a1 = fmaf(qa.y, kv.x, a1);
+                a2 = fmaf(qa.z, kv.x, a2); a3 = fmaf(qa.w, kv.x, a3);
+                a0 = fmaf(qb.x, kv.y, a0); a1 = fmaf(qb.y, kv.y, a1);
+                a2 = fmaf(qb.z, kv.y, a2); a3 = fmaf(qb.w, kv.y, a3);
+            }
+        }
+        sc[0][t] = a0 * p.scale; sc[1][t] = a1 * p.scale;
+        sc[2][t] = a2 * p.scale; sc[3][t] = a3 * p.scale;
+    }
+    __syncthreads();
+    // Max and exp-sum per head.
+    float mx[kGroup];
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g) {
+        float v = -INFINITY;
+        for (int t = tid; t < m; t += kDThreads) v = fmaxf(v, sc[g][t]);
+        mx[g] = warp_max(v);
+        if (lane == 0) red[warp][g] = mx[g];
+    }
+    __syncthreads();
+    if (tid < kGroup) {
+        float v = -INFINITY;
+        for (int w = 0; w < 8; ++w) v = fmaxf(v, red[w][tid]);
+        stat[0][tid] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g) {
+        const float M = stat[0][g];
+        float s = 0.f;
+        for (int t = tid; t < m; t += kDThreads) {
+            const float e = expf(sc[g][t] - M);
+            sc[g][t] = e;
+            s += e;
+        }
+        s = warp_sum(s);
+        if (lane == 0) red[warp][g] = s;
+    }
+    __syncthreads();
+    if (tid < kGroup) {
+        float v = 0.f;
+        for (int w = 0; w < 8; ++w) v += red[w][tid];
+        stat[1][tid] = v;
+    }
+    // Partial outputs: thread = (channel pair, quarter of the tokens).
+    const int dp = tid & 63, quarter = tid >> 6;
+    float o[kGroup][2] = {};
+    const int per = (m + 3) / 4;
+    const int tb = quarter * per, te = std::min(m, tb + per);
+    for (int t = tb; t < te; ++t) {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(p.vc + (t0 + t) * p.stride + kh * kDim + 2 * dp);
+        const float2 v2 = __half22float2(*reinterpret_cast<const __half2*>(&w));
+#pragma unroll
+        for (int g = 0; g < kGroup; ++g) {
+            const float pg = sc[g][t];
+            o[g][0] = fmaf(pg, v2.x, o[g][0]);
+            o[g][1] = fmaf(pg, v2.y, o[g][1]);
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g) {
+        accs[quarter][g][2 * dp] = o[g][0];
+        accs[quarter][g][2 * dp + 1] = o[g][1];
+    }
+    __syncthreads();
+    for (int i = tid; i < kGroup * kDim; i += kDThreads) {
+        const int g = i >> 7, d = i & 127;
+        const float v = (accs[0][g][d] + accs[1][g][d]) + (accs[2][g][d] + accs[3][g][d]);
+        float* part = p.part + ((size_t)(kh * kGroup + g) * p.nsplit + j) * kPart;
+        part[2 + d] = v;
+        if (d == 0) {
+            part[0] = stat[0][g];
+            part[1] = stat[1][g];
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = atomicAdd(&p.arrive[kh], 1u) == (unsigned)(p.nsplit - 1);
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int i = tid; i < kGroup * kDim; i += kDThreads) {
+        const int g = i >> 7, d = i & 127;
+        const float* base = p.part + (size_t)(kh * kGroup + g) * p.nsplit * kPart;
+        float M = -INFINITY;
+        for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, __ldcg(base + s * kPart));
+        float L = 0.f, acc = 0.f;
+        for (int s = 0; s < p.nsplit; ++s) {
+            const float w = expf(__ldcg(base + s * kPart) - M);
+            L = fmaf(__ldcg(base + s * kPart + 1), w, L);
+            acc = fmaf(__ldcg(base + s * kPart + 2 + d), w, acc);
+        }
+        p.out[(kh * kGroup + g) * kDim + d] = acc / L;
+    }
+}
+
+size_t align256(size_t b) { return (b + 255) / 256 * 256; }
+
+}  // namespace
+
+size_t attention_workspace_bytes(size_t count) {
+    const size_t nsplit = std::max<size_t>(1, (count + kSplit - 1) / kSplit);
+    return align256(kHeads * sizeof(unsigned)) + align256(kHeads * nsplit * kPart * sizeof(float));
+}
+
+cudaError_t launch_attention_packed(const float* q, const uint16_t* k, const uint16_t* v, size_t count,
+                                    const float* mask, size_t qpad, const uint32_t* sizes,
+                                    size_t sizes_stride, float* out, void* workspace, cudaStream_t stream) {
+    PackedParams p{};
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.count = count;
+    p.mask = mask;
+    p.qpad = qpad;
+    p.sizes = sizes;
+    p.sizes_stride = sizes_stride;
+    p.out = out;
+    p.nsplit = (int)std::max<size_t>(1, (count + kSplit - 1) / kSplit);
+    p.arrive = static_cast<unsigned*>(workspace);
+    p.part = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + align256(kHeads * sizeof(unsigned)));
+    p.scale = 1.0f / sqrtf(128.0f);
+    cudaError_t e = cudaMemsetAsync(p.arrive, 0, kHeads * sizeof(unsigned), stream);
+    if (e != cudaSuccess) return e;
+    attention_packed_kernel<<<dim3(p.nsplit, kHeads), kPThreads, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+size_t attention_dense_workspace_bytes(size_t tokens) {
+    const size_t nsplit = std::max<size_t>(1, (tokens + kDTokens - 1) / kDTokens);
+    return align256(kKvHeads * sizeof(unsigned)) + align256(kHeads * nsplit * kPart * sizeof(float));
+}
+
+cudaError_t launch_attention_dense(const float* q, const uint16_t* kcache, const uint16_t* vcache, size_t tokens,
+                                   size_t stride_words, float* out, void* workspace, cudaStream_t stream) {
+    DenseParams p{};
+    p.q = q;
+    p.kc = kcache;
+    p.vc = vcache;
+    p.tokens = tokens;
+    p.stride = stride_words;
+    p.out = out;
+    p.nsplit = (int)((tokens + kDTokens - 1) / kDTokens);
+    p.arrive = static_cast<unsigned*>(workspace);
+    p.part = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + align256(kKvHeads * sizeof(unsigned)));
+    p.scale = 1.0f / sqrtf(128.0f);
+    cudaError_t e = cudaMemsetAsync(p.arrive, 0, kKvHeads * sizeof(unsigned), stream);
+    if (e != cudaSuccess) return e;
+    attention_dense_kernel<<<dim3(p.nsplit, kKvHeads), kDThreads, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace hsb

@@ -1,0 +1,494 @@
+// capi.cu -- the extern "C" boundary (include/hsb.h): argument validation in
+// the reference's order and wording, the thread-local last-error string,
+// device status read-back, and the fused selected-KV layer step.
+#include <cuda_runtime.h>
+
+#include <cfenv>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <limits>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "internal.h"
+
+namespace hsb {
+
+namespace {
+thread_local std::string g_last_error;
+
+int fail(int status, const char* message) {
+    g_last_error = message;
+    return status;
+}
+int fail_cuda(cudaError_t e, const char* what) {
+    g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+    return HSB_E_CUDA;
+}
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+std::mutex g_dev_mutex;
+DeviceInfo g_devices[64];
+}  // namespace
+
+const DeviceInfo& device_info() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    DeviceInfo& d = g_devices[dev];
+    if (d.ordinal != dev) {
+        std::lock_guard<std::mutex> lock(g_dev_mutex);
+        if (d.ordinal != dev) {
+            cudaDeviceProp prop{};
+            if (cudaGetDeviceProperties(&prop, dev) == cudaSuccess) {
+                d.sms = prop.multiProcessorCount;
+                d.major = prop.major;
+                d.minor = prop.minor;
+                d.smem_optin = prop.sharedMemPerBlockOptin;
+            } else {
+                d.sms = 148;
+            }
+            d.ordinal = dev;
+        }
+    }
+    return d;
+}
+
+}  // namespace hsb
+
+using namespace hsb;
+
+extern "C" {
+
+int hsb_abi_version(void) { return HSB_ABI_VERSION; }
+const char* hsb_last_error(void) { return g_last_error.c_str(); }
+
+const char* hsb_status_message(int status) {
+    switch (status) {
+    case HSB_OK: return "";
+    case HSB_E_INVALID: return "invalid argument";
+    case HSB_E_CUDA: return "CUDA runtime error";
+    case HSB_E_WORKSPACE: return "workspace missing or too small";
+    case HSB_E_TIMEOUT: return "bounded device wait timed out";
+    case HSB_E_NO_DEVICE: return "no sm_100 device";
+    case HSB_E_SCORE_SHAPE: return "full GQA CPU key view shape/stride/extent";
+    case HSB_E_SCORE_ALIAS: return "full GQA CPU output must not alias the query";
+    case HSB_E_SCORE_V3_TOKENS: return "HS_FULL_GQA_PIPELINE_F16_V3 requires64<=N<=32768,N%64==0;no padding or fallback";
+    case HSB_E_SEL_SHAPE: return "GQA selector shape";
+    case HSB_E_SEL_PARAMS: return "GQA selector numeric parameters";
+    case HSB_E_SEL_NONFINITE_HEAD0: return "nonfinite head0 score";
+    case HSB_E_SEL_THRESHOLD: return "F16 threshold overflow";
+    case HSB_E_SEL_NONFINITE: return "nonfinite GQA score";
+    case HSB_E_SEL_U32: return "threshold count exceeds u32";
+    case HSB_E_SEL_COUNT_F16: return "public F16 count overflow; long-count policy extension required";
+    case HSB_E_SEL_MEAN_F16: return "public F16 mean overflow; long-count policy extension required";
+    case HSB_E_SEL_CAPACITY: return "selected ID buffer smaller than min(floor(valid*ratio), valid)";
+    case HSB_E_UNION_BOUNDS: return "GQA union bounds";
+    case HSB_E_UNION_DUPLICATE: return "GQA duplicate/future selected ID";
+    case HSB_E_PACK_SHAPE: return "GQA packing shape";
+    case HSB_E_PACK_PHYSICAL: return "duplicate/future physical position";
+    case HSB_E_PACK_SLOTS: return "per-head selection exceeds slots";
+    case HSB_E_PACK_MISSING: return "future or missing selected KV";
+    case HSB_E_MAP_GEOMETRY: return "prefetch CUDA delivery geometry/stream";
+    case HSB_E_MAP_ROW: return "prefetch row outside uploaded payload";
+    case HSB_E_MAP_MISS: return "prefetch miss row outside payload";
+    case HSB_E_COVER_RANGE: return "payload prefetch historical cap/range mismatch";
+    case HSB_E_COVER_THRESHOLD: return "prefetch threshold upper-bound requires finite historical threshold";
+    case HSB_E_COVER_COUNT: return "prefetch count upper-bound exceeds original F16 range";
+    case HSB_E_COVER_MEAN: return "prefetch mean upper-bound invalid";
+    case HSB_E_ZERO_SELECTION: return "full GQA zero selection; no dense/current-token fallback";
+    default: return "unknown hsb status";
+    }
+}
+
+int hsb_status_check(const hsb_device_status* d_status, void* stream) {
+    if (!d_status) return fail(HSB_E_INVALID, "null status");
+    hsb_device_status h{};
+    cudaError_t e = cudaMemcpyAsync(&h, d_status, sizeof(h), cudaMemcpyDeviceToHost, as_stream(stream));
+    if (e == cudaSuccess) e = cudaStreamSynchronize(as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "status read-back");
+    if (h.code) return fail(h.code, hsb_status_message(h.code));
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+// ------------------------------------------------------------------ stage 1
+static int check_views(const hsb_key_view* views, size_t nviews, size_t* total) {
+    // policy/full_gqa_cpu.cpp:214-227
+    if (!views || nviews == 0) return fail(HSB_E_SCORE_SHAPE, "full GQA CPU query/views shape");
+    size_t tokens = 0;
+    for (size_t i = 0; i < nviews; ++i) {
+        const hsb_key_view& v = views[i];
+        if (!v.data || v.tokens == 0 || (v.stride_words != 1024 && v.stride_words != 2048) ||
+            v.tokens > std::numeric_limits<size_t>::max() / v.stride_words ||
+            v.tokens > std::numeric_limits<size_t>::max() / HSB_QUERY_HEADS - tokens)
+            return fail(HSB_E_SCORE_SHAPE, "full GQA CPU key view shape/stride/extent");
+        if (!aligned(v.data, 16)) return fail(HSB_E_INVALID, "key view must be 16-byte aligned");
+        tokens += v.tokens;
+    }
+    *total = tokens;
+    return HSB_OK;
+}
+
+int hsb_score_views(const uint16_t* d_q, const hsb_key_view* h_views, size_t nviews, uint16_t* d_scores,
+                    void* stream) {
+    if (!d_q) return fail(HSB_E_SCORE_SHAPE, "full GQA CPU query/views shape");
+    if (d_scores == d_q) return fail(HSB_E_SCORE_ALIAS, "full GQA CPU output must not alias the query");
+    size_t total = 0;
+    int rc = check_views(h_views, nviews, &total);
+    if (rc) return rc;
+    if (!d_scores) return fail(HSB_E_INVALID, "null score output");
+    size_t col = 0;
+    for (size_t first = 0; first < nviews; first += HSB_MAX_VIEWS) {
+        const size_t n = std::min<size_t>(HSB_MAX_VIEWS, nviews - first);
+        cudaError_t e = launch_score(d_q, h_views + first, n, d_scores, total, col, nullptr, as_stream(stream));
+        if (e != cudaSuccess) return fail_cuda(e, "score launch");
+        for (size_t i = 0; i < n; ++i) col += h_views[first + i].tokens;
+    }
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+int hsb_score_v3(const uint16_t* d_q, const uint16_t* d_keys, size_t tokens, size_t stride_words,
+                 uint16_t* d_scores, void* stream) {
+    const hsb_key_view view{d_keys, tokens, stride_words};
+    return hsb_score_views(d_q, &view, 1, d_scores, stream);
+}
+
+int hsb_score_pipeline_v3(const uint16_t* d_q, const uint16_t* d_keys, uint32_t tokens, uint16_t* d_scores,
+                          void* stream) {
+    // smartssd/adapter.hpp:97-104 and the kernel's own guard (kernel.cpp:237-253):
+    // invalid counts are rejected before any memory access.
+    if (tokens < 64 || tokens > 32768 || tokens % 64)
+        return fail(HSB_E_SCORE_V3_TOKENS,
+                    "HS_FULL_GQA_PIPELINE_F16_V3 requires64<=N<=32768,N%64==0;no padding or fallback");
+    return hsb_score_v3(d_q, d_keys, tokens, 1024, d_scores, stream);
+}
+
+int hsb_scale_scores(const uint16_t* d_raw, size_t count, uint16_t* d_out, void* stream) {
+    if (!d_raw || !d_out) return fail(HSB_E_INVALID, "null score buffer");
+    if (count == 0) return HSB_OK;
+    cudaError_t e = launch_scale(d_raw, count, d_out, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "scale launch");
+    return HSB_OK;
+}
+
+// ------------------------------------------------------------------ stage 2
+size_t hsb_select_workspace_bytes(size_t heads, size_t stride, size_t valid, size_t kcap) {
+    (void)stride;
+    return select_workspace_bytes(heads, valid, kcap);
+}
+
+static int check_select(size_t heads, size_t stride, size_t valid, float alpha, float ratio) {
+    // policy/gqa_policy.cpp:48-49
+    if (!(heads > 0 && heads <= 128 && valid > 0 && valid <= stride))
+        return fail(HSB_E_SEL_SHAPE, "GQA selector shape");
+    if (!(std::isfinite(alpha) && alpha >= 0 && std::isfinite(ratio) && ratio > 0 && ratio <= 1))
+        return fail(HSB_E_SEL_PARAMS, "GQA selector numeric parameters");
+    if (valid > 0xffffffffull) return fail(HSB_E_SEL_SHAPE, "GQA selector shape (valid >= 2^32)");
+    return HSB_OK;
+}
+
+static size_t select_kmax(size_t valid, float ratio) {
+    const size_t cap = (size_t)std::floor((double)valid * (double)ratio);
+    return std::min(cap, valid);
+}
+
+int hsb_select(const uint16_t* d_scores, int input_is_raw, size_t heads, size_t stride, size_t valid, float alpha,
+               float ratio, int fp32_counts, uint32_t* d_ids, size_t kcap, uint32_t* d_counts,
+               hsb_selection* d_result, void* d_workspace, size_t workspace_bytes, void* stream) {
+    int rc = check_select(heads, stride, valid, alpha, ratio);
+    if (rc) return rc;
+    if (!d_scores || !d_ids || !d_result) return fail(HSB_E_INVALID, "null selector buffer");
+    if (!aligned(d_result, 8)) return fail(HSB_E_INVALID, "selection result must be 8-byte aligned");
+    if (kcap < select_kmax(valid, ratio)) return fail(HSB_E_SEL_CAPACITY, hsb_status_message(HSB_E_SEL_CAPACITY));
+    if (!d_workspace || workspace_bytes < select_workspace_bytes(heads, valid, kcap) || !aligned(d_workspace, 256))
+        return fail(HSB_E_WORKSPACE, "selector workspace missing or too small");
+    SelectLaunch s{};
+    s.scores = d_scores;
+    s.raw = input_is_raw != 0;
+    s.cover = 0;
+    s.heads = (uint32_t)heads;
+    s.stride = stride;
+    s.valid = valid;
+    s.alpha = alpha;
+    s.ratio = ratio;
+    s.fp32_counts = fp32_counts != 0;
+    s.ids = d_ids;
+    s.kcap = kcap;
+    s.counts = d_counts;
+    s.result = d_result;
+    s.workspace = d_workspace;
+    s.workspace_bytes = workspace_bytes;
+    cudaError_t e = launch_select(s, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "select launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+int hsb_selection_read(const hsb_selection* d_result, hsb_selection* h_result, void* stream) {
+    if (!d_result || !h_result) return fail(HSB_E_INVALID, "null selection");
+    cudaError_t e = cudaMemcpyAsync(h_result, d_result, sizeof(*h_result), cudaMemcpyDeviceToHost, as_stream(stream));
+    if (e == cudaSuccess) e = cudaStreamSynchronize(as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "selection read-back");
+    if (h_result->status.code) return fail(h_result->status.code, hsb_status_message(h_result->status.code));
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+int hsb_prefetch_cover(const uint16_t* d_raw, size_t capacity, size_t position, float alpha, int fp32_counts,
+                       uint32_t* d_per_head, size_t cap, hsb_selection* d_result, void* d_workspace,
+                       size_t workspace_bytes, void* stream) {
+    // policy/full_gqa_runtime.cpp:314-317
+    const size_t by_ratio = (size_t)std::floor((double)(position + 1) * (double)0.2f);
+    const size_t want = std::min(position, by_ratio);
+    if (!(position && position < capacity && want))
+        return fail(HSB_E_COVER_RANGE, "payload prefetch historical cap/range mismatch");
+    if (cap != want) return fail(HSB_E_INVALID, "per-head cover buffer stride must equal the cap");
+    if (!d_raw || !d_per_head || !d_result) return fail(HSB_E_INVALID, "null cover buffer");
+    if (!aligned(d_result, 8)) return fail(HSB_E_INVALID, "selection result must be 8-byte aligned");
+    if (!d_workspace || workspace_bytes < select_workspace_bytes(HSB_QUERY_HEADS, position, cap) ||
+        !aligned(d_workspace, 256))
+        return fail(HSB_E_WORKSPACE, "cover workspace missing or too small");
+    SelectLaunch s{};
+    s.scores = d_raw;
+    s.raw = 1;
+    s.cover = 1;
+    s.heads = HSB_QUERY_HEADS;
+    s.stride = capacity;
+    s.valid = position;
+    s.alpha = alpha;
+    s.ratio = 1.0f;
+    s.fp32_counts = fp32_counts != 0;
+    s.ids = d_per_head;
+    s.kcap = cap;
+    s.counts = nullptr;
+    s.result = d_result;
+    s.workspace = d_workspace;
+    s.workspace_bytes = workspace_bytes;
+    s.cover_cap = cap;
+    cudaError_t e = launch_select(s, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "cover launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+// ------------------------------------------------------------------ stage 3
+size_t hsb_union_workspace_bytes(size_t visible) { return union_workspace_bytes(visible); }
+
+int hsb_union(const uint32_t* d_ids, size_t kstride, const uint32_t* d_sizes, size_t sizes_stride, size_t visible,
+              uint32_t* d_physical, uint32_t* d_physical_count, hsb_device_status* d_status, void* d_workspace,
+              size_t workspace_bytes, void* stream) {
+    // runtime/gqa_pack.hpp:14
+    if (!visible || visible > 66048) return fail(HSB_E_UNION_BOUNDS, "GQA union bounds");
+    if (!d_ids || !d_sizes || !d_physical || !d_physical_count) return fail(HSB_E_INVALID, "null union buffer");
+    if (d_status && !aligned(d_status, 8)) return fail(HSB_E_INVALID, "status must be 8-byte aligned");
+    if (!d_workspace || workspace_bytes < union_workspace_bytes(visible))
+        return fail(HSB_E_WORKSPACE, "union workspace missing or too small");
+    cudaError_t e = launch_union(d_ids, kstride, d_sizes, sizes_stride, visible, d_physical, d_physical_count,
+                                 d_status, d_workspace, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "union launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+size_t hsb_pack_workspace_bytes(uint64_t last_position) { return pack_workspace_bytes(last_position); }
+
+int hsb_pack(const uint32_t* d_ids, size_t kstride, const uint32_t* d_sizes, size_t sizes_stride,
+             const uint64_t* d_positions, size_t npositions, uint64_t last_position, const uint32_t* d_physical,
+             size_t nphysical, const uint8_t* d_payload, size_t payload_bytes, size_t count, uint16_t* d_k,
+             uint16_t* d_v, float* d_mask, hsb_device_status* d_status, void* d_workspace,
+             size_t workspace_bytes, void* stream) {
+    // runtime/gqa_pack.hpp:29-30
+    if (npositions == 0 || npositions > 256 || last_position >= 66048 || !count || count > 66048 ||
+        payload_bytes != nphysical * 4096)
+        return fail(HSB_E_PACK_SHAPE, "GQA packing shape");
+    if (!d_ids || !d_sizes || !d_k || !d_v || (nphysical && (!d_physical || !d_payload)) ||
+        (d_mask && !d_positions))
+        return fail(HSB_E_INVALID, "null pack buffer");
+    if ((nphysical && !aligned(d_payload, 16)) || !aligned(d_k, 16) || (d_status && !aligned(d_status, 8)))
+        return fail(HSB_E_INVALID, "pack buffers must be 16-byte aligned");
+    if (!d_workspace || workspace_bytes < pack_workspace_bytes(last_position))
+        return fail(HSB_E_WORKSPACE, "pack workspace missing or too small");
+    cudaError_t e = launch_pack(d_ids, kstride, d_sizes, sizes_stride, d_positions, npositions, last_position,
+                                d_physical, nphysical, d_payload, count, d_k, d_v, d_mask, d_status, d_workspace,
+                                as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "pack launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+int hsb_gather_map(const uint16_t* d_prefetched, size_t prefetched_rows, const uint16_t* d_misses, size_t miss_rows,
+                   const int32_t* d_map, size_t count, uint16_t* d_k, uint16_t* d_v, hsb_device_status* d_status,
+                   void* stream) {
+    if (!d_map || !d_k || !d_v || count == 0) return fail(HSB_E_MAP_GEOMETRY, "prefetch CUDA delivery geometry/stream");
+    if ((prefetched_rows && !aligned(d_prefetched, 16)) || (miss_rows && !aligned(d_misses, 16)) || !aligned(d_k, 16) ||
+        (d_status && !aligned(d_status, 8)))
+        return fail(HSB_E_INVALID, "gather buffers must be 16-byte aligned");
+    cudaError_t e = launch_gather_map(d_prefetched, prefetched_rows, d_misses, miss_rows, d_map, count, d_k, d_v,
+                                      d_status, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "gather launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+int hsb_gather_cache(const uint32_t* d_ids, size_t kstride, const uint32_t* d_sizes, size_t sizes_stride,
+                     const uint16_t* d_kcache, const uint16_t* d_vcache, size_t stride_words, size_t visible,
+                     size_t count, int zero_padding, uint16_t* d_k, uint16_t* d_v, hsb_device_status* d_status,
+                     void* stream) {
+    if (!d_ids || !d_sizes || !d_kcache || !d_vcache || !d_k || !d_v || count == 0 || visible == 0 || kstride < count)
+        return fail(HSB_E_INVALID, "gather_cache arguments");
+    if (stride_words % 8 || !aligned(d_kcache, 16) || !aligned(d_vcache, 16) || !aligned(d_k, 16) ||
+        (d_status && !aligned(d_status, 8)))
+        return fail(HSB_E_INVALID, "gather_cache buffers must be 16-byte aligned");
+    cudaError_t e = launch_gather_cache(d_ids, kstride, d_sizes, sizes_stride, d_kcache, d_vcache, stride_words,
+                                        visible, count, zero_padding, d_k, d_v, d_status, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "gather_cache launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+int hsb_stage_rows(const uint8_t* d_rows, const uint32_t* d_physical, const uint32_t* d_count, size_t max_rows,
+                   uint8_t* d_dst, void* stream) {
+    if (!d_rows || !d_physical || !d_count || !d_dst) return fail(HSB_E_INVALID, "null staging buffer");
+    if (!aligned(d_rows, 16) || !aligned(d_dst, 16)) return fail(HSB_E_INVALID, "staging buffers must be 16-byte aligned");
+    if (max_rows == 0) return HSB_OK;
+    // The row store may be device memory or pinned host memory; translate it
+    // to the address the GPU uses and refuse memory the GPU cannot reach.
+    cudaPointerAttributes attr{};
+    if (cudaPointerGetAttributes(&attr, d_rows) != cudaSuccess || attr.devicePointer == nullptr) {
+        cudaGetLastError();
+        return fail(HSB_E_INVALID, "row store is neither device memory nor mapped pinned host memory");
+    }
+    const uint8_t* rows = static_cast<const uint8_t*>(attr.devicePointer);
+    if (!aligned(rows, 16)) return fail(HSB_E_INVALID, "staging buffers must be 16-byte aligned");
+    cudaError_t e = launch_stage_rows(rows, d_physical, d_count, max_rows, d_dst, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "stage launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+// ------------------------------------------------------------------ stage 4
+size_t hsb_attention_workspace_bytes(size_t count) { return attention_workspace_bytes(count); }
+
+int hsb_attention_packed(const float* d_q, const uint16_t* d_k, const uint16_t* d_v, size_t count, const float* d_mask,
+                         size_t qpad, const uint32_t* d_sizes, size_t sizes_stride, float* d_out, void* d_workspace,
+                         size_t workspace_bytes, void* stream) {
+    if (!d_q || !d_k || !d_v || !d_out || count == 0 || (!d_mask && !d_sizes) || (d_mask && qpad == 0))
+        return fail(HSB_E_INVALID, "attention arguments");
+    if (!aligned(d_q, 16) || !aligned(d_k, 16)) return fail(HSB_E_INVALID, "attention buffers must be 16-byte aligned");
+    if (!d_workspace || workspace_bytes < attention_workspace_bytes(count))
+        return fail(HSB_E_WORKSPACE, "attention workspace missing or too small");
+    cudaError_t e = launch_attention_packed(d_q, d_k, d_v, count, d_mask, qpad, d_sizes, sizes_stride, d_out,
+                                            d_workspace, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "attention launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+size_t hsb_attention_dense_workspace_bytes(size_t tokens) { return attention_dense_workspace_bytes(tokens); }
+
+int hsb_attention_dense(const float* d_q, const uint16_t* d_kcache, const uint16_t* d_vcache, size_t tokens,
+                        size_t stride_words, float* d_out, void* d_workspace, size_t workspace_bytes, void* stream) {
+    if (!d_q || !d_kcache || !d_vcache || !d_out || tokens == 0 || stride_words < 1024 || stride_words % 8)
+        return fail(HSB_E_INVALID, "dense attention arguments");
+    if (!aligned(d_kcache, 16) || !aligned(d_vcache, 16))
+        return fail(HSB_E_INVALID, "dense attention caches must be 16-byte aligned");
+    if (!d_workspace || workspace_bytes < attention_dense_workspace_bytes(tokens))
+        return fail(HSB_E_WORKSPACE, "dense attention workspace missing or too small");
+    cudaError_t e = launch_attention_dense(d_q, d_kcache, d_vcache, tokens, stride_words, d_out, d_workspace,
+                                           as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "dense attention launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+// ------------------------------------------------------------- rehearsal
+int hsb_rehearsal_query(const uint16_t* d_x, const uint16_t* d_w, uint64_t position, float theta, float* d_q_f32,
+                        uint16_t* d_q_f16, void* stream) {
+    if (!d_x || !d_w || (!d_q_f32 && !d_q_f16) || !(theta > 0.0f) || !std::isfinite(theta))
+        return fail(HSB_E_INVALID, "rehearsal arguments");
+    if (!aligned(d_w, 16)) return fail(HSB_E_INVALID, "rehearsal weights must be 16-byte aligned");
+    cudaError_t e = launch_rehearsal(d_x, d_w, position, theta, d_q_f32, d_q_f16, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "rehearsal launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+// ------------------------------------------------------------- layer step
+size_t hsb_layer_workspace_bytes(size_t valid, size_t count) {
+    const size_t sel = select_workspace_bytes(HSB_QUERY_HEADS, valid, count);
+    const size_t att = attention_workspace_bytes(count);
+    return (sel + 255) / 256 * 256 + (att + 255) / 256 * 256;
+}
+
+int hsb_layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_kcache, const uint16_t* d_vcache,
+                   size_t stride_words, size_t valid, float alpha, float ratio, size_t count,
+                   const hsb_layer_buffers* b, float* d_out, void* stream) {
+    if (!b || !d_q16 || !d_q32 || !d_out) return fail(HSB_E_INVALID, "layer step arguments");
+    int rc = check_select(HSB_QUERY_HEADS, valid, valid, alpha, ratio);
+    if (rc) return rc;
+    if (count < select_kmax(valid, ratio) || count == 0)
+        return fail(HSB_E_SEL_CAPACITY, hsb_status_message(HSB_E_SEL_CAPACITY));
+    if (!b->scores || !b->ids || !b->result || !b->k_packed || !b->v_packed || !b->workspace ||
+        b->workspace_bytes < hsb_layer_workspace_bytes(valid, count) || !aligned(b->workspace, 256))
+        return fail(HSB_E_WORKSPACE, "layer step buffers missing or too small");
+    cudaStream_t s = as_stream(stream);
+    const hsb_key_view view{d_kcache, valid, stride_words};
+    size_t total = 0;
+    if ((rc = check_views(&view, 1, &total))) return rc;
+    cudaError_t e = cudaMemsetAsync(b->result, 0, sizeof(hsb_selection), s);
+    if (e != cudaSuccess) return fail_cuda(e, "result reset");
+    if ((e = launch_score(d_q16, &view, 1, b->scores, valid, 0, &b->result->status, s)) != cudaSuccess)
+        return fail_cuda(e, "score launch");
+    const size_t sel_bytes = (select_workspace_bytes(HSB_QUERY_HEADS, valid, count) + 255) / 256 * 256;
+    SelectLaunch sl{};
+    sl.scores = b->scores;
+    sl.raw = 1;
+    sl.heads = HSB_QUERY_HEADS;
+    sl.stride = valid;
+    sl.valid = valid;
+    sl.alpha = alpha;
+    sl.ratio = ratio;
+    sl.ids = b->ids;
+    sl.kcap = count;
+    sl.counts = b->counts;
+    sl.result = b->result;
+    sl.workspace = b->workspace;
+    sl.workspace_bytes = sel_bytes;
+    sl.reset_result = 0;
+    sl.zero_is_error = 1;
+    if ((e = launch_select(sl, s)) != cudaSuccess) return fail_cuda(e, "select launch");
+    if ((e = launch_gather_cache(b->ids, count, &b->result->k, 0, d_kcache, d_vcache, stride_words, valid, count, 0,
+                                 b->k_packed, b->v_packed, &b->result->status, s)) != cudaSuccess)
+        return fail_cuda(e, "gather launch");
+    if ((e = launch_attention_packed(d_q32, b->k_packed, b->v_packed, count, nullptr, 0, &b->result->k, 0, d_out,
+                                     static_cast<unsigned char*>(b->workspace) + sel_bytes, s)) != cudaSuccess)
+        return fail_cuda(e, "attention launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+// ------------------------------------------------------------- synthetic
+int hsb_synth_normal_f16(uint16_t* d_out, size_t count, uint64_t seed, float stddev, void* stream) {
+    if (!d_out) return fail(HSB_E_INVALID, "null output");
+    cudaError_t e = launch_synth_normal(d_out, count, seed, stddev, 0, as_stream(stream));
+    return e == cudaSuccess ? HSB_OK : fail_cuda(e, "synth launch");
+}
+int hsb_synth_normal_bf16(uint16_t* d_out, size_t count, uint64_t seed, float stddev, void* stream) {
+    if (!d_out) return fail(HSB_E_INVALID, "null output");
+    cudaError_t e = launch_synth_normal(d_out, count, seed, stddev, 1, as_stream(stream));
+    return e == cudaSuccess ? HSB_OK : fail_cuda(e, "synth launch");
+}
+int hsb_synth_keys(uint16_t* d_rows, size_t tokens, size_t stride_words, uint64_t seed, float heavy_fraction,
+                   float heavy_scale, int rope, float theta, void* stream) {
+    if (!d_rows || stride_words < 1024) return fail(HSB_E_INVALID, "synth keys arguments");
+    cudaError_t e = launch_synth_keys(d_rows, tokens, stride_words, seed, heavy_fraction, heavy_scale, rope, theta,
+                                      as_stream(stream));
+    return e == cudaSuccess ? HSB_OK : fail_cuda(e, "synth launch");
+}
+
+}  // extern "C"

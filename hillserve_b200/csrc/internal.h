@@ -1,0 +1,98 @@
+// internal.h -- host-side declarations shared by the kernel files and the
+// C-ABI layer (capi.cu).  Not installed; the public interface is hsb.h.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "hsb.h"
+
+namespace hsb {
+
+struct DeviceInfo {
+    int ordinal = -1;
+    int sms = 0;
+    int major = 0, minor = 0;
+    size_t smem_optin = 0;
+};
+// Properties of the current device, cached per device.
+const DeviceInfo& device_info();
+
+// Stage 1
+cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nviews,
+                         uint16_t* out, size_t out_stride, size_t col0,
+                         hsb_device_status* status, cudaStream_t stream);
+cudaError_t launch_scale(const uint16_t* raw, size_t count, uint16_t* out, cudaStream_t stream);
+
+// Stage 2
+struct SelectLaunch {
+    const uint16_t* scores;
+    int raw;           // normalise in the kernel
+    int cover;         // prefetch-cover rules instead of select_gqa_scores
+    uint32_t heads;
+    unsigned long long stride, valid;
+    float alpha, ratio;
+    int fp32_counts;
+    uint32_t* ids;
+    unsigned long long kcap;
+    uint32_t* counts;  // may be null (cover)
+    hsb_selection* result;
+    void* workspace;
+    size_t workspace_bytes;
+    unsigned long long cover_cap;  // cover: min(position, floor((position+1)*0.2f))
+    int reset_result = 1;          // zero *result before the kernel
+    int zero_is_error = 0;         // k == 0 -> HSB_E_ZERO_SELECTION (layer step)
+};
+size_t select_workspace_bytes(size_t heads, size_t valid, size_t kcap);
+cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream);
+
+// Stage 3
+size_t union_workspace_bytes(size_t visible);
+cudaError_t launch_union(const uint32_t* ids, size_t kstride, const uint32_t* sizes,
+                         size_t sizes_stride, size_t visible, uint32_t* physical,
+                         uint32_t* physical_count, hsb_device_status* status, void* workspace,
+                         cudaStream_t stream);
+size_t pack_workspace_bytes(uint64_t last_position);
+cudaError_t launch_pack(const uint32_t* ids, size_t kstride, const uint32_t* sizes,
+                        size_t sizes_stride, const uint64_t* positions, size_t npositions,
+                        uint64_t last_position, const uint32_t* physical, size_t nphysical,
+                        const uint8_t* payload, size_t count, uint16_t* k, uint16_t* v,
+                        float* mask, hsb_device_status* status, void* workspace,
+                        cudaStream_t stream);
+cudaError_t launch_gather_map(const uint16_t* prefetched, size_t prefetched_rows,
+                              const uint16_t* misses, size_t miss_rows, const int32_t* map,
+                              size_t count, uint16_t* k, uint16_t* v, hsb_device_status* status,
+                              cudaStream_t stream);
+cudaError_t launch_gather_cache(const uint32_t* ids, size_t kstride, const uint32_t* sizes,
+                                size_t sizes_stride, const uint16_t* kcache,
+                                const uint16_t* vcache, size_t stride_words, size_t visible,
+                                size_t count, int zero_padding, uint16_t* k, uint16_t* v,
+                                hsb_device_status* status, cudaStream_t stream);
+cudaError_t launch_stage_rows(const uint8_t* rows, const uint32_t* physical,
+                              const uint32_t* count, size_t max_rows, uint8_t* dst,
+                              cudaStream_t stream);
+
+// Stage 4
+size_t attention_workspace_bytes(size_t count);
+cudaError_t launch_attention_packed(const float* q, const uint16_t* k, const uint16_t* v,
+                                    size_t count, const float* mask, size_t qpad,
+                                    const uint32_t* sizes, size_t sizes_stride, float* out,
+                                    void* workspace, cudaStream_t stream);
+size_t attention_dense_workspace_bytes(size_t tokens);
+cudaError_t launch_attention_dense(const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                                   size_t tokens, size_t stride_words, float* out,
+                                   void* workspace, cudaStream_t stream);
+
+// Rehearsal query
+cudaError_t launch_rehearsal(const uint16_t* x, const uint16_t* w, uint64_t position, float theta,
+                             float* q32, uint16_t* q16, cudaStream_t stream);
+
+// Synthetic inputs
+cudaError_t launch_synth_normal(uint16_t* out, size_t count, uint64_t seed, float stddev,
+                                int bf16, cudaStream_t stream);
+cudaError_t launch_synth_keys(uint16_t* rows, size_t tokens, size_t stride_words, uint64_t seed,
+                              float heavy_fraction, float heavy_scale, int rope, float theta,
+                              cudaStream_t stream);
+
+}  // namespace hsb

@@ -1,0 +1,272 @@
+/*
+ * hsb.h -- C ABI of the B200-native selected-KV decode path.
+ *
+ * The path has four stages, each a hand-written sm_100a kernel:
+ *   1. full-GQA key scoring under the HS_FULL_GQA_PIPELINE_F16_V3 contract
+ *      (F16 Q[32,128] . K[N,8,128], query head h -> KV head h/4, channels
+ *      0..127 accumulated in order in FP32 from +0, one RNE rounding to F16);
+ *   2. the gqa_policy selector (head-0 maximum broadcast, alpha margin,
+ *      inclusive count, F16 count/mean, ratio cap, ordered per-head top-k);
+ *   3. the physical union and the packing / gather of selected K/V rows;
+ *   4. flash-decode attention over the gathered K/V.
+ *
+ * Conventions
+ *  - Every pointer named d_* is CUDA device memory (or host memory the GPU
+ *    can address, where a function says so).  Arrays named h_* are host.
+ *  - `stream` is a cudaStream_t passed as void*; NULL means the legacy
+ *    default stream.  Every call only enqueues work on `stream` unless its
+ *    comment says it synchronises.
+ *  - Functions return an hsb_status.  A non-zero status leaves a message,
+ *    worded like the reference exception it stands for, in a thread-local
+ *    buffer read by hsb_last_error().  Errors that only the GPU can see
+ *    (non-finite scores, duplicate IDs, ...) are written to a device status
+ *    word that the caller reads after the stream completes (hsb_*_check()).
+ *  - Workspaces are caller-allocated device memory sized by the matching
+ *    *_workspace_bytes() query; the library allocates nothing per call.
+ *  - Token IDs are uint32 (the reference uses uint64; every ID it admits is
+ *    below 2^32).
+ *
+ * Reference citations are paths inside the HillServe project.
+ */
+#ifndef HSB_H
+#define HSB_H
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HSB_ABI_VERSION 1
+#define HSB_QUERY_HEADS 32
+#define HSB_KV_HEADS 8
+#define HSB_DIM 128
+#define HSB_ROW_WORDS 2048 /* one interleaved KV row: K[8,128] then V[8,128] */
+#define HSB_MAX_VIEWS 8    /* key views per scoring launch (more are split) */
+
+typedef enum hsb_status {
+    HSB_OK = 0,
+    HSB_E_INVALID = 1,   /* null pointer / bad enum / misaligned argument */
+    HSB_E_CUDA = 2,      /* a CUDA runtime call failed */
+    HSB_E_WORKSPACE = 3, /* workspace missing or smaller than required */
+    HSB_E_TIMEOUT = 4,   /* a bounded device wait gave up */
+    HSB_E_NO_DEVICE = 5, /* no sm_100 device / kernel image */
+    /* stage 1 -- policy/full_gqa_cpu.cpp:210-227, smartssd/adapter.hpp:97-104 */
+    HSB_E_SCORE_SHAPE = 10,
+    HSB_E_SCORE_ALIAS = 11,
+    HSB_E_SCORE_V3_TOKENS = 12,
+    /* stage 2 -- policy/gqa_policy.cpp:48-61 (same order of checks) */
+    HSB_E_SEL_SHAPE = 20,
+    HSB_E_SEL_PARAMS = 21,
+    HSB_E_SEL_NONFINITE_HEAD0 = 22,
+    HSB_E_SEL_THRESHOLD = 23,
+    HSB_E_SEL_NONFINITE = 24,
+    HSB_E_SEL_U32 = 25,
+    HSB_E_SEL_COUNT_F16 = 26,
+    HSB_E_SEL_MEAN_F16 = 27,
+    HSB_E_SEL_CAPACITY = 28,
+    /* stage 3 -- runtime/gqa_pack.hpp:14-44, runtime/gqa_prefetch_cuda.cu:217-218 */
+    HSB_E_UNION_BOUNDS = 30,
+    HSB_E_UNION_DUPLICATE = 31,
+    HSB_E_PACK_SHAPE = 40,
+    HSB_E_PACK_PHYSICAL = 41,
+    HSB_E_PACK_SLOTS = 42,
+    HSB_E_PACK_MISSING = 43,
+    HSB_E_MAP_GEOMETRY = 50,
+    HSB_E_MAP_ROW = 51,
+    HSB_E_MAP_MISS = 52,
+    /* prefetch cover -- policy/full_gqa_runtime.cpp:316-333 */
+    HSB_E_COVER_RANGE = 60,
+    HSB_E_COVER_THRESHOLD = 61,
+    HSB_E_COVER_COUNT = 62,
+    HSB_E_COVER_MEAN = 63,
+    /* layer step -- policy/full_gqa_runtime.cpp:573 */
+    HSB_E_ZERO_SELECTION = 70
+} hsb_status;
+
+int hsb_abi_version(void);
+/* Message of the last failing call made by this thread ("" if none). */
+const char* hsb_last_error(void);
+/* Reference-worded message for a status code. */
+const char* hsb_status_message(int status);
+
+/* Device status word written by kernels: 0 = ok, else an hsb_status in the
+ * low 8 bits and the (query head or row) index that raised it above them. */
+typedef struct hsb_device_status {
+    int32_t code;
+    int32_t index;
+} hsb_device_status;
+/* Synchronises `stream`, reads *d_status, sets the last-error message and
+ * returns the status it holds.  Does not clear it. */
+int hsb_status_check(const hsb_device_status* d_status, void* stream);
+
+/* ------------------------------------------------------------------ stage 1
+ * Replaces FullGqaCpuScorer::score (policy/full_gqa_cpu.hpp:43-45,
+ * .cpp:206-250) and score_full_gqa_legacy_cpu (.cpp:109-138): identical bits.
+ * d_q: F16 [32][128]; keys of token t start at view.data + t*stride_words
+ * (stride 1024 = token-major K, 2048 = interleaved K|V rows); tokens of the
+ * views are concatenated in order; d_scores: F16 [32][sum tokens]. */
+typedef struct hsb_key_view {
+    const uint16_t* data;
+    size_t tokens;
+    size_t stride_words;
+} hsb_key_view;
+
+int hsb_score_v3(const uint16_t* d_q, const uint16_t* d_keys, size_t tokens,
+                 size_t stride_words, uint16_t* d_scores, void* stream);
+int hsb_score_views(const uint16_t* d_q, const hsb_key_view* h_views, size_t nviews,
+                    uint16_t* d_scores, void* stream);
+/* The V3 pipeline contract (kernels/full_gqa_pipeline/ABI.json:20-30,
+ * kernel.cpp:237-253): token-major K, 64 <= tokens <= 32768, tokens % 64 == 0;
+ * any other count is rejected before touching memory. */
+int hsb_score_pipeline_v3(const uint16_t* d_q, const uint16_t* d_keys, uint32_t tokens,
+                          uint16_t* d_scores, void* stream);
+/* The runtime's normalisation (policy/full_gqa_runtime.cpp:571):
+ * d_out[i] = F16(F32(d_raw[i]) / sqrtf(128)).  d_out may equal d_raw. */
+int hsb_scale_scores(const uint16_t* d_raw, size_t count, uint16_t* d_out, void* stream);
+
+/* ------------------------------------------------------------------ stage 2
+ * Replaces select_gqa_scores (policy/gqa_policy.hpp:19-21, .cpp:47-70).
+ * d_scores: F16 [heads][stride], tokens [0,valid) are candidates.  With
+ * input_is_raw != 0 the scores are raw dot products and are normalised in the
+ * kernel exactly as hsb_scale_scores does (the runtime's select path,
+ * full_gqa_runtime.cpp:571-572); otherwise they are already normalised.
+ * Outputs: d_ids [heads][kcap] (top-k per head, order key descending then ID
+ * ascending), d_counts [heads] (inclusive threshold counts), *d_result.
+ * kcap must be >= min(floor(valid*ratio), valid). */
+typedef struct hsb_selection {
+    uint32_t k;
+    uint32_t boundary_tied_heads;
+    hsb_device_status status;
+} hsb_selection;
+
+size_t hsb_select_workspace_bytes(size_t heads, size_t stride, size_t valid, size_t kcap);
+int hsb_select(const uint16_t* d_scores, int input_is_raw, size_t heads, size_t stride,
+               size_t valid, float alpha, float ratio, int fp32_counts, uint32_t* d_ids,
+               size_t kcap, uint32_t* d_counts, hsb_selection* d_result, void* d_workspace,
+               size_t workspace_bytes, void* stream);
+/* Synchronises, copies *d_result to *h_result and returns its status. */
+int hsb_selection_read(const hsb_selection* d_result, hsb_selection* h_result, void* stream);
+
+/* History-only prefetch cover (policy/full_gqa_runtime.cpp:299-344): from raw
+ * scores [32][capacity] of tokens [0,position), the per-head top-`bound`
+ * lists that cover every final selection once the current token is added.
+ * d_per_head is [32][cap], cap = min(position, floor((position+1)*0.2f));
+ * d_result->k receives `bound`. */
+int hsb_prefetch_cover(const uint16_t* d_raw, size_t capacity, size_t position, float alpha,
+                       int fp32_counts, uint32_t* d_per_head, size_t cap,
+                       hsb_selection* d_result, void* d_workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* ------------------------------------------------------------------ stage 3
+ * Per-head list sizes are read from d_sizes[h * sizes_stride]; pass
+ * sizes_stride = 0 to give every head d_sizes[0] (e.g. &selection->k). */
+
+/* gqa_physical_union (runtime/gqa_pack.hpp:12-22): sorted unique IDs of the
+ * 32 per-head lists; duplicates within a head or IDs >= visible are errors. */
+size_t hsb_union_workspace_bytes(size_t visible);
+int hsb_union(const uint32_t* d_ids, size_t kstride, const uint32_t* d_sizes,
+              size_t sizes_stride, size_t visible, uint32_t* d_physical,
+              uint32_t* d_physical_count, hsb_device_status* d_status, void* d_workspace,
+              size_t workspace_bytes, void* stream);
+
+/* pack_gqa_workspace (runtime/gqa_pack.hpp:26-58), bit-exact:
+ * K [count][32][128], V [32][128][count] and mask F32 [32][qpad][count]
+ * (qpad = roundup(npositions, 64)) from payload rows (4096 B each, F16 K[8][128]
+ * then V[8][128]) listed in d_physical order.  d_mask may be NULL. */
+size_t hsb_pack_workspace_bytes(uint64_t last_position);
+int hsb_pack(const uint32_t* d_ids, size_t kstride, const uint32_t* d_sizes,
+             size_t sizes_stride, const uint64_t* d_positions, size_t npositions,
+             uint64_t last_position, const uint32_t* d_physical, size_t nphysical,
+             const uint8_t* d_payload, size_t payload_bytes, size_t count, uint16_t* d_k,
+             uint16_t* d_v, float* d_mask, hsb_device_status* d_status, void* d_workspace,
+             size_t workspace_bytes, void* stream);
+
+/* gather_gqa (runtime/gqa_prefetch_cuda.cu:12-22) with deliver's row checks
+ * (:217-218): d_map[h*count+s] >= 0 selects prefetched row, <= -2 miss row
+ * (-2-index), -1 padding (zeros). */
+int hsb_gather_map(const uint16_t* d_prefetched, size_t prefetched_rows,
+                   const uint16_t* d_misses, size_t miss_rows, const int32_t* d_map,
+                   size_t count, uint16_t* d_k, uint16_t* d_v, hsb_device_status* d_status,
+                   void* stream);
+
+/* The device-resident gather: selected rows read straight from an HBM KV
+ * cache (K at d_kcache + id*stride_words, V at d_vcache + id*stride_words)
+ * into the packed layout of hsb_pack.  zero_padding != 0 zero-fills slots
+ * [size_h, count) as the reference does; 0 writes live slots only. */
+int hsb_gather_cache(const uint32_t* d_ids, size_t kstride, const uint32_t* d_sizes,
+                     size_t sizes_stride, const uint16_t* d_kcache, const uint16_t* d_vcache,
+                     size_t stride_words, size_t visible, size_t count, int zero_padding,
+                     uint16_t* d_k, uint16_t* d_v, hsb_device_status* d_status, void* stream);
+
+/* Copies union rows (4096 B each) from a row store the GPU can address --
+ * HBM or mapped pinned host memory (the cold tier) -- into HBM:
+ * d_dst[i] = d_rows[d_physical[i]] for i < *d_count (at most max_rows). */
+int hsb_stage_rows(const uint8_t* d_rows, const uint32_t* d_physical,
+                   const uint32_t* d_count, size_t max_rows, uint8_t* d_dst, void* stream);
+
+/* ------------------------------------------------------------------ stage 4
+ * Attention over the packed workspace (the ggml graph of
+ * runtime/gqa_delivery.cpp:19-20): per query head,
+ * softmax(K.q / sqrt(128) + mask) . V with q F32 [32][128], out F32 [32][128].
+ * Slot validity comes from d_mask (query row 0 of [32][qpad][count]) when it
+ * is non-NULL, else from the per-head sizes. */
+size_t hsb_attention_workspace_bytes(size_t count);
+int hsb_attention_packed(const float* d_q, const uint16_t* d_k, const uint16_t* d_v,
+                         size_t count, const float* d_mask, size_t qpad,
+                         const uint32_t* d_sizes, size_t sizes_stride, float* d_out,
+                         void* d_workspace, size_t workspace_bytes, void* stream);
+/* Dense decode attention over a token-major cache (dense layers,
+ * runtime/gqa_executor.cpp:174-176). */
+size_t hsb_attention_dense_workspace_bytes(size_t tokens);
+int hsb_attention_dense(const float* d_q, const uint16_t* d_kcache, const uint16_t* d_vcache,
+                        size_t tokens, size_t stride_words, float* d_out, void* d_workspace,
+                        size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------- rehearsal query
+ * The rehearsal query producer (patches/llama-b6000-round2.patch:303-317 and
+ * the F16 cast of policy/full_gqa_runtime.cpp:61-64): q = RoPE_position(W x),
+ * x bf16 [4096], W bf16 [4096 out][4096 in], NORM-mode RoPE with base theta.
+ * Writes d_q_f32 [32][128] and/or d_q_f16 (either may be NULL). */
+int hsb_rehearsal_query(const uint16_t* d_x, const uint16_t* d_w, uint64_t position,
+                        float theta, float* d_q_f32, uint16_t* d_q_f16, void* stream);
+
+/* ------------------------------------------------------------- layer step
+ * One selected-KV decode layer, all on `stream` with no host round trip:
+ * score (raw) -> select (raw input) -> gather from the HBM cache into the
+ * packed live-slot layout -> attention.  count (slot capacity per head) must
+ * be >= min(floor(valid*ratio), valid).  d_out receives F32 [32][128];
+ * d_ids/d_counts/d_result as hsb_select.  k == 0 leaves d_out zero and sets
+ * d_result->status to HSB_E_ZERO_SELECTION (the reference throws there). */
+typedef struct hsb_layer_buffers {
+    uint16_t* scores;  /* F16 [32][valid] */
+    uint32_t* ids;     /* [32][count] */
+    uint32_t* counts;  /* [32] */
+    hsb_selection* result;
+    uint16_t* k_packed; /* [count][32][128] */
+    uint16_t* v_packed; /* [32][128][count] */
+    void* workspace;
+    size_t workspace_bytes;
+} hsb_layer_buffers;
+size_t hsb_layer_workspace_bytes(size_t valid, size_t count);
+int hsb_layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_kcache,
+                   const uint16_t* d_vcache, size_t stride_words, size_t valid, float alpha,
+                   float ratio, size_t count, const hsb_layer_buffers* buffers, float* d_out,
+                   void* stream);
+
+/* ------------------------------------------------------ synthetic inputs
+ * Benchmark inputs, not part of the reference interface: seeded F16 normal
+ * values (counter-based hash + Box-Muller).  For K rows, a heavy_fraction of
+ * token rows is multiplied by heavy_scale before rounding, and rope != 0
+ * rotates adjacent channel pairs by position * theta^(-2i/128). */
+int hsb_synth_normal_f16(uint16_t* d_out, size_t count, uint64_t seed, float stddev,
+                         void* stream);
+int hsb_synth_normal_bf16(uint16_t* d_out, size_t count, uint64_t seed, float stddev,
+                          void* stream);
+int hsb_synth_keys(uint16_t* d_rows, size_t tokens, size_t stride_words, uint64_t seed,
+                   float heavy_fraction, float heavy_scale, int rope, float theta,
+                   void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

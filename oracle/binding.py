@@ -1,0 +1,347 @@
+"""numpy front end of the C oracle and of the reference bridge (tests only).
+
+Every function takes and returns numpy arrays; uint16 arrays hold F16 bits.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_SO = HERE / "_build" / "libhs_oracle.so"
+REF_SO = HERE / "_ref" / "libhs_ref.so"
+
+P = C.c_void_p
+SZ = C.c_size_t
+
+_oracle = None
+_ref = None
+
+
+def build(reference_root: str | None = None) -> None:
+    """Builds the oracle (and the reference bridge when its sources exist)."""
+    cmd = ["make", "-s", "-C", str(HERE)]
+    if reference_root:
+        cmd.append(f"R={reference_root}")
+    subprocess.run(cmd, check=True)
+
+
+def _p(a) -> C.c_void_p:
+    return C.c_void_p(0 if a is None else a.ctypes.data)
+
+
+def oracle() -> C.CDLL:
+    global _oracle
+    if _oracle is None:
+        if not ORACLE_SO.exists():
+            build()
+        lib = C.CDLL(str(ORACLE_SO))
+        lib.orc_half_value.restype = C.c_float
+        lib.orc_half_value.argtypes = [C.c_uint16]
+        lib.orc_half_bits.restype = C.c_uint16
+        lib.orc_half_bits.argtypes = [C.c_float]
+        lib.orc_order_key.restype = C.c_uint16
+        lib.orc_order_key.argtypes = [C.c_uint16]
+        lib.orc_score.argtypes = [P, P, SZ, SZ, P, SZ, SZ, C.c_int]
+        lib.orc_scale.argtypes = [P, SZ, P]
+        lib.orc_scale.restype = None
+        lib.orc_select.argtypes = [P, SZ, SZ, SZ, C.c_float, C.c_float, C.c_int, P, SZ, P, P, P]
+        lib.orc_union.argtypes = [P, SZ, P, SZ, P, P]
+        lib.orc_pack.argtypes = [P, SZ, P, P, SZ, P, SZ, P, SZ, SZ, P, P, P]
+        lib.orc_gather_map.argtypes = [P, SZ, P, SZ, P, SZ, P, P]
+        lib.orc_prefetch_cover.argtypes = [P, SZ, SZ, C.c_float, C.c_int, P, P, P, P]
+        lib.orc_attention_packed.argtypes = [P, P, P, SZ, SZ, P, P]
+        lib.orc_attention_packed.restype = None
+        lib.orc_attention_compact.argtypes = [P, P, SZ, P, P, P]
+        lib.orc_attention_compact.restype = None
+        lib.orc_attention_dense.argtypes = [P, P, SZ, SZ, P, P]
+        lib.orc_attention_dense.restype = None
+        lib.orc_attention_dense_f32.argtypes = [P, P, SZ, SZ, P, P, C.c_int]
+        lib.orc_attention_dense_f32.restype = None
+        lib.orc_attention_packed_f32.argtypes = [P, P, P, SZ, SZ, P, P, C.c_int]
+        lib.orc_attention_packed_f32.restype = None
+        lib.orc_rehearsal.argtypes = [P, P, C.c_uint64, C.c_double, P]
+        lib.orc_rehearsal.restype = None
+        _oracle = lib
+    return _oracle
+
+
+def reference_available() -> bool:
+    return REF_SO.exists()
+
+
+def ref() -> C.CDLL:
+    global _ref
+    if _ref is None:
+        lib = C.CDLL(str(REF_SO))
+        lib.ref_half_value.restype = C.c_float
+        lib.ref_half_value.argtypes = [C.c_uint16]
+        lib.ref_half_bits.restype = C.c_uint16
+        lib.ref_half_bits.argtypes = [C.c_float]
+        lib.ref_scorer_create.restype = P
+        lib.ref_scorer_create.argtypes = [C.c_uint, C.c_int, C.c_char_p, SZ]
+        lib.ref_scorer_destroy.argtypes = [P]
+        lib.ref_scorer_name.restype = C.c_char_p
+        lib.ref_scorer_name.argtypes = [P]
+        lib.ref_scorer_score.argtypes = [P, P, P, P, P, SZ, P, SZ, C.c_char_p, SZ]
+        lib.ref_legacy_score.argtypes = [P, P, SZ, SZ, C.c_uint, P, C.c_char_p, SZ]
+        lib.ref_scale.argtypes = [P, SZ, P]
+        lib.ref_scale.restype = None
+        lib.ref_select.argtypes = [P, SZ, SZ, SZ, C.c_float, C.c_float, C.c_int, P, SZ, P, P, P, C.c_char_p, SZ]
+        lib.ref_union.argtypes = [P, SZ, P, SZ, P, P, C.c_char_p, SZ]
+        lib.ref_pack.argtypes = [P, SZ, P, P, SZ, P, SZ, P, SZ, SZ, P, P, P, C.c_char_p, SZ]
+        _ref = lib
+    return _ref
+
+
+class OracleError(RuntimeError):
+    def __init__(self, code: int, message: str = ""):
+        super().__init__(message or f"oracle error {code}")
+        self.code = code
+
+
+# ------------------------------------------------------------------ oracle
+def half_bits(x: float) -> int:
+    return int(oracle().orc_half_bits(float(x)))
+
+
+def half_value(h: int) -> float:
+    return float(oracle().orc_half_value(int(h)))
+
+
+def score(q: np.ndarray, k: np.ndarray, n: int, stride: int, threads: int = 8) -> np.ndarray:
+    q = np.ascontiguousarray(q, dtype=np.uint16)
+    k = np.ascontiguousarray(k, dtype=np.uint16)
+    out = np.empty((32, n), dtype=np.uint16)
+    rc = oracle().orc_score(_p(q), _p(k), n, stride, _p(out), n, 0, threads)
+    if rc:
+        raise OracleError(rc)
+    return out
+
+
+def score_views(q: np.ndarray, views: list, threads: int = 8) -> np.ndarray:
+    """views: list of (array, first_token_word_offset, tokens, stride)."""
+    total = sum(v[2] for v in views)
+    out = np.empty((32, total), dtype=np.uint16)
+    q = np.ascontiguousarray(q, dtype=np.uint16)
+    col = 0
+    for arr, off, tokens, stride in views:
+        base = arr.ctypes.data + 2 * off
+        rc = oracle().orc_score(_p(q), C.c_void_p(base), tokens, stride, _p(out), total, col, threads)
+        if rc:
+            raise OracleError(rc)
+        col += tokens
+    return out
+
+
+def scale(raw: np.ndarray) -> np.ndarray:
+    raw = np.ascontiguousarray(raw, dtype=np.uint16)
+    out = np.empty_like(raw)
+    oracle().orc_scale(_p(raw), raw.size, _p(out))
+    return out
+
+
+def select(scaled: np.ndarray, heads: int, stride: int, valid: int, alpha: float, ratio: float,
+           fp32_counts: bool = False):
+    """Returns (ids [heads, k] uint64, counts [heads] uint32, k, tied)."""
+    scaled = np.ascontiguousarray(scaled, dtype=np.uint16)
+    kcap = max(1, min(int(np.floor(float(valid) * float(np.float32(ratio)))), valid)) if valid else 1
+    ids = np.zeros((max(heads, 1), kcap), dtype=np.uint64)
+    counts = np.zeros(max(heads, 1), dtype=np.uint32)
+    k = C.c_size_t()
+    tied = C.c_size_t()
+    rc = oracle().orc_select(_p(scaled), heads, stride, valid, C.c_float(alpha), C.c_float(ratio), int(fp32_counts),
+                             _p(ids), kcap, _p(counts), C.byref(k), C.byref(tied))
+    if rc:
+        raise OracleError(rc)
+    return ids[:, : k.value], counts, k.value, tied.value
+
+
+def union(ids: np.ndarray, sizes, visible: int) -> np.ndarray:
+    ids = np.ascontiguousarray(ids, dtype=np.uint64)
+    sz = np.ascontiguousarray(sizes, dtype=np.uint64)
+    out = np.zeros(max(1, visible), dtype=np.uint64)
+    cnt = C.c_size_t()
+    rc = oracle().orc_union(_p(ids), ids.shape[1], _p(sz), visible, _p(out), C.byref(cnt))
+    if rc:
+        raise OracleError(rc)
+    return out[: cnt.value]
+
+
+def pack(ids: np.ndarray, sizes, positions, physical, payload: np.ndarray, count: int):
+    ids = np.ascontiguousarray(ids, dtype=np.uint64)
+    sz = np.ascontiguousarray(sizes, dtype=np.uint64)
+    pos = np.ascontiguousarray(positions, dtype=np.uint64)
+    phys = np.ascontiguousarray(physical, dtype=np.uint64)
+    payload = np.ascontiguousarray(payload, dtype=np.uint8)
+    qpad = (len(pos) + 63) // 64 * 64
+    k = np.empty(count * 4096, dtype=np.uint16)
+    v = np.empty(count * 4096, dtype=np.uint16)
+    mask = np.empty(count * qpad * 32, dtype=np.float32)
+    rc = oracle().orc_pack(_p(ids), ids.shape[1], _p(sz), _p(pos), len(pos), _p(phys), len(phys), _p(payload),
+                           payload.size, count, _p(k), _p(v), _p(mask))
+    if rc:
+        raise OracleError(rc)
+    return k, v, mask
+
+
+def gather_map(prefetched: np.ndarray, prows: int, misses: np.ndarray, mrows: int, row_map: np.ndarray, count: int):
+    k = np.empty(count * 4096, dtype=np.uint16)
+    v = np.empty(count * 4096, dtype=np.uint16)
+    row_map = np.ascontiguousarray(row_map, dtype=np.int32)
+    rc = oracle().orc_gather_map(_p(prefetched), prows, _p(misses), mrows, _p(row_map), count, _p(k), _p(v))
+    if rc:
+        raise OracleError(rc)
+    return k, v
+
+
+def prefetch_cover(raw: np.ndarray, capacity: int, position: int, alpha: float, fp32_counts: bool = False):
+    raw = np.ascontiguousarray(raw, dtype=np.uint16)
+    cap = min(position, int(np.floor(float(position + 1) * float(np.float32(0.2)))))
+    per_head = np.zeros((32, max(cap, 1)), dtype=np.uint64)
+    physical = np.zeros(max(position, 1), dtype=np.uint64)
+    bound = C.c_size_t()
+    nphys = C.c_size_t()
+    rc = oracle().orc_prefetch_cover(_p(raw), capacity, position, C.c_float(alpha), int(fp32_counts), _p(per_head),
+                                     C.byref(bound), _p(physical), C.byref(nphys))
+    if rc:
+        raise OracleError(rc)
+    return per_head[:, : bound.value], physical[: nphys.value]
+
+
+def attention_packed(k, v, mask, count: int, qpad: int, q) -> np.ndarray:
+    out = np.empty((32, 128), dtype=np.float64)
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    oracle().orc_attention_packed(_p(k), _p(v), _p(mask), count, qpad, _p(q), _p(out))
+    return out
+
+
+def attention_compact(k, v, count: int, lengths, q) -> np.ndarray:
+    out = np.empty((32, 128), dtype=np.float64)
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    lengths = np.ascontiguousarray(lengths, dtype=np.uint32)
+    oracle().orc_attention_compact(_p(k), _p(v), count, _p(lengths), _p(q), _p(out))
+    return out
+
+
+def attention_dense(kc, vc, n: int, stride: int, q) -> np.ndarray:
+    out = np.empty((32, 128), dtype=np.float64)
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    oracle().orc_attention_dense(_p(kc), _p(vc), n, stride, _p(q), _p(out))
+    return out
+
+
+def attention_dense_fast(kc, vc, n: int, q, threads: int) -> np.ndarray:
+    """CPU-baseline dense attention (float, threads over heads)."""
+    out = np.empty((32, 128), dtype=np.float32)
+    oracle().orc_attention_dense_f32(_p(kc), _p(vc), n, 1024, _p(np.ascontiguousarray(q, dtype=np.float32)),
+                                     _p(out), threads)
+    return out
+
+
+def attention_packed_fast(k, v, mask, count: int, q, threads: int, qpad: int = 64) -> np.ndarray:
+    """CPU-baseline attention over the packed workspace (float)."""
+    out = np.empty((32, 128), dtype=np.float32)
+    oracle().orc_attention_packed_f32(_p(k), _p(v), _p(mask), count, qpad,
+                                      _p(np.ascontiguousarray(q, dtype=np.float32)), _p(out), threads)
+    return out
+
+
+def rehearsal(x_bf16, w_bf16, position: int, theta: float = 500000.0) -> np.ndarray:
+    out = np.empty(4096, dtype=np.float64)
+    oracle().orc_rehearsal(_p(np.ascontiguousarray(x_bf16, dtype=np.uint16)),
+                           _p(np.ascontiguousarray(w_bf16, dtype=np.uint16)), position, theta, _p(out))
+    return out
+
+
+# ------------------------------------------------------------- reference
+def _err():
+    return C.create_string_buffer(512)
+
+
+class ReferenceError_(RuntimeError):
+    pass
+
+
+class RefScorer:
+    """The reference FullGqaCpuScorer (implementation 0 automatic, 1 scalar, 2 avx2)."""
+
+    def __init__(self, threads: int, implementation: int = 0):
+        e = _err()
+        self.h = ref().ref_scorer_create(threads, implementation, e, 512)
+        if not self.h:
+            raise ReferenceError_(e.value.decode())
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            ref().ref_scorer_destroy(self.h)
+
+    def name(self) -> str:
+        return ref().ref_scorer_name(self.h).decode()
+
+    def score(self, q: np.ndarray, views: list) -> np.ndarray:
+        """views: list of (array, word offset, tokens, stride)."""
+        n = len(views)
+        data = (C.c_void_p * max(n, 1))(*[C.c_void_p(a.ctypes.data + 2 * off) for a, off, _, _ in views])
+        tokens = (C.c_size_t * max(n, 1))(*[t for _, _, t, _ in views])
+        strides = (C.c_size_t * max(n, 1))(*[s for _, _, _, s in views])
+        total = sum(t for _, _, t, _ in views)
+        out = np.empty((32, max(total, 1)), dtype=np.uint16)
+        q = np.ascontiguousarray(q, dtype=np.uint16)
+        e = _err()
+        if ref().ref_scorer_score(self.h, _p(q), data, tokens, strides, n, _p(out), out.size, e, 512):
+            raise ReferenceError_(e.value.decode())
+        return out[:, :total]
+
+
+def ref_select(scaled: np.ndarray, heads: int, stride: int, valid: int, alpha: float, ratio: float,
+               fp32_counts: bool = False):
+    scaled = np.ascontiguousarray(scaled, dtype=np.uint16)
+    kcap = max(1, valid)
+    ids = np.zeros((heads, kcap), dtype=np.uint64)
+    counts = np.zeros(heads, dtype=np.uint32)
+    k = C.c_size_t()
+    tied = C.c_size_t()
+    e = _err()
+    if ref().ref_select(_p(scaled), heads, stride, valid, C.c_float(alpha), C.c_float(ratio), int(fp32_counts),
+                        _p(ids), kcap, _p(counts), C.byref(k), C.byref(tied), e, 512):
+        raise ReferenceError_(e.value.decode())
+    return ids[:, : k.value], counts, k.value, tied.value
+
+
+def ref_scale(raw: np.ndarray) -> np.ndarray:
+    raw = np.ascontiguousarray(raw, dtype=np.uint16)
+    out = np.empty_like(raw)
+    ref().ref_scale(_p(raw), raw.size, _p(out))
+    return out
+
+
+def ref_union(ids: np.ndarray, sizes, visible: int) -> np.ndarray:
+    ids = np.ascontiguousarray(ids, dtype=np.uint64)
+    sz = np.ascontiguousarray(sizes, dtype=np.uint64)
+    out = np.zeros(max(1, visible), dtype=np.uint64)
+    cnt = C.c_size_t()
+    e = _err()
+    if ref().ref_union(_p(ids), ids.shape[1], _p(sz), visible, _p(out), C.byref(cnt), e, 512):
+        raise ReferenceError_(e.value.decode())
+    return out[: cnt.value]
+
+
+def ref_pack(ids, sizes, positions, physical, payload, count: int):
+    ids = np.ascontiguousarray(ids, dtype=np.uint64)
+    sz = np.ascontiguousarray(sizes, dtype=np.uint64)
+    pos = np.ascontiguousarray(positions, dtype=np.uint64)
+    phys = np.ascontiguousarray(physical, dtype=np.uint64)
+    payload = np.ascontiguousarray(payload, dtype=np.uint8)
+    qpad = (len(pos) + 63) // 64 * 64
+    k = np.empty(count * 4096, dtype=np.uint16)
+    v = np.empty(count * 4096, dtype=np.uint16)
+    mask = np.empty(count * qpad * 32, dtype=np.float32)
+    e = _err()
+    if ref().ref_pack(_p(ids), ids.shape[1], _p(sz), _p(pos), len(pos), _p(phys), len(phys), _p(payload),
+                      payload.size, count, _p(k), _p(v), _p(mask), e, 512):
+        raise ReferenceError_(e.value.decode())
+    return k, v, mask

@@ -1,0 +1,153 @@
+// ref_capi.cpp -- TEST / BASELINE INFRASTRUCTURE ONLY.
+//
+// A thin C-ABI bridge, compiled together with the UNMODIFIED reference
+// HillServe sources (policy/host_policy.cpp, policy/full_gqa_cpu.cpp,
+// policy/gqa_policy.cpp, smartssd/adapter.cpp and the header-only
+// runtime/gqa_pack.hpp) into oracle/_ref/libhs_ref.so by oracle/Makefile.
+// It lets the tests pin the C oracle against the reference's own code on
+// seeded inputs, and lets bench.py time the reference CPU path.  Nothing in
+// the product links it.
+#include "policy/full_gqa_cpu.hpp"
+#include "policy/gqa_policy.hpp"
+#include "policy/host_policy.hpp"
+#include "runtime/gqa_pack.hpp"
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <exception>
+#include <string>
+#include <vector>
+
+namespace {
+void copy_error(const std::exception& e, char* err, std::size_t errlen) {
+    if (err && errlen) {
+        std::strncpy(err, e.what(), errlen - 1);
+        err[errlen - 1] = 0;
+    }
+}
+}  // namespace
+
+extern "C" {
+
+float ref_half_value(std::uint16_t h) { return hillserve::half_value(h); }
+std::uint16_t ref_half_bits(float f) { return hillserve::half_bits(f); }
+
+// FullGqaCpuScorer(threads, implementation) -- policy/full_gqa_cpu.hpp:27-50.
+// implementation: 0 automatic, 1 scalar, 2 avx2_f16c.
+void* ref_scorer_create(unsigned threads, int implementation, char* err, std::size_t errlen) {
+    try {
+        return new hillserve::FullGqaCpuScorer(
+            threads, static_cast<hillserve::FullGqaCpuImplementation>(implementation));
+    } catch (const std::exception& e) {
+        copy_error(e, err, errlen);
+        return nullptr;
+    }
+}
+void ref_scorer_destroy(void* scorer) { delete static_cast<hillserve::FullGqaCpuScorer*>(scorer); }
+const char* ref_scorer_name(void* scorer) {
+    return static_cast<hillserve::FullGqaCpuScorer*>(scorer)->implementation_name();
+}
+
+// score(query, views, output); views given as parallel arrays.  out receives
+// 32*sum(tokens) scores, head-major.
+int ref_scorer_score(void* scorer, const std::uint16_t* q, const std::uint16_t* const* data,
+                     const std::size_t* tokens, const std::size_t* strides, std::size_t nviews,
+                     std::uint16_t* out, std::size_t out_capacity, char* err, std::size_t errlen) {
+    try {
+        static thread_local std::vector<std::uint16_t> query, output;
+        query.assign(q, q + 4096);
+        std::vector<hillserve::FullGqaKeyView> views(nviews);
+        for (std::size_t i = 0; i < nviews; ++i) views[i] = {data[i], tokens[i], strides[i]};
+        static_cast<hillserve::FullGqaCpuScorer*>(scorer)->score(query, views, output);
+        if (output.size() > out_capacity) throw std::runtime_error("bridge output capacity");
+        std::memcpy(out, output.data(), output.size() * 2);
+        return 0;
+    } catch (const std::exception& e) {
+        copy_error(e, err, errlen);
+        return -1;
+    }
+}
+
+// score_full_gqa_legacy_cpu -- policy/full_gqa_cpu.cpp:109-138
+int ref_legacy_score(const std::uint16_t* q, const std::uint16_t* k, std::size_t n,
+                     std::size_t stride, unsigned threads, std::uint16_t* out, char* err,
+                     std::size_t errlen) {
+    try {
+        std::vector<std::uint16_t> query(q, q + 4096);
+        auto result = hillserve::score_full_gqa_legacy_cpu(query, k, n, stride, threads);
+        std::memcpy(out, result.data(), result.size() * 2);
+        return 0;
+    } catch (const std::exception& e) {
+        copy_error(e, err, errlen);
+        return -1;
+    }
+}
+
+// The runtime's score scaling -- policy/full_gqa_runtime.cpp:571
+void ref_scale(const std::uint16_t* raw, std::size_t count, std::uint16_t* out) {
+    for (std::size_t i = 0; i < count; ++i)
+        out[i] = hillserve::half_bits(hillserve::half_value(raw[i]) / std::sqrt(128.f));
+}
+
+// select_gqa_scores -- policy/gqa_policy.hpp:19-21.  ids is [heads][kcap].
+int ref_select(const std::uint16_t* scaled, std::size_t heads, std::size_t stride,
+               std::size_t valid, float alpha, float ratio, int fp32_counts, std::uint64_t* ids,
+               std::size_t kcap, std::uint32_t* counts, std::size_t* k_out,
+               std::size_t* tied_out, char* err, std::size_t errlen) {
+    try {
+        std::vector<std::uint16_t> scores(scaled, scaled + heads * stride);
+        auto s = hillserve::policy::select_gqa_scores(scores, heads, stride, valid, alpha, ratio,
+                                                      fp32_counts != 0);
+        if (s.k > kcap) throw std::runtime_error("bridge ids capacity");
+        for (std::size_t h = 0; h < heads; ++h) {
+            counts[h] = s.counts[h];
+            for (std::size_t j = 0; j < s.k; ++j) ids[h * kcap + j] = s.ids[h][j];
+        }
+        *k_out = s.k;
+        *tied_out = s.boundary_tied_heads;
+        return 0;
+    } catch (const std::exception& e) {
+        copy_error(e, err, errlen);
+        return -1;
+    }
+}
+
+// gqa_physical_union -- runtime/gqa_pack.hpp:12-22
+int ref_union(const std::uint64_t* ids, std::size_t kstride, const std::size_t* sizes,
+              std::size_t visible, std::uint64_t* physical, std::size_t* count, char* err,
+              std::size_t errlen) {
+    try {
+        std::vector<std::vector<std::uint64_t>> heads(32);
+        for (std::size_t h = 0; h < 32; ++h)
+            heads[h].assign(ids + h * kstride, ids + h * kstride + sizes[h]);
+        auto u = hillserve::gqa_physical_union(heads, visible);
+        std::memcpy(physical, u.data(), u.size() * 8);
+        *count = u.size();
+        return 0;
+    } catch (const std::exception& e) {
+        copy_error(e, err, errlen);
+        return -1;
+    }
+}
+
+// pack_gqa_workspace -- runtime/gqa_pack.hpp:26-58
+int ref_pack(const std::uint64_t* ids, std::size_t kstride, const std::size_t* sizes,
+             const std::uint64_t* positions, std::size_t npos, const std::uint64_t* physical,
+             std::size_t nphys, const std::uint8_t* payload, std::size_t payload_bytes,
+             std::size_t count, std::uint16_t* k, std::uint16_t* v, float* mask, char* err,
+             std::size_t errlen) {
+    try {
+        std::vector<std::vector<std::uint64_t>> heads(32);
+        for (std::size_t h = 0; h < 32; ++h)
+            heads[h].assign(ids + h * kstride, ids + h * kstride + sizes[h]);
+        std::vector<std::uint64_t> pos(positions, positions + npos), phys(physical, physical + nphys);
+        std::vector<std::uint8_t> bytes(payload, payload + payload_bytes);
+        hillserve::pack_gqa_workspace(heads, pos, phys, bytes, count, k, v, mask);
+        return 0;
+    } catch (const std::exception& e) {
+        copy_error(e, err, errlen);
+        return -1;
+    }
+}
+}

@@ -1,0 +1,144 @@
+"""Generates the golden fixtures in tests/golden/ by running the REFERENCE's
+own CPU code (oracle/_ref/libhs_ref.so, compiled from the HillServe sources by
+oracle/Makefile) on seeded inputs.  Run here, where the reference sources
+exist:
+
+    make -C oracle && python tests/golden/make_golden.py
+
+Inputs are regenerated bit-exactly from their seeds by tests/inputs.py, so
+the fixtures hold only input digests and the reference's outputs.
+"""
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parents[2]
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests"))
+
+from oracle import binding as ob  # noqa: E402
+import inputs  # noqa: E402
+
+OUT = Path(__file__).resolve().parent
+ALPHAS = (0.1, 5.0, 10.0, 20.0, 50.0)
+
+
+def ref_scores(q, k, n, stride, threads=8):
+    scorer = ob.RefScorer(threads, 0)
+    return scorer.score(q, [(k, 0, n, stride)])
+
+
+def scorer_vectors():
+    """The reference scorer test's own vectors (full_gqa_cpu_tests.cpp:76-86)."""
+    rng = inputs.XorShift32(0x7F123451)
+    out = {}
+    for n in (1, 2, 7, 8, 9, 17, 65, 129):
+        for stride in (1024, 2048):
+            q, data = inputs.cpu_test_case(rng, n, stride)
+            s = ref_scores(q, data, n, stride)
+            out[f"n{n}_s{stride}"] = (inputs.digest(q, data), inputs.digest(s))
+            if n >= 9:  # mixed views: tokens 7-8, 0-2, 1
+                views = [(data, 7 * stride, 2, stride), (data, 0, 3, stride), (data, stride, 1, stride)]
+                mv = ob.RefScorer(2, 0).score(q, views)
+                out[f"n{n}_s{stride}_views"] = (inputs.digest(q, data), inputs.digest(mv))
+    return out
+
+
+def main() -> None:
+    assert ob.reference_available(), "build oracle/_ref first (make -C oracle)"
+    # ---- 1. reference scorer test vectors
+    vec = scorer_vectors()
+    names = sorted(vec)
+    np.savez_compressed(OUT / "scorer_vectors.npz", names=np.array(names),
+                        input_digest=np.array([vec[n][0] for n in names]),
+                        score_digest=np.array([vec[n][1] for n in names]))
+
+    # ---- 2. config 1 (N=4096, seed 0) + alpha sweep, and config-3 lengths
+    for n in (64, 1024, 4096, 16384):
+        q, k, heavy = inputs.config1(n, seed=0)
+        raw = ref_scores(q, k, n, 1024)
+        scaled = ob.ref_scale(raw)
+        fields = dict(n=n, input_digest=inputs.digest(q, k), raw_digest=inputs.digest(raw),
+                      scaled_digest=inputs.digest(scaled), alphas=np.array(ALPHAS, dtype=np.float32))
+        if n <= 1024:
+            fields["raw"] = raw  # small enough to keep verbatim
+        for a in ALPHAS:
+            ids, counts, kk, tied = ob.ref_select(scaled, 32, n, n, a, 0.2)
+            tag = f"a{a:g}".replace(".", "p")
+            fields[f"{tag}_k"] = kk
+            fields[f"{tag}_tied"] = tied
+            fields[f"{tag}_counts"] = counts
+            fields[f"{tag}_ids_digest"] = inputs.digest(ids.astype(np.uint32))
+            fields[f"{tag}_ids_head"] = ids[:, : min(kk, 64)].astype(np.uint32)
+        np.savez_compressed(OUT / f"config1_n{n}.npz", **fields)
+        print("config1", n, {a: int(fields[f"a{a:g}".replace('.', 'p') + '_k']) for a in ALPHAS})
+
+    # ---- 3. random selector trials (structure of gqa_policy_tests.cpp:49-59)
+    rng = inputs.XorShift32(1741)
+    sel = {}
+    for trial in range(24):
+        heads, n, stride = 32, 257, 288
+        x = np.full(heads * stride, inputs.f16_bits(np.float32(1000.0)), dtype=np.uint16)
+        for h in range(heads):
+            for t in range(n):
+                if t % 17 == 0:
+                    x[h * stride + t] = 0 if t % 2 else 0x8000
+                else:
+                    x[h * stride + t] = inputs.f16_bits(np.float32((int(rng() % 97) - 48) / 2))
+        ids, counts, kk, tied = ob.ref_select(x, heads, stride, n, 10.0, 0.2)
+        sel[f"t{trial}"] = (inputs.digest(x), kk, tied, inputs.digest(ids.astype(np.uint64)), inputs.digest(counts))
+    names = sorted(sel)
+    np.savez_compressed(OUT / "select_trials.npz", names=np.array(names),
+                        input_digest=np.array([sel[n][0] for n in names]),
+                        k=np.array([sel[n][1] for n in names]), tied=np.array([sel[n][2] for n in names]),
+                        ids_digest=np.array([sel[n][3] for n in names]),
+                        counts_digest=np.array([sel[n][4] for n in names]))
+
+    # ---- 4. pack / union trials (structure of gqa_pack_tests.cpp:15-39)
+    pk = {}
+    for trial in range(16):
+        case = pack_case(trial)
+        ids, sizes, positions, rows, payload, slots = case
+        k, v, mask = ob.ref_pack(ids, sizes, positions, rows, payload, slots)
+        u = ob.ref_union(ids, sizes, len(rows))
+        pk[f"t{trial:02d}"] = (inputs.digest(ids, sizes, positions, rows, payload), inputs.digest(k), inputs.digest(v),
+                               inputs.digest(mask), inputs.digest(u))
+    names = sorted(pk)
+    np.savez_compressed(OUT / "pack_trials.npz", names=np.array(names),
+                        input_digest=np.array([pk[n][0] for n in names]),
+                        k_digest=np.array([pk[n][1] for n in names]), v_digest=np.array([pk[n][2] for n in names]),
+                        mask_digest=np.array([pk[n][3] for n in names]),
+                        union_digest=np.array([pk[n][4] for n in names]))
+    print("fixtures written to", OUT)
+
+
+def pack_case(trial: int):
+    """A seeded pack case: n rows in shuffled physical order, per-head
+    shuffled selections (full or truncated), two query positions."""
+    rng = inputs.XorShift32(781 + 7919 * trial)
+    n = 65 + trial * 4
+    slots = (n + 31) // 32 * 32
+    rows = np.arange(n, dtype=np.uint64)
+    for i in range(n - 1, 0, -1):  # Fisher-Yates with the xorshift stream
+        j = rng() % (i + 1)
+        rows[i], rows[j] = rows[j], rows[i]
+    payload = np.array([rng() & 0xFF for _ in range(n * 4096)], dtype=np.uint8)
+    ids = np.zeros((32, n), dtype=np.uint64)
+    sizes = np.zeros(32, dtype=np.uint64)
+    for h in range(32):
+        head = rows.copy()
+        for i in range(n - 1, 0, -1):
+            j = rng() % (i + 1)
+            head[i], head[j] = head[j], head[i]
+        size = n if trial % 2 == 0 else 1 + rng() % n
+        ids[h, :size] = head[:size]
+        sizes[h] = size
+    positions = np.array([n // 2, n - 1], dtype=np.uint64)
+    return ids, sizes, positions, rows, payload, slots
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,119 @@
+"""End-to-end on the GPU: the rehearsal query producer, the prefetch cover, and
+the fused selected-KV layer step (score -> select -> gather -> attention)
+against the oracle chain (scores, IDs and gathered K/V bit-exact, attention
+within 2e-3)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import inputs
+from conftest import dev_u16, host_u16
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+
+
+def _t(a, dtype):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dtype).to("cuda")
+
+
+def test_rehearsal_query(cuda, ob):
+    """Config 4's producer: x bf16 ~ N(0,1), W bf16 ~ N(0,0.02), RoPE at N.
+    Parity is unpinned (ggml); the oracle is FP64.  The F16 output is the RNE
+    cast of the F32 output, bit-exactly."""
+    import torch
+
+    x = torch.randn(4096, dtype=torch.float32).to(torch.bfloat16)
+    w = (torch.randn(4096, 4096, dtype=torch.float32) * 0.02).to(torch.bfloat16)
+    for position in (0, 1, 4097, 32768):
+        q32, q16 = cuda.rehearsal_query(x.cuda(), w.cuda(), position, 500000.0)
+        torch.cuda.synchronize()
+        want = ob.rehearsal(x.view(torch.int16).numpy().view(np.uint16), w.view(torch.int16).numpy().view(np.uint16),
+                            position, 500000.0)
+        got = q32.cpu().numpy().reshape(-1).astype(np.float64)
+        assert np.max(np.abs(got - want)) <= 1e-4 * np.max(np.abs(want))
+        assert np.array_equal(host_u16(q16).reshape(-1), q32.cpu().numpy().reshape(-1).astype(np.float16).view(np.uint16))
+
+
+@pytest.mark.parametrize("position,layer", [(128, 0), (129, 2), (140, 1), (1000, 3)])
+def test_prefetch_cover(cuda, ob, position, layer):
+    import torch
+    from test_oracle_pin import _cover_key
+
+    capacity = max(192, position + 8)
+    raw = np.zeros(32 * capacity, dtype=np.uint16)
+    for h in range(32):
+        for t in range(position + 1):
+            raw[h * capacity + t] = ob.half_bits(_cover_key(layer, t, h // 4, 0) + (t % 7) * 0.01 * h)
+    per_head, physical = cuda.prefetch_cover(dev_u16(raw), capacity, position, 5.0)
+    torch.cuda.synchronize()
+    wper, wphys = ob.prefetch_cover(raw, capacity, position, 5.0)
+    assert np.array_equal(per_head.cpu().numpy().astype(np.uint64), wper)
+    assert np.array_equal(physical.cpu().numpy().astype(np.uint64), wphys)
+
+
+def oracle_layer(ob, q16, q32, k, v, n, alpha):
+    raw = ob.score(q16, k, n, 1024)
+    scaled = ob.scale(raw)
+    ids, counts, kk, tied = ob.select(scaled, 32, n, n, alpha, 0.2)
+    return raw, ids, counts, kk
+
+
+@pytest.mark.parametrize("n,alpha", [(4096, 10.0), (4096, 5.0), (4096, 0.1), (16384, 10.0), (32768, 10.0),
+                                     (2000, 50.0)])
+def test_layer_step(cuda, ob, n, alpha):
+    import torch
+
+    q16, k, _ = inputs.config1(n, seed=1)
+    v = inputs.values(1, n)
+    q32 = np.frombuffer(q16.astype(np.uint16).tobytes(), dtype=np.float16).astype(np.float32)
+    layer = cuda.SelectedKVLayer(n, alpha)
+    out = layer(dev_u16(q16), _t(q32, torch.float32), dev_u16(k), dev_u16(v))
+    sel = layer.selection()
+    raw, ids, counts, kk = oracle_layer(ob, q16, q32, k, v, n, alpha)
+    assert np.array_equal(host_u16(layer.scores), raw)
+    assert sel.k == kk
+    assert np.array_equal(layer.counts.cpu().numpy().astype(np.uint32), counts)
+    if kk == 0:
+        assert sel.status.code == 70  # the reference throws "zero selection" here
+        assert float(out.abs().max()) == 0.0
+        return
+    assert sel.status.code == 0
+    assert np.array_equal(layer.ids[:, :kk].cpu().numpy().astype(np.uint64), ids)
+    count = layer.count
+    payload = inputs.interleave(k, v, n).view(np.uint8)
+    wk, wv, _ = ob.pack(ids, np.full(32, kk), [n - 1], np.arange(n, dtype=np.uint64), payload, count)
+    gk = host_u16(layer.k_packed).reshape(count, 32, 128)[:kk]
+    assert np.array_equal(gk, wk.reshape(count, 32, 128)[:kk])
+    gv = host_u16(layer.v_packed).reshape(32, 128, count)[:, :, :kk]
+    assert np.array_equal(gv, wv.reshape(32, 128, count)[:, :, :kk])
+    want = ob.attention_compact(wk, wv, count, np.full(32, kk, dtype=np.uint32), q32)
+    got = out.cpu().numpy().astype(np.float64)
+    assert np.max(np.abs(got - want)) <= TOL * np.max(np.abs(want))
+
+
+def test_layer_step_repeatable_in_graph(cuda, ob):
+    """The layer step has no host round trip, so it captures into a CUDA
+    graph; replays give identical bits."""
+    import torch
+
+    n, alpha = 4096, 10.0
+    q16, k, _ = inputs.config1(n, seed=2)
+    v = inputs.values(2, n)
+    q32 = np.frombuffer(q16.astype(np.uint16).tobytes(), dtype=np.float16).astype(np.float32)
+    layer = cuda.SelectedKVLayer(n, alpha)
+    qd, q32d, kd, vd = dev_u16(q16), _t(q32, torch.float32), dev_u16(k), dev_u16(v)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        first = layer(qd, q32d, kd, vd).clone()
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        layer(qd, q32d, kd, vd)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(layer.out, first)
