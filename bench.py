@@ -129,6 +129,7 @@ class Model:
         self.q32.copy_(self.q16.view(torch.float16).float())
         self.count = hsb.select_kmax(tokens, 0.2)
         self.scores = torch.empty((HEADS, tokens), dtype=torch.int16, device=dev)
+        self.keys = torch.empty((HEADS, tokens), dtype=torch.int16, device=dev)
         self.ids = torch.empty((layers, HEADS, self.count), dtype=torch.int32, device=dev)
         self.counts = torch.zeros((layers, HEADS), dtype=torch.int32, device=dev)
         self.results = torch.zeros((layers, 4), dtype=torch.int32, device=dev)
@@ -160,10 +161,10 @@ class Model:
             e = self.ev[l - DENSE]
             res = self.results[l]
             e[0].record(stream)
-            rc = lib.hsb_score_v3(P(self.q16[l]), P(self.kc[l]), n, 1024, P(self.scores), s)
+            rc = lib.hsb_score_with_keys(P(self.q16[l]), P(self.kc[l]), n, 1024, P(self.scores), P(self.keys), s)
             e[1].record(stream)
-            rc |= lib.hsb_select(P(self.scores), 1, HEADS, n, n, self.alpha, 0.2, 0, P(self.ids[l]), self.count,
-                                 P(self.counts[l]), P(res), P(self.ws_sel), self.ws_sel.numel(), s)
+            rc |= lib.hsb_select_keys(P(self.keys), P(self.scores), HEADS, n, n, self.alpha, 0.2, 0, P(self.ids[l]),
+                                      self.count, P(self.counts[l]), P(res), P(self.ws_sel), self.ws_sel.numel(), s)
             e[2].record(stream)
             rc |= lib.hsb_gather_cache(P(self.ids[l]), self.count, P(res), 0, P(self.kc[l]), P(self.vc[l]), 1024, n,
                                        self.count, 0, P(self.kp), P(self.vp), P(res[2:]), s)

@@ -47,6 +47,8 @@ _SIGNATURES = {
     "hsb_score_v3": (I, [P, P, SZ, SZ, P, P]),
     "hsb_score_views": (I, [P, P, SZ, P, P]),
     "hsb_score_pipeline_v3": (I, [P, P, C.c_uint32, P, P]),
+    "hsb_score_with_keys": (I, [P, P, SZ, SZ, P, P, P]),
+    "hsb_select_keys": (I, [P, P, SZ, SZ, SZ, F, F, I, P, SZ, P, P, P, SZ, P]),
     "hsb_scale_scores": (I, [P, SZ, P, P]),
     "hsb_select_workspace_bytes": (SZ, [SZ, SZ, SZ, SZ]),
     "hsb_select": (I, [P, I, SZ, SZ, SZ, F, F, I, P, SZ, P, P, P, SZ, P]),

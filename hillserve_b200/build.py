@@ -22,6 +22,9 @@ CSRC = PKG / "csrc"
 LIBDIR = PKG / "_lib"
 OBJDIR = PKG / "_build"
 LIB = LIBDIR / "libhsb.so"
+COMPAT = PKG / "compat"
+COMPAT_LIB = LIBDIR / "libhsb_compat.so"
+CUDA_LIB = "/usr/local/cuda/lib64"
 SOURCES = ["score.cu", "select.cu", "pack.cu", "attention.cu", "rehearsal.cu", "capi.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -72,8 +75,19 @@ def build(force: bool = False, verbose: bool = False) -> Path:
                 cmd.insert(1, "-Xptxas=-v")
                 print(" ".join(cmd), file=sys.stderr)
             subprocess.run(cmd, check=True)
+    # The shared CUDA runtime: one runtime instance per process (PyTorch's when
+    # it is loaded), so the current device and streams are the caller's.
+    link = ["--cudart", "shared", f"-Xlinker=-rpath,{CUDA_LIB}"]
     if force or _stale(LIB, objs):
-        cmd = [nvcc, *ARCH, "-shared", "--cudart", "static", "-o", str(LIB), *map(str, objs)]
+        cmd = [nvcc, *ARCH, "-shared", *link, "-o", str(LIB), *map(str, objs)]
+        subprocess.run(cmd, check=True)
+    # C++ drop-in layer over the C ABI (reference header names and classes).
+    csrc = COMPAT / "compat.cpp"
+    deps = [csrc, LIB, *COMPAT.rglob("*.hpp"), ROOT / "include" / "hsb.h"]
+    if force or _stale(COMPAT_LIB, deps):
+        cmd = [nvcc, "-std=c++17", "-O2", "-Xcompiler", "-fPIC", "-shared", "-x", "cu", *ARCH,
+               f"-I{ROOT / 'include'}", f"-I{COMPAT}", str(csrc), "-o", str(COMPAT_LIB), f"-L{LIBDIR}", "-lhsb",
+               *link, "-Xlinker=-rpath,$ORIGIN"]
         subprocess.run(cmd, check=True)
     return LIB
 

@@ -1,0 +1,614 @@
+// compat.cpp -- the reference's C++ interfaces for the selected-KV path
+// (policy/full_gqa_cpu.hpp, policy/gqa_policy.hpp, runtime/gqa_pack.hpp,
+// runtime/gqa_prefetch_cuda.hpp, runtime/gqa_delivery.hpp), implemented over
+// the C ABI of include/hsb.h.  Host vectors in, host results out, exceptions
+// as in the reference; device work is enqueued on private streams and
+// completed before each synchronous call returns.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cfenv>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <limits>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+
+#include "hsb.h"
+#include "policy/full_gqa_cpu.hpp"
+#include "policy/gqa_policy.hpp"
+#include "policy/host_policy.hpp"
+#include "runtime/gqa_delivery.hpp"
+#include "runtime/gqa_pack.hpp"
+#include "runtime/gqa_prefetch_cuda.hpp"
+
+namespace hillserve {
+namespace {
+
+using Clock = std::chrono::steady_clock;
+std::uint64_t now_ns() {
+    return std::chrono::duration_cast<std::chrono::nanoseconds>(Clock::now().time_since_epoch()).count();
+}
+
+void cuda_check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// Maps an hsb status to the reference's exception type.
+[[noreturn]] void throw_status(int status) {
+    const std::string msg = hsb_last_error()[0] ? hsb_last_error() : hsb_status_message(status);
+    switch (status) {
+    case HSB_E_SCORE_SHAPE: case HSB_E_SCORE_ALIAS: case HSB_E_SCORE_V3_TOKENS:
+    case HSB_E_UNION_BOUNDS: case HSB_E_UNION_DUPLICATE: case HSB_E_PACK_SHAPE:
+    case HSB_E_PACK_PHYSICAL: case HSB_E_PACK_SLOTS: case HSB_E_PACK_MISSING:
+        throw std::invalid_argument(msg);
+    default:
+        throw std::runtime_error(msg);
+    }
+}
+void hsb_check(int status) {
+    if (status != HSB_OK) throw_status(status);
+}
+
+bool is_device_pointer(const void* p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// Growable device buffer.
+struct DeviceBuffer {
+    void* ptr = nullptr;
+    std::size_t bytes = 0;
+    ~DeviceBuffer() {
+        if (ptr) cudaFree(ptr);
+    }
+    void* reserve(std::size_t n) {
+        if (n > bytes) {
+            if (ptr) cudaFree(ptr);
+            ptr = nullptr;
+            bytes = 0;
+            cuda_check(cudaMalloc(&ptr, std::max<std::size_t>(n, 256)), "device allocation");
+            bytes = std::max<std::size_t>(n, 256);
+        }
+        return ptr;
+    }
+    template <class T>
+    T* as() const { return static_cast<T*>(ptr); }
+};
+
+struct Stream {
+    cudaStream_t s = nullptr;
+    Stream() { cuda_check(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "stream"); }
+    ~Stream() {
+        if (s) {
+            cudaStreamSynchronize(s);
+            cudaStreamDestroy(s);
+        }
+    }
+};
+
+// Stream and scratch shared by the free functions of one thread.
+struct ThreadContext {
+    Stream stream;
+    DeviceBuffer a, b, c, d, e, f, ws;
+};
+ThreadContext& tls() {
+    static thread_local ThreadContext ctx;
+    return ctx;
+}
+
+void h2d(void* dst, const void* src, std::size_t n, cudaStream_t s) {
+    if (n) cuda_check(cudaMemcpyAsync(dst, src, n, cudaMemcpyHostToDevice, s), "host to device copy");
+}
+void d2h(void* dst, const void* src, std::size_t n, cudaStream_t s) {
+    if (n) cuda_check(cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToHost, s), "device to host copy");
+}
+void sync(cudaStream_t s) { cuda_check(cudaStreamSynchronize(s), "stream synchronize"); }
+
+}  // namespace
+
+// ------------------------------------------------------------ host_policy
+float half_value(std::uint16_t h) {
+    const std::uint32_t sign = std::uint32_t(h & 0x8000u) << 16, e = (h >> 10) & 31u, m = h & 1023u;
+    std::uint32_t bits;
+    if (e == 0) {
+        float mag = std::ldexp(float(m), -24);
+        std::memcpy(&bits, &mag, 4);
+        bits |= sign;
+    } else {
+        bits = sign | (e == 31 ? (0x7f800000u | (m << 13)) : (((e + 112u) << 23) | (m << 13)));
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+std::uint16_t half_bits(float f) {
+    std::uint32_t x;
+    std::memcpy(&x, &f, 4);
+    const std::uint16_t sign = std::uint16_t((x >> 16) & 0x8000u);
+    const std::uint32_t e = (x >> 23) & 255u, m = x & 0x7fffffu;
+    if (e == 255) return std::uint16_t(sign | 0x7c00u | (m ? 0x200u : 0u));
+    const int he = int(e) - 112;
+    if (he >= 31) return std::uint16_t(sign | 0x7c00u);
+    if (he <= 0) {
+        if (he < -10) return sign;
+        const std::uint32_t full = m | 0x800000u, sh = std::uint32_t(14 - he);
+        std::uint32_t q = full >> sh;
+        const std::uint32_t r = full & ((1u << sh) - 1u), half = 1u << (sh - 1u);
+        q += (r > half) || (r == half && (q & 1u));
+        return std::uint16_t(sign | q);
+    }
+    std::uint32_t q = (std::uint32_t(he) << 10) | (m >> 13);
+    const std::uint32_t r = m & 0x1fffu;
+    q += (r > 0x1000u) || (r == 0x1000u && (q & 1u));
+    return std::uint16_t(sign | q);
+}
+
+// ------------------------------------------------------------ scorer
+struct FullGqaCpuScorer::Impl {
+    unsigned count;
+    std::mutex invocation;
+    Stream stream;
+    DeviceBuffer q, keys, out;
+    std::vector<hsb_key_view> views;
+};
+
+FullGqaCpuScorer::FullGqaCpuScorer(unsigned threads, FullGqaCpuImplementation implementation) {
+    // policy/full_gqa_cpu.cpp:153-163
+    if (std::fegetround() != FE_TONEAREST)
+        throw std::invalid_argument("full GQA CPU workers require round-to-nearest FP32 mode");
+    if (threads == 0 || threads > 128) throw std::invalid_argument("full GQA CPU threads must be 1..128");
+    if (implementation != FullGqaCpuImplementation::automatic && implementation != FullGqaCpuImplementation::scalar &&
+        implementation != FullGqaCpuImplementation::avx2_f16c)
+        throw std::invalid_argument("unknown full GQA CPU implementation");
+    impl_.reset(new Impl{});
+    impl_->count = threads;
+}
+FullGqaCpuScorer::~FullGqaCpuScorer() = default;
+unsigned FullGqaCpuScorer::threads() const noexcept { return impl_->count; }
+const char* FullGqaCpuScorer::implementation_name() const noexcept { return "sm100a_ordered_fp32"; }
+std::size_t FullGqaCpuScorer::workspace_bytes() const noexcept {
+    return sizeof(Impl) + impl_->q.bytes + impl_->keys.bytes + impl_->out.bytes;
+}
+bool FullGqaCpuScorer::avx2_f16c_available() noexcept { return true; }
+
+void FullGqaCpuScorer::score(const std::vector<std::uint16_t>& q, const std::vector<FullGqaKeyView>& views,
+                             std::vector<std::uint16_t>& result) {
+    std::lock_guard<std::mutex> call(impl_->invocation);
+    // policy/full_gqa_cpu.cpp:210-227, same order and messages
+    if (std::fegetround() != FE_TONEAREST)
+        throw std::invalid_argument("full GQA CPU scoring requires round-to-nearest FP32 mode");
+    if (&q == &result) throw std::invalid_argument("full GQA CPU output must not alias the query");
+    if (q.size() != 32 * 128 || views.empty()) throw std::invalid_argument("full GQA CPU query/views shape");
+    std::size_t tokens = 0, host_tokens = 0;
+    for (const auto& v : views) {
+        if (!v.data || v.tokens == 0 || (v.token_stride_words != 1024 && v.token_stride_words != 2048) ||
+            v.tokens > std::numeric_limits<std::size_t>::max() / v.token_stride_words ||
+            v.tokens > std::numeric_limits<std::size_t>::max() / 32 - tokens)
+            throw std::invalid_argument("full GQA CPU key view shape/stride/extent");
+        tokens += v.tokens;
+        if (!is_device_pointer(v.data)) host_tokens += v.tokens;
+    }
+    cudaStream_t s = impl_->stream.s;
+    auto* dq = static_cast<std::uint16_t*>(impl_->q.reserve(4096 * 2));
+    h2d(dq, q.data(), 4096 * 2, s);
+    // Host views: stage only their K words (1024 per token) into one buffer.
+    auto* staged = static_cast<std::uint16_t*>(impl_->keys.reserve(host_tokens * 2048 + 16));
+    impl_->views.clear();
+    std::size_t cursor = 0;
+    for (const auto& v : views) {
+        if (is_device_pointer(v.data)) {
+            impl_->views.push_back({v.data, v.tokens, v.token_stride_words});
+            continue;
+        }
+        cuda_check(cudaMemcpy2DAsync(staged + cursor * 1024, 2048, v.data, v.token_stride_words * 2, 2048, v.tokens,
+                                     cudaMemcpyHostToDevice, s),
+                   "key staging");
+        impl_->views.push_back({staged + cursor * 1024, v.tokens, 1024});
+        cursor += v.tokens;
+    }
+    auto* dout = impl_->out.reserve(tokens * 32 * 2);
+    hsb_check(hsb_score_views(dq, impl_->views.data(), impl_->views.size(), static_cast<std::uint16_t*>(dout), s));
+    result.resize(tokens * 32);
+    d2h(result.data(), dout, tokens * 32 * 2, s);
+    sync(s);
+}
+
+std::vector<std::uint16_t> score_full_gqa_legacy_cpu(const std::vector<std::uint16_t>& q, const std::uint16_t* input,
+                                                     std::size_t n, std::size_t token_stride, unsigned threads) {
+    // policy/full_gqa_cpu.cpp:111-118
+    if (!(q.size() == 32 * 128 && input && n > 0 && (token_stride == 1024 || token_stride == 2048) && threads >= 1 &&
+          threads <= 32))
+        throw std::invalid_argument("raw128 physical GQA CPU shape/stride/thread bound");
+    if (n > std::numeric_limits<std::size_t>::max() / 32 || n > std::numeric_limits<std::size_t>::max() / token_stride)
+        throw std::invalid_argument("legacy full GQA CPU extent overflow");
+    if (std::fegetround() != FE_TONEAREST)
+        throw std::invalid_argument("legacy full GQA CPU requires round-to-nearest FP32 mode");
+    static thread_local std::unique_ptr<FullGqaCpuScorer> scorer;
+    if (!scorer) scorer.reset(new FullGqaCpuScorer(1));
+    std::vector<std::uint16_t> out;
+    scorer->score(q, {{input, n, token_stride}}, out);
+    return out;
+}
+
+// ------------------------------------------------------------ selector
+namespace policy {
+GQASelection select_gqa_scores(const std::vector<std::uint16_t>& score, std::size_t h, std::size_t stride,
+                               std::size_t n, float alpha, float ratio, bool fp32_counts) {
+    // policy/gqa_policy.cpp:48-49 shape checks (incl. the vector size)
+    if (!(h > 0 && h <= 128 && n > 0 && n <= stride && score.size() == h * stride))
+        throw std::runtime_error("GQA selector shape");
+    if (!(std::isfinite(alpha) && alpha >= 0 && std::isfinite(ratio) && ratio > 0 && ratio <= 1))
+        throw std::runtime_error("GQA selector numeric parameters");
+    auto& c = tls();
+    cudaStream_t s = c.stream.s;
+    const std::size_t kcap = std::max<std::size_t>(1, std::min<std::size_t>(std::floor(double(n) * double(ratio)), n));
+    auto* dscores = c.a.reserve(score.size() * 2);
+    auto* dids = c.b.reserve(h * kcap * 4);
+    auto* dcounts = c.c.reserve(h * 4);
+    auto* dres = c.d.reserve(sizeof(hsb_selection));
+    const std::size_t wsb = hsb_select_workspace_bytes(h, stride, n, kcap);
+    auto* ws = c.ws.reserve(wsb);
+    h2d(dscores, score.data(), score.size() * 2, s);
+    const int rc = hsb_select(static_cast<const std::uint16_t*>(dscores), 0, h, stride, n, alpha, ratio, fp32_counts,
+                              static_cast<std::uint32_t*>(dids), kcap, static_cast<std::uint32_t*>(dcounts),
+                              static_cast<hsb_selection*>(dres), ws, c.ws.bytes, s);
+    if (rc) throw std::runtime_error(hsb_last_error());
+    hsb_selection res{};
+    const int st = hsb_selection_read(static_cast<hsb_selection*>(dres), &res, s);
+    if (st) throw std::runtime_error(hsb_last_error());
+    GQASelection r;
+    r.k = res.k;
+    r.boundary_tied_heads = res.boundary_tied_heads;
+    r.counts.resize(h);
+    std::vector<std::uint32_t> ids(h * kcap);
+    d2h(r.counts.data(), dcounts, h * 4, s);
+    d2h(ids.data(), dids, h * kcap * 4, s);
+    sync(s);
+    r.ids.resize(h);
+    for (std::size_t head = 0; head < h; ++head)
+        r.ids[head].assign(ids.begin() + head * kcap, ids.begin() + head * kcap + r.k);
+    return r;
+}
+}  // namespace policy
+
+// ------------------------------------------------------------ union / pack
+namespace {
+// Flattens ragged per-head lists into [32][kstride] u32 + sizes, as the
+// device kernels read them.  IDs >= 2^32 cannot be admitted (visible <= 66048).
+void flatten_ids(const std::vector<std::vector<std::uint64_t>>& ids, std::vector<std::uint32_t>& flat,
+                 std::vector<std::uint32_t>& sizes, std::size_t& kstride, std::uint32_t out_of_range) {
+    kstride = 1;
+    for (const auto& h : ids) kstride = std::max(kstride, h.size());
+    flat.assign(32 * kstride, 0);
+    sizes.assign(32, 0);
+    for (std::size_t h = 0; h < ids.size() && h < 32; ++h) {
+        sizes[h] = std::uint32_t(ids[h].size());
+        for (std::size_t s = 0; s < ids[h].size(); ++s)
+            flat[h * kstride + s] = ids[h][s] > 0xffffffffull ? out_of_range : std::uint32_t(ids[h][s]);
+    }
+}
+}  // namespace
+
+std::vector<std::uint64_t> gqa_physical_union(const std::vector<std::vector<std::uint64_t>>& ids, std::size_t visible) {
+    if (ids.size() != 32 || !visible || visible > 66048) throw std::invalid_argument("GQA union bounds");
+    std::vector<std::uint32_t> flat, sizes;
+    std::size_t kstride;
+    flatten_ids(ids, flat, sizes, kstride, 0xffffffffu);
+    auto& c = tls();
+    cudaStream_t s = c.stream.s;
+    auto* dids = c.a.reserve(flat.size() * 4);
+    auto* dsizes = c.b.reserve(32 * 4);
+    auto* dphys = c.c.reserve(visible * 4);
+    auto* dcount = c.d.reserve(16);
+    auto* dstatus = c.e.reserve(sizeof(hsb_device_status));
+    auto* ws = c.ws.reserve(hsb_union_workspace_bytes(visible));
+    h2d(dids, flat.data(), flat.size() * 4, s);
+    h2d(dsizes, sizes.data(), 32 * 4, s);
+    cuda_check(cudaMemsetAsync(dstatus, 0, sizeof(hsb_device_status), s), "status reset");
+    hsb_check(hsb_union(static_cast<std::uint32_t*>(dids), kstride, static_cast<std::uint32_t*>(dsizes), 1, visible,
+                        static_cast<std::uint32_t*>(dphys), static_cast<std::uint32_t*>(dcount),
+                        static_cast<hsb_device_status*>(dstatus), ws, c.ws.bytes, s));
+    hsb_check(hsb_status_check(static_cast<hsb_device_status*>(dstatus), s));
+    std::uint32_t count = 0;
+    d2h(&count, dcount, 4, s);
+    sync(s);
+    std::vector<std::uint32_t> phys(count);
+    d2h(phys.data(), dphys, count * 4, s);
+    sync(s);
+    return std::vector<std::uint64_t>(phys.begin(), phys.end());
+}
+
+void pack_gqa_workspace(const std::vector<std::vector<std::uint64_t>>& ids, const std::vector<std::uint64_t>& positions,
+                        const std::vector<std::uint64_t>& physical, const std::vector<std::uint8_t>& payload,
+                        std::size_t count, std::uint16_t* k, std::uint16_t* v, float* mask) {
+    // runtime/gqa_pack.hpp:29-30
+    if (ids.size() != 32 || positions.empty() || positions.size() > 256 || positions.back() >= 66048 || !count ||
+        count > 66048 || payload.size() != physical.size() * 4096)
+        throw std::invalid_argument("GQA packing shape");
+    const std::uint64_t last = positions.back();
+    std::vector<std::uint32_t> flat, sizes, phys(physical.size());
+    std::size_t kstride;
+    flatten_ids(ids, flat, sizes, kstride, 0xffffffffu);
+    for (std::size_t i = 0; i < physical.size(); ++i)
+        phys[i] = physical[i] > 0xffffffffull ? 0xffffffffu : std::uint32_t(physical[i]);
+    auto& c = tls();
+    cudaStream_t s = c.stream.s;
+    const std::size_t qpad = (positions.size() + 63) / 64 * 64;
+    auto* dids = c.a.reserve(flat.size() * 4);
+    auto* dsizes = c.b.reserve(32 * 4);
+    auto* dpos = c.f.reserve(positions.size() * 8);
+    auto* dphys = c.c.reserve(phys.size() * 4 + 16);
+    auto* dpayload = c.d.reserve(payload.size() + 16);
+    auto* dout = static_cast<std::uint8_t*>(c.e.reserve(count * 4096 * 4 + count * qpad * 32 * 4 + 512));
+    auto* dk = reinterpret_cast<std::uint16_t*>(dout);
+    auto* dv = dk + count * 4096;
+    auto* dmask = reinterpret_cast<float*>(dv + count * 4096);
+    auto* dstatus = reinterpret_cast<hsb_device_status*>(dmask + count * qpad * 32);
+    auto* ws = c.ws.reserve(hsb_pack_workspace_bytes(last));
+    h2d(dids, flat.data(), flat.size() * 4, s);
+    h2d(dsizes, sizes.data(), 32 * 4, s);
+    h2d(dpos, positions.data(), positions.size() * 8, s);
+    h2d(dphys, phys.data(), phys.size() * 4, s);
+    h2d(dpayload, payload.data(), payload.size(), s);
+    cuda_check(cudaMemsetAsync(dstatus, 0, sizeof(hsb_device_status), s), "status reset");
+    hsb_check(hsb_pack(static_cast<std::uint32_t*>(dids), kstride, static_cast<std::uint32_t*>(dsizes), 1,
+                       reinterpret_cast<const std::uint64_t*>(dpos), positions.size(), last,
+                       static_cast<std::uint32_t*>(dphys), phys.size(), static_cast<std::uint8_t*>(dpayload),
+                       payload.size(), count, dk, dv, dmask, dstatus, ws, c.ws.bytes, s));
+    hsb_check(hsb_status_check(dstatus, s));
+    d2h(k, dk, count * 4096 * 2, s);
+    d2h(v, dv, count * 4096 * 2, s);
+    d2h(mask, dmask, count * qpad * 32 * 4, s);
+    sync(s);
+}
+
+// ------------------------------------------------------------ prefetch
+struct GQAPrefetchCuda::Impl {
+    int device = 0;
+    std::size_t rows = 0, bytes = 0;
+    struct Slot {
+        void* host = nullptr;
+        void* gpu = nullptr;
+        cudaStream_t stream = nullptr;
+        cudaEvent_t start = nullptr, ready = nullptr;
+        std::size_t valid = 0;
+    };
+    Slot slots[2];
+    void* misses = nullptr;
+    std::int32_t* map = nullptr;
+    hsb_device_status* status = nullptr;
+    cudaEvent_t delivery = nullptr;
+    cudaStream_t consume_stream = nullptr;
+    bool consume_pending = false;
+    ~Impl() {
+        // Drain everything that may still read a slot before freeing it;
+        // cleanup never throws (runtime/gqa_prefetch_cuda.cu:31-41).
+        cudaSetDevice(device);
+        if (consume_pending && consume_stream) cudaStreamSynchronize(consume_stream);
+        if (delivery) cudaEventSynchronize(delivery);
+        for (auto& s : slots)
+            if (s.stream) cudaStreamSynchronize(s.stream);
+        for (auto& s : slots) {
+            if (s.start) cudaEventDestroy(s.start);
+            if (s.ready) cudaEventDestroy(s.ready);
+            if (s.gpu) cudaFree(s.gpu);
+            if (s.host) cudaFreeHost(s.host);
+            if (s.stream) cudaStreamDestroy(s.stream);
+        }
+        if (misses) cudaFree(misses);
+        if (map) cudaFree(map);
+        if (status) cudaFree(status);
+        if (delivery) cudaEventDestroy(delivery);
+    }
+};
+
+GQAPrefetchCuda::GQAPrefetchCuda(void* pointer, std::size_t max_rows) : impl_(new Impl) {
+    auto& p = *impl_;
+    cudaPointerAttributes a{};
+    cuda_check(cudaPointerGetAttributes(&a, pointer), "prefetch GPU pointer attributes");
+    if (a.type != cudaMemoryTypeDevice) throw std::runtime_error("prefetch target must be CUDA device memory");
+    p.device = a.device;
+    p.rows = max_rows;
+    p.bytes = max_rows * 4096;
+    cuda_check(cudaSetDevice(p.device), "prefetch set device");
+    for (auto& s : p.slots) {
+        cuda_check(cudaMalloc(&s.gpu, std::max<std::size_t>(p.bytes, 256)), "prefetch slot allocation");
+        cuda_check(cudaMallocHost(&s.host, std::max<std::size_t>(p.bytes, 256)), "prefetch pinned slot allocation");
+        cuda_check(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking), "prefetch private stream");
+        cuda_check(cudaEventCreate(&s.start), "prefetch start event");
+        cuda_check(cudaEventCreate(&s.ready), "prefetch ready event");
+    }
+    cuda_check(cudaMalloc(&p.misses, std::max<std::size_t>(p.bytes, 256)), "prefetch miss allocation");
+    cuda_check(cudaMalloc(reinterpret_cast<void**>(&p.map), std::max<std::size_t>(max_rows * 32 * 4, 256)),
+               "prefetch map allocation");
+    cuda_check(cudaMalloc(reinterpret_cast<void**>(&p.status), sizeof(hsb_device_status)), "prefetch status");
+    cuda_check(cudaEventCreateWithFlags(&p.delivery, cudaEventDisableTiming), "prefetch delivery event");
+}
+GQAPrefetchCuda::~GQAPrefetchCuda() = default;
+std::size_t GQAPrefetchCuda::gpu_bytes() const { return impl_->bytes * 3 + impl_->rows * 32 * 4; }
+std::size_t GQAPrefetchCuda::host_bytes() const { return impl_->bytes * 2; }
+
+GQAPrefetchCuda::Upload GQAPrefetchCuda::stage(unsigned slot, const std::vector<std::uint8_t>& payload) {
+    auto& p = *impl_;
+    if (slot >= 2 || payload.size() > p.bytes || payload.size() % 4096)
+        throw std::runtime_error("prefetch CUDA slot geometry");
+    auto& s = p.slots[slot];
+    cuda_check(cudaSetDevice(p.device), "prefetch worker device");
+    Upload out;
+    if (!payload.empty()) std::memcpy(s.host, payload.data(), payload.size());
+    out.started_ns = now_ns();
+    out.bytes = payload.size();
+    s.valid = payload.size() / 4096;
+    try {
+        cuda_check(cudaEventRecord(s.start, s.stream), "prefetch upload start");
+        if (!payload.empty())
+            cuda_check(cudaMemcpyAsync(s.gpu, s.host, payload.size(), cudaMemcpyHostToDevice, s.stream), "prefetch H2D");
+        cuda_check(cudaEventRecord(s.ready, s.stream), "prefetch ready record");
+        cuda_check(cudaEventSynchronize(s.ready), "prefetch upload completion");
+        out.ready_observed_ns = now_ns();
+        cuda_check(cudaEventElapsedTime(&out.device_ms, s.start, s.ready), "prefetch upload interval");
+        return out;
+    } catch (...) {
+        cudaStreamSynchronize(s.stream);  // never release the pinned source mid-copy
+        throw;
+    }
+}
+
+GQAPrefetchCuda::Delivery GQAPrefetchCuda::deliver(unsigned slot, const std::vector<std::int32_t>& rows,
+                                                   const std::vector<std::uint8_t>& misses, const float* mask,
+                                                   std::size_t mask_elements, std::size_t count, void* k, void* v,
+                                                   void* gpu_mask, void* raw_stream) {
+    auto& p = *impl_;
+    // runtime/gqa_prefetch_cuda.cu:217-218
+    if (slot >= 2 || !raw_stream || count > p.rows || rows.size() != count * 32 || misses.size() > p.bytes ||
+        misses.size() % 4096)
+        throw std::runtime_error("prefetch CUDA delivery geometry/stream");
+    auto& s = p.slots[slot];
+    std::size_t valid_pairs = 0;
+    for (auto row : rows) {
+        if (row >= 0 && std::size_t(row) >= s.valid) throw std::runtime_error("prefetch row outside uploaded payload");
+        if (row <= -2 && std::size_t(-2 - static_cast<long long>(row)) >= misses.size() / 4096)
+            throw std::runtime_error("prefetch miss row outside payload");
+        if (row != -1) ++valid_pairs;
+    }
+    cuda_check(cudaSetDevice(p.device), "prefetch consumer device");
+    const auto stream = static_cast<cudaStream_t>(raw_stream);
+    Delivery out;
+    out.started_ns = now_ns();
+    p.consume_stream = stream;
+    p.consume_pending = true;
+    try {
+        cuda_check(cudaStreamWaitEvent(stream, s.ready, 0), "attention stream waits for prefetched payload");
+        if (!misses.empty())
+            cuda_check(cudaMemcpyAsync(p.misses, misses.data(), misses.size(), cudaMemcpyHostToDevice, stream),
+                       "prefetch miss H2D");
+        cuda_check(cudaMemcpyAsync(p.map, rows.data(), rows.size() * 4, cudaMemcpyHostToDevice, stream),
+                   "prefetch gather map H2D");
+        if (mask_elements)
+            cuda_check(cudaMemcpyAsync(gpu_mask, mask, mask_elements * 4, cudaMemcpyHostToDevice, stream),
+                       "prefetch attention mask H2D");
+        cuda_check(cudaMemsetAsync(p.status, 0, sizeof(hsb_device_status), stream), "status reset");
+        hsb_check(hsb_gather_map(static_cast<const std::uint16_t*>(s.gpu), s.valid,
+                                 static_cast<const std::uint16_t*>(p.misses), misses.size() / 4096, p.map, count,
+                                 static_cast<std::uint16_t*>(k), static_cast<std::uint16_t*>(v), p.status, stream));
+        cuda_check(cudaEventRecord(p.delivery, stream), "prefetch delivery completion record");
+        const auto wait = Clock::now();
+        cuda_check(cudaEventSynchronize(p.delivery), "prefetch delivery completion");
+        hsb_check(hsb_status_check(p.status, stream));
+        out.wait_ms = std::chrono::duration<double, std::milli>(Clock::now() - wait).count();
+        out.ready_observed_ns = now_ns();
+        out.h2d_bytes = misses.size() + rows.size() * 4 + mask_elements * 4;
+        out.d2d_bytes = valid_pairs * 128 * 4;
+        p.consume_pending = false;
+        p.consume_stream = nullptr;
+        return out;
+    } catch (...) {
+        if (cudaStreamSynchronize(stream) == cudaSuccess) {
+            p.consume_pending = false;
+            p.consume_stream = nullptr;
+        }
+        throw;
+    }
+}
+
+// ------------------------------------------------------------ delivery
+struct GQADeliveryWorkspace::Impl {
+    std::size_t count = 0;
+    Stream stream;
+    DeviceBuffer q, k, v, mask, ids, sizes, pos, phys, payload, status, out, ws;
+    std::vector<float> output;
+    std::uint64_t packed = 0;
+};
+
+GQADeliveryWorkspace::GQADeliveryWorkspace(std::size_t count, const std::vector<float>& actual) : p(new Impl) {
+    // runtime/gqa_delivery.cpp:13,21
+    if (!(count > 0 && count <= 6592 && count % 32 == 0 && actual.size() == 4096))
+        throw std::runtime_error("bounded real GQA delivery shape");
+    p->count = count;
+    p->q.reserve(4096 * 4);
+    p->k.reserve(count * 4096 * 2);
+    p->v.reserve(count * 4096 * 2);
+    p->mask.reserve(count * 64 * 32 * 4);
+    p->out.reserve(4096 * 4);
+    p->status.reserve(sizeof(hsb_device_status));
+    p->ws.reserve(std::max(hsb_attention_workspace_bytes(count), hsb_pack_workspace_bytes(66047)));
+    if (gpu_bytes() > 256ull * 1024 * 1024) throw std::runtime_error("GPU workspace budget");
+    h2d(p->q.ptr, actual.data(), 4096 * 4, p->stream.s);
+    sync(p->stream.s);
+}
+GQADeliveryWorkspace::~GQADeliveryWorkspace() = default;
+std::uint64_t GQADeliveryWorkspace::gpu_bytes() const {
+    return p->k.bytes + p->v.bytes + p->mask.bytes + p->q.bytes + p->out.bytes;
+}
+const std::vector<float>& GQADeliveryWorkspace::output() const { return p->output; }
+
+GQADeliveryResult GQADeliveryWorkspace::deliver(const std::vector<std::vector<std::uint64_t>>& ids,
+                                                std::uint64_t position, const std::vector<std::uint64_t>& physical,
+                                                const std::vector<std::uint8_t>& payload) {
+    GQADeliveryResult r;
+    const auto t0 = Clock::now();
+    if (ids.size() != 32 || position >= 66048 || payload.size() != physical.size() * 4096)
+        throw std::invalid_argument("GQA packing shape");
+    std::vector<std::uint32_t> flat, sizes, phys(physical.size());
+    std::size_t kstride;
+    flatten_ids(ids, flat, sizes, kstride, 0xffffffffu);
+    for (std::size_t i = 0; i < physical.size(); ++i)
+        phys[i] = physical[i] > 0xffffffffull ? 0xffffffffu : std::uint32_t(physical[i]);
+    cudaStream_t s = p->stream.s;
+    auto* dids = p->ids.reserve(flat.size() * 4);
+    auto* dsizes = p->sizes.reserve(32 * 4);
+    auto* dpos = p->pos.reserve(8);
+    auto* dphys = p->phys.reserve(phys.size() * 4 + 16);
+    auto* dpayload = p->payload.reserve(payload.size() + 16);
+    h2d(dids, flat.data(), flat.size() * 4, s);
+    h2d(dsizes, sizes.data(), 32 * 4, s);
+    h2d(dpos, &position, 8, s);
+    h2d(dphys, phys.data(), phys.size() * 4, s);
+    h2d(dpayload, payload.data(), payload.size(), s);
+    cuda_check(cudaMemsetAsync(p->status.ptr, 0, sizeof(hsb_device_status), s), "status reset");
+    hsb_check(hsb_pack(static_cast<std::uint32_t*>(dids), kstride, static_cast<std::uint32_t*>(dsizes), 1,
+                       static_cast<std::uint64_t*>(dpos), 1, position, static_cast<std::uint32_t*>(dphys),
+                       phys.size(), static_cast<std::uint8_t*>(dpayload), payload.size(), p->count,
+                       p->k.as<std::uint16_t>(), p->v.as<std::uint16_t>(), p->mask.as<float>(),
+                       p->status.as<hsb_device_status>(), p->ws.ptr, p->ws.bytes, s));
+    hsb_check(hsb_status_check(p->status.as<hsb_device_status>(), s));
+    r.pack_ms = std::chrono::duration<double, std::milli>(Clock::now() - t0).count();
+    r.gpu_ready_ns = now_ns();
+    r.upload_bytes = flat.size() * 4 + 32 * 4 + 8 + phys.size() * 4 + payload.size();
+    r.upload_wall_ms = r.pack_ms;
+    p->packed = 1;
+    return r;
+}
+
+std::string GQADeliveryWorkspace::verify_and_consume() {
+    if (!p->packed) throw std::runtime_error("nothing delivered");
+    cudaStream_t s = p->stream.s;
+    const auto t0 = Clock::now();
+    hsb_check(hsb_attention_packed(p->q.as<float>(), p->k.as<std::uint16_t>(), p->v.as<std::uint16_t>(), p->count,
+                                   p->mask.as<float>(), 64, nullptr, 0, p->out.as<float>(), p->ws.ptr, p->ws.bytes, s));
+    p->output.resize(4096);
+    d2h(p->output.data(), p->out.ptr, 4096 * 4, s);
+    sync(s);
+    const double ms = std::chrono::duration<double, std::milli>(Clock::now() - t0).count();
+    std::uint64_t h = 1469598103934665603ull;  // FNV-1a over the output bytes
+    const auto* b = reinterpret_cast<const unsigned char*>(p->output.data());
+    for (std::size_t i = 0; i < 4096 * 4; ++i) h = (h ^ b[i]) * 1099511628211ull;
+    for (float x : p->output)
+        if (!std::isfinite(x)) throw std::runtime_error("actual attention produced nonfinite output");
+    char buf[256];
+    std::snprintf(buf, sizeof buf,
+                  "{\"attention_output_checksum\":\"%llu\",\"attention_after_delivery_ms_excluded\":%.6f,"
+                  "\"attention\":\"sm100a split-K flash-decode\"}",
+                  static_cast<unsigned long long>(h), ms);
+    return buf;
+}
+
+}  // namespace hillserve

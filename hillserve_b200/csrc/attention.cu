@@ -107,6 +107,10 @@ __global__ void __launch_bounds__(kPThreads) attention_packed_kernel(const __gri
     const uint16_t* vrow = p.v + ((size_t)h * kDim + tid) * p.count + s0;
     float acc = 0.0f;
     for (int s = 0; s < m; ++s) acc = fmaf(sc[s], half_value(vrow[s]), acc);
+    if (live == 1) {  // one split: no partials to fold
+        p.out[h * kDim + tid] = l > 0.0f ? acc / l : 0.0f;
+        return;
+    }
     float* part = p.part + ((size_t)h * p.nsplit + j) * kPart;
     if (tid == 0) {
         part[0] = mx;

@@ -168,6 +168,22 @@ int hsb_score_pipeline_v3(const uint16_t* d_q, const uint16_t* d_keys, uint32_t 
     return hsb_score_v3(d_q, d_keys, tokens, 1024, d_scores, stream);
 }
 
+int hsb_score_with_keys(const uint16_t* d_q, const uint16_t* d_keys, size_t tokens, size_t stride_words,
+                        uint16_t* d_scores, uint16_t* d_order_keys, void* stream) {
+    if (!d_q) return fail(HSB_E_SCORE_SHAPE, "full GQA CPU query/views shape");
+    if (d_scores == d_q || d_order_keys == d_q)
+        return fail(HSB_E_SCORE_ALIAS, "full GQA CPU output must not alias the query");
+    const hsb_key_view view{d_keys, tokens, stride_words};
+    size_t total = 0;
+    int rc = check_views(&view, 1, &total);
+    if (rc) return rc;
+    if (!d_scores || !d_order_keys) return fail(HSB_E_INVALID, "null score output");
+    cudaError_t e = launch_score(d_q, &view, 1, d_scores, total, 0, nullptr, as_stream(stream), d_order_keys);
+    if (e != cudaSuccess) return fail_cuda(e, "score launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
 int hsb_scale_scores(const uint16_t* d_raw, size_t count, uint16_t* d_out, void* stream) {
     if (!d_raw || !d_out) return fail(HSB_E_INVALID, "null score buffer");
     if (count == 0) return HSB_OK;
@@ -211,6 +227,38 @@ int hsb_select(const uint16_t* d_scores, int input_is_raw, size_t heads, size_t 
     s.scores = d_scores;
     s.raw = input_is_raw != 0;
     s.cover = 0;
+    s.heads = (uint32_t)heads;
+    s.stride = stride;
+    s.valid = valid;
+    s.alpha = alpha;
+    s.ratio = ratio;
+    s.fp32_counts = fp32_counts != 0;
+    s.ids = d_ids;
+    s.kcap = kcap;
+    s.counts = d_counts;
+    s.result = d_result;
+    s.workspace = d_workspace;
+    s.workspace_bytes = workspace_bytes;
+    cudaError_t e = launch_select(s, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "select launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+int hsb_select_keys(const uint16_t* d_order_keys, const uint16_t* d_raw, size_t heads, size_t stride, size_t valid,
+                    float alpha, float ratio, int fp32_counts, uint32_t* d_ids, size_t kcap, uint32_t* d_counts,
+                    hsb_selection* d_result, void* d_workspace, size_t workspace_bytes, void* stream) {
+    int rc = check_select(heads, stride, valid, alpha, ratio);
+    if (rc) return rc;
+    if (!d_order_keys || !d_raw || !d_ids || !d_result) return fail(HSB_E_INVALID, "null selector buffer");
+    if (!aligned(d_result, 8)) return fail(HSB_E_INVALID, "selection result must be 8-byte aligned");
+    if (kcap < select_kmax(valid, ratio)) return fail(HSB_E_SEL_CAPACITY, hsb_status_message(HSB_E_SEL_CAPACITY));
+    if (!d_workspace || workspace_bytes < select_workspace_bytes(heads, valid, kcap) || !aligned(d_workspace, 256))
+        return fail(HSB_E_WORKSPACE, "selector workspace missing or too small");
+    SelectLaunch s{};
+    s.scores = d_order_keys;
+    s.keys = 1;
+    s.tie_raw = d_raw;
     s.heads = (uint32_t)heads;
     s.stride = stride;
     s.valid = valid;
@@ -339,7 +387,7 @@ int hsb_gather_cache(const uint32_t* d_ids, size_t kstride, const uint32_t* d_si
                      const uint16_t* d_kcache, const uint16_t* d_vcache, size_t stride_words, size_t visible,
                      size_t count, int zero_padding, uint16_t* d_k, uint16_t* d_v, hsb_device_status* d_status,
                      void* stream) {
-    if (!d_ids || !d_sizes || !d_kcache || !d_vcache || !d_k || !d_v || count == 0 || visible == 0 || kstride < count)
+    if (!d_ids || !d_sizes || !d_kcache || !d_vcache || !d_k || !d_v || count == 0 || visible == 0 || kstride == 0)
         return fail(HSB_E_INVALID, "gather_cache arguments");
     if (stride_words % 8 || !aligned(d_kcache, 16) || !aligned(d_vcache, 16) || !aligned(d_k, 16) ||
         (d_status && !aligned(d_status, 8)))
@@ -419,10 +467,11 @@ int hsb_rehearsal_query(const uint16_t* d_x, const uint16_t* d_w, uint64_t posit
 }
 
 // ------------------------------------------------------------- layer step
+// Layer-step workspace: selector | attention | order keys [32][valid].
+static size_t align256(size_t b) { return (b + 255) / 256 * 256; }
 size_t hsb_layer_workspace_bytes(size_t valid, size_t count) {
-    const size_t sel = select_workspace_bytes(HSB_QUERY_HEADS, valid, count);
-    const size_t att = attention_workspace_bytes(count);
-    return (sel + 255) / 256 * 256 + (att + 255) / 256 * 256;
+    return align256(select_workspace_bytes(HSB_QUERY_HEADS, valid, count)) + align256(attention_workspace_bytes(count)) +
+           align256(HSB_QUERY_HEADS * valid * 2);
 }
 
 int hsb_layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_kcache, const uint16_t* d_vcache,
@@ -442,12 +491,16 @@ int hsb_layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_
     if ((rc = check_views(&view, 1, &total))) return rc;
     cudaError_t e = cudaMemsetAsync(b->result, 0, sizeof(hsb_selection), s);
     if (e != cudaSuccess) return fail_cuda(e, "result reset");
-    if ((e = launch_score(d_q16, &view, 1, b->scores, valid, 0, &b->result->status, s)) != cudaSuccess)
+    const size_t sel_bytes = align256(select_workspace_bytes(HSB_QUERY_HEADS, valid, count));
+    const size_t att_bytes = align256(attention_workspace_bytes(count));
+    uint16_t* keys = reinterpret_cast<uint16_t*>(static_cast<unsigned char*>(b->workspace) + sel_bytes + att_bytes);
+    if ((e = launch_score(d_q16, &view, 1, b->scores, valid, 0, &b->result->status, s, keys)) != cudaSuccess)
         return fail_cuda(e, "score launch");
-    const size_t sel_bytes = (select_workspace_bytes(HSB_QUERY_HEADS, valid, count) + 255) / 256 * 256;
     SelectLaunch sl{};
-    sl.scores = b->scores;
-    sl.raw = 1;
+    sl.scores = keys;
+    sl.keys = 1;
+    sl.tie_raw = b->scores;
+    sl.raw = 0;
     sl.heads = HSB_QUERY_HEADS;
     sl.stride = valid;
     sl.valid = valid;

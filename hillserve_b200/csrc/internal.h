@@ -20,15 +20,19 @@ struct DeviceInfo {
 const DeviceInfo& device_info();
 
 // Stage 1
+// keys (optional): also writes order_key(F16(raw / sqrtf(128))) per score, the
+// selector's input in the fused layer step.
 cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nviews,
                          uint16_t* out, size_t out_stride, size_t col0,
-                         hsb_device_status* status, cudaStream_t stream);
+                         hsb_device_status* status, cudaStream_t stream, uint16_t* keys = nullptr);
 cudaError_t launch_scale(const uint16_t* raw, size_t count, uint16_t* out, cudaStream_t stream);
 
 // Stage 2
 struct SelectLaunch {
     const uint16_t* scores;
     int raw;           // normalise in the kernel
+    int keys = 0;      // scores are order keys of normalised scores (from the scorer)
+    const uint16_t* tie_raw = nullptr;  // keys mode: raw scores (tells +0 from -0 at a tie)
     int cover;         // prefetch-cover rules instead of select_gqa_scores
     uint32_t heads;
     unsigned long long stride, valid;

@@ -161,18 +161,23 @@ template <int Mode>
 __global__ void __launch_bounds__(kThreads) gather_tiles_kernel(const __grid_constant__ PackParams p) {
     __shared__ SlotSource src[kSlotTile];
     __shared__ __align__(16) uint16_t vt[kSlotTile][kVPitch];
+    __shared__ uint32_t sizes[kHeads];
+    // Per-head list sizes are read once; tiles past a head's size cost nothing
+    // unless the reference's zero padding is requested.
+    if (threadIdx.x < kHeads) sizes[threadIdx.x] = head_size(p.sizes, p.sizes_stride, threadIdx.x);
+    __syncthreads();
     const size_t tiles_per_head = (p.count + kSlotTile - 1) / kSlotTile;
     const size_t total = tiles_per_head * kHeads;
     for (size_t item = blockIdx.x; item < total; item += gridDim.x) {
         const int h = (int)(item / tiles_per_head);
         const size_t s0 = (item % tiles_per_head) * kSlotTile;
-        const uint32_t size = head_size(p.sizes, p.sizes_stride, h);
-        if (Mode == 0 && (size == 0 || size > p.count)) {
-            if (threadIdx.x == 0 && s0 == 0) raise_status(p.status, HSB_E_PACK_SLOTS, h);
+        const uint32_t size = sizes[h];
+        if (size > p.kstride || (Mode == 1 && size > p.count)) {
+            if (threadIdx.x == 0 && s0 == 0) raise_status(p.status, HSB_E_INVALID, h);
             continue;
         }
-        if (Mode == 1 && size > p.count) {
-            if (threadIdx.x == 0 && s0 == 0) raise_status(p.status, HSB_E_INVALID, h);
+        if (Mode == 0 && (size == 0 || size > p.count)) {
+            if (threadIdx.x == 0 && s0 == 0) raise_status(p.status, HSB_E_PACK_SLOTS, h);
             continue;
         }
         const int live = (int)std::min<size_t>(kSlotTile, size > s0 ? size - s0 : 0);

@@ -47,6 +47,7 @@ struct ScoreParams {
     int nviews;
     unsigned long long tokens;      // tokens scored by this launch
     uint16_t* out;                  // [32][out_stride]
+    uint16_t* keys;                 // optional [32][out_stride] order keys of normalised scores
     unsigned long long out_stride;  // columns of the output matrix
     unsigned long long col0;        // first output column of this launch
     hsb_device_status* status;
@@ -139,11 +140,20 @@ __global__ void __launch_bounds__(kThreads, 1) score_v3_kernel(const __grid_cons
                     a3 = __fmaf_rn(q.w, k, a3);
                 }
             }
-            uint16_t* o = p.out + (unsigned long long)(kh * kGroup) * p.out_stride + p.col0 + t;
-            o[0] = half_bits(a0);
-            o[p.out_stride] = half_bits(a1);
-            o[2 * p.out_stride] = half_bits(a2);
-            o[3 * p.out_stride] = half_bits(a3);
+            const unsigned long long at = (unsigned long long)(kh * kGroup) * p.out_stride + p.col0 + t;
+            const uint16_t s0 = half_bits(a0), s1 = half_bits(a1), s2 = half_bits(a2), s3 = half_bits(a3);
+            uint16_t* o = p.out + at;
+            o[0] = s0;
+            o[p.out_stride] = s1;
+            o[2 * p.out_stride] = s2;
+            o[3 * p.out_stride] = s3;
+            if (p.keys) {
+                uint16_t* kk = p.keys + at;
+                kk[0] = (uint16_t)order_key(scale_half(s0));
+                kk[p.out_stride] = (uint16_t)order_key(scale_half(s1));
+                kk[2 * p.out_stride] = (uint16_t)order_key(scale_half(s2));
+                kk[3 * p.out_stride] = (uint16_t)order_key(scale_half(s3));
+            }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
@@ -161,7 +171,7 @@ __global__ void scale_kernel(const uint16_t* __restrict__ raw, unsigned long lon
 
 cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nviews,
                          uint16_t* out, size_t out_stride, size_t col0, hsb_device_status* status,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, uint16_t* keys) {
     const DeviceInfo& dev = device_info();
     static thread_local int configured_device = -1;
     if (configured_device != dev.ordinal) {
@@ -183,6 +193,7 @@ cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nv
     p.first[nviews] = tokens;
     p.tokens = tokens;
     p.out = out;
+    p.keys = keys;
     p.out_stride = out_stride;
     p.col0 = col0;
     p.status = status;

@@ -2,23 +2,24 @@
 // and the history-only prefetch cover (policy/full_gqa_runtime.cpp:299-344).
 //
 // One CTA of 1024 threads per query head, launched cooperatively so that all
-// heads are resident and can meet at one bounded grid barrier:
-//   1. every CTA reduces the head-0 maximum itself (head 0's row is read from
-//      L2 by each CTA, which avoids a second barrier) and forms the F16
-//      threshold F16(max - alpha);
-//   2. each CTA normalises its own row (F16(raw / sqrtf(128)) when the input is
-//      raw), stores the 16-bit order keys and counts keys >= threshold;
-//   3. grid barrier; every CTA reads the 32 counts, rounds them as the
-//      reference does (F16 count, FP32 sum, F16 mean) and derives k -- all
-//      CTAs compute the same k and the same first error;
-//   4. radix select on the order key (two 8-bit histogram passes) finds the
-//      k-th key K*; an ordered compaction keeps keys > K* and the first
-//      k - #(> K*) ties of K* in ID order;
-//   5. a stable LSD radix sort (two passes, descending digits) of those k
-//      elements reproduces the reference order: key descending, ID ascending.
-// Histograms and ranks use warp-aggregated counting (__match_any_sync); the
-// ordered scatter walks each warp's contiguous segment in order, so ties keep
-// ID order without a comparison sort.
+// heads are resident and can meet at one bounded grid barrier.
+//
+// Everything works on 16-bit order keys of the normalised F16 scores (the key
+// order is the FP32 comparator order with -0 == +0, policy/half_order.hpp):
+//   1. each CTA reads head 0's row and its own row with 16-byte loads, forms
+//      the keys (from normalised bits, from raw bits by the exact division,
+//      or as given when the scorer already emitted keys), reduces the head-0
+//      maximum, derives the F16 threshold F16(max - alpha), and counts keys
+//      >= threshold while storing its row's keys in shared memory;
+//   2. grid barrier; every CTA reads the per-head counts, rounds them as the
+//      reference does (F16 count, FP32 sum, F16 mean) and derives the same k
+//      and the same first error;
+//   3. radix select: a high-byte histogram and a low-byte pass over the keys
+//      of the chosen bin give the k-th largest key K*;
+//   4. ordered compaction (ballots, warp-contiguous segments) keeps keys > K*
+//      and the first k - #(> K*) ties of K* in ID order;
+//   5. the k survivors are put in reference order -- key descending, ID
+//      ascending -- by a rank sort (small k) or a stable LSD radix sort.
 #include <algorithm>
 #include <cmath>
 
@@ -31,18 +32,23 @@ namespace {
 constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
 constexpr unsigned long long kSmemKeysMax = 65536;  // keys kept in shared memory up to this
+constexpr unsigned kSmemSortMax = 4096;             // survivors sorted in shared memory up to this
+constexpr unsigned kRankSortMax = 256;              // rank sort up to this, radix above
+
+enum InputMode { kInputScaled = 0, kInputRaw = 1, kInputKeys = 2 };
 
 // Workspace header (zeroed before each launch).
 struct SelectHeader {
     unsigned int arrived;
     unsigned int pad[31];
-    unsigned int err[128];     // bit0 non-finite score, bit1 rounded count overflow
+    unsigned int err[128];  // bit0 non-finite score, bit1 rounded count overflow
     float rounded[128];
 };
 
 struct SelectParams {
-    const uint16_t* scores;
-    int raw, cover, fp32_counts, zero_is_error;
+    const uint16_t* scores;   // normalised bits, raw bits, or keys (mode)
+    const uint16_t* tie_raw;  // keys mode: raw scores, to tell +0 from -0 at a tie
+    int mode, cover, fp32_counts, zero_is_error;
     uint32_t heads;
     unsigned long long stride, valid, kcap, cover_cap;
     float alpha, ratio;
@@ -50,30 +56,36 @@ struct SelectParams {
     uint32_t* counts;
     hsb_selection* result;
     SelectHeader* header;
-    uint16_t* gkeys;             // [heads][valid] when valid > kSmemKeysMax
-    unsigned long long* sortbuf;  // [heads][2][kcap]
+    uint16_t* gkeys;              // [heads][valid] when valid > kSmemKeysMax
+    unsigned long long* sortbuf;  // [heads][2][kcap] when k > kSmemSortMax
 };
 
 struct SelectShared {
     unsigned int hist[kWarps][256];  // per-warp histograms / scatter offsets
     unsigned int bins[256];
     unsigned int scan[kWarps];
-    float fred[kWarps];
-    unsigned int ured[kWarps];
-    unsigned int b_bin, b_above, b_eqtotal;
+    unsigned int wa[kWarps], wb[kWarps];
+    unsigned int b_bin, b_above, b_eqtotal, total;
     unsigned int status, status_index;
+    unsigned int maxkey, bad0, cnt, bad;
     unsigned long long k;
     unsigned int last_id, next_id;
     int timeout;
 };
 
-__device__ __forceinline__ uint16_t load_norm(const SelectParams& p, unsigned long long i) {
-    const uint16_t s = p.scores[i];
-    return p.raw ? scale_half(s) : s;
+// key -> F16 bits (inverse of order_key; -0 comes back as +0)
+__device__ __forceinline__ uint32_t key_bits(uint32_t key) {
+    return (key & 0x8000u) ? (key ^ 0x8000u) : (~key & 0xffffu);
+}
+__device__ __forceinline__ bool key_nan(uint32_t key) { return key > 0xfc00u || key < 0x03ffu; }
+__device__ __forceinline__ bool key_nonfinite(uint32_t key) { return key >= 0xfc00u || key <= 0x03ffu; }
+
+__device__ __forceinline__ uint32_t to_key(uint32_t v, int mode) {
+    if (mode == kInputKeys) return v;
+    return order_key(mode == kInputRaw ? scale_half((uint16_t)v) : v);
 }
 
-// Block-wide exclusive scan of one u32 per thread; returns the exclusive
-// prefix and writes the block total to *total.
+// Block-wide exclusive scan of one u32 per thread; the total goes to *total.
 __device__ unsigned int block_exclusive_scan(unsigned int v, unsigned int* scan, unsigned int* total) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     unsigned int x = v;
@@ -85,14 +97,14 @@ __device__ unsigned int block_exclusive_scan(unsigned int v, unsigned int* scan,
     if (lane == 31) scan[warp] = x;
     __syncthreads();
     if (warp == 0) {
-        unsigned int w = scan[lane];
+        const unsigned int w = scan[lane];
         unsigned int s = w;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const unsigned int y = __shfl_up_sync(0xffffffffu, s, o);
             if (lane >= o) s += y;
         }
-        scan[lane] = s - w;  // exclusive warp offsets
+        scan[lane] = s - w;
         if (lane == 31) *total = s;
     }
     __syncthreads();
@@ -104,40 +116,30 @@ __device__ unsigned int block_exclusive_scan(unsigned int v, unsigned int* scan,
 __device__ __forceinline__ void zero_hist(SelectShared& sh) {
     for (int i = threadIdx.x; i < kWarps * 256; i += kThreads) (&sh.hist[0][0])[i] = 0;
 }
-
-// Per-warp histogram of digit(key) over keys[0,n) (strided by the block);
-// keys outside the filter count nowhere.  Result summed into sh.bins.
-template <class DigitFn>
-__device__ void key_histogram(SelectShared& sh, const uint16_t* keys, unsigned long long n, DigitFn digit) {
-    zero_hist(sh);
-    __syncthreads();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (unsigned long long base = (unsigned long long)warp * 32; base < n; base += kThreads) {
-        const unsigned long long i = base + lane;
-        const unsigned int d = i < n ? digit(keys[i]) : 0x100u;  // 0x100 = not counted
-        const unsigned int peers = __match_any_sync(0xffffffffu, d);
-        if (d < 0x100u && lane == __ffs(peers) - 1) sh.hist[warp][d] += __popc(peers);
-    }
-    __syncthreads();
+__device__ __forceinline__ void sum_hist(SelectShared& sh) {
     if (threadIdx.x < 256) {
         unsigned int s = 0;
 #pragma unroll 8
         for (int w = 0; w < kWarps; ++w) s += sh.hist[w][threadIdx.x];
         sh.bins[threadIdx.x] = s;
     }
-    __syncthreads();
+}
+// Warp-aggregated increment of hist[warp][d] (d == 0x100: nothing).
+__device__ __forceinline__ void warp_count(SelectShared& sh, unsigned int d) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const unsigned int peers = __match_any_sync(0xffffffffu, d);
+    if (d < 0x100u && lane == __ffs(peers) - 1) sh.hist[warp][d] += __popc(peers);
 }
 
 // Finds the bin holding the `need`-th largest element: the bin b with
 // (#elements in bins > b) < need <= (#elements in bins >= b).
 __device__ void find_bin(SelectShared& sh, unsigned int need) {
-    // Suffix sums over 256 bins, computed by warp 0 with 8 bins per lane.
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
         unsigned int local[8];
         unsigned int s = 0;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {  // lane owns bins 255-8*lane-j, descending
+        for (int j = 0; j < 8; ++j) {
             local[j] = sh.bins[255 - 8 * lane - j];
             s += local[j];
         }
@@ -147,7 +149,7 @@ __device__ void find_bin(SelectShared& sh, unsigned int need) {
             const unsigned int y = __shfl_up_sync(0xffffffffu, x, o);
             if (lane >= o) x += y;
         }
-        unsigned int above = x - s;  // elements in bins above this lane's first bin
+        unsigned int above = x - s;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const unsigned int b = 255 - 8 * lane - j;
@@ -162,10 +164,10 @@ __device__ void find_bin(SelectShared& sh, unsigned int need) {
     __syncthreads();
 }
 
-// Stable LSD pass over m elements: src -> dst by digit 255-((key>>shift)&255),
-// i.e. keys descending, earlier elements first among equal digits.
-__device__ void sort_pass(SelectShared& sh, const unsigned long long* src, unsigned long long* dst,
-                          unsigned int m, int shift) {
+// Stable LSD pass over m elements (key << 32 | id): src -> dst by digit
+// 255 - ((key >> shift) & 255), i.e. keys descending, earlier first on ties.
+__device__ void sort_pass(SelectShared& sh, const unsigned long long* src, unsigned long long* dst, unsigned int m,
+                          int shift) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const unsigned int seg = (m + kWarps - 1) / kWarps;
     const unsigned int begin = min(m, warp * seg), end = min(m, begin + seg);
@@ -173,13 +175,9 @@ __device__ void sort_pass(SelectShared& sh, const unsigned long long* src, unsig
     __syncthreads();
     for (unsigned int base = begin; base < end; base += 32) {
         const unsigned int i = base + lane;
-        const unsigned int d = i < end ? 255u - (unsigned int)((src[i] >> (32 + shift)) & 0xffu) : 0x100u;
-        const unsigned int peers = __match_any_sync(0xffffffffu, d);
-        if (d < 0x100u && lane == __ffs(peers) - 1) sh.hist[warp][d] += __popc(peers);
+        warp_count(sh, i < end ? 255u - (unsigned int)((src[i] >> (32 + shift)) & 0xffu) : 0x100u);
     }
     __syncthreads();
-    // Exclusive scan over (digit, warp) in digit-major order: 8192 counters,
-    // eight consecutive ones per thread.
     unsigned int vals[8], local = 0;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -187,9 +185,7 @@ __device__ void sort_pass(SelectShared& sh, const unsigned long long* src, unsig
         vals[j] = sh.hist[f & 31][f >> 5];
         local += vals[j];
     }
-    unsigned int total;
-    unsigned int off = block_exclusive_scan(local, sh.scan, &total);
-    __syncthreads();
+    unsigned int off = block_exclusive_scan(local, sh.scan, &sh.total);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const unsigned int f = threadIdx.x * 8 + j;
@@ -206,7 +202,7 @@ __device__ void sort_pass(SelectShared& sh, const unsigned long long* src, unsig
         if (d < 0x100u) pos = sh.hist[warp][d] + __popc(peers & lanemask_lt());
         __syncwarp();
         if (d < 0x100u) {
-            if (pos < m) dst[pos] = e;
+            if (pos < m) dst[pos] = e;  // pos < m by construction; the guard keeps a slip in bounds
             if (lane == __ffs(peers) - 1) sh.hist[warp][d] += __popc(peers);
         }
         __syncwarp();
@@ -220,37 +216,51 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(const __grid_consta
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t h = blockIdx.x;
     const unsigned long long n = p.valid;
-    uint16_t* keys = n <= kSmemKeysMax ? reinterpret_cast<uint16_t*>(dyn) : p.gkeys + (unsigned long long)h * n;
+    const bool smem_keys = n <= kSmemKeysMax;
+    uint16_t* keys = smem_keys ? reinterpret_cast<uint16_t*>(dyn) : p.gkeys + (unsigned long long)h * n;
+    const uint16_t* row0 = p.scores;
+    const uint16_t* row = p.scores + (unsigned long long)h * p.stride;
+    // Vector path: 16-byte aligned rows; the tail of a row goes element-wise.
+    const bool vec = (p.stride % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.scores) & 15) == 0) &&
+                     (smem_keys || (reinterpret_cast<uintptr_t>(keys) & 15) == 0);
+    const unsigned long long n8 = vec ? n / 8 : 0;
 
-    // ---- 1. head-0 maximum of the normalised scores, threshold
-    float mx = -INFINITY;
-    unsigned int bad0 = 0;
-    for (unsigned long long i = tid; i < n; i += kThreads) {
-        const uint16_t x = load_norm(p, i);
-        if (!is_finite_half(x)) bad0 = 1;
-        const float v = half_value(x);
-        mx = fmaxf(mx, v);  // NaN never replaces the running maximum, as std::max
-    }
-    mx = warp_max(mx);
-    bad0 = __any_sync(0xffffffffu, bad0);
-    if (lane == 0) {
-        sh.fred[warp] = mx;
-        sh.ured[warp] = bad0;
-    }
-    __syncthreads();
     if (tid == 0) {
-        float m = -INFINITY;
-        unsigned int b = 0;
-        for (int w = 0; w < kWarps; ++w) {
-            m = fmaxf(m, sh.fred[w]);
-            b |= sh.ured[w];
+        sh.maxkey = 0;
+        sh.bad0 = 0;
+        sh.cnt = 0;
+        sh.bad = 0;
+    }
+    zero_hist(sh);
+    // ---- 1a. head-0 maximum key (NaN never becomes the maximum, as std::max)
+    unsigned int mx = 0, bad0 = 0;
+#pragma unroll 4
+    for (unsigned long long g = tid; g < n8; g += kThreads) {
+        const uint4 w = reinterpret_cast<const uint4*>(row0)[g];
+        const uint32_t v[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t key = to_key((v[j >> 1] >> (16 * (j & 1))) & 0xffffu, p.mode);
+            bad0 |= key_nonfinite(key);
+            mx = key_nan(key) ? mx : max(mx, key);
         }
-        sh.fred[0] = m;
-        sh.ured[0] = b;
+    }
+    for (unsigned long long i = n8 * 8 + tid; i < n; i += kThreads) {
+        const uint32_t key = to_key(row0[i], p.mode);
+        bad0 |= key_nonfinite(key);
+        mx = key_nan(key) ? mx : max(mx, key);
+    }
+    mx = __reduce_max_sync(0xffffffffu, mx);
+    bad0 = __any_sync(0xffffffffu, bad0);
+    __syncthreads();
+    if (lane == 0) {
+        atomicMax(&sh.maxkey, mx);
+        if (bad0) atomicOr(&sh.bad0, 1u);
     }
     __syncthreads();
-    const float threshold = half_value(half_bits(sh.fred[0] - p.alpha));
-    const bool head0_bad = !p.cover && sh.ured[0];
+    const float maximum = half_value((uint16_t)key_bits(sh.maxkey));
+    const float threshold = half_value(half_bits(sh.maxkey ? maximum - p.alpha : -INFINITY));
+    const bool head0_bad = !p.cover && sh.bad0;
     const bool thr_bad = !isfinite(threshold);
     if (head0_bad || thr_bad) {
         if (h == 0 && tid == 0) {
@@ -263,38 +273,43 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(const __grid_consta
     }
     const unsigned int thr_key = order_key(half_bits(threshold));
 
-    // ---- 2. own row: keys, count >= threshold
+    // ---- 1b. own row: keys to shared memory, count >= threshold
     unsigned int cnt = 0, bad = 0;
-    const uint16_t* row = p.scores + (unsigned long long)h * p.stride;
-    for (unsigned long long i = tid; i < n; i += kThreads) {
-        const uint16_t s = row[i];
-        const uint16_t x = p.raw ? scale_half(s) : s;
-        const bool nan = (x & 0x7fffu) > 0x7c00u;
-        if (!is_finite_half(x)) bad = 1;
-        const unsigned int key = order_key(x);
-        keys[i] = (uint16_t)key;
-        cnt += (!nan && key >= thr_key) ? 1u : 0u;
+#pragma unroll 4
+    for (unsigned long long g = tid; g < n8; g += kThreads) {
+        const uint4 w = reinterpret_cast<const uint4*>(row)[g];
+        const uint32_t v[4] = {w.x, w.y, w.z, w.w};
+        uint32_t k2[4];
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+            const uint32_t a = to_key(v[j >> 1] & 0xffffu, p.mode), b = to_key(v[j >> 1] >> 16, p.mode);
+            bad |= key_nonfinite(a) | key_nonfinite(b);
+            cnt += (!key_nan(a) && a >= thr_key) + (!key_nan(b) && b >= thr_key);
+            k2[j >> 1] = a | (b << 16);
+        }
+        reinterpret_cast<uint4*>(keys)[g] = make_uint4(k2[0], k2[1], k2[2], k2[3]);
     }
-    cnt = warp_sum_u32(cnt);
+    for (unsigned long long i = n8 * 8 + tid; i < n; i += kThreads) {
+        const uint32_t key = to_key(row[i], p.mode);
+        bad |= key_nonfinite(key);
+        cnt += (!key_nan(key) && key >= thr_key) ? 1u : 0u;
+        keys[i] = (uint16_t)key;
+    }
+    cnt = __reduce_add_sync(0xffffffffu, cnt);
     bad = __any_sync(0xffffffffu, bad);
     if (lane == 0) {
-        sh.ured[warp] = cnt;
-        sh.scan[warp] = bad;
+        atomicAdd(&sh.cnt, cnt);
+        if (bad) atomicOr(&sh.bad, 1u);
     }
     __syncthreads();
     if (tid == 0) {
-        unsigned long long c = 0;
-        unsigned int b = 0;
-        for (int w = 0; w < kWarps; ++w) {
-            c += sh.ured[w];
-            b |= sh.scan[w];
-        }
+        unsigned long long c = sh.cnt;
         if (p.cover) c += 1;  // at most one newly appended current token
         const float rounded = p.fp32_counts ? (float)c : half_value(half_bits((float)c));
         p.header->rounded[h] = rounded;
-        p.header->err[h] = ((!p.cover && b) ? 1u : 0u) | (isfinite(rounded) ? 0u : 2u);
+        p.header->err[h] = ((!p.cover && sh.bad) ? 1u : 0u) | (isfinite(rounded) ? 0u : 2u);
         if (p.counts) p.counts[h] = (uint32_t)c;
-        // ---- 3. grid barrier (bounded)
+        // ---- 2. grid barrier (bounded)
         __threadfence();
         atomicAdd(&p.header->arrived, 1u);
         const unsigned long long start = global_ns();
@@ -304,10 +319,9 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(const __grid_consta
                 sh.timeout = 1;
                 break;
             }
-            __nanosleep(64);
+            __nanosleep(32);
         }
         __threadfence();
-        // Every CTA derives the same status and k from the shared counts.
         unsigned int status = 0, index = 0;
         float total = 0.0f;
         if (!sh.timeout) {
@@ -347,78 +361,133 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(const __grid_consta
     }
     __syncthreads();
     const unsigned long long k = sh.k;
-    if (sh.status || k == 0) return;
+    if (k == 0) return;
 
-    // ---- 4. radix select: K* = k-th largest key
-    key_histogram(sh, keys, n, [](unsigned int key) { return key >> 8; });
+    // ---- 3. radix select: K* = k-th largest key
+    const unsigned long long seg = ((n + kWarps - 1) / kWarps + 31) / 32 * 32;
+    const unsigned long long s0 = min(n, (unsigned long long)warp * seg), s1 = min(n, s0 + seg);
+    for (unsigned long long base = s0; base < s1; base += 32) {
+        const unsigned long long i = base + lane;
+        warp_count(sh, i < s1 ? (unsigned int)keys[i] >> 8 : 0x100u);
+    }
+    __syncthreads();
+    sum_hist(sh);
+    __syncthreads();
     find_bin(sh, (unsigned int)k);
     const unsigned int hi = sh.b_bin, above_hi = sh.b_above;
-    key_histogram(sh, keys, n, [hi](unsigned int key) { return (key >> 8) == hi ? (key & 0xffu) : 0x100u; });
+    zero_hist(sh);
+    __syncthreads();
+    for (unsigned long long base = s0; base < s1; base += 32) {
+        const unsigned long long i = base + lane;
+        const unsigned int key = i < s1 ? keys[i] : 0u;
+        warp_count(sh, (i < s1 && (key >> 8) == hi) ? (key & 0xffu) : 0x100u);
+    }
+    __syncthreads();
+    sum_hist(sh);
+    __syncthreads();
     find_bin(sh, (unsigned int)(k - above_hi));
     const unsigned int kstar = (hi << 8) | sh.b_bin;
     const unsigned int gt = above_hi + sh.b_above;
     const unsigned int need_eq = (unsigned int)k - gt;  // >= 1
     const unsigned int eq_total = sh.b_eqtotal;
 
-    // ---- ordered compaction into sort buffer A (ID order)
-    unsigned long long* bufA = p.sortbuf + (unsigned long long)h * 2 * p.kcap;
-    unsigned long long* bufB = bufA + p.kcap;
-    const unsigned long long seg = (n + kThreads - 1) / kThreads;
-    const unsigned long long b0 = min(n, (unsigned long long)tid * seg), b1 = min(n, b0 + seg);
-    unsigned int n_gt = 0, n_eq = 0;
-    for (unsigned long long i = b0; i < b1; ++i) {
-        const unsigned int key = keys[i];
-        n_gt += key > kstar;
-        n_eq += key == kstar;
+    // ---- 4. ordered compaction (ID order) of keys > K* and the first need_eq ties
+    const bool small = k <= kSmemSortMax;
+    unsigned long long* bufA =
+        small ? reinterpret_cast<unsigned long long*>(dyn + (smem_keys ? ((n * 2 + 15) / 16 * 16) : 0))
+              : p.sortbuf + (unsigned long long)h * 2 * p.kcap;
+    unsigned long long* bufB = bufA + (small ? kSmemSortMax : p.kcap);
+    unsigned int w_gt = 0, w_eq = 0;
+    for (unsigned long long base = s0; base < s1; base += 32) {
+        const unsigned long long i = base + lane;
+        const unsigned int key = i < s1 ? keys[i] : 0u;
+        w_gt += __popc(__ballot_sync(0xffffffffu, i < s1 && key > kstar));
+        w_eq += __popc(__ballot_sync(0xffffffffu, i < s1 && key == kstar));
     }
-    unsigned int tot;
-    const unsigned int gt_before = block_exclusive_scan(n_gt, sh.scan, &tot);
-    unsigned int eq_rank = block_exclusive_scan(n_eq, sh.scan, &tot);
-    unsigned int pos = gt_before + min(eq_rank, need_eq);
+    if (lane == 0) {
+        sh.wa[warp] = w_gt;
+        sh.wb[warp] = w_eq;
+    }
     if (tid == 0) {
         sh.last_id = 0xffffffffu;
         sh.next_id = 0xffffffffu;
     }
     __syncthreads();
-    for (unsigned long long i = b0; i < b1; ++i) {
-        const unsigned int key = keys[i];
-        // pos < k holds by construction; the guard keeps any slip in bounds.
-        if (key > kstar) {
-            if (pos < k) bufA[pos] = ((unsigned long long)key << 32) | (unsigned int)i;
-            ++pos;
-        } else if (key == kstar) {
-            if (eq_rank < need_eq) {
-                if (pos < k) bufA[pos] = ((unsigned long long)key << 32) | (unsigned int)i;
-                ++pos;
-            }
-            if (eq_rank + 1 == need_eq) sh.last_id = (unsigned int)i;
-            if (eq_rank == need_eq) sh.next_id = (unsigned int)i;
-            ++eq_rank;
+    unsigned int gt_before = 0, eq_before = 0;
+    for (int w = 0; w < warp; ++w) {
+        gt_before += sh.wa[w];
+        eq_before += sh.wb[w];
+    }
+    unsigned int pos = gt_before + min(eq_before, need_eq);
+    for (unsigned long long base = s0; base < s1; base += 32) {
+        const unsigned long long i = base + lane;
+        const unsigned int key = i < s1 ? keys[i] : 0u;
+        const bool is_gt = i < s1 && key > kstar;
+        const bool is_eq = i < s1 && key == kstar;
+        const unsigned int meq = __ballot_sync(0xffffffffu, is_eq);
+        const unsigned int my_eq = eq_before + __popc(meq & lanemask_lt());
+        const bool take = is_gt || (is_eq && my_eq < need_eq);
+        const unsigned int mtake = __ballot_sync(0xffffffffu, take);
+        if (take) {
+            const unsigned int at = pos + __popc(mtake & lanemask_lt());
+            if (at < k) bufA[at] = ((unsigned long long)key << 32) | (unsigned int)i;
         }
+        if (is_eq && my_eq + 1 == need_eq) sh.last_id = (unsigned int)i;
+        if (is_eq && my_eq == need_eq) sh.next_id = (unsigned int)i;
+        pos += __popc(mtake);
+        eq_before += __popc(meq);
     }
     __syncthreads();
     // Boundary tie (gqa_policy.cpp:66): the k-th and (k+1)-th ordered IDs carry
-    // the same normalised F16 bits.  Only possible among ties of K*.
+    // the same normalised F16 bits.  Only ties of K* can, and equal keys have
+    // equal bits except +0 / -0, which are told apart from the scores.
     if (!p.cover && tid == 0 && k < n && eq_total > need_eq) {
-        const uint16_t a = load_norm(p, (unsigned long long)h * p.stride + sh.last_id);
-        const uint16_t b = load_norm(p, (unsigned long long)h * p.stride + sh.next_id);
-        if (a == b) atomicAdd(&p.result->boundary_tied_heads, 1u);
+        bool tied = true;
+        if (kstar == 0x8000u) {
+            const unsigned long long base = (unsigned long long)h * p.stride;
+            uint16_t a, b;
+            if (p.mode == kInputKeys) {
+                a = p.tie_raw ? scale_half(p.tie_raw[base + sh.last_id]) : 0;
+                b = p.tie_raw ? scale_half(p.tie_raw[base + sh.next_id]) : 0;
+            } else {
+                a = p.scores[base + sh.last_id];
+                b = p.scores[base + sh.next_id];
+                if (p.mode == kInputRaw) {
+                    a = scale_half(a);
+                    b = scale_half(b);
+                }
+            }
+            tied = a == b;
+        }
+        if (tied) atomicAdd(&p.result->boundary_tied_heads, 1u);
     }
 
-    // ---- 5. stable sort by key descending (low byte, then high byte)
-    __threadfence_block();
+    // ---- 5. reference order: key descending, ID ascending
     __syncthreads();
+    uint32_t* out = p.ids + (unsigned long long)h * p.kcap;
+    if (k <= kRankSortMax) {
+        // rank = #(greater key) + #(equal key earlier in ID order)
+        if ((unsigned)tid < k) {
+            const unsigned long long e = bufA[tid];
+            const unsigned int ek = (unsigned int)(e >> 32);
+            unsigned int r = 0;
+            for (unsigned int j = 0; j < k; ++j) {
+                const unsigned int ok = (unsigned int)(bufA[j] >> 32);
+                r += (ok > ek) || (ok == ek && j < (unsigned)tid);
+            }
+            if (r < k) out[r] = (uint32_t)(e & 0xffffffffu);
+        }
+        return;
+    }
     sort_pass(sh, bufA, bufB, (unsigned int)k, 0);
     sort_pass(sh, bufB, bufA, (unsigned int)k, 8);
-    uint32_t* out = p.ids + (unsigned long long)h * p.kcap;
     for (unsigned int j = tid; j < k; j += kThreads) out[j] = (uint32_t)(bufA[j] & 0xffffffffu);
 }
 
 }  // namespace
 
 size_t select_workspace_bytes(size_t heads, size_t valid, size_t kcap) {
-    size_t bytes = sizeof(SelectHeader);
-    bytes = (bytes + 255) / 256 * 256;
+    size_t bytes = (sizeof(SelectHeader) + 255) / 256 * 256;
     if (valid > kSmemKeysMax) bytes += (heads * valid * 2 + 255) / 256 * 256;
     bytes += heads * 2 * kcap * 8;
     return bytes;
@@ -428,7 +497,8 @@ cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream) {
     const DeviceInfo& dev = device_info();
     SelectParams p{};
     p.scores = s.scores;
-    p.raw = s.raw;
+    p.tie_raw = s.tie_raw;
+    p.mode = s.keys ? kInputKeys : (s.raw ? kInputRaw : kInputScaled);
     p.cover = s.cover;
     p.fp32_counts = s.fp32_counts;
     p.zero_is_error = s.zero_is_error;
@@ -456,11 +526,12 @@ cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream) {
         e = cudaMemsetAsync(s.result, 0, sizeof(hsb_selection), stream);
         if (e != cudaSuccess) return e;
     }
-    const size_t smem = s.valid <= kSmemKeysMax ? (size_t)s.valid * 2 : 0;
+    const size_t keys_bytes = s.valid <= kSmemKeysMax ? ((size_t)s.valid * 2 + 15) / 16 * 16 : 0;
+    const size_t smem = keys_bytes + 2 * kSmemSortMax * 8;
     static thread_local int configured_device = -1;
     if (configured_device != dev.ordinal) {
         e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)(kSmemKeysMax * 2));
+                                 (int)(kSmemKeysMax * 2 + 2 * kSmemSortMax * 8));
         if (e != cudaSuccess) return e;
         configured_device = dev.ordinal;
     }

@@ -120,6 +120,11 @@ int hsb_score_views(const uint16_t* d_q, const hsb_key_view* h_views, size_t nvi
  * any other count is rejected before touching memory. */
 int hsb_score_pipeline_v3(const uint16_t* d_q, const uint16_t* d_keys, uint32_t tokens,
                           uint16_t* d_scores, void* stream);
+/* hsb_score_v3 that also writes, per score, the 16-bit order key
+ * (policy/half_order.hpp:7-10) of its normalised value F16(raw / sqrtf(128))
+ * to d_order_keys [32][tokens] -- the input of hsb_select_keys. */
+int hsb_score_with_keys(const uint16_t* d_q, const uint16_t* d_keys, size_t tokens, size_t stride_words,
+                        uint16_t* d_scores, uint16_t* d_order_keys, void* stream);
 /* The runtime's normalisation (policy/full_gqa_runtime.cpp:571):
  * d_out[i] = F16(F32(d_raw[i]) / sqrtf(128)).  d_out may equal d_raw. */
 int hsb_scale_scores(const uint16_t* d_raw, size_t count, uint16_t* d_out, void* stream);
@@ -144,6 +149,13 @@ int hsb_select(const uint16_t* d_scores, int input_is_raw, size_t heads, size_t 
                size_t valid, float alpha, float ratio, int fp32_counts, uint32_t* d_ids,
                size_t kcap, uint32_t* d_counts, hsb_selection* d_result, void* d_workspace,
                size_t workspace_bytes, void* stream);
+/* hsb_select on order keys of normalised scores (hsb_score_with_keys); the
+ * raw scores d_raw [heads][stride] are read only to tell +0 from -0 when the
+ * boundary-tie rule compares F16 bits.  Same outputs, checks and errors. */
+int hsb_select_keys(const uint16_t* d_order_keys, const uint16_t* d_raw, size_t heads, size_t stride,
+                    size_t valid, float alpha, float ratio, int fp32_counts, uint32_t* d_ids, size_t kcap,
+                    uint32_t* d_counts, hsb_selection* d_result, void* d_workspace,
+                    size_t workspace_bytes, void* stream);
 /* Synchronises, copies *d_result to *h_result and returns its status. */
 int hsb_selection_read(const hsb_selection* d_result, hsb_selection* h_result, void* stream);
 

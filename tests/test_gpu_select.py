@@ -133,7 +133,7 @@ def test_coarse_values_many_ties(cuda, ob):
     n = 5000
     vals = rng.integers(-4, 5, size=H * n).astype(np.float16)
     sc = vals.view(np.uint16).copy()
-    sc[::7] ^= 0x8000 * (sc[::7] == 0)  # some -0
+    sc[::7] ^= (0x8000 * (sc[::7] == 0)).astype(np.uint16)  # some -0
     for alpha in (0.0, 1.0, 3.0, 8.0):
         for ratio in (0.2, 0.5, 1.0):
             same_as_oracle(cuda, ob, sc, H, n, n, alpha, ratio)
@@ -162,3 +162,75 @@ def test_errors_in_reference_order(cuda, ob):
     padded = base.copy().reshape(H, n)
     padded[:, 40:] = 0x7C00
     same_as_oracle(cuda, ob, padded.reshape(-1), H, n, 40, 1.0, 0.2)
+
+
+def _keys_select(hsb, raw_dev, heads, n, alpha, ratio=0.2):
+    """hsb_select_keys on keys derived on the GPU from raw scores."""
+    import torch
+
+    lib = hsb._capi.lib()
+    s = torch.cuda.current_stream().cuda_stream
+    keys = torch.empty_like(raw_dev)
+    # scale then key on the GPU: the scorer path is exercised separately below
+    kcap = max(1, hsb.select_kmax(n, ratio))
+    ids = torch.empty((heads, kcap), dtype=torch.int32, device="cuda")
+    counts = torch.zeros(heads, dtype=torch.int32, device="cuda")
+    res = torch.zeros(4, dtype=torch.int32, device="cuda")
+    ws = hsb._workspace(lib.hsb_select_workspace_bytes(heads, n, n, kcap), "cuda")
+    return lib, s, keys, ids, counts, res, ws, kcap
+
+
+@pytest.mark.parametrize("n,alpha", [(4096, 0.1), (4096, 10.0), (32768, 5.0), (32768, 50.0), (5000, 3.0)])
+def test_score_with_keys_then_select_keys(cuda, ob, n, alpha):
+    """The fused pipeline path: the scorer emits order keys of normalised
+    scores, the selector consumes them -- same IDs/counts/k/ties as the
+    reference chain score -> scale -> select."""
+    import ctypes as C
+
+    import torch
+
+    q, k, _ = inputs.config1(n, seed=9)
+    lib, s, keys, ids, counts, res, ws, kcap = _keys_select(cuda, torch.empty((32, n), dtype=torch.int16,
+                                                                                device="cuda"), 32, n, alpha)
+    raw = torch.empty((32, n), dtype=torch.int16, device="cuda")
+    assert lib.hsb_score_with_keys(dev_u16(q).data_ptr(), dev_u16(k).data_ptr(), n, 1024, raw.data_ptr(),
+                                   keys.data_ptr(), s) == 0
+    assert lib.hsb_select_keys(keys.data_ptr(), raw.data_ptr(), 32, n, n, C.c_float(alpha), C.c_float(0.2), 0,
+                               ids.data_ptr(), kcap, counts.data_ptr(), res.data_ptr(), ws.data_ptr(), ws.numel(),
+                               s) == 0
+    torch.cuda.synchronize()
+    raw_h = ob.score(q, k, n, 1024)
+    assert np.array_equal(host_u16(raw), raw_h)
+    scaled = ob.scale(raw_h)
+    want_keys = np.array([ob.oracle().orc_order_key(int(b)) for b in scaled.reshape(-1)[:4096]], dtype=np.uint16)
+    assert np.array_equal(host_u16(keys).reshape(-1)[:4096], want_keys)
+    wids, wcounts, wk, wtied = ob.select(scaled, 32, n, n, alpha, 0.2)
+    r = res.cpu().numpy()
+    assert r[0] == wk and r[1] == wtied and r[2] == 0
+    assert np.array_equal(counts.cpu().numpy().astype(np.uint32), wcounts)
+    assert np.array_equal(ids[:, :wk].cpu().numpy().astype(np.uint64), wids)
+
+
+def test_select_keys_signed_zero_ties(cuda, ob):
+    """Keys lose the sign of zero; the boundary-tie rule reads it back from the
+    raw scores (gqa_policy.cpp:66 compares F16 bits, so +0 / -0 differ)."""
+    import ctypes as C
+
+    import torch
+
+    n = 512
+    rng = np.random.default_rng(8)
+    raw = np.where(rng.random(32 * n) < 0.5, 0x0000, 0x8000).astype(np.uint16)  # only +0 / -0
+    raw[rng.random(32 * n) < 0.01] = ob.half_bits(8.0)
+    scaled = ob.scale(raw)
+    keys = np.array([ob.oracle().orc_order_key(int(b)) for b in scaled], dtype=np.uint16)
+    for alpha in (0.0, 0.5, 20.0):
+        lib, s, _, ids, counts, res, ws, kcap = _keys_select(cuda, dev_u16(raw), 32, n, alpha)
+        assert lib.hsb_select_keys(dev_u16(keys).data_ptr(), dev_u16(raw).data_ptr(), 32, n, n, C.c_float(alpha),
+                                   C.c_float(0.2), 0, ids.data_ptr(), kcap, counts.data_ptr(), res.data_ptr(),
+                                   ws.data_ptr(), ws.numel(), s) == 0
+        torch.cuda.synchronize()
+        wids, wcounts, wk, wtied = ob.select(scaled, 32, n, n, alpha, 0.2)
+        r = res.cpu().numpy()
+        assert r[0] == wk and r[1] == wtied
+        assert np.array_equal(ids[:, :wk].cpu().numpy().astype(np.uint64), wids)
