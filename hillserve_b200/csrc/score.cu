@@ -13,16 +13,21 @@
 // and keeps the reference's order, which is what makes the result bit-exact;
 // it never reassociates the channel sum.
 //
-// Memory.  The scorer streams K once (2 KB per token) and is HBM-bound.  One
-// persistent CTA per SM: a producer warp moves whole 2 KB token rows into
-// shared memory with 1-D bulk copies (the TMA engine), three stages deep; the
-// eight consumer warps each own one KV head and read their 256-byte slice of
-// 32 rows.  Rows are stored at a 2064-byte pitch so that eight consecutive
-// lanes' 16-byte reads fall in distinct bank groups.  Q lives in shared memory
-// as FP32, laid out [kv head][channel][4 heads] so each channel's four
-// query values are one broadcast 16-byte load.
+// Memory.  The scorer streams K once (2 KB per token) and is HBM-bound.  The
+// production kernel (score_tma_kernel, below) loads 32-token x 64-channel
+// tiles with 3-D tensor-map TMA copies and runs two CTAs per SM.  The
+// row-copy kernel (score_v3_kernel) is kept for the case where a tensor map
+// cannot be encoded: one persistent CTA per SM, a producer warp moving whole
+// 2 KB token rows with 1-D bulk copies into rows of 2064-byte pitch (eight
+// consecutive lanes' 16-byte reads fall in distinct bank groups), and Q in
+// shared memory as FP32 [kv head][channel][4 heads] (one broadcast 16-byte
+// load per channel).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
 #include "internal.h"
@@ -160,6 +165,200 @@ __global__ void __launch_bounds__(kThreads, 1) score_v3_kernel(const __grid_cons
     }
 }
 
+// ===================================================================== TMA
+// The production scorer.  Per CTA: one producer warp and eight consumer
+// warps; two CTAs per SM.  A work tile is 32 tokens x 8 KV heads; it is
+// brought in as two 32 KB half-channel stages (channels 0-63, then 64-127) by
+// 3-D tensor-map TMA loads with the 128-byte swizzle, three stages deep.
+// Lane = (token of 4, KV head of 8), so the eight lanes of a shared-memory
+// phase read eight different 16-byte columns (the swizzle XORs the column
+// with the row's KV head): conflict-free.  Q is kept as F16 [c][kv][4] and the
+// products use the mixed-precision FMA (F16 x F16 + F32 -> F32, one
+// rounding), exact for the same reason as above: no conversions at all.
+constexpr int kTTile = 32;                               // tokens per tile
+constexpr int kTHalf = 64;                               // channels per stage
+constexpr int kTStageBytes = kTTile * kKvHeads * kTHalf * 2;  // 32768
+constexpr int kTStages = 3;
+constexpr int kTConsumerWarps = 8;
+constexpr int kTThreads = (kTConsumerWarps + 1) * 32;
+constexpr int kTQBytes = kDim * kKvHeads * kGroup * 2;   // 8192
+constexpr int kTOutBytes = kHeads * kTTile * 2 * 2;      // scores + keys staging
+constexpr int kTSmemBytes = 1024 + kTStages * kTStageBytes + kTQBytes + kTOutBytes + 64;
+
+struct TmaParams {
+    CUtensorMap maps[HSB_MAX_VIEWS];
+    const uint16_t* q;
+    unsigned long long view_tokens[HSB_MAX_VIEWS];
+    unsigned long long view_tile0[HSB_MAX_VIEWS + 1];  // tile prefix per view
+    unsigned long long view_col[HSB_MAX_VIEWS];        // first output column
+    int nviews;
+    unsigned long long tiles;
+    uint16_t* out;
+    uint16_t* keys;
+    unsigned long long out_stride;
+    hsb_device_status* status;
+};
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+        : "memory");
+}
+__device__ __forceinline__ float fma_f16(uint32_t a16, uint32_t b16, float c) {
+    float d;
+    asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"((unsigned short)a16), "h"((unsigned short)b16), "f"(c));
+    return d;
+}
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+__device__ __forceinline__ int tile_view(const TmaParams& p, unsigned long long tile) {
+    int v = 0;
+#pragma unroll 1
+    while (v + 1 < p.nviews && tile >= p.view_tile0[v + 1]) ++v;
+    return v;
+}
+
+__global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_constant__ TmaParams p) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* stages = smem;
+    uint2* qs = reinterpret_cast<uint2*>(smem + kTStages * kTStageBytes);  // [c][kv] -> 4 F16
+    uint16_t* stage_out = reinterpret_cast<uint16_t*>(smem + kTStages * kTStageBytes + kTQBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTStages * kTStageBytes + kTQBytes + kTOutBytes);
+    uint64_t* empty = full + kTStages;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < kHeads * kDim; i += blockDim.x) {
+        const int h = i >> 7, c = i & 127;
+        reinterpret_cast<uint16_t*>(qs)[(c * kKvHeads + (h >> 2)) * kGroup + (h & 3)] = p.q[i];
+    }
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kTStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kTConsumerWarps);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    if (warp == kTConsumerWarps) {
+        if (lane != 0) return;
+        // ---------------- producer: two half-channel TMA loads per tile
+        uint32_t it = 0;
+        bool ok = true;
+        for (unsigned long long tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
+            const int v = tile_view(p, tile);
+            const int t0 = (int)((tile - p.view_tile0[v]) * kTTile);
+            for (int half = 0; half < 2; ++half, ++it) {
+                const uint32_t s = it % kTStages;
+                if (it >= kTStages && !mbar_wait(&empty[s], ((it / kTStages) - 1) & 1)) {
+                    raise_status(p.status, HSB_E_TIMEOUT, blockIdx.x);
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[s], kTStageBytes);
+                tma_load_3d(stages + s * kTStageBytes, &p.maps[v], half * kTHalf, 0, t0, &full[s]);
+            }
+        }
+        if (!ok) {  // let copies in flight land before shared memory is released
+            const uint32_t first = it > kTStages ? it - kTStages : 0;
+            for (uint32_t j = first; j < it; ++j) (void)mbar_wait(&full[j % kTStages], (j / kTStages) & 1);
+        }
+        return;
+    }
+
+    // ---------------- consumers
+    const int kh = lane & 7, tl = warp * 4 + (lane >> 3);  // KV head, token in tile
+    uint32_t it = 0;
+    for (unsigned long long tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
+        const int v = tile_view(p, tile);
+        const unsigned long long t0 = (tile - p.view_tile0[v]) * kTTile;
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        for (int half = 0; half < 2; ++half, ++it) {
+            const uint32_t s = it % kTStages;
+            if (!mbar_wait(&full[s], (it / kTStages) & 1)) {
+                raise_status(p.status, HSB_E_TIMEOUT, blockIdx.x);
+                return;
+            }
+            const unsigned char* row = stages + s * kTStageBytes + (tl * kKvHeads + kh) * 128;
+            const uint2* qh = qs + (half * kTHalf) * kKvHeads + kh;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint4 w = *reinterpret_cast<const uint4*>(row + ((j ^ kh) << 4));
+                const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const uint32_t kb = (e & 1) ? (words[e >> 1] >> 16) : (words[e >> 1] & 0xffffu);
+                    const uint2 qq = qh[(j * 8 + e) * kKvHeads];
+                    // Exact F16 products => one rounding per step, as the reference.
+                    a0 = fma_f16(qq.x & 0xffffu, kb, a0);
+                    a1 = fma_f16(qq.x >> 16, kb, a1);
+                    a2 = fma_f16(qq.y & 0xffffu, kb, a2);
+                    a3 = fma_f16(qq.y >> 16, kb, a3);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        // Stage the tile's 32 x 32 scores (and keys), then write whole rows.
+        const uint16_t s0 = half_bits(a0), s1 = half_bits(a1), s2 = half_bits(a2), s3 = half_bits(a3);
+        uint16_t* so = stage_out + (kh * kGroup) * kTTile + tl;
+        so[0] = s0;
+        so[kTTile] = s1;
+        so[2 * kTTile] = s2;
+        so[3 * kTTile] = s3;
+        if (p.keys) {
+            uint16_t* sk = so + kHeads * kTTile;
+            sk[0] = (uint16_t)order_key(scale_half(s0));
+            sk[kTTile] = (uint16_t)order_key(scale_half(s1));
+            sk[2 * kTTile] = (uint16_t)order_key(scale_half(s2));
+            sk[3 * kTTile] = (uint16_t)order_key(scale_half(s3));
+        }
+        consumer_sync();
+        const unsigned long long valid = min((unsigned long long)kTTile, p.view_tokens[v] - t0);
+        if ((unsigned long long)lane < valid) {
+            const unsigned long long col = p.view_col[v] + t0 + lane;
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const int h = warp * 4 + r;
+                p.out[h * p.out_stride + col] = stage_out[h * kTTile + lane];
+                if (p.keys) p.keys[h * p.out_stride + col] = stage_out[(kHeads + h) * kTTile + lane];
+            }
+        }
+        consumer_sync();
+    }
+}
+
+// Resolves cuTensorMapEncodeTiled through the runtime (no libcuda link).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+// Token-major keys of one view as a 3-D tensor {channel, KV head, token}.
+bool encode_view(CUtensorMap* map, const hsb_key_view& v) {
+    auto encode = tensor_map_encoder();
+    if (!encode) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)kDim, (cuuint64_t)kKvHeads, (cuuint64_t)v.tokens};
+    const cuuint64_t strides[2] = {(cuuint64_t)kDim * 2, (cuuint64_t)v.stride_words * 2};
+    const cuuint32_t box[3] = {(cuuint32_t)kTHalf, (cuuint32_t)kKvHeads, (cuuint32_t)kTTile};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<uint16_t*>(v.data), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 __global__ void scale_kernel(const uint16_t* __restrict__ raw, unsigned long long count,
                              uint16_t* __restrict__ out) {
     for (unsigned long long i = blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x; i < count;
@@ -177,8 +376,37 @@ cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nv
     if (configured_device != dev.ordinal) {
         cudaError_t e = cudaFuncSetAttribute(score_v3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              kSmemBytes);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(score_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemBytes);
         if (e != cudaSuccess) return e;
         configured_device = dev.ordinal;
+    }
+    // Tensor-map path (all views encodable); else the row-copy kernel.
+    {
+        TmaParams t{};
+        bool ok = tensor_map_encoder() != nullptr;
+        unsigned long long tiles = 0, col = col0;
+        for (size_t v = 0; v < nviews && ok; ++v) {
+            ok = encode_view(&t.maps[v], views[v]);
+            t.view_tokens[v] = views[v].tokens;
+            t.view_tile0[v] = tiles;
+            t.view_col[v] = col;
+            tiles += (views[v].tokens + kTTile - 1) / kTTile;
+            col += views[v].tokens;
+        }
+        if (ok) {
+            t.view_tile0[nviews] = tiles;
+            t.nviews = (int)nviews;
+            t.tiles = tiles;
+            t.q = q;
+            t.out = out;
+            t.keys = keys;
+            t.out_stride = out_stride;
+            t.status = status;
+            const int grid = (int)std::min<unsigned long long>(tiles, (unsigned long long)dev.sms * 2);
+            score_tma_kernel<<<grid, kTThreads, kTSmemBytes, stream>>>(t);
+            return cudaGetLastError();
+        }
     }
     ScoreParams p{};
     p.q = q;

@@ -322,15 +322,43 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(const __grid_consta
             __nanosleep(32);
         }
         __threadfence();
+    }
+    __syncthreads();
+    if (warp == 0) {
+        // All heads' flags and rounded counts, read in parallel (4 per lane),
+        // then folded in head order -- the first error is the reference's.
+        unsigned int e[4] = {0, 0, 0, 0};
+        float r[4] = {0.f, 0.f, 0.f, 0.f};
+        if (!sh.timeout) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t hh = lane * 4 + j;
+                if (hh < p.heads) {
+                    e[j] = __ldcg(&p.header->err[hh]);
+                    r[j] = __ldcg(&p.header->rounded[hh]);
+                }
+            }
+        }
         unsigned int status = 0, index = 0;
         float total = 0.0f;
-        if (!sh.timeout) {
-            for (uint32_t hh = 0; hh < p.heads; ++hh) {
-                const unsigned int e = ((volatile unsigned int*)p.header->err)[hh];
-                if (e & 1u) { status = HSB_E_SEL_NONFINITE; index = hh; break; }
-                if (e & 2u) { status = p.cover ? HSB_E_COVER_COUNT : HSB_E_SEL_COUNT_F16; index = hh; break; }
-                total += ((volatile float*)p.header->rounded)[hh];
+        for (int src = 0; src < 32 && !sh.timeout; ++src) {
+            unsigned int ej[4];
+            float rj[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                ej[j] = __shfl_sync(0xffffffffu, e[j], src);
+                rj[j] = __shfl_sync(0xffffffffu, r[j], src);
             }
+            bool stop = false;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t hh = src * 4 + j;
+                if (stop || hh >= p.heads) continue;
+                if (ej[j] & 1u) { status = HSB_E_SEL_NONFINITE; index = hh; stop = true; continue; }
+                if (ej[j] & 2u) { status = p.cover ? HSB_E_COVER_COUNT : HSB_E_SEL_COUNT_F16; index = hh; stop = true; continue; }
+                total += rj[j];  // FP32 sum in head order (gqa_policy.cpp:60)
+            }
+            if (stop || (uint32_t)(src + 1) * 4 >= p.heads) break;
         }
         unsigned long long k = 0;
         if (!sh.timeout && !status) {
@@ -350,13 +378,15 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(const __grid_consta
         }
         if (sh.timeout) status = HSB_E_TIMEOUT;
         if (!status && k == 0 && p.zero_is_error) status = HSB_E_ZERO_SELECTION;
-        sh.status = status;
-        sh.status_index = index;
-        sh.k = status ? 0 : k;
-        if (h == 0) {
-            p.result->k = (uint32_t)sh.k;
-            p.result->status.code = (int)status;
-            p.result->status.index = (int)index;
+        if (lane == 0) {
+            sh.status = status;
+            sh.status_index = index;
+            sh.k = status ? 0 : k;
+            if (h == 0) {
+                p.result->k = status ? 0u : (uint32_t)k;
+                p.result->status.code = (int)status;
+                p.result->status.index = (int)index;
+            }
         }
     }
     __syncthreads();
