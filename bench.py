@@ -145,33 +145,41 @@ class Model:
         self.ev_dense = [[mk() for _ in range(2)] for _ in range(DENSE)]
         self.lib = lib
 
-    def step(self, stream):
+    def step(self, stream, events: bool = False):
+        """Launches one 32-layer decode step on `stream`.  With events=True,
+        timing events bracket every stage (the profiling replay only; the
+        timed graph carries no event nodes)."""
         lib, P = self.lib, self.hsb._ptr
         s = stream.cuda_stream
         n = self.n
+
+        def mark(e):
+            if events:
+                e.record(stream)
+
         for l in range(self.layers):
             if l < DENSE:
                 e = self.ev_dense[l]
-                e[0].record(stream)
+                mark(e[0])
                 rc = lib.hsb_attention_dense(P(self.q32[l]), P(self.kc[l]), P(self.vc[l]), n, 1024, P(self.out[l]),
                                              P(self.ws_dense), self.ws_dense.numel(), s)
-                e[1].record(stream)
+                mark(e[1])
                 assert rc == 0, lib.hsb_last_error()
                 continue
             e = self.ev[l - DENSE]
             res = self.results[l]
-            e[0].record(stream)
+            mark(e[0])
             rc = lib.hsb_score_with_keys(P(self.q16[l]), P(self.kc[l]), n, 1024, P(self.scores), P(self.keys), s)
-            e[1].record(stream)
+            mark(e[1])
             rc |= lib.hsb_select_keys(P(self.keys), P(self.scores), HEADS, n, n, self.alpha, 0.2, 0, P(self.ids[l]),
                                       self.count, P(self.counts[l]), P(res), P(self.ws_sel), self.ws_sel.numel(), s)
-            e[2].record(stream)
+            mark(e[2])
             rc |= lib.hsb_gather_cache(P(self.ids[l]), self.count, P(res), 0, P(self.kc[l]), P(self.vc[l]), 1024, n,
                                        self.count, 0, P(self.kp), P(self.vp), P(res[2:]), s)
-            e[3].record(stream)
+            mark(e[3])
             rc |= lib.hsb_attention_packed(P(self.q32[l]), P(self.kp), P(self.vp), self.count, None, 0, P(res), 0,
                                            P(self.out[l]), P(self.ws_att), self.ws_att.numel(), s)
-            e[4].record(stream)
+            mark(e[4])
             assert rc == 0, lib.hsb_last_error()
 
     def stage_ms(self):
@@ -222,6 +230,9 @@ def run_ours(args, rank, world, torch, dist):
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         m.step(stream)
+    prof_graph = torch.cuda.CUDAGraph()  # same step with per-stage events
+    with torch.cuda.graph(prof_graph, stream=stream):
+        m.step(stream, events=True)
     for _ in range(max(args.warmup, 3)):
         graph.replay()
     torch.cuda.synchronize()
@@ -241,6 +252,11 @@ def run_ours(args, rank, world, torch, dist):
     if dist:
         dist.barrier()
     ms = start.elapsed_time(stop)
+    # Per-stage breakdown from a separate replay whose graph carries events
+    # (event nodes add their own gaps, so the sum exceeds ms_per_step).
+    with torch.cuda.stream(stream):
+        prof_graph.replay()
+    stream.synchronize()
     stages = m.stage_ms()
     t = torch.tensor([ms], dtype=torch.float64, device="cuda")
     if dist:
@@ -300,6 +316,7 @@ def run_ours(args, rank, world, torch, dist):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(m, torch, args)
     graph.reset()
+    prof_graph.reset()
     return line
 
 

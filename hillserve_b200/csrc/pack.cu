@@ -8,8 +8,9 @@
 // Every gather is index-driven and tiled: a CTA owns (query head, 32 slots);
 // K slices (256 B per slot) are copied with 16-byte loads/stores, V slices go
 // through a shared-memory tile so that the transposed stores of 32 slots are
-// contiguous.  Persistent grids walk (head, slot tile) pairs so that slot
-// counts known only on the device (the selected k) cost no empty CTAs.
+// contiguous.  The grid is (slot-tile stride, query head): each CTA reads its
+// head's list size once and walks only live tiles, so slot counts known only
+// on the device (the selected k) cost no empty work.
 #include <algorithm>
 
 #include "common.cuh"
@@ -161,17 +162,14 @@ template <int Mode>
 __global__ void __launch_bounds__(kThreads) gather_tiles_kernel(const __grid_constant__ PackParams p) {
     __shared__ SlotSource src[kSlotTile];
     __shared__ __align__(16) uint16_t vt[kSlotTile][kVPitch];
-    __shared__ uint32_t sizes[kHeads];
-    // Per-head list sizes are read once; tiles past a head's size cost nothing
-    // unless the reference's zero padding is requested.
-    if (threadIdx.x < kHeads) sizes[threadIdx.x] = head_size(p.sizes, p.sizes_stride, threadIdx.x);
-    __syncthreads();
-    const size_t tiles_per_head = (p.count + kSlotTile - 1) / kSlotTile;
-    const size_t total = tiles_per_head * kHeads;
-    for (size_t item = blockIdx.x; item < total; item += gridDim.x) {
-        const int h = (int)(item / tiles_per_head);
-        const size_t s0 = (item % tiles_per_head) * kSlotTile;
-        const uint32_t size = sizes[h];
+    // Grid: x strides over the slot tiles of query head blockIdx.y.  The head's
+    // list size is read once; tiles past it cost nothing unless the
+    // reference's zero padding is requested.
+    const int h = blockIdx.y;
+    const uint32_t size = head_size(p.sizes, p.sizes_stride, h);
+    const size_t limit = p.zero_padding ? p.count : std::min<size_t>(size, p.count);
+    for (size_t s0 = (size_t)blockIdx.x * kSlotTile; s0 < limit || (s0 == 0 && blockIdx.x == 0);
+         s0 += (size_t)gridDim.x * kSlotTile) {
         if (size > p.kstride || (Mode == 1 && size > p.count)) {
             if (threadIdx.x == 0 && s0 == 0) raise_status(p.status, HSB_E_INVALID, h);
             continue;
@@ -294,6 +292,11 @@ __global__ void stage_rows_kernel(const uint8_t* __restrict__ rows, const uint32
     }
 }
 
+// (slot-tile stride, query head): up to 16 CTAs per head.
+dim3 tile_grid(size_t count) {
+    return dim3((unsigned)std::max<size_t>(1, std::min<size_t>((count + kSlotTile - 1) / kSlotTile, 16)), kHeads);
+}
+
 int persistent_grid(size_t items, int per_sm) {
     const DeviceInfo& dev = device_info();
     return (int)std::max<size_t>(1, std::min<size_t>(items, (size_t)dev.sms * per_sm));
@@ -345,8 +348,7 @@ cudaError_t launch_pack(const uint32_t* ids, size_t kstride, const uint32_t* siz
     p.k = k;
     p.v = v;
     p.status = status;
-    const size_t items = (count + kSlotTile - 1) / kSlotTile * kHeads;
-    gather_tiles_kernel<0><<<persistent_grid(items, 8), kThreads, 0, stream>>>(p);
+    gather_tiles_kernel<0><<<tile_grid(count), kThreads, 0, stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (mask) {
         MaskParams m{ids, kstride, sizes, sizes_stride, positions, npositions, (npositions + 63) / 64 * 64, count, mask};
@@ -384,8 +386,7 @@ cudaError_t launch_gather_cache(const uint32_t* ids, size_t kstride, const uint3
     p.k = k;
     p.v = v;
     p.status = status;
-    const size_t items = (count + kSlotTile - 1) / kSlotTile * kHeads;
-    gather_tiles_kernel<1><<<persistent_grid(items, 8), kThreads, 0, stream>>>(p);
+    gather_tiles_kernel<1><<<tile_grid(count), kThreads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 

@@ -182,7 +182,8 @@ constexpr int kTStages = 3;
 constexpr int kTConsumerWarps = 8;
 constexpr int kTThreads = (kTConsumerWarps + 1) * 32;
 constexpr int kTQBytes = kDim * kKvHeads * kGroup * 2;   // 8192
-constexpr int kTOutBytes = kHeads * kTTile * 2 * 2;      // scores + keys staging
+constexpr int kTOutPitch = kTTile + 1;                   // u32 words per head row (bank spread)
+constexpr int kTOutBytes = kHeads * kTOutPitch * 4;      // (score | key << 16) staging
 constexpr int kTSmemBytes = 1024 + kTStages * kTStageBytes + kTQBytes + kTOutBytes + 64;
 
 struct TmaParams {
@@ -221,10 +222,13 @@ __device__ __forceinline__ int tile_view(const TmaParams& p, unsigned long long 
 
 __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_constant__ TmaParams p) {
     extern __shared__ unsigned char smem_raw[];
-    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // The 128-byte swizzle pattern repeats every 1024 bytes of shared address:
+    // align by offsetting the shared array itself (keeps the pointers in the
+    // shared address space, so accesses stay shared-memory loads).
+    unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     unsigned char* stages = smem;
     uint2* qs = reinterpret_cast<uint2*>(smem + kTStages * kTStageBytes);  // [c][kv] -> 4 F16
-    uint16_t* stage_out = reinterpret_cast<uint16_t*>(smem + kTStages * kTStageBytes + kTQBytes);
+    uint32_t* stage_out = reinterpret_cast<uint32_t*>(smem + kTStages * kTStageBytes + kTQBytes);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTStages * kTStageBytes + kTQBytes + kTOutBytes);
     uint64_t* empty = full + kTStages;
 
@@ -301,19 +305,14 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
-        // Stage the tile's 32 x 32 scores (and keys), then write whole rows.
-        const uint16_t s0 = half_bits(a0), s1 = half_bits(a1), s2 = half_bits(a2), s3 = half_bits(a3);
-        uint16_t* so = stage_out + (kh * kGroup) * kTTile + tl;
-        so[0] = s0;
-        so[kTTile] = s1;
-        so[2 * kTTile] = s2;
-        so[3 * kTTile] = s3;
-        if (p.keys) {
-            uint16_t* sk = so + kHeads * kTTile;
-            sk[0] = (uint16_t)order_key(scale_half(s0));
-            sk[kTTile] = (uint16_t)order_key(scale_half(s1));
-            sk[2 * kTTile] = (uint16_t)order_key(scale_half(s2));
-            sk[3 * kTTile] = (uint16_t)order_key(scale_half(s3));
+        // Stage the tile's 32 x 32 (score | key << 16) words in a padded
+        // [head][token] array (conflict-free both ways), then write rows.
+        const float acc[4] = {a0, a1, a2, a3};
+#pragma unroll
+        for (int g = 0; g < kGroup; ++g) {
+            const uint32_t sc = half_bits(acc[g]);
+            const uint32_t key = p.keys ? order_key(scale_half((uint16_t)sc)) : 0u;
+            stage_out[(kh * kGroup + g) * kTOutPitch + tl] = sc | (key << 16);
         }
         consumer_sync();
         const unsigned long long valid = min((unsigned long long)kTTile, p.view_tokens[v] - t0);
@@ -322,8 +321,9 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
                 const int h = warp * 4 + r;
-                p.out[h * p.out_stride + col] = stage_out[h * kTTile + lane];
-                if (p.keys) p.keys[h * p.out_stride + col] = stage_out[(kHeads + h) * kTTile + lane];
+                const uint32_t w = stage_out[h * kTOutPitch + lane];
+                p.out[h * p.out_stride + col] = (uint16_t)(w & 0xffffu);
+                if (p.keys) p.keys[h * p.out_stride + col] = (uint16_t)(w >> 16);
             }
         }
         consumer_sync();

@@ -14,8 +14,9 @@
 //   2. grid barrier; every CTA reads the per-head counts, rounds them as the
 //      reference does (F16 count, FP32 sum, F16 mean) and derives the same k
 //      and the same first error;
-//   3. radix select: a high-byte histogram and a low-byte pass over the keys
-//      of the chosen bin give the k-th largest key K*;
+//   3. radix select: a 1024-bin histogram of key >> 6 (built while loading)
+//      and a 64-bin pass over the keys of the chosen bin give the k-th
+//      largest key K*;
 //   4. ordered compaction (ballots, warp-contiguous segments) keeps keys > K*
 //      and the first k - #(> K*) ties of K* in ID order;
 //   5. the k survivors are put in reference order -- key descending, ID
@@ -32,7 +33,7 @@ namespace {
 constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
 constexpr unsigned long long kSmemKeysMax = 65536;  // keys kept in shared memory up to this
-constexpr unsigned kSmemSortMax = 4096;             // survivors sorted in shared memory up to this
+constexpr unsigned kSmemSortMax = 2048;             // survivors sorted in shared memory up to this
 constexpr unsigned kRankSortMax = 256;              // rank sort up to this, radix above
 
 enum InputMode { kInputScaled = 0, kInputRaw = 1, kInputKeys = 2 };
@@ -62,6 +63,8 @@ struct SelectParams {
 
 struct SelectShared {
     unsigned int hist[kWarps][256];  // per-warp histograms / scatter offsets
+    unsigned int coarse[1024];       // histogram of key >> 6, built while loading
+    unsigned int fine[64];           // histogram of key & 63 inside the chosen coarse bin
     unsigned int bins[256];
     unsigned int scan[kWarps];
     unsigned int wa[kWarps], wb[kWarps];
@@ -116,52 +119,11 @@ __device__ unsigned int block_exclusive_scan(unsigned int v, unsigned int* scan,
 __device__ __forceinline__ void zero_hist(SelectShared& sh) {
     for (int i = threadIdx.x; i < kWarps * 256; i += kThreads) (&sh.hist[0][0])[i] = 0;
 }
-__device__ __forceinline__ void sum_hist(SelectShared& sh) {
-    if (threadIdx.x < 256) {
-        unsigned int s = 0;
-#pragma unroll 8
-        for (int w = 0; w < kWarps; ++w) s += sh.hist[w][threadIdx.x];
-        sh.bins[threadIdx.x] = s;
-    }
-}
 // Warp-aggregated increment of hist[warp][d] (d == 0x100: nothing).
 __device__ __forceinline__ void warp_count(SelectShared& sh, unsigned int d) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const unsigned int peers = __match_any_sync(0xffffffffu, d);
     if (d < 0x100u && lane == __ffs(peers) - 1) sh.hist[warp][d] += __popc(peers);
-}
-
-// Finds the bin holding the `need`-th largest element: the bin b with
-// (#elements in bins > b) < need <= (#elements in bins >= b).
-__device__ void find_bin(SelectShared& sh, unsigned int need) {
-    if (threadIdx.x < 32) {
-        const int lane = threadIdx.x;
-        unsigned int local[8];
-        unsigned int s = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            local[j] = sh.bins[255 - 8 * lane - j];
-            s += local[j];
-        }
-        unsigned int x = s;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const unsigned int y = __shfl_up_sync(0xffffffffu, x, o);
-            if (lane >= o) x += y;
-        }
-        unsigned int above = x - s;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const unsigned int b = 255 - 8 * lane - j;
-            if (above < need && above + local[j] >= need) {
-                sh.b_bin = b;
-                sh.b_above = above;
-                sh.b_eqtotal = local[j];
-            }
-            above += local[j];
-        }
-    }
-    __syncthreads();
 }
 
 // Stable LSD pass over m elements (key << 32 | id): src -> dst by digit
@@ -231,7 +193,8 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(const __grid_consta
         sh.cnt = 0;
         sh.bad = 0;
     }
-    zero_hist(sh);
+    sh.coarse[tid] = 0;
+    if (tid < 64) sh.fine[tid] = 0;
     // ---- 1a. head-0 maximum key (NaN never becomes the maximum, as std::max)
     unsigned int mx = 0, bad0 = 0;
 #pragma unroll 4
@@ -285,6 +248,8 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(const __grid_consta
             const uint32_t a = to_key(v[j >> 1] & 0xffffu, p.mode), b = to_key(v[j >> 1] >> 16, p.mode);
             bad |= key_nonfinite(a) | key_nonfinite(b);
             cnt += (!key_nan(a) && a >= thr_key) + (!key_nan(b) && b >= thr_key);
+            atomicAdd(&sh.coarse[a >> 6], 1u);
+            atomicAdd(&sh.coarse[b >> 6], 1u);
             k2[j >> 1] = a | (b << 16);
         }
         reinterpret_cast<uint4*>(keys)[g] = make_uint4(k2[0], k2[1], k2[2], k2[3]);
@@ -293,6 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(const __grid_consta
         const uint32_t key = to_key(row[i], p.mode);
         bad |= key_nonfinite(key);
         cnt += (!key_nan(key) && key >= thr_key) ? 1u : 0u;
+        atomicAdd(&sh.coarse[key >> 6], 1u);
         keys[i] = (uint16_t)key;
     }
     cnt = __reduce_add_sync(0xffffffffu, cnt);
@@ -393,30 +359,50 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(const __grid_consta
     const unsigned long long k = sh.k;
     if (k == 0) return;
 
-    // ---- 3. radix select: K* = k-th largest key
+    // ---- 3. radix select: K* = k-th largest key.  Coarse bins (key >> 6) were
+    // counted while loading; thread t owns bin 1023 - t, so an exclusive scan
+    // gives "elements in higher bins".
     const unsigned long long seg = ((n + kWarps - 1) / kWarps + 31) / 32 * 32;
     const unsigned long long s0 = min(n, (unsigned long long)warp * seg), s1 = min(n, s0 + seg);
-    for (unsigned long long base = s0; base < s1; base += 32) {
-        const unsigned long long i = base + lane;
-        warp_count(sh, i < s1 ? (unsigned int)keys[i] >> 8 : 0x100u);
+    {
+        const unsigned int bin = 1023u - tid, c = sh.coarse[bin];
+        const unsigned int above = block_exclusive_scan(c, sh.scan, &sh.total);
+        if (above < k && above + c >= k) {
+            sh.b_bin = bin;
+            sh.b_above = above;
+        }
     }
     __syncthreads();
-    sum_hist(sh);
-    __syncthreads();
-    find_bin(sh, (unsigned int)k);
     const unsigned int hi = sh.b_bin, above_hi = sh.b_above;
-    zero_hist(sh);
-    __syncthreads();
-    for (unsigned long long base = s0; base < s1; base += 32) {
-        const unsigned long long i = base + lane;
-        const unsigned int key = i < s1 ? keys[i] : 0u;
-        warp_count(sh, (i < s1 && (key >> 8) == hi) ? (key & 0xffu) : 0x100u);
+    for (unsigned long long i = tid; i < n; i += kThreads) {
+        const unsigned int key = keys[i];
+        if ((key >> 6) == hi) atomicAdd(&sh.fine[key & 63u], 1u);
     }
     __syncthreads();
-    sum_hist(sh);
+    if (warp == 0) {  // 64 fine bins, two per lane, descending
+        const unsigned int c0 = sh.fine[63 - 2 * lane], c1 = sh.fine[62 - 2 * lane];
+        unsigned int x = c0 + c1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        const unsigned int need = (unsigned int)k - above_hi;
+        unsigned int above = x - c0 - c1;
+        if (above < need && above + c0 >= need) {
+            sh.b_bin = 63 - 2 * lane;
+            sh.b_above = above;
+            sh.b_eqtotal = c0;
+        }
+        above += c0;
+        if (above < need && above + c1 >= need) {
+            sh.b_bin = 62 - 2 * lane;
+            sh.b_above = above;
+            sh.b_eqtotal = c1;
+        }
+    }
     __syncthreads();
-    find_bin(sh, (unsigned int)(k - above_hi));
-    const unsigned int kstar = (hi << 8) | sh.b_bin;
+    const unsigned int kstar = (hi << 6) | sh.b_bin;
     const unsigned int gt = above_hi + sh.b_above;
     const unsigned int need_eq = (unsigned int)k - gt;  // >= 1
     const unsigned int eq_total = sh.b_eqtotal;
