@@ -127,7 +127,7 @@ class Model:
             lib.hsb_synth_keys(self.kc[l].data_ptr(), tokens, 1024, ls * 7 + 2, 0.02, 4.0, 1, THETA, s)
             lib.hsb_synth_keys(self.vc[l].data_ptr(), tokens, 1024, ls * 7 + 3, 0.0, 1.0, 0, THETA, s)
         self.q32.copy_(self.q16.view(torch.float16).float())
-        self.count = hsb.select_kmax(tokens, 0.2)
+        self.count = (hsb.select_kmax(tokens, 0.2) + 31) // 32 * 32  # slot capacity, rows 64-byte aligned
         self.scores = torch.empty((HEADS, tokens), dtype=torch.int16, device=dev)
         self.keys = torch.empty((HEADS, tokens), dtype=torch.int16, device=dev)
         self.ids = torch.empty((layers, HEADS, self.count), dtype=torch.int32, device=dev)

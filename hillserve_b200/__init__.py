@@ -430,7 +430,8 @@ class SelectedKVLayer:
     def __init__(self, valid: int, alpha: float, ratio: float = 0.2, device="cuda"):
         torch = _torch()
         self.valid, self.alpha, self.ratio = int(valid), float(alpha), float(ratio)
-        self.count = max(1, select_kmax(self.valid, self.ratio))
+        # Slot capacity: the largest k, rounded up to 32 so V rows stay aligned.
+        self.count = max(32, (select_kmax(self.valid, self.ratio) + 31) // 32 * 32)
         dev = torch.device(device)
         self.scores = torch.empty((32, self.valid), dtype=torch.int16, device=dev)
         self.ids = torch.empty((32, self.count), dtype=torch.int32, device=dev)

@@ -80,16 +80,27 @@ __global__ void __launch_bounds__(kPThreads) attention_packed_kernel(const __gri
     const int m = (int)(s1 - s0);
 
     const float4 q4 = reinterpret_cast<const float4*>(p.q + h * kDim)[lane];
-    for (int s = warp; s < m; s += 4) {
-        const uint2 raw = *reinterpret_cast<const uint2*>(p.k + ((s0 + s) * kHeads + h) * kDim + lane * 4);
-        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-        float dot = a.x * q4.x + a.y * q4.y + b.x * q4.z + b.y * q4.w;
-        dot = warp_sum(dot);
-        if (lane == 0) {
-            float x = dot * p.scale;
-            if (p.mask) x += p.mask[(size_t)h * p.qpad * p.count + s0 + s];
-            sc[s] = x;
+    // Scores: each warp takes 4 slots per round (loads issued together).
+    for (int base = warp; base < m; base += 16) {
+        uint2 raw[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int s = base + 4 * u;
+            raw[u] = s < m ? *reinterpret_cast<const uint2*>(p.k + ((s0 + s) * kHeads + h) * kDim + lane * 4)
+                           : make_uint2(0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int s = base + 4 * u;
+            const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw[u].x));
+            const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw[u].y));
+            float dot = a.x * q4.x + a.y * q4.y + b.x * q4.z + b.y * q4.w;
+            dot = warp_sum(dot);
+            if (lane == 0 && s < m) {
+                float x = dot * p.scale;
+                if (p.mask) x += p.mask[(size_t)h * p.qpad * p.count + s0 + s];
+                sc[s] = x;
+            }
         }
     }
     __syncthreads();
@@ -106,7 +117,25 @@ __global__ void __launch_bounds__(kPThreads) attention_packed_kernel(const __gri
     // out[d] partial: thread d walks its V row over the split's slots.
     const uint16_t* vrow = p.v + ((size_t)h * kDim + tid) * p.count + s0;
     float acc = 0.0f;
-    for (int s = 0; s < m; ++s) acc = fmaf(sc[s], half_value(vrow[s]), acc);
+    int s = 0;
+    if ((p.count & 7) == 0) {  // rows 16-byte aligned: 8 slots per load, 4 loads in flight
+        for (; s + 32 <= m; s += 32) {
+            uint4 w[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) w[u] = *reinterpret_cast<const uint4*>(vrow + s + 8 * u);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t x[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&x[e]));
+                    acc = fmaf(sc[s + 8 * u + 2 * e], f.x, acc);
+                    acc = fmaf(sc[s + 8 * u + 2 * e + 1], f.y, acc);
+                }
+            }
+        }
+    }
+    for (; s < m; ++s) acc = fmaf(sc[s], half_value(vrow[s]), acc);
     if (live == 1) {  // one split: no partials to fold
         p.out[h * kDim + tid] = l > 0.0f ? acc / l : 0.0f;
         return;

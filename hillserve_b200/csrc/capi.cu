@@ -427,7 +427,8 @@ int hsb_attention_packed(const float* d_q, const uint16_t* d_k, const uint16_t* 
                          size_t workspace_bytes, void* stream) {
     if (!d_q || !d_k || !d_v || !d_out || count == 0 || (!d_mask && !d_sizes) || (d_mask && qpad == 0))
         return fail(HSB_E_INVALID, "attention arguments");
-    if (!aligned(d_q, 16) || !aligned(d_k, 16)) return fail(HSB_E_INVALID, "attention buffers must be 16-byte aligned");
+    if (!aligned(d_q, 16) || !aligned(d_k, 16) || !aligned(d_v, 16))
+        return fail(HSB_E_INVALID, "attention buffers must be 16-byte aligned");
     if (!d_workspace || workspace_bytes < attention_workspace_bytes(count))
         return fail(HSB_E_WORKSPACE, "attention workspace missing or too small");
     cudaError_t e = launch_attention_packed(d_q, d_k, d_v, count, d_mask, qpad, d_sizes, sizes_stride, d_out,

@@ -169,12 +169,15 @@ __global__ void __launch_bounds__(kThreads, 1) score_v3_kernel(const __grid_cons
 // The production scorer.  Per CTA: one producer warp and eight consumer
 // warps; two CTAs per SM.  A work tile is 32 tokens x 8 KV heads; it is
 // brought in as two 32 KB half-channel stages (channels 0-63, then 64-127) by
-// 3-D tensor-map TMA loads with the 128-byte swizzle, three stages deep.
-// Lane = (token of 4, KV head of 8), so the eight lanes of a shared-memory
-// phase read eight different 16-byte columns (the swizzle XORs the column
-// with the row's KV head): conflict-free.  Q is kept as F16 [c][kv][4] and the
-// products use the mixed-precision FMA (F16 x F16 + F32 -> F32, one
-// rounding), exact for the same reason as above: no conversions at all.
+// TMA loads of a 3-D tensor map whose dimensions are ordered {channel, token,
+// KV head}, so the shared tile is [KV head][token][64 channels] with the
+// 128-byte swizzle (16-byte column XOR token % 8), three stages deep.
+// Warp = KV head, lane = token: Q reads are whole-warp broadcasts, K reads of
+// any eight consecutive lanes hit eight different columns (conflict-free), and
+// the four scores of a lane go to four head rows with coalesced stores.  Q is
+// kept as F16 [kv][c][4] and the products use the mixed-precision FMA
+// (F16 x F16 + F32 -> F32, one rounding), exact for the same reason as above:
+// no conversion instructions at all.
 constexpr int kTTile = 32;                               // tokens per tile
 constexpr int kTHalf = 64;                               // channels per stage
 constexpr int kTStageBytes = kTTile * kKvHeads * kTHalf * 2;  // 32768
@@ -182,9 +185,7 @@ constexpr int kTStages = 3;
 constexpr int kTConsumerWarps = 8;
 constexpr int kTThreads = (kTConsumerWarps + 1) * 32;
 constexpr int kTQBytes = kDim * kKvHeads * kGroup * 2;   // 8192
-constexpr int kTOutPitch = kTTile + 1;                   // u32 words per head row (bank spread)
-constexpr int kTOutBytes = kHeads * kTOutPitch * 4;      // (score | key << 16) staging
-constexpr int kTSmemBytes = 1024 + kTStages * kTStageBytes + kTQBytes + kTOutBytes + 64;
+constexpr int kTSmemBytes = 1024 + kTStages * kTStageBytes + kTQBytes + 64;
 
 struct TmaParams {
     CUtensorMap maps[HSB_MAX_VIEWS];
@@ -211,7 +212,6 @@ __device__ __forceinline__ float fma_f16(uint32_t a16, uint32_t b16, float c) {
     asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"((unsigned short)a16), "h"((unsigned short)b16), "f"(c));
     return d;
 }
-__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 __device__ __forceinline__ int tile_view(const TmaParams& p, unsigned long long tile) {
     int v = 0;
@@ -227,15 +227,15 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
     // shared address space, so accesses stay shared-memory loads).
     unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     unsigned char* stages = smem;
-    uint2* qs = reinterpret_cast<uint2*>(smem + kTStages * kTStageBytes);  // [c][kv] -> 4 F16
-    uint32_t* stage_out = reinterpret_cast<uint32_t*>(smem + kTStages * kTStageBytes + kTQBytes);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTStages * kTStageBytes + kTQBytes + kTOutBytes);
+    // Q as F16 [kv][c][4 heads]: one 16-byte load gives channels c, c+1.
+    uint4* qs = reinterpret_cast<uint4*>(smem + kTStages * kTStageBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTStages * kTStageBytes + kTQBytes);
     uint64_t* empty = full + kTStages;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < kHeads * kDim; i += blockDim.x) {
         const int h = i >> 7, c = i & 127;
-        reinterpret_cast<uint16_t*>(qs)[(c * kKvHeads + (h >> 2)) * kGroup + (h & 3)] = p.q[i];
+        reinterpret_cast<uint16_t*>(qs)[((h >> 2) * kDim + c) * kGroup + (h & 3)] = p.q[i];
     }
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTStages; ++s) {
@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
                     break;
                 }
                 mbar_arrive_expect_tx(&full[s], kTStageBytes);
-                tma_load_3d(stages + s * kTStageBytes, &p.maps[v], half * kTHalf, 0, t0, &full[s]);
+                tma_load_3d(stages + s * kTStageBytes, &p.maps[v], half * kTHalf, t0, 0, &full[s]);
             }
         }
         if (!ok) {  // let copies in flight land before shared memory is released
@@ -273,7 +273,8 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
     }
 
     // ---------------- consumers
-    const int kh = lane & 7, tl = warp * 4 + (lane >> 3);  // KV head, token in tile
+    const int kh = warp, tl = lane;  // KV head, token in tile
+    const uint4* qv = qs + kh * (kDim / 2);
     uint32_t it = 0;
     for (unsigned long long tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
         const int v = tile_view(p, tile);
@@ -285,48 +286,41 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
                 raise_status(p.status, HSB_E_TIMEOUT, blockIdx.x);
                 return;
             }
-            const unsigned char* row = stages + s * kTStageBytes + (tl * kKvHeads + kh) * 128;
-            const uint2* qh = qs + (half * kTHalf) * kKvHeads + kh;
+            const unsigned char* row = stages + s * kTStageBytes + (kh * kTTile + tl) * 128;
+            const uint4* qh = qv + half * (kTHalf / 2);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                const uint4 w = *reinterpret_cast<const uint4*>(row + ((j ^ kh) << 4));
+                const uint4 w = *reinterpret_cast<const uint4*>(row + ((j ^ (tl & 7)) << 4));
                 const uint32_t words[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const uint32_t kb = (e & 1) ? (words[e >> 1] >> 16) : (words[e >> 1] & 0xffffu);
-                    const uint2 qq = qh[(j * 8 + e) * kKvHeads];
+                for (int e = 0; e < 8; e += 2) {
+                    const uint4 qq = qh[j * 4 + (e >> 1)];  // channels c, c+1: 4 heads each
+                    const uint32_t k0 = words[e >> 1] & 0xffffu, k1 = words[e >> 1] >> 16;
                     // Exact F16 products => one rounding per step, as the reference.
-                    a0 = fma_f16(qq.x & 0xffffu, kb, a0);
-                    a1 = fma_f16(qq.x >> 16, kb, a1);
-                    a2 = fma_f16(qq.y & 0xffffu, kb, a2);
-                    a3 = fma_f16(qq.y >> 16, kb, a3);
+                    a0 = fma_f16(qq.x & 0xffffu, k0, a0);
+                    a1 = fma_f16(qq.x >> 16, k0, a1);
+                    a2 = fma_f16(qq.y & 0xffffu, k0, a2);
+                    a3 = fma_f16(qq.y >> 16, k0, a3);
+                    a0 = fma_f16(qq.z & 0xffffu, k1, a0);
+                    a1 = fma_f16(qq.z >> 16, k1, a1);
+                    a2 = fma_f16(qq.w & 0xffffu, k1, a2);
+                    a3 = fma_f16(qq.w >> 16, k1, a3);
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
-        // Stage the tile's 32 x 32 (score | key << 16) words in a padded
-        // [head][token] array (conflict-free both ways), then write rows.
-        const float acc[4] = {a0, a1, a2, a3};
+        if ((unsigned long long)tl < p.view_tokens[v] - t0) {
+            const unsigned long long col = p.view_col[v] + t0 + tl;
+            const float acc[4] = {a0, a1, a2, a3};
 #pragma unroll
-        for (int g = 0; g < kGroup; ++g) {
-            const uint32_t sc = half_bits(acc[g]);
-            const uint32_t key = p.keys ? order_key(scale_half((uint16_t)sc)) : 0u;
-            stage_out[(kh * kGroup + g) * kTOutPitch + tl] = sc | (key << 16);
-        }
-        consumer_sync();
-        const unsigned long long valid = min((unsigned long long)kTTile, p.view_tokens[v] - t0);
-        if ((unsigned long long)lane < valid) {
-            const unsigned long long col = p.view_col[v] + t0 + lane;
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const int h = warp * 4 + r;
-                const uint32_t w = stage_out[h * kTOutPitch + lane];
-                p.out[h * p.out_stride + col] = (uint16_t)(w & 0xffffu);
-                if (p.keys) p.keys[h * p.out_stride + col] = (uint16_t)(w >> 16);
+            for (int g = 0; g < kGroup; ++g) {
+                const uint16_t sc = half_bits(acc[g]);
+                const unsigned long long at = (unsigned long long)(kh * kGroup + g) * p.out_stride + col;
+                p.out[at] = sc;
+                if (p.keys) p.keys[at] = (uint16_t)order_key(scale_half(sc));
             }
         }
-        consumer_sync();
     }
 }
 
@@ -346,13 +340,15 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// Token-major keys of one view as a 3-D tensor {channel, KV head, token}.
+// Token-major keys of one view seen as a 3-D tensor {channel, token, KV head}
+// (strides: token = stride_words words, KV head = 128 words), so that a box
+// lands in shared memory as [KV head][token][channels].
 bool encode_view(CUtensorMap* map, const hsb_key_view& v) {
     auto encode = tensor_map_encoder();
     if (!encode) return false;
-    const cuuint64_t dims[3] = {(cuuint64_t)kDim, (cuuint64_t)kKvHeads, (cuuint64_t)v.tokens};
-    const cuuint64_t strides[2] = {(cuuint64_t)kDim * 2, (cuuint64_t)v.stride_words * 2};
-    const cuuint32_t box[3] = {(cuuint32_t)kTHalf, (cuuint32_t)kKvHeads, (cuuint32_t)kTTile};
+    const cuuint64_t dims[3] = {(cuuint64_t)kDim, (cuuint64_t)v.tokens, (cuuint64_t)kKvHeads};
+    const cuuint64_t strides[2] = {(cuuint64_t)v.stride_words * 2, (cuuint64_t)kDim * 2};
+    const cuuint32_t box[3] = {(cuuint32_t)kTHalf, (cuuint32_t)kTTile, (cuuint32_t)kKvHeads};
     const cuuint32_t estr[3] = {1, 1, 1};
     return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<uint16_t*>(v.data), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
