@@ -306,7 +306,7 @@ def run_ours(args, rank, world, torch, dist):
                               "attention over an empty selection returns zeros"},
         "score_select_gather": {"bytes": b_score + b_select + b_gather, "GB_s": round(ssg_gbs, 1),
                                 "frac_of_peak": round(ssg_gbs / peak, 4), "peak_GB_s": peak, "peak_kind": peak_kind},
-        "roofline": {"kernel": "score_v3_kernel", "bound": "hbm", "achieved": round(score_gbs, 1), "peak": peak,
+        "roofline": {"kernel": "score_tma_kernel", "bound": "hbm", "achieved": round(score_gbs, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(score_gbs / peak, 4), "traffic": traffic,
                      "algorithmic_bytes_per_launch": b_score, "peak_kind": peak_kind},
         "e2e": e2e,
