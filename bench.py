@@ -279,7 +279,7 @@ def run_ours(args, rank, world, torch, dist):
     peak, peak_kind = peaks()
     score_gbs = b_score / (stages["score"] / 1e3) / 1e9
     ssg_gbs = (b_score + b_select + b_gather) / (stages["score_select_gather"] / 1e3) / 1e9
-    traffic = ncu_traffic()
+    traffic = ncu_traffic() if n == N else None  # the capture is of the N=32768 launch
 
     line = {
         "metric": "selected-KV decode layer-steps/s at N=32K (score+select+gather HBM GB/s vs peak)",
@@ -375,7 +375,7 @@ def run_e2e(m, graph, stream, torch, args, dist):
 
 def ncu_traffic():
     """DRAM bytes per scorer launch from the committed ncu summary, if any."""
-    p = ROOT / "profiles" / "score_v3_traffic.json"
+    p = ROOT / "profiles" / "score_tma_kernel_n32768_traffic.json"
     if p.exists():
         try:
             return json.loads(p.read_text()).get("dram_bytes_per_launch_full_size")
