@@ -1,8 +1,15 @@
 // select.cu -- stage 2: the gqa_policy selector (policy/gqa_policy.cpp:47-70)
 // and the history-only prefetch cover (policy/full_gqa_runtime.cpp:299-344).
 //
-// One CTA of 1024 threads per query head, launched cooperatively so that all
-// heads are resident and can meet at one bounded grid barrier.
+// Two kernels, both launched cooperatively so that all CTAs are resident and
+// can meet at one bounded grid barrier (the cross-head count exchange):
+//  - select_cluster_kernel (valid <= 65536, the usual case): each head is a
+//    cluster of four 512-thread CTAs, each owning a quarter of the head's
+//    tokens, sharing histograms through distributed shared memory;
+//  - select_kernel (longer rows, or more heads than clusters fit): one CTA
+//    of 1024 threads per head.
+// The steps below are those of select_kernel; the cluster kernel runs the
+// same steps on its chunk and combines per-chunk histograms and counts.
 //
 // Everything works on 16-bit order keys of the normalised F16 scores (the key
 // order is the FP32 comparator order with -0 == +0, policy/half_order.hpp):
@@ -21,8 +28,11 @@
 //      and the first k - #(> K*) ties of K* in ID order;
 //   5. the k survivors are put in reference order -- key descending, ID
 //      ascending -- by a rank sort (small k) or a stable LSD radix sort.
+#include <cooperative_groups.h>
+
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 
 #include "common.cuh"
 #include "internal.h"
@@ -44,6 +54,7 @@ struct SelectHeader {
     unsigned int pad[31];
     unsigned int err[128];  // bit0 non-finite score, bit1 rounded count overflow
     float rounded[128];
+    unsigned int cnt[128];  // cluster path: per-head threshold counts, summed over the head's CTAs
 };
 
 struct SelectParams {
@@ -65,7 +76,6 @@ struct SelectShared {
     unsigned int hist[kWarps][256];  // per-warp histograms / scatter offsets
     unsigned int coarse[1024];       // histogram of key >> 6, built while loading
     unsigned int fine[64];           // histogram of key & 63 inside the chosen coarse bin
-    unsigned int bins[256];
     unsigned int scan[kWarps];
     unsigned int wa[kWarps], wb[kWarps];
     unsigned int b_bin, b_above, b_eqtotal, total;
@@ -88,8 +98,11 @@ __device__ __forceinline__ uint32_t to_key(uint32_t v, int mode) {
     return order_key(mode == kInputRaw ? scale_half((uint16_t)v) : v);
 }
 
-// Block-wide exclusive scan of one u32 per thread; the total goes to *total.
+// Block-wide exclusive scan of one u32 per thread (NT threads); the total
+// goes to *total.  scan[] holds one word per warp.
+template <int NT>
 __device__ unsigned int block_exclusive_scan(unsigned int v, unsigned int* scan, unsigned int* total) {
+    constexpr int kW = NT / 32;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     unsigned int x = v;
 #pragma unroll
@@ -100,14 +113,14 @@ __device__ unsigned int block_exclusive_scan(unsigned int v, unsigned int* scan,
     if (lane == 31) scan[warp] = x;
     __syncthreads();
     if (warp == 0) {
-        const unsigned int w = scan[lane];
+        const unsigned int w = lane < kW ? scan[lane] : 0u;
         unsigned int s = w;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const unsigned int y = __shfl_up_sync(0xffffffffu, s, o);
             if (lane >= o) s += y;
         }
-        scan[lane] = s - w;
+        if (lane < kW) scan[lane] = s - w;
         if (lane == 31) *total = s;
     }
     __syncthreads();
@@ -116,42 +129,39 @@ __device__ unsigned int block_exclusive_scan(unsigned int v, unsigned int* scan,
     return r;
 }
 
-__device__ __forceinline__ void zero_hist(SelectShared& sh) {
-    for (int i = threadIdx.x; i < kWarps * 256; i += kThreads) (&sh.hist[0][0])[i] = 0;
-}
-// Warp-aggregated increment of hist[warp][d] (d == 0x100: nothing).
-__device__ __forceinline__ void warp_count(SelectShared& sh, unsigned int d) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const unsigned int peers = __match_any_sync(0xffffffffu, d);
-    if (d < 0x100u && lane == __ffs(peers) - 1) sh.hist[warp][d] += __popc(peers);
-}
-
 // Stable LSD pass over m elements (key << 32 | id): src -> dst by digit
 // 255 - ((key >> shift) & 255), i.e. keys descending, earlier first on ties.
-__device__ void sort_pass(SelectShared& sh, const unsigned long long* src, unsigned long long* dst, unsigned int m,
-                          int shift) {
+// hist is [NT / 32][256] per-warp counts / scatter offsets.
+template <int NT>
+__device__ void sort_pass(unsigned int (*hist)[256], unsigned int* scan, unsigned int* total,
+                          const unsigned long long* src, unsigned long long* dst, unsigned int m, int shift) {
+    constexpr int kW = NT / 32;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const unsigned int seg = (m + kWarps - 1) / kWarps;
+    const unsigned int seg = (m + kW - 1) / kW;
     const unsigned int begin = min(m, warp * seg), end = min(m, begin + seg);
-    zero_hist(sh);
+    for (int i = threadIdx.x; i < kW * 256; i += NT) (&hist[0][0])[i] = 0;
     __syncthreads();
     for (unsigned int base = begin; base < end; base += 32) {
         const unsigned int i = base + lane;
-        warp_count(sh, i < end ? 255u - (unsigned int)((src[i] >> (32 + shift)) & 0xffu) : 0x100u);
+        const unsigned int d = i < end ? 255u - (unsigned int)((src[i] >> (32 + shift)) & 0xffu) : 0x100u;
+        const unsigned int peers = __match_any_sync(0xffffffffu, d);
+        if (d < 0x100u && lane == __ffs(peers) - 1) hist[warp][d] += __popc(peers);
     }
     __syncthreads();
-    unsigned int vals[8], local = 0;
+    // Entry f = digit * kW + warp: digit-major, warp-minor -> stable offsets.
+    constexpr int kPer = kW * 256 / NT;  // 8
+    unsigned int vals[kPer], local = 0;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const unsigned int f = threadIdx.x * 8 + j;  // f = digit*32 + warp
-        vals[j] = sh.hist[f & 31][f >> 5];
+    for (int j = 0; j < kPer; ++j) {
+        const unsigned int f = threadIdx.x * kPer + j;
+        vals[j] = hist[f % kW][f / kW];
         local += vals[j];
     }
-    unsigned int off = block_exclusive_scan(local, sh.scan, &sh.total);
+    unsigned int off = block_exclusive_scan<NT>(local, scan, total);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const unsigned int f = threadIdx.x * 8 + j;
-        sh.hist[f & 31][f >> 5] = off;
+    for (int j = 0; j < kPer; ++j) {
+        const unsigned int f = threadIdx.x * kPer + j;
+        hist[f % kW][f / kW] = off;
         off += vals[j];
     }
     __syncthreads();
@@ -161,11 +171,11 @@ __device__ void sort_pass(SelectShared& sh, const unsigned long long* src, unsig
         const unsigned int d = i < end ? 255u - (unsigned int)((e >> (32 + shift)) & 0xffu) : 0x100u;
         const unsigned int peers = __match_any_sync(0xffffffffu, d);
         unsigned int pos = 0;
-        if (d < 0x100u) pos = sh.hist[warp][d] + __popc(peers & lanemask_lt());
+        if (d < 0x100u) pos = hist[warp][d] + __popc(peers & lanemask_lt());
         __syncwarp();
         if (d < 0x100u) {
             if (pos < m) dst[pos] = e;  // pos < m by construction; the guard keeps a slip in bounds
-            if (lane == __ffs(peers) - 1) sh.hist[warp][d] += __popc(peers);
+            if (lane == __ffs(peers) - 1) hist[warp][d] += __popc(peers);
         }
         __syncwarp();
     }
@@ -366,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(const __grid_consta
     const unsigned long long s0 = min(n, (unsigned long long)warp * seg), s1 = min(n, s0 + seg);
     {
         const unsigned int bin = 1023u - tid, c = sh.coarse[bin];
-        const unsigned int above = block_exclusive_scan(c, sh.scan, &sh.total);
+        const unsigned int above = block_exclusive_scan<kThreads>(c, sh.scan, &sh.total);
         if (above < k && above + c >= k) {
             sh.b_bin = bin;
             sh.b_above = above;
@@ -495,9 +505,492 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(const __grid_consta
         }
         return;
     }
-    sort_pass(sh, bufA, bufB, (unsigned int)k, 0);
-    sort_pass(sh, bufB, bufA, (unsigned int)k, 8);
+    sort_pass<kThreads>(sh.hist, sh.scan, &sh.total, bufA, bufB, (unsigned int)k, 0);
+    sort_pass<kThreads>(sh.hist, sh.scan, &sh.total, bufB, bufA, (unsigned int)k, 8);
     for (unsigned int j = tid; j < k; j += kThreads) out[j] = (uint32_t)(bufA[j] & 0xffffffffu);
+}
+
+
+// ------------------------------------------------------------------ cluster path
+// The same selector with each head spread over a cluster of kCluster CTAs
+// (kCThreads threads each, two CTAs per SM): CTA r of head h owns the
+// contiguous token chunk [r*cs, (r+1)*cs), keeps its keys in its own shared
+// memory, and the cluster shares histograms through distributed shared
+// memory.  Chunks are in ID order, so the cluster prefix of a CTA's
+// survivors is its place in ID order.  Synchronisation per call: one bounded
+// grid barrier (the cross-head count exchange, with the cluster barrier's
+// release/acquire split around it) and two cluster barriers.
+namespace cg = cooperative_groups;
+constexpr int kCluster = 4;
+constexpr int kCThreads = 512;
+constexpr int kCWarps = kCThreads / 32;
+constexpr unsigned long long kClusterKeysMax = 65536;           // valid tokens per head on this path
+constexpr unsigned long long kCChunkMax = kClusterKeysMax / kCluster;
+
+struct ClusterShared {
+    unsigned int hist[kCWarps][256];  // leader: LSD sort offsets
+    unsigned int coarse[1024];        // histogram of key >> 6 over this CTA's chunk
+    unsigned int fine[64];            // key & 63 inside the chosen coarse bin, this chunk
+    unsigned int scan[32];
+    unsigned int red[kCWarps][kCluster];
+    unsigned int maxkey, bad0, cnt, bad;
+    unsigned int b_bin, b_above, b_eqtotal, total;
+    unsigned int gt_before, eq_before;  // survivors of the cluster's earlier chunks
+    unsigned int last_id, next_id;      // leader: the need_eq-th and next tie of K*
+    unsigned int status, status_index;
+    unsigned long long k;
+    int timeout;
+};
+
+__device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
+    select_cluster_kernel(const __grid_constant__ SelectParams p) {
+    extern __shared__ __align__(16) unsigned char dyn[];
+    __shared__ ClusterShared sh;
+    cg::cluster_group cl = cg::this_cluster();
+    const unsigned int r = cl.block_rank();
+    const uint32_t h = blockIdx.x / kCluster;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const unsigned long long n = p.valid;
+    const unsigned long long cs = ((n + kCluster - 1) / kCluster + 7) / 8 * 8;
+    const unsigned long long b0 = min(n, (unsigned long long)r * cs), b1 = min(n, b0 + cs);
+    const unsigned int m = (unsigned int)(b1 - b0);
+    uint16_t* keys = reinterpret_cast<uint16_t*>(dyn);  // [cs] this chunk's keys
+    unsigned long long* bufA = reinterpret_cast<unsigned long long*>(dyn + (cs * 2 + 15) / 16 * 16);
+    unsigned long long* bufB = bufA + kSmemSortMax;
+    const uint16_t* row0 = p.scores;
+    const uint16_t* row = p.scores + (unsigned long long)h * p.stride;
+    // 16-byte loads when rows are 16-byte aligned (b0 is a multiple of 8).
+    const bool vec = (p.stride % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.scores) & 15) == 0);
+    const unsigned long long n8 = vec ? n / 8 : 0;
+    const unsigned int m8 = vec ? m / 8 : 0;
+
+    if (tid == 0) {
+        sh.maxkey = 0;
+        sh.bad0 = 0;
+        sh.cnt = 0;
+        sh.bad = 0;
+        sh.last_id = 0xffffffffu;
+        sh.next_id = 0xffffffffu;
+    }
+    for (int i = tid; i < 1024; i += kCThreads) sh.coarse[i] = 0;
+    if (tid < 64) sh.fine[tid] = 0;
+    __syncthreads();
+
+    // ---- 1. head-0 maximum over the whole row (every CTA, from L2), own
+    // chunk's keys to shared memory with the coarse histogram.
+    unsigned int mx = 0, bad0 = 0, bad = 0;
+#pragma unroll 4
+    for (unsigned long long g = tid; g < n8; g += kCThreads) {
+        const uint4 w = reinterpret_cast<const uint4*>(row0)[g];
+        const uint32_t v[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t key = to_key((v[j >> 1] >> (16 * (j & 1))) & 0xffffu, p.mode);
+            bad0 |= key_nonfinite(key);
+            mx = key_nan(key) ? mx : max(mx, key);
+        }
+    }
+    for (unsigned long long i = n8 * 8 + tid; i < n; i += kCThreads) {
+        const uint32_t key = to_key(row0[i], p.mode);
+        bad0 |= key_nonfinite(key);
+        mx = key_nan(key) ? mx : max(mx, key);
+    }
+    for (unsigned int g = tid; g < m8; g += kCThreads) {
+        const uint4 w = reinterpret_cast<const uint4*>(row + b0)[g];
+        const uint32_t v[4] = {w.x, w.y, w.z, w.w};
+        uint32_t k2[4];
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+            const uint32_t a = to_key(v[j >> 1] & 0xffffu, p.mode), b = to_key(v[j >> 1] >> 16, p.mode);
+            bad |= key_nonfinite(a) | key_nonfinite(b);
+            atomicAdd(&sh.coarse[a >> 6], 1u);
+            atomicAdd(&sh.coarse[b >> 6], 1u);
+            k2[j >> 1] = a | (b << 16);
+        }
+        reinterpret_cast<uint4*>(keys)[g] = make_uint4(k2[0], k2[1], k2[2], k2[3]);
+    }
+    for (unsigned int i = m8 * 8 + tid; i < m; i += kCThreads) {
+        const uint32_t key = to_key(row[b0 + i], p.mode);
+        bad |= key_nonfinite(key);
+        atomicAdd(&sh.coarse[key >> 6], 1u);
+        keys[i] = (uint16_t)key;
+    }
+    mx = __reduce_max_sync(0xffffffffu, mx);
+    bad0 = __any_sync(0xffffffffu, bad0);
+    if (lane == 0) {
+        atomicMax(&sh.maxkey, mx);
+        if (bad0) atomicOr(&sh.bad0, 1u);
+    }
+    __syncthreads();
+    const float maximum = half_value((uint16_t)key_bits(sh.maxkey));
+    const float threshold = half_value(half_bits(sh.maxkey ? maximum - p.alpha : -INFINITY));
+    const bool head0_bad = !p.cover && sh.bad0;
+    const bool thr_bad = !isfinite(threshold);
+    if (head0_bad || thr_bad) {
+        if (blockIdx.x == 0 && tid == 0) {
+            p.result->k = 0;
+            p.result->status.code = head0_bad ? HSB_E_SEL_NONFINITE_HEAD0
+                                              : (p.cover ? HSB_E_COVER_THRESHOLD : HSB_E_SEL_THRESHOLD);
+            p.result->status.index = 0;
+        }
+        return;  // every CTA of the grid takes this branch; nothing is pending
+    }
+    const unsigned int thr_key = order_key(half_bits(threshold));
+    unsigned int cnt = 0;
+    for (unsigned int i = tid; i < m; i += kCThreads) {
+        const unsigned int key = keys[i];
+        cnt += (!key_nan(key) && key >= thr_key) ? 1u : 0u;
+    }
+    cnt = __reduce_add_sync(0xffffffffu, cnt);
+    bad = __any_sync(0xffffffffu, bad);
+    if (lane == 0) {
+        if (cnt) atomicAdd(&sh.cnt, cnt);
+        if (bad) atomicOr(&sh.bad, 1u);
+    }
+    __syncthreads();
+    // The coarse histograms are complete: release them to the cluster now,
+    // acquire after the grid barrier.
+    cluster_arrive_release();
+    if (tid == 0) {
+        if (sh.cnt) atomicAdd(&p.header->cnt[h], sh.cnt);
+        if (!p.cover && sh.bad) atomicOr(&p.header->err[h], 1u);
+        // ---- 2. grid barrier (bounded)
+        __threadfence();
+        atomicAdd(&p.header->arrived, 1u);
+        const unsigned long long start = global_ns();
+        sh.timeout = 0;
+        while (ld_acquire(&p.header->arrived) < gridDim.x) {  // plain loads: no RMW traffic on the line
+            if (global_ns() - start > kWaitLimitNs) {
+                sh.timeout = 1;
+                break;
+            }
+            __nanosleep(20);
+        }
+        __threadfence();
+    }
+    __syncthreads();
+    cluster_wait_acquire();
+    if (warp == 0) {
+        // Per-head counts (4 heads per lane), F16 rounding, fold in head order.
+        unsigned int e[4] = {0, 0, 0, 0};
+        float rr[4] = {0.f, 0.f, 0.f, 0.f};
+        unsigned long long own = 0;
+        if (!sh.timeout) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t hh = lane * 4 + j;
+                if (hh < p.heads) {
+                    unsigned long long c = __ldcg(&p.header->cnt[hh]);
+                    if (p.cover) c += 1;  // at most one newly appended current token
+                    const float rounded = p.fp32_counts ? (float)c : half_value(half_bits((float)c));
+                    e[j] = (__ldcg(&p.header->err[hh]) & 1u) | (isfinite(rounded) ? 0u : 2u);
+                    rr[j] = rounded;
+                    if (hh == h) own = c;
+                }
+            }
+        }
+        own = __reduce_max_sync(0xffffffffu, (unsigned int)own);
+        if (r == 0 && lane == 0 && p.counts && !sh.timeout) p.counts[h] = (uint32_t)own;
+        // First failing head in head order (non-finite before count overflow
+        // within a head), found by ballot.  The rounded counts are integers
+        // below 2^16 and there are at most 128 of them, so every partial sum
+        // is an integer below 2^24 and exact in FP32: the tree sum equals the
+        // reference's sequential FP32 sum (gqa_policy.cpp:60) bit for bit.
+        unsigned int my_status = 0, my_index = 0;
+#pragma unroll
+        for (int j = 3; j >= 0; --j) {
+            if (e[j]) {
+                my_status = (e[j] & 1u) ? HSB_E_SEL_NONFINITE : (p.cover ? HSB_E_COVER_COUNT : HSB_E_SEL_COUNT_F16);
+                my_index = lane * 4 + j;
+            }
+        }
+        const unsigned int failing = __ballot_sync(0xffffffffu, my_status != 0);
+        unsigned int status = 0, index = 0;
+        if (failing) {
+            const int src = __ffs(failing) - 1;
+            status = __shfl_sync(0xffffffffu, my_status, src);
+            index = __shfl_sync(0xffffffffu, my_index, src);
+        }
+        float total = (rr[0] + rr[1]) + (rr[2] + rr[3]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+        unsigned long long k = 0;
+        if (!sh.timeout && !status) {
+            const float mean = p.fp32_counts ? __fdiv_rn(total, (float)p.heads)
+                                             : half_value(half_bits(__fdiv_rn(total, (float)p.heads)));
+            if (p.cover) {
+                if (!(isfinite(mean) && mean >= 1.0f)) status = HSB_E_COVER_MEAN;
+                else k = min(p.cover_cap, (unsigned long long)mean);
+            } else {
+                if (!isfinite(mean)) status = HSB_E_SEL_MEAN_F16;
+                else {
+                    k = (unsigned long long)mean;
+                    const unsigned long long cap = (unsigned long long)floor((double)n * (double)p.ratio);
+                    k = min(k, min(cap, n));
+                }
+            }
+        }
+        if (sh.timeout) status = HSB_E_TIMEOUT;
+        if (!status && k == 0 && p.zero_is_error) status = HSB_E_ZERO_SELECTION;
+        if (lane == 0) {
+            sh.status = status;
+            sh.status_index = index;
+            sh.k = status ? 0 : k;
+            // *result starts zeroed (the launcher clears it).
+            if (blockIdx.x == 0) p.result->k = status ? 0u : (uint32_t)k;
+            if (sh.timeout) raise_status(&p.result->status, HSB_E_TIMEOUT, (int)blockIdx.x);
+            else if (blockIdx.x == 0 && status) raise_status(&p.result->status, (int)status, (int)index);
+        }
+    }
+    __syncthreads();
+    if (sh.timeout) {
+        // Cluster peers that passed the barrier may still read this CTA's
+        // shared memory: stay resident through their two cluster barriers.
+        cl.sync();
+        cl.sync();
+        return;
+    }
+    const unsigned long long k = sh.k;
+    if (k == 0) return;  // the same k in every CTA that passed the barrier
+
+    // ---- 3. radix select over the cluster's histograms.  Thread t owns
+    // coarse bins 1023 - 2t and 1022 - 2t (descending).
+    const unsigned int bin0 = 1023u - 2u * tid, bin1 = bin0 - 1u;
+    unsigned int cq0[kCluster], cq1[kCluster];
+#pragma unroll
+    for (int q = 0; q < kCluster; ++q) {
+        const unsigned int* rc = cl.map_shared_rank(&sh.coarse[0], q);
+        cq0[q] = rc[bin0];
+        cq1[q] = rc[bin1];
+    }
+    unsigned int c0 = 0, c1 = 0;
+#pragma unroll
+    for (int q = 0; q < kCluster; ++q) {
+        c0 += cq0[q];
+        c1 += cq1[q];
+    }
+    {
+        const unsigned int above = block_exclusive_scan<kCThreads>(c0 + c1, sh.scan, &sh.total);
+        if (above < k && above + c0 >= k) {
+            sh.b_bin = bin0;
+            sh.b_above = above;
+        } else if (above + c0 < k && above + c0 + c1 >= k) {
+            sh.b_bin = bin1;
+            sh.b_above = above + c0;
+        }
+    }
+    __syncthreads();
+    const unsigned int hi = sh.b_bin, above_hi = sh.b_above;
+    // Per-chunk counts above the chosen coarse bin (for the cluster prefix).
+#pragma unroll
+    for (int q = 0; q < kCluster; ++q) {
+        unsigned int v = (bin0 > hi ? cq0[q] : 0u) + (bin1 > hi ? cq1[q] : 0u);
+        v = __reduce_add_sync(0xffffffffu, v);
+        if (lane == 0) sh.red[warp][q] = v;
+    }
+    for (unsigned int i = tid; i < m; i += kCThreads) {
+        const unsigned int key = keys[i];
+        if ((key >> 6) == hi) atomicAdd(&sh.fine[key & 63u], 1u);
+    }
+    cl.sync();  // every chunk's fine histogram is complete
+    if (warp == 0) {  // 64 fine bins, two per lane, descending
+        unsigned int f0[kCluster], f1[kCluster], s0 = 0, s1 = 0;
+#pragma unroll
+        for (int q = 0; q < kCluster; ++q) {
+            const unsigned int* rf = cl.map_shared_rank(&sh.fine[0], q);
+            f0[q] = rf[63 - 2 * lane];
+            f1[q] = rf[62 - 2 * lane];
+            s0 += f0[q];
+            s1 += f1[q];
+        }
+        unsigned int x = s0 + s1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        const unsigned int need = (unsigned int)k - above_hi;
+        unsigned int above = x - s0 - s1;
+        int found = -1;
+        unsigned int f_above = 0, f_eq = 0;
+        if (above < need && above + s0 >= need) {
+            found = 63 - 2 * lane;
+            f_above = above;
+            f_eq = s0;
+        } else if (above + s0 < need && above + s0 + s1 >= need) {
+            found = 62 - 2 * lane;
+            f_above = above + s0;
+            f_eq = s1;
+        }
+        const unsigned int who = __ballot_sync(0xffffffffu, found >= 0);
+        const int src = __ffs(who) - 1;  // exactly one lane holds the bin
+        const int b2 = __shfl_sync(0xffffffffu, found, src);
+        f_above = __shfl_sync(0xffffffffu, f_above, src);
+        f_eq = __shfl_sync(0xffffffffu, f_eq, src);
+        // Per-chunk gt / eq counts of K* = (hi << 6) | b2, then the prefix of
+        // the chunks before this CTA.
+        unsigned int gt_before = 0, eq_before = 0;
+#pragma unroll
+        for (int q = 0; q < kCluster; ++q) {
+            unsigned int g = ((63 - 2 * lane) > b2 ? f0[q] : 0u) + ((62 - 2 * lane) > b2 ? f1[q] : 0u);
+            unsigned int eq = ((63 - 2 * lane) == b2 ? f0[q] : 0u) + ((62 - 2 * lane) == b2 ? f1[q] : 0u);
+            g = __reduce_add_sync(0xffffffffu, g);
+            eq = __reduce_add_sync(0xffffffffu, eq);
+            unsigned int cg_above = 0;
+            for (int w = 0; w < kCWarps; ++w) cg_above += sh.red[w][q];
+            if ((unsigned int)q < r) {
+                gt_before += g + cg_above;
+                eq_before += eq;
+            }
+        }
+        if (lane == 0) {
+            sh.b_bin = (unsigned int)b2;
+            sh.b_above = f_above;
+            sh.b_eqtotal = f_eq;
+            sh.gt_before = gt_before;
+            sh.eq_before = eq_before;
+        }
+    }
+    __syncthreads();
+    const unsigned int kstar = (hi << 6) | sh.b_bin;
+    const unsigned int gt = above_hi + sh.b_above;
+    const unsigned int need_eq = (unsigned int)k - gt;  // >= 1
+    const unsigned int eq_total = sh.b_eqtotal;
+
+    // ---- 4. ordered compaction of this chunk into the leader's buffer (or
+    // the head's workspace buffer when k exceeds it)
+    const bool small = k <= kSmemSortMax;
+    unsigned long long* dst = small ? cl.map_shared_rank(bufA, 0) : p.sortbuf + (unsigned long long)h * 2 * p.kcap;
+    ClusterShared* lead = cl.map_shared_rank(&sh, 0);
+    // Thread t owns keys [t*per, t*per + per) of the chunk (ID order follows
+    // thread order); one block scan of (gt << 16 | eq) places its survivors.
+    const unsigned int per = ((m + kCThreads - 1) / kCThreads + 7) / 8 * 8;
+    const unsigned int j0 = min(m, tid * per), j1 = min(m, j0 + per);
+    unsigned int n_gt = 0, n_eq = 0;
+    for (unsigned int j = j0; j < j1; j += 8) {
+        uint32_t w[4];
+        if (j + 8 <= j1) {
+            const uint4 v = *reinterpret_cast<const uint4*>(keys + j);
+            w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const uint32_t lo = j + 2 * e < j1 ? keys[j + 2 * e] : 0u;
+                const uint32_t hi16 = j + 2 * e + 1 < j1 ? keys[j + 2 * e + 1] : 0u;
+                w[e] = lo | (hi16 << 16);  // positions past j1 are masked below
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const bool in = j + e < j1;
+            const uint32_t key = (w[e >> 1] >> (16 * (e & 1))) & 0xffffu;
+            n_gt += (in && key > kstar) ? 1u : 0u;
+            n_eq += (in && key == kstar) ? 1u : 0u;
+        }
+    }
+    const unsigned int excl = block_exclusive_scan<kCThreads>((n_gt << 16) | n_eq, sh.scan, &sh.total);
+    if (n_gt | n_eq) {
+        unsigned int gt_run = sh.gt_before + (excl >> 16), eq_run = sh.eq_before + (excl & 0xffffu);
+        for (unsigned int j = j0; j < j1; ++j) {
+            const unsigned int key = keys[j];
+            const unsigned int id = (unsigned int)(b0 + j);
+            if (key > kstar) {
+                const unsigned int at = gt_run + min(eq_run, need_eq);
+                if (at < k) dst[at] = ((unsigned long long)key << 32) | id;
+                ++gt_run;
+            } else if (key == kstar) {
+                if (eq_run < need_eq) {
+                    const unsigned int at = gt_run + eq_run;
+                    if (at < k) dst[at] = ((unsigned long long)key << 32) | id;
+                }
+                if (eq_run + 1 == need_eq) lead->last_id = id;
+                if (eq_run == need_eq) lead->next_id = id;
+                ++eq_run;
+            }
+        }
+    }
+    cl.sync();  // survivors and tie witnesses are in the leader
+    if (r != 0) return;
+
+    // ---- leader: boundary tie (gqa_policy.cpp:66) and reference order
+    unsigned long long* src = small ? bufA : p.sortbuf + (unsigned long long)h * 2 * p.kcap;
+    unsigned long long* tmp = small ? bufB : src + p.kcap;
+    if (!p.cover && tid == 0 && k < n && eq_total > need_eq && sh.last_id < n && sh.next_id < n) {
+        bool tied = true;
+        if (kstar == 0x8000u) {
+            const unsigned long long base = (unsigned long long)h * p.stride;
+            uint16_t a, b;
+            if (p.mode == kInputKeys) {
+                a = p.tie_raw ? scale_half(p.tie_raw[base + sh.last_id]) : 0;
+                b = p.tie_raw ? scale_half(p.tie_raw[base + sh.next_id]) : 0;
+            } else {
+                a = p.scores[base + sh.last_id];
+                b = p.scores[base + sh.next_id];
+                if (p.mode == kInputRaw) {
+                    a = scale_half(a);
+                    b = scale_half(b);
+                }
+            }
+            tied = a == b;
+        }
+        if (tied) atomicAdd(&p.result->boundary_tied_heads, 1u);
+    }
+    uint32_t* out = p.ids + (unsigned long long)h * p.kcap;
+    if (k <= kRankSortMax) {
+        if ((unsigned)tid < k) {
+            const unsigned long long e = src[tid];
+            const unsigned int ek = (unsigned int)(e >> 32);
+            unsigned int rk = 0;
+            for (unsigned int j = 0; j < k; ++j) {
+                const unsigned int ok = (unsigned int)(src[j] >> 32);
+                rk += (ok > ek) || (ok == ek && j < (unsigned)tid);
+            }
+            if (rk < k) out[rk] = (uint32_t)(e & 0xffffffffu);
+        }
+        return;
+    }
+    sort_pass<kCThreads>(sh.hist, sh.scan, &sh.total, src, tmp, (unsigned int)k, 0);
+    sort_pass<kCThreads>(sh.hist, sh.scan, &sh.total, tmp, src, (unsigned int)k, 8);
+    for (unsigned int j = tid; j < k; j += kCThreads) out[j] = (uint32_t)(src[j] & 0xffffffffu);
+}
+
+// Heads (clusters of kCluster CTAs) the cluster path can hold resident at
+// once on a device, at its largest shared-memory size; 0 if unavailable.
+// Computed once per device (with that device current).
+int cluster_capacity(int device) {
+    static std::mutex mu;
+    static int cap[64];
+    static bool known[64] = {};
+    if (device < 0 || device >= 64) return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!known[device]) {
+        int c = 0;
+        const int smem = (int)(kCChunkMax * 2 + 2 * kSmemSortMax * 8);
+        if (cudaFuncSetAttribute(select_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) ==
+            cudaSuccess) {
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(kCluster * 32);
+            cfg.blockDim = dim3(kCThreads);
+            cfg.dynamicSmemBytes = smem;
+            if (cudaOccupancyMaxActiveClusters(&c, select_cluster_kernel, &cfg) != cudaSuccess) c = 0;
+        }
+        (void)cudaGetLastError();
+        cap[device] = c;
+        known[device] = true;
+    }
+    return cap[device];
 }
 
 }  // namespace
@@ -542,8 +1035,21 @@ cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream) {
         e = cudaMemsetAsync(s.result, 0, sizeof(hsb_selection), stream);
         if (e != cudaSuccess) return e;
     }
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (s.valid <= kClusterKeysMax && s.heads <= (uint32_t)cluster_capacity(dev.ordinal)) {
+        const size_t cs = ((size_t)s.valid + kCluster - 1) / kCluster;
+        cfg.gridDim = dim3(s.heads * kCluster);
+        cfg.blockDim = dim3(kCThreads);
+        cfg.dynamicSmemBytes = ((cs + 7) / 8 * 8 * 2 + 15) / 16 * 16 + 2 * kSmemSortMax * 8;
+        return cudaLaunchKernelEx(&cfg, select_cluster_kernel, p);
+    }
     const size_t keys_bytes = s.valid <= kSmemKeysMax ? ((size_t)s.valid * 2 + 15) / 16 * 16 : 0;
-    const size_t smem = keys_bytes + 2 * kSmemSortMax * 8;
     static thread_local int configured_device = -1;
     if (configured_device != dev.ordinal) {
         e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -551,16 +1057,9 @@ cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         configured_device = dev.ordinal;
     }
-    cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(s.heads);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.dynamicSmemBytes = keys_bytes + 2 * kSmemSortMax * 8;
     return cudaLaunchKernelEx(&cfg, select_kernel, p);
 }
 
