@@ -63,6 +63,7 @@ _SIGNATURES = {
     "hsb_stage_rows": (I, [P, P, P, SZ, P, P]),
     "hsb_attention_workspace_bytes": (SZ, [SZ]),
     "hsb_attention_packed": (I, [P, P, P, SZ, P, SZ, P, SZ, P, P, SZ, P]),
+    "hsb_attention_packed_noalloc": (I, [P, P, P, SZ, P, SZ, P, SZ, P, P]),
     "hsb_attention_dense_workspace_bytes": (SZ, [SZ]),
     "hsb_attention_dense": (I, [P, P, P, SZ, SZ, P, P, SZ, P]),
     "hsb_rehearsal_query": (I, [P, P, U64, F, P, P, P]),

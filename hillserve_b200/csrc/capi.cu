@@ -34,6 +34,9 @@ std::mutex g_dev_mutex;
 DeviceInfo g_devices[64];
 }  // namespace
 
+int record_error(int status, const char* message) { return fail(status, message); }
+int record_cuda_error(cudaError_t e, const char* what) { return fail_cuda(e, what); }
+
 const DeviceInfo& device_info() {
     int dev = 0;
     cudaGetDevice(&dev);

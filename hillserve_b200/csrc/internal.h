@@ -28,6 +28,11 @@ cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nv
 cudaError_t launch_scale(const uint16_t* raw, size_t count, uint16_t* out, cudaStream_t stream);
 
 // Stage 2
+// Sets the thread-local message read by hsb_last_error() and returns status
+// (record_cuda_error: HSB_E_CUDA with the runtime's error string appended).
+int record_error(int status, const char* message);
+int record_cuda_error(cudaError_t e, const char* what);
+
 struct SelectLaunch {
     const uint16_t* scores;
     int raw;           // normalise in the kernel

@@ -227,6 +227,24 @@ int hsb_attention_packed(const float* d_q, const uint16_t* d_k, const uint16_t* 
                          size_t count, const float* d_mask, size_t qpad,
                          const uint32_t* d_sizes, size_t sizes_stride, float* d_out,
                          void* d_workspace, size_t workspace_bytes, void* stream);
+/* hsb_attention_packed without a workspace argument; it has no counterpart in
+ * the reference.  It is meant for callers that cannot provide or allocate any
+ * device memory beyond their inputs and outputs: an operator run inside a
+ * host framework's compute graph, whose tensors are handed to it and whose
+ * allocator owns device memory, or a step captured in global capture mode,
+ * where cudaMalloc is refused.  The scratch is a static device array of
+ * 448 KiB that every GPU loading this library holds until exit; count must be
+ * <= HSB_NOALLOC_MAX_SLOTS (the reference delivery workspace's slot limit),
+ * else HSB_E_WORKSPACE.  The call allocates nothing.  The first call on each
+ * device resolves the array's address (cudaGetSymbolAddress) and should come
+ * before any stream capture.  All calls on a device share the array and its
+ * last contents: calls that overlap on the GPU race, so order them on one
+ * stream. */
+#define HSB_NOALLOC_MAX_SLOTS 6592
+int hsb_attention_packed_noalloc(const float* d_q, const uint16_t* d_k, const uint16_t* d_v,
+                                 size_t count, const float* d_mask, size_t qpad,
+                                 const uint32_t* d_sizes, size_t sizes_stride, float* d_out,
+                                 void* stream);
 /* Dense decode attention over a token-major cache (dense layers,
  * runtime/gqa_executor.cpp:174-176). */
 size_t hsb_attention_dense_workspace_bytes(size_t tokens);
