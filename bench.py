@@ -19,6 +19,7 @@ max over ranks.  --impl reference times the reference HillServe CPU path
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import math
 import os
@@ -41,7 +42,7 @@ THETA = 500000.0
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--alpha", type=float, default=0.1)
@@ -139,19 +140,30 @@ class Model:
         self.ws_sel = hsb._workspace(lib.hsb_select_workspace_bytes(HEADS, tokens, tokens, self.count), dev)
         self.ws_att = hsb._workspace(lib.hsb_attention_workspace_bytes(self.count), dev)
         self.ws_dense = hsb._workspace(lib.hsb_attention_dense_workspace_bytes(tokens), dev)
+        self.ws_layer = hsb._workspace(lib.hsb_layer_workspace_bytes(tokens, self.count), dev)
+        self.buffers = [hsb._capi.LayerBuffers(self.scores.data_ptr(), self.ids[l].data_ptr(),
+                                               self.counts[l].data_ptr(), self.results[l].data_ptr(),
+                                               self.kp.data_ptr(), self.vp.data_ptr(), self.ws_layer.data_ptr(),
+                                               self.ws_layer.numel()) for l in range(layers)]
         nsparse = layers - DENSE
         mk = lambda: torch.cuda.Event(enable_timing=True, external=True)  # noqa: E731
         self.ev = [[mk() for _ in range(5)] for _ in range(nsparse)]
+        self.ev_layer = [[mk() for _ in range(2)] for _ in range(nsparse)]
         self.ev_dense = [[mk() for _ in range(2)] for _ in range(DENSE)]
         self.lib = lib
 
-    def step(self, stream, events: bool = False):
-        """Launches one 32-layer decode step on `stream`.  With events=True,
-        timing events bracket every stage (the profiling replay only; the
-        timed graph carries no event nodes)."""
+    def step(self, stream, mode: str = "timed"):
+        """Launches one 32-layer decode step on `stream`.
+
+        timed:  selected-KV layers through hsb_layer_step (score -> select ->
+                fused gather + attention, three kernels), no event nodes;
+        layers: the same with events around each layer step (profiling);
+        stages: the four separate C-ABI calls with events between them
+                (profiling: per-stage attribution)."""
         lib, P = self.lib, self.hsb._ptr
         s = stream.cuda_stream
         n = self.n
+        events = mode != "timed"
 
         def mark(e):
             if events:
@@ -163,6 +175,15 @@ class Model:
                 mark(e[0])
                 rc = lib.hsb_attention_dense(P(self.q32[l]), P(self.kc[l]), P(self.vc[l]), n, 1024, P(self.out[l]),
                                              P(self.ws_dense), self.ws_dense.numel(), s)
+                mark(e[1])
+                assert rc == 0, lib.hsb_last_error()
+                continue
+            if mode in ("timed", "layers"):
+                e = self.ev_layer[l - DENSE]
+                mark(e[0])
+                rc = lib.hsb_layer_step(P(self.q16[l]), P(self.q32[l]), P(self.kc[l]), P(self.vc[l]), 1024, n,
+                                        self.alpha, 0.2, self.count, ctypes.byref(self.buffers[l]),
+                                        P(self.out[l]), s)
                 mark(e[1])
                 assert rc == 0, lib.hsb_last_error()
                 continue
@@ -196,6 +217,10 @@ class Model:
                 "attention": float(np.mean(at)), "dense_attention": float(np.mean(dn)) if dn else 0.0,
                 "score_select_gather": float(np.mean(np.array(sc) + np.array(se) + np.array(ga)))}
 
+    def layer_ms(self):
+        """Mean duration (ms) of one hsb_layer_step in the last 'layers' replay."""
+        return float(np.mean([e[0].elapsed_time(e[1]) for e in self.ev_layer])) if self.ev_layer else 0.0
+
     def selection_stats(self):
         """k per sparse layer and physical-union sizes (outside timing)."""
         torch, hsb = self.torch, self.hsb
@@ -227,12 +252,18 @@ def run_ours(args, rank, world, torch, dist):
     with torch.cuda.stream(stream):
         m.step(stream)  # eager run: sets kernel attributes before capture
     stream.synchronize()
+    with torch.cuda.stream(stream):
+        m.step(stream, "stages")  # eager: the separate-call path's attributes too
+    stream.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         m.step(stream)
-    prof_graph = torch.cuda.CUDAGraph()  # same step with per-stage events
+    prof_graph = torch.cuda.CUDAGraph()  # separate C-ABI calls with per-stage events
     with torch.cuda.graph(prof_graph, stream=stream):
-        m.step(stream, events=True)
+        m.step(stream, "stages")
+    layer_graph = torch.cuda.CUDAGraph()  # the timed step with events around each layer step
+    with torch.cuda.graph(layer_graph, stream=stream):
+        m.step(stream, "layers")
     for _ in range(max(args.warmup, 3)):
         graph.replay()
     torch.cuda.synchronize()
@@ -258,6 +289,10 @@ def run_ours(args, rank, world, torch, dist):
         prof_graph.replay()
     stream.synchronize()
     stages = m.stage_ms()
+    with torch.cuda.stream(stream):
+        layer_graph.replay()
+    stream.synchronize()
+    stages["layer_step"] = m.layer_ms()
     t = torch.tensor([ms], dtype=torch.float64, device="cuda")
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -279,6 +314,8 @@ def run_ours(args, rank, world, torch, dist):
     peak, peak_kind = peaks()
     score_gbs = b_score / (stages["score"] / 1e3) / 1e9
     ssg_gbs = (b_score + b_select + b_gather) / (stages["score_select_gather"] / 1e3) / 1e9
+    b_attn = 16384 * mean_k + 16384
+    layer_gbs = (b_score + b_select + b_gather + b_attn) / (stages["layer_step"] / 1e3) / 1e9
     traffic = ncu_traffic() if n == N else None  # the capture is of the N=32768 launch
 
     line = {
@@ -305,7 +342,11 @@ def run_ours(args, rank, world, torch, dist):
                       "note": "k==0 is the reference's own outcome at this alpha (it throws there); "
                               "attention over an empty selection returns zeros"},
         "score_select_gather": {"bytes": b_score + b_select + b_gather, "GB_s": round(ssg_gbs, 1),
-                                "frac_of_peak": round(ssg_gbs / peak, 4), "peak_GB_s": peak, "peak_kind": peak_kind},
+                                "frac_of_peak": round(ssg_gbs / peak, 4), "peak_GB_s": peak, "peak_kind": peak_kind,
+                                "path": "separate C-ABI calls (score_with_keys, select_keys, gather_cache)"},
+        "layer_step": {"bytes": b_score + b_select + b_gather + b_attn, "us": round(stages["layer_step"] * 1e3, 2),
+                       "GB_s": round(layer_gbs, 1), "frac_of_peak": round(layer_gbs / peak, 4),
+                       "path": "hsb_layer_step (score -> select -> fused gather + attention), the timed path"},
         "roofline": {"kernel": "score_tma_kernel", "bound": "hbm", "achieved": round(score_gbs, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(score_gbs / peak, 4), "traffic": traffic,
                      "algorithmic_bytes_per_launch": b_score, "peak_kind": peak_kind},
@@ -317,12 +358,13 @@ def run_ours(args, rank, world, torch, dist):
         line["cpu_baseline"] = cpu_baseline(m, torch, args)
     graph.reset()
     prof_graph.reset()
+    layer_graph.reset()
     return line
 
 
 def kernel_launches_per_step(layers: int) -> int:
-    # dense: 1 kernel; sparse: score, select, gather, attention
-    return DENSE * 1 + (layers - DENSE) * 4
+    # dense: 1 kernel; selected-KV layer step: score, select, gather+attention
+    return DENSE * 1 + (layers - DENSE) * 3
 
 
 def run_e2e(m, graph, stream, torch, args, dist):

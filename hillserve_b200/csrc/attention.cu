@@ -363,4 +363,217 @@ cudaError_t launch_attention_dense(const float* q, const uint16_t* kcache, const
     return cudaGetLastError();
 }
 
+// ------------------------------------------------------------ gather + attention
+// The layer step's last stage in one kernel: for each (query head, 32-slot
+// tile) of the selection it reads the selected K/V rows once from the HBM
+// cache, writes them to the packed workspace (K [slot][32][128] straight from
+// registers, V [32][128][slot] transposed through shared memory; live slots
+// only, as hsb_gather_cache with zero_padding 0), and from the same data forms
+// the tile's softmax partial (max, sum, P.V).  The last tile of a head to
+// finish folds the head's partials.  Work items (tile-major, head-minor) are
+// spread over a fixed grid, so a small selection occupies few CTAs.
+namespace {
+constexpr int kGAThreads = 128;  // thread t: slot t / 4 of the tile, channel quarter t % 4
+constexpr int kGAPitch = kDim + 8;  // V tile row pitch in halves (16-byte aligned rows)
+
+struct GatherAttnParams {
+    const float* q;         // F32 [32][128]
+    const uint32_t* ids;    // [32][kstride], per-head order (key desc, id asc)
+    size_t kstride;
+    const uint32_t* size;   // the selection's k (same for every head)
+    const uint16_t* kcache;
+    const uint16_t* vcache;
+    size_t stride_words, visible, count;
+    uint16_t* kp;           // [count][32][128]
+    uint16_t* vp;           // [32][128][count]
+    float* out;             // [32][128]
+    float* part;            // [32][tiles_cap][kPart]
+    unsigned* arrive;       // [32], zero at launch
+    unsigned tiles_cap;
+    hsb_device_status* status;
+    float scale;
+};
+
+__global__ void __launch_bounds__(kGAThreads) gather_attention_kernel(const __grid_constant__ GatherAttnParams p) {
+    __shared__ __align__(16) uint16_t vt[32][kGAPitch];
+    __shared__ float wgt[32];
+    __shared__ float red[4];
+    __shared__ int last;
+    const int tid = threadIdx.x, slot = tid >> 2, qd = tid & 3;
+    uint32_t k = *p.size;
+    if (k > p.kstride || k > p.count) {  // cannot come from the selector; keep every access in bounds
+        if (blockIdx.x == 0 && tid == 0) raise_status(p.status, HSB_E_INVALID, 0);
+        k = 0;
+    }
+    if (k == 0) {  // empty selection: zero output (the reference throws earlier)
+        if (blockIdx.x == 0)
+            for (int i = tid; i < kHeads * kDim; i += kGAThreads) p.out[i] = 0.0f;
+        return;
+    }
+    const unsigned ntiles = (k + 31) / 32;
+    const unsigned items = ntiles * kHeads;
+    const bool vec_v = (p.count & 7) == 0;
+    for (unsigned item = blockIdx.x; item < items; item += gridDim.x) {
+        const int h = (int)(item % kHeads), kh = h >> 2;
+        const unsigned tile = item / kHeads, s0 = tile * 32;
+        const int live = (int)min(32u, k - s0);
+        // ---- rows of this thread's slot (quarter qd: channels 32*qd .. 32*qd+31)
+        uint4 kr[4], vr[4];
+        bool ok = slot < live;
+        if (ok) {
+            const uint32_t id = p.ids[(size_t)h * p.kstride + s0 + slot];
+            if (id >= p.visible) {
+                raise_status(p.status, HSB_E_PACK_MISSING, h);
+                ok = false;
+            } else {
+                const uint4* ks = reinterpret_cast<const uint4*>(p.kcache + (size_t)id * p.stride_words + kh * kDim) + qd * 4;
+                const uint4* vs = reinterpret_cast<const uint4*>(p.vcache + (size_t)id * p.stride_words + kh * kDim) + qd * 4;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    kr[u] = __ldg(ks + u);
+                    vr[u] = __ldg(vs + u);
+                }
+            }
+        }
+        if (!ok) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) kr[u] = vr[u] = make_uint4(0, 0, 0, 0);
+        }
+        if (slot < live) {
+            uint4* kd = reinterpret_cast<uint4*>(p.kp + ((size_t)(s0 + slot) * kHeads + h) * kDim) + qd * 4;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) kd[u] = kr[u];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) *reinterpret_cast<uint4*>(&vt[slot][qd * 32 + u * 8]) = vr[u];
+        // ---- logit of the slot: four quarter dot products, combined by shuffles
+        const float4* qv = reinterpret_cast<const float4*>(p.q + h * kDim + qd * 32);
+        float dot = 0.0f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float4 qa = __ldg(qv + 2 * u), qb = __ldg(qv + 2 * u + 1);
+            const uint32_t w[4] = {kr[u].x, kr[u].y, kr[u].z, kr[u].w};
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&w[0]));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&w[1]));
+            const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&w[2]));
+            const float2 f3 = __half22float2(*reinterpret_cast<const __half2*>(&w[3]));
+            dot = fmaf(f0.x, qa.x, dot);
+            dot = fmaf(f0.y, qa.y, dot);
+            dot = fmaf(f1.x, qa.z, dot);
+            dot = fmaf(f1.y, qa.w, dot);
+            dot = fmaf(f2.x, qb.x, dot);
+            dot = fmaf(f2.y, qb.y, dot);
+            dot = fmaf(f3.x, qb.z, dot);
+            dot = fmaf(f3.y, qb.w, dot);
+        }
+        dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+        if (qd == 0) wgt[slot] = slot < live ? dot * p.scale : -INFINITY;
+        __syncthreads();
+        // ---- tile softmax weights (warp 0), then P.V per channel (thread = channel)
+        float mx = -INFINITY;
+        if (tid < 32) {
+            const float x = wgt[tid];
+            mx = warp_max(x);
+            const float e = tid < live ? expf(x - mx) : 0.0f;
+            wgt[tid] = e;
+            const float l = warp_sum(e);
+            if (tid == 0) {
+                red[0] = mx;
+                red[1] = l;
+            }
+        }
+        __syncthreads();
+        mx = red[0];
+        const float l = red[1];
+        const int d = tid;
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int s = 0; s < 32; ++s) acc = fmaf(wgt[s], half_value(vt[s][d]), acc);
+        // ---- V packed (transposed): row d of head h, slots s0 .. s0+live-1
+        uint16_t* vrow = p.vp + ((size_t)h * kDim + d) * p.count + s0;
+        if (live == 32 && vec_v) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    w[e] = (uint32_t)vt[8 * u + 2 * e][d] | ((uint32_t)vt[8 * u + 2 * e + 1][d] << 16);
+                reinterpret_cast<uint4*>(vrow)[u] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        } else {
+            for (int s = 0; s < live; ++s) vrow[s] = vt[s][d];
+        }
+        if (ntiles == 1) {  // one tile: no partials to fold
+            p.out[h * kDim + d] = l > 0.0f ? acc / l : 0.0f;
+            __syncthreads();  // vt / wgt are rewritten by the next item
+            continue;
+        }
+        float* part = p.part + ((size_t)h * p.tiles_cap + tile) * kPart;
+        if (tid == 0) {
+            part[0] = mx;
+            part[1] = l;
+        }
+        part[2 + d] = acc;
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) last = atomicAdd(&p.arrive[h], 1u) == ntiles - 1;
+        __syncthreads();
+        if (last) {
+            __threadfence();
+            const float* base = p.part + (size_t)h * p.tiles_cap * kPart;
+            float M = -INFINITY;
+            for (unsigned i = 0; i < ntiles; ++i) M = fmaxf(M, __ldcg(base + i * kPart));
+            float L = 0.0f, o = 0.0f;
+            for (unsigned i = 0; i < ntiles; ++i) {
+                const float w = expf(__ldcg(base + i * kPart) - M);
+                L = fmaf(__ldcg(base + i * kPart + 1), w, L);
+                o = fmaf(__ldcg(base + i * kPart + 2 + d), w, o);
+            }
+            p.out[h * kDim + d] = L > 0.0f ? o / L : 0.0f;
+        }
+        __syncthreads();
+    }
+}
+}  // namespace
+
+size_t gather_attention_workspace_bytes(size_t count) {
+    const size_t tiles = std::max<size_t>(1, (count + 31) / 32);
+    return align256(kHeads * sizeof(unsigned)) + align256(kHeads * tiles * kPart * sizeof(float));
+}
+
+cudaError_t launch_gather_attention(const float* q, const uint32_t* ids, size_t kstride, const uint32_t* size,
+                                    const uint16_t* kcache, const uint16_t* vcache, size_t stride_words,
+                                    size_t visible, size_t count, uint16_t* kp, uint16_t* vp, float* out,
+                                    void* workspace, int reset_arrive, hsb_device_status* status,
+                                    cudaStream_t stream) {
+    const DeviceInfo& dev = device_info();
+    GatherAttnParams p{};
+    p.q = q;
+    p.ids = ids;
+    p.kstride = kstride;
+    p.size = size;
+    p.kcache = kcache;
+    p.vcache = vcache;
+    p.stride_words = stride_words;
+    p.visible = visible;
+    p.count = count;
+    p.kp = kp;
+    p.vp = vp;
+    p.out = out;
+    p.arrive = static_cast<unsigned*>(workspace);
+    p.part = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + align256(kHeads * sizeof(unsigned)));
+    p.tiles_cap = (unsigned)std::max<size_t>(1, (count + 31) / 32);
+    p.status = status;
+    p.scale = 1.0f / sqrtf(128.0f);
+    if (reset_arrive) {
+        cudaError_t e = cudaMemsetAsync(p.arrive, 0, kHeads * sizeof(unsigned), stream);
+        if (e != cudaSuccess) return e;
+    }
+    const unsigned items = p.tiles_cap * kHeads;
+    const unsigned grid = std::min<unsigned>(items, (unsigned)dev.sms * 8);
+    gather_attention_kernel<<<grid, kGAThreads, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
 }  // namespace hsb

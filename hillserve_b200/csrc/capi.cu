@@ -473,10 +473,24 @@ int hsb_rehearsal_query(const uint16_t* d_x, const uint16_t* d_w, uint64_t posit
 // ------------------------------------------------------------- layer step
 // Layer-step workspace: selector | attention | order keys [32][valid].
 static size_t align256(size_t b) { return (b + 255) / 256 * 256; }
-size_t hsb_layer_workspace_bytes(size_t valid, size_t count) {
-    return align256(select_workspace_bytes(HSB_QUERY_HEADS, valid, count)) + align256(attention_workspace_bytes(count)) +
-           align256(HSB_QUERY_HEADS * valid * 2);
+// Layer workspace: selector | gather+attention | order keys [32][valid] |
+// head-0 partials [kH0Partials].
+namespace {
+struct LayerLayout {
+    size_t sel, att, keys, h0, total;
+};
+LayerLayout layer_layout(size_t valid, size_t count) {
+    LayerLayout l{};
+    l.sel = 0;
+    l.att = align256(select_workspace_bytes(HSB_QUERY_HEADS, valid, count));
+    l.keys = l.att + align256(gather_attention_workspace_bytes(count));
+    l.h0 = l.keys + align256(HSB_QUERY_HEADS * valid * 2);
+    l.total = l.h0 + kH0Partials * sizeof(uint32_t);
+    return l;
 }
+}  // namespace
+
+size_t hsb_layer_workspace_bytes(size_t valid, size_t count) { return layer_layout(valid, count).total; }
 
 int hsb_layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_kcache, const uint16_t* d_vcache,
                    size_t stride_words, size_t valid, float alpha, float ratio, size_t count,
@@ -486,19 +500,34 @@ int hsb_layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_
     if (rc) return rc;
     if (count < select_kmax(valid, ratio) || count == 0)
         return fail(HSB_E_SEL_CAPACITY, hsb_status_message(HSB_E_SEL_CAPACITY));
+    const LayerLayout lay = layer_layout(valid, count);
     if (!b->scores || !b->ids || !b->result || !b->k_packed || !b->v_packed || !b->workspace ||
-        b->workspace_bytes < hsb_layer_workspace_bytes(valid, count) || !aligned(b->workspace, 256))
+        b->workspace_bytes < lay.total || !aligned(b->workspace, 256))
         return fail(HSB_E_WORKSPACE, "layer step buffers missing or too small");
     cudaStream_t s = as_stream(stream);
     const hsb_key_view view{d_kcache, valid, stride_words};
     size_t total = 0;
     if ((rc = check_views(&view, 1, &total))) return rc;
-    cudaError_t e = cudaMemsetAsync(b->result, 0, sizeof(hsb_selection), s);
-    if (e != cudaSuccess) return fail_cuda(e, "result reset");
-    const size_t sel_bytes = align256(select_workspace_bytes(HSB_QUERY_HEADS, valid, count));
-    const size_t att_bytes = align256(attention_workspace_bytes(count));
-    uint16_t* keys = reinterpret_cast<uint16_t*>(static_cast<unsigned char*>(b->workspace) + sel_bytes + att_bytes);
-    if ((e = launch_score(d_q16, &view, 1, b->scores, valid, 0, &b->result->status, s, keys)) != cudaSuccess)
+    // 16-byte row and query loads / packed stores.
+    if (!d_vcache || !aligned(d_vcache, 16) || !aligned(d_q32, 16) || !aligned(b->k_packed, 16) ||
+        !aligned(b->v_packed, 16))
+        return fail(HSB_E_INVALID, "layer step: V cache, F32 query and packed buffers must be 16-byte aligned");
+    unsigned char* ws = static_cast<unsigned char*>(b->workspace);
+    uint16_t* keys = reinterpret_cast<uint16_t*>(ws + lay.keys);
+    uint32_t* h0 = reinterpret_cast<uint32_t*>(ws + lay.h0);
+    // The scorer clears what the later stages expect at zero (selector
+    // header, result, attention counters) and leaves head-0 partials, so the
+    // step has no memset nodes and the selector no pass over head 0's row.
+    ScoreExtras x{};
+    x.h0 = h0;
+    x.zero[0] = reinterpret_cast<uint32_t*>(ws + lay.sel);
+    x.zero_words[0] = (unsigned)(select_header_bytes() / 4);
+    x.zero[1] = reinterpret_cast<uint32_t*>(b->result);
+    x.zero_words[1] = (unsigned)(sizeof(hsb_selection) / 4);
+    x.zero[2] = reinterpret_cast<uint32_t*>(ws + lay.att);
+    x.zero_words[2] = HSB_QUERY_HEADS;
+    cudaError_t e;
+    if ((e = launch_score(d_q16, &view, 1, b->scores, valid, 0, &b->result->status, s, keys, &x)) != cudaSuccess)
         return fail_cuda(e, "score launch");
     SelectLaunch sl{};
     sl.scores = keys;
@@ -514,17 +543,17 @@ int hsb_layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_
     sl.kcap = count;
     sl.counts = b->counts;
     sl.result = b->result;
-    sl.workspace = b->workspace;
-    sl.workspace_bytes = sel_bytes;
+    sl.workspace = ws + lay.sel;
+    sl.workspace_bytes = lay.att - lay.sel;
     sl.reset_result = 0;
+    sl.reset_header = 0;
+    sl.h0 = h0;
     sl.zero_is_error = 1;
     if ((e = launch_select(sl, s)) != cudaSuccess) return fail_cuda(e, "select launch");
-    if ((e = launch_gather_cache(b->ids, count, &b->result->k, 0, d_kcache, d_vcache, stride_words, valid, count, 0,
-                                 b->k_packed, b->v_packed, &b->result->status, s)) != cudaSuccess)
-        return fail_cuda(e, "gather launch");
-    if ((e = launch_attention_packed(d_q32, b->k_packed, b->v_packed, count, nullptr, 0, &b->result->k, 0, d_out,
-                                     static_cast<unsigned char*>(b->workspace) + sel_bytes, s)) != cudaSuccess)
-        return fail_cuda(e, "attention launch");
+    if ((e = launch_gather_attention(d_q32, b->ids, count, &b->result->k, d_kcache, d_vcache, stride_words, valid,
+                                     count, b->k_packed, b->v_packed, d_out, ws + lay.att, 0, &b->result->status,
+                                     s)) != cudaSuccess)
+        return fail_cuda(e, "gather-attention launch");
     g_last_error.clear();
     return HSB_OK;
 }

@@ -38,6 +38,9 @@ __device__ __forceinline__ uint32_t order_key(uint32_t bits) {
     if ((bits & 0x7fffu) == 0) bits = 0;
     return (bits & 0x8000u) ? (~bits & 0xffffu) : (bits ^ 0x8000u);
 }
+// Order keys of NaNs lie above +inf's (0xfc00) or below -inf's (0x03ff).
+__device__ __forceinline__ bool key_nan(uint32_t key) { return key > 0xfc00u || key < 0x03ffu; }
+__device__ __forceinline__ bool key_nonfinite(uint32_t key) { return key >= 0xfc00u || key <= 0x03ffu; }
 // The runtime's normalisation (policy/full_gqa_runtime.cpp:571):
 // F16(F32(raw) / sqrtf(128)), an IEEE division.
 __device__ __forceinline__ uint16_t scale_half(uint16_t raw) {

@@ -22,9 +22,22 @@ const DeviceInfo& device_info();
 // Stage 1
 // keys (optional): also writes order_key(F16(raw / sqrtf(128))) per score, the
 // selector's input in the fused layer step.
+// Extra duties of the scorer inside the fused layer step:
+//  - h0: per-CTA head-0 partials, h0[b] = (non-finite seen << 16) | max order
+//    key of query head 0 over CTA b's tokens (0 when none); entries from the
+//    grid size to kH0Partials are written 0.  Needs keys.
+//  - zero[i] / zero_words[i]: small buffers (selector header, selection
+//    result, attention counters) cleared by CTA 0 before any use downstream.
+constexpr unsigned kH0Partials = 1024;
+struct ScoreExtras {
+    uint32_t* h0 = nullptr;
+    uint32_t* zero[3] = {nullptr, nullptr, nullptr};
+    unsigned zero_words[3] = {0, 0, 0};
+};
 cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nviews,
                          uint16_t* out, size_t out_stride, size_t col0,
-                         hsb_device_status* status, cudaStream_t stream, uint16_t* keys = nullptr);
+                         hsb_device_status* status, cudaStream_t stream, uint16_t* keys = nullptr,
+                         const ScoreExtras* extras = nullptr);
 cudaError_t launch_scale(const uint16_t* raw, size_t count, uint16_t* out, cudaStream_t stream);
 
 // Stage 2
@@ -52,8 +65,11 @@ struct SelectLaunch {
     unsigned long long cover_cap;  // cover: min(position, floor((position+1)*0.2f))
     int reset_result = 1;          // zero *result before the kernel
     int zero_is_error = 0;         // k == 0 -> HSB_E_ZERO_SELECTION (layer step)
+    int reset_header = 1;          // zero the workspace header before the kernel
+    const uint32_t* h0 = nullptr;  // the scorer's head-0 partials (ScoreExtras::h0)
 };
 size_t select_workspace_bytes(size_t heads, size_t valid, size_t kcap);
+size_t select_header_bytes();  // leading bytes of the workspace that start at zero
 cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream);
 
 // Stage 3
@@ -88,6 +104,15 @@ cudaError_t launch_attention_packed(const float* q, const uint16_t* k, const uin
                                     size_t count, const float* mask, size_t qpad,
                                     const uint32_t* sizes, size_t sizes_stride, float* out,
                                     void* workspace, cudaStream_t stream);
+// The layer step's fused gather + attention (live slots only, sizes = *size
+// for every head).  Workspace: [32] arrival counters (zero at launch: cleared
+// here when reset_arrive, else by the caller) + [32][ceil(count/32)] partials.
+size_t gather_attention_workspace_bytes(size_t count);
+cudaError_t launch_gather_attention(const float* q, const uint32_t* ids, size_t kstride, const uint32_t* size,
+                                    const uint16_t* kcache, const uint16_t* vcache, size_t stride_words,
+                                    size_t visible, size_t count, uint16_t* kp, uint16_t* vp, float* out,
+                                    void* workspace, int reset_arrive, hsb_device_status* status,
+                                    cudaStream_t stream);
 size_t attention_dense_workspace_bytes(size_t tokens);
 cudaError_t launch_attention_dense(const float* q, const uint16_t* kcache, const uint16_t* vcache,
                                    size_t tokens, size_t stride_words, float* out,

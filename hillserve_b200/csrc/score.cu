@@ -56,7 +56,27 @@ struct ScoreParams {
     unsigned long long out_stride;  // columns of the output matrix
     unsigned long long col0;        // first output column of this launch
     hsb_device_status* status;
+    ScoreExtras extras;
 };
+
+// CTA 0 clears the extras' buffers and the unused tail of the head-0 partials.
+__device__ __forceinline__ void clear_extras(const ScoreExtras& x) {
+    if (blockIdx.x != 0) return;
+    for (int i = 0; i < 3; ++i)
+        for (unsigned w = threadIdx.x; w < x.zero_words[i]; w += blockDim.x) x.zero[i][w] = 0u;
+    if (x.h0)
+        for (unsigned w = gridDim.x + threadIdx.x; w < kH0Partials; w += blockDim.x) x.h0[w] = 0u;
+}
+// Running head-0 partial of one lane: order key of a normalised score.
+__device__ __forceinline__ void track_head0(uint32_t key, uint32_t& mx, uint32_t& bad) {
+    bad |= key_nonfinite(key) ? 1u : 0u;
+    mx = key_nan(key) ? mx : max(mx, key);
+}
+__device__ __forceinline__ void write_head0(const ScoreExtras& x, uint32_t mx, uint32_t bad) {
+    mx = __reduce_max_sync(0xffffffffu, mx);
+    bad = __reduce_or_sync(0xffffffffu, bad);
+    if ((threadIdx.x & 31) == 0) x.h0[blockIdx.x] = (bad << 16) | mx;
+}
 
 __device__ __forceinline__ const uint16_t* token_row(const ScoreParams& p, unsigned long long t) {
     int v = 0;
@@ -73,6 +93,7 @@ __global__ void __launch_bounds__(kThreads, 1) score_v3_kernel(const __grid_cons
     uint64_t* empty = full + kStages;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    clear_extras(p.extras);
     for (int i = threadIdx.x; i < kHeads * kDim; i += blockDim.x) {
         const int h = i >> 7, c = i & 127;
         qs[((h >> 2) * kDim + c) * kGroup + (h & 3)] = half_value(p.q[i]);
@@ -118,7 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1) score_v3_kernel(const __grid_cons
     // ---------------- consumers: warp = KV head, lane = token of the tile
     const int kh = warp;
     const float4* qv = reinterpret_cast<const float4*>(qs) + kh * kDim;
-    uint32_t it = 0;
+    uint32_t it = 0, h0max = 0, h0bad = 0;
     for (unsigned long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
         const uint32_t s = it % kStages;
         if (!mbar_wait(&full[s], (it / kStages) & 1)) {
@@ -154,15 +175,18 @@ __global__ void __launch_bounds__(kThreads, 1) score_v3_kernel(const __grid_cons
             o[3 * p.out_stride] = s3;
             if (p.keys) {
                 uint16_t* kk = p.keys + at;
-                kk[0] = (uint16_t)order_key(scale_half(s0));
+                const uint32_t key0 = order_key(scale_half(s0));
+                kk[0] = (uint16_t)key0;
                 kk[p.out_stride] = (uint16_t)order_key(scale_half(s1));
                 kk[2 * p.out_stride] = (uint16_t)order_key(scale_half(s2));
                 kk[3 * p.out_stride] = (uint16_t)order_key(scale_half(s3));
+                if (kh == 0) track_head0(key0, h0max, h0bad);
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
+    if (kh == 0 && p.extras.h0) write_head0(p.extras, h0max, h0bad);
 }
 
 // ===================================================================== TMA
@@ -199,6 +223,7 @@ struct TmaParams {
     uint16_t* keys;
     unsigned long long out_stride;
     hsb_device_status* status;
+    ScoreExtras extras;
 };
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
@@ -233,6 +258,7 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
     uint64_t* empty = full + kTStages;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    clear_extras(p.extras);
     for (int i = threadIdx.x; i < kHeads * kDim; i += blockDim.x) {
         const int h = i >> 7, c = i & 127;
         reinterpret_cast<uint16_t*>(qs)[((h >> 2) * kDim + c) * kGroup + (h & 3)] = p.q[i];
@@ -275,7 +301,7 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
     // ---------------- consumers
     const int kh = warp, tl = lane;  // KV head, token in tile
     const uint4* qv = qs + kh * (kDim / 2);
-    uint32_t it = 0;
+    uint32_t it = 0, h0max = 0, h0bad = 0;
     for (unsigned long long tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
         const int v = tile_view(p, tile);
         const unsigned long long t0 = (tile - p.view_tile0[v]) * kTTile;
@@ -318,10 +344,15 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
                 const uint16_t sc = half_bits(acc[g]);
                 const unsigned long long at = (unsigned long long)(kh * kGroup + g) * p.out_stride + col;
                 p.out[at] = sc;
-                if (p.keys) p.keys[at] = (uint16_t)order_key(scale_half(sc));
+                if (p.keys) {
+                    const uint32_t key = order_key(scale_half(sc));
+                    p.keys[at] = (uint16_t)key;
+                    if (kh == 0 && g == 0) track_head0(key, h0max, h0bad);
+                }
             }
         }
     }
+    if (kh == 0 && p.extras.h0) write_head0(p.extras, h0max, h0bad);
 }
 
 // Resolves cuTensorMapEncodeTiled through the runtime (no libcuda link).
@@ -366,7 +397,9 @@ __global__ void scale_kernel(const uint16_t* __restrict__ raw, unsigned long lon
 
 cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nviews,
                          uint16_t* out, size_t out_stride, size_t col0, hsb_device_status* status,
-                         cudaStream_t stream, uint16_t* keys) {
+                         cudaStream_t stream, uint16_t* keys, const ScoreExtras* extras) {
+    const ScoreExtras none{};
+    const ScoreExtras& x = extras ? *extras : none;
     const DeviceInfo& dev = device_info();
     static thread_local int configured_device = -1;
     if (configured_device != dev.ordinal) {
@@ -399,6 +432,7 @@ cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nv
             t.keys = keys;
             t.out_stride = out_stride;
             t.status = status;
+            t.extras = x;
             const int grid = (int)std::min<unsigned long long>(tiles, (unsigned long long)dev.sms * 2);
             score_tma_kernel<<<grid, kTThreads, kTSmemBytes, stream>>>(t);
             return cudaGetLastError();
@@ -421,6 +455,7 @@ cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nv
     p.out_stride = out_stride;
     p.col0 = col0;
     p.status = status;
+    p.extras = x;
     const unsigned long long ntiles = (tokens + kTile - 1) / kTile;
     const int grid = (int)std::min<unsigned long long>(ntiles, (unsigned long long)dev.sms);
     score_v3_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);

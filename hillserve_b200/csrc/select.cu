@@ -70,7 +70,19 @@ struct SelectParams {
     SelectHeader* header;
     uint16_t* gkeys;              // [heads][valid] when valid > kSmemKeysMax
     unsigned long long* sortbuf;  // [heads][2][kcap] when k > kSmemSortMax
+    const uint32_t* h0;           // optional: the scorer's head-0 partials [kH0Partials]
 };
+
+// Head-0 maximum key and non-finite flag from the scorer's per-CTA partials
+// (the fused layer step), instead of a pass over head 0's row.
+template <int NT>
+__device__ __forceinline__ void head0_from_partials(const uint32_t* h0, unsigned int& mx, unsigned int& bad0) {
+    for (unsigned int i = threadIdx.x; i < kH0Partials; i += NT) {
+        const uint32_t v = __ldcg(h0 + i);
+        mx = max(mx, v & 0xffffu);
+        bad0 |= v >> 16;
+    }
+}
 
 struct SelectShared {
     unsigned int hist[kWarps][256];  // per-warp histograms / scatter offsets
@@ -90,8 +102,6 @@ struct SelectShared {
 __device__ __forceinline__ uint32_t key_bits(uint32_t key) {
     return (key & 0x8000u) ? (key ^ 0x8000u) : (~key & 0xffffu);
 }
-__device__ __forceinline__ bool key_nan(uint32_t key) { return key > 0xfc00u || key < 0x03ffu; }
-__device__ __forceinline__ bool key_nonfinite(uint32_t key) { return key >= 0xfc00u || key <= 0x03ffu; }
 
 __device__ __forceinline__ uint32_t to_key(uint32_t v, int mode) {
     if (mode == kInputKeys) return v;
@@ -207,8 +217,9 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(const __grid_consta
     if (tid < 64) sh.fine[tid] = 0;
     // ---- 1a. head-0 maximum key (NaN never becomes the maximum, as std::max)
     unsigned int mx = 0, bad0 = 0;
+    if (p.h0) head0_from_partials<kThreads>(p.h0, mx, bad0);
 #pragma unroll 4
-    for (unsigned long long g = tid; g < n8; g += kThreads) {
+    for (unsigned long long g = tid; g < (p.h0 ? 0 : n8); g += kThreads) {
         const uint4 w = reinterpret_cast<const uint4*>(row0)[g];
         const uint32_t v[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -218,7 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(const __grid_consta
             mx = key_nan(key) ? mx : max(mx, key);
         }
     }
-    for (unsigned long long i = n8 * 8 + tid; i < n; i += kThreads) {
+    for (unsigned long long i = n8 * 8 + tid; i < (p.h0 ? 0 : n); i += kThreads) {
         const uint32_t key = to_key(row0[i], p.mode);
         bad0 |= key_nonfinite(key);
         mx = key_nan(key) ? mx : max(mx, key);
@@ -591,8 +602,9 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     // ---- 1. head-0 maximum over the whole row (every CTA, from L2), own
     // chunk's keys to shared memory with the coarse histogram.
     unsigned int mx = 0, bad0 = 0, bad = 0;
+    if (p.h0) head0_from_partials<kCThreads>(p.h0, mx, bad0);
 #pragma unroll 4
-    for (unsigned long long g = tid; g < n8; g += kCThreads) {
+    for (unsigned long long g = tid; g < (p.h0 ? 0 : n8); g += kCThreads) {
         const uint4 w = reinterpret_cast<const uint4*>(row0)[g];
         const uint32_t v[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -602,7 +614,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
             mx = key_nan(key) ? mx : max(mx, key);
         }
     }
-    for (unsigned long long i = n8 * 8 + tid; i < n; i += kCThreads) {
+    for (unsigned long long i = n8 * 8 + tid; i < (p.h0 ? 0 : n); i += kCThreads) {
         const uint32_t key = to_key(row0[i], p.mode);
         bad0 |= key_nonfinite(key);
         mx = key_nan(key) ? mx : max(mx, key);
@@ -995,6 +1007,8 @@ int cluster_capacity(int device) {
 
 }  // namespace
 
+size_t select_header_bytes() { return sizeof(SelectHeader); }
+
 size_t select_workspace_bytes(size_t heads, size_t valid, size_t kcap) {
     size_t bytes = (sizeof(SelectHeader) + 255) / 256 * 256;
     if (valid > kSmemKeysMax) bytes += (heads * valid * 2 + 255) / 256 * 256;
@@ -1029,8 +1043,12 @@ cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream) {
         off += (s.heads * s.valid * 2 + 255) / 256 * 256;
     }
     p.sortbuf = reinterpret_cast<unsigned long long*>(ws + off);
-    cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(SelectHeader), stream);
-    if (e != cudaSuccess) return e;
+    p.h0 = s.h0;
+    cudaError_t e = cudaSuccess;
+    if (s.reset_header) {
+        e = cudaMemsetAsync(ws, 0, sizeof(SelectHeader), stream);
+        if (e != cudaSuccess) return e;
+    }
     if (s.reset_result) {
         e = cudaMemsetAsync(s.result, 0, sizeof(hsb_selection), stream);
         if (e != cudaSuccess) return e;

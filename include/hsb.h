@@ -262,11 +262,15 @@ int hsb_rehearsal_query(const uint16_t* d_x, const uint16_t* d_w, uint64_t posit
 
 /* ------------------------------------------------------------- layer step
  * One selected-KV decode layer, all on `stream` with no host round trip:
- * score (raw) -> select (raw input) -> gather from the HBM cache into the
- * packed live-slot layout -> attention.  count (slot capacity per head) must
- * be >= min(floor(valid*ratio), valid).  d_out receives F32 [32][128];
- * d_ids/d_counts/d_result as hsb_select.  k == 0 leaves d_out zero and sets
- * d_result->status to HSB_E_ZERO_SELECTION (the reference throws there). */
+ * score (raw, plus order keys) -> select -> gather from the HBM cache into
+ * the packed live-slot layout fused with the attention over those rows:
+ * three kernels and no memset or host round trip (capturable in a CUDA
+ * graph).  count (slot capacity per head) must be >= min(floor(valid*ratio),
+ * valid).  The V cache, d_q32 and the packed buffers must be 16-byte
+ * aligned.  d_out receives F32 [32][128]; d_ids/d_counts/d_result as
+ * hsb_select.  k == 0 leaves d_out zero and sets d_result->status to
+ * HSB_E_ZERO_SELECTION (the reference throws there).  Calls sharing one
+ * workspace must be ordered on one stream. */
 typedef struct hsb_layer_buffers {
     uint16_t* scores;  /* F16 [32][valid] */
     uint32_t* ids;     /* [32][count] */
