@@ -307,6 +307,210 @@ __global__ void __launch_bounds__(kDThreads) attention_dense_kernel(const __grid
     }
 }
 
+// ------------------------------------------------------------- dense (TMA)
+// Dense decode attention streamed like the scorer: a ring of 32 KB TMA boxes
+// ({64 channels, 32 tokens, 8 KV heads}, 128-byte swizzle) carries, per
+// 32-token tile, K channels 0-63, K 64-127, V 0-63, V 64-127.  Warp w is KV
+// head w.  For the logits lane l is token l (the scorer's dot products, FP32);
+// an online softmax per query head keeps (max, sum) per warp; for P.V lane l
+// owns channels 2l, 2l+1 of each half, the tile's weights arriving by
+// shuffle.  One CTA per SM walks tiles blockIdx.x, +gridDim.x, ... and writes
+// one (max, sum, out[128]) partial per query head; dense_combine_kernel folds
+// them.
+constexpr int kDTBox = 32 * kKvHeads * 64 * 2;  // bytes per box
+constexpr int kDTSlots = 6;
+constexpr int kDTConsumers = kKvHeads;
+constexpr int kDTThreads = (kDTConsumers + 1) * 32;
+constexpr int kDTQBytes = kKvHeads * kDim * kGroup * 4;  // F32 [kv][c][4 heads]
+constexpr int kDTSmem = 1024 + kDTSlots * kDTBox + kDTQBytes + 2 * kDTSlots * 8;
+constexpr int kDenseMaxCtas = 256;
+
+struct DenseTmaParams {
+    CUtensorMap kmap, vmap;
+    const float* q;
+    unsigned tokens, tiles;
+    float* part;  // [32][gridDim.x][kPart]
+    hsb_device_status* status;
+    float scale;
+};
+
+__global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(const __grid_constant__ DenseTmaParams p) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    unsigned char* slots = smem;
+    float4* qs = reinterpret_cast<float4*>(smem + kDTSlots * kDTBox);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDTSlots * kDTBox + kDTQBytes);
+    uint64_t* empty = full + kDTSlots;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < kHeads * kDim; i += blockDim.x) {
+        const int h = i >> 7, c = i & 127;
+        reinterpret_cast<float*>(qs)[((h >> 2) * kDim + c) * kGroup + (h & 3)] = p.q[i];
+    }
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kDTSlots; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kDTConsumers);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    if (warp == kDTConsumers) {
+        if (lane != 0) return;
+        // ---------------- producer: four boxes per tile
+        uint32_t it = 0;
+        bool ok = true;
+        for (unsigned tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
+            for (int box = 0; box < 4; ++box, ++it) {
+                const uint32_t s = it % kDTSlots;
+                if (it >= kDTSlots && !mbar_wait(&empty[s], ((it / kDTSlots) - 1) & 1)) {
+                    raise_status(p.status, HSB_E_TIMEOUT, blockIdx.x);
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[s], kDTBox);
+                tma_load_3d(slots + s * kDTBox, box < 2 ? &p.kmap : &p.vmap, (box & 1) * 64, (int)(tile * 32), 0,
+                            &full[s]);
+            }
+        }
+        if (!ok) {  // let copies in flight land before shared memory is released
+            const uint32_t first = it > kDTSlots ? it - kDTSlots : 0;
+            for (uint32_t j = first; j < it; ++j) (void)mbar_wait(&full[j % kDTSlots], (j / kDTSlots) & 1);
+        }
+        return;
+    }
+
+    // ---------------- consumers
+    const int kh = warp;
+    const float4* qv = qs + kh * kDim;
+    float M[kGroup], L[kGroup], o[kGroup][4];
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g) {
+        M[g] = -INFINITY;
+        L[g] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[g][j] = 0.0f;
+    }
+    uint32_t it = 0;
+    for (unsigned tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
+        float a[kGroup] = {0.f, 0.f, 0.f, 0.f};
+        for (int half = 0; half < 2; ++half, ++it) {
+            const uint32_t s = it % kDTSlots;
+            if (!mbar_wait(&full[s], (it / kDTSlots) & 1)) {
+                raise_status(p.status, HSB_E_TIMEOUT, blockIdx.x);
+                return;
+            }
+            const unsigned char* row = slots + s * kDTBox + (kh * 32 + lane) * 128;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint4 w = *reinterpret_cast<const uint4*>(row + ((j ^ (lane & 7)) << 4));
+                const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&words[e]));
+                    const float4 qa = qv[half * 64 + j * 8 + 2 * e], qb = qv[half * 64 + j * 8 + 2 * e + 1];
+                    a[0] = fmaf(qa.x, f.x, a[0]);
+                    a[1] = fmaf(qa.y, f.x, a[1]);
+                    a[2] = fmaf(qa.z, f.x, a[2]);
+                    a[3] = fmaf(qa.w, f.x, a[3]);
+                    a[0] = fmaf(qb.x, f.y, a[0]);
+                    a[1] = fmaf(qb.y, f.y, a[1]);
+                    a[2] = fmaf(qb.z, f.y, a[2]);
+                    a[3] = fmaf(qb.w, f.y, a[3]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        // online softmax over this tile (tokens past the end weigh 0)
+        const bool valid = tile * 32 + lane < p.tokens;
+        float pr[kGroup];
+#pragma unroll
+        for (int g = 0; g < kGroup; ++g) {
+            const float sg = valid ? a[g] * p.scale : -INFINITY;
+            const float mn = fmaxf(M[g], warp_max(sg));  // finite: the tile has a valid token
+            const float f = expf(M[g] - mn);              // 0 on the first tile
+            pr[g] = valid ? expf(sg - mn) : 0.0f;
+            L[g] = fmaf(L[g], f, warp_sum(pr[g]));
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[g][j] *= f;
+            M[g] = mn;
+        }
+        for (int half = 0; half < 2; ++half, ++it) {
+            const uint32_t s = it % kDTSlots;
+            if (!mbar_wait(&full[s], (it / kDTSlots) & 1)) {
+                raise_status(p.status, HSB_E_TIMEOUT, blockIdx.x);
+                return;
+            }
+            const unsigned char* base = slots + s * kDTBox + kh * 32 * 128 + (lane & 3) * 4;
+#pragma unroll 8
+            for (int t = 0; t < 32; ++t) {
+                const uint32_t w = *reinterpret_cast<const uint32_t*>(base + t * 128 + (((lane >> 2) ^ (t & 7)) << 4));
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+#pragma unroll
+                for (int g = 0; g < kGroup; ++g) {
+                    const float pg = __shfl_sync(0xffffffffu, pr[g], t);
+                    o[g][2 * half] = fmaf(pg, f.x, o[g][2 * half]);
+                    o[g][2 * half + 1] = fmaf(pg, f.y, o[g][2 * half + 1]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g) {
+        float* part = p.part + ((size_t)(kh * kGroup + g) * gridDim.x + blockIdx.x) * kPart;
+        if (lane == 0) {
+            part[0] = M[g];
+            part[1] = L[g];
+        }
+        part[2 + 2 * lane] = o[g][0];
+        part[3 + 2 * lane] = o[g][1];
+        part[2 + 64 + 2 * lane] = o[g][2];
+        part[3 + 64 + 2 * lane] = o[g][3];
+    }
+}
+
+// out[h][d] = sum_c exp(M_c - M) o_c[d] / sum_c exp(M_c - M) L_c over the
+// dense kernel's per-CTA partials.  One CTA per query head: the partials'
+// weights go to shared memory once, then 8 groups of 128 threads (thread =
+// channel) each sum every 8th partial with independent loads.
+constexpr int kCombineGroups = 8;
+__global__ void __launch_bounds__(kDim * kCombineGroups) dense_combine_kernel(const float* __restrict__ part,
+                                                                             int nparts, float* __restrict__ out) {
+    __shared__ float w[kDenseMaxCtas];
+    __shared__ float acc_s[kCombineGroups][kDim];
+    __shared__ float red[2];
+    const int h = blockIdx.x, tid = threadIdx.x, d = tid & (kDim - 1), grp = tid / kDim;
+    const float* base = part + (size_t)h * nparts * kPart;
+    if (tid < 32) {
+        float m = -INFINITY;
+        for (int c = tid; c < nparts; c += 32) m = fmaxf(m, __ldg(base + (size_t)c * kPart));
+        m = warp_max(m);
+        float l = 0.0f;
+        for (int c = tid; c < nparts; c += 32) {
+            const float wc = expf(__ldg(base + (size_t)c * kPart) - m);
+            w[c] = wc;
+            l = fmaf(__ldg(base + (size_t)c * kPart + 1), wc, l);
+        }
+        l = warp_sum(l);
+        if (tid == 0) red[0] = l;
+    }
+    __syncthreads();
+    float acc = 0.0f;
+#pragma unroll 4
+    for (int c = grp; c < nparts; c += kCombineGroups) acc = fmaf(__ldg(base + (size_t)c * kPart + 2 + d), w[c], acc);
+    acc_s[grp][d] = acc;
+    __syncthreads();
+    if (tid < kDim) {
+        float o = 0.0f;
+#pragma unroll
+        for (int g = 0; g < kCombineGroups; ++g) o += acc_s[g][d];
+        out[h * kDim + d] = red[0] > 0.0f ? o / red[0] : 0.0f;
+    }
+}
+
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
 
 }  // namespace
@@ -341,11 +545,40 @@ cudaError_t launch_attention_packed(const float* q, const uint16_t* k, const uin
 
 size_t attention_dense_workspace_bytes(size_t tokens) {
     const size_t nsplit = std::max<size_t>(1, (tokens + kDTokens - 1) / kDTokens);
-    return align256(kKvHeads * sizeof(unsigned)) + align256(kHeads * nsplit * kPart * sizeof(float));
+    const size_t legacy = align256(kKvHeads * sizeof(unsigned)) + align256(kHeads * nsplit * kPart * sizeof(float));
+    const size_t ctas = std::min<size_t>(kDenseMaxCtas, std::max<size_t>(1, (tokens + 31) / 32));
+    return std::max(legacy, align256(kHeads * ctas * kPart * sizeof(float)));
 }
 
 cudaError_t launch_attention_dense(const float* q, const uint16_t* kcache, const uint16_t* vcache, size_t tokens,
                                    size_t stride_words, float* out, void* workspace, cudaStream_t stream) {
+    // TMA path: one CTA per SM streaming K/V tiles, then a combine kernel.
+    {
+        DenseTmaParams t{};
+        if (tokens <= 0x7fffffffull && encode_kv_map(&t.kmap, kcache, tokens, stride_words) &&
+            encode_kv_map(&t.vmap, vcache, tokens, stride_words)) {
+            const DeviceInfo& dev = device_info();
+            static thread_local int configured_device = -1;
+            if (configured_device != dev.ordinal) {
+                cudaError_t e = cudaFuncSetAttribute(attention_dense_tma_kernel,
+                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kDTSmem);
+                if (e != cudaSuccess) return e;
+                configured_device = dev.ordinal;
+            }
+            t.q = q;
+            t.tokens = (unsigned)tokens;
+            t.tiles = (unsigned)((tokens + 31) / 32);
+            t.part = static_cast<float*>(workspace);
+            t.status = nullptr;
+            t.scale = 1.0f / sqrtf(128.0f);
+            const unsigned grid = std::min<unsigned>({t.tiles, (unsigned)dev.sms, (unsigned)kDenseMaxCtas});
+            attention_dense_tma_kernel<<<grid, kDTThreads, kDTSmem, stream>>>(t);
+            cudaError_t e = cudaGetLastError();
+            if (e != cudaSuccess) return e;
+            dense_combine_kernel<<<kHeads, kDim * kCombineGroups, 0, stream>>>(t.part, (int)grid, out);
+            return cudaGetLastError();
+        }
+    }
     DenseParams p{};
     p.q = q;
     p.kc = kcache;

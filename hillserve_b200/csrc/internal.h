@@ -1,6 +1,7 @@
 // internal.h -- host-side declarations shared by the kernel files and the
 // C-ABI layer (capi.cu).  Not installed; the public interface is hsb.h.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstddef>
@@ -39,6 +40,10 @@ cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nv
                          hsb_device_status* status, cudaStream_t stream, uint16_t* keys = nullptr,
                          const ScoreExtras* extras = nullptr);
 cudaError_t launch_scale(const uint16_t* raw, size_t count, uint16_t* out, cudaStream_t stream);
+// Tensor map of a token-major [tokens][8][128] F16 cache seen as {channel,
+// token, KV head} with 64 x 32 x 8 boxes and the 128-byte swizzle (the
+// scorer's tiles).  False if it cannot be encoded.
+bool encode_kv_map(CUtensorMap* map, const uint16_t* data, size_t tokens, size_t stride_words);
 
 // Stage 2
 // Sets the thread-local message read by hsb_last_error() and returns status

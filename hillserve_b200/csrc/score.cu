@@ -60,13 +60,15 @@ struct ScoreParams {
 };
 
 // CTA 0 clears the extras' buffers and the unused tail of the head-0 partials.
-__device__ __forceinline__ void clear_extras(const ScoreExtras& x) {
+// Threads [0, nthreads) of the CTA take part.
+__device__ __forceinline__ void clear_extras(const ScoreExtras& x, unsigned nthreads) {
     if (blockIdx.x != 0) return;
     for (int i = 0; i < 3; ++i)
-        for (unsigned w = threadIdx.x; w < x.zero_words[i]; w += blockDim.x) x.zero[i][w] = 0u;
+        for (unsigned w = threadIdx.x; w < x.zero_words[i]; w += nthreads) x.zero[i][w] = 0u;
     if (x.h0)
-        for (unsigned w = gridDim.x + threadIdx.x; w < kH0Partials; w += blockDim.x) x.h0[w] = 0u;
+        for (unsigned w = gridDim.x + threadIdx.x; w < kH0Partials; w += nthreads) x.h0[w] = 0u;
 }
+
 // Running head-0 partial of one lane: order key of a normalised score.
 __device__ __forceinline__ void track_head0(uint32_t key, uint32_t& mx, uint32_t& bad) {
     bad |= key_nonfinite(key) ? 1u : 0u;
@@ -93,7 +95,7 @@ __global__ void __launch_bounds__(kThreads, 1) score_v3_kernel(const __grid_cons
     uint64_t* empty = full + kStages;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    clear_extras(p.extras);
+    clear_extras(p.extras, blockDim.x);
     for (int i = threadIdx.x; i < kHeads * kDim; i += blockDim.x) {
         const int h = i >> 7, c = i & 127;
         qs[((h >> 2) * kDim + c) * kGroup + (h & 3)] = half_value(p.q[i]);
@@ -226,12 +228,6 @@ struct TmaParams {
     ScoreExtras extras;
 };
 
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
-        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
-        : "memory");
-}
 __device__ __forceinline__ float fma_f16(uint32_t a16, uint32_t b16, float c) {
     float d;
     asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"((unsigned short)a16), "h"((unsigned short)b16), "f"(c));
@@ -258,7 +254,7 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
     uint64_t* empty = full + kTStages;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    clear_extras(p.extras);
+    clear_extras(p.extras, blockDim.x);
     for (int i = threadIdx.x; i < kHeads * kDim; i += blockDim.x) {
         const int h = i >> 7, c = i & 127;
         reinterpret_cast<uint16_t*>(qs)[((h >> 2) * kDim + c) * kGroup + (h & 3)] = p.q[i];
@@ -270,6 +266,8 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
         }
         mbar_fence_init();
     }
+    // Q is staged before any K tile is requested: issued after the stream
+    // starts, its loads queue behind the whole grid's first tiles.
     __syncthreads();
 
     if (warp == kTConsumerWarps) {
@@ -382,7 +380,7 @@ bool encode_view(CUtensorMap* map, const hsb_key_view& v) {
     const cuuint32_t box[3] = {(cuuint32_t)kTHalf, (cuuint32_t)kTTile, (cuuint32_t)kKvHeads};
     const cuuint32_t estr[3] = {1, 1, 1};
     return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<uint16_t*>(v.data), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -394,6 +392,11 @@ __global__ void scale_kernel(const uint16_t* __restrict__ raw, unsigned long lon
 }
 
 }  // namespace
+
+bool encode_kv_map(CUtensorMap* map, const uint16_t* data, size_t tokens, size_t stride_words) {
+    const hsb_key_view v{data, tokens, stride_words};
+    return encode_view(map, v);
+}
 
 cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nviews,
                          uint16_t* out, size_t out_stride, size_t col0, hsb_device_status* status,
