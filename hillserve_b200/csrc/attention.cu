@@ -335,6 +335,8 @@ struct DenseTmaParams {
 };
 
 __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(const __grid_constant__ DenseTmaParams p) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     unsigned char* slots = smem;
@@ -479,6 +481,8 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
 constexpr int kCombineGroups = 8;
 __global__ void __launch_bounds__(kDim * kCombineGroups) dense_combine_kernel(const float* __restrict__ part,
                                                                              int nparts, float* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float w[kDenseMaxCtas];
     __shared__ float acc_s[kCombineGroups][kDim];
     __shared__ float red[2];
@@ -572,11 +576,11 @@ cudaError_t launch_attention_dense(const float* q, const uint16_t* kcache, const
             t.status = nullptr;
             t.scale = 1.0f / sqrtf(128.0f);
             const unsigned grid = std::min<unsigned>({t.tiles, (unsigned)dev.sms, (unsigned)kDenseMaxCtas});
-            attention_dense_tma_kernel<<<grid, kDTThreads, kDTSmem, stream>>>(t);
-            cudaError_t e = cudaGetLastError();
+            cudaError_t e = launch_dependent(attention_dense_tma_kernel, dim3(grid), dim3(kDTThreads), kDTSmem,
+                                             stream, false, t);
             if (e != cudaSuccess) return e;
-            dense_combine_kernel<<<kHeads, kDim * kCombineGroups, 0, stream>>>(t.part, (int)grid, out);
-            return cudaGetLastError();
+            return launch_dependent(dense_combine_kernel, dim3(kHeads), dim3(kDim * kCombineGroups), 0, stream,
+                                    false, static_cast<const float*>(t.part), (int)grid, out);
         }
     }
     DenseParams p{};
@@ -628,6 +632,8 @@ struct GatherAttnParams {
 };
 
 __global__ void __launch_bounds__(kGAThreads) gather_attention_kernel(const __grid_constant__ GatherAttnParams p) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ __align__(16) uint16_t vt[32][kGAPitch];
     __shared__ float wgt[32];
     __shared__ float red[4];
@@ -805,8 +811,7 @@ cudaError_t launch_gather_attention(const float* q, const uint32_t* ids, size_t 
     }
     const unsigned items = p.tiles_cap * kHeads;
     const unsigned grid = std::min<unsigned>(items, (unsigned)dev.sms * 8);
-    gather_attention_kernel<<<grid, kGAThreads, 0, stream>>>(p);
-    return cudaGetLastError();
+    return launch_dependent(gather_attention_kernel, dim3(grid), dim3(kGAThreads), 0, stream, false, p);
 }
 
 }  // namespace hsb

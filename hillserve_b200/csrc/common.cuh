@@ -147,6 +147,15 @@ __device__ __forceinline__ uint32_t warp_sum_u32(uint32_t v) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
 }
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start while its predecessor in the stream drains;
+// pdl_wait() blocks until the predecessor grid has completed and its memory
+// is visible, so it comes before the kernel's first global access.
+// pdl_trigger() lets this kernel's own dependents start launching.  Both are
+// no-ops for an ordinary launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // 3-D tiled TMA load (no multicast) into this CTA's shared memory,
 // completing on the mbarrier `bar`.  x (innermost) must be a multiple of 8
 // 16-bit elements.

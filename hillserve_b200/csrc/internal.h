@@ -20,6 +20,26 @@ struct DeviceInfo {
 // Properties of the current device, cached per device.
 const DeviceInfo& device_info();
 
+// Launch with programmatic stream serialization (the kernel calls pdl_wait()
+// before touching global memory), optionally cooperative.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                             bool cooperative, Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeCooperative;
+    attr[1].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = cooperative ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 // Stage 1
 // keys (optional): also writes order_key(F16(raw / sqrtf(128))) per score, the
 // selector's input in the fused layer step.

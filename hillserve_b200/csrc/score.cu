@@ -88,6 +88,8 @@ __device__ __forceinline__ const uint16_t* token_row(const ScoreParams& p, unsig
 }
 
 __global__ void __launch_bounds__(kThreads, 1) score_v3_kernel(const __grid_constant__ ScoreParams p) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ __align__(128) unsigned char smem[];
     float* qs = reinterpret_cast<float*>(smem);
     unsigned char* tiles = smem + kQBytes;
@@ -242,6 +244,8 @@ __device__ __forceinline__ int tile_view(const TmaParams& p, unsigned long long 
 }
 
 __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_constant__ TmaParams p) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ unsigned char smem_raw[];
     // The 128-byte swizzle pattern repeats every 1024 bytes of shared address:
     // align by offsetting the shared array itself (keeps the pointers in the
@@ -437,8 +441,7 @@ cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nv
             t.status = status;
             t.extras = x;
             const int grid = (int)std::min<unsigned long long>(tiles, (unsigned long long)dev.sms * 2);
-            score_tma_kernel<<<grid, kTThreads, kTSmemBytes, stream>>>(t);
-            return cudaGetLastError();
+            return launch_dependent(score_tma_kernel, dim3(grid), dim3(kTThreads), kTSmemBytes, stream, false, t);
         }
     }
     ScoreParams p{};
@@ -461,8 +464,7 @@ cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nv
     p.extras = x;
     const unsigned long long ntiles = (tokens + kTile - 1) / kTile;
     const int grid = (int)std::min<unsigned long long>(ntiles, (unsigned long long)dev.sms);
-    score_v3_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
-    return cudaGetLastError();
+    return launch_dependent(score_v3_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, false, p);
 }
 
 cudaError_t launch_scale(const uint16_t* raw, size_t count, uint16_t* out, cudaStream_t stream) {

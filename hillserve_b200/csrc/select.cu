@@ -193,6 +193,8 @@ __device__ void sort_pass(unsigned int (*hist)[256], unsigned int* scan, unsigne
 }
 
 __global__ void __launch_bounds__(kThreads, 1) select_kernel(const __grid_constant__ SelectParams p) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ __align__(16) unsigned char dyn[];
     __shared__ SelectShared sh;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -567,6 +569,8 @@ __device__ __forceinline__ void cluster_wait_acquire() {
 
 __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     select_cluster_kernel(const __grid_constant__ SelectParams p) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ __align__(16) unsigned char dyn[];
     __shared__ ClusterShared sh;
     cg::cluster_group cl = cg::this_cluster();
@@ -1053,13 +1057,15 @@ cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream) {
         e = cudaMemsetAsync(s.result, 0, sizeof(hsb_selection), stream);
         if (e != cudaSuccess) return e;
     }
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg{};
     cfg.stream = stream;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     if (s.valid <= kClusterKeysMax && s.heads <= (uint32_t)cluster_capacity(dev.ordinal)) {
         const size_t cs = ((size_t)s.valid + kCluster - 1) / kCluster;
         cfg.gridDim = dim3(s.heads * kCluster);
