@@ -549,8 +549,22 @@ int hsb_layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_
     sl.reset_header = 0;
     sl.h0 = h0;
     sl.zero_is_error = 1;
+    // The cluster selector gathers and attends in its epilogue; otherwise a
+    // separate gather + attention kernel follows.
+    sl.ga.q = d_q32;
+    sl.ga.kcache = d_kcache;
+    sl.ga.vcache = d_vcache;
+    sl.ga.stride_words = stride_words;
+    sl.ga.kp = b->k_packed;
+    sl.ga.vp = b->v_packed;
+    sl.ga.count = count;
+    sl.ga.out = d_out;
+    sl.ga.scale = 1.0f / sqrtf(128.0f);
+    int fused = 0;
+    sl.ga_done = &fused;
     if ((e = launch_select(sl, s)) != cudaSuccess) return fail_cuda(e, "select launch");
-    if ((e = launch_gather_attention(d_q32, b->ids, count, &b->result->k, d_kcache, d_vcache, stride_words, valid,
+    if (!fused &&
+        (e = launch_gather_attention(d_q32, b->ids, count, &b->result->k, d_kcache, d_vcache, stride_words, valid,
                                      count, b->k_packed, b->v_packed, d_out, ws + lay.att, 0, &b->result->status,
                                      s)) != cudaSuccess)
         return fail_cuda(e, "gather-attention launch");

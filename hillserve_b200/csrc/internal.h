@@ -71,6 +71,20 @@ bool encode_kv_map(CUtensorMap* map, const uint16_t* data, size_t tokens, size_t
 int record_error(int status, const char* message);
 int record_cuda_error(cudaError_t e, const char* what);
 
+// Optional epilogue of the cluster selector (the layer step): gather each
+// head's selected K/V rows from the cache into the packed layout and attend
+// over them, writing out[32][128].
+struct SelectEpilogue {
+    const float* q = nullptr;  // F32 [32][128]
+    const uint16_t* kcache = nullptr;
+    const uint16_t* vcache = nullptr;
+    size_t stride_words = 0;
+    uint16_t* kp = nullptr;  // [count][32][128]
+    uint16_t* vp = nullptr;  // [32][128][count]
+    size_t count = 0;
+    float* out = nullptr;    // null: no epilogue
+    float scale = 0.0f;
+};
 struct SelectLaunch {
     const uint16_t* scores;
     int raw;           // normalise in the kernel
@@ -92,6 +106,8 @@ struct SelectLaunch {
     int zero_is_error = 0;         // k == 0 -> HSB_E_ZERO_SELECTION (layer step)
     int reset_header = 1;          // zero the workspace header before the kernel
     const uint32_t* h0 = nullptr;  // the scorer's head-0 partials (ScoreExtras::h0)
+    SelectEpilogue ga;             // run by the cluster kernel only
+    int* ga_done = nullptr;        // out: 1 when the epilogue was launched
 };
 size_t select_workspace_bytes(size_t heads, size_t valid, size_t kcap);
 size_t select_header_bytes();  // leading bytes of the workspace that start at zero

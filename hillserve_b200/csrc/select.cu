@@ -31,6 +31,7 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
+#include <cstddef>
 #include <cmath>
 #include <mutex>
 
@@ -71,6 +72,7 @@ struct SelectParams {
     uint16_t* gkeys;              // [heads][valid] when valid > kSmemKeysMax
     unsigned long long* sortbuf;  // [heads][2][kcap] when k > kSmemSortMax
     const uint32_t* h0;           // optional: the scorer's head-0 partials [kH0Partials]
+    SelectEpilogue ga;            // cluster path: gather + attention of the selection (ga.out != null)
 };
 
 // Head-0 maximum key and non-finite flag from the scorer's per-CTA partials
@@ -560,6 +562,118 @@ __device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+// ---- gather + attention epilogue of the cluster kernel (layer step).
+// Each CTA runs four 128-thread groups; group g of CTA r takes the head's
+// 32-slot tiles 4g + r, +16, ...  Per tile a thread owns slot t/4 and the
+// channel quarter t%4 of its K/V rows: K goes to the packed layout from
+// registers, V is staged for the transposed packed write and P.V, and the
+// group folds the tile into an online softmax (thread = output channel).
+constexpr int kEpiGroups = 4;
+constexpr int kEpiThreads = 128;
+constexpr int kEpiPitch = kDim + 8;  // halves per staged V row (16-byte aligned)
+// Every member that is accessed with 16-byte vectors starts on a 16-byte
+// boundary: rows of vt (272 B), each group (sizeof a multiple of 16), q.
+struct __align__(16) EpiGroupSmem {
+    uint16_t vt[32][kEpiPitch];
+    float wgt[32];
+    float stat[4];
+};
+static_assert(sizeof(EpiGroupSmem) % 16 == 0 && (kEpiPitch * 2) % 16 == 0, "16-byte aligned V staging");
+struct __align__(16) EpiSmem {
+    EpiGroupSmem g[kEpiGroups];
+    __align__(16) float q[4][36];  // the head's query, channel quarters padded apart (distinct banks)
+    float part[kCluster * kEpiGroups][kDim + 2];  // leader: every group's (max, sum, out[128])
+};
+static_assert(offsetof(EpiSmem, q) % 16 == 0, "16-byte aligned query");
+constexpr size_t kEpiSmemBytes = (sizeof(EpiSmem) + 15) / 16 * 16;
+
+__device__ __forceinline__ void group_sync(int id) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(kEpiThreads) : "memory");
+}
+
+// One 32-slot tile of head h into the group's running (M, L, acc).
+__device__ __forceinline__ void epilogue_tile(const SelectEpilogue& e, const uint32_t* ids, int h, unsigned s0,
+                                              int live, const float* qs, EpiGroupSmem& gs, int gtid, int bar,
+                                              float& M, float& L, float& acc) {
+    const int slot = gtid >> 2, qd = gtid & 3, kh = h >> 2;
+    uint4 kr[4], vr[4];
+    if (slot < live) {
+        const uint32_t id = __ldcg(ids + s0 + slot);  // written by the leader CTA
+        const uint4* ks = reinterpret_cast<const uint4*>(e.kcache + (size_t)id * e.stride_words + kh * kDim) + qd * 4;
+        const uint4* vs = reinterpret_cast<const uint4*>(e.vcache + (size_t)id * e.stride_words + kh * kDim) + qd * 4;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            kr[u] = __ldg(ks + u);
+            vr[u] = __ldg(vs + u);
+        }
+        uint4* kd = reinterpret_cast<uint4*>(e.kp + ((size_t)(s0 + slot) * kHeads + h) * kDim) + qd * 4;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) kd[u] = kr[u];
+    } else {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) kr[u] = vr[u] = make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) *reinterpret_cast<uint4*>(&gs.vt[slot][qd * 32 + u * 8]) = vr[u];
+    float dot = 0.0f;
+    const float4* q4 = reinterpret_cast<const float4*>(qs + qd * 36);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const uint32_t w[4] = {kr[u].x, kr[u].y, kr[u].z, kr[u].w};
+        const float4 qa = q4[2 * u], qb = q4[2 * u + 1];
+        const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+            dot = fmaf(f.x, qv[2 * j], dot);
+            dot = fmaf(f.y, qv[2 * j + 1], dot);
+        }
+    }
+    dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+    dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+    if (qd == 0) gs.wgt[slot] = slot < live ? dot * e.scale : -INFINITY;
+    group_sync(bar);
+    if (gtid < 32) {
+        const float x = gs.wgt[gtid];
+        const float mt = warp_max(x);
+        const float ex = gtid < live ? expf(x - mt) : 0.0f;
+        gs.wgt[gtid] = ex;
+        const float lt = warp_sum(ex);
+        if (gtid == 0) {
+            gs.stat[0] = mt;
+            gs.stat[1] = lt;
+        }
+    }
+    group_sync(bar);
+    const int d = gtid;
+    float acc_t = 0.0f;
+#pragma unroll 8
+    for (int t = 0; t < 32; ++t) acc_t = fmaf(gs.wgt[t], half_value(gs.vt[t][d]), acc_t);
+    uint16_t* vrow = e.vp + ((size_t)h * kDim + d) * e.count + s0;
+    if (live == 32 && (e.count & 7) == 0) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                w[j] = (uint32_t)gs.vt[8 * u + 2 * j][d] | ((uint32_t)gs.vt[8 * u + 2 * j + 1][d] << 16);
+            reinterpret_cast<uint4*>(vrow)[u] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    } else {
+        for (int t = 0; t < live; ++t) vrow[t] = gs.vt[t][d];
+    }
+    const float mt = gs.stat[0], lt = gs.stat[1];
+    const float mn = fmaxf(M, mt);
+    const float a = expf(M - mn), b = expf(mt - mn);  // M = -inf on the first tile: a = 0
+    acc = fmaf(acc, a, acc_t * b);
+    L = fmaf(L, a, lt * b);
+    M = mn;
+    group_sync(bar);  // vt / wgt / stat are rewritten by the next tile
+}
+
+__device__ __forceinline__ void red_add_release(unsigned int* p, unsigned int v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ void cluster_arrive_release() {
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
@@ -682,19 +796,17 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     if (tid == 0) {
         if (sh.cnt) atomicAdd(&p.header->cnt[h], sh.cnt);
         if (!p.cover && sh.bad) atomicOr(&p.header->err[h], 1u);
-        // ---- 2. grid barrier (bounded)
-        __threadfence();
-        atomicAdd(&p.header->arrived, 1u);
+        // ---- 2. grid barrier (bounded): a release-ordered arrival (orders
+        // this CTA's count atomics before it) and acquire-load polling.
+        red_add_release(&p.header->arrived, 1u);
         const unsigned long long start = global_ns();
         sh.timeout = 0;
-        while (ld_acquire(&p.header->arrived) < gridDim.x) {  // plain loads: no RMW traffic on the line
+        while (ld_acquire(&p.header->arrived) < gridDim.x) {
             if (global_ns() - start > kWaitLimitNs) {
                 sh.timeout = 1;
                 break;
             }
-            __nanosleep(20);
         }
-        __threadfence();
     }
     __syncthreads();
     cluster_wait_acquire();
@@ -771,15 +883,19 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
         }
     }
     __syncthreads();
+    const bool fused = p.ga.out != nullptr;
     if (sh.timeout) {
         // Cluster peers that passed the barrier may still read this CTA's
-        // shared memory: stay resident through their two cluster barriers.
-        cl.sync();
-        cl.sync();
+        // shared memory: stay resident through their cluster barriers.
+        for (int i = 0; i < (fused ? 4 : 2); ++i) cl.sync();
         return;
     }
     const unsigned long long k = sh.k;
-    if (k == 0) return;  // the same k in every CTA that passed the barrier
+    if (k == 0) {  // the same k in every CTA that passed the barrier
+        if (fused && r == 0)
+            for (int d = tid; d < kDim; d += kCThreads) p.ga.out[h * kDim + d] = 0.0f;
+        return;
+    }
 
     // ---- 3. radix select over the cluster's histograms.  Thread t owns
     // coarse bins 1023 - 2t and 1022 - 2t (descending).
@@ -938,48 +1054,84 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
         }
     }
     cl.sync();  // survivors and tie witnesses are in the leader
-    if (r != 0) return;
-
-    // ---- leader: boundary tie (gqa_policy.cpp:66) and reference order
-    unsigned long long* src = small ? bufA : p.sortbuf + (unsigned long long)h * 2 * p.kcap;
-    unsigned long long* tmp = small ? bufB : src + p.kcap;
-    if (!p.cover && tid == 0 && k < n && eq_total > need_eq && sh.last_id < n && sh.next_id < n) {
-        bool tied = true;
-        if (kstar == 0x8000u) {
-            const unsigned long long base = (unsigned long long)h * p.stride;
-            uint16_t a, b;
-            if (p.mode == kInputKeys) {
-                a = p.tie_raw ? scale_half(p.tie_raw[base + sh.last_id]) : 0;
-                b = p.tie_raw ? scale_half(p.tie_raw[base + sh.next_id]) : 0;
-            } else {
-                a = p.scores[base + sh.last_id];
-                b = p.scores[base + sh.next_id];
-                if (p.mode == kInputRaw) {
-                    a = scale_half(a);
-                    b = scale_half(b);
-                }
-            }
-            tied = a == b;
-        }
-        if (tied) atomicAdd(&p.result->boundary_tied_heads, 1u);
-    }
     uint32_t* out = p.ids + (unsigned long long)h * p.kcap;
-    if (k <= kRankSortMax) {
-        if ((unsigned)tid < k) {
-            const unsigned long long e = src[tid];
-            const unsigned int ek = (unsigned int)(e >> 32);
-            unsigned int rk = 0;
-            for (unsigned int j = 0; j < k; ++j) {
-                const unsigned int ok = (unsigned int)(src[j] >> 32);
-                rk += (ok > ek) || (ok == ek && j < (unsigned)tid);
+    if (r == 0) {
+        // ---- leader: boundary tie (gqa_policy.cpp:66) and reference order
+        unsigned long long* src = small ? bufA : p.sortbuf + (unsigned long long)h * 2 * p.kcap;
+        unsigned long long* tmp = small ? bufB : src + p.kcap;
+        if (!p.cover && tid == 0 && k < n && eq_total > need_eq && sh.last_id < n && sh.next_id < n) {
+            bool tied = true;
+            if (kstar == 0x8000u) {
+                const unsigned long long base = (unsigned long long)h * p.stride;
+                uint16_t a, b;
+                if (p.mode == kInputKeys) {
+                    a = p.tie_raw ? scale_half(p.tie_raw[base + sh.last_id]) : 0;
+                    b = p.tie_raw ? scale_half(p.tie_raw[base + sh.next_id]) : 0;
+                } else {
+                    a = p.scores[base + sh.last_id];
+                    b = p.scores[base + sh.next_id];
+                    if (p.mode == kInputRaw) {
+                        a = scale_half(a);
+                        b = scale_half(b);
+                    }
+                }
+                tied = a == b;
             }
-            if (rk < k) out[rk] = (uint32_t)(e & 0xffffffffu);
+            if (tied) atomicAdd(&p.result->boundary_tied_heads, 1u);
         }
-        return;
+        if (k <= kRankSortMax) {
+            if ((unsigned)tid < k) {
+                const unsigned long long e = src[tid];
+                const unsigned int ek = (unsigned int)(e >> 32);
+                unsigned int rk = 0;
+                for (unsigned int j = 0; j < k; ++j) {
+                    const unsigned int ok = (unsigned int)(src[j] >> 32);
+                    rk += (ok > ek) || (ok == ek && j < (unsigned)tid);
+                }
+                if (rk < k) out[rk] = (uint32_t)(e & 0xffffffffu);
+            }
+        } else {
+            sort_pass<kCThreads>(sh.hist, sh.scan, &sh.total, src, tmp, (unsigned int)k, 0);
+            sort_pass<kCThreads>(sh.hist, sh.scan, &sh.total, tmp, src, (unsigned int)k, 8);
+            for (unsigned int j = tid; j < k; j += kCThreads) out[j] = (uint32_t)(src[j] & 0xffffffffu);
+        }
     }
-    sort_pass<kCThreads>(sh.hist, sh.scan, &sh.total, src, tmp, (unsigned int)k, 0);
-    sort_pass<kCThreads>(sh.hist, sh.scan, &sh.total, tmp, src, (unsigned int)k, 8);
-    for (unsigned int j = tid; j < k; j += kCThreads) out[j] = (uint32_t)(src[j] & 0xffffffffu);
+    if (!fused) return;
+
+    // ---- epilogue: gather the head's selected rows and attend over them
+    cl.sync();  // the ordered ids are written (cluster-scope release / acquire)
+    EpiSmem& es = *reinterpret_cast<EpiSmem*>(dyn);  // keys and sort buffers are no longer needed
+    const int grp = tid / kEpiThreads, gtid = tid % kEpiThreads;
+    if (tid < kDim) es.q[tid >> 5][tid & 31] = __ldg(p.ga.q + h * kDim + tid);
+    __syncthreads();
+    float M = -INFINITY, L = 0.0f, acc = 0.0f;
+    const unsigned ntiles = (unsigned)((k + 31) / 32);
+    // Tile t goes to CTA t % 4, group (t / 4) % 4: a few tiles spread over SMs first.
+    for (unsigned t = grp * kCluster + r; t < ntiles; t += kCluster * kEpiGroups) {
+        const unsigned s0 = t * 32;
+        epilogue_tile(p.ga, out, (int)h, s0, (int)min(32ull, k - s0), &es.q[0][0], es.g[grp], gtid, 1 + grp, M, L,
+                      acc);
+    }
+    EpiSmem* lead_es = cl.map_shared_rank(&es, 0);
+    float* part = lead_es->part[r * kEpiGroups + grp];
+    if (gtid == 0) {
+        part[0] = M;
+        part[1] = L;
+    }
+    part[2 + gtid] = acc;
+    cl.sync();  // every group's partial is in the leader
+    if (r != 0) return;
+    if (tid < kDim) {
+        float mx = -INFINITY;
+        for (int i = 0; i < kCluster * kEpiGroups; ++i) mx = fmaxf(mx, es.part[i][0]);
+        float lsum = 0.0f, o = 0.0f;
+        for (int i = 0; i < kCluster * kEpiGroups; ++i) {
+            const float w = es.part[i][0] == -INFINITY ? 0.0f : expf(es.part[i][0] - mx);
+            lsum = fmaf(es.part[i][1], w, lsum);
+            o = fmaf(es.part[i][2 + tid], w, o);
+        }
+        p.ga.out[h * kDim + tid] = lsum > 0.0f ? o / lsum : 0.0f;
+    }
 }
 
 // Heads (clusters of kCluster CTAs) the cluster path can hold resident at
@@ -1048,6 +1200,8 @@ cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream) {
     }
     p.sortbuf = reinterpret_cast<unsigned long long*>(ws + off);
     p.h0 = s.h0;
+    p.ga = s.ga;
+    if (s.ga_done) *s.ga_done = 0;
     cudaError_t e = cudaSuccess;
     if (s.reset_header) {
         e = cudaMemsetAsync(ws, 0, sizeof(SelectHeader), stream);
@@ -1071,8 +1225,12 @@ cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream) {
         cfg.gridDim = dim3(s.heads * kCluster);
         cfg.blockDim = dim3(kCThreads);
         cfg.dynamicSmemBytes = ((cs + 7) / 8 * 8 * 2 + 15) / 16 * 16 + 2 * kSmemSortMax * 8;
-        return cudaLaunchKernelEx(&cfg, select_cluster_kernel, p);
+        if (s.ga.out) cfg.dynamicSmemBytes = std::max(cfg.dynamicSmemBytes, kEpiSmemBytes);
+        const cudaError_t le = cudaLaunchKernelEx(&cfg, select_cluster_kernel, p);
+        if (le == cudaSuccess && s.ga_done) *s.ga_done = s.ga.out != nullptr;
+        return le;
     }
+    p.ga = SelectEpilogue{};  // the one-CTA-per-head kernel has no epilogue
     const size_t keys_bytes = s.valid <= kSmemKeysMax ? ((size_t)s.valid * 2 + 15) / 16 * 16 : 0;
     static thread_local int configured_device = -1;
     if (configured_device != dev.ordinal) {
