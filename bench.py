@@ -49,6 +49,10 @@ def parse():
     ap.add_argument("--tokens", type=int, default=N)
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="decode", choices=["decode", "kv-sharded"],
+                    help="decode: configs[1] (the headline); kv-sharded: configs[4], one selected-KV layer "
+                         "over --batch sequences with the KV heads split over the ranks")
+    ap.add_argument("--batch", type=int, default=64)
     return ap.parse_args()
 
 
@@ -536,6 +540,76 @@ def run_reference(args, rank, world, torch):
                     "d2h_bytes_per_step": 0}}
 
 
+def run_sharded(args, rank, world, torch, dist):
+    """--batch independent sequences of N tokens, one selected-KV
+    layer, KV heads split over the ranks (G = 8 / world per rank), with the
+    threshold broadcast, count-record and output all-gathers over NCCL.  The
+    whole step (kernels and collectives) is captured in one CUDA graph."""
+    import hillserve_b200 as hsb
+    from hillserve_b200 import sharded as sh
+
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+    lib = hsb._capi.lib()
+    n, batch, g = args.tokens, args.batch, 8 // world
+    s = torch.cuda.current_stream().cuda_stream
+    q16 = torch.empty((batch, HEADS, 128), dtype=torch.int16, device="cuda")
+    kshard = torch.empty((batch, n, g, 128), dtype=torch.int16, device="cuda")
+    vshard = torch.empty_like(kshard)
+    rows = torch.empty((n, 8, 128), dtype=torch.int16, device="cuda")
+    for b in range(batch):  # the same sequences on every rank; each keeps its own heads
+        lib.hsb_synth_normal_f16(q16[b].data_ptr(), 4096, 9000 + 7 * b, 1.0, s)
+        lib.hsb_synth_keys(rows.data_ptr(), n, 1024, 9001 + 7 * b, 0.02, 4.0, 1, THETA, s)
+        kshard[b].copy_(rows[:, g * rank:g * (rank + 1), :])
+        lib.hsb_synth_keys(rows.data_ptr(), n, 1024, 9002 + 7 * b, 0.0, 1.0, 0, THETA, s)
+        vshard[b].copy_(rows[:, g * rank:g * (rank + 1), :])
+    del rows
+    q32 = q16.view(torch.float16).float()
+    q16l, q32l = sh.shard_queries(q16, world, rank), sh.shard_queries(q32, world, rank)
+    layer = sh.KVHeadShardedLayer(n, batch, world, rank, alpha=args.alpha)
+    stream = torch.cuda.Stream()
+    holder = {}
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            holder["out"], holder["res"] = layer.step(q16l, q32l, kshard, vshard)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        holder["out"], holder["res"] = layer.step(q16l, q32l, kshard, vshard)
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            stop.record(stream)
+        stop.synchronize()
+    torch.cuda.synchronize()
+    dist.barrier()
+    t = torch.tensor([start.elapsed_time(stop)], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    res = holder["res"].cpu().numpy()
+    graph.reset()
+    b_layer = 2048 * n + 8192 + 64 * n  # per sequence: K read by the scorer, Q, scores + keys
+    return {"metric": "KV-head-sharded selected-KV layer: sequence-layer-steps/s at N=32K",
+            "value": round(batch * args.steps / (ms / 1e3), 1), "unit": "sequence-layer-steps/s",
+            "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 in, f32 accumulate (ordered)", "data": "synthetic",
+            "config": {"workload": "configs[4]: one selected-KV layer, KV heads sharded over the GPUs",
+                       "sequences": batch, "tokens": n, "alpha": args.alpha, "cap_ratio": 0.2,
+                       "kv_heads_per_gpu": g, "parallelism": f"KV-head shards x{world}",
+                       "exchange": "NCCL broadcast of thresholds, all-gather of count records and outputs",
+                       "launch": "one CUDA graph per step (kernels and collectives)"},
+            "score_bytes_per_step": b_layer * batch, "selection": {"k_mean": float(res[:, 0].mean()),
+                                                                 "zero_selection": int((res[:, 0] == 0).sum())},
+            "clocks": clocks.summary()}
+
+
 def main():
     args = parse()
     import torch
@@ -553,6 +627,17 @@ def main():
         dist = tdist
     if args.impl == "reference":
         line = run_reference(args, rank, world, torch)
+    elif args.workload == "kv-sharded":
+        if dist is None:  # one GPU: a world of one, still through the process-group code
+            import datetime
+
+            import torch.distributed as tdist
+
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            os.environ.setdefault("MASTER_PORT", "29533")
+            tdist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=120))
+            dist = tdist
+        line = run_sharded(args, rank, world, torch, dist)
     else:
         line = run_ours(args, rank, world, torch, dist)
     if rank == 0 and line is not None:

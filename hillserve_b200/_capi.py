@@ -69,6 +69,12 @@ _SIGNATURES = {
     "hsb_rehearsal_query": (I, [P, P, U64, F, P, P, P]),
     "hsb_layer_workspace_bytes": (SZ, [SZ, SZ]),
     "hsb_layer_step": (I, [P, P, P, P, SZ, SZ, F, F, SZ, P, P, P]),
+    "hsb_shard_head0_words": (SZ, []),
+    "hsb_shard_score": (I, [P, I, P, SZ, SZ, P, P, P, P]),
+    "hsb_shard_threshold": (I, [P, SZ, F, P, P]),
+    "hsb_shard_count": (I, [P, SZ, SZ, SZ, P, P, P]),
+    "hsb_shard_select_workspace_bytes": (SZ, [I, SZ, SZ, SZ]),
+    "hsb_shard_select": (I, [P, P, I, SZ, SZ, P, P, SZ, SZ, F, F, P, SZ, P, P, P, P, P, P, P, P, P, SZ, P]),
     "hsb_synth_normal_f16": (I, [P, SZ, U64, F, P]),
     "hsb_synth_normal_bf16": (I, [P, SZ, U64, F, P]),
     "hsb_synth_keys": (I, [P, SZ, SZ, U64, F, F, I, F, P]),

@@ -572,6 +572,117 @@ int hsb_layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_
     return HSB_OK;
 }
 
+// ------------------------------------------------------------ KV-head shards
+size_t hsb_shard_head0_words(void) { return kH0Partials; }
+
+static bool valid_kv_heads(int g) { return g == 1 || g == 2 || g == 4 || g == 8; }
+
+int hsb_shard_score(const uint16_t* d_q, int kv_heads, const uint16_t* d_kshard, size_t tokens, size_t batch,
+                    uint16_t* d_scores, uint16_t* d_order_keys, uint32_t* d_head0, void* stream) {
+    if (!d_q || !d_kshard || !d_scores || !d_order_keys || !valid_kv_heads(kv_heads) || tokens == 0 || batch == 0 ||
+        batch > 65535 || tokens * batch > 0x7fffffffull)
+        return fail(HSB_E_INVALID, "shard score arguments");
+    if (!aligned(d_kshard, 16)) return fail(HSB_E_INVALID, "key shard must be 16-byte aligned");
+    ScoreExtras x{};
+    x.h0 = d_head0;
+    const cudaError_t e = launch_score_shard(d_q, kv_heads, d_kshard, tokens, (size_t)kv_heads * HSB_DIM, d_scores,
+                                             d_order_keys, nullptr, &x, as_stream(stream), batch);
+    if (e != cudaSuccess) return fail_cuda(e, "shard score launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+int hsb_shard_threshold(const uint32_t* d_head0, size_t batch, float alpha, uint32_t* d_thr, void* stream) {
+    if (!d_head0 || !d_thr || batch == 0 || batch > 65535) return fail(HSB_E_INVALID, "shard threshold arguments");
+    if (!(alpha >= 0.0f) || !std::isfinite(alpha)) return fail(HSB_E_SEL_PARAMS, "GQA selector numeric parameters");
+    const cudaError_t e = launch_shard_threshold(d_head0, batch, alpha, d_thr, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "shard threshold launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+int hsb_shard_count(const uint16_t* d_order_keys, size_t heads, size_t tokens, size_t batch, const uint32_t* d_thr,
+                    uint32_t* d_records, void* stream) {
+    if (!d_order_keys || !d_thr || !d_records || heads == 0 || heads > 128 || tokens == 0 ||
+        tokens > 0x7fffffffull || batch == 0 || heads * batch > 0x7fffffffull)
+        return fail(HSB_E_INVALID, "shard count arguments");
+    const cudaError_t e = launch_shard_count(d_order_keys, heads, tokens, batch, d_thr, d_records, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "shard count launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+size_t hsb_shard_select_workspace_bytes(int kv_heads, size_t tokens, size_t kcap, size_t batch) {
+    return select_workspace_bytes((size_t)(valid_kv_heads(kv_heads) ? kv_heads : 8) * 4 * (batch ? batch : 1), tokens,
+                                  kcap);
+}
+
+int hsb_shard_select(const uint16_t* d_order_keys, const uint16_t* d_raw, int kv_heads, size_t tokens, size_t batch,
+                     const uint32_t* d_thr, const uint32_t* d_records, size_t heads_total, size_t head_base,
+                     float alpha, float ratio, uint32_t* d_ids, size_t kcap, uint32_t* d_counts,
+                     hsb_selection* d_result, const float* d_q32, const uint16_t* d_kshard, const uint16_t* d_vshard,
+                     uint16_t* d_k_packed, uint16_t* d_v_packed, float* d_out, void* d_workspace,
+                     size_t workspace_bytes, void* stream) {
+    if (!valid_kv_heads(kv_heads)) return fail(HSB_E_INVALID, "shard select: kv_heads must be 1, 2, 4 or 8");
+    const size_t heads = (size_t)kv_heads * 4;
+    int rc = check_select(heads_total, tokens, tokens, alpha, ratio);
+    if (rc) return rc;
+    if (batch == 0 || batch * heads * 4 > 0x7fffffffull)
+        return fail(HSB_E_INVALID, "shard select: batch out of range");
+    if (heads_total % 4 || head_base % 4 || head_base + heads > heads_total)
+        return fail(HSB_E_INVALID, "shard select: head range outside the query heads");
+    if (!d_order_keys || !d_thr || !d_records || !d_ids || !d_result || !d_q32 || !d_kshard || !d_vshard ||
+        !d_k_packed || !d_v_packed || !d_out)
+        return fail(HSB_E_INVALID, "shard select arguments");
+    if (kcap < select_kmax(tokens, ratio)) return fail(HSB_E_SEL_CAPACITY, hsb_status_message(HSB_E_SEL_CAPACITY));
+    if (!aligned(d_q32, 16) || !aligned(d_kshard, 16) || !aligned(d_vshard, 16) || !aligned(d_k_packed, 16) ||
+        !aligned(d_v_packed, 16))
+        return fail(HSB_E_INVALID, "shard select: query, shards and packed buffers must be 16-byte aligned");
+    if (!select_cluster_available(tokens))
+        return fail(HSB_E_INVALID, "shard select: at most 65536 tokens per head on this device");
+    if (!d_workspace || workspace_bytes < select_workspace_bytes(heads * batch, tokens, kcap))
+        return fail(HSB_E_WORKSPACE, "shard select workspace missing or too small");
+    cudaError_t e = cudaMemsetAsync(d_result, 0, batch * sizeof(hsb_selection), as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "result reset");
+    SelectLaunch sl{};
+    sl.scores = d_order_keys;
+    sl.keys = 1;
+    sl.tie_raw = d_raw;
+    sl.heads = (uint32_t)heads;
+    sl.stride = tokens;
+    sl.valid = tokens;
+    sl.alpha = alpha;
+    sl.ratio = ratio;
+    sl.ids = d_ids;
+    sl.kcap = kcap;
+    sl.counts = d_counts;
+    sl.result = d_result;
+    sl.workspace = d_workspace;
+    sl.workspace_bytes = workspace_bytes;
+    sl.zero_is_error = 1;
+    sl.reset_result = 0;
+    sl.ext = d_records;
+    sl.ext_thr = d_thr;
+    sl.head_base = (uint32_t)head_base;
+    sl.heads_total = (uint32_t)heads_total;
+    sl.batch = (uint32_t)batch;
+    sl.seq_scores = (unsigned long long)heads * tokens;
+    sl.ga.q = d_q32;
+    sl.ga.kcache = d_kshard;
+    sl.ga.vcache = d_vshard;
+    sl.ga.stride_words = (size_t)kv_heads * HSB_DIM;
+    sl.ga.kp = d_k_packed;
+    sl.ga.vp = d_v_packed;
+    sl.ga.count = kcap;
+    sl.ga.out = d_out;
+    sl.ga.scale = 1.0f / sqrtf(128.0f);
+    sl.ga.heads = (unsigned)heads;
+    e = launch_select(sl, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "shard select launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
 // ------------------------------------------------------------- synthetic
 int hsb_synth_normal_f16(uint16_t* d_out, size_t count, uint64_t seed, float stddev, void* stream) {
     if (!d_out) return fail(HSB_E_INVALID, "null output");

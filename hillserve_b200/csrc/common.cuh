@@ -156,7 +156,7 @@ __device__ __forceinline__ uint32_t warp_sum_u32(uint32_t v) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// 3-D tiled TMA load (no multicast) into this CTA's shared memory,
+// 3-D tiled TMA load into this CTA's own shared memory,
 // completing on the mbarrier `bar`.  x (innermost) must be a multiple of 8
 // 16-bit elements.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {

@@ -59,6 +59,15 @@ cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nv
                          uint16_t* out, size_t out_stride, size_t col0,
                          hsb_device_status* status, cudaStream_t stream, uint16_t* keys = nullptr,
                          const ScoreExtras* extras = nullptr);
+// A KV-head shard: keys_cache rows hold kv_heads (1, 2, 4 or 8) KV heads of
+// 128 channels; q holds the shard's 4 * kv_heads query heads; out / keys are
+// [4 * kv_heads][tokens].  extras->h0 when the shard holds query head 0.
+// batch > 1: that many sequences back to back (keys_cache [batch][tokens],
+// q [batch][4 kv_heads][128], out / keys [batch][4 kv_heads][tokens],
+// extras->h0 [batch][kH0Partials]).
+cudaError_t launch_score_shard(const uint16_t* q, int kv_heads, const uint16_t* keys_cache, size_t tokens,
+                               size_t stride_words, uint16_t* out, uint16_t* keys, hsb_device_status* status,
+                               const ScoreExtras* extras, cudaStream_t stream, size_t batch = 1);
 cudaError_t launch_scale(const uint16_t* raw, size_t count, uint16_t* out, cudaStream_t stream);
 // Tensor map of a token-major [tokens][8][128] F16 cache seen as {channel,
 // token, KV head} with 64 x 32 x 8 boxes and the 128-byte swizzle (the
@@ -84,6 +93,7 @@ struct SelectEpilogue {
     size_t count = 0;
     float* out = nullptr;    // null: no epilogue
     float scale = 0.0f;
+    unsigned heads = 32;     // query heads per packed K slot (a shard packs its own)
 };
 struct SelectLaunch {
     const uint16_t* scores;
@@ -108,7 +118,22 @@ struct SelectLaunch {
     const uint32_t* h0 = nullptr;  // the scorer's head-0 partials (ScoreExtras::h0)
     SelectEpilogue ga;             // run by the cluster kernel only
     int* ga_done = nullptr;        // out: 1 when the epilogue was launched
+    // KV-head shard step: records from the exchange replace count + barrier.
+    const uint32_t* ext = nullptr;      // [heads_total] count | non-finite << 31
+    const uint32_t* ext_thr = nullptr;  // {threshold key, status}
+    uint32_t head_base = 0, heads_total = 0;
+    // Shard steps over a batch of sequences: scores / keys [batch][heads][stride]
+    // (seq_scores = heads * stride), ids [batch][heads][kcap], counts
+    // [batch][heads], result [batch], ext [batch][heads_total], ext_thr [batch][2],
+    // and the epilogue's buffers per sequence.
+    uint32_t batch = 1;
+    unsigned long long seq_scores = 0;
 };
+cudaError_t launch_shard_threshold(const uint32_t* h0, size_t batch, float alpha, uint32_t* thr,
+                                   cudaStream_t stream);
+cudaError_t launch_shard_count(const uint16_t* keys, size_t heads, size_t tokens, size_t batch, const uint32_t* thr,
+                               uint32_t* records, cudaStream_t stream);
+bool select_cluster_available(size_t valid);
 size_t select_workspace_bytes(size_t heads, size_t valid, size_t kcap);
 size_t select_header_bytes();  // leading bytes of the workspace that start at zero
 cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream);

@@ -228,6 +228,11 @@ struct TmaParams {
     unsigned long long out_stride;
     hsb_device_status* status;
     ScoreExtras extras;
+    // Batch of sequences (blockIdx.y = sequence; 1 outside shard steps): one
+    // view of batch * seq_tokens tokens, sequence b at token b * seq_tokens;
+    // per sequence, q advances by q_seq, out / keys by out_seq elements and
+    // extras.h0 by kH0Partials words.
+    unsigned long long seq_tokens, q_seq, out_seq;
 };
 
 __device__ __forceinline__ float fma_f16(uint32_t a16, uint32_t b16, float c) {
@@ -243,7 +248,13 @@ __device__ __forceinline__ int tile_view(const TmaParams& p, unsigned long long 
     return v;
 }
 
+// G = KV heads per cache row (8 for a whole cache, fewer for a KV-head shard);
+// a tile is T = 256 / G tokens x G KV heads, so every stage stays 32 KB.
+// Consumer warp w scores KV head w % G for tokens [32 (w / G), +32) of the
+// tile; its four output rows are the query heads 4 (w % G) + g.
+template <int G>
 __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_constant__ TmaParams p) {
+    constexpr int T = 256 / G;
     pdl_wait();
     pdl_trigger();
     extern __shared__ unsigned char smem_raw[];
@@ -258,10 +269,23 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
     uint64_t* empty = full + kTStages;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    clear_extras(p.extras, blockDim.x);
-    for (int i = threadIdx.x; i < kHeads * kDim; i += blockDim.x) {
+    const unsigned seq = blockIdx.y;
+    const uint16_t* qg = p.q + seq * p.q_seq;
+    uint16_t* out = p.out + seq * p.out_seq;
+    uint16_t* okeys = p.keys ? p.keys + seq * p.out_seq : nullptr;
+    ScoreExtras extras = p.extras;
+    if (extras.h0) extras.h0 += (size_t)seq * kH0Partials;
+    const int y0 = (int)(seq * p.seq_tokens);  // first token row of this sequence in the view
+    clear_extras(extras, blockDim.x);
+    for (int i = threadIdx.x; i < G * kGroup * kDim; i += blockDim.x) {
         const int h = i >> 7, c = i & 127;
-        reinterpret_cast<uint16_t*>(qs)[((h >> 2) * kDim + c) * kGroup + (h & 3)] = p.q[i];
+        reinterpret_cast<uint16_t*>(qs)[((h >> 2) * kDim + c) * kGroup + (h & 3)] = qg[i];
+    }
+    __shared__ unsigned int h0_max, h0_bad, h0_done;
+    if (threadIdx.x == 0) {
+        h0_max = 0;
+        h0_bad = 0;
+        h0_done = 0;
     }
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTStages; ++s) {
@@ -281,7 +305,7 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
         bool ok = true;
         for (unsigned long long tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
             const int v = tile_view(p, tile);
-            const int t0 = (int)((tile - p.view_tile0[v]) * kTTile);
+            const int t0 = (int)((tile - p.view_tile0[v]) * T);
             for (int half = 0; half < 2; ++half, ++it) {
                 const uint32_t s = it % kTStages;
                 if (it >= kTStages && !mbar_wait(&empty[s], ((it / kTStages) - 1) & 1)) {
@@ -290,7 +314,7 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
                     break;
                 }
                 mbar_arrive_expect_tx(&full[s], kTStageBytes);
-                tma_load_3d(stages + s * kTStageBytes, &p.maps[v], half * kTHalf, t0, 0, &full[s]);
+                tma_load_3d(stages + s * kTStageBytes, &p.maps[v], half * kTHalf, y0 + t0, 0, &full[s]);
             }
         }
         if (!ok) {  // let copies in flight land before shared memory is released
@@ -301,12 +325,12 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
     }
 
     // ---------------- consumers
-    const int kh = warp, tl = lane;  // KV head, token in tile
+    const int kh = warp % G, tl = (warp / G) * 32 + lane;  // KV head, token in tile
     const uint4* qv = qs + kh * (kDim / 2);
     uint32_t it = 0, h0max = 0, h0bad = 0;
     for (unsigned long long tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
         const int v = tile_view(p, tile);
-        const unsigned long long t0 = (tile - p.view_tile0[v]) * kTTile;
+        const unsigned long long t0 = (tile - p.view_tile0[v]) * T;
         float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
         for (int half = 0; half < 2; ++half, ++it) {
             const uint32_t s = it % kTStages;
@@ -314,7 +338,7 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
                 raise_status(p.status, HSB_E_TIMEOUT, blockIdx.x);
                 return;
             }
-            const unsigned char* row = stages + s * kTStageBytes + (kh * kTTile + tl) * 128;
+            const unsigned char* row = stages + s * kTStageBytes + (kh * T + tl) * 128;
             const uint4* qh = qv + half * (kTHalf / 2);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
@@ -345,16 +369,29 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
             for (int g = 0; g < kGroup; ++g) {
                 const uint16_t sc = half_bits(acc[g]);
                 const unsigned long long at = (unsigned long long)(kh * kGroup + g) * p.out_stride + col;
-                p.out[at] = sc;
-                if (p.keys) {
+                out[at] = sc;
+                if (okeys) {
                     const uint32_t key = order_key(scale_half(sc));
-                    p.keys[at] = (uint16_t)key;
+                    okeys[at] = (uint16_t)key;
                     if (kh == 0 && g == 0) track_head0(key, h0max, h0bad);
                 }
             }
         }
     }
-    if (kh == 0 && p.extras.h0) write_head0(p.extras, h0max, h0bad);
+    if (extras.h0) {
+        if (G == kKvHeads) {
+            if (kh == 0) write_head0(extras, h0max, h0bad);
+        } else if (kh == 0) {  // 8 / G warps hold KV head 0: the last one to finish writes
+            const uint32_t m = __reduce_max_sync(0xffffffffu, h0max);
+            const uint32_t b = __reduce_or_sync(0xffffffffu, h0bad);
+            if (lane == 0) {
+                atomicMax(&h0_max, m);
+                atomicOr(&h0_bad, b);
+                if (atomicAdd(&h0_done, 1u) == (unsigned)(kTConsumerWarps / G) - 1)
+                    extras.h0[blockIdx.x] = (atomicOr(&h0_bad, 0u) << 16) | atomicMax(&h0_max, 0u);
+            }
+        }
+    }
 }
 
 // Resolves cuTensorMapEncodeTiled through the runtime (no libcuda link).
@@ -376,12 +413,12 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // Token-major keys of one view seen as a 3-D tensor {channel, token, KV head}
 // (strides: token = stride_words words, KV head = 128 words), so that a box
 // lands in shared memory as [KV head][token][channels].
-bool encode_view(CUtensorMap* map, const hsb_key_view& v) {
+bool encode_view(CUtensorMap* map, const hsb_key_view& v, int g = kKvHeads) {
     auto encode = tensor_map_encoder();
     if (!encode) return false;
-    const cuuint64_t dims[3] = {(cuuint64_t)kDim, (cuuint64_t)v.tokens, (cuuint64_t)kKvHeads};
+    const cuuint64_t dims[3] = {(cuuint64_t)kDim, (cuuint64_t)v.tokens, (cuuint64_t)g};
     const cuuint64_t strides[2] = {(cuuint64_t)v.stride_words * 2, (cuuint64_t)kDim * 2};
-    const cuuint32_t box[3] = {(cuuint32_t)kTHalf, (cuuint32_t)kTTile, (cuuint32_t)kKvHeads};
+    const cuuint32_t box[3] = {(cuuint32_t)kTHalf, (cuuint32_t)(256 / g), (cuuint32_t)g};
     const cuuint32_t estr[3] = {1, 1, 1};
     return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<uint16_t*>(v.data), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
@@ -396,6 +433,17 @@ __global__ void scale_kernel(const uint16_t* __restrict__ raw, unsigned long lon
 }
 
 }  // namespace
+
+cudaError_t configure_tma_kernels() {
+    cudaError_t e = cudaFuncSetAttribute(score_tma_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(score_tma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(score_tma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(score_tma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemBytes);
+    return e;
+}
 
 bool encode_kv_map(CUtensorMap* map, const uint16_t* data, size_t tokens, size_t stride_words) {
     const hsb_key_view v{data, tokens, stride_words};
@@ -412,8 +460,7 @@ cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nv
     if (configured_device != dev.ordinal) {
         cudaError_t e = cudaFuncSetAttribute(score_v3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              kSmemBytes);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(score_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemBytes);
+        if (e == cudaSuccess) e = configure_tma_kernels();
         if (e != cudaSuccess) return e;
         configured_device = dev.ordinal;
     }
@@ -441,7 +488,8 @@ cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nv
             t.status = status;
             t.extras = x;
             const int grid = (int)std::min<unsigned long long>(tiles, (unsigned long long)dev.sms * 2);
-            return launch_dependent(score_tma_kernel, dim3(grid), dim3(kTThreads), kTSmemBytes, stream, false, t);
+            return launch_dependent(score_tma_kernel<kKvHeads>, dim3(grid), dim3(kTThreads), kTSmemBytes, stream,
+                                    false, t);
         }
     }
     ScoreParams p{};
@@ -465,6 +513,49 @@ cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nv
     const unsigned long long ntiles = (tokens + kTile - 1) / kTile;
     const int grid = (int)std::min<unsigned long long>(ntiles, (unsigned long long)dev.sms);
     return launch_dependent(score_v3_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, false, p);
+}
+
+cudaError_t launch_score_shard(const uint16_t* q, int kv_heads, const uint16_t* keys_cache, size_t tokens,
+                               size_t stride_words, uint16_t* out, uint16_t* keys, hsb_device_status* status,
+                               const ScoreExtras* extras, cudaStream_t stream, size_t batch) {
+    const DeviceInfo& dev = device_info();
+    static thread_local int configured_device = -1;
+    if (configured_device != dev.ordinal) {
+        const cudaError_t e = configure_tma_kernels();
+        if (e != cudaSuccess) return e;
+        configured_device = dev.ordinal;
+    }
+    TmaParams t{};
+    if (batch == 0 || tokens * batch > 0x7fffffffull) return cudaErrorInvalidValue;
+    const hsb_key_view view{keys_cache, tokens * batch, stride_words};  // the whole batch as one view
+    if (!encode_view(&t.maps[0], view, kv_heads)) return cudaErrorInvalidValue;
+    const unsigned long long tile_tokens = 256 / kv_heads;
+    t.seq_tokens = tokens;
+    t.q_seq = (unsigned long long)kv_heads * kGroup * kDim;
+    t.out_seq = (unsigned long long)kv_heads * kGroup * tokens;
+    t.view_tokens[0] = tokens;
+    t.view_tile0[0] = 0;
+    t.view_col[0] = 0;
+    t.tiles = (tokens + tile_tokens - 1) / tile_tokens;
+    t.view_tile0[1] = t.tiles;
+    t.nviews = 1;
+    t.q = q;
+    t.out = out;
+    t.keys = keys;
+    t.out_stride = tokens;
+    t.status = status;
+    if (extras) t.extras = *extras;
+    // CTAs per sequence: the whole batch fills two CTAs per SM.
+    const unsigned long long per_seq =
+        std::max<unsigned long long>(1, ((unsigned long long)dev.sms * 2 + batch - 1) / batch);
+    const dim3 grid((unsigned)std::min<unsigned long long>(t.tiles, per_seq), (unsigned)batch);
+    switch (kv_heads) {
+    case 1: return launch_dependent(score_tma_kernel<1>, grid, dim3(kTThreads), kTSmemBytes, stream, false, t);
+    case 2: return launch_dependent(score_tma_kernel<2>, grid, dim3(kTThreads), kTSmemBytes, stream, false, t);
+    case 4: return launch_dependent(score_tma_kernel<4>, grid, dim3(kTThreads), kTSmemBytes, stream, false, t);
+    case 8: return launch_dependent(score_tma_kernel<8>, grid, dim3(kTThreads), kTSmemBytes, stream, false, t);
+    default: return cudaErrorInvalidValue;
+    }
 }
 
 cudaError_t launch_scale(const uint16_t* raw, size_t count, uint16_t* out, cudaStream_t stream) {

@@ -73,6 +73,18 @@ struct SelectParams {
     unsigned long long* sortbuf;  // [heads][2][kcap] when k > kSmemSortMax
     const uint32_t* h0;           // optional: the scorer's head-0 partials [kH0Partials]
     SelectEpilogue ga;            // cluster path: gather + attention of the selection (ga.out != null)
+    // KV-head shard (cluster path): the heads [head_base, head_base + heads)
+    // of heads_total; the threshold record ext_thr = {key, status} and every
+    // head's count record ext[heads_total] (count | non-finite << 31) come
+    // from the exchange between shards, replacing the count and the barrier.
+    const uint32_t* ext;
+    const uint32_t* ext_thr;
+    uint32_t head_base, heads_total;
+    // Batch of sequences (shard steps; 1 otherwise): blockIdx.x covers
+    // batch x heads x kCluster.  Sequence b's scores / keys start b *
+    // seq_scores elements in; every per-head output advances by its own size.
+    uint32_t batch;
+    unsigned long long seq_scores;
 };
 
 // Head-0 maximum key and non-finite flag from the scorer's per-CTA partials
@@ -606,7 +618,7 @@ __device__ __forceinline__ void epilogue_tile(const SelectEpilogue& e, const uin
             kr[u] = __ldg(ks + u);
             vr[u] = __ldg(vs + u);
         }
-        uint4* kd = reinterpret_cast<uint4*>(e.kp + ((size_t)(s0 + slot) * kHeads + h) * kDim) + qd * 4;
+        uint4* kd = reinterpret_cast<uint4*>(e.kp + ((size_t)(s0 + slot) * e.heads + h) * kDim) + qd * 4;
 #pragma unroll
         for (int u = 0; u < 4; ++u) kd[u] = kr[u];
     } else {
@@ -689,7 +701,11 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     __shared__ ClusterShared sh;
     cg::cluster_group cl = cg::this_cluster();
     const unsigned int r = cl.block_rank();
-    const uint32_t h = blockIdx.x / kCluster;
+    const uint32_t h = (blockIdx.x / kCluster) % p.heads;
+    const uint32_t seqb = blockIdx.x / (kCluster * p.heads);  // sequence of the batch
+    const bool seq_first = blockIdx.x % (kCluster * p.heads) == 0;  // first CTA of the sequence
+    const uint16_t* scores = p.scores + seqb * p.seq_scores;
+    hsb_selection* result = p.result + seqb;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const unsigned long long n = p.valid;
     const unsigned long long cs = ((n + kCluster - 1) / kCluster + 7) / 8 * 8;
@@ -698,10 +714,10 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     uint16_t* keys = reinterpret_cast<uint16_t*>(dyn);  // [cs] this chunk's keys
     unsigned long long* bufA = reinterpret_cast<unsigned long long*>(dyn + (cs * 2 + 15) / 16 * 16);
     unsigned long long* bufB = bufA + kSmemSortMax;
-    const uint16_t* row0 = p.scores;
-    const uint16_t* row = p.scores + (unsigned long long)h * p.stride;
+    const uint16_t* row0 = scores;
+    const uint16_t* row = scores + (unsigned long long)h * p.stride;
     // 16-byte loads when rows are 16-byte aligned (b0 is a multiple of 8).
-    const bool vec = (p.stride % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.scores) & 15) == 0);
+    const bool vec = (p.stride % 8 == 0) && ((reinterpret_cast<uintptr_t>(scores) & 15) == 0);
     const unsigned long long n8 = vec ? n / 8 : 0;
     const unsigned int m8 = vec ? m / 8 : 0;
 
@@ -720,9 +736,10 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     // ---- 1. head-0 maximum over the whole row (every CTA, from L2), own
     // chunk's keys to shared memory with the coarse histogram.
     unsigned int mx = 0, bad0 = 0, bad = 0;
-    if (p.h0) head0_from_partials<kCThreads>(p.h0, mx, bad0);
+    const bool ext = p.ext != nullptr;
+    if (p.h0 && !ext) head0_from_partials<kCThreads>(p.h0, mx, bad0);
 #pragma unroll 4
-    for (unsigned long long g = tid; g < (p.h0 ? 0 : n8); g += kCThreads) {
+    for (unsigned long long g = tid; g < ((p.h0 || ext) ? 0 : n8); g += kCThreads) {
         const uint4 w = reinterpret_cast<const uint4*>(row0)[g];
         const uint32_t v[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -732,7 +749,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
             mx = key_nan(key) ? mx : max(mx, key);
         }
     }
-    for (unsigned long long i = n8 * 8 + tid; i < (p.h0 ? 0 : n); i += kCThreads) {
+    for (unsigned long long i = n8 * 8 + tid; i < ((p.h0 || ext) ? 0 : n); i += kCThreads) {
         const uint32_t key = to_key(row0[i], p.mode);
         bad0 |= key_nonfinite(key);
         mx = key_nan(key) ? mx : max(mx, key);
@@ -766,20 +783,24 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     __syncthreads();
     const float maximum = half_value((uint16_t)key_bits(sh.maxkey));
     const float threshold = half_value(half_bits(sh.maxkey ? maximum - p.alpha : -INFINITY));
-    const bool head0_bad = !p.cover && sh.bad0;
-    const bool thr_bad = !isfinite(threshold);
-    if (head0_bad || thr_bad) {
-        if (blockIdx.x == 0 && tid == 0) {
-            p.result->k = 0;
-            p.result->status.code = head0_bad ? HSB_E_SEL_NONFINITE_HEAD0
+    const int ext_status = ext ? (int)__ldg(p.ext_thr + 2 * seqb + 1) : 0;
+    const bool head0_bad = !ext && !p.cover && sh.bad0;
+    const bool thr_bad = !ext && !isfinite(threshold);
+    if (head0_bad || thr_bad || ext_status) {
+        if (seq_first && tid == 0) {
+            result->k = 0;
+            result->status.code = ext_status ? ext_status
+                                  : head0_bad ? HSB_E_SEL_NONFINITE_HEAD0
                                               : (p.cover ? HSB_E_COVER_THRESHOLD : HSB_E_SEL_THRESHOLD);
-            p.result->status.index = 0;
+            result->status.index = 0;
         }
+        if (p.ga.out && r == 0)  // the layer's output stays zero
+            for (int d = tid; d < kDim; d += kCThreads) p.ga.out[(seqb * p.heads + h) * kDim + d] = 0.0f;
         return;  // every CTA of the grid takes this branch; nothing is pending
     }
     const unsigned int thr_key = order_key(half_bits(threshold));
     unsigned int cnt = 0;
-    for (unsigned int i = tid; i < m; i += kCThreads) {
+    for (unsigned int i = tid; i < (ext ? 0u : m); i += kCThreads) {
         const unsigned int key = keys[i];
         cnt += (!key_nan(key) && key >= thr_key) ? 1u : 0u;
     }
@@ -793,7 +814,8 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     // The coarse histograms are complete: release them to the cluster now,
     // acquire after the grid barrier.
     cluster_arrive_release();
-    if (tid == 0) {
+    if (tid == 0 && ext) sh.timeout = 0;  // counts come from the exchange: no barrier
+    if (tid == 0 && !ext) {
         if (sh.cnt) atomicAdd(&p.header->cnt[h], sh.cnt);
         if (!p.cover && sh.bad) atomicOr(&p.header->err[h], 1u);
         // ---- 2. grid barrier (bounded): a release-ordered arrival (orders
@@ -815,22 +837,32 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
         unsigned int e[4] = {0, 0, 0, 0};
         float rr[4] = {0.f, 0.f, 0.f, 0.f};
         unsigned long long own = 0;
+        const uint32_t nh = ext ? p.heads_total : p.heads, own_head = ext ? p.head_base + h : h;
         if (!sh.timeout) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const uint32_t hh = lane * 4 + j;
-                if (hh < p.heads) {
-                    unsigned long long c = __ldcg(&p.header->cnt[hh]);
+                if (hh < nh) {
+                    unsigned long long c;
+                    uint32_t nonfinite;
+                    if (ext) {
+                        const uint32_t rec = __ldg(p.ext + seqb * p.heads_total + hh);
+                        c = rec & 0x7fffffffu;
+                        nonfinite = rec >> 31;
+                    } else {
+                        c = __ldcg(&p.header->cnt[hh]);
+                        nonfinite = __ldcg(&p.header->err[hh]) & 1u;
+                    }
                     if (p.cover) c += 1;  // at most one newly appended current token
                     const float rounded = p.fp32_counts ? (float)c : half_value(half_bits((float)c));
-                    e[j] = (__ldcg(&p.header->err[hh]) & 1u) | (isfinite(rounded) ? 0u : 2u);
+                    e[j] = nonfinite | (isfinite(rounded) ? 0u : 2u);
                     rr[j] = rounded;
-                    if (hh == h) own = c;
+                    if (hh == own_head) own = c;
                 }
             }
         }
         own = __reduce_max_sync(0xffffffffu, (unsigned int)own);
-        if (r == 0 && lane == 0 && p.counts && !sh.timeout) p.counts[h] = (uint32_t)own;
+        if (r == 0 && lane == 0 && p.counts && !sh.timeout) p.counts[seqb * p.heads + h] = (uint32_t)own;
         // First failing head in head order (non-finite before count overflow
         // within a head), found by ballot.  The rounded counts are integers
         // below 2^16 and there are at most 128 of them, so every partial sum
@@ -856,8 +888,8 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
         for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
         unsigned long long k = 0;
         if (!sh.timeout && !status) {
-            const float mean = p.fp32_counts ? __fdiv_rn(total, (float)p.heads)
-                                             : half_value(half_bits(__fdiv_rn(total, (float)p.heads)));
+            const float mean = p.fp32_counts ? __fdiv_rn(total, (float)nh)
+                                             : half_value(half_bits(__fdiv_rn(total, (float)nh)));
             if (p.cover) {
                 if (!(isfinite(mean) && mean >= 1.0f)) status = HSB_E_COVER_MEAN;
                 else k = min(p.cover_cap, (unsigned long long)mean);
@@ -877,9 +909,9 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
             sh.status_index = index;
             sh.k = status ? 0 : k;
             // *result starts zeroed (the launcher clears it).
-            if (blockIdx.x == 0) p.result->k = status ? 0u : (uint32_t)k;
-            if (sh.timeout) raise_status(&p.result->status, HSB_E_TIMEOUT, (int)blockIdx.x);
-            else if (blockIdx.x == 0 && status) raise_status(&p.result->status, (int)status, (int)index);
+            if (seq_first) result->k = status ? 0u : (uint32_t)k;
+            if (sh.timeout) raise_status(&result->status, HSB_E_TIMEOUT, (int)blockIdx.x);
+            else if (seq_first && status) raise_status(&result->status, (int)status, (int)index);
         }
     }
     __syncthreads();
@@ -893,7 +925,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     const unsigned long long k = sh.k;
     if (k == 0) {  // the same k in every CTA that passed the barrier
         if (fused && r == 0)
-            for (int d = tid; d < kDim; d += kCThreads) p.ga.out[h * kDim + d] = 0.0f;
+            for (int d = tid; d < kDim; d += kCThreads) p.ga.out[(seqb * p.heads + h) * kDim + d] = 0.0f;
         return;
     }
 
@@ -1004,7 +1036,8 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     // ---- 4. ordered compaction of this chunk into the leader's buffer (or
     // the head's workspace buffer when k exceeds it)
     const bool small = k <= kSmemSortMax;
-    unsigned long long* dst = small ? cl.map_shared_rank(bufA, 0) : p.sortbuf + (unsigned long long)h * 2 * p.kcap;
+    unsigned long long* sortbuf = p.sortbuf + ((unsigned long long)seqb * p.heads + h) * 2 * p.kcap;
+    unsigned long long* dst = small ? cl.map_shared_rank(bufA, 0) : sortbuf;
     ClusterShared* lead = cl.map_shared_rank(&sh, 0);
     // Thread t owns keys [t*per, t*per + per) of the chunk (ID order follows
     // thread order); one block scan of (gt << 16 | eq) places its survivors.
@@ -1054,10 +1087,10 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
         }
     }
     cl.sync();  // survivors and tie witnesses are in the leader
-    uint32_t* out = p.ids + (unsigned long long)h * p.kcap;
+    uint32_t* out = p.ids + ((unsigned long long)seqb * p.heads + h) * p.kcap;
     if (r == 0) {
         // ---- leader: boundary tie (gqa_policy.cpp:66) and reference order
-        unsigned long long* src = small ? bufA : p.sortbuf + (unsigned long long)h * 2 * p.kcap;
+        unsigned long long* src = small ? bufA : sortbuf;
         unsigned long long* tmp = small ? bufB : src + p.kcap;
         if (!p.cover && tid == 0 && k < n && eq_total > need_eq && sh.last_id < n && sh.next_id < n) {
             bool tied = true;
@@ -1065,11 +1098,12 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
                 const unsigned long long base = (unsigned long long)h * p.stride;
                 uint16_t a, b;
                 if (p.mode == kInputKeys) {
-                    a = p.tie_raw ? scale_half(p.tie_raw[base + sh.last_id]) : 0;
-                    b = p.tie_raw ? scale_half(p.tie_raw[base + sh.next_id]) : 0;
+                    const uint16_t* raw = p.tie_raw ? p.tie_raw + seqb * p.seq_scores : nullptr;
+                    a = raw ? scale_half(raw[base + sh.last_id]) : 0;
+                    b = raw ? scale_half(raw[base + sh.next_id]) : 0;
                 } else {
-                    a = p.scores[base + sh.last_id];
-                    b = p.scores[base + sh.next_id];
+                    a = scores[base + sh.last_id];
+                    b = scores[base + sh.next_id];
                     if (p.mode == kInputRaw) {
                         a = scale_half(a);
                         b = scale_half(b);
@@ -1077,7 +1111,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
                 }
                 tied = a == b;
             }
-            if (tied) atomicAdd(&p.result->boundary_tied_heads, 1u);
+            if (tied) atomicAdd(&result->boundary_tied_heads, 1u);
         }
         if (k <= kRankSortMax) {
             if ((unsigned)tid < k) {
@@ -1102,14 +1136,22 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     cl.sync();  // the ordered ids are written (cluster-scope release / acquire)
     EpiSmem& es = *reinterpret_cast<EpiSmem*>(dyn);  // keys and sort buffers are no longer needed
     const int grp = tid / kEpiThreads, gtid = tid % kEpiThreads;
-    if (tid < kDim) es.q[tid >> 5][tid & 31] = __ldg(p.ga.q + h * kDim + tid);
+    // This sequence's view of the epilogue's buffers.
+    SelectEpilogue ga = p.ga;
+    ga.q += ((size_t)seqb * p.heads) * kDim;
+    ga.out += ((size_t)seqb * p.heads) * kDim;
+    ga.kcache += (size_t)seqb * p.valid * ga.stride_words;
+    ga.vcache += (size_t)seqb * p.valid * ga.stride_words;
+    ga.kp += (size_t)seqb * ga.count * ga.heads * kDim;
+    ga.vp += (size_t)seqb * ga.count * ga.heads * kDim;
+    if (tid < kDim) es.q[tid >> 5][tid & 31] = __ldg(ga.q + h * kDim + tid);
     __syncthreads();
     float M = -INFINITY, L = 0.0f, acc = 0.0f;
     const unsigned ntiles = (unsigned)((k + 31) / 32);
     // Tile t goes to CTA t % 4, group (t / 4) % 4: a few tiles spread over SMs first.
     for (unsigned t = grp * kCluster + r; t < ntiles; t += kCluster * kEpiGroups) {
         const unsigned s0 = t * 32;
-        epilogue_tile(p.ga, out, (int)h, s0, (int)min(32ull, k - s0), &es.q[0][0], es.g[grp], gtid, 1 + grp, M, L,
+        epilogue_tile(ga, out, (int)h, s0, (int)min(32ull, k - s0), &es.q[0][0], es.g[grp], gtid, 1 + grp, M, L,
                       acc);
     }
     EpiSmem* lead_es = cl.map_shared_rank(&es, 0);
@@ -1130,8 +1172,90 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
             lsum = fmaf(es.part[i][1], w, lsum);
             o = fmaf(es.part[i][2 + tid], w, o);
         }
-        p.ga.out[h * kDim + tid] = lsum > 0.0f ? o / lsum : 0.0f;
+        ga.out[h * kDim + tid] = lsum > 0.0f ? o / lsum : 0.0f;
     }
+}
+
+// ------------------------------------------------------------- shard steps
+// The threshold record of a KV-head-sharded step, on the shard that holds
+// query head 0: {order key of F16(max - alpha), status}, the status being the
+// reference's head-0 / threshold errors (gqa_policy.cpp:50-54).
+constexpr int kShardThreads = 256;
+__global__ void __launch_bounds__(kShardThreads) shard_threshold_kernel(const uint32_t* h0, float alpha,
+                                                                       uint32_t* thr) {
+    pdl_wait();
+    pdl_trigger();
+    h0 += (size_t)blockIdx.x * kH0Partials;  // one CTA per sequence
+    thr += 2 * blockIdx.x;
+    __shared__ unsigned int smax, sbad;
+    if (threadIdx.x == 0) {
+        smax = 0;
+        sbad = 0;
+    }
+    __syncthreads();
+    unsigned int mx = 0, bad0 = 0;
+    head0_from_partials<kShardThreads>(h0, mx, bad0);
+    mx = __reduce_max_sync(0xffffffffu, mx);
+    bad0 = __reduce_or_sync(0xffffffffu, bad0);
+    if ((threadIdx.x & 31) == 0) {
+        atomicMax(&smax, mx);
+        atomicOr(&sbad, bad0);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const float maximum = half_value((uint16_t)key_bits(smax));
+        const float threshold = half_value(half_bits(smax ? maximum - alpha : -INFINITY));
+        uint32_t status = 0;
+        if (sbad) status = HSB_E_SEL_NONFINITE_HEAD0;
+        else if (!isfinite(threshold)) status = HSB_E_SEL_THRESHOLD;
+        thr[0] = status ? 0u : order_key(half_bits(threshold));
+        thr[1] = status;
+    }
+}
+
+// Count record of one of the shard's heads: #{keys >= threshold key} (NaN
+// never counts) | (any non-finite score) << 31.  One CTA per head.
+constexpr int kCountThreads = 1024;
+__global__ void __launch_bounds__(kCountThreads) shard_count_kernel(const uint16_t* keys, unsigned long long tokens,
+                                                                   unsigned heads, const uint32_t* thr,
+                                                                   uint32_t* records) {
+    pdl_wait();
+    pdl_trigger();
+    thr += 2 * (blockIdx.x / heads);  // CTA = (sequence, head), keys [batch][heads][tokens]
+    __shared__ unsigned int scnt, sbad;
+    if (threadIdx.x == 0) {
+        scnt = 0;
+        sbad = 0;
+    }
+    __syncthreads();
+    const unsigned int thr_key = __ldg(thr);
+    const uint16_t* row = keys + (unsigned long long)blockIdx.x * tokens;
+    const bool vec = tokens % 8 == 0 && (reinterpret_cast<uintptr_t>(keys) & 15) == 0;
+    const unsigned long long n8 = vec ? tokens / 8 : 0;
+    unsigned int cnt = 0, bad = 0;
+    for (unsigned long long g = threadIdx.x; g < n8; g += kCountThreads) {
+        const uint4 w = reinterpret_cast<const uint4*>(row)[g];
+        const uint32_t v[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t key = (v[j >> 1] >> (16 * (j & 1))) & 0xffffu;
+            bad |= key_nonfinite(key);
+            cnt += (!key_nan(key) && key >= thr_key) ? 1u : 0u;
+        }
+    }
+    for (unsigned long long i = n8 * 8 + threadIdx.x; i < tokens; i += kCountThreads) {
+        const uint32_t key = row[i];
+        bad |= key_nonfinite(key);
+        cnt += (!key_nan(key) && key >= thr_key) ? 1u : 0u;
+    }
+    cnt = __reduce_add_sync(0xffffffffu, cnt);
+    bad = __any_sync(0xffffffffu, bad);
+    if ((threadIdx.x & 31) == 0) {
+        if (cnt) atomicAdd(&scnt, cnt);
+        if (bad) atomicOr(&sbad, 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) records[blockIdx.x] = scnt | (sbad << 31);
 }
 
 // Heads (clusters of kCluster CTAs) the cluster path can hold resident at
@@ -1164,6 +1288,22 @@ int cluster_capacity(int device) {
 }  // namespace
 
 size_t select_header_bytes() { return sizeof(SelectHeader); }
+
+cudaError_t launch_shard_threshold(const uint32_t* h0, size_t batch, float alpha, uint32_t* thr,
+                                   cudaStream_t stream) {
+    return launch_dependent(shard_threshold_kernel, dim3((unsigned)batch), dim3(kShardThreads), 0, stream, false, h0,
+                            alpha, thr);
+}
+
+cudaError_t launch_shard_count(const uint16_t* keys, size_t heads, size_t tokens, size_t batch, const uint32_t* thr,
+                               uint32_t* records, cudaStream_t stream) {
+    return launch_dependent(shard_count_kernel, dim3((unsigned)(heads * batch)), dim3(kCountThreads), 0, stream, false,
+                            keys, (unsigned long long)tokens, (unsigned)heads, thr, records);
+}
+
+bool select_cluster_available(size_t valid) {
+    return valid <= kClusterKeysMax && cluster_capacity(device_info().ordinal) > 0;
+}
 
 size_t select_workspace_bytes(size_t heads, size_t valid, size_t kcap) {
     size_t bytes = (sizeof(SelectHeader) + 255) / 256 * 256;
@@ -1201,6 +1341,12 @@ cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream) {
     p.sortbuf = reinterpret_cast<unsigned long long*>(ws + off);
     p.h0 = s.h0;
     p.ga = s.ga;
+    p.ext = s.ext;
+    p.ext_thr = s.ext_thr;
+    p.head_base = s.head_base;
+    p.heads_total = s.ext ? s.heads_total : s.heads;
+    p.batch = s.batch ? s.batch : 1;
+    p.seq_scores = s.seq_scores;
     if (s.ga_done) *s.ga_done = 0;
     cudaError_t e = cudaSuccess;
     if (s.reset_header) {
@@ -1220,9 +1366,13 @@ cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream) {
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    if (s.valid <= kClusterKeysMax && s.heads <= (uint32_t)cluster_capacity(dev.ordinal)) {
+    const int capacity = cluster_capacity(dev.ordinal);  // also configures the cluster kernel
+    if (s.valid <= kClusterKeysMax && (s.ext || s.heads <= (uint32_t)capacity)) {
         const size_t cs = ((size_t)s.valid + kCluster - 1) / kCluster;
-        cfg.gridDim = dim3(s.heads * kCluster);
+        cfg.gridDim = dim3(p.batch * s.heads * kCluster);
+        // Shard steps (records from the exchange) have no grid barrier, so a
+        // batch of any size needs no co-residency: an ordinary cluster launch.
+        if (s.ext) cfg.numAttrs = 1, attr[0] = attr[1];
         cfg.blockDim = dim3(kCThreads);
         cfg.dynamicSmemBytes = ((cs + 7) / 8 * 8 * 2 + 15) / 16 * 16 + 2 * kSmemSortMax * 8;
         if (s.ga.out) cfg.dynamicSmemBytes = std::max(cfg.dynamicSmemBytes, kEpiSmemBytes);
@@ -1230,6 +1380,7 @@ cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream) {
         if (le == cudaSuccess && s.ga_done) *s.ga_done = s.ga.out != nullptr;
         return le;
     }
+    if (s.ext) return cudaErrorInvalidValue;  // shard steps need the cluster kernel
     p.ga = SelectEpilogue{};  // the one-CTA-per-head kernel has no epilogue
     const size_t keys_bytes = s.valid <= kSmemKeysMax ? ((size_t)s.valid * 2 + 15) / 16 * 16 : 0;
     static thread_local int configured_device = -1;

@@ -1,0 +1,166 @@
+"""KV-head-sharded selected-KV decode layer over several GPUs.
+
+A batch of independent sequences, each with Q [32,128] and K/V [N,8,128],
+runs one selected-KV layer with the 8 KV heads split evenly over the ranks of
+a process group: rank r holds KV heads [G r, G (r+1)) with G = 8 / world, i.e.
+query heads [4 G r, 4 G (r+1)), of every sequence, as token-major shards
+[N][G][128].  The reference couples all heads of a sequence twice
+(policy/gqa_policy.cpp:49-63): the threshold comes from query head 0 and k
+from the F16 mean of all 32 heads' F16 counts.  A shard step reproduces both
+exactly with small exchanges, and then all-gathers the attention outputs:
+
+    1. every rank scores its heads (the rank holding query head 0 also keeps
+       head-0 partials);
+    2. rank 0 derives each sequence's threshold record -> broadcast;
+    3. every rank counts its heads against it -> records all-gathered in head
+       order (every rank then folds the same 32 records into the same k);
+    4. every rank selects its heads' top-k, gathers their K/V rows into its
+       packed buffers and attends over them -> outputs all-gathered.
+
+The sum of F16-rounded integer counts is exact in FP32 in any order, so the
+folded k equals the unsharded selector's (policy/full_gqa_runtime.cpp:307-309
+makes the same argument).  Phases are methods so that a caller (or a test)
+can place the exchanges itself; step() places them with torch.distributed.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+from . import _capi
+
+HEADS, KV_HEADS, DIM = 32, 8, 128
+
+
+def _ptr(t) -> int:
+    return t.data_ptr()
+
+
+@dataclass
+class ShardGeometry:
+    world: int
+    rank: int
+
+    @property
+    def kv_heads(self) -> int:
+        return KV_HEADS // self.world
+
+    @property
+    def heads(self) -> int:
+        return 4 * self.kv_heads
+
+    @property
+    def head_base(self) -> int:
+        return self.heads * self.rank
+
+
+def slot_capacity(tokens: int, ratio: float) -> int:
+    from . import select_kmax
+
+    return max(32, (select_kmax(tokens, ratio) + 31) // 32 * 32)
+
+
+class KVHeadShardedLayer:
+    """One rank's part of a KV-head-sharded selected-KV layer for `batch`
+    sequences of `tokens` tokens.  Device buffers are allocated once."""
+
+    def __init__(self, tokens: int, batch: int, world: int, rank: int, alpha: float = 0.1, ratio: float = 0.2,
+                 device="cuda"):
+        import torch
+
+        if KV_HEADS % world:
+            raise ValueError("world size must divide the 8 KV heads")
+        self.torch = torch
+        self.geo = ShardGeometry(world, rank)
+        self.tokens, self.batch = tokens, batch
+        self.alpha, self.ratio = float(alpha), float(ratio)
+        self.count = slot_capacity(tokens, ratio)
+        h, dev = self.geo.heads, torch.device(device)
+        self.lib = _capi.lib()
+        u16 = torch.int16
+        self.scores = torch.empty((batch, h, tokens), dtype=u16, device=dev)
+        self.keys = torch.empty((batch, h, tokens), dtype=u16, device=dev)
+        self.head0 = torch.zeros((batch, self.lib.hsb_shard_head0_words()), dtype=torch.int32, device=dev)
+        self.thr = torch.zeros((batch, 2), dtype=torch.int32, device=dev)
+        self.records = torch.zeros((batch, h), dtype=torch.int32, device=dev)
+        self.records_all = torch.zeros((batch, HEADS), dtype=torch.int32, device=dev)
+        self.ids = torch.empty((batch, h, self.count), dtype=torch.int32, device=dev)
+        self.counts = torch.zeros((batch, h), dtype=torch.int32, device=dev)
+        self.results = torch.zeros((batch, 4), dtype=torch.int32, device=dev)
+        # The whole batch runs in each kernel: packed K/V per sequence.
+        self.k_packed = torch.empty((batch, self.count * h * DIM), dtype=u16, device=dev)
+        self.v_packed = torch.empty((batch, self.count * h * DIM), dtype=u16, device=dev)
+        self.out = torch.zeros((batch, h, DIM), dtype=torch.float32, device=dev)
+        ws = self.lib.hsb_shard_select_workspace_bytes(self.geo.kv_heads, tokens, self.count, batch)
+        self.workspace = torch.empty((ws + 255) // 256 * 256, dtype=torch.uint8, device=dev)
+
+    # ---------------------------------------------------------------- phases
+    def _check(self, rc: int, what: str):
+        if rc != 0:
+            from . import HsbError
+
+            raise HsbError(rc, f"{what}: {self.lib.hsb_last_error().decode()}")
+
+    def score(self, q16, kshard, stream: int):
+        """q16 [batch][heads][128] F16 bits, kshard [batch][tokens][G][128]; one launch."""
+        owner = self.geo.rank == 0
+        self._check(self.lib.hsb_shard_score(_ptr(q16), self.geo.kv_heads, _ptr(kshard), self.tokens, self.batch,
+                                             _ptr(self.scores), _ptr(self.keys),
+                                             _ptr(self.head0) if owner else None, stream), "shard score")
+
+    def threshold(self, stream: int):
+        """Rank 0 only: per-sequence {threshold key, status} records."""
+        self._check(self.lib.hsb_shard_threshold(_ptr(self.head0), self.batch, C.c_float(self.alpha),
+                                                 _ptr(self.thr), stream), "shard threshold")
+
+    def count_heads(self, stream: int):
+        self._check(self.lib.hsb_shard_count(_ptr(self.keys), self.geo.heads, self.tokens, self.batch,
+                                             _ptr(self.thr), _ptr(self.records), stream), "shard count")
+
+    def select(self, q32, kshard, vshard, stream: int):
+        """q32 [batch][heads][128] F32; uses self.thr and self.records_all."""
+        self._check(self.lib.hsb_shard_select(
+            _ptr(self.keys), _ptr(self.scores), self.geo.kv_heads, self.tokens, self.batch, _ptr(self.thr),
+            _ptr(self.records_all), HEADS, self.geo.head_base, C.c_float(self.alpha), C.c_float(self.ratio),
+            _ptr(self.ids), self.count, _ptr(self.counts), _ptr(self.results), _ptr(q32), _ptr(kshard),
+            _ptr(vshard), _ptr(self.k_packed), _ptr(self.v_packed), _ptr(self.out), _ptr(self.workspace),
+            self.workspace.numel(), stream), "shard select")
+
+    # ------------------------------------------------------------------ step
+    def step(self, q16, q32, kshard, vshard, group=None):
+        """The whole layer on this rank; returns the all-gathered outputs
+        [batch][32][128] and the combined selection records [batch][4]
+        (k, boundary-tied heads summed over ranks, status code, index)."""
+        import torch.distributed as dist
+
+        torch = self.torch
+        stream = torch.cuda.current_stream().cuda_stream if self.scores.is_cuda else 0
+        world = self.geo.world
+        self.score(q16, kshard, stream)
+        if self.geo.rank == 0:
+            self.threshold(stream)
+        dist.broadcast(self.thr, src=0, group=group)
+        self.count_heads(stream)
+        parts = [torch.empty_like(self.records) for _ in range(world)]
+        dist.all_gather(parts, self.records, group=group)
+        self.records_all.copy_(torch.cat(parts, dim=1))
+        self.select(q32, kshard, vshard, stream)
+        outs = [torch.empty_like(self.out) for _ in range(world)]
+        dist.all_gather(outs, self.out, group=group)
+        res = [torch.empty_like(self.results) for _ in range(world)]
+        dist.all_gather(res, self.results, group=group)
+        combined = res[0].clone()
+        combined[:, 1] = sum(r[:, 1] for r in res)
+        return torch.cat(outs, dim=1), combined
+
+
+def shard_rows(full, world: int, rank: int):
+    """[batch][tokens][8][128] -> this rank's contiguous [batch][tokens][G][128]."""
+    g = KV_HEADS // world
+    return full[:, :, g * rank:g * (rank + 1), :].contiguous()
+
+
+def shard_queries(full, world: int, rank: int):
+    """[batch][32][128] -> this rank's [batch][4G][128]."""
+    h = HEADS // world
+    return full[:, h * rank:h * (rank + 1), :].contiguous()

@@ -287,6 +287,47 @@ int hsb_layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_
                    float ratio, size_t count, const hsb_layer_buffers* buffers, float* d_out,
                    void* stream);
 
+/* ------------------------------------------------------- KV-head shards
+ * One selected-KV layer split across GPUs by KV head (each GPU holds
+ * kv_heads of the 8 KV heads, i.e. query heads [head_base, head_base +
+ * 4*kv_heads), of every sequence).  The reference couples heads through the
+ * head-0 threshold and the mean of all heads' counts (policy/gqa_policy.cpp:
+ * 49-63); a shard step reproduces that exactly with two tiny exchanges:
+ *   1. every shard: hsb_shard_score (the shard holding query head 0 also
+ *      writes head-0 partials);
+ *   2. that shard: hsb_shard_threshold -> {threshold key, status}, broadcast;
+ *   3. every shard: hsb_shard_count -> one record per local head
+ *      (count | non-finite << 31), all-gathered in head order;
+ *   4. every shard: hsb_shard_select -> the same k as the unsharded
+ *      selector, its heads' ordered IDs, packed K/V and attention output.
+ * Shard caches are token-major [tokens][kv_heads][128] F16. */
+size_t hsb_shard_head0_words(void);  /* head-0 partial words per sequence */
+/* A batch of `batch` sequences back to back: d_q [batch][4 kv_heads][128],
+ * d_kshard [batch][tokens][kv_heads][128], d_scores / d_order_keys
+ * [batch][4 kv_heads][tokens], d_head0 [batch][hsb_shard_head0_words()]
+ * (only on the shard holding query head 0, else NULL). */
+int hsb_shard_score(const uint16_t* d_q, int kv_heads, const uint16_t* d_kshard, size_t tokens,
+                    size_t batch, uint16_t* d_scores, uint16_t* d_order_keys, uint32_t* d_head0,
+                    void* stream);
+/* d_thr [batch][2]: {threshold order key, status}. */
+int hsb_shard_threshold(const uint32_t* d_head0, size_t batch, float alpha, uint32_t* d_thr,
+                        void* stream);
+/* d_records [batch][heads]: count | non-finite << 31 per local head. */
+int hsb_shard_count(const uint16_t* d_order_keys, size_t heads, size_t tokens, size_t batch,
+                    const uint32_t* d_thr, uint32_t* d_records, void* stream);
+size_t hsb_shard_select_workspace_bytes(int kv_heads, size_t tokens, size_t kcap, size_t batch);
+/* d_records: [batch][heads_total] from every shard, in head order.  Outputs
+ * per sequence: d_ids [4 kv_heads][kcap], d_counts [4 kv_heads], d_result,
+ * d_k_packed [kcap][4 kv_heads][128], d_v_packed [4 kv_heads][128][kcap],
+ * d_out [4 kv_heads][128]; d_q32 [batch][4 kv_heads][128], V as K. */
+int hsb_shard_select(const uint16_t* d_order_keys, const uint16_t* d_raw, int kv_heads, size_t tokens,
+                     size_t batch, const uint32_t* d_thr, const uint32_t* d_records,
+                     size_t heads_total, size_t head_base, float alpha, float ratio, uint32_t* d_ids,
+                     size_t kcap, uint32_t* d_counts, hsb_selection* d_result, const float* d_q32,
+                     const uint16_t* d_kshard, const uint16_t* d_vshard, uint16_t* d_k_packed,
+                     uint16_t* d_v_packed, float* d_out, void* d_workspace, size_t workspace_bytes,
+                     void* stream);
+
 /* ------------------------------------------------------ synthetic inputs
  * Benchmark inputs, not part of the reference interface: seeded F16 normal
  * values (counter-based hash + Box-Muller).  For K rows, a heavy_fraction of
