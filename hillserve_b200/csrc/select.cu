@@ -918,7 +918,8 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     const bool fused = p.ga.out != nullptr;
     if (sh.timeout) {
         // Cluster peers that passed the barrier may still read this CTA's
-        // shared memory: stay resident through their cluster barriers.
+        // shared memory: stay resident through as many cluster barriers as
+        // any of their paths takes (extra ones complete once they exit).
         for (int i = 0; i < (fused ? 4 : 2); ++i) cl.sync();
         return;
     }
@@ -929,6 +930,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
         return;
     }
 
+    uint32_t* out = p.ids + ((unsigned long long)seqb * p.heads + h) * p.kcap;
     // ---- 3. radix select over the cluster's histograms.  Thread t owns
     // coarse bins 1023 - 2t and 1022 - 2t (descending).
     const unsigned int bin0 = 1023u - 2u * tid, bin1 = bin0 - 1u;
@@ -1087,7 +1089,6 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
         }
     }
     cl.sync();  // survivors and tie witnesses are in the leader
-    uint32_t* out = p.ids + ((unsigned long long)seqb * p.heads + h) * p.kcap;
     if (r == 0) {
         // ---- leader: boundary tie (gqa_policy.cpp:66) and reference order
         unsigned long long* src = small ? bufA : sortbuf;
@@ -1357,22 +1358,24 @@ cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream) {
         e = cudaMemsetAsync(s.result, 0, sizeof(hsb_selection), stream);
         if (e != cudaSuccess) return e;
     }
-    cudaLaunchAttribute attr[2];
+    // Cooperative (the grid barrier needs every CTA resident).  Measured
+    // slower with programmatic stream serialization on this launch, so the
+    // selector starts only once the scorer has completed; it still lets its
+    // own dependents start early (pdl_trigger).
+    cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg{};
     cfg.stream = stream;
     cfg.attrs = attr;
-    cfg.numAttrs = 2;
+    cfg.numAttrs = 1;
     const int capacity = cluster_capacity(dev.ordinal);  // also configures the cluster kernel
     if (s.valid <= kClusterKeysMax && (s.ext || s.heads <= (uint32_t)capacity)) {
         const size_t cs = ((size_t)s.valid + kCluster - 1) / kCluster;
         cfg.gridDim = dim3(p.batch * s.heads * kCluster);
         // Shard steps (records from the exchange) have no grid barrier, so a
         // batch of any size needs no co-residency: an ordinary cluster launch.
-        if (s.ext) cfg.numAttrs = 1, attr[0] = attr[1];
+        if (s.ext) cfg.numAttrs = 0;
         cfg.blockDim = dim3(kCThreads);
         cfg.dynamicSmemBytes = ((cs + 7) / 8 * 8 * 2 + 15) / 16 * 16 + 2 * kSmemSortMax * 8;
         if (s.ga.out) cfg.dynamicSmemBytes = std::max(cfg.dynamicSmemBytes, kEpiSmemBytes);
