@@ -117,3 +117,51 @@ def test_layer_step_repeatable_in_graph(cuda, ob):
         g.replay()
     torch.cuda.synchronize()
     assert torch.equal(layer.out, first)
+
+
+@pytest.mark.parametrize("alpha", [5.0, 10.0])
+def test_rehearsal_prefetch_step(cuda, ob, alpha):
+    """configs[3] at N=4096: rehearsal query (x bf16, W_q bf16, RoPE at
+    position N) -> F16 Q -> score the HBM keys -> select -> physical union ->
+    stage the union's K|V rows from a pinned-host cold tier into HBM -> pack.
+    From the GPU's F16 query on (the producer itself is checked to tolerance
+    above), every stage is bit-exact against the oracle chain."""
+    import torch
+
+    n = 4096
+    torch.manual_seed(11)
+    x = torch.randn(4096, dtype=torch.float32).to(torch.bfloat16)
+    w = (torch.randn(4096, 4096, dtype=torch.float32) * 0.02).to(torch.bfloat16)
+    _, q16 = cuda.rehearsal_query(x.cuda(), w.cuda(), n, 500000.0)
+    q16h = host_u16(q16).reshape(-1)
+    _, k, _ = inputs.config1(n, seed=3)
+    v = inputs.values(3, n)
+    rows = inputs.interleave(k, v, n)  # [n][2048] F16 bits: K[8][128] then V[8][128]
+    cold = torch.from_numpy(rows.view(np.uint8).copy()).pin_memory()  # the pinned-host tier
+    raw = cuda.score_full_gqa(q16.reshape(-1), [(dev_u16(k), n, 1024)])
+    scaled = cuda.scale_scores(raw)
+    sel = cuda.select_gqa_scores(scaled, 32, n, n, alpha, 0.2)
+    torch.cuda.synchronize()
+    wraw = ob.score(q16h, k, n, 1024)
+    assert np.array_equal(host_u16(raw).reshape(-1), wraw.reshape(-1))
+    wids, _, wk, _ = ob.select(ob.scale(wraw), 32, n, n, alpha, 0.2)
+    assert sel.k == wk and wk > 0
+    assert np.array_equal(sel.ids.cpu().numpy().astype(np.uint64), wids)
+    sizes = torch.full((32,), sel.k, dtype=torch.int32, device="cuda")
+    physical = cuda.gqa_physical_union(sel.ids_buffer, sizes, n)
+    wphys = ob.union(wids, np.full(32, wk), n)
+    assert np.array_equal(physical.cpu().numpy().astype(np.uint64), wphys)
+    nphys = physical.numel()
+    staged = torch.zeros(nphys * 4096, dtype=torch.uint8, device="cuda")
+    cuda.stage_rows(cold.data_ptr(), physical, torch.tensor([nphys], dtype=torch.int32, device="cuda"), nphys, staged)
+    torch.cuda.synchronize()
+    assert np.array_equal(staged.cpu().numpy().reshape(nphys, 4096), rows.view(np.uint8).reshape(n, 4096)[wphys])
+    count = max(32, (cuda.select_kmax(n, 0.2) + 31) // 32 * 32)
+    kp = torch.empty(count * 4096, dtype=torch.int16, device="cuda")
+    vp = torch.empty_like(kp)
+    mask = torch.empty(32 * 64 * count, dtype=torch.float32, device="cuda")
+    cuda.pack_gqa_workspace(sel.ids_buffer, sizes, [n], physical, staged, count, kp, vp, mask)
+    payload = rows.view(np.uint8).reshape(n, 4096)[wphys].reshape(-1)
+    wkp, wvp, wmask = ob.pack(wids, np.full(32, wk), [n], wphys, payload, count)
+    assert np.array_equal(host_u16(kp), wkp) and np.array_equal(host_u16(vp), wvp)
+    assert np.array_equal(mask.cpu().numpy(), wmask)
