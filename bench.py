@@ -49,9 +49,10 @@ def parse():
     ap.add_argument("--tokens", type=int, default=N)
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "kv-sharded"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "kv-sharded", "sweep"],
                     help="decode: configs[1] (the headline); kv-sharded: configs[4], one selected-KV layer "
-                         "over --batch sequences with the KV heads split over the ranks")
+                         "over --batch sequences with the KV heads split over the ranks; sweep: configs[2], "
+                         "the selected-KV layer step per length N")
     ap.add_argument("--batch", type=int, default=64)
     return ap.parse_args()
 
@@ -610,6 +611,60 @@ def run_sharded(args, rank, world, torch, dist):
             "clocks": clocks.summary()}
 
 
+def run_sweep(args, torch):
+    """latency and HBM GB/s of one selected-KV layer step
+    (score -> select -> gather + attention) per length N, the configs[0]
+    generator with RoPE'd keys.  Each N cycles over enough layers of data
+    to exceed the L2 (at least 4; up to 256 MB of K+V per layer set)."""
+    import hillserve_b200 as hsb
+
+    lib = hsb._capi.lib()
+    s = torch.cuda.current_stream().cuda_stream
+    lines = []
+    for n in (64, 1024, 4096, 16384, 32768):
+        layers = max(4, min(64, (512 << 20) // (4096 * n)))
+        m = Model(hsb, torch, n, layers + DENSE, args.alpha, seed=1)
+        stream = torch.cuda.Stream()
+        g = torch.cuda.CUDAGraph()
+
+        def body():
+            for l in range(DENSE, DENSE + layers):
+                rc = lib.hsb_layer_step(m.q16[l].data_ptr(), m.q32[l].data_ptr(), m.kc[l].data_ptr(),
+                                        m.vc[l].data_ptr(), 1024, n, m.alpha, 0.2, m.count,
+                                        ctypes.byref(m.buffers[l]), m.out[l].data_ptr(), stream.cuda_stream)
+                assert rc == 0, lib.hsb_last_error()
+
+        with torch.cuda.stream(stream):
+            body()
+        stream.synchronize()
+        with torch.cuda.graph(g, stream=stream):
+            body()
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        reps = max(5, args.steps // 4)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            a.record(stream)
+            for _ in range(reps):
+                g.replay()
+            b.record(stream)
+        b.synchronize()
+        us = a.elapsed_time(b) * 1e3 / (reps * layers)
+        ks = m.results[DENSE:DENSE + layers, 0].float().mean().item()
+        unions = 4096 * ks * 32  # upper bound: every selected row distinct
+        b_ssg = 2048 * n + 8192 + 64 * n + 64 * n + 128 * ks + unions + 16384 * ks
+        lines.append({"tokens": n, "layer_step_us": round(us, 2), "k_mean": round(ks, 2),
+                      "ssg_bytes_upper": int(b_ssg), "GB_s": round(b_ssg / (us * 1e-6) / 1e9, 1),
+                      "layers_cycled": layers})
+        g.reset()
+        del m
+        torch.cuda.empty_cache()
+    s = None
+    return {"metric": "selected-KV layer step latency per length N (configs[2])", "impl": "ours",
+            "unit": "us per layer step", "alpha": args.alpha, "data": "synthetic", "sweep": lines}
+
+
 def main():
     args = parse()
     import torch
@@ -627,6 +682,8 @@ def main():
         dist = tdist
     if args.impl == "reference":
         line = run_reference(args, rank, world, torch)
+    elif args.workload == "sweep":
+        line = run_sweep(args, torch)
     elif args.workload == "kv-sharded":
         if dist is None:  # one GPU: a world of one, still through the process-group code
             import datetime
