@@ -563,6 +563,8 @@ struct ClusterShared {
     unsigned int maxkey, bad0, cnt, bad;
     unsigned int b_bin, b_above, b_eqtotal, total;
     unsigned int gt_before, eq_before;  // survivors of the cluster's earlier chunks
+    unsigned int c_hi;                  // keys of the whole head in the chosen coarse bin
+    unsigned int tie_key0, tie_key1;    // direct path, leader: keys at ranks k - 1 and k
     unsigned int last_id, next_id;      // leader: the need_eq-th and next tie of K*
     unsigned int status, status_index;
     unsigned long long k;
@@ -952,20 +954,112 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
         if (above < k && above + c0 >= k) {
             sh.b_bin = bin0;
             sh.b_above = above;
+            sh.c_hi = c0;
         } else if (above + c0 < k && above + c0 + c1 >= k) {
             sh.b_bin = bin1;
             sh.b_above = above + c0;
+            sh.c_hi = c1;
         }
     }
     __syncthreads();
     const unsigned int hi = sh.b_bin, above_hi = sh.b_above;
-    // Per-chunk counts above the chosen coarse bin (for the cluster prefix).
+    // Direct path: when the keys of bins >= hi fit the leader's buffer they
+    // are all candidates, and the leader orders them (no fine pass).
+    const bool direct = above_hi + sh.c_hi <= kSmemSortMax;
+    // Per-chunk counts of bins > hi (radix path) or >= hi (direct path):
+    // the cluster prefix of each chunk.
 #pragma unroll
     for (int q = 0; q < kCluster; ++q) {
-        unsigned int v = (bin0 > hi ? cq0[q] : 0u) + (bin1 > hi ? cq1[q] : 0u);
+        const unsigned int lo_bin = direct ? hi : hi + 1;
+        unsigned int v = (bin0 >= lo_bin ? cq0[q] : 0u) + (bin1 >= lo_bin ? cq1[q] : 0u);
         v = __reduce_add_sync(0xffffffffu, v);
         if (lane == 0) sh.red[warp][q] = v;
     }
+    if (direct) {
+        // ---- 3'. the candidates: every key of bins >= hi, in ID order
+        __syncthreads();
+        unsigned int before = 0;
+        for (unsigned int q = 0; q < r; ++q)
+            for (int w = 0; w < kCWarps; ++w) before += sh.red[w][q];
+        unsigned long long* dst = cl.map_shared_rank(bufA, 0);
+        const unsigned int per = ((m + kCThreads - 1) / kCThreads + 7) / 8 * 8;
+        const unsigned int j0 = min(m, tid * per), j1 = min(m, j0 + per);
+        unsigned int mine = 0;
+        for (unsigned int j = j0; j < j1; ++j) mine += (keys[j] >> 6) >= hi ? 1u : 0u;
+        unsigned int pos = before + block_exclusive_scan<kCThreads>(mine, sh.scan, &sh.total);
+        if (mine) {
+            for (unsigned int j = j0; j < j1; ++j) {
+                const unsigned int key = keys[j];
+                if ((key >> 6) >= hi && pos < kSmemSortMax)
+                    dst[pos++] = ((unsigned long long)key << 32) | (unsigned int)(b0 + j);
+            }
+        }
+        cl.sync();  // every chunk's candidates are in the leader
+        if (r == 0) {
+            // Stable order by key descending (ID ascending on ties) of the
+            // cand candidates; the first k are the selection.
+            const unsigned int cand = min(above_hi + sh.c_hi, kSmemSortMax);
+            unsigned long long* src = bufA;
+            if (cand <= kRankSortMax) {
+                if ((unsigned)tid < cand) {
+                    const unsigned long long e = src[tid];
+                    const unsigned int ek = (unsigned int)(e >> 32);
+                    unsigned int rk = 0;
+                    for (unsigned int j = 0; j < cand; ++j) {
+                        const unsigned int ok = (unsigned int)(src[j] >> 32);
+                        rk += (ok > ek) || (ok == ek && j < (unsigned)tid);
+                    }
+                    if (rk < k) out[rk] = (uint32_t)(e & 0xffffffffu);
+                    if (rk + 1 == k) {
+                        sh.last_id = (uint32_t)(e & 0xffffffffu);
+                        sh.tie_key0 = ek;
+                    }
+                    if (rk == k) {
+                        sh.next_id = (uint32_t)(e & 0xffffffffu);
+                        sh.tie_key1 = ek;
+                    }
+                }
+            } else {
+                sort_pass<kCThreads>(sh.hist, sh.scan, &sh.total, src, bufB, cand, 0);
+                sort_pass<kCThreads>(sh.hist, sh.scan, &sh.total, bufB, src, cand, 8);
+                for (unsigned int j = tid; j < k; j += kCThreads) out[j] = (uint32_t)(src[j] & 0xffffffffu);
+                if (tid == 0) {
+                    sh.last_id = (uint32_t)(src[k - 1] & 0xffffffffu);
+                    sh.tie_key0 = (uint32_t)(src[k - 1] >> 32);
+                    if (k < cand) {
+                        sh.next_id = (uint32_t)(src[k] & 0xffffffffu);
+                        sh.tie_key1 = (uint32_t)(src[k] >> 32);
+                    }
+                }
+            }
+            __syncthreads();
+            // Boundary tie (gqa_policy.cpp:66): only a (k+1)-th candidate with
+            // the k-th key can tie (keys of lower bins are smaller); equal
+            // keys are equal bits except +0 / -0, told apart from the scores.
+            if (!p.cover && tid == 0 && k < n && k < cand && sh.last_id < n && sh.next_id < n &&
+                sh.tie_key0 == sh.tie_key1) {
+                bool tied = true;
+                if (sh.tie_key0 == 0x8000u) {
+                    const unsigned long long base = (unsigned long long)h * p.stride;
+                    uint16_t a, b;
+                    if (p.mode == kInputKeys) {
+                        const uint16_t* raw = p.tie_raw ? p.tie_raw + seqb * p.seq_scores : nullptr;
+                        a = raw ? scale_half(raw[base + sh.last_id]) : 0;
+                        b = raw ? scale_half(raw[base + sh.next_id]) : 0;
+                    } else {
+                        a = scores[base + sh.last_id];
+                        b = scores[base + sh.next_id];
+                        if (p.mode == kInputRaw) {
+                            a = scale_half(a);
+                            b = scale_half(b);
+                        }
+                    }
+                    tied = a == b;
+                }
+                if (tied) atomicAdd(&result->boundary_tied_heads, 1u);
+            }
+        }
+    } else {
     for (unsigned int i = tid; i < m; i += kCThreads) {
         const unsigned int key = keys[i];
         if ((key >> 6) == hi) atomicAdd(&sh.fine[key & 63u], 1u);
@@ -1131,6 +1225,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
             for (unsigned int j = tid; j < k; j += kCThreads) out[j] = (uint32_t)(src[j] & 0xffffffffu);
         }
     }
+    }  // radix path
     if (!fused) return;
 
     // ---- epilogue: gather the head's selected rows and attend over them
