@@ -1229,7 +1229,6 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     if (!fused) return;
 
     // ---- epilogue: gather the head's selected rows and attend over them
-    cl.sync();  // the ordered ids are written (cluster-scope release / acquire)
     EpiSmem& es = *reinterpret_cast<EpiSmem*>(dyn);  // keys and sort buffers are no longer needed
     const int grp = tid / kEpiThreads, gtid = tid % kEpiThreads;
     // This sequence's view of the epilogue's buffers.
@@ -1240,6 +1239,21 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     ga.vcache += (size_t)seqb * p.valid * ga.stride_words;
     ga.kp += (size_t)seqb * ga.count * ga.heads * kDim;
     ga.vp += (size_t)seqb * ga.count * ga.heads * kDim;
+    if (k <= 32) {
+        // One tile: the leader, which has just written the ordered ids,
+        // gathers and attends alone; its peers are done.
+        if (r != 0) return;
+        __syncthreads();  // the sort's reads of the candidate buffers are over
+        if (tid < kDim) es.q[tid >> 5][tid & 31] = __ldg(ga.q + h * kDim + tid);
+        __syncthreads();  // the ids (written by this CTA) and q are in place
+        if (grp == 0) {
+            float M = -INFINITY, L = 0.0f, acc = 0.0f;
+            epilogue_tile(ga, out, (int)h, 0u, (int)k, &es.q[0][0], es.g[0], gtid, 1, M, L, acc);
+            ga.out[h * kDim + gtid] = L > 0.0f ? acc / L : 0.0f;
+        }
+        return;
+    }
+    cl.sync();  // the ordered ids are written (cluster-scope release / acquire)
     if (tid < kDim) es.q[tid >> 5][tid & 31] = __ldg(ga.q + h * kDim + tid);
     __syncthreads();
     float M = -INFINITY, L = 0.0f, acc = 0.0f;
