@@ -816,31 +816,33 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     // The coarse histograms are complete: release them to the cluster now,
     // acquire after the grid barrier.
     cluster_arrive_release();
-    if (tid == 0 && ext) sh.timeout = 0;  // counts come from the exchange: no barrier
-    if (tid == 0 && !ext) {
-        if (sh.cnt) atomicAdd(&p.header->cnt[h], sh.cnt);
-        if (!p.cover && sh.bad) atomicOr(&p.header->err[h], 1u);
-        // ---- 2. grid barrier (bounded): a release-ordered arrival (orders
-        // this CTA's count atomics before it) and acquire-load polling.
-        red_add_release(&p.header->arrived, 1u);
-        const unsigned long long start = global_ns();
-        sh.timeout = 0;
-        while (ld_acquire(&p.header->arrived) < gridDim.x) {
-            if (global_ns() - start > kWaitLimitNs) {
-                sh.timeout = 1;
-                break;
+    if (warp == 0) {
+        // ---- 2. grid barrier (bounded): lane 0 adds this CTA's count, makes a
+        // release-ordered arrival and polls with acquire loads; the warp then
+        // reads every head's record at once (__syncwarp orders its lanes after
+        // lane 0's acquire).
+        int timeout = 0;
+        if (!ext && lane == 0) {
+            if (sh.cnt) atomicAdd(&p.header->cnt[h], sh.cnt);
+            if (!p.cover && sh.bad) atomicOr(&p.header->err[h], 1u);
+            red_add_release(&p.header->arrived, 1u);
+            const unsigned long long start = global_ns();
+            while (ld_acquire(&p.header->arrived) < gridDim.x) {
+                if (global_ns() - start > kWaitLimitNs) {
+                    timeout = 1;
+                    break;
+                }
             }
         }
-    }
-    __syncthreads();
-    cluster_wait_acquire();
-    if (warp == 0) {
+        timeout = __shfl_sync(0xffffffffu, timeout, 0);
+        __syncwarp();
+        if (lane == 0) sh.timeout = timeout;
         // Per-head counts (4 heads per lane), F16 rounding, fold in head order.
         unsigned int e[4] = {0, 0, 0, 0};
         float rr[4] = {0.f, 0.f, 0.f, 0.f};
         unsigned long long own = 0;
         const uint32_t nh = ext ? p.heads_total : p.heads, own_head = ext ? p.head_base + h : h;
-        if (!sh.timeout) {
+        if (!timeout) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const uint32_t hh = lane * 4 + j;
@@ -864,7 +866,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
             }
         }
         own = __reduce_max_sync(0xffffffffu, (unsigned int)own);
-        if (r == 0 && lane == 0 && p.counts && !sh.timeout) p.counts[seqb * p.heads + h] = (uint32_t)own;
+        if (r == 0 && lane == 0 && p.counts && !timeout) p.counts[seqb * p.heads + h] = (uint32_t)own;
         // First failing head in head order (non-finite before count overflow
         // within a head), found by ballot.  The rounded counts are integers
         // below 2^16 and there are at most 128 of them, so every partial sum
@@ -889,7 +891,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
         unsigned long long k = 0;
-        if (!sh.timeout && !status) {
+        if (!timeout && !status) {
             const float mean = p.fp32_counts ? __fdiv_rn(total, (float)nh)
                                              : half_value(half_bits(__fdiv_rn(total, (float)nh)));
             if (p.cover) {
@@ -904,7 +906,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
                 }
             }
         }
-        if (sh.timeout) status = HSB_E_TIMEOUT;
+        if (timeout) status = HSB_E_TIMEOUT;
         if (!status && k == 0 && p.zero_is_error) status = HSB_E_ZERO_SELECTION;
         if (lane == 0) {
             sh.status = status;
@@ -912,11 +914,12 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
             sh.k = status ? 0 : k;
             // *result starts zeroed (the launcher clears it).
             if (seq_first) result->k = status ? 0u : (uint32_t)k;
-            if (sh.timeout) raise_status(&result->status, HSB_E_TIMEOUT, (int)blockIdx.x);
+            if (timeout) raise_status(&result->status, HSB_E_TIMEOUT, (int)blockIdx.x);
             else if (seq_first && status) raise_status(&result->status, (int)status, (int)index);
         }
     }
     __syncthreads();
+    cluster_wait_acquire();  // every chunk's coarse histogram is visible (arrived before the barrier)
     const bool fused = p.ga.out != nullptr;
     if (sh.timeout) {
         // Cluster peers that passed the barrier may still read this CTA's
@@ -985,7 +988,23 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
         const unsigned int per = ((m + kCThreads - 1) / kCThreads + 7) / 8 * 8;
         const unsigned int j0 = min(m, tid * per), j1 = min(m, j0 + per);
         unsigned int mine = 0;
-        for (unsigned int j = j0; j < j1; ++j) mine += (keys[j] >> 6) >= hi ? 1u : 0u;
+        for (unsigned int j = j0; j < j1; j += 8) {  // 16-byte loads: no bank conflicts
+            uint32_t w[4];
+            if (j + 8 <= j1) {
+                const uint4 v = *reinterpret_cast<const uint4*>(keys + j);
+                w[0] = v.x;
+                w[1] = v.y;
+                w[2] = v.z;
+                w[3] = v.w;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    w[e] = (j + 2 * e < j1 ? keys[j + 2 * e] : 0u) | ((j + 2 * e + 1 < j1 ? keys[j + 2 * e + 1] : 0u) << 16);
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+                mine += (j + e < j1 && ((w[e >> 1] >> (16 * (e & 1))) & 0xffffu) >> 6 >= hi) ? 1u : 0u;
+        }
         unsigned int pos = before + block_exclusive_scan<kCThreads>(mine, sh.scan, &sh.total);
         if (mine) {
             for (unsigned int j = j0; j < j1; ++j) {
