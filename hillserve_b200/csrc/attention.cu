@@ -322,7 +322,8 @@ constexpr int kDTSlots = 6;
 constexpr int kDTConsumers = kKvHeads;
 constexpr int kDTThreads = (kDTConsumers + 1) * 32;
 constexpr int kDTQBytes = kKvHeads * kDim * kGroup * 4;  // F32 [kv][c][4 heads]
-constexpr int kDTSmem = 1024 + kDTSlots * kDTBox + kDTQBytes + 2 * kDTSlots * 8;
+constexpr int kDTPBytes = kDTConsumers * 32 * 16;  // per warp: the tile's weights, float4 [token][4 heads]
+constexpr int kDTSmem = 1024 + kDTSlots * kDTBox + kDTQBytes + kDTPBytes + 2 * kDTSlots * 8;
 constexpr int kDenseMaxCtas = 256;
 
 struct DenseTmaParams {
@@ -341,7 +342,8 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
     unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     unsigned char* slots = smem;
     float4* qs = reinterpret_cast<float4*>(smem + kDTSlots * kDTBox);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDTSlots * kDTBox + kDTQBytes);
+    float4* pw = reinterpret_cast<float4*>(smem + kDTSlots * kDTBox + kDTQBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDTSlots * kDTBox + kDTQBytes + kDTPBytes);
     uint64_t* empty = full + kDTSlots;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < kHeads * kDim; i += blockDim.x) {
@@ -438,6 +440,9 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
             for (int j = 0; j < 4; ++j) o[g][j] *= f;
             M[g] = mn;
         }
+        // The tile's weights, one float4 per token: P.V reads them by broadcast.
+        pw[kh * 32 + lane] = make_float4(pr[0], pr[1], pr[2], pr[3]);
+        __syncwarp();
         for (int half = 0; half < 2; ++half, ++it) {
             const uint32_t s = it % kDTSlots;
             if (!mbar_wait(&full[s], (it / kDTSlots) & 1)) {
@@ -445,15 +450,17 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
                 return;
             }
             const unsigned char* base = slots + s * kDTBox + kh * 32 * 128 + (lane & 3) * 4;
+            const float4* pt = pw + kh * 32;
 #pragma unroll 8
             for (int t = 0; t < 32; ++t) {
                 const uint32_t w = *reinterpret_cast<const uint32_t*>(base + t * 128 + (((lane >> 2) ^ (t & 7)) << 4));
                 const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+                const float4 p4 = pt[t];
+                const float pg[kGroup] = {p4.x, p4.y, p4.z, p4.w};
 #pragma unroll
                 for (int g = 0; g < kGroup; ++g) {
-                    const float pg = __shfl_sync(0xffffffffu, pr[g], t);
-                    o[g][2 * half] = fmaf(pg, f.x, o[g][2 * half]);
-                    o[g][2 * half + 1] = fmaf(pg, f.y, o[g][2 * half + 1]);
+                    o[g][2 * half] = fmaf(pg[g], f.x, o[g][2 * half]);
+                    o[g][2 * half + 1] = fmaf(pg[g], f.y, o[g][2 * half + 1]);
                 }
             }
             __syncwarp();
