@@ -91,6 +91,9 @@ class KVHeadShardedLayer:
         self.k_packed = torch.empty((batch, self.count * h * DIM), dtype=u16, device=dev)
         self.v_packed = torch.empty((batch, self.count * h * DIM), dtype=u16, device=dev)
         self.out = torch.zeros((batch, h, DIM), dtype=torch.float32, device=dev)
+        # Outputs and the selection record of each sequence travel together:
+        # [batch][heads * 128 + 4] (the record's int32 words bit-cast).
+        self.outbox = torch.zeros((batch, h * DIM + 4), dtype=torch.float32, device=dev)
         ws = self.lib.hsb_shard_select_workspace_bytes(self.geo.kv_heads, tokens, self.count, batch)
         self.workspace = torch.empty((ws + 255) // 256 * 256, dtype=torch.uint8, device=dev)
 
@@ -145,13 +148,16 @@ class KVHeadShardedLayer:
         dist.all_gather(parts, self.records, group=group)
         self.records_all.copy_(torch.cat(parts, dim=1))
         self.select(q32, kshard, vshard, stream)
-        outs = [torch.empty_like(self.out) for _ in range(world)]
-        dist.all_gather(outs, self.out, group=group)
-        res = [torch.empty_like(self.results) for _ in range(world)]
-        dist.all_gather(res, self.results, group=group)
+        h = self.geo.heads
+        self.outbox[:, :h * DIM].copy_(self.out.view(self.batch, h * DIM))
+        self.outbox[:, h * DIM:].copy_(self.results.view(torch.float32))
+        boxes = [torch.empty_like(self.outbox) for _ in range(world)]
+        dist.all_gather(boxes, self.outbox, group=group)
+        out = torch.cat([bx[:, :h * DIM].view(self.batch, h, DIM) for bx in boxes], dim=1)
+        res = [bx[:, h * DIM:].contiguous().view(torch.int32) for bx in boxes]
         combined = res[0].clone()
         combined[:, 1] = sum(r[:, 1] for r in res)
-        return torch.cat(outs, dim=1), combined
+        return out, combined
 
 
 def shard_rows(full, world: int, rank: int):
