@@ -49,11 +49,14 @@ def parse():
     ap.add_argument("--tokens", type=int, default=N)
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "kv-sharded", "sweep"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "kv-sharded", "sweep", "h2o"],
                     help="decode: configs[1] (the headline); kv-sharded: configs[4], one selected-KV layer "
                          "over --batch sequences with the KV heads split over the ranks; sweep: configs[2], "
-                         "the selected-KV layer step per length N")
+                         "the selected-KV layer step per length N; h2o: the H2O group-sum reduction "
+                         "(decode and prefill-block shapes) beside the reference's CUDA kernel")
     ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--h2o-keys", type=int, default=32768, help="h2o workload: keys N")
+    ap.add_argument("--h2o-queries", default="1,16,512", help="h2o workload: comma-separated query counts")
     return ap.parse_args()
 
 
@@ -665,6 +668,169 @@ def run_sweep(args, torch):
             "unit": "us per layer step", "alpha": args.alpha, "data": "synthetic", "sweep": lines}
 
 
+def run_h2o(args, torch):
+    """H2O group sums (runtime/gqa_h2o_stats.cu:41-57) at N = 32768 keys for a
+    decode query (Q = 1), a 16-query block and a 512-query prefill block of
+    the 32 x Q x N F32 softmax tensor (ggml layout, key-contiguous).  Each
+    shape cycles over enough distinct tensors to exceed the L2.  Per shape:
+    our kernel's device time per launch (a CUDA graph of C-ABI calls), the
+    reference's own CUDA reduction (oracle/_ref/libhs_ref_h2o.so, compiled
+    from its sources for sm_100a) timed by its own events, both reduce() calls
+    end to end (kernel + D2H of the sums + wait, wall clock; ours through the
+    C++ drop-in class), and the CPU restatement on one host core."""
+    import hillserve_b200 as hsb
+    from oracle import binding as ob
+
+    lib = hsb._capi.lib()
+    compat = ctypes.CDLL(str(ROOT / "hillserve_b200" / "_lib" / "libhsb_compat.so"))
+    compat.hsb_compat_h2o_create.restype = ctypes.c_void_p
+    compat.hsb_compat_h2o_create.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_size_t]
+    compat.hsb_compat_h2o_destroy.argtypes = [ctypes.c_void_p]
+    compat.hsb_compat_h2o_reduce.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                             ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p,
+                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]
+    peak, peak_kind = peaks()
+    ref_so = ROOT / "oracle" / "_ref" / "libhs_ref_h2o.so"
+    ref = None
+    if ref_so.exists():
+        ref = ctypes.CDLL(str(ref_so))
+        ref.refh2o_create.restype = ctypes.c_void_p
+        ref.refh2o_create.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_size_t]
+        ref.refh2o_destroy.argtypes = [ctypes.c_void_p]
+        ref.refh2o_reduce.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                      ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p,
+                                      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]
+    keys = args.h2o_keys
+    stream = torch.cuda.Stream()
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    shapes = []
+    launches = 0
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        for queries in [int(x) for x in args.h2o_queries.split(",")]:
+            elems = 32 * queries * keys
+            nbufs = max(1, min(64, (512 << 20) // (4 * elems)))
+            bufs = []
+            for _ in range(nbufs):
+                logits = torch.randn((32, queries, keys), generator=gen, device="cuda") * 3.0
+                bufs.append(torch.softmax(logits, dim=2))
+                del logits
+            ne = (ctypes.c_int64 * 4)(keys, queries, 32, 1)
+            nb = (ctypes.c_size_t * 4)(4, 4 * keys, 4 * keys * queries, 4 * elems)
+            out = torch.empty(8 * keys, dtype=torch.float32, device="cuda")
+
+            order = bufs * max(1, -(-8 // nbufs))  # at least 8 launches per graph replay
+
+            def body():
+                for b in order:
+                    rc = lib.hsb_h2o_group_sums(b.data_ptr(), ne, nb, keys, queries, out.data_ptr(), keys, None,
+                                                stream.cuda_stream)
+                    assert rc == 0, lib.hsb_last_error()
+
+            with torch.cuda.stream(stream):
+                body()
+            stream.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                body()
+            for _ in range(max(3, args.warmup)):
+                g.replay()
+            torch.cuda.synchronize()
+            reps = max(3, min(200, (8 << 30) // (4 * elems * len(order))))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                e0.record(stream)
+                for _ in range(reps):
+                    g.replay()
+                e1.record(stream)
+            e1.synchronize()
+            launches += reps * len(order)
+            ours_us = e0.elapsed_time(e1) * 1e3 / (reps * len(order))
+            alg = 4 * elems + 4 * 8 * keys
+            row = {"keys": keys, "queries": queries, "tensors_cycled": nbufs, "bytes_per_launch": alg,
+                   "ours_kernel_us": round(ours_us, 2), "ours_GB_s": round(alg / (ours_us * 1e-6) / 1e9, 1)}
+            row["ours_frac_of_" + peak_kind] = round(alg / (ours_us * 1e-6) / 1e9 / peak, 3)
+            # reduce() end to end (kernel, D2H of the 8 x N sums, wait) through
+            # the C++ drop-in class, called like the reference's below
+            err = ctypes.create_string_buffer(512)
+            red = compat.hsb_compat_h2o_create(bufs[0].data_ptr(), keys, err, 512)
+            assert red, err.value
+            sums_p = ctypes.POINTER(ctypes.c_float)()
+            cms, cdm = ctypes.c_double(), ctypes.c_double()
+
+            def ours_call(b):
+                rc = compat.hsb_compat_h2o_reduce(red, b.data_ptr(), ne, nb, keys, queries, stream.cuda_stream,
+                                                  ctypes.byref(sums_p), ctypes.byref(cms), ctypes.byref(cdm), err,
+                                                  512)
+                assert rc == 0, err.value
+                return cms.value
+
+            calls = max(5, min(50, reps * len(order)))
+            for b in bufs[:2]:
+                ours_call(b)
+            t0 = time.perf_counter()
+            ks = [ours_call(bufs[i % nbufs]) for i in range(calls)]
+            row["ours_reduce_wall_us"] = round((time.perf_counter() - t0) * 1e6 / calls, 2)
+            row["ours_reduce_event_kernel_us"] = round(float(np.median(ks)) * 1e3, 2)
+            launches += calls + 2
+
+            def ours_sums(b):
+                ours_call(b)
+                return np.ctypeslib.as_array(sums_p, shape=(8 * keys,)).copy()
+
+            if ref is not None:
+                err = ctypes.create_string_buffer(512)
+                h = ref.refh2o_create(bufs[0].data_ptr(), keys, err, 512)
+                assert h, err.value
+                rms, dms = ctypes.c_double(), ctypes.c_double()
+                sums = np.empty(8 * keys, dtype=np.float32)
+
+                def ref_call(b, dst=None):
+                    rc = ref.refh2o_reduce(h, b.data_ptr(), ne, nb, keys, queries, stream.cuda_stream,
+                                           None if dst is None else dst.ctypes.data, ctypes.byref(rms),
+                                           ctypes.byref(dms), err, 512)
+                    assert rc == 0, err.value
+                    return rms.value
+
+                for b in bufs[:2]:
+                    ref_call(b)
+                t0 = time.perf_counter()
+                rk = [ref_call(bufs[i % nbufs]) for i in range(calls)]
+                row["ref_reduce_wall_us"] = round((time.perf_counter() - t0) * 1e6 / calls, 2)
+                row["ref_kernel_us"] = round(float(np.median(rk)) * 1e3, 2)
+                row["ref_GB_s"] = round(alg / (row["ref_kernel_us"] * 1e-6) / 1e9, 1)
+                row["kernel_speedup_vs_ref"] = round(row["ref_kernel_us"] / ours_us, 2)
+                row["reduce_speedup_vs_ref"] = round(row["ref_reduce_wall_us"] / row["ours_reduce_wall_us"], 2)
+                # identical sums from both implementations on the same tensor
+                ref_call(bufs[0], sums)
+                row["bitwise_equal_to_ref"] = bool(np.array_equal(ours_sums(bufs[0]).view(np.uint32),
+                                                                  sums.view(np.uint32)))
+                ref.refh2o_destroy(h)
+            # the CPU restatement on one core, on the first tensor of the shape
+            if not args.no_cpu_baseline:
+                host = bufs[0].cpu().numpy()
+                gpu0 = ours_sums(bufs[0])
+                t0 = time.perf_counter()
+                cpu = ob.h2o_group_sums(host, keys, queries, 4, 4 * keys, 4 * keys * queries)
+                row["cpu_port_us"] = round((time.perf_counter() - t0) * 1e6, 1)
+                row["cpu_port_cores"] = 1
+                row["bitwise_equal_to_cpu_port"] = bool(np.array_equal(cpu.reshape(-1).view(np.uint32),
+                                                                       gpu0.view(np.uint32)))
+            shapes.append(row)
+            compat.hsb_compat_h2o_destroy(red)
+            g.reset()
+            del bufs, out, order
+            torch.cuda.empty_cache()
+    big = shapes[-1]
+    line = {"metric": "H2O group-sum reduction HBM throughput", "impl": "ours", "workload": "h2o",
+            "unit": "GB/s", "value": big["ours_GB_s"], "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"H2O group sums, 32 Q heads / 8 KV heads, N={keys}, Q in {{{args.h2o_queries}}}",
+                       "l2": "inputs cycled past the 126 MB L2"},
+            "roofline": {"bound": "hbm", "achieved": big["ours_GB_s"], "peak": peak, "unit": "GB/s",
+                         "frac": round(big["ours_GB_s"] / peak, 3), "peak_kind": peak_kind},
+            "gpu_launches": launches, "shapes": shapes, "clocks": clocks.summary()}
+    return line
+
+
 def main():
     args = parse()
     import torch
@@ -684,6 +850,8 @@ def main():
         line = run_reference(args, rank, world, torch)
     elif args.workload == "sweep":
         line = run_sweep(args, torch)
+    elif args.workload == "h2o":
+        line = run_h2o(args, torch)
     elif args.workload == "kv-sharded":
         if dist is None:  # one GPU: a world of one, still through the process-group code
             import datetime

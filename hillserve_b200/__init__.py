@@ -34,7 +34,7 @@ __all__ = [
     "scale_scores", "GQASelection", "select_gqa_scores", "prefetch_cover", "gqa_physical_union",
     "pack_gqa_workspace", "gather_map", "gather_cache", "stage_rows", "attention_packed",
     "attention_dense", "rehearsal_query", "GQAPrefetchCuda", "GQADeliveryWorkspace",
-    "SelectedKVLayer", "attention_slots",
+    "SelectedKVLayer", "attention_slots", "h2o_group_sums", "GQAH2OStatsCuda",
 ]
 
 # Status codes the reference reports as std::invalid_argument.
@@ -329,6 +329,97 @@ def attention_slots(position: int, ratio: float = 0.2) -> int:
     """Reference delivery slot count max(32, roundup32(floor(0.2*(pos+1))))
     (runtime/gqa_executor.cpp:145)."""
     return max(32, (int(math.floor((position + 1) * ratio)) + 31) // 32 * 32)
+
+
+# ------------------------------------------------------- H2O statistics
+def _h2o_args(ne, nb):
+    ne_arr = (C.c_int64 * 4)(*[int(x) for x in ne])
+    nb_arr = (C.c_size_t * 4)(*[int(x) for x in nb])
+    return ne_arr, nb_arr
+
+
+def h2o_group_sums(probabilities, ne, byte_strides, valid_keys: int, valid_queries: int, out=None,
+                   stream=None):
+    """Device-resident H2O group sums (runtime/gqa_h2o_stats.cu:41-57):
+    F32 [8, valid_keys] on the probabilities' device, enqueued on `stream`.
+    `probabilities` is a CUDA tensor (its storage holds the F32 softmax with
+    ggml byte strides) or a raw device address (int)."""
+    torch = _torch()
+    dev = probabilities.device if hasattr(probabilities, "device") else torch.device("cuda")
+    if out is None:
+        out = torch.empty((8, max(int(valid_keys), 1)), dtype=torch.float32, device=dev)
+    ptr = C.c_void_p(probabilities.data_ptr() if hasattr(probabilities, "data_ptr") else int(probabilities))
+    ne_arr, nb_arr = _h2o_args(ne, byte_strides)
+    cap = out.numel() // 8
+    _raise(lib().hsb_h2o_group_sums(ptr, ne_arr, nb_arr, int(valid_keys), int(valid_queries), _ptr(out), cap, None,
+                                    _stream(stream)))
+    return out
+
+
+@dataclass
+class H2OResult:
+    """GQAH2OStatsCuda::Result (runtime/gqa_h2o_stats.hpp:16-25); `sums` is
+    [8 * valid_keys] F32 in pinned host memory, borrowed until the next
+    reduce()."""
+    sums: object = None
+    elements: int = 0
+    started_ns: int = 0
+    ready_observed_ns: int = 0
+    d2h_bytes: int = 0
+    reduction_ms: float = 0.0
+    d2h_ms: float = 0.0
+
+
+class GQAH2OStatsCuda:
+    """runtime/gqa_h2o_stats.hpp:12-45 on B200: 8 x capacity_keys F32 on the
+    device and in pinned host memory; reduce() runs the group-sum kernel on
+    the caller's attention stream, copies the sums to the host and waits for
+    them, timing both with events."""
+
+    def __init__(self, actual_gpu_tensor, capacity_keys: int):
+        torch = _torch()
+        if actual_gpu_tensor is None or not capacity_keys:
+            raise HsbError(80, "H2O statistics needs CUDA pointer and nonzero capacity")
+        if not getattr(actual_gpu_tensor, "is_cuda", False):
+            raise HsbError(80, "H2O attention statistics requires CUDA device memory")
+        self.device = actual_gpu_tensor.device
+        self.capacity = int(capacity_keys)
+        self._gpu = torch.empty(8 * self.capacity, dtype=torch.float32, device=self.device)
+        self._host = torch.empty(8 * self.capacity, dtype=torch.float32, pin_memory=True)
+        self._events = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+
+    def gpu_bytes(self) -> int:
+        return 8 * self.capacity * 4
+
+    def host_bytes(self) -> int:
+        return 8 * self.capacity * 4
+
+    def reduce(self, probabilities, ne, byte_strides, valid_keys: int, valid_queries: int, stream) -> H2OResult:
+        import time
+
+        torch = _torch()
+        if stream is None:
+            raise HsbError(80, "H2O reduction invalid pointer, actual CUDA stream or capacity")
+        if probabilities.device != self.device:
+            raise HsbError(80, "H2O softmax tensor is not on the expected CUDA device")
+        keys = int(valid_keys)
+        out = H2OResult(elements=8 * keys, d2h_bytes=8 * keys * 4, started_ns=time.monotonic_ns())
+        begin, reduced, copied = self._events
+        ptr = C.c_void_p(probabilities.data_ptr())
+        ne_arr, nb_arr = _h2o_args(ne, byte_strides)
+        with torch.cuda.stream(stream):
+            begin.record(stream)
+            _raise(lib().hsb_h2o_group_sums(ptr, ne_arr, nb_arr, keys, int(valid_queries), _ptr(self._gpu),
+                                            self.capacity, None, _stream(stream)))
+            reduced.record(stream)
+            self._host[:8 * keys].copy_(self._gpu[:8 * keys], non_blocking=True)
+            copied.record(stream)
+        copied.synchronize()
+        out.ready_observed_ns = time.monotonic_ns()
+        out.reduction_ms = begin.elapsed_time(reduced)
+        out.d2h_ms = reduced.elapsed_time(copied)
+        out.sums = self._host[:8 * keys].numpy()
+        return out
 
 
 # ------------------------------------------------------------ delivery

@@ -75,6 +75,7 @@ _SIGNATURES = {
     "hsb_shard_count": (I, [P, SZ, SZ, SZ, P, P, P]),
     "hsb_shard_select_workspace_bytes": (SZ, [I, SZ, SZ, SZ]),
     "hsb_shard_select": (I, [P, P, I, SZ, SZ, P, P, SZ, SZ, F, F, P, SZ, P, P, P, P, P, P, P, P, P, SZ, P]),
+    "hsb_h2o_group_sums": (I, [P, P, P, SZ, SZ, P, SZ, P, P]),
     "hsb_synth_normal_f16": (I, [P, SZ, U64, F, P]),
     "hsb_synth_normal_bf16": (I, [P, SZ, U64, F, P]),
     "hsb_synth_keys": (I, [P, SZ, SZ, U64, F, F, I, F, P]),

@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <array>
 #include <cfenv>
 #include <chrono>
 #include <cmath>
@@ -18,10 +19,12 @@
 #include <string>
 
 #include "hsb.h"
+#include "hsb_compat.h"
 #include "policy/full_gqa_cpu.hpp"
 #include "policy/gqa_policy.hpp"
 #include "policy/host_policy.hpp"
 #include "runtime/gqa_delivery.hpp"
+#include "runtime/gqa_h2o_stats.hpp"
 #include "runtime/gqa_pack.hpp"
 #include "runtime/gqa_prefetch_cuda.hpp"
 
@@ -611,4 +614,151 @@ std::string GQADeliveryWorkspace::verify_and_consume() {
     return buf;
 }
 
+// ------------------------------------------------------- H2O statistics
+// runtime/gqa_h2o_stats.cu:60-173 over hsb_h2o_group_sums.
+struct GQAH2OStatsCuda::Impl {
+    int device = 0;
+    std::size_t keys = 0, bytes = 0;
+    float* gpu = nullptr;
+    float* host = nullptr;
+    cudaEvent_t begin = nullptr, reduced = nullptr, copied = nullptr;
+    cudaStream_t pending_stream = nullptr;
+    bool pending = false;
+    ~Impl() {
+        // Never throws; a submission that failed before its completion event
+        // may still use the buffers on the borrowed stream, so drain it first.
+        int previous = 0;
+        const bool restore = cudaGetDevice(&previous) == cudaSuccess;
+        cudaSetDevice(device);
+        if (pending && pending_stream) cudaStreamSynchronize(pending_stream);
+        if (begin) cudaEventDestroy(begin);
+        if (reduced) cudaEventDestroy(reduced);
+        if (copied) cudaEventDestroy(copied);
+        if (gpu) cudaFree(gpu);
+        if (host) cudaFreeHost(host);
+        if (restore) cudaSetDevice(previous);
+    }
+};
+
+namespace {
+// Makes `device` current for one scope and restores the caller's device.
+struct DeviceScope {
+    int previous = 0;
+    explicit DeviceScope(int device) {
+        cuda_check(cudaGetDevice(&previous), "H2O get CUDA device");
+        if (previous != device) cuda_check(cudaSetDevice(device), "H2O set CUDA device");
+    }
+    ~DeviceScope() { cudaSetDevice(previous); }
+};
+}  // namespace
+
+GQAH2OStatsCuda::GQAH2OStatsCuda(const void* reference, std::size_t capacity) : impl_(new Impl) {
+    if (!reference || !capacity) throw std::runtime_error("H2O statistics needs CUDA pointer and nonzero capacity");
+    auto& p = *impl_;
+    if (capacity > std::numeric_limits<std::size_t>::max() / (8 * sizeof(float)))
+        throw std::runtime_error("H2O attention statistics size overflow");
+    p.keys = capacity;
+    p.bytes = capacity * 8 * sizeof(float);
+    cudaPointerAttributes a{};
+    cuda_check(cudaPointerGetAttributes(&a, reference), "H2O reference pointer attributes");
+    if (a.type != cudaMemoryTypeDevice) throw std::runtime_error("H2O attention statistics requires CUDA device memory");
+    p.device = a.device;
+    DeviceScope scope(p.device);
+    cuda_check(cudaMalloc(reinterpret_cast<void**>(&p.gpu), p.bytes), "H2O reduction allocation");
+    cuda_check(cudaMallocHost(reinterpret_cast<void**>(&p.host), p.bytes), "H2O pinned sums allocation");
+    cuda_check(cudaEventCreate(&p.begin), "H2O begin event");
+    cuda_check(cudaEventCreate(&p.reduced), "H2O reduction event");
+    cuda_check(cudaEventCreate(&p.copied), "H2O D2H completion event");
+}
+GQAH2OStatsCuda::~GQAH2OStatsCuda() = default;
+std::size_t GQAH2OStatsCuda::gpu_bytes() const noexcept { return impl_->bytes; }
+std::size_t GQAH2OStatsCuda::host_bytes() const noexcept { return impl_->bytes; }
+
+GQAH2OStatsCuda::Result GQAH2OStatsCuda::reduce(const void* probabilities, const std::array<std::int64_t, 4>& ne,
+                                                const std::array<std::size_t, 4>& nb, std::size_t keys,
+                                                std::size_t queries, void* raw_stream) {
+    auto& p = *impl_;
+    // The C ABI takes a null stream as the default stream; the reference
+    // requires the attention backend's own stream.
+    if (!raw_stream) throw std::runtime_error("H2O reduction invalid pointer, actual CUDA stream or capacity");
+    DeviceScope scope(p.device);
+    const auto stream = static_cast<cudaStream_t>(raw_stream);
+    Result out;
+    out.started_ns = now_ns();
+    p.pending_stream = stream;
+    p.pending = true;
+    try {
+        cuda_check(cudaEventRecord(p.begin, stream), "H2O reduction start record");
+        const int rc = hsb_h2o_group_sums(probabilities, ne.data(), nb.data(), keys, queries, p.gpu, p.keys, nullptr,
+                                          stream);
+        if (rc != HSB_OK) {  // rejected before any launch: nothing of ours is on the stream
+            p.pending = false;
+            p.pending_stream = nullptr;
+            throw_status(rc);
+        }
+        out.elements = keys * 8;
+        out.d2h_bytes = out.elements * sizeof(float);
+        cuda_check(cudaEventRecord(p.reduced, stream), "H2O reduction ready record");
+        cuda_check(cudaMemcpyAsync(p.host, p.gpu, out.d2h_bytes, cudaMemcpyDeviceToHost, stream), "H2O group sums D2H");
+        cuda_check(cudaEventRecord(p.copied, stream), "H2O D2H ready record");
+        cuda_check(cudaEventSynchronize(p.copied), "H2O group sums completion");
+        out.ready_observed_ns = now_ns();
+        p.pending = false;
+        p.pending_stream = nullptr;
+        float reduction_ms = 0, d2h_ms = 0;
+        cuda_check(cudaEventElapsedTime(&reduction_ms, p.begin, p.reduced), "H2O reduction interval");
+        cuda_check(cudaEventElapsedTime(&d2h_ms, p.reduced, p.copied), "H2O D2H interval");
+        out.reduction_ms = reduction_ms;
+        out.d2h_ms = d2h_ms;
+        out.sums = p.host;
+        return out;
+    } catch (...) {
+        if (p.pending && cudaStreamSynchronize(stream) == cudaSuccess) {
+            p.pending = false;
+            p.pending_stream = nullptr;
+        }
+        throw;
+    }
+}
+
 }  // namespace hillserve
+
+// ------------------------------------------------------- C handles
+namespace {
+void copy_message(const std::exception& e, char* err, std::size_t errlen) {
+    if (err && errlen) {
+        std::strncpy(err, e.what(), errlen - 1);
+        err[errlen - 1] = 0;
+    }
+}
+}  // namespace
+
+extern "C" {
+void* hsb_compat_h2o_create(const void* pointer, std::size_t capacity, char* err, std::size_t errlen) {
+    try {
+        return new hillserve::GQAH2OStatsCuda(pointer, capacity);
+    } catch (const std::exception& e) {
+        copy_message(e, err, errlen);
+        return nullptr;
+    }
+}
+void hsb_compat_h2o_destroy(void* reducer) { delete static_cast<hillserve::GQAH2OStatsCuda*>(reducer); }
+int hsb_compat_h2o_reduce(void* reducer, const void* probabilities, const std::int64_t ne[4], const std::size_t nb[4],
+                          std::size_t keys, std::size_t queries, void* stream, const float** sums,
+                          double* reduction_ms, double* d2h_ms, char* err, std::size_t errlen) {
+    try {
+        if (!reducer || !ne || !nb) throw std::runtime_error("H2O reduction invalid pointer, actual CUDA stream or capacity");
+        const std::array<std::int64_t, 4> n{{ne[0], ne[1], ne[2], ne[3]}};
+        const std::array<std::size_t, 4> b{{nb[0], nb[1], nb[2], nb[3]}};
+        const auto r = static_cast<hillserve::GQAH2OStatsCuda*>(reducer)->reduce(probabilities, n, b, keys, queries,
+                                                                               stream);
+        if (sums) *sums = r.sums;
+        if (reduction_ms) *reduction_ms = r.reduction_ms;
+        if (d2h_ms) *d2h_ms = r.d2h_ms;
+        return 0;
+    } catch (const std::exception& e) {
+        copy_message(e, err, errlen);
+        return 1;
+    }
+}
+}

@@ -103,6 +103,13 @@ const char* hsb_status_message(int status) {
     case HSB_E_COVER_COUNT: return "prefetch count upper-bound exceeds original F16 range";
     case HSB_E_COVER_MEAN: return "prefetch mean upper-bound invalid";
     case HSB_E_ZERO_SELECTION: return "full GQA zero selection; no dense/current-token fallback";
+    case HSB_E_H2O_ARGS: return "H2O reduction invalid pointer, actual CUDA stream or capacity";
+    case HSB_E_H2O_SHAPE: return "H2O reduction requires [keys,queries,32,1] actual attention";
+    case HSB_E_H2O_STRIDE: return "H2O reduction invalid F32 tensor stride";
+    case HSB_E_H2O_OVERFLOW: return "H2O attention statistics address overflow";
+    case HSB_E_H2O_ALIGN: return "H2O reduction requires aligned F32 tensor";
+    case HSB_E_H2O_GRID: return "H2O reduction exceeds CUDA grid limit";
+    case HSB_E_H2O_DEVICE: return "H2O softmax tensor is not on the expected CUDA device";
     default: return "unknown hsb status";
     }
 }
@@ -700,6 +707,49 @@ int hsb_synth_keys(uint16_t* d_rows, size_t tokens, size_t stride_words, uint64_
     cudaError_t e = launch_synth_keys(d_rows, tokens, stride_words, seed, heavy_fraction, heavy_scale, rope, theta,
                                       as_stream(stream));
     return e == cudaSuccess ? HSB_OK : fail_cuda(e, "synth launch");
+}
+
+// ------------------------------------------------------- H2O statistics
+int hsb_h2o_group_sums(const void* d_probabilities, const int64_t ne[4], const size_t nb[4],
+                       size_t valid_keys, size_t valid_queries, float* d_sums, size_t capacity_keys,
+                       hsb_device_status* d_status, void* stream) {
+    // runtime/gqa_h2o_stats.cu:110-133, in the reference's order.
+    if (!d_probabilities || !d_sums || !ne || !nb || !valid_keys || !valid_queries || valid_keys > capacity_keys)
+        return fail(HSB_E_H2O_ARGS, "H2O reduction invalid pointer, actual CUDA stream or capacity");
+    if (!(ne[0] > 0 && ne[1] > 0 && ne[2] == 32 && ne[3] == 1 && valid_keys <= (uint64_t)ne[0] &&
+          valid_queries <= (uint64_t)ne[1]))
+        return fail(HSB_E_H2O_SHAPE, "H2O reduction requires [keys,queries,32,1] actual attention");
+    const size_t extents[3] = {valid_keys, valid_queries, 32};
+    size_t max_offset = 0;
+    for (int axis = 0; axis < 3; ++axis) {
+        if (nb[axis] < sizeof(float) || nb[axis] % alignof(float) != 0)
+            return fail(HSB_E_H2O_STRIDE, "H2O reduction invalid F32 tensor stride");
+        if (nb[axis] && extents[axis] - 1 > std::numeric_limits<size_t>::max() / nb[axis])
+            return fail(HSB_E_H2O_OVERFLOW, "H2O attention statistics size overflow");
+        const size_t offset = (extents[axis] - 1) * nb[axis];
+        if (offset > std::numeric_limits<size_t>::max() - max_offset)
+            return fail(HSB_E_H2O_OVERFLOW, "H2O attention statistics address overflow");
+        max_offset += offset;
+    }
+    if (max_offset > std::numeric_limits<size_t>::max() - sizeof(float))
+        return fail(HSB_E_H2O_OVERFLOW, "H2O attention statistics final address overflow");
+    if (!aligned(d_probabilities, alignof(float)))
+        return fail(HSB_E_H2O_ALIGN, "H2O reduction requires aligned F32 tensor");
+    if ((valid_keys - 1) / 256 + 1 > 2147483647u)
+        return fail(HSB_E_H2O_GRID, "H2O reduction exceeds CUDA grid limit");
+    int device = -1;
+    cudaPointerAttributes attributes{};
+    if (cudaGetDevice(&device) != cudaSuccess || cudaPointerGetAttributes(&attributes, d_probabilities) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(HSB_E_H2O_DEVICE, "H2O softmax tensor is not on the expected CUDA device");
+    }
+    if (attributes.type != cudaMemoryTypeDevice || attributes.device != device)
+        return fail(HSB_E_H2O_DEVICE, "H2O softmax tensor is not on the expected CUDA device");
+    cudaError_t e = launch_h2o_group_sums(d_probabilities, valid_keys, valid_queries, nb[0], nb[1], nb[2], d_sums,
+                                          d_status, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "H2O attention reduction launch");
+    g_last_error.clear();
+    return HSB_OK;
 }
 
 }  // extern "C"

@@ -2,6 +2,7 @@
 // C-ABI layer (capi.cu).  Not installed; the public interface is hsb.h.
 #pragma once
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <cstddef>
@@ -19,6 +20,9 @@ struct DeviceInfo {
 };
 // Properties of the current device, cached per device.
 const DeviceInfo& device_info();
+// cuTensorMapEncodeTiled resolved through the runtime (no libcuda link);
+// null when the driver does not provide it.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 // Launch with programmatic stream serialization (the kernel calls pdl_wait()
 // before touching global memory), optionally cooperative.
@@ -183,6 +187,12 @@ size_t attention_dense_workspace_bytes(size_t tokens);
 cudaError_t launch_attention_dense(const float* q, const uint16_t* kcache, const uint16_t* vcache,
                                    size_t tokens, size_t stride_words, float* out,
                                    void* workspace, cudaStream_t stream);
+
+// H2O residency statistics (runtime/gqa_h2o_stats.cu:41-57): out[kv][key]
+// over valid keys x queries of F32 probabilities with byte strides nb0 (key),
+// nb1 (query), nb2 (Q head); arguments already validated.
+cudaError_t launch_h2o_group_sums(const void* probs, size_t keys, size_t queries, size_t nb0, size_t nb1,
+                                  size_t nb2, float* out, hsb_device_status* status, cudaStream_t stream);
 
 // Rehearsal query
 cudaError_t launch_rehearsal(const uint16_t* x, const uint16_t* w, uint64_t position, float theta,

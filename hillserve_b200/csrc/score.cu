@@ -394,22 +394,6 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
     }
 }
 
-// Resolves cuTensorMapEncodeTiled through the runtime (no libcuda link).
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-        else
-            cudaGetLastError();
-    });
-    return fn;
-}
-
 // Token-major keys of one view seen as a 3-D tensor {channel, token, KV head}
 // (strides: token = stride_words words, KV head = 128 words), so that a box
 // lands in shared memory as [KV head][token][channels].
@@ -433,6 +417,22 @@ __global__ void scale_kernel(const uint16_t* __restrict__ raw, unsigned long lon
 }
 
 }  // namespace
+
+// Resolves cuTensorMapEncodeTiled through the runtime (no libcuda link).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
 
 cudaError_t configure_tma_kernels() {
     cudaError_t e = cudaFuncSetAttribute(score_tma_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemBytes);

@@ -80,7 +80,15 @@ typedef enum hsb_status {
     HSB_E_COVER_COUNT = 62,
     HSB_E_COVER_MEAN = 63,
     /* layer step -- policy/full_gqa_runtime.cpp:573 */
-    HSB_E_ZERO_SELECTION = 70
+    HSB_E_ZERO_SELECTION = 70,
+    /* H2O statistics -- runtime/gqa_h2o_stats.cu:110-133 */
+    HSB_E_H2O_ARGS = 80,
+    HSB_E_H2O_SHAPE = 81,
+    HSB_E_H2O_STRIDE = 82,
+    HSB_E_H2O_OVERFLOW = 83,
+    HSB_E_H2O_ALIGN = 84,
+    HSB_E_H2O_GRID = 85,
+    HSB_E_H2O_DEVICE = 86
 } hsb_status;
 
 int hsb_abi_version(void);
@@ -327,6 +335,24 @@ int hsb_shard_select(const uint16_t* d_order_keys, const uint16_t* d_raw, int kv
                      const uint16_t* d_kshard, const uint16_t* d_vshard, uint16_t* d_k_packed,
                      uint16_t* d_v_packed, float* d_out, void* d_workspace, size_t workspace_bytes,
                      void* stream);
+
+/* ---------------------------------------------- H2O residency statistics
+ * The device work of GQAH2OStatsCuda::reduce (runtime/gqa_h2o_stats.cu:
+ * 106-173; kernel sum_actual_attention :41-57).  d_probabilities is the
+ * actual F32 softmax tensor, ne = {keys, queries, Q heads, streams} with
+ * ggml byte strides nb[] (nb[3] unused); only ne[2] == 32, ne[3] == 1.
+ * Writes d_sums[kv * valid_keys + key] for the 8 KV heads: the F32 sum over
+ * Q heads 4kv..4kv+3 (outer) and queries 0..valid_queries-1 (inner), from
+ * +0, each addition rounded -- the reference's order, bit for bit.  Padding
+ * keys and queries are never read.  Validation and messages follow reduce()
+ * (:110-133); capacity_keys is the d_sums capacity per KV head (the
+ * reducer's constructor argument); as there, the probabilities must be
+ * device memory of the current device.  A null stream is the default stream.
+ * Enqueues on `stream` and never synchronises; d_status (nullable) receives
+ * HSB_E_TIMEOUT if a bounded device wait gave up. */
+int hsb_h2o_group_sums(const void* d_probabilities, const int64_t ne[4], const size_t nb[4],
+                       size_t valid_keys, size_t valid_queries, float* d_sums, size_t capacity_keys,
+                       hsb_device_status* d_status, void* stream);
 
 /* ------------------------------------------------------ synthetic inputs
  * Benchmark inputs, not part of the reference interface: seeded F16 normal

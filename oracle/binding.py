@@ -65,6 +65,8 @@ def oracle() -> C.CDLL:
         lib.orc_attention_packed_f32.restype = None
         lib.orc_rehearsal.argtypes = [P, P, C.c_uint64, C.c_double, P]
         lib.orc_rehearsal.restype = None
+        lib.orc_h2o_group_sums.argtypes = [P, SZ, SZ, SZ, SZ, SZ, P]
+        lib.orc_h2o_group_sums.restype = None
         _oracle = lib
     return _oracle
 
@@ -93,6 +95,14 @@ def ref() -> C.CDLL:
         lib.ref_select.argtypes = [P, SZ, SZ, SZ, C.c_float, C.c_float, C.c_int, P, SZ, P, P, P, C.c_char_p, SZ]
         lib.ref_union.argtypes = [P, SZ, P, SZ, P, P, C.c_char_p, SZ]
         lib.ref_pack.argtypes = [P, SZ, P, P, SZ, P, SZ, P, SZ, SZ, P, P, P, C.c_char_p, SZ]
+        lib.ref_h2o_create.restype = P
+        lib.ref_h2o_create.argtypes = [SZ, SZ, SZ, SZ, SZ, SZ, C.c_uint64, C.c_char_p, SZ]
+        lib.ref_h2o_destroy.argtypes = [P]
+        lib.ref_h2o_destroy.restype = None
+        lib.ref_h2o_observe_attention.argtypes = [P, SZ, SZ, SZ, SZ, P, SZ, C.c_char_p, SZ]
+        lib.ref_h2o_observe_group_sums.argtypes = [P, SZ, SZ, SZ, SZ, P, SZ, C.c_char_p, SZ]
+        lib.ref_h2o_importance.argtypes = [P, SZ, SZ, SZ, P, C.c_char_p, SZ]
+        lib.ref_h2o_resident_ids.argtypes = [P, SZ, P, SZ, P, C.c_char_p, SZ]
         _ref = lib
     return _ref
 
@@ -345,3 +355,59 @@ def ref_pack(ids, sizes, positions, physical, payload, count: int):
                       payload.size, count, _p(k), _p(v), _p(mask), e, 512):
         raise ReferenceError_(e.value.decode())
     return k, v, mask
+
+
+def h2o_group_sums(buf: np.ndarray, keys: int, queries: int, nb0: int, nb1: int, nb2: int,
+                   offset: int = 0) -> np.ndarray:
+    """runtime/gqa_h2o_stats.cu:41-57 over the bytes of `buf` (any dtype) from
+    byte `offset`: F32 [8][keys] group sums."""
+    buf = np.ascontiguousarray(buf)
+    need = offset + (keys - 1) * nb0 + (queries - 1) * nb1 + 31 * nb2 + 4
+    assert buf.nbytes >= need, "probability buffer too small for the strides"
+    out = np.empty((8, keys), dtype=np.float32)
+    oracle().orc_h2o_group_sums(C.c_void_p(buf.ctypes.data + offset), keys, queries, nb0, nb1, nb2, _p(out))
+    return out
+
+
+class RefH2O:
+    """The reference's H2OResidency (policy/h2o_residency.hpp:16-77)."""
+
+    def __init__(self, layers: int = 1, query_heads: int = 32, kv_heads: int = 8, prompt_tokens: int = 1,
+                 generated_capacity: int = 0, prompt_resident: int = 0, budget: int = 1 << 40):
+        e = _err()
+        self.kv_heads = kv_heads
+        self.h = ref().ref_h2o_create(layers, query_heads, kv_heads, prompt_tokens, generated_capacity,
+                                      prompt_resident, budget, e, 512)
+        if not self.h:
+            raise ReferenceError_(e.value.decode())
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            ref().ref_h2o_destroy(self.h)
+
+    def observe_attention(self, layer: int, first: int, queries: int, keys: int, p: np.ndarray) -> None:
+        p = np.ascontiguousarray(p, dtype=np.float32)
+        e = _err()
+        if ref().ref_h2o_observe_attention(self.h, layer, first, queries, keys, _p(p), p.size, e, 512):
+            raise ReferenceError_(e.value.decode())
+
+    def observe_group_sums(self, layer: int, first: int, queries: int, keys: int, sums: np.ndarray) -> None:
+        sums = np.ascontiguousarray(sums, dtype=np.float32)
+        e = _err()
+        if ref().ref_h2o_observe_group_sums(self.h, layer, first, queries, keys, _p(sums), sums.size, e, 512):
+            raise ReferenceError_(e.value.decode())
+
+    def importance(self, layer: int, count: int) -> np.ndarray:
+        out = np.empty((self.kv_heads, count), dtype=np.float32)
+        e = _err()
+        if ref().ref_h2o_importance(self.h, layer, self.kv_heads, count, _p(out), e, 512):
+            raise ReferenceError_(e.value.decode())
+        return out
+
+    def resident_ids(self, layer: int, capacity: int) -> list:
+        out = np.zeros((self.kv_heads, capacity), dtype=np.uint64)
+        sizes = np.zeros(self.kv_heads, dtype=np.uint64)
+        e = _err()
+        if ref().ref_h2o_resident_ids(self.h, layer, _p(out), capacity, _p(sizes), e, 512):
+            raise ReferenceError_(e.value.decode())
+        return [out[h, :int(sizes[h])].tolist() for h in range(self.kv_heads)]

@@ -563,3 +563,28 @@ void orc_attention_packed_f32(const uint16_t* k, const uint16_t* v, const float*
     attn_job j = {k, v, mask, q, 0, 0, count, qpad, out, 0, 0, 0};
     run_attn(j, threads);
 }
+
+/* ------------------------------------------------------------------ H2O
+ * runtime/gqa_h2o_stats.cu:41-57: one F32 accumulator per (KV head, key),
+ * each addition rounded (this file is built with -ffp-contract=off and SSE
+ * single precision, so a float add is one IEEE binary32 addition).  The
+ * loops run Q head, query, key as H2OResidency::observe_attention does
+ * (policy/h2o_residency.cpp:65-76): each accumulator still sees Q heads
+ * 4kv..4kv+3 in turn and, within one, queries 0..Q-1 -- the CUDA kernel's
+ * per-output order -- while the key loop streams through memory. */
+void orc_h2o_group_sums(const void* probabilities, size_t keys, size_t queries, size_t nb0, size_t nb1,
+                        size_t nb2, float* out) {
+    const unsigned char* base = (const unsigned char*)probabilities;
+    for (size_t i = 0; i < 8 * keys; ++i) out[i] = 0.0f;
+    for (size_t h = 0; h < 32; ++h) {
+        float* acc = out + (h / 4) * keys;
+        for (size_t q = 0; q < queries; ++q) {
+            const unsigned char* row = base + q * nb1 + h * nb2;
+            for (size_t key = 0; key < keys; ++key) {
+                float p;
+                memcpy(&p, row + key * nb0, sizeof p);
+                acc[key] = acc[key] + p;
+            }
+        }
+    }
+}

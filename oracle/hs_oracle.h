@@ -127,6 +127,14 @@ void orc_attention_dense_f32(const uint16_t* kc, const uint16_t* vc, size_t n, s
 void orc_attention_packed_f32(const uint16_t* k, const uint16_t* v, const float* mask,
                               size_t count, size_t qpad, const float* q, float* out, int threads);
 
+/* H2O residency statistics, runtime/gqa_h2o_stats.cu:41-57
+ * (sum_actual_attention).  probabilities: bytes of an F32 tensor [key][query]
+ * [Q head] with byte strides nb0, nb1, nb2; out[kv * keys + key] = F32 sum,
+ * from +0, over Q heads 4kv..4kv+3 (outer) and queries 0..queries-1 (inner).
+ * The same order as H2OResidency::observe_attention (h2o_residency.cpp:66-76). */
+void orc_h2o_group_sums(const void* probabilities, size_t keys, size_t queries, size_t nb0, size_t nb1,
+                        size_t nb2, float* out);
+
 #ifdef __cplusplus
 }
 #endif

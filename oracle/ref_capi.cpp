@@ -2,7 +2,7 @@
 //
 // A thin C-ABI bridge, compiled together with the UNMODIFIED reference
 // HillServe sources (policy/host_policy.cpp, policy/full_gqa_cpu.cpp,
-// policy/gqa_policy.cpp, smartssd/adapter.cpp and the header-only
+// policy/gqa_policy.cpp, smartssd/adapter.cpp, policy/h2o_residency.cpp and the header-only
 // runtime/gqa_pack.hpp) into oracle/_ref/libhs_ref.so by oracle/Makefile.
 // It lets the tests pin the C oracle against the reference's own code on
 // seeded inputs, and lets bench.py time the reference CPU path.  Nothing in
@@ -11,6 +11,7 @@
 #include "policy/gqa_policy.hpp"
 #include "policy/host_policy.hpp"
 #include "runtime/gqa_pack.hpp"
+#include "policy/h2o_residency.hpp"
 
 #include <cmath>
 #include <cstdint>
@@ -144,6 +145,82 @@ int ref_pack(const std::uint64_t* ids, std::size_t kstride, const std::size_t* s
         std::vector<std::uint64_t> pos(positions, positions + npos), phys(physical, physical + nphys);
         std::vector<std::uint8_t> bytes(payload, payload + payload_bytes);
         hillserve::pack_gqa_workspace(heads, pos, phys, bytes, count, k, v, mask);
+        return 0;
+    } catch (const std::exception& e) {
+        copy_error(e, err, errlen);
+        return -1;
+    }
+}
+
+// H2OResidency -- policy/h2o_residency.hpp:16-77, the CPU consumer of the
+// H2O group sums and the reference's CPU path for them (observe_attention).
+void* ref_h2o_create(std::size_t layers, std::size_t query_heads, std::size_t kv_heads,
+                     std::size_t prompt_tokens, std::size_t generated_capacity,
+                     std::size_t prompt_resident_tokens_per_head, std::uint64_t budget, char* err,
+                     std::size_t errlen) {
+    try {
+        hillserve::policy::H2OResidency::Config c;
+        c.layers = layers;
+        c.query_heads = query_heads;
+        c.kv_heads = kv_heads;
+        c.prompt_tokens = prompt_tokens;
+        c.generated_capacity = generated_capacity;
+        c.prompt_resident_tokens_per_head = prompt_resident_tokens_per_head;
+        c.metadata_budget_bytes = budget;
+        return new hillserve::policy::H2OResidency(c);
+    } catch (const std::exception& e) {
+        copy_error(e, err, errlen);
+        return nullptr;
+    }
+}
+void ref_h2o_destroy(void* h) { delete static_cast<hillserve::policy::H2OResidency*>(h); }
+int ref_h2o_observe_attention(void* h, std::size_t layer, std::size_t first, std::size_t queries,
+                              std::size_t keys, const float* p, std::size_t elements, char* err,
+                              std::size_t errlen) {
+    try {
+        static_cast<hillserve::policy::H2OResidency*>(h)->observe_attention(layer, first, queries, keys, p,
+                                                                            elements);
+        return 0;
+    } catch (const std::exception& e) {
+        copy_error(e, err, errlen);
+        return -1;
+    }
+}
+int ref_h2o_observe_group_sums(void* h, std::size_t layer, std::size_t first, std::size_t queries,
+                               std::size_t keys, const float* sums, std::size_t elements, char* err,
+                               std::size_t errlen) {
+    try {
+        static_cast<hillserve::policy::H2OResidency*>(h)->observe_group_sums(layer, first, queries, keys, sums,
+                                                                             elements);
+        return 0;
+    } catch (const std::exception& e) {
+        copy_error(e, err, errlen);
+        return -1;
+    }
+}
+// importance(layer, head, position) for positions [0, count) of every KV head.
+int ref_h2o_importance(void* h, std::size_t layer, std::size_t kv_heads, std::size_t count, float* out,
+                       char* err, std::size_t errlen) {
+    try {
+        auto* r = static_cast<hillserve::policy::H2OResidency*>(h);
+        for (std::size_t kh = 0; kh < kv_heads; ++kh)
+            for (std::size_t k = 0; k < count; ++k) out[kh * count + k] = r->importance(layer, kh, k);
+        return 0;
+    } catch (const std::exception& e) {
+        copy_error(e, err, errlen);
+        return -1;
+    }
+}
+// resident_ids(layer): head h's IDs at out[h * stride ...], sizes[h].
+int ref_h2o_resident_ids(void* h, std::size_t layer, std::uint64_t* out, std::size_t stride,
+                         std::size_t* sizes, char* err, std::size_t errlen) {
+    try {
+        auto ids = static_cast<hillserve::policy::H2OResidency*>(h)->resident_ids(layer);
+        for (std::size_t kh = 0; kh < ids.size(); ++kh) {
+            if (ids[kh].size() > stride) throw std::runtime_error("bridge resident capacity");
+            std::memcpy(out + kh * stride, ids[kh].data(), ids[kh].size() * 8);
+            sizes[kh] = ids[kh].size();
+        }
         return 0;
     } catch (const std::exception& e) {
         copy_error(e, err, errlen);

@@ -1,13 +1,15 @@
 // C++ drop-in tests: the reference's own interfaces (policy/full_gqa_cpu.hpp,
 // policy/gqa_policy.hpp, runtime/gqa_pack.hpp, runtime/gqa_prefetch_cuda.hpp,
-// runtime/gqa_delivery.hpp), included by their reference paths and backed by
-// the B200 kernels.  The checks follow the reference unit tests
-// (tests/full_gqa_cpu_tests.cpp, tests/gqa_policy_tests.cpp,
-// tests/gqa_pack_tests.cpp) with independent scalar oracles written here.
+// runtime/gqa_delivery.hpp, runtime/gqa_h2o_stats.hpp), included by their
+// reference paths and backed by the B200 kernels.  The checks follow the
+// reference unit tests (tests/full_gqa_cpu_tests.cpp, tests/gqa_policy_tests.cpp,
+// tests/gqa_pack_tests.cpp, tests/gqa_h2o_stats_tests.cu) with independent
+// scalar oracles written here.
 // Prints one JSON status line; exit code 0 on success.
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <array>
 #include <cfenv>
 #include <cmath>
 #include <cstdint>
@@ -24,6 +26,7 @@
 #include "policy/gqa_policy.hpp"
 #include "policy/host_policy.hpp"
 #include "runtime/gqa_delivery.hpp"
+#include "runtime/gqa_h2o_stats.hpp"
 #include "runtime/gqa_pack.hpp"
 #include "runtime/gqa_prefetch_cuda.hpp"
 
@@ -328,6 +331,76 @@ void prefetch_and_delivery_tests() {
     need(report.find("attention_output_checksum") != std::string::npos, "report");
     for (float x : ws.output()) need(std::isfinite(x), "finite attention");
 }
+
+// tests/gqa_h2o_stats_tests.cu:39-95: a strided [11, 6, 32, 1] F32 tensor with
+// holes between keys and NaN in every byte that is not a valid probability;
+// blocks (first 0, 3 queries) and (first 3, 2 queries); the sums must equal a
+// scalar F32 sum in (Q head, query) order, bit for bit.
+void h2o_tests() {
+    const std::array<std::int64_t, 4> ne{{11, 6, 32, 1}};
+    const std::array<std::size_t, 4> nb{{8, 112, 704, 22528}};
+    std::vector<float> storage(nb[3] / sizeof(float));
+    void* gpu = nullptr;
+    cudaStream_t stream = nullptr;
+    if (cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&gpu, nb[3]) != cudaSuccess)
+        throw std::runtime_error("H2O fixture allocation");
+    struct Free {
+        void* g;
+        cudaStream_t s;
+        ~Free() {
+            cudaStreamSynchronize(s);
+            cudaFree(g);
+            cudaStreamDestroy(s);
+        }
+    } guard{gpu, stream};
+    GQAH2OStatsCuda reducer(gpu, 7);
+    need(reducer.gpu_bytes() == 8 * 7 * sizeof(float) && reducer.host_bytes() == 8 * 7 * sizeof(float),
+         "H2O buffers bounded by 8 x capacity");
+    for (std::size_t first : {0u, 3u}) {
+        const std::size_t queries = first == 0 ? 3 : 2, keys = first + queries;
+        std::fill(storage.begin(), storage.end(), std::numeric_limits<float>::quiet_NaN());
+        std::vector<float> dense(32 * queries * keys, 0.f);
+        for (std::size_t h = 0; h < 32; ++h)
+            for (std::size_t q = 0; q < queries; ++q) {
+                const std::size_t available = first + q + 1;
+                double total = 0;
+                for (std::size_t k = 0; k < available; ++k) total += 1 + (k + h / 4) % 5;
+                for (std::size_t k = 0; k < keys; ++k) {
+                    const float x = k < available ? float((1 + (k + h / 4) % 5) / total) : 0.f;
+                    storage[(h * nb[2] + q * nb[1] + k * nb[0]) / sizeof(float)] = x;
+                    dense[(h * queries + q) * keys + k] = x;
+                }
+            }
+        if (cudaMemcpyAsync(gpu, storage.data(), nb[3], cudaMemcpyHostToDevice, stream) != cudaSuccess)
+            throw std::runtime_error("H2O fixture upload");
+        const auto r = reducer.reduce(gpu, ne, nb, keys, queries, stream);
+        need(r.sums && r.elements == 8 * keys && r.d2h_bytes == 8 * keys * sizeof(float), "H2O result shape");
+        need(r.ready_observed_ns >= r.started_ns && r.reduction_ms >= 0 && r.d2h_ms >= 0, "H2O timings");
+        for (std::size_t kh = 0; kh < 8; ++kh)
+            for (std::size_t k = 0; k < keys; ++k) {
+                float want = 0.f;
+                for (std::size_t lane = 0; lane < 4; ++lane)
+                    for (std::size_t q = 0; q < queries; ++q) want += dense[((kh * 4 + lane) * queries + q) * keys + k];
+                std::uint32_t a, b;
+                std::memcpy(&a, &r.sums[kh * keys + k], 4);
+                std::memcpy(&b, &want, 4);
+                need(a == b, "H2O strided F32 group sum");
+            }
+    }
+    auto heads = ne;
+    heads[2] = 8;
+    throws<std::runtime_error>([&] { reducer.reduce(gpu, heads, nb, 5, 2, stream); }, "non-GQA32 head shape");
+    auto streams = ne;
+    streams[3] = 2;
+    throws<std::runtime_error>([&] { reducer.reduce(gpu, streams, nb, 5, 2, stream); }, "multi-sequence shape");
+    throws<std::runtime_error>([&] { reducer.reduce(gpu, ne, nb, 8, 2, stream); }, "capacity overrun");
+    throws<std::runtime_error>([&] { reducer.reduce(gpu, ne, nb, 5, 7, stream); }, "padding query overrun");
+    throws<std::runtime_error>([&] { reducer.reduce(gpu, ne, nb, 5, 2, nullptr); }, "missing attention stream");
+    std::vector<float> host(16);
+    throws<std::runtime_error>([&] { GQAH2OStatsCuda bad(host.data(), 4); }, "host pointer as reference");
+    throws<std::runtime_error>([&] { reducer.reduce(host.data(), ne, nb, 5, 2, stream); }, "host probabilities");
+}
 }  // namespace
 
 int main() {
@@ -336,6 +409,7 @@ int main() {
         selector_tests();
         pack_tests();
         prefetch_and_delivery_tests();
+        h2o_tests();
         std::cout << "{\"status\":\"passed\",\"bitwise_scores_compared\":" << compared << "}" << std::endl;
         return 0;
     } catch (const std::exception& e) {

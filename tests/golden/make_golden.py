@@ -3,7 +3,7 @@ own CPU code (oracle/_ref/libhs_ref.so, compiled from the HillServe sources by
 oracle/Makefile) on seeded inputs.  Run here, where the reference sources
 exist:
 
-    make -C oracle && python tests/golden/make_golden.py
+    make -C oracle && python tests/golden/make_golden.py [--only h2o]
 
 Inputs are regenerated bit-exactly from their seeds by tests/inputs.py, so
 the fixtures hold only input digests and the reference's outputs.
@@ -47,8 +47,45 @@ def scorer_vectors():
     return out
 
 
+# (first, queries) blocks of the H2O fixture; keys = first + queries.
+H2O_BLOCKS = ((0, 1), (0, 3), (0, 7), (0, 16), (0, 17), (0, 64), (0, 129),
+              (3, 2), (5, 1), (63, 1), (100, 17), (255, 1), (200, 56), (511, 4))
+
+
+def h2o_reference_importance(seed: int, first: int, queries: int) -> np.ndarray:
+    """The reference H2OResidency's importance after observing, through its
+    own CPU observe_attention (policy/h2o_residency.cpp:60-80), a one-hot
+    block on key 0 for queries 0..first-1 and then the seeded block
+    (first, queries).  Keys >= 1 hold exactly that block's group sums."""
+    keys = first + queries
+    r = ob.RefH2O(prompt_tokens=keys)
+    if first:
+        prior = np.zeros((32, first, first), dtype=np.float32)
+        prior[:, :, 0] = 1.0
+        r.observe_attention(0, 0, first, first, prior)
+    r.observe_attention(0, first, queries, keys, inputs.h2o_probabilities(seed, first, queries, keys))
+    return r.importance(0, keys)
+
+
+def h2o_vectors() -> None:
+    names, digests, heads = [], [], []
+    for i, (first, queries) in enumerate(H2O_BLOCKS):
+        imp = h2o_reference_importance(1000 + i, first, queries)
+        names.append(f"f{first}_q{queries}")
+        digests.append(inputs.digest(imp))
+        heads.append(imp[:, :8] if imp.shape[1] >= 8 else np.pad(imp, ((0, 0), (0, 8 - imp.shape[1]))))
+    np.savez_compressed(OUT / "h2o_vectors.npz", names=np.array(names), blocks=np.array(H2O_BLOCKS),
+                        importance_digest=np.array(digests), importance_head=np.stack(heads))
+
+
 def main() -> None:
     assert ob.reference_available(), "build oracle/_ref first (make -C oracle)"
+    if sys.argv[1:] == ["--only", "h2o"]:
+        h2o_vectors()
+        print("h2o fixture written to", OUT)
+        return
+    # ---- 0. H2O group sums through the reference's CPU policy
+    h2o_vectors()
     # ---- 1. reference scorer test vectors
     vec = scorer_vectors()
     names = sorted(vec)

@@ -124,3 +124,36 @@ def cpu_test_case(rng: XorShift32, n: int, stride: int):
         for c in range(1024):
             data[t * stride + c] = cpu_test_half(rng)
     return q, data
+
+
+def h2o_probabilities(seed: int, first: int, queries: int, keys: int, heads: int = 32) -> np.ndarray:
+    """Causal softmax-like rows, F32 [heads][queries][keys]: row (h, q) is
+    w / sum(w) over keys 0..first+q (0 after), with integer weights w in
+    1..1024 from splitmix64 (1 in 256 of them scaled by 1024: heavy hitters).
+    Integer sums and one IEEE division per element make the values
+    bit-reproducible on any platform."""
+    n = heads * queries * keys
+    x = splitmix64(np.arange(n, dtype=np.uint64) + np.uint64((seed * 0x9E3779B97F4A7C15) % (1 << 64)))
+    w = ((x >> np.uint64(54)) + np.uint64(1)).astype(np.int64)
+    w = np.where((x & np.uint64(0xff)) == 0, w << 10, w).reshape(heads, queries, keys)
+    causal = np.arange(keys)[None, None, :] <= (first + np.arange(queries))[None, :, None]
+    w = np.where(causal, w, 0)
+    total = w.sum(axis=2, keepdims=True)
+    return (w / total).astype(np.float32)
+
+
+def h2o_layout(p: np.ndarray, ne0: int, ne1: int, nb0: int, nb1: int, nb2: int, fill=np.nan,
+               total_bytes: int = 0) -> np.ndarray:
+    """Places p [32][queries][keys] into a byte buffer with ggml strides (key
+    nb0, query nb1, head nb2) over ne0 x ne1 x 32 elements; every byte not
+    holding a valid probability is the F32 `fill` pattern (NaN by default),
+    as in the reference's strided test."""
+    heads, queries, keys = p.shape
+    size = (ne0 - 1) * nb0 + (ne1 - 1) * nb1 + (heads - 1) * nb2 + 4
+    size = max((size + 15) // 16 * 16, total_bytes)
+    buf = np.full(size // 4, fill, dtype=np.float32).view(np.uint8)
+    h, q, k = np.meshgrid(np.arange(heads), np.arange(queries), np.arange(keys), indexing="ij")
+    offs = (k * nb0 + q * nb1 + h * nb2).reshape(-1)
+    assert np.all(offs % 4 == 0)
+    buf.view(np.float32)[offs // 4] = p.reshape(-1)
+    return buf

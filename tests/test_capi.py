@@ -109,6 +109,49 @@ def test_cover_range_checks(lib):
     assert lib.hsb_prefetch_cover(p, 192, 3, C.c_float(5.0), 0, p, 0, p, p, 1 << 24, None) == 60
 
 
+def test_compat_handles_exported():
+    """Every C handle include/hsb_compat.h declares is exported by libhsb_compat."""
+    from hillserve_b200 import build
+
+    text = (ROOT / "include" / "hsb_compat.h").read_text()
+    names = set(re.findall(r"(hsb_compat_\w+)\s*\(", text))
+    assert len(names) == 3
+    compat = C.CDLL(str(build.COMPAT_LIB))
+    for name in names:
+        assert hasattr(compat, name), name
+
+
+def test_h2o_shape_guards(lib):
+    """runtime/gqa_h2o_stats.cu:110-133 and the guards of
+    tests/gqa_h2o_stats_tests.cu:90-95, rejected before any device work."""
+    p = C.c_void_p(0x1000)
+    ne = (C.c_int64 * 4)(11, 6, 32, 1)
+    nb = (C.c_size_t * 4)(8, 112, 704, 22528)
+
+    def call(ne_, nb_, keys, queries, cap=7, probs=p):
+        return lib.hsb_h2o_group_sums(probs, ne_, nb_, keys, queries, p, cap, None, None)
+
+    bad_heads = (C.c_int64 * 4)(11, 6, 8, 1)
+    assert call(bad_heads, nb, 5, 2) == 81
+    assert lib.hsb_last_error() == b"H2O reduction requires [keys,queries,32,1] actual attention"
+    bad_streams = (C.c_int64 * 4)(11, 6, 32, 2)
+    assert call(bad_streams, nb, 5, 2) == 81
+    assert call(ne, nb, 8, 2) == 80  # capacity overrun
+    assert lib.hsb_last_error() == b"H2O reduction invalid pointer, actual CUDA stream or capacity"
+    assert call(ne, nb, 5, 7) == 81  # padding query overrun
+    assert call(ne, nb, 12, 2, cap=12) == 81  # key overrun
+    assert call(ne, nb, 0, 2) == 80 and call(ne, nb, 5, 0) == 80
+    assert call(ne, nb, 5, 2, probs=None) == 80
+    assert call(ne, (C.c_size_t * 4)(2, 112, 704, 0), 5, 2) == 82
+    assert call(ne, (C.c_size_t * 4)(8, 110, 704, 0), 5, 2) == 82
+    assert lib.hsb_last_error() == b"H2O reduction invalid F32 tensor stride"
+    assert call(ne, nb, 5, 2, probs=C.c_void_p(0x1002)) == 84
+    assert lib.hsb_last_error() == b"H2O reduction requires aligned F32 tensor"
+    huge = (C.c_size_t * 4)(1 << 62, 112, 704, 0)
+    assert call(ne, huge, 5, 2) == 83
+    assert lib.hsb_status_message(84) == b"H2O reduction requires aligned F32 tensor"
+
+
 def test_status_messages_match_reference_wording(lib):
     want = {
         22: b"nonfinite head0 score", 23: b"F16 threshold overflow", 24: b"nonfinite GQA score",
