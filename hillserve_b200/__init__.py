@@ -35,10 +35,12 @@ __all__ = [
     "pack_gqa_workspace", "gather_map", "gather_cache", "stage_rows", "attention_packed",
     "attention_dense", "rehearsal_query", "GQAPrefetchCuda", "GQADeliveryWorkspace",
     "SelectedKVLayer", "attention_slots", "h2o_group_sums", "GQAH2OStatsCuda",
+    "segment_header", "segment_extent_bytes", "kv_records_encode", "kv_records_verify", "kv_read_plan",
+    "kv_read_groups",
 ]
 
 # Status codes the reference reports as std::invalid_argument.
-_INVALID_ARGUMENT = {10, 11, 12, 30, 31, 40, 41, 42, 43}
+_INVALID_ARGUMENT = {10, 11, 12, 30, 31, 40, 41, 42, 43, 93}
 
 
 class InvalidArgument(HsbError, ValueError):
@@ -420,6 +422,80 @@ class GQAH2OStatsCuda:
         out.d2h_ms = reduced.elapsed_time(copied)
         out.sums = self._host[:8 * keys].numpy()
         return out
+
+
+# ------------------------------------------------- cold-tier KV records
+def segment_extent_bytes(layers: int, positions: int, record_bytes: int) -> int:
+    """Page-rounded SegmentedKVStore v1 file extent (segmented_store.cpp:26)."""
+    n = lib().hsb_segment_extent_bytes(int(layers), int(positions), int(record_bytes))
+    if not n:
+        raise HsbError(93, "bounded segmented geometry/quota")
+    return int(n)
+
+
+def segment_header(request: int, layers: int, positions: int, record_bytes: int) -> bytes:
+    """The 4096-byte file header (segmented_store.cpp:30)."""
+    buf = C.create_string_buffer(4096)
+    _raise(lib().hsb_segment_header(buf, int(request), int(layers), int(positions), int(record_bytes)))
+    return buf.raw
+
+
+def kv_records_encode(payload, count: int, record_bytes: int, request: int, layer: int, first: int,
+                      payload_stride: Optional[int] = None, out=None, stream=None):
+    """File image of records (layer, first + i), i < count, from device
+    payload rows: uint8 [count * (record_bytes + 32)] on the payload's device."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty(int(count) * (int(record_bytes) + 32), dtype=torch.uint8, device=payload.device)
+    stride = int(record_bytes) if payload_stride is None else int(payload_stride)
+    _raise(lib().hsb_kv_records_encode(_ptr(payload), stride, int(count), int(record_bytes), int(request),
+                                       int(layer), int(first), _ptr(out), _stream(stream)))
+    return out
+
+
+def kv_records_verify(window, offsets, positions, request: int, layer: int, record_bytes: int, out,
+                      groups=None, out_rows=None, check: bool = True, stream=None):
+    """Checks records of a device window and gathers their payloads into
+    `out` (rows of record_bytes).  offsets / positions: uint64 (int64)
+    device tensors; groups, out_rows: optional int32 device tensors.
+    Raises the reference's error (check=True) or returns the status tensor."""
+    st = _status_buffer(window.device)
+    count = int(offsets.numel())
+    stride = out.stride(0) * out.element_size() if out.dim() > 1 else int(record_bytes)
+    capacity = out.numel() * out.element_size() // stride
+    _raise(lib().hsb_kv_records_verify(_ptr(window), window.numel() * window.element_size(), _ptr(offsets),
+                                       _ptr(positions), _ptr(groups), count, int(request), int(layer),
+                                       int(record_bytes), _ptr(out), stride, _ptr(out_rows), capacity, _ptr(st),
+                                       _stream(stream)))
+    if check:
+        _check_status(st, stream)
+    return st
+
+
+class KVReadWindow(C.Structure):
+    _fields_ = [("begin", C.c_uint64), ("end", C.c_uint64), ("required_page_bytes", C.c_uint64),
+                ("first_record", C.c_uint64), ("end_record", C.c_uint64)]
+
+
+def kv_read_plan(offsets, record_bytes: int, extent: int, window_bytes: int = 1 << 20, gap_bytes: int = 16 << 10,
+                 max_amplification_permille: int = 1500) -> list:
+    """storage/kv_read_plan.hpp:34-59 on the host: [(begin, end,
+    required_page_bytes, first_record, end_record), ...]."""
+    offs = [int(o) for o in offsets]
+    arr = (C.c_uint64 * max(1, len(offs)))(*offs)
+    wins = (KVReadWindow * max(1, len(offs)))()
+    n = C.c_size_t(0)
+    _raise(lib().hsb_kv_read_plan(arr, len(offs), int(record_bytes), int(extent), int(window_bytes), int(gap_bytes),
+                                  int(max_amplification_permille), wins, len(wins), C.byref(n)))
+    return [(w.begin, w.end, w.required_page_bytes, w.first_record, w.end_record) for w in wins[:n.value]]
+
+
+def kv_read_groups(windows: list, count: int) -> list:
+    """The reference's validation groups (batches of four per window)."""
+    wins = (KVReadWindow * max(1, len(windows)))(*[KVReadWindow(*w) for w in windows])
+    out = (C.c_uint32 * max(1, count))()
+    _raise(lib().hsb_kv_read_groups(wins, len(windows), out, int(count)))
+    return list(out[:count])
 
 
 # ------------------------------------------------------------ delivery

@@ -76,6 +76,13 @@ _SIGNATURES = {
     "hsb_shard_select_workspace_bytes": (SZ, [I, SZ, SZ, SZ]),
     "hsb_shard_select": (I, [P, P, I, SZ, SZ, P, P, SZ, SZ, F, F, P, SZ, P, P, P, P, P, P, P, P, P, SZ, P]),
     "hsb_h2o_group_sums": (I, [P, P, P, SZ, SZ, P, SZ, P, P]),
+    "hsb_segment_extent_bytes": (U64, [SZ, U64, SZ]),
+    "hsb_segment_header": (I, [P, U64, SZ, U64, SZ]),
+    "hsb_fnv1a64": (U64, [P, SZ]),
+    "hsb_kv_records_encode": (I, [P, SZ, SZ, SZ, U64, C.c_uint32, U64, P, P]),
+    "hsb_kv_records_verify": (I, [P, SZ, P, P, P, SZ, U64, C.c_uint32, SZ, P, SZ, P, SZ, P, P]),
+    "hsb_kv_read_plan": (I, [P, SZ, U64, U64, SZ, SZ, C.c_uint, P, SZ, P]),
+    "hsb_kv_read_groups": (I, [P, SZ, P, SZ]),
     "hsb_synth_normal_f16": (I, [P, SZ, U64, F, P]),
     "hsb_synth_normal_bf16": (I, [P, SZ, U64, F, P]),
     "hsb_synth_keys": (I, [P, SZ, SZ, U64, F, F, I, F, P]),

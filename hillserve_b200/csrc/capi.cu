@@ -3,6 +3,7 @@
 // device status read-back, and the fused selected-KV layer step.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cfenv>
 #include <cmath>
 #include <cstdio>
@@ -110,6 +111,11 @@ const char* hsb_status_message(int status) {
     case HSB_E_H2O_ALIGN: return "H2O reduction requires aligned F32 tensor";
     case HSB_E_H2O_GRID: return "H2O reduction exceeds CUDA grid limit";
     case HSB_E_H2O_DEVICE: return "H2O softmax tensor is not on the expected CUDA device";
+    case HSB_E_RECORD_IDENTITY: return "prefetch complete KV record layer/position/request mismatch";
+    case HSB_E_RECORD_CHECKSUM: return "prefetch complete KV checksum mismatch";
+    case HSB_E_RECORD_BOUNDS: return "complete KV record outside the uploaded window or output rows";
+    case HSB_E_SEGMENT_GEOMETRY: return "bounded segmented geometry/quota";
+    case HSB_E_READ_PLAN: return "invalid complete-KV read plan";
     default: return "unknown hsb status";
     }
 }
@@ -748,6 +754,140 @@ int hsb_h2o_group_sums(const void* d_probabilities, const int64_t ne[4], const s
     cudaError_t e = launch_h2o_group_sums(d_probabilities, valid_keys, valid_queries, nb[0], nb[1], nb[2], d_sums,
                                           d_status, as_stream(stream));
     if (e != cudaSuccess) return fail_cuda(e, "H2O attention reduction launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+// ------------------------------------------------- cold-tier KV records
+static bool segment_geometry_ok(size_t layers, uint64_t positions, size_t record_bytes) {
+    // storage/segmented_store.cpp:25
+    return layers && layers <= 128 && positions && positions <= 66048 && record_bytes && record_bytes <= 65536;
+}
+
+uint64_t hsb_segment_extent_bytes(size_t layers, uint64_t positions, size_t record_bytes) {
+    if (!segment_geometry_ok(layers, positions, record_bytes)) return 0;
+    const uint64_t stride = (uint64_t)record_bytes + HSB_RECORD_HEADER_BYTES;
+    return (HSB_SEGMENT_HEADER_BYTES + (uint64_t)layers * positions * stride + 4095) / 4096 * 4096;
+}
+
+int hsb_segment_header(void* header, uint64_t request, size_t layers, uint64_t positions, size_t record_bytes) {
+    if (!header) return fail(HSB_E_INVALID, "null segment header");
+    if (!segment_geometry_ok(layers, positions, record_bytes))
+        return fail(HSB_E_SEGMENT_GEOMETRY, "bounded segmented geometry/quota");
+    // segmented_store.cpp:30: 512 u64 words, the first eight set.
+    uint64_t words[HSB_SEGMENT_HEADER_BYTES / 8] = {};
+    words[0] = 0x48534b5653454731ull;  // "HSKVSEG1"
+    words[1] = 1;
+    words[2] = request;
+    words[3] = layers;
+    words[4] = positions;
+    words[5] = record_bytes;
+    words[6] = (uint64_t)record_bytes + HSB_RECORD_HEADER_BYTES;
+    words[7] = hsb_segment_extent_bytes(layers, positions, record_bytes);
+    std::memcpy(header, words, sizeof words);
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+uint64_t hsb_fnv1a64(const void* data, size_t n) {
+    const unsigned char* p = static_cast<const unsigned char*>(data);
+    uint64_t h = 14695981039346656037ull;
+    for (size_t i = 0; i < n; ++i) h = (h ^ p[i]) * 1099511628211ull;
+    return h;
+}
+
+int hsb_kv_records_encode(const void* d_payload, size_t payload_stride, size_t count, size_t record_bytes,
+                          uint64_t request, uint32_t layer, uint64_t first, void* d_records, void* stream) {
+    if (!record_bytes || record_bytes > 65536)
+        return fail(HSB_E_SEGMENT_GEOMETRY, "bounded segmented geometry/quota");
+    // segmented_store.cpp:98: an empty append is rejected.
+    if (!d_payload || !d_records || !count || payload_stride < record_bytes)
+        return fail(HSB_E_INVALID, "append epoch/size/poisoned state");
+    if (first > std::numeric_limits<uint64_t>::max() - count) return fail(HSB_E_INVALID, "append capacity");
+    cudaError_t e = launch_records_encode(d_payload, payload_stride, count, record_bytes, request, layer, first,
+                                          d_records, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "record encode launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+int hsb_kv_records_verify(const void* d_window, size_t window_bytes, const uint64_t* d_offsets,
+                          const uint64_t* d_positions, const uint32_t* d_groups, size_t count, uint64_t request,
+                          uint32_t layer, size_t record_bytes, void* d_out, size_t out_stride,
+                          const uint32_t* d_out_rows, size_t out_rows_capacity, hsb_device_status* d_status,
+                          void* stream) {
+    if (!record_bytes || record_bytes > 65536)
+        return fail(HSB_E_SEGMENT_GEOMETRY, "bounded segmented geometry/quota");
+    if (!d_status || out_stride < record_bytes || count > 0xffffffffull)
+        return fail(HSB_E_INVALID, "record verify arguments");
+    if (count == 0) {
+        g_last_error.clear();
+        return HSB_OK;
+    }
+    if (!d_window || !d_offsets || !d_positions || !d_out) return fail(HSB_E_INVALID, "record verify arguments");
+    cudaError_t e = launch_records_verify(d_window, window_bytes, d_offsets, d_positions, d_groups, count, request,
+                                          layer, record_bytes, d_out, out_stride, d_out_rows, out_rows_capacity,
+                                          d_status, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "record verify launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+int hsb_kv_read_plan(const uint64_t* offsets, size_t count, uint64_t record_bytes, uint64_t extent,
+                     size_t window_bytes, size_t gap_bytes, unsigned amplification, hsb_kv_read_window* windows,
+                     size_t windows_capacity, size_t* nwindows) {
+    // storage/kv_read_plan.hpp:22-28 (limits), :37-39 (geometry), :41-59 (plan)
+    if (window_bytes < 8192 || window_bytes > 1024 * 1024 || window_bytes % 4096 || gap_bytes > 64 * 1024 ||
+        gap_bytes % 4096 || amplification < 1000 || amplification > 2000)
+        return fail(HSB_E_READ_PLAN, "invalid bounded complete-KV read limits");
+    if (!record_bytes || extent % 4096 || record_bytes > window_bytes - 4095)
+        return fail(HSB_E_READ_PLAN, "invalid complete-KV record geometry");
+    if (!nwindows || (count && (!offsets || !windows))) return fail(HSB_E_INVALID, "read plan arguments");
+    size_t n = 0;
+    uint64_t previous_end = 0, last_page_end = 0;
+    for (size_t i = 0; i < count; ++i) {
+        const uint64_t offset = offsets[i];
+        if (offset > extent || record_bytes > extent - offset || (i && offset < previous_end))
+            return fail(HSB_E_READ_PLAN, "unordered, overlapping or out-of-extent KV record");
+        previous_end = offset + record_bytes;
+        if (previous_end > std::numeric_limits<uint64_t>::max() - 4095)
+            return fail(HSB_E_READ_PLAN, "complete-KV aligned offset overflow");
+        const uint64_t begin = offset / 4096 * 4096, end = (previous_end + 4095) / 4096 * 4096;
+        if (end > extent) return fail(HSB_E_READ_PLAN, "complete-KV aligned read exceeds extent");
+        bool merged = false;
+        if (n) {
+            hsb_kv_read_window& w = windows[n - 1];
+            const uint64_t required = w.required_page_bytes + end - std::max(begin, last_page_end);
+            const uint64_t span = end - w.begin, gap = begin > w.end ? begin - w.end : 0;
+            if (span <= window_bytes && gap <= gap_bytes && span * 1000 <= required * amplification) {
+                w.end = end;
+                w.required_page_bytes = required;
+                w.end_record = i + 1;
+                merged = true;
+            }
+        }
+        if (!merged) {
+            if (n == windows_capacity) return fail(HSB_E_INVALID, "read plan window capacity");
+            windows[n++] = hsb_kv_read_window{begin, end, end - begin, i, i + 1};
+        }
+        last_page_end = end;
+    }
+    *nwindows = n;
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+int hsb_kv_read_groups(const hsb_kv_read_window* windows, size_t nwindows, uint32_t* groups, size_t count) {
+    if ((nwindows && !windows) || (count && !groups)) return fail(HSB_E_INVALID, "read group arguments");
+    uint64_t next = 0, group = 0;
+    for (size_t w = 0; w < nwindows; ++w) {
+        if (windows[w].first_record != next || windows[w].end_record <= next || windows[w].end_record > count)
+            return fail(HSB_E_READ_PLAN, "read windows do not cover the records in order");
+        for (uint64_t j = windows[w].first_record; j < windows[w].end_record; j += 4, ++group)
+            for (uint64_t k = j; k < std::min<uint64_t>(j + 4, windows[w].end_record); ++k) groups[k] = (uint32_t)group;
+        next = windows[w].end_record;
+    }
+    if (next != count) return fail(HSB_E_READ_PLAN, "read windows do not cover the records in order");
     g_last_error.clear();
     return HSB_OK;
 }

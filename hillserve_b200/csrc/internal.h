@@ -194,6 +194,18 @@ cudaError_t launch_attention_dense(const float* q, const uint16_t* kcache, const
 cudaError_t launch_h2o_group_sums(const void* probs, size_t keys, size_t queries, size_t nb0, size_t nb1,
                                   size_t nb2, float* out, hsb_device_status* status, cudaStream_t stream);
 
+// Cold-tier KV records (storage/segmented_store.cpp): the file image of
+// `count` records from payload rows, and the check + gather of records read
+// back into a device window.  Arguments already validated.
+cudaError_t launch_records_encode(const void* payload, size_t payload_stride, size_t count, size_t record_bytes,
+                                  uint64_t request, uint32_t layer, uint64_t first, void* records,
+                                  cudaStream_t stream);
+cudaError_t launch_records_verify(const void* window, size_t window_bytes, const uint64_t* offsets,
+                                  const uint64_t* positions, const uint32_t* groups, size_t count, uint64_t request,
+                                  uint32_t layer, size_t record_bytes, void* out, size_t out_stride,
+                                  const uint32_t* out_rows, size_t out_capacity, hsb_device_status* status,
+                                  cudaStream_t stream);
+
 // Rehearsal query
 cudaError_t launch_rehearsal(const uint16_t* x, const uint16_t* w, uint64_t position, float theta,
                              float* q32, uint16_t* q16, cudaStream_t stream);

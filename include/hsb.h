@@ -88,7 +88,14 @@ typedef enum hsb_status {
     HSB_E_H2O_OVERFLOW = 83,
     HSB_E_H2O_ALIGN = 84,
     HSB_E_H2O_GRID = 85,
-    HSB_E_H2O_DEVICE = 86
+    HSB_E_H2O_DEVICE = 86,
+    /* cold-tier KV records -- policy/full_gqa_runtime.cpp:395-409,
+     * storage/segmented_store.cpp:24-26,98,116-119, storage/kv_read_plan.hpp:22-59 */
+    HSB_E_RECORD_IDENTITY = 90,
+    HSB_E_RECORD_CHECKSUM = 91,
+    HSB_E_RECORD_BOUNDS = 92,
+    HSB_E_SEGMENT_GEOMETRY = 93,
+    HSB_E_READ_PLAN = 94
 } hsb_status;
 
 int hsb_abi_version(void);
@@ -353,6 +360,62 @@ int hsb_shard_select(const uint16_t* d_order_keys, const uint16_t* d_raw, int kv
 int hsb_h2o_group_sums(const void* d_probabilities, const int64_t ne[4], const size_t nb[4],
                        size_t valid_keys, size_t valid_queries, float* d_sums, size_t capacity_keys,
                        hsb_device_status* d_status, void* stream);
+
+/* ------------------------------------------------- cold-tier KV records
+ * SegmentedKVStore v1 (storage/segmented_store.{hpp,cpp}): a 4096-byte file
+ * header, then the record of (layer, position) at byte
+ *     4096 + (layer * positions + position) * (record_bytes + 32):
+ * a 32-byte header {u64 digest, u64 position, u64 request, u32 layer,
+ * u32 version = 1} and the payload (for this model one K||V row, 4096
+ * bytes).  digest = FNV-1a 64 of the payload (storage/file_store.cpp:12-16).
+ * Geometry bounds as the store's constructor: layers 1..128, positions
+ * 1..66048, record_bytes 1..65536 (segmented_store.cpp:24-26). */
+#define HSB_SEGMENT_HEADER_BYTES 4096
+#define HSB_RECORD_HEADER_BYTES 32
+/* Page-rounded file extent (segmented_store.cpp:26); 0 for invalid geometry. */
+uint64_t hsb_segment_extent_bytes(size_t layers, uint64_t positions, size_t record_bytes);
+/* The 4096-byte file header (segmented_store.cpp:30) into host memory. */
+int hsb_segment_header(void* header, uint64_t request, size_t layers, uint64_t positions, size_t record_bytes);
+/* FNV-1a 64 of n host bytes (storage/file_store.cpp:12-16). */
+uint64_t hsb_fnv1a64(const void* data, size_t n);
+/* Device: the file image of records (layer, first .. first+count-1), i.e.
+ * the bytes SegmentedKVStore::append writes (segmented_store.cpp:95-104),
+ * contiguous at d_records (count * (record_bytes + 32) bytes), from payload
+ * rows d_payload + i * payload_stride. */
+int hsb_kv_records_encode(const void* d_payload, size_t payload_stride, size_t count, size_t record_bytes,
+                          uint64_t request, uint32_t layer, uint64_t first, void* d_records, void* stream);
+/* Device: checks records read back from the file into d_window (window_bytes
+ * of raw file bytes) and copies their payloads to device rows.  Record i
+ * starts at d_window + d_offsets[i]; it must carry position d_positions[i],
+ * `request`, `layer` and version 1 (else HSB_E_RECORD_IDENTITY) and a digest
+ * equal to the FNV-1a of its payload (else HSB_E_RECORD_CHECKSUM), checked
+ * in that order as policy/full_gqa_runtime.cpp:395-409 does.  The payload
+ * goes to d_out + row * out_stride, row = d_out_rows ? d_out_rows[i] : i
+ * (< out_rows_capacity, else HSB_E_RECORD_BOUNDS, as for a record outside
+ * the window).  The first failure in the reference's order is written to
+ * *d_status: by validation group (d_groups[i], the reference's batches of
+ * four per read window -- hsb_kv_read_groups; NULL: one group per record,
+ * SegmentedKVStore::fetch's order), identity before checksum, then index. */
+int hsb_kv_records_verify(const void* d_window, size_t window_bytes, const uint64_t* d_offsets,
+                          const uint64_t* d_positions, const uint32_t* d_groups, size_t count, uint64_t request,
+                          uint32_t layer, size_t record_bytes, void* d_out, size_t out_stride,
+                          const uint32_t* d_out_rows, size_t out_rows_capacity, hsb_device_status* d_status,
+                          void* stream);
+/* Host: the bounded read plan of storage/kv_read_plan.hpp:34-59 over
+ * records at ascending file offsets (record_bytes here includes the 32-byte
+ * header, as the reference passes it).  Limits as KVReadLimits (defaults
+ * 1 MiB window, 16 KiB gap, 1500 permille). */
+typedef struct hsb_kv_read_window {
+    uint64_t begin, end, required_page_bytes;
+    uint64_t first_record, end_record;
+} hsb_kv_read_window;
+int hsb_kv_read_plan(const uint64_t* offsets, size_t count, uint64_t record_bytes, uint64_t extent,
+                     size_t window_bytes, size_t gap_bytes, unsigned max_amplification_permille,
+                     hsb_kv_read_window* windows, size_t windows_capacity, size_t* nwindows);
+/* Host: the reference's validation groups for hsb_kv_records_verify: records
+ * of each window in batches of four from the window's first record
+ * (policy/full_gqa_runtime.cpp:394-395); groups[i] for i < count. */
+int hsb_kv_read_groups(const hsb_kv_read_window* windows, size_t nwindows, uint32_t* groups, size_t count);
 
 /* ------------------------------------------------------ synthetic inputs
  * Benchmark inputs, not part of the reference interface: seeded F16 normal

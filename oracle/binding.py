@@ -67,6 +67,11 @@ def oracle() -> C.CDLL:
         lib.orc_rehearsal.restype = None
         lib.orc_h2o_group_sums.argtypes = [P, SZ, SZ, SZ, SZ, SZ, P]
         lib.orc_h2o_group_sums.restype = None
+        lib.orc_fnv1a64.argtypes = [P, SZ]
+        lib.orc_fnv1a64.restype = C.c_uint64
+        lib.orc_kv_records_encode.argtypes = [P, SZ, SZ, SZ, C.c_uint64, C.c_uint32, C.c_uint64, P]
+        lib.orc_kv_records_encode.restype = None
+        lib.orc_kv_records_verify.argtypes = [P, SZ, P, P, P, SZ, C.c_uint64, C.c_uint32, SZ, P, SZ, P, SZ, P]
         _oracle = lib
     return _oracle
 
@@ -103,6 +108,14 @@ def ref() -> C.CDLL:
         lib.ref_h2o_observe_group_sums.argtypes = [P, SZ, SZ, SZ, SZ, P, SZ, C.c_char_p, SZ]
         lib.ref_h2o_importance.argtypes = [P, SZ, SZ, SZ, P, C.c_char_p, SZ]
         lib.ref_h2o_resident_ids.argtypes = [P, SZ, P, SZ, P, C.c_char_p, SZ]
+        lib.ref_checksum.restype = C.c_uint64
+        lib.ref_checksum.argtypes = [P, SZ]
+        lib.ref_checksum_four.argtypes = [P, SZ, SZ, P, C.c_char_p, SZ]
+        lib.ref_checksum_records.argtypes = [P, P, SZ, SZ, P]
+        lib.ref_checksum_records.restype = None
+        lib.ref_read_plan.argtypes = [P, SZ, C.c_uint64, C.c_uint64, SZ, SZ, C.c_uint, P, SZ, P, C.c_char_p, SZ]
+        lib.ref_segment_roundtrip.argtypes = [C.c_char_p, C.c_uint64, SZ, C.c_uint64, SZ, C.c_uint64, P, P,
+                                              C.c_longlong, C.c_ubyte, SZ, P, SZ, P, C.c_char_p, SZ]
         _ref = lib
     return _ref
 
@@ -411,3 +424,94 @@ class RefH2O:
         if ref().ref_h2o_resident_ids(self.h, layer, _p(out), capacity, _p(sizes), e, 512):
             raise ReferenceError_(e.value.decode())
         return [out[h, :int(sizes[h])].tolist() for h in range(self.kv_heads)]
+
+
+# ------------------------------------------------------------ KV records
+def fnv1a64(data) -> int:
+    b = np.ascontiguousarray(np.frombuffer(bytes(data), dtype=np.uint8) if isinstance(data, (bytes, bytearray))
+                             else data).view(np.uint8)
+    return int(oracle().orc_fnv1a64(_p(b), b.nbytes))
+
+
+def records_encode(payload: np.ndarray, count: int, record_bytes: int, request: int, layer: int, first: int,
+                   payload_stride: int | None = None) -> np.ndarray:
+    """storage/segmented_store.cpp:95-104: the file image of `count` records."""
+    payload = np.ascontiguousarray(payload).view(np.uint8).reshape(-1)
+    stride = record_bytes if payload_stride is None else payload_stride
+    assert payload.nbytes >= (count - 1) * stride + record_bytes
+    out = np.empty(count * (record_bytes + 32), dtype=np.uint8)
+    oracle().orc_kv_records_encode(_p(payload), stride, count, record_bytes, request, layer, first, _p(out))
+    return out
+
+
+def records_verify(window: np.ndarray, offsets, positions, request: int, layer: int, record_bytes: int,
+                   groups=None, out_rows=None, out_capacity: int | None = None):
+    """Returns (code, index, rows [capacity][record_bytes]) walking the
+    reference's validation loop (policy/full_gqa_runtime.cpp:394-409)."""
+    window = np.ascontiguousarray(window).view(np.uint8).reshape(-1)
+    off = np.ascontiguousarray(offsets, dtype=np.uint64)
+    pos = np.ascontiguousarray(positions, dtype=np.uint64)
+    grp = None if groups is None else np.ascontiguousarray(groups, dtype=np.uint32)
+    rows = None if out_rows is None else np.ascontiguousarray(out_rows, dtype=np.uint32)
+    cap = len(off) if out_capacity is None else out_capacity
+    out = np.zeros((max(cap, 1), record_bytes), dtype=np.uint8)
+    idx = np.zeros(1, dtype=np.uint32)
+    code = oracle().orc_kv_records_verify(_p(window), window.nbytes, _p(off), _p(pos), _p(grp), len(off), request,
+                                          layer, record_bytes, _p(out), record_bytes, _p(rows), cap, _p(idx))
+    return int(code), int(idx[0]), out[:cap]
+
+
+def ref_checksum(data: np.ndarray) -> int:
+    data = np.ascontiguousarray(data).view(np.uint8)
+    return int(ref().ref_checksum(_p(data), data.nbytes))
+
+
+def ref_checksum_four(rows: list, nbytes: int) -> list:
+    arrs = [np.ascontiguousarray(r).view(np.uint8) for r in rows]
+    ptrs = (C.c_void_p * 4)(*[a.ctypes.data for a in arrs])
+    out = np.zeros(4, dtype=np.uint64)
+    e = _err()
+    if ref().ref_checksum_four(ptrs, nbytes, len(arrs), _p(out), e, 512):
+        raise ReferenceError_(e.value.decode())
+    return [int(x) for x in out[:len(arrs)]]
+
+
+def ref_checksum_records(base: np.ndarray, offsets, nbytes: int) -> np.ndarray:
+    """The reference runtime's four-at-a-time digest loop over payloads at
+    base + offsets[i] (policy/full_gqa_runtime.cpp:394-408)."""
+    base = np.ascontiguousarray(base).view(np.uint8)
+    off = np.ascontiguousarray(offsets, dtype=np.uint64)
+    assert len(off) == 0 or int(off.max()) + nbytes <= base.nbytes
+    out = np.zeros(len(off), dtype=np.uint64)
+    ref().ref_checksum_records(_p(base), _p(off), len(off), nbytes, _p(out))
+    return out
+
+
+def ref_read_plan(offsets, record_bytes: int, extent: int, window_bytes: int = 1 << 20, gap_bytes: int = 16384,
+                  amplification: int = 1500) -> np.ndarray:
+    off = np.ascontiguousarray(offsets, dtype=np.uint64)
+    out = np.zeros((max(len(off), 1), 5), dtype=np.uint64)
+    n = C.c_size_t(0)
+    e = _err()
+    if ref().ref_read_plan(_p(off), len(off), record_bytes, extent, window_bytes, gap_bytes, amplification,
+                           _p(out), out.shape[0], C.byref(n), e, 512):
+        raise ReferenceError_(e.value.decode())
+    return out[:n.value]
+
+
+def ref_segment_roundtrip(path: str, request: int, layers: int, positions: int, record_bytes: int, quota: int,
+                          payloads: list, mutate_offset: int = -1, mutate_xor: int = 0, fetch_layer: int = 0,
+                          ids=()) -> np.ndarray:
+    """The reference SegmentedKVStore writes payloads[l] (rows of layer l from
+    position 0) to a new file at `path`, optionally flips one byte, then
+    fetches `ids` of `fetch_layer`; returns the fetched bytes."""
+    arrs = [np.ascontiguousarray(p).view(np.uint8).reshape(-1) for p in payloads]
+    ptrs = (C.c_void_p * layers)(*[a.ctypes.data if a.size else 0 for a in arrs])
+    counts = np.array([a.nbytes // record_bytes for a in arrs], dtype=np.uint64)
+    want = np.ascontiguousarray(ids, dtype=np.uint64)
+    out = np.zeros(max(1, len(want) * record_bytes), dtype=np.uint8)
+    e = _err()
+    if ref().ref_segment_roundtrip(path.encode(), request, layers, positions, record_bytes, quota, ptrs, _p(counts),
+                                   mutate_offset, mutate_xor, fetch_layer, _p(want), len(want), _p(out), e, 512):
+        raise ReferenceError_(e.value.decode())
+    return out[:len(want) * record_bytes]

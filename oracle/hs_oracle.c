@@ -588,3 +588,72 @@ void orc_h2o_group_sums(const void* probabilities, size_t keys, size_t queries, 
         }
     }
 }
+
+/* ------------------------------------------------------------- records */
+uint64_t orc_fnv1a64(const void* data, size_t n) {
+    const unsigned char* p = (const unsigned char*)data;
+    uint64_t h = 14695981039346656037ull;
+    for (size_t i = 0; i < n; ++i) {
+        h ^= p[i];
+        h *= 1099511628211ull;
+    }
+    return h;
+}
+
+typedef struct {
+    uint64_t digest, position, request;
+    uint32_t layer, version;
+} orc_record_header;
+
+void orc_kv_records_encode(const void* payload, size_t payload_stride, size_t count, size_t record_bytes,
+                           uint64_t request, uint32_t layer, uint64_t first, void* records) {
+    const unsigned char* src = (const unsigned char*)payload;
+    unsigned char* dst = (unsigned char*)records;
+    for (size_t i = 0; i < count; ++i) {
+        const unsigned char* row = src + i * payload_stride;
+        unsigned char* rec = dst + i * (record_bytes + 32);
+        orc_record_header h = {orc_fnv1a64(row, record_bytes), first + i, request, layer, 1u};
+        memcpy(rec, &h, 32);
+        memcpy(rec + 32, row, record_bytes);
+    }
+}
+
+int orc_kv_records_verify(const void* window, size_t window_bytes, const uint64_t* offsets,
+                          const uint64_t* positions, const uint32_t* groups, size_t count, uint64_t request,
+                          uint32_t layer, size_t record_bytes, void* out, size_t out_stride,
+                          const uint32_t* out_rows, size_t out_capacity, uint32_t* error_index) {
+    const unsigned char* base = (const unsigned char*)window;
+    unsigned char* dst = (unsigned char*)out;
+    size_t g0 = 0;
+    while (g0 < count) {  /* one validation group: records g0 .. g1-1 */
+        size_t g1 = g0 + 1;
+        while (groups && g1 < count && groups[g1] == groups[g0]) ++g1;
+        /* bounds (our own guard), then identities, then checksums */
+        for (size_t i = g0; i < g1; ++i) {
+            const size_t row = out_rows ? out_rows[i] : i;
+            if (offsets[i] > window_bytes || window_bytes - offsets[i] < record_bytes + 32 || row >= out_capacity) {
+                *error_index = (uint32_t)i;
+                return 92;
+            }
+        }
+        for (size_t i = g0; i < g1; ++i) {
+            orc_record_header h;
+            memcpy(&h, base + offsets[i], 32);
+            if (h.position != positions[i] || h.request != request || h.layer != layer || h.version != 1) {
+                *error_index = (uint32_t)i;
+                return 90;
+            }
+            memcpy(dst + (out_rows ? out_rows[i] : i) * out_stride, base + offsets[i] + 32, record_bytes);
+        }
+        for (size_t i = g0; i < g1; ++i) {
+            orc_record_header h;
+            memcpy(&h, base + offsets[i], 32);
+            if (orc_fnv1a64(base + offsets[i] + 32, record_bytes) != h.digest) {
+                *error_index = (uint32_t)i;
+                return 91;
+            }
+        }
+        g0 = g1;
+    }
+    return 0;
+}

@@ -135,6 +135,25 @@ void orc_attention_packed_f32(const uint16_t* k, const uint16_t* v, const float*
 void orc_h2o_group_sums(const void* probabilities, size_t keys, size_t queries, size_t nb0, size_t nb1,
                         size_t nb2, float* out);
 
+/* Cold-tier KV records (SegmentedKVStore v1).
+ * FNV-1a 64, storage/file_store.cpp:12-16. */
+uint64_t orc_fnv1a64(const void* data, size_t n);
+/* The bytes SegmentedKVStore::append writes for records (layer, first + i),
+ * storage/segmented_store.cpp:95-104: {digest, position, request, layer,
+ * version 1} then the payload, count * (record_bytes + 32) bytes. */
+void orc_kv_records_encode(const void* payload, size_t payload_stride, size_t count, size_t record_bytes,
+                           uint64_t request, uint32_t layer, uint64_t first, void* records);
+/* Checks records at window + offsets[i] and copies their payloads to
+ * out + row * out_stride (row = out_rows ? out_rows[i] : i), walking the
+ * reference's validation loop (policy/full_gqa_runtime.cpp:394-409):
+ * records in validation groups (groups[i]; NULL: one per record), each
+ * group's identity checks before its checksums.  Returns 0 or the first
+ * error (90 identity, 91 checksum, 92 bounds) and its record index. */
+int orc_kv_records_verify(const void* window, size_t window_bytes, const uint64_t* offsets,
+                          const uint64_t* positions, const uint32_t* groups, size_t count, uint64_t request,
+                          uint32_t layer, size_t record_bytes, void* out, size_t out_stride,
+                          const uint32_t* out_rows, size_t out_capacity, uint32_t* error_index);
+
 #ifdef __cplusplus
 }
 #endif

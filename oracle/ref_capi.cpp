@@ -2,7 +2,8 @@
 //
 // A thin C-ABI bridge, compiled together with the UNMODIFIED reference
 // HillServe sources (policy/host_policy.cpp, policy/full_gqa_cpu.cpp,
-// policy/gqa_policy.cpp, smartssd/adapter.cpp, policy/h2o_residency.cpp and the header-only
+// policy/gqa_policy.cpp, smartssd/adapter.cpp, policy/h2o_residency.cpp,
+// storage/{file_store,segmented_store}.cpp and the header-only
 // runtime/gqa_pack.hpp) into oracle/_ref/libhs_ref.so by oracle/Makefile.
 // It lets the tests pin the C oracle against the reference's own code on
 // seeded inputs, and lets bench.py time the reference CPU path.  Nothing in
@@ -12,7 +13,15 @@
 #include "policy/host_policy.hpp"
 #include "runtime/gqa_pack.hpp"
 #include "policy/h2o_residency.hpp"
+#include "storage/file_store.hpp"
+#include "storage/kv_checksum.hpp"
+#include "storage/kv_read_plan.hpp"
+#include "storage/segmented_store.hpp"
 
+#include <fcntl.h>
+#include <unistd.h>
+
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -225,6 +234,100 @@ int ref_h2o_resident_ids(void* h, std::size_t layer, std::uint64_t* out, std::si
     } catch (const std::exception& e) {
         copy_error(e, err, errlen);
         return -1;
+    }
+}
+
+// checksum -- storage/file_store.cpp:12-16
+std::uint64_t ref_checksum(const void* data, std::size_t n) { return hillserve::checksum(data, n); }
+// checksum_four -- storage/kv_checksum.hpp:11-23
+int ref_checksum_four(const unsigned char* const* rows, std::size_t bytes, std::size_t count, std::uint64_t* out,
+                      char* err, std::size_t errlen) {
+    try {
+        std::array<const unsigned char*, 4> r{};
+        for (std::size_t i = 0; i < count && i < 4; ++i) r[i] = rows[i];
+        const auto h = hillserve::storage::checksum_four(r, bytes, count);
+        for (std::size_t i = 0; i < count; ++i) out[i] = h[i];
+        return 0;
+    } catch (const std::exception& e) {
+        copy_error(e, err, errlen);
+        return -1;
+    }
+}
+// plan_kv_reads -- storage/kv_read_plan.hpp:34-59; windows as 5 u64 each.
+int ref_read_plan(const std::uint64_t* offsets, std::size_t count, std::uint64_t record_bytes,
+                  std::uint64_t extent, std::size_t window_bytes, std::size_t gap_bytes, unsigned amplification,
+                  std::uint64_t* windows, std::size_t capacity, std::size_t* n, char* err, std::size_t errlen) {
+    try {
+        std::vector<hillserve::storage::KVReadRecord> records(count);
+        for (std::size_t i = 0; i < count; ++i) records[i] = {offsets[i], i};
+        hillserve::storage::KVReadLimits limits;
+        limits.window_bytes = window_bytes;
+        limits.gap_bytes = gap_bytes;
+        limits.max_amplification_permille = amplification;
+        const auto w = hillserve::storage::plan_kv_reads(records, record_bytes, extent, limits);
+        if (w.size() > capacity) throw std::runtime_error("bridge window capacity");
+        for (std::size_t i = 0; i < w.size(); ++i) {
+            windows[5 * i + 0] = w[i].begin;
+            windows[5 * i + 1] = w[i].end;
+            windows[5 * i + 2] = w[i].required_page_bytes;
+            windows[5 * i + 3] = w[i].first_record;
+            windows[5 * i + 4] = w[i].end_record;
+        }
+        *n = w.size();
+        return 0;
+    } catch (const std::exception& e) {
+        copy_error(e, err, errlen);
+        return -1;
+    }
+}
+// SegmentedKVStore (storage/segmented_store.cpp): creates the store file at
+// `path`, appends per layer l the `counts[l]` records of payload rows
+// payload[l] (record_bytes each, positions 0..), drains, then (optionally)
+// XORs one byte of the file at mutate_offset (when >= 0) and fetches `nids`
+// positions of `fetch_layer` into out.  The file stays for the caller.
+int ref_segment_roundtrip(const char* path, std::uint64_t request, std::size_t layers, std::uint64_t positions,
+                          std::size_t record_bytes, std::uint64_t quota, const unsigned char* const* payload,
+                          const std::uint64_t* counts, long long mutate_offset, unsigned char mutate_xor,
+                          std::size_t fetch_layer, const std::uint64_t* ids, std::size_t nids, unsigned char* out,
+                          char* err, std::size_t errlen) {
+    try {
+        hillserve::SegmentedKVStore store(path, request, layers, positions, record_bytes, quota);
+        for (std::size_t l = 0; l < layers; ++l) {
+            if (!counts[l]) continue;
+            std::vector<std::uint8_t> rows(payload[l], payload[l] + counts[l] * record_bytes);
+            store.append(l, 0, rows);
+        }
+        store.drain();
+        if (mutate_offset >= 0) {
+            const int fd = open(path, O_RDWR | O_CLOEXEC);
+            if (fd < 0) throw std::runtime_error("bridge reopen");
+            unsigned char b = 0;
+            const bool ok = pread(fd, &b, 1, mutate_offset) == 1 && (b ^= mutate_xor, pwrite(fd, &b, 1, mutate_offset) == 1);
+            close(fd);
+            if (!ok) throw std::runtime_error("bridge mutate");
+        }
+        if (nids) {
+            std::vector<std::uint64_t> want(ids, ids + nids);
+            const auto data = store.fetch(fetch_layer, want, nids * record_bytes);
+            std::memcpy(out, data.data(), data.size());
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        copy_error(e, err, errlen);
+        return -1;
+    }
+}
+// The runtime's integrity loop (policy/full_gqa_runtime.cpp:394-408): the
+// digests of `count` payloads at base + offsets[i], four at a time through
+// checksum_four; bench.py times it as the reference's CPU cost.
+void ref_checksum_records(const unsigned char* base, const std::uint64_t* offsets, std::size_t count,
+                          std::size_t bytes, std::uint64_t* out) {
+    for (std::size_t j = 0; j < count; j += 4) {
+        const std::size_t n = std::min<std::size_t>(4, count - j);
+        std::array<const unsigned char*, 4> rows{};
+        for (std::size_t k = 0; k < n; ++k) rows[k] = base + offsets[j + k];
+        const auto h = hillserve::storage::checksum_four(rows, bytes, n);
+        for (std::size_t k = 0; k < n; ++k) out[j + k] = h[k];
     }
 }
 }

@@ -3,7 +3,7 @@ own CPU code (oracle/_ref/libhs_ref.so, compiled from the HillServe sources by
 oracle/Makefile) on seeded inputs.  Run here, where the reference sources
 exist:
 
-    make -C oracle && python tests/golden/make_golden.py [--only h2o]
+    make -C oracle && python tests/golden/make_golden.py [--only h2o|records]
 
 Inputs are regenerated bit-exactly from their seeds by tests/inputs.py, so
 the fixtures hold only input digests and the reference's outputs.
@@ -78,12 +78,72 @@ def h2o_vectors() -> None:
                         importance_digest=np.array(digests), importance_head=np.stack(heads))
 
 
+# (request, layers, positions, record_bytes, rows per layer) of the record fixture
+RECORD_CASES = ((991, 3, 70, 4096, (70, 33, 0)), (765, 2, 37, 100, (37, 5)), (7, 1, 9, 4128, (9,)))
+
+
+def record_case(i: int):
+    request, layers, positions, nbytes, rows = RECORD_CASES[i]
+    payloads = [inputs.record_payload(100 * i + l, r, nbytes) for l, r in enumerate(rows)]
+    return request, layers, positions, nbytes, payloads
+
+
+def plan_case(seed: int):
+    """Seeded sorted record offsets of one layer of a 32 x 4096-position store
+    (stride 4128) and read limits, in the shape of kv_read_plan_tests.cpp."""
+    rng = np.random.default_rng(seed)
+    capacity, stride = 4096, 4128
+    extent = (4096 + 32 * capacity * stride + 4095) // 4096 * 4096
+    layer = int(rng.integers(0, 32))
+    n = int(rng.integers(1, 600))
+    ids = np.sort(rng.choice(capacity, size=n, replace=False))
+    offsets = (4096 + (layer * capacity + ids) * stride).astype(np.uint64)
+    window = int(rng.choice([12288, 65536, 1 << 20]))
+    gap = int(rng.choice([0, 4096, 16384, 65536]))
+    amp = int(rng.choice([1000, 1250, 1500, 2000]))
+    return offsets, stride, extent, window, gap, amp
+
+
+def records_vectors() -> None:
+    import tempfile
+
+    fields = {}
+    # checksum_four over the reference reader test's bytes (direct_read_batch_tests.cpp:17-19)
+    i = np.arange(4 * 65536, dtype=np.uint64)
+    data = ((i // 4096 * 31 + i * 17) % 251).astype(np.uint8)
+    rows = [data[j * 65536:(j + 1) * 65536] for j in range(4)]
+    four = []
+    for length in (0, 1, 17, 4096, 65536):
+        for n in range(1, 5):
+            four.append(ob.ref_checksum_four(rows[:n], length) + [0] * (4 - n))
+    fields["checksum_four"] = np.array(four, dtype=np.uint64)
+    # whole store files written by the reference SegmentedKVStore
+    with tempfile.TemporaryDirectory() as tmp:
+        for c in range(len(RECORD_CASES)):
+            request, layers, positions, nbytes, payloads = record_case(c)
+            path = f"{tmp}/store{c}"
+            ob.ref_segment_roundtrip(path, request, layers, positions, nbytes, 9 << 30, payloads)
+            fields[f"file{c}_digest"] = inputs.digest(np.fromfile(path, dtype=np.uint8))
+    # read plans
+    plans = []
+    for seed in range(24):
+        offsets, stride, extent, window, gap, amp = plan_case(seed)
+        plans.append(inputs.digest(ob.ref_read_plan(offsets, stride, extent, window, gap, amp)))
+    fields["plan_digest"] = np.array(plans)
+    np.savez_compressed(OUT / "records_vectors.npz", **fields)
+
+
 def main() -> None:
     assert ob.reference_available(), "build oracle/_ref first (make -C oracle)"
     if sys.argv[1:] == ["--only", "h2o"]:
         h2o_vectors()
         print("h2o fixture written to", OUT)
         return
+    if sys.argv[1:] == ["--only", "records"]:
+        records_vectors()
+        print("records fixture written to", OUT)
+        return
+    records_vectors()
     # ---- 0. H2O group sums through the reference's CPU policy
     h2o_vectors()
     # ---- 1. reference scorer test vectors

@@ -157,3 +157,29 @@ def h2o_layout(p: np.ndarray, ne0: int, ne1: int, nb0: int, nb1: int, nb2: int, 
     assert np.all(offs % 4 == 0)
     buf.view(np.float32)[offs // 4] = p.reshape(-1)
     return buf
+
+
+def record_payload(seed: int, rows: int, record_bytes: int) -> np.ndarray:
+    """Seeded payload bytes, uint8 [rows][record_bytes] (splitmix64 stream)."""
+    n = (rows * record_bytes + 7) // 8
+    x = splitmix64(np.arange(n, dtype=np.uint64) + np.uint64((seed * 0xD1B54A32D192ED03) % (1 << 64)))
+    return x.view(np.uint8)[:rows * record_bytes].reshape(rows, record_bytes).copy()
+
+
+def segment_image(request: int, layers: int, positions: int, record_bytes: int, payloads: list,
+                  encode) -> np.ndarray:
+    """The SegmentedKVStore v1 file holding payloads[l] at positions 0.. of
+    layer l: a 4096-byte header, records at 4096 + (l*positions+p)*(B+32),
+    zeros elsewhere, page-rounded extent.  `encode` makes the records."""
+    stride = record_bytes + 32
+    extent = (4096 + layers * positions * stride + 4095) // 4096 * 4096
+    img = np.zeros(extent, dtype=np.uint8)
+    words = np.zeros(512, dtype=np.uint64)
+    words[:8] = [0x48534B5653454731, 1, request, layers, positions, record_bytes, stride, extent]
+    img[:4096] = words.view(np.uint8)
+    for l, rows in enumerate(payloads):
+        if len(rows):
+            recs = encode(rows, len(rows), record_bytes, request, l, 0)
+            start = 4096 + l * positions * stride
+            img[start:start + recs.nbytes] = recs
+    return img
