@@ -455,11 +455,11 @@ def kv_records_encode(payload, count: int, record_bytes: int, request: int, laye
 
 def kv_records_verify(window, offsets, positions, request: int, layer: int, record_bytes: int, out,
                       groups=None, out_rows=None, check: bool = True, stream=None):
-    """Checks records of a device window and gathers their payloads into
-    `out` (rows of record_bytes).  offsets / positions: uint64 (int64)
+    """Checks records of a window (device memory, or pinned host memory read
+    in place) and gathers their payloads into the device rows `out`.  offsets / positions: uint64 (int64)
     device tensors; groups, out_rows: optional int32 device tensors.
     Raises the reference's error (check=True) or returns the status tensor."""
-    st = _status_buffer(window.device)
+    st = _status_buffer(out.device)
     count = int(offsets.numel())
     stride = out.stride(0) * out.element_size() if out.dim() > 1 else int(record_bytes)
     capacity = out.numel() * out.element_size() // stride

@@ -825,6 +825,17 @@ int hsb_kv_records_verify(const void* d_window, size_t window_bytes, const uint6
         return HSB_OK;
     }
     if (!d_window || !d_offsets || !d_positions || !d_out) return fail(HSB_E_INVALID, "record verify arguments");
+    // The window is device memory, or pinned host memory the kernel reads in
+    // place over the bus (mapped at the same address); never pageable memory.
+    cudaPointerAttributes wa{};
+    if (cudaPointerGetAttributes(&wa, d_window) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(HSB_E_INVALID, "record window is not device or pinned host memory");
+    }
+    const bool device_window = wa.type == cudaMemoryTypeDevice || wa.type == cudaMemoryTypeManaged;
+    const bool mapped_host = wa.type == cudaMemoryTypeHost && wa.devicePointer == d_window;
+    if (!device_window && !mapped_host)
+        return fail(HSB_E_INVALID, "record window is not device or pinned host memory");
     cudaError_t e = launch_records_verify(d_window, window_bytes, d_offsets, d_positions, d_groups, count, request,
                                           layer, record_bytes, d_out, out_stride, d_out_rows, out_rows_capacity,
                                           d_status, as_stream(stream));

@@ -47,25 +47,39 @@ __device__ __forceinline__ void fnv_word(Fnv& h, uint32_t x) {
 }
 __device__ __forceinline__ uint64_t fnv_value(const Fnv& h) { return ((uint64_t)h.hi << 32) | h.lo; }
 
-// Hashes `bytes` bytes from src and copies them to dst (either may be
-// unaligned: vector path only when both are 16-byte aligned and bytes % 16
-// == 0, decided by the caller through `vec`).
+// Hashes `bytes` bytes from src and copies them to dst (dst may be null).
+// Vector path (src, dst 16-byte aligned, bytes % 16 == 0, chosen by the
+// caller through `vec`): the payload moves a 128-byte line (eight 16-byte
+// loads) at a time, the next line's loads in flight while the current line
+// is hashed, so one record's ~800 cycles of hashing per line cover the
+// memory latency of the next.
 __device__ uint64_t hash_copy(const unsigned char* __restrict__ src, unsigned char* __restrict__ dst, size_t bytes,
                               bool vec) {
     Fnv h{(uint32_t)kFnvSeed, (uint32_t)(kFnvSeed >> 32)};
     if (vec) {
+        constexpr int kLine = 8;  // 16-byte chunks per line
         const uint4* s = reinterpret_cast<const uint4*>(src);
         uint4* d = reinterpret_cast<uint4*>(dst);
         const size_t n = bytes / 16;
-        uint4 next = n ? __ldcs(s) : make_uint4(0, 0, 0, 0);
-        for (size_t i = 0; i < n; ++i) {
-            const uint4 cur = next;
-            if (i + 1 < n) next = __ldcs(s + i + 1);  // the next load is in flight while this one is hashed
-            if (d) d[i] = cur;
-            fnv_word(h, cur.x);
-            fnv_word(h, cur.y);
-            fnv_word(h, cur.z);
-            fnv_word(h, cur.w);
+        uint4 cur[kLine], nxt[kLine];
+#pragma unroll
+        for (int c = 0; c < kLine; ++c) cur[c] = (size_t)c < n ? __ldg(s + c) : make_uint4(0, 0, 0, 0);
+        for (size_t j = 0; j < n; j += kLine) {
+#pragma unroll
+            for (int c = 0; c < kLine; ++c)
+                nxt[c] = j + kLine + c < n ? __ldg(s + j + kLine + c) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int c = 0; c < kLine; ++c) {
+                if (j + c < n) {
+                    if (d) d[j + c] = cur[c];
+                    fnv_word(h, cur[c].x);
+                    fnv_word(h, cur[c].y);
+                    fnv_word(h, cur[c].z);
+                    fnv_word(h, cur[c].w);
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < kLine; ++c) cur[c] = nxt[c];
         }
     } else {
         for (size_t i = 0; i < bytes; ++i) {

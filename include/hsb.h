@@ -395,7 +395,11 @@ int hsb_kv_records_encode(const void* d_payload, size_t payload_stride, size_t c
  * the window).  The first failure in the reference's order is written to
  * *d_status: by validation group (d_groups[i], the reference's batches of
  * four per read window -- hsb_kv_read_groups; NULL: one group per record,
- * SegmentedKVStore::fetch's order), identity before checksum, then index. */
+ * SegmentedKVStore::fetch's order), identity before checksum, then index.
+ * d_window may also be pinned host memory (the read buffers themselves,
+ * mapped at the same address): the kernel then reads only the records'
+ * bytes across the bus, with no staging copy.  Pageable memory is rejected
+ * (HSB_E_INVALID). */
 int hsb_kv_records_verify(const void* d_window, size_t window_bytes, const uint64_t* d_offsets,
                           const uint64_t* d_positions, const uint32_t* d_groups, size_t count, uint64_t request,
                           uint32_t layer, size_t record_bytes, void* d_out, size_t out_stride,

@@ -162,3 +162,28 @@ def test_full_size_encode_verify_round_trip(cuda):
     for j, r in enumerate(sample):
         l, p = divmod(int(r), positions)
         assert np.array_equal(recs[j], ob.records_encode(host[j], 1, nbytes, request, l, p))
+
+
+def test_verify_in_place_from_pinned_host_window(cuda):
+    """The verifier reads the records straight from pinned host read buffers;
+    pageable host memory is refused before any launch."""
+    import torch
+    import hillserve_b200 as hsb
+
+    img, payloads, request, positions = _store(4096)
+    ids = np.sort(np.random.default_rng(5).choice(positions, 61, replace=False)).astype(np.uint64)
+    window, offsets, groups = _windows(img, ids, 1, positions, 4096)
+    host = torch.from_numpy(window).pin_memory()
+    out = torch.zeros((len(ids), 4096), dtype=torch.uint8, device="cuda")
+    hsb.kv_records_verify(host, _dev(offsets.astype(np.int64)), _dev(ids.astype(np.int64)), request, 1, 4096, out,
+                          groups=_dev(groups.astype(np.int32)))
+    assert np.array_equal(out.cpu().numpy(), payloads[1][ids.astype(np.int64)])
+    bad = window.copy()
+    bad[int(offsets[17]) + 32 + 9] ^= 1
+    st = hsb.kv_records_verify(torch.from_numpy(bad).pin_memory(), _dev(offsets.astype(np.int64)),
+                               _dev(ids.astype(np.int64)), request, 1, 4096, out, check=False)
+    torch.cuda.synchronize()
+    assert st.cpu().numpy().tolist() == [91, 17]
+    with pytest.raises(hsb.HsbError):
+        hsb.kv_records_verify(torch.from_numpy(window), _dev(offsets.astype(np.int64)), _dev(ids.astype(np.int64)),
+                              request, 1, 4096, out)
