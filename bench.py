@@ -836,7 +836,8 @@ def run_records(args, torch):
     """Cold-tier KV records (SegmentedKVStore v1, FNV-1a 64 per 4096-byte
     K||V record) for one 32-layer sequence at N = 32768.
       encode: the file image of every record of the sequence (the prefill
-              append, 4 GiB of payload), one launch per layer;
+              append, 4 GiB of payload), one launch per layer on four side
+              streams;
       verify: a decode layer's selected cold set (k = 6553 records, 20 % of
               N) and a whole layer (32768 records), read back as the bounded
               read plan's windows, checked and gathered into HBM rows;
@@ -859,11 +860,23 @@ def run_records(args, torch):
     launches = 0
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
+    # One launch per layer, as the layers' appends arrive, spread over four
+    # side streams (the layers are independent), joined back to `s`.
+    side = [torch.cuda.Stream() for _ in range(4)]
+    fork, joins = torch.cuda.Event(), [torch.cuda.Event() for _ in side]
+
     def encode_all():
+        fork.record(s)
+        for q in side:
+            q.wait_event(fork)
         for l in range(layers):
+            q = side[l % len(side)]
             rc = lib.hsb_kv_records_encode(payload[l].data_ptr(), nbytes, positions, nbytes, request, l, 0,
-                                           records.data_ptr() + l * positions * stride, s.cuda_stream)
+                                           records.data_ptr() + l * positions * stride, q.cuda_stream)
             assert rc == 0, lib.hsb_last_error()
+        for q, j in zip(side, joins):
+            j.record(q)
+            s.wait_event(j)
 
     with ClockSampler(torch.cuda.current_device()) as clocks:
         with torch.cuda.stream(s):

@@ -838,7 +838,7 @@ int hsb_kv_records_verify(const void* d_window, size_t window_bytes, const uint6
         return fail(HSB_E_INVALID, "record window is not device or pinned host memory");
     cudaError_t e = launch_records_verify(d_window, window_bytes, d_offsets, d_positions, d_groups, count, request,
                                           layer, record_bytes, d_out, out_stride, d_out_rows, out_rows_capacity,
-                                          d_status, as_stream(stream));
+                                          mapped_host ? 1 : 0, d_status, as_stream(stream));
     if (e != cudaSuccess) return fail_cuda(e, "record verify launch");
     g_last_error.clear();
     return HSB_OK;

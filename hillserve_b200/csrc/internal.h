@@ -203,8 +203,8 @@ cudaError_t launch_records_encode(const void* payload, size_t payload_stride, si
 cudaError_t launch_records_verify(const void* window, size_t window_bytes, const uint64_t* offsets,
                                   const uint64_t* positions, const uint32_t* groups, size_t count, uint64_t request,
                                   uint32_t layer, size_t record_bytes, void* out, size_t out_stride,
-                                  const uint32_t* out_rows, size_t out_capacity, hsb_device_status* status,
-                                  cudaStream_t stream);
+                                  const uint32_t* out_rows, size_t out_capacity, int host_window,
+                                  hsb_device_status* status, cudaStream_t stream);
 
 // Rehearsal query
 cudaError_t launch_rehearsal(const uint16_t* x, const uint16_t* w, uint64_t position, float theta,

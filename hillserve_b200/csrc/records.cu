@@ -28,7 +28,7 @@ namespace hsb {
 namespace {
 
 constexpr uint64_t kFnvSeed = 14695981039346656037ull;
-constexpr int kRecordThreads = 128;
+constexpr int kRecordThreads = 64;  // one record per thread; small blocks spread few records over many SMs
 
 struct Fnv {
     uint32_t lo, hi;
@@ -52,9 +52,10 @@ __device__ __forceinline__ uint64_t fnv_value(const Fnv& h) { return ((uint64_t)
 // caller through `vec`): the payload moves a 128-byte line (eight 16-byte
 // loads) at a time, the next line's loads in flight while the current line
 // is hashed, so one record's ~800 cycles of hashing per line cover the
-// memory latency of the next.
+// memory latency of the next; from device memory the two lines after it
+// are also prefetched to L2 (not from a pinned host window).
 __device__ uint64_t hash_copy(const unsigned char* __restrict__ src, unsigned char* __restrict__ dst, size_t bytes,
-                              bool vec) {
+                              bool vec, bool prefetch) {
     Fnv h{(uint32_t)kFnvSeed, (uint32_t)(kFnvSeed >> 32)};
     if (vec) {
         constexpr int kLine = 8;  // 16-byte chunks per line
@@ -65,6 +66,10 @@ __device__ uint64_t hash_copy(const unsigned char* __restrict__ src, unsigned ch
 #pragma unroll
         for (int c = 0; c < kLine; ++c) cur[c] = (size_t)c < n ? __ldg(s + c) : make_uint4(0, 0, 0, 0);
         for (size_t j = 0; j < n; j += kLine) {
+            // lines j+2 and j+3 start moving into L2 now, so that the next
+            // iterations' loads find them there
+            if (prefetch && j + 2 * kLine < n) asm volatile("prefetch.global.L2 [%0];" ::"l"(s + j + 2 * kLine));
+            if (prefetch && j + 3 * kLine < n) asm volatile("prefetch.global.L2 [%0];" ::"l"(s + j + 3 * kLine));
 #pragma unroll
             for (int c = 0; c < kLine; ++c)
                 nxt[c] = j + kLine + c < n ? __ldg(s + j + kLine + c) : make_uint4(0, 0, 0, 0);
@@ -106,7 +111,7 @@ __global__ void __launch_bounds__(kRecordThreads) records_encode_kernel(
     const unsigned long long i = (unsigned long long)blockIdx.x * kRecordThreads + threadIdx.x;
     if (i >= count) return;
     unsigned char* rec = records + i * (record_bytes + 32);
-    const uint64_t digest = hash_copy(payload + i * payload_stride, rec + 32, record_bytes, vec != 0);
+    const uint64_t digest = hash_copy(payload + i * payload_stride, rec + 32, record_bytes, vec != 0, true);
     RecordHeader h{digest, first + i, request, layer, 1u};
     if (vec) {
         const uint4* w = reinterpret_cast<const uint4*>(&h);
@@ -156,6 +161,7 @@ struct VerifyParams {
     unsigned long long out_capacity;
     hsb_device_status* status;
     int vec;
+    int host_window;  // the window is pinned host memory read in place
 };
 
 __global__ void __launch_bounds__(kRecordThreads) records_verify_kernel(const __grid_constant__ VerifyParams p) {
@@ -180,7 +186,7 @@ __global__ void __launch_bounds__(kRecordThreads) records_verify_kernel(const __
         unsigned char* d = reinterpret_cast<unsigned char*>(&h);
         for (int j = 0; j < 32; ++j) d[j] = rec[j];
     }
-    const uint64_t digest = hash_copy(rec + 32, p.out + row * p.out_stride, p.record_bytes, vec);
+    const uint64_t digest = hash_copy(rec + 32, p.out + row * p.out_stride, p.record_bytes, vec, !p.host_window);
     // The reference checks the record's identity before its digest
     // (policy/full_gqa_runtime.cpp:397-408, segmented_store.cpp:116-119).
     if (h.position != p.positions[i] || h.request != p.request || h.layer != p.layer || h.version != 1u)
@@ -207,8 +213,8 @@ cudaError_t launch_records_encode(const void* payload, size_t payload_stride, si
 cudaError_t launch_records_verify(const void* window, size_t window_bytes, const uint64_t* offsets,
                                   const uint64_t* positions, const uint32_t* groups, size_t count, uint64_t request,
                                   uint32_t layer, size_t record_bytes, void* out, size_t out_stride,
-                                  const uint32_t* out_rows, size_t out_capacity, hsb_device_status* status,
-                                  cudaStream_t stream) {
+                                  const uint32_t* out_rows, size_t out_capacity, int host_window,
+                                  hsb_device_status* status, cudaStream_t stream) {
     VerifyParams p{};
     p.window = static_cast<const unsigned char*>(window);
     p.window_bytes = window_bytes;
@@ -224,6 +230,7 @@ cudaError_t launch_records_verify(const void* window, size_t window_bytes, const
     p.out_rows = out_rows;
     p.out_capacity = out_capacity;
     p.status = status;
+    p.host_window = host_window;
     p.vec = aligned16(window) && aligned16(out) && out_stride % 16 == 0 && record_bytes % 16 == 0;
     const size_t blocks = (count + kRecordThreads - 1) / kRecordThreads;
     return launch_dependent(records_verify_kernel, dim3((unsigned)blocks), dim3(kRecordThreads), 0, stream, false, p);
