@@ -58,6 +58,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--h2o-keys", type=int, default=32768, help="h2o workload: keys N")
     ap.add_argument("--h2o-queries", default="1,16,512", help="h2o workload: comma-separated query counts")
+    ap.add_argument("--records-layers", type=int, default=32, help="records workload: layers of the sequence")
     return ap.parse_args()
 
 
@@ -850,7 +851,7 @@ def run_records(args, torch):
 
     lib = hsb._capi.lib()
     peak, peak_kind = peaks()
-    layers, positions, nbytes, request = 32, 32768, 4096, 7
+    layers, positions, nbytes, request = args.records_layers, 32768, 4096, 7
     stride = nbytes + 32
     s = torch.cuda.Stream()
     g = torch.Generator(device="cuda").manual_seed(9)
@@ -897,9 +898,10 @@ def run_records(args, torch):
                            "frac_of_" + peak_kind: round(alg / (enc_ms * 1e-3) / 1e9 / peak, 3)}
         # verify: read plan windows of a selected set in layer 5
         rng = np.random.default_rng(1)
+        vl = min(5, layers - 1)  # the layer read back
         for name, k in (("verify_decode_k6553", 6553), ("verify_layer_32768", positions)):
             ids = np.sort(rng.choice(positions, k, replace=False)) if k < positions else np.arange(positions)
-            offs = [4096 + (5 * positions + int(i)) * stride for i in ids]
+            offs = [4096 + (vl * positions + int(i)) * stride for i in ids]
             extent = hsb.segment_extent_bytes(layers, positions, nbytes)
             plan = hsb.kv_read_plan(offs, stride, extent)
             groups = torch.tensor(hsb.kv_read_groups(plan, k), dtype=torch.int32, device="cuda")
@@ -923,7 +925,7 @@ def run_records(args, torch):
 
             def verify():
                 rc = lib.hsb_kv_records_verify(window.data_ptr(), base, offsets.data_ptr(), pos.data_ptr(),
-                                               groups.data_ptr(), k, request, 5, nbytes, out.data_ptr(), nbytes,
+                                               groups.data_ptr(), k, request, vl, nbytes, out.data_ptr(), nbytes,
                                                None, k, st.data_ptr(), s.cuda_stream)
                 assert rc == 0, lib.hsb_last_error()
 
@@ -938,7 +940,7 @@ def run_records(args, torch):
             e1.synchronize()
             launches += reps + 3
             assert int(st.abs().sum()) == 0, st
-            assert torch.equal(out, payload[5][torch.from_numpy(ids).cuda()])
+            assert torch.equal(out, payload[vl][torch.from_numpy(ids).cuda()])
             us = e0.elapsed_time(e1) * 1e3 / reps
             alg = base + k * nbytes
             row = {"records": k, "window_bytes": base, "read_windows": len(plan), "us": round(us, 2),
@@ -965,7 +967,7 @@ def run_records(args, torch):
                     with torch.cuda.stream(s):
                         e0.record(s)
                         rc = lib.hsb_kv_records_verify(host.data_ptr(), base, offsets.data_ptr(), pos.data_ptr(),
-                                                       groups.data_ptr(), k, request, 5, nbytes, out.data_ptr(),
+                                                       groups.data_ptr(), k, request, vl, nbytes, out.data_ptr(),
                                                        nbytes, None, k, st.data_ptr(), s.cuda_stream)
                         assert rc == 0, lib.hsb_last_error()
                         e1.record(s)
@@ -973,7 +975,7 @@ def run_records(args, torch):
                     t_zc.append(e0.elapsed_time(e1) * 1e3)
                 launches += 10
                 assert int(st.abs().sum()) == 0, st
-                assert torch.equal(out, payload[5][torch.from_numpy(ids).cuda()])
+                assert torch.equal(out, payload[vl][torch.from_numpy(ids).cuda()])
                 row["e2e_us"] = round(float(np.median(t_zc)), 2)
                 row["e2e_bus_bytes"] = k * stride
                 if not args.no_cpu_baseline and ob.reference_available():
@@ -990,8 +992,8 @@ def run_records(args, torch):
     big = lines["encode"]
     line = {"metric": "cold-tier KV record encode (FNV-1a) throughput", "impl": "ours", "workload": "records",
             "unit": "GB/s", "value": big["GB_s"], "dtype": "u8 / u64 FNV-1a", "data": "synthetic",
-            "config": {"workload": "SegmentedKVStore v1 records, 32 layers x 32768 positions x 4096 B K||V",
-                       "l2": "4.3 GB of records, far past the 126 MB L2"},
+            "config": {"workload": f"SegmentedKVStore v1 records, {layers} layers x 32768 positions x 4096 B K||V",
+                       "l2": f"{layers * positions * stride / 1e9:.1f} GB of records, past the 126 MB L2"},
             "roofline": {"bound": "hbm", "achieved": big["GB_s"], "peak": peak, "unit": "GB/s",
                          "frac": big["frac_of_" + peak_kind], "peak_kind": peak_kind},
             "gpu_launches": launches, "results": lines, "clocks": clocks.summary()}
