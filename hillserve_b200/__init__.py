@@ -36,7 +36,7 @@ __all__ = [
     "attention_dense", "rehearsal_query", "GQAPrefetchCuda", "GQADeliveryWorkspace",
     "SelectedKVLayer", "attention_slots", "h2o_group_sums", "GQAH2OStatsCuda",
     "segment_header", "segment_extent_bytes", "kv_records_encode", "kv_records_verify", "kv_read_plan",
-    "kv_read_groups",
+    "kv_read_groups", "plan_hot_slots", "score_history", "History",
 ]
 
 # Status codes the reference reports as std::invalid_argument.
@@ -496,6 +496,121 @@ def kv_read_groups(windows: list, count: int) -> list:
     out = (C.c_uint32 * max(1, count))()
     _raise(lib().hsb_kv_read_groups(wins, len(windows), out, int(count)))
     return list(out[:count])
+
+
+# ------------------------------------------------------- decode history
+class HistoryConfig(C.Structure):
+    _fields_ = [("layers", C.c_size_t), ("capacity", C.c_size_t), ("prompt_tokens", C.c_size_t),
+                ("generated_capacity", C.c_size_t), ("alpha", C.c_float), ("fp32_counts", C.c_int)]
+
+
+def plan_hot_slots(prompt_tokens: int, generated_capacity: int, capacity: int, beta: float = 1.0,
+                   allow_partial_prompt: bool = False):
+    """plan_full_gqa_runtime's placement (runtime/full_gqa_contract.hpp):
+    (hot_slot_by_position int64 [capacity], prompt hot tokens)."""
+    import numpy as np
+
+    out = np.zeros(int(capacity), dtype=np.int64)
+    hot = C.c_size_t(0)
+    _raise(lib().hsb_history_plan_slots(int(prompt_tokens), int(generated_capacity), int(capacity), float(beta),
+                                        int(allow_partial_prompt), out.ctypes.data, C.byref(hot)))
+    return out, hot.value
+
+
+def score_history(q, hot_pool, cold_k, row_of_position, valid: int, out=None, order_keys=None, stream=None):
+    """Raw V3 scores of positions [0, valid) whose K rows live in a hot pool
+    (rows of 2048 words) or a cold K store (rows of 1024 words); see
+    hsb_score_history.  row_of_position: host int64 array."""
+    import numpy as np
+
+    torch = _torch()
+    rows = np.ascontiguousarray(row_of_position, dtype=np.int64)
+    if out is None:
+        out = torch.empty((32, int(valid)), dtype=torch.int16, device=q.device)
+    stride = out.stride(0)
+    _raise(lib().hsb_score_history(_ptr(_u16(q)), _ptr(hot_pool), 2048, _ptr(cold_k), 1024, rows.ctypes.data,
+                                   int(valid), _ptr(out), stride, _ptr(order_keys), _stream(stream)))
+    return out
+
+
+class History:
+    """FullGqaRuntimePolicy's decode history (policy/full_gqa_runtime.hpp:
+    14-106) on the GPU: append / prepare_history / select / fetch of one
+    request, the hot KV rows and every K row in HBM (hsb_history_*)."""
+
+    def __init__(self, layers: int, capacity: int, prompt_tokens: int, generated_capacity: int, beta: float = 1.0,
+                 alpha: float = 5.0, fp32_counts: bool = False, allow_partial_prompt: bool = False,
+                 hot_slot_by_position=None):
+        import numpy as np
+
+        if hot_slot_by_position is None:
+            hot_slot_by_position, _ = plan_hot_slots(prompt_tokens, generated_capacity, capacity, beta,
+                                                     allow_partial_prompt)
+        self.slots = np.ascontiguousarray(hot_slot_by_position, dtype=np.int64)
+        cfg = HistoryConfig(layers, capacity, prompt_tokens, generated_capacity, alpha, int(fp32_counts))
+        self.capacity = capacity
+        self._h = C.c_void_p()
+        _raise(lib().hsb_history_create(C.byref(cfg), self.slots.ctypes.data, C.byref(self._h)))
+        self.kcap = lib().hsb_history_select_capacity(self._h)
+        self.hot_slots = lib().hsb_history_hot_slots(self._h)
+        self.cold_rows = lib().hsb_history_cold_rows(self._h)
+
+    def close(self):
+        if self._h:
+            lib().hsb_history_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        self.close()
+
+    def append(self, layer: int, first: int, rows, stream=None):
+        """rows: [count][2048] 16-bit device tensor of K||V rows."""
+        _raise(lib().hsb_history_append(self._h, layer, first, rows.shape[0], _ptr(_u16(rows)), _stream(stream)))
+
+    def prepare_history(self, layer: int, position: int, q16, stream=None):
+        _raise(lib().hsb_history_prepare(self._h, layer, position, _ptr(_u16(q16)), _stream(stream)))
+
+    def cover(self, layer: int, stream=None):
+        """(cold positions of the cover, ascending int32 device tensor; bound)."""
+        torch = _torch()
+        dev = torch.device("cuda")
+        ids = torch.empty(self.capacity, dtype=torch.int32, device=dev)
+        n = torch.zeros(1, dtype=torch.int32, device=dev)
+        res = torch.zeros(4, dtype=torch.int32, device=dev)
+        _raise(lib().hsb_history_cover(self._h, layer, _ptr(ids), _ptr(n), _ptr(res), _stream(stream)))
+        count = int(n.item())
+        if int(res[2].item()):
+            _raise(int(res[2].item()))
+        return ids[:count], int(res[0].item())
+
+    def select(self, layer: int, position: int, q16, stream=None):
+        """(ids int32 [32][kcap], counts int32 [32], result int32 [4] =
+        {k, tied heads, status code, status index}) on the device."""
+        torch = _torch()
+        dev = torch.device("cuda")
+        ids = torch.zeros((32, max(self.kcap, 1)), dtype=torch.int32, device=dev)
+        counts = torch.zeros(32, dtype=torch.int32, device=dev)
+        res = torch.zeros(4, dtype=torch.int32, device=dev)
+        _raise(lib().hsb_history_select(self._h, layer, position, _ptr(_u16(q16)), _ptr(ids), ids.shape[1],
+                                        _ptr(counts), _ptr(res), _stream(stream)))
+        return ids, counts, res
+
+    def fetch(self, layer: int, ids, result, staged_ids, staged_rows, count: int, stream=None, check: bool = True):
+        """Packed K [count][32][128] and V [32][128][count] (int16) of the
+        selection; cold rows from staged_rows (rows of the ascending
+        staged_ids)."""
+        torch = _torch()
+        dev = torch.device("cuda")
+        k = torch.empty((count, 32, 128), dtype=torch.int16, device=dev)
+        v = torch.empty((32, 128, count), dtype=torch.int16, device=dev)
+        st = _status_buffer(dev)
+        n = 0 if staged_ids is None else int(staged_ids.numel())
+        _raise(lib().hsb_history_fetch(self._h, layer, _ptr(ids), ids.shape[1], _ptr(result), _ptr(staged_ids), n,
+                                       _ptr(None if staged_rows is None else _u16(staged_rows)), count, _ptr(k),
+                                       _ptr(v), _ptr(st), _stream(stream)))
+        if check:
+            _check_status(st, stream)
+        return k, v, st
 
 
 # ------------------------------------------------------------ delivery

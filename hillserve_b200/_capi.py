@@ -83,6 +83,18 @@ _SIGNATURES = {
     "hsb_kv_records_verify": (I, [P, SZ, P, P, P, SZ, U64, C.c_uint32, SZ, P, SZ, P, SZ, P, P]),
     "hsb_kv_read_plan": (I, [P, SZ, U64, U64, SZ, SZ, C.c_uint, P, SZ, P]),
     "hsb_kv_read_groups": (I, [P, SZ, P, SZ]),
+    "hsb_score_history": (I, [P, P, SZ, P, SZ, P, SZ, P, SZ, P, P]),
+    "hsb_history_plan_slots": (I, [SZ, SZ, SZ, C.c_double, I, P, P]),
+    "hsb_history_create": (I, [P, P, P]),
+    "hsb_history_destroy": (None, [P]),
+    "hsb_history_hot_slots": (SZ, [P]),
+    "hsb_history_cold_rows": (SZ, [P]),
+    "hsb_history_select_capacity": (SZ, [P]),
+    "hsb_history_append": (I, [P, SZ, U64, SZ, P, P]),
+    "hsb_history_prepare": (I, [P, SZ, U64, P, P]),
+    "hsb_history_cover": (I, [P, SZ, P, P, P, P]),
+    "hsb_history_select": (I, [P, SZ, U64, P, P, SZ, P, P, P]),
+    "hsb_history_fetch": (I, [P, SZ, P, SZ, P, P, SZ, P, SZ, P, P, P, P]),
     "hsb_synth_normal_f16": (I, [P, SZ, U64, F, P]),
     "hsb_synth_normal_bf16": (I, [P, SZ, U64, F, P]),
     "hsb_synth_keys": (I, [P, SZ, SZ, U64, F, F, I, F, P]),

@@ -116,6 +116,10 @@ const char* hsb_status_message(int status) {
     case HSB_E_RECORD_BOUNDS: return "complete KV record outside the uploaded window or output rows";
     case HSB_E_SEGMENT_GEOMETRY: return "bounded segmented geometry/quota";
     case HSB_E_READ_PLAN: return "invalid complete-KV read plan";
+    case HSB_E_HISTORY_RESIDENCY: return "full GQA hot lookup on cold/unreserved token";
+    case HSB_E_HISTORY_GEOMETRY: return "full GQA common store capacity must cover prompt+decode and align64";
+    case HSB_E_HISTORY_PROTOCOL: return "full GQA history protocol violation";
+    case HSB_E_HISTORY_QUERY: return "history Q/position differs from current same-query selection";
     default: return "unknown hsb status";
     }
 }

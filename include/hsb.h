@@ -95,7 +95,13 @@ typedef enum hsb_status {
     HSB_E_RECORD_CHECKSUM = 91,
     HSB_E_RECORD_BOUNDS = 92,
     HSB_E_SEGMENT_GEOMETRY = 93,
-    HSB_E_READ_PLAN = 94
+    HSB_E_READ_PLAN = 94,
+    /* decode history -- policy/full_gqa_runtime.cpp:236,472-483,550-560,
+     * runtime/full_gqa_contract.hpp:116-122 */
+    HSB_E_HISTORY_RESIDENCY = 100,
+    HSB_E_HISTORY_GEOMETRY = 101,
+    HSB_E_HISTORY_PROTOCOL = 102,
+    HSB_E_HISTORY_QUERY = 103
 } hsb_status;
 
 int hsb_abi_version(void);
@@ -420,6 +426,77 @@ int hsb_kv_read_plan(const uint64_t* offsets, size_t count, uint64_t record_byte
  * of each window in batches of four from the window's first record
  * (policy/full_gqa_runtime.cpp:394-395); groups[i] for i < count. */
 int hsb_kv_read_groups(const hsb_kv_read_window* windows, size_t nwindows, uint32_t* groups, size_t count);
+
+/* ---------------------------------------------------- decode history
+ * One request's decode history on the GPU: FullGqaRuntimePolicy's hot/cold
+ * history scoring and its prepare -> select -> fetch protocol
+ * (policy/full_gqa_runtime.cpp:418-471, 477-499, 549-585, 586-690) with the
+ * hot KV rows in HBM.
+ *
+ * hsb_score_history: raw V3 scores of positions [0, valid) into
+ * d_scores[h * out_stride + t] (order keys too when d_order_keys != NULL),
+ * each position's K row found through row_of_position (HOST array): >= 0 a
+ * row of the hot pool (rows of pool_stride_words, K first), <= -2 the row
+ * -2-r of the cold K store (cold_stride_words), -1 not resident (rejected,
+ * HSB_E_HISTORY_RESIDENCY).  Runs of positions whose rows are consecutive
+ * become key views of the TMA scorer; the scores are those of the
+ * reference's hot + cold merge, bit for bit. */
+int hsb_score_history(const uint16_t* d_q, const uint16_t* d_hot_pool, size_t pool_stride_words,
+                      const uint16_t* d_cold_k, size_t cold_stride_words, const int64_t* row_of_position,
+                      size_t valid, uint16_t* d_scores, size_t out_stride, uint16_t* d_order_keys,
+                      void* stream);
+
+/* The hot placement of plan_full_gqa_runtime (runtime/full_gqa_contract.hpp:
+ * 42-56, 128-134, 168-184): beta's hot 64-token blocks (the earliest ones
+ * plus a recent window of up to 16 blocks and the partial tail), generated
+ * positions after them; cold prompt positions -1.  Writes [capacity]. */
+int hsb_history_plan_slots(size_t prompt_tokens, size_t generated_capacity, size_t capacity, double beta,
+                           int allow_partial_prompt, int64_t* hot_slot_by_position, size_t* hot_prompt_tokens);
+
+typedef struct hsb_history hsb_history;
+typedef struct hsb_history_config {
+    size_t layers;              /* <= 32 */
+    size_t capacity;            /* positions per layer, multiple of 64 */
+    size_t prompt_tokens;
+    size_t generated_capacity;  /* 1 .. 512 */
+    float alpha;                /* selector alpha, shared by the cover and the final selection */
+    int fp32_counts;
+} hsb_history_config;
+/* hot_slot_by_position (HOST, [capacity]): the placement of
+ * runtime/full_gqa_contract.hpp:168-184 (hot pool slot, -1 cold).  Cold
+ * prompt positions keep their K rows in an HBM cold K store; their V stays in
+ * the caller's cold tier (records).  Every generated position must be hot. */
+int hsb_history_create(const hsb_history_config* cfg, const int64_t* hot_slot_by_position, hsb_history** out);
+void hsb_history_destroy(hsb_history* h);
+size_t hsb_history_hot_slots(const hsb_history* h);
+size_t hsb_history_cold_rows(const hsb_history* h);
+size_t hsb_history_select_capacity(const hsb_history* h); /* ids per head kcap that always suffices */
+/* append (:472-492): `count` token-major K||V rows (2048 words each, device,
+ * 16-byte aligned) for positions first .. first+count-1 = the next ones. */
+int hsb_history_append(hsb_history* h, size_t layer, uint64_t first, size_t count, const uint16_t* d_rows,
+                       void* stream);
+/* prepare_history (:493-516): scores the history [0, position) and its
+ * payload cover on the history's own stream, once `stream` has the query;
+ * at most two prepared histories, none twice for a layer. */
+int hsb_history_prepare(hsb_history* h, size_t layer, uint64_t position, const uint16_t* d_q16, void* stream);
+/* The cover of a prepared history, ordered on `stream`: its cold positions
+ * (ascending: the records to read) and its per-head bound (d_cover_result->k). */
+int hsb_history_cover(hsb_history* h, size_t layer, uint32_t* d_cold_ids, uint32_t* d_cold_count,
+                      hsb_selection* d_cover_result, void* stream);
+/* select (:549-585): joins the prepared history (or scores it now), adds the
+ * current token's score, normalises and selects: d_ids [32][kcap], d_counts
+ * [32], *d_result (HSB_E_HISTORY_QUERY when the query differs from prepare's). */
+int hsb_history_select(hsb_history* h, size_t layer, uint64_t position, const uint16_t* d_q16, uint32_t* d_ids,
+                       size_t kcap, uint32_t* d_counts, hsb_selection* d_result, void* stream);
+/* fetch (:586-690) into the packed layout: K [count][32][128], V
+ * [32][128][count]; hot rows from the pool, cold rows from d_staged_rows
+ * (4096-byte K||V rows of the ascending d_staged_ids, e.g. the cover's cold
+ * positions read with hsb_kv_records_verify).  A selected cold ID that was not
+ * staged sets HSB_E_MAP_MISS.  Consumes the layer's prepared history. */
+int hsb_history_fetch(hsb_history* h, size_t layer, const uint32_t* d_ids, size_t kcap,
+                      const hsb_selection* d_result, const uint32_t* d_staged_ids, size_t nstaged,
+                      const uint16_t* d_staged_rows, size_t count, uint16_t* d_k, uint16_t* d_v,
+                      hsb_device_status* d_status, void* stream);
 
 /* ------------------------------------------------------ synthetic inputs
  * Benchmark inputs, not part of the reference interface: seeded F16 normal

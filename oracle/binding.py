@@ -112,6 +112,8 @@ def ref() -> C.CDLL:
         lib.ref_checksum.argtypes = [P, SZ]
         lib.ref_checksum_four.argtypes = [P, SZ, SZ, P, C.c_char_p, SZ]
         lib.ref_checksum_records.argtypes = [P, P, SZ, SZ, P]
+        lib.ref_plan_hot_slots.argtypes = [C.c_uint64, C.c_uint64, C.c_uint64, C.c_double, C.c_int, P, P,
+                                           C.c_char_p, SZ]
         lib.ref_checksum_records.restype = None
         lib.ref_read_plan.argtypes = [P, SZ, C.c_uint64, C.c_uint64, SZ, SZ, C.c_uint, P, SZ, P, C.c_char_p, SZ]
         lib.ref_segment_roundtrip.argtypes = [C.c_char_p, C.c_uint64, SZ, C.c_uint64, SZ, C.c_uint64, P, P,
@@ -515,3 +517,14 @@ def ref_segment_roundtrip(path: str, request: int, layers: int, positions: int, 
                                    mutate_offset, mutate_xor, fetch_layer, _p(want), len(want), _p(out), e, 512):
         raise ReferenceError_(e.value.decode())
     return out[:len(want) * record_bytes]
+
+
+
+def ref_plan_hot_slots(capacity: int, prompt: int, generated: int, beta: float, allow_partial: bool = False):
+    """plan_full_gqa_runtime's hot_slot_by_position and prompt hot tokens."""
+    out = np.zeros(capacity, dtype=np.int64)
+    hot = C.c_uint64(0)
+    e = _err()
+    if ref().ref_plan_hot_slots(capacity, prompt, generated, beta, int(allow_partial), _p(out), C.byref(hot), e, 512):
+        raise ReferenceError_(e.value.decode())
+    return out, hot.value

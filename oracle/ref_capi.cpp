@@ -13,6 +13,7 @@
 #include "policy/host_policy.hpp"
 #include "runtime/gqa_pack.hpp"
 #include "policy/h2o_residency.hpp"
+#include "runtime/full_gqa_contract.hpp"
 #include "storage/file_store.hpp"
 #include "storage/kv_checksum.hpp"
 #include "storage/kv_read_plan.hpp"
@@ -328,6 +329,31 @@ void ref_checksum_records(const unsigned char* base, const std::uint64_t* offset
         for (std::size_t k = 0; k < n; ++k) rows[k] = base + offsets[j + k];
         const auto h = hillserve::storage::checksum_four(rows, bytes, n);
         for (std::size_t k = 0; k < n; ++k) out[j + k] = h[k];
+    }
+}
+// plan_full_gqa_runtime's placement (runtime/full_gqa_contract.hpp:110-185)
+// with budgets large enough to pass; writes hot_slot_by_position [capacity].
+int ref_plan_hot_slots(std::uint64_t capacity, std::uint64_t prompt, std::uint64_t generated, double beta,
+                       int allow_partial, std::int64_t* out, std::uint64_t* hot_tokens, char* err,
+                       std::size_t errlen) {
+    try {
+        hillserve::runtime::FullGqaRuntimeSpec s;
+        s.layers = 32;
+        s.capacity = capacity;
+        s.prompt_tokens = prompt;
+        s.generated_capacity = generated;
+        s.allow_partial_prompt = allow_partial != 0;
+        s.beta = beta;
+        s.hot_kv_budget_bytes = ~0ull >> 2;
+        s.total_host_workspace_budget_bytes = ~0ull >> 1;
+        s.fp32_selection_counts = capacity > 65536;
+        const auto p = hillserve::runtime::plan_full_gqa_runtime(s);
+        std::memcpy(out, p.hot_slot_by_position.data(), capacity * 8);
+        *hot_tokens = p.prompt_hot_tokens;
+        return 0;
+    } catch (const std::exception& e) {
+        copy_error(e, err, errlen);
+        return -1;
     }
 }
 }

@@ -3,7 +3,7 @@ own CPU code (oracle/_ref/libhs_ref.so, compiled from the HillServe sources by
 oracle/Makefile) on seeded inputs.  Run here, where the reference sources
 exist:
 
-    make -C oracle && python tests/golden/make_golden.py [--only h2o|records]
+    make -C oracle && python tests/golden/make_golden.py [--only h2o|records|history]
 
 Inputs are regenerated bit-exactly from their seeds by tests/inputs.py, so
 the fixtures hold only input digests and the reference's outputs.
@@ -133,8 +133,27 @@ def records_vectors() -> None:
     np.savez_compressed(OUT / "records_vectors.npz", **fields)
 
 
+# (capacity, prompt, generated, beta, allow_partial) of the placement fixture
+PLAN_CASES = ((4096, 3968, 128, 1.0, False), (4096, 4000, 16, 1.0, True), (32832, 32768, 64, 1.0, False),
+              (32832, 32768, 64, 0.25, False), (8192, 8000, 100, float("inf"), True), (192, 128, 1, 1.0, False),
+              (49152, 48000, 512, 3.0, False), (4096, 2048, 512, 0.0, False), (16384, 16000, 200, 7.5, True))
+
+
+def history_plans() -> None:
+    digests, hots = [], []
+    for cap, prompt, gen, beta, partial in PLAN_CASES:
+        slots, hot = ob.ref_plan_hot_slots(cap, prompt, gen, beta, partial)
+        digests.append(inputs.digest(slots))
+        hots.append(hot)
+    np.savez_compressed(OUT / "history_plans.npz", slots_digest=np.array(digests), hot_tokens=np.array(hots))
+
+
 def main() -> None:
     assert ob.reference_available(), "build oracle/_ref first (make -C oracle)"
+    if sys.argv[1:] == ["--only", "history"]:
+        history_plans()
+        print("history fixture written to", OUT)
+        return
     if sys.argv[1:] == ["--only", "h2o"]:
         h2o_vectors()
         print("h2o fixture written to", OUT)
@@ -144,6 +163,7 @@ def main() -> None:
         print("records fixture written to", OUT)
         return
     records_vectors()
+    history_plans()
     # ---- 0. H2O group sums through the reference's CPU policy
     h2o_vectors()
     # ---- 1. reference scorer test vectors
