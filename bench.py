@@ -49,12 +49,14 @@ def parse():
     ap.add_argument("--tokens", type=int, default=N)
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "kv-sharded", "sweep", "h2o", "records"],
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "kv-sharded", "sweep", "h2o", "records", "history"],
                     help="decode: configs[1] (the headline); kv-sharded: configs[4], one selected-KV layer "
                          "over --batch sequences with the KV heads split over the ranks; sweep: configs[2], "
                          "the selected-KV layer step per length N; h2o: the H2O group-sum reduction "
                          "(decode and prefill-block shapes) beside the reference's CUDA kernel; records: the "
-                         "cold-tier KV record encoder and verifier (FNV-1a) beside the reference's CPU checksum")
+                         "cold-tier KV record encoder and verifier (FNV-1a) beside the reference's CPU checksum; "
+                         "history: the hot/cold decode history protocol (prepare/select/fetch) per layer")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--h2o-keys", type=int, default=32768, help="h2o workload: keys N")
     ap.add_argument("--h2o-queries", default="1,16,512", help="h2o workload: comma-separated query counts")
@@ -1000,6 +1002,81 @@ def run_records(args, torch):
     return line
 
 
+def run_history(args, torch):
+    """The hot/cold decode history (hsb_history_*, FullGqaRuntimePolicy's
+    protocol) at N = 32768: prompt 32768 tokens, beta = 1 (half of the
+    prompt's 64-token blocks hot in the HBM pool, the other half's K in the
+    HBM cold K store), 30 sparse layers.  Per layer and decode step, device
+    time by CUDA events on the caller's stream:
+      prepare: prepare_history (history scores of 32768 positions over the
+               pool and cold-K runs, on the history's stream) + the payload
+               cover and its cold positions;
+      select + fetch: the current token's append, select (current-token
+               score, normalise, select) and fetch into packed K/V, the
+               cover's cold payload rows staged in HBM beforehand (the rows
+               hsb_kv_records_verify would have left there).
+    The host reads the cover's cold count between the two (the read list of
+    the cold tier), so the two halves are timed apart, without overlap."""
+    import hillserve_b200 as hsb
+
+    prompt, gen, cap, layers = 32768, 64, 32832, 30
+    steps = max(2, min(args.steps, 6))
+    alpha = args.alpha if args.alpha > 0 else 5.0
+    hist = hsb.History(layers, cap, prompt, gen, beta=1.0, alpha=alpha)
+    g = torch.Generator(device="cuda").manual_seed(11)
+    stream = torch.cuda.current_stream()
+    rows = []
+    for l in range(layers):
+        r = torch.empty((prompt + steps + 1, 2048), dtype=torch.float16, device="cuda")
+        r.normal_(generator=g)
+        heavy = torch.randint(0, prompt, (prompt // 50,), generator=g, device="cuda")
+        r[heavy, :1024] *= 4
+        rows.append(r.view(torch.int16))
+        hist.append(l, 0, rows[l][:prompt])
+    qs = [torch.empty((32, 128), dtype=torch.float16, device="cuda").normal_(generator=g).view(torch.int16)
+          for _ in range(layers)]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    prep, self_, ks, colds = [], [], [], []
+    launches = 0
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        for step in range(steps + 1):  # the first step warms up
+            pos = prompt + step
+            t_prep = t_sel = 0.0
+            for l in range(layers):
+                ev[0].record(stream)
+                hist.prepare_history(l, pos, qs[l])
+                cold_ids, _ = hist.cover(l)  # reads the cold count on the host
+                ev[1].record(stream)
+                staged = rows[l][cold_ids.long()]
+                count = hist.kcap // 32 * 32
+                ev[2].record(stream)
+                hist.append(l, pos, rows[l][pos:pos + 1])
+                ids, counts, res = hist.select(l, pos, qs[l])
+                hist.fetch(l, ids, res, cold_ids, staged, count, check=False)
+                ev[3].record(stream)
+                ev[3].synchronize()
+                t_prep += ev[0].elapsed_time(ev[1])
+                t_sel += ev[2].elapsed_time(ev[3])
+                if step:
+                    ks.append(int(res[0].item()))
+                    colds.append(int(cold_ids.numel()))
+                    assert int(res[2].item()) == 0, res
+            launches += layers * 12
+            if step:
+                prep.append(t_prep)
+                self_.append(t_sel)
+    hist.close()
+    p_us = float(np.median(prep)) * 1e3 / layers
+    s_us = float(np.median(self_)) * 1e3 / layers
+    return {"metric": "hot/cold decode history (prepare + select + fetch) per layer", "impl": "ours",
+            "workload": "history", "unit": "us per layer", "value": round(p_us + s_us, 2), "data": "synthetic",
+            "config": {"workload": f"prompt {prompt}, beta 1, capacity {cap}, {layers} sparse layers, alpha {alpha}",
+                       "hot_slots": hist.hot_slots, "cold_rows": hist.cold_rows, "steps": steps},
+            "prepare_cover_us_per_layer": round(p_us, 2), "select_fetch_us_per_layer": round(s_us, 2),
+            "k_mean": round(float(np.mean(ks)), 2), "cover_cold_rows_mean": round(float(np.mean(colds)), 1),
+            "gpu_launches": launches, "clocks": clocks.summary()}
+
+
 def main():
     args = parse()
     import torch
@@ -1023,6 +1100,8 @@ def main():
         line = run_h2o(args, torch)
     elif args.workload == "records":
         line = run_records(args, torch)
+    elif args.workload == "history":
+        line = run_history(args, torch)
     elif args.workload == "kv-sharded":
         if dist is None:  # one GPU: a world of one, still through the process-group code
             import datetime

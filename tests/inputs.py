@@ -46,7 +46,7 @@ def f16_bits(x: np.ndarray) -> np.ndarray:
 def heavy_rows(seed: int, n: int, fraction: float = 0.02) -> np.ndarray:
     """round(fraction*n) distinct token rows, uniformly chosen."""
     m = int(round(fraction * n))
-    keys = splitmix64(np.arange(n, dtype=np.uint64) + np.uint64(seed) * np.uint64(0x5851F42D4C957F2D))
+    keys = splitmix64(np.arange(n, dtype=np.uint64) + np.uint64((seed * 0x5851F42D4C957F2D) % (1 << 64)))
     return np.sort(np.argsort(keys, kind="stable")[:m])
 
 
