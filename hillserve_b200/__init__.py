@@ -36,7 +36,7 @@ __all__ = [
     "attention_dense", "rehearsal_query", "GQAPrefetchCuda", "GQADeliveryWorkspace",
     "SelectedKVLayer", "attention_slots", "h2o_group_sums", "GQAH2OStatsCuda",
     "segment_header", "segment_extent_bytes", "kv_records_encode", "kv_records_verify", "kv_read_plan",
-    "kv_read_groups", "plan_hot_slots", "score_history", "History",
+    "kv_read_groups", "plan_hot_slots", "score_history", "History", "DecodeExecutor",
 ]
 
 # Status codes the reference reports as std::invalid_argument.
@@ -611,6 +611,59 @@ class History:
         if check:
             _check_status(st, stream)
         return k, v, st
+
+
+# ------------------------------------------------------ layer executor
+class DecodeExecutor:
+    """The model-facing decode step of GQALayerExecutor
+    (runtime/gqa_executor.cpp:149-249) on the GPU: one HBM cache per layer,
+    the model's current K/V appended by hsb_executor_append, attention over
+    the selected live slots (hsb_executor_decode_layer)."""
+
+    def __init__(self, layers: int, capacity: int, alpha: float = 5.0, ratio: float = 0.2, dense_layers: int = 2,
+                 device=None):
+        torch = _torch()
+        dev = torch.device("cuda") if device is None else device
+        self.layers, self.capacity, self.alpha, self.ratio, self.dense = layers, capacity, alpha, ratio, dense_layers
+        self.count = max(32, (int(math.floor(capacity * ratio)) + 31) // 32 * 32)
+        self.cache = [torch.zeros((capacity, 2048), dtype=torch.int16, device=dev) for _ in range(layers)]
+        self.completed = [0] * layers
+        ws = lib().hsb_executor_workspace_bytes(capacity, self.count)
+        self.ws = torch.empty(ws, dtype=torch.uint8, device=dev)
+        self.scores = torch.empty((32, capacity), dtype=torch.int16, device=dev)
+        self.ids = torch.empty((32, self.count), dtype=torch.int32, device=dev)
+        self.counts = torch.empty(32, dtype=torch.int32, device=dev)
+        self.result = torch.zeros(4, dtype=torch.int32, device=dev)
+        self.k_packed = torch.empty((self.count, 32, 128), dtype=torch.int16, device=dev)
+        self.v_packed = torch.empty((32, 128, self.count), dtype=torch.int16, device=dev)
+        self.status = torch.zeros(2, dtype=torch.int32, device=dev)
+
+    def _buffers(self):
+        return LayerBuffers(self.scores.data_ptr(), self.ids.data_ptr(), self.counts.data_ptr(),
+                            self.result.data_ptr(), self.k_packed.data_ptr(), self.v_packed.data_ptr(),
+                            self.ws.data_ptr(), self.ws.numel())
+
+    def append(self, layer: int, current, stream=None):
+        """current: F16 [n_tokens][8][256] (K 128 | V 128 per KV head)."""
+        n = current.shape[0]
+        _raise(lib().hsb_executor_append(_ptr(_u16(current)), n, _ptr(self.cache[layer]), self.capacity,
+                                         self.completed[layer], _ptr(self.status), _stream(stream)))
+        self.completed[layer] += n
+
+    def decode_layer(self, layer: int, current, rehearsal, q, out=None, stream=None):
+        """Appends the current token and returns the attention output F32 [32][128]."""
+        torch = _torch()
+        if out is None:
+            out = torch.empty((32, 128), dtype=torch.float32, device=q.device)
+        b = self._buffers()
+        pos = self.completed[layer]
+        _raise(lib().hsb_executor_decode_layer(_ptr(_u16(current)), _ptr(rehearsal), _ptr(q),
+                                               _ptr(self.cache[layer]), self.capacity, pos,
+                                               int(layer < self.dense), C.c_float(self.alpha),
+                                               C.c_float(self.ratio), self.count, C.byref(b), _ptr(out),
+                                               _ptr(self.status), _stream(stream)))
+        self.completed[layer] += 1
+        return out
 
 
 # ------------------------------------------------------------ delivery

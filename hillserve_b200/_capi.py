@@ -95,6 +95,10 @@ _SIGNATURES = {
     "hsb_history_cover": (I, [P, SZ, P, P, P, P]),
     "hsb_history_select": (I, [P, SZ, U64, P, P, SZ, P, P, P]),
     "hsb_history_fetch": (I, [P, SZ, P, SZ, P, P, SZ, P, SZ, P, P, P, P]),
+    "hsb_executor_append": (I, [P, SZ, P, SZ, SZ, P, P]),
+    "hsb_executor_query": (I, [P, P, P, P]),
+    "hsb_executor_workspace_bytes": (SZ, [SZ, SZ]),
+    "hsb_executor_decode_layer": (I, [P, P, P, P, SZ, SZ, I, F, F, SZ, P, P, P, P]),
     "hsb_synth_normal_f16": (I, [P, SZ, U64, F, P]),
     "hsb_synth_normal_bf16": (I, [P, SZ, U64, F, P]),
     "hsb_synth_keys": (I, [P, SZ, SZ, U64, F, F, I, F, P]),

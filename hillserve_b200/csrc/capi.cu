@@ -120,6 +120,10 @@ const char* hsb_status_message(int status) {
     case HSB_E_HISTORY_GEOMETRY: return "full GQA common store capacity must cover prompt+decode and align64";
     case HSB_E_HISTORY_PROTOCOL: return "full GQA history protocol violation";
     case HSB_E_HISTORY_QUERY: return "history Q/position differs from current same-query selection";
+    case HSB_E_EXECUTOR_SHAPE: return "GQA current KV ABI mismatch";
+    case HSB_E_EXECUTOR_NONFINITE_KV: return "GQA current model KV contains nonfinite F16";
+    case HSB_E_EXECUTOR_REHEARSAL: return "full GQA rehearsal nonfinite";
+    case HSB_E_EXECUTOR_REHEARSAL_F16: return "full GQA rehearsal F16 overflow";
     default: return "unknown hsb status";
     }
 }

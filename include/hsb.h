@@ -101,7 +101,13 @@ typedef enum hsb_status {
     HSB_E_HISTORY_RESIDENCY = 100,
     HSB_E_HISTORY_GEOMETRY = 101,
     HSB_E_HISTORY_PROTOCOL = 102,
-    HSB_E_HISTORY_QUERY = 103
+    HSB_E_HISTORY_QUERY = 103,
+    /* layer executor -- runtime/gqa_executor.cpp:151-153,
+     * policy/full_gqa_runtime.cpp:61-64 */
+    HSB_E_EXECUTOR_SHAPE = 110,
+    HSB_E_EXECUTOR_NONFINITE_KV = 111,
+    HSB_E_EXECUTOR_REHEARSAL = 112,
+    HSB_E_EXECUTOR_REHEARSAL_F16 = 113
 } hsb_status;
 
 int hsb_abi_version(void);
@@ -497,6 +503,35 @@ int hsb_history_fetch(hsb_history* h, size_t layer, const uint32_t* d_ids, size_
                       const hsb_selection* d_result, const uint32_t* d_staged_ids, size_t nstaged,
                       const uint16_t* d_staged_rows, size_t count, uint16_t* d_k, uint16_t* d_v,
                       hsb_device_status* d_status, void* stream);
+
+/* ------------------------------------------------------ layer executor
+ * The model-facing decode step of GQALayerExecutor::prepare
+ * (runtime/gqa_executor.cpp:149-249) with the attention hook of
+ * patches/llama-b6000-round2.patch:218-244, on the GPU end to end: the
+ * model's current K/V is appended to the HBM cache, the rehearsal query is
+ * rounded to F16, and attention runs over the selected live slots only -- no
+ * padded per-head K/V/mask workspace, no host copy, no upload.
+ *
+ * d_current: the model's current KV tensor, ggml_concat(k_cur, v_cur, 0) in
+ * F16, [n_tokens][8 KV heads][K 128 | V 128].  d_cache: token-major cache
+ * rows [capacity][2048 words] (K[8][128] then V[8][128]).  A non-finite F16
+ * in the current KV sets HSB_E_EXECUTOR_NONFINITE_KV (index = token). */
+int hsb_executor_append(const uint16_t* d_current, size_t n_tokens, uint16_t* d_cache, size_t capacity,
+                        size_t first_position, hsb_device_status* d_status, void* stream);
+/* query_f16 (policy/full_gqa_runtime.cpp:61-64) of the F32 rehearsal
+ * [32][128]: HSB_E_EXECUTOR_REHEARSAL for a non-finite input,
+ * HSB_E_EXECUTOR_REHEARSAL_F16 when its F16 overflows. */
+int hsb_executor_query(const float* d_rehearsal, uint16_t* d_q16, hsb_device_status* d_status, void* stream);
+size_t hsb_executor_workspace_bytes(size_t capacity, size_t count);
+/* One decode layer: append the current token at `position`, then either
+ * dense attention over [0, position] (dense != 0: layers 0-1) or the
+ * selected-KV layer step with the rehearsal as the selection query and d_q
+ * (the layer's own F32 query) for attention; d_out F32 [32][128] (the
+ * model's kqv_out layout).  buffers->workspace >= hsb_executor_workspace_bytes. */
+int hsb_executor_decode_layer(const uint16_t* d_current, const float* d_rehearsal, const float* d_q,
+                              uint16_t* d_cache, size_t capacity, size_t position, int dense, float alpha,
+                              float ratio, size_t count, const hsb_layer_buffers* buffers, float* d_out,
+                              hsb_device_status* d_status, void* stream);
 
 /* ------------------------------------------------------ synthetic inputs
  * Benchmark inputs, not part of the reference interface: seeded F16 normal
