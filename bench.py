@@ -374,9 +374,11 @@ def run_ours(args, rank, world, torch, dist):
     return line
 
 
-def kernel_launches_per_step(layers: int) -> int:
-    # dense: 1 kernel; selected-KV layer step: score, select, gather+attention
-    return DENSE * 1 + (layers - DENSE) * 3
+def kernel_launches_per_step(layers: int, fused: bool = True) -> int:
+    # dense layer: attention_dense_tma_kernel + dense_combine_kernel; selected-KV
+    # layer step: score_tma_kernel + select_cluster_kernel (its epilogue gathers
+    # and attends), or a third launch (gather + attention) without the cluster path
+    return DENSE * 2 + (layers - DENSE) * (2 if fused else 3)
 
 
 def run_e2e(m, graph, stream, torch, args, dist):
