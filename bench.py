@@ -1056,7 +1056,7 @@ def run_history(args, torch):
                 ev[2].record(stream)
                 hist.append(l, pos, rows[l][pos:pos + 1])
                 ids, counts, res = hist.select(l, pos, qs[l])
-                hist.fetch(l, ids, res, cold_ids, staged, count, check=False)
+                hist.fetch(l, ids, res, cold_ids, staged, count, check=False, zero_padding=False)
                 ev[3].record(stream)
                 ev[3].synchronize()
                 t_prep += ev[0].elapsed_time(ev[1])
@@ -1085,7 +1085,7 @@ def run_history(args, torch):
                 hist.prepare_history(l, pos, qs[l], stream=gs)
                 hist.append(l, pos, rows[l][pos:pos + 1], stream=gs)
                 ids, counts, res = hist.select(l, pos, qs[l], stream=gs)
-                hist.fetch(l, ids, res, cold_pos, staged_all[l], count, stream=gs, check=False)
+                hist.fetch(l, ids, res, cold_pos, staged_all[l], count, stream=gs, check=False, zero_padding=False)
         torch.cuda.synchronize()
         for _ in range(3):
             graph.replay()

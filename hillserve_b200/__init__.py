@@ -585,32 +585,40 @@ class History:
 
     def select(self, layer: int, position: int, q16, stream=None):
         """(ids int32 [32][kcap], counts int32 [32], result int32 [4] =
-        {k, tied heads, status code, status index}) on the device."""
+        {k, tied heads, status code, status index}) on the device; the
+        tensors are the history's own, valid until its next select()."""
         torch = _torch()
-        dev = torch.device("cuda")
-        ids = torch.zeros((32, max(self.kcap, 1)), dtype=torch.int32, device=dev)
-        counts = torch.zeros(32, dtype=torch.int32, device=dev)
-        res = torch.zeros(4, dtype=torch.int32, device=dev)
-        _raise(lib().hsb_history_select(self._h, layer, position, _ptr(_u16(q16)), _ptr(ids), ids.shape[1],
-                                        _ptr(counts), _ptr(res), _stream(stream)))
-        return ids, counts, res
+        if not hasattr(self, "_ids"):
+            dev = torch.device("cuda")
+            self._ids = torch.zeros((32, max(self.kcap, 1)), dtype=torch.int32, device=dev)
+            self._counts = torch.zeros(32, dtype=torch.int32, device=dev)
+            self._res = torch.zeros(4, dtype=torch.int32, device=dev)
+        _raise(lib().hsb_history_select(self._h, layer, position, _ptr(_u16(q16)), _ptr(self._ids),
+                                        self._ids.shape[1], _ptr(self._counts), _ptr(self._res), _stream(stream)))
+        return self._ids, self._counts, self._res
 
-    def fetch(self, layer: int, ids, result, staged_ids, staged_rows, count: int, stream=None, check: bool = True):
+    def fetch(self, layer: int, ids, result, staged_ids, staged_rows, count: int, stream=None, check: bool = True,
+              zero_padding: bool = True):
         """Packed K [count][32][128] and V [32][128][count] (int16) of the
         selection; cold rows from staged_rows (rows of the ascending
-        staged_ids)."""
+        staged_ids).  zero_padding=False writes the live slots only.  The
+        tensors are the history's own, valid until its next fetch()."""
         torch = _torch()
         dev = torch.device("cuda")
-        k = torch.empty((count, 32, 128), dtype=torch.int16, device=dev)
-        v = torch.empty((32, 128, count), dtype=torch.int16, device=dev)
-        st = _status_buffer(dev)
+        if getattr(self, "_count", None) != count:
+            self._k = torch.zeros((count, 32, 128), dtype=torch.int16, device=dev)
+            self._v = torch.zeros((32, 128, count), dtype=torch.int16, device=dev)
+            self._count = count
+            self._st = torch.zeros(2, dtype=torch.int32, device=dev)
+        self._st.zero_()
         n = 0 if staged_ids is None else int(staged_ids.numel())
         _raise(lib().hsb_history_fetch(self._h, layer, _ptr(ids), ids.shape[1], _ptr(result), _ptr(staged_ids), n,
-                                       _ptr(None if staged_rows is None else _u16(staged_rows)), count, _ptr(k),
-                                       _ptr(v), _ptr(st), _stream(stream)))
+                                       _ptr(None if staged_rows is None else _u16(staged_rows)), count,
+                                       int(zero_padding), _ptr(self._k), _ptr(self._v), _ptr(self._st),
+                                       _stream(stream)))
         if check:
-            _check_status(st, stream)
-        return k, v, st
+            _check_status(self._st, stream)
+        return self._k, self._v, self._st
 
 
 # ------------------------------------------------------ layer executor

@@ -94,7 +94,7 @@ _SIGNATURES = {
     "hsb_history_prepare": (I, [P, SZ, U64, P, P]),
     "hsb_history_cover": (I, [P, SZ, P, P, P, P]),
     "hsb_history_select": (I, [P, SZ, U64, P, P, SZ, P, P, P]),
-    "hsb_history_fetch": (I, [P, SZ, P, SZ, P, P, SZ, P, SZ, P, P, P, P]),
+    "hsb_history_fetch": (I, [P, SZ, P, SZ, P, P, SZ, P, SZ, I, P, P, P, P]),
     "hsb_executor_append": (I, [P, SZ, P, SZ, SZ, P, P]),
     "hsb_executor_query": (I, [P, P, P, P]),
     "hsb_executor_workspace_bytes": (SZ, [SZ, SZ]),

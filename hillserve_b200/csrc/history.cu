@@ -18,11 +18,13 @@
 // the same raw F16 scores as the reference's hot + cold merge.
 //
 // Protocol.  prepare() scores the history [0, position) and its payload
-// cover (hsb_prefetch_cover + union) on the history's own stream, like the
-// reference's async job; select() joins it on the caller's stream, scores
+// cover (hsb_prefetch_cover) on the history's own stream, like the
+// reference's async job (cover() then lists the cover's cold positions);
+// select() joins it on the caller's stream, scores
 // the current token, normalises and selects; fetch() builds the gather map
 // of the selected IDs (hot -> pool slot, cold -> the caller's staged rows)
-// and packs K/V with hsb_gather_map's kernel.  The reference's protocol
+// and packs K/V with hsb_gather_map's kernel (live slots only, or zero
+// padding up to `count`).  The reference's protocol
 // checks are kept, with its messages.
 #include <algorithm>
 #include <cmath>
@@ -115,35 +117,53 @@ __global__ void history_append_kernel(const uint16_t* __restrict__ rows, unsigne
     }
 }
 
-// The cold members of the cover's physical union, ascending (the caller's
-// payload read list).  One block; the union is ascending already.
-__global__ void history_cold_cover_kernel(const uint32_t* __restrict__ physical, const uint32_t* __restrict__ count,
-                                          const int32_t* __restrict__ slot, uint32_t* __restrict__ out,
-                                          uint32_t* __restrict__ out_count) {
-    __shared__ uint32_t base;
-    if (threadIdx.x == 0) base = 0;
+// The cold positions of a prepared cover, ascending: every position some
+// head's top-`bound` list names whose K lives in the cold store (the cold
+// tier's read list; the cover's hot rows are in the pool already).  One
+// block: a bitmap of the history in shared memory, then a block-wide
+// compaction in position order.
+constexpr unsigned kCoverWords = (66048 + 31) / 32;
+__global__ void __launch_bounds__(1024) history_cover_cold_kernel(const uint32_t* __restrict__ cover,
+                                                                  unsigned long long cap,
+                                                                  const hsb_selection* __restrict__ result,
+                                                                  const int32_t* __restrict__ slot,
+                                                                  unsigned long long position,
+                                                                  uint32_t* __restrict__ out,
+                                                                  uint32_t* __restrict__ out_count) {
+    __shared__ uint32_t bits[kCoverWords];
+    __shared__ uint32_t warp_total[32];
+    const unsigned tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const unsigned words = (unsigned)((position + 31) / 32);
+    for (unsigned w = tid; w < words; w += blockDim.x) bits[w] = 0;
     __syncthreads();
-    const uint32_t n = *count;
-    for (uint32_t i0 = 0; i0 < n; i0 += blockDim.x) {
-        const uint32_t i = i0 + threadIdx.x;
-        const bool cold = i < n && slot[physical[i]] < 0;
-        const unsigned ballot = __ballot_sync(0xffffffffu, cold);
-        __shared__ uint32_t warp_count[32];
-        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        if (lane == 0) warp_count[warp] = __popc(ballot);
-        __syncthreads();
-        uint32_t before = base;
-        for (int w = 0; w < warp; ++w) before += warp_count[w];
-        if (cold) out[before + __popc(ballot & lanemask_lt())] = physical[i];
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            uint32_t total = 0;
-            for (int w = 0; w < (int)(blockDim.x >> 5); ++w) total += warp_count[w];
-            base += total;
-        }
-        __syncthreads();
+    const unsigned long long bound = result->status.code ? 0ull : (result->k < cap ? result->k : cap);
+    for (unsigned long long i = tid; i < 32ull * bound; i += blockDim.x) {
+        const uint32_t id = cover[(i / bound) * cap + i % bound];
+        if (id < position && slot[id] < 0) atomicOr(&bits[id >> 5], 1u << (id & 31));
     }
-    if (threadIdx.x == 0) *out_count = base;
+    __syncthreads();
+    const unsigned per = (words + blockDim.x - 1) / blockDim.x;
+    const unsigned w0 = min(words, tid * per), w1 = min(words, w0 + per);
+    unsigned mine = 0;
+    for (unsigned w = w0; w < w1; ++w) mine += __popc(bits[w]);
+    unsigned scan = mine;  // inclusive scan within the warp
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned y = __shfl_up_sync(0xffffffffu, scan, o);
+        if (lane >= (unsigned)o) scan += y;
+    }
+    if (lane == 31) warp_total[warp] = scan;
+    __syncthreads();
+    unsigned before = scan - mine;
+    for (unsigned w = 0; w < warp; ++w) before += warp_total[w];
+    for (unsigned w = w0; w < w1; ++w) {
+        uint32_t b = bits[w];
+        while (b) {
+            out[before++] = w * 32 + (__ffs(b) - 1);
+            b &= b - 1;
+        }
+    }
+    if (tid == blockDim.x - 1) *out_count = before;
 }
 
 // Gather map of a selection: map[h * count + j] = the pool slot of
@@ -239,11 +259,9 @@ struct hsb_history {
         uint64_t position = 0;
         uint16_t* raw = nullptr;   // [32][capacity]
         uint16_t* query = nullptr; // [32][128] F16 of prepare()
-        uint32_t* cover = nullptr; // [32][cover_cap]
-        uint32_t* physical = nullptr;
-        uint32_t* physical_count = nullptr;
+        uint32_t* cover = nullptr; // [32][cap]
+        size_t cap = 0;
         hsb_selection* cover_result = nullptr;
-        hsb_device_status* union_status = nullptr;
         cudaEvent_t ready = nullptr;
         cudaEvent_t inputs = nullptr;
     } jobs[2];
@@ -252,8 +270,6 @@ struct hsb_history {
     size_t select_ws_bytes = 0;
     void* cover_ws = nullptr;
     size_t cover_ws_bytes = 0;
-    void* union_ws = nullptr;
-    size_t union_ws_bytes = 0;
     int32_t* map = nullptr;  // [32][count] of the last fetch
     size_t map_capacity = 0;
     std::vector<void*> allocations;
@@ -405,24 +421,19 @@ int hsb_history_create(const hsb_history_config* cfg, const int64_t* hot_slot_by
         if (e == cudaSuccess) e = cudaMemcpy(L.slot, slot32.data(), c.capacity * 4, cudaMemcpyHostToDevice);
         if (e == cudaSuccess) e = cudaMemcpy(L.cold_row, cold32.data(), c.capacity * 4, cudaMemcpyHostToDevice);
     }
-    h->union_ws_bytes = union_workspace_bytes(c.capacity);
     h->cover_ws_bytes = select_workspace_bytes(kHeads, c.capacity, h->cover_cap);
     h->select_ws_bytes = select_workspace_bytes(kHeads, c.capacity, h->kcap);
     for (auto& j : h->jobs) {
         j.raw = keep(h.get(), dev_alloc<uint16_t>((size_t)kHeads * c.capacity, &e));
         j.query = keep(h.get(), dev_alloc<uint16_t>((size_t)kHeads * kDim, &e));
         j.cover = keep(h.get(), dev_alloc<uint32_t>((size_t)kHeads * h->cover_cap, &e));
-        j.physical = keep(h.get(), dev_alloc<uint32_t>(c.capacity, &e));
-        j.physical_count = keep(h.get(), dev_alloc<uint32_t>(1, &e));
         j.cover_result = keep(h.get(), dev_alloc<hsb_selection>(1, &e));
-        j.union_status = keep(h.get(), dev_alloc<hsb_device_status>(1, &e));
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&j.ready, cudaEventDisableTiming);
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&j.inputs, cudaEventDisableTiming);
     }
     h->raw_direct = keep(h.get(), dev_alloc<uint16_t>((size_t)kHeads * c.capacity, &e));
     h->select_ws = keep(h.get(), dev_alloc<unsigned char>(h->select_ws_bytes, &e));
     h->cover_ws = keep(h.get(), dev_alloc<unsigned char>(h->cover_ws_bytes, &e));
-    h->union_ws = keep(h.get(), dev_alloc<unsigned char>(h->union_ws_bytes, &e));
     if (e != cudaSuccess) return record_cuda_error(e, "history allocation");
     *out = h.release();
     record_error(HSB_OK, "");
@@ -483,15 +494,12 @@ int hsb_history_prepare(hsb_history* h, size_t layer, uint64_t position, const u
         e = score_runs(J.query, L.runs, position, L.pool, kRowWords, L.cold, kKeyWords, J.raw, c.capacity, nullptr,
                        h->work);
     if (e != cudaSuccess) return record_cuda_error(e, "history prepare launch");
-    // The payload cover of the final selection (policy/full_gqa_runtime.cpp:299-344)
-    // and its physical union.
+    // The payload cover of the final selection (policy/full_gqa_runtime.cpp:299-344).
     const size_t cap = std::min<size_t>(position, (size_t)std::floor(double(position + 1) * double(0.2f)));
     int rc = hsb_prefetch_cover(J.raw, c.capacity, position, c.alpha, c.fp32_counts, J.cover, cap, J.cover_result,
                                 h->cover_ws, h->cover_ws_bytes, h->work);
     if (rc) return rc;
-    rc = hsb_union(J.cover, cap, &J.cover_result->k, 0, position, J.physical, J.physical_count, J.union_status,
-                   h->union_ws, h->union_ws_bytes, h->work);
-    if (rc) return rc;
+    J.cap = cap;
     e = cudaEventRecord(J.ready, h->work);
     if (e != cudaSuccess) return record_cuda_error(e, "history prepare event");
     J.used = true;
@@ -511,7 +519,8 @@ int hsb_history_cover(hsb_history* h, size_t layer, uint32_t* d_cold_ids, uint32
     const auto s = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaStreamWaitEvent(s, J.ready, 0);
     if (e == cudaSuccess && d_cold_ids && d_cold_count)
-        history_cold_cover_kernel<<<1, 1024, 0, s>>>(J.physical, J.physical_count, L.slot, d_cold_ids, d_cold_count);
+        history_cover_cold_kernel<<<1, 1024, 0, s>>>(J.cover, J.cap, J.cover_result, L.slot, J.position, d_cold_ids,
+                                                     d_cold_count);
     if (e == cudaSuccess && d_cover_result)
         e = cudaMemcpyAsync(d_cover_result, J.cover_result, sizeof(hsb_selection), cudaMemcpyDeviceToDevice, s);
     if (e == cudaSuccess) e = cudaGetLastError();
@@ -567,8 +576,8 @@ int hsb_history_select(hsb_history* h, size_t layer, uint64_t position, const ui
 
 int hsb_history_fetch(hsb_history* h, size_t layer, const uint32_t* d_ids, size_t kcap,
                       const hsb_selection* d_result, const uint32_t* d_staged_ids, size_t nstaged,
-                      const uint16_t* d_staged_rows, size_t count, uint16_t* d_k, uint16_t* d_v,
-                      hsb_device_status* d_status, void* stream) {
+                      const uint16_t* d_staged_rows, size_t count, int zero_padding, uint16_t* d_k,
+                      uint16_t* d_v, hsb_device_status* d_status, void* stream) {
     if (!h || layer >= h->layers.size()) return history_fail(HSB_E_HISTORY_PROTOCOL, "full GQA layer out of bounds");
     auto& L = h->layers[layer];
     if (!d_ids || !d_result || !d_k || !d_v || !d_status || !count || (nstaged && (!d_staged_ids || !d_staged_rows)))
@@ -592,7 +601,7 @@ int hsb_history_fetch(hsb_history* h, size_t layer, const uint32_t* d_ids, size_
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess)
         e = launch_gather_map(L.pool, h->hot_slots, d_staged_rows ? d_staged_rows : L.pool, nstaged, h->map, count,
-                              d_k, d_v, d_status, s);
+                              d_k, d_v, d_status, s, zero_padding);
     if (e != cudaSuccess) return record_cuda_error(e, "history fetch launch");
     // The prepared job is consumed (policy/full_gqa_runtime.cpp:620-622).
     if (L.job >= 0) {

@@ -234,11 +234,15 @@ __global__ void mask_kernel(const __grid_constant__ MaskParams p) {
 }
 
 // ------------------------------------------------------------ prefetch map
+// zero_padding false: the map's sources form a prefix of each head's slots
+// (the rest -1) and only that prefix is written; a tile without a source
+// is skipped.
 __global__ void __launch_bounds__(kThreads) gather_map_kernel(const uint16_t* __restrict__ prefetched,
                                                               size_t prows, const uint16_t* __restrict__ misses,
                                                               size_t mrows, const int32_t* __restrict__ map,
                                                               size_t count, uint16_t* __restrict__ k,
-                                                              uint16_t* __restrict__ v, hsb_device_status* status) {
+                                                              uint16_t* __restrict__ v, hsb_device_status* status,
+                                                              int zero_padding) {
     __shared__ SlotSource src[kSlotTile];
     __shared__ __align__(16) uint16_t vt[kSlotTile][kVPitch];
     const size_t tiles_per_head = (count + kSlotTile - 1) / kSlotTile;
@@ -268,8 +272,10 @@ __global__ void __launch_bounds__(kThreads) gather_map_kernel(const uint16_t* __
             }
             src[s] = ss;
         }
-        __syncthreads();
-        write_tile(src, live, true, h, s0, count, k, v, vt);
+        const int filled = __syncthreads_count(threadIdx.x < kSlotTile && src[threadIdx.x < kSlotTile ? threadIdx.x : 0].k);
+        if (zero_padding) write_tile(src, live, true, h, s0, count, k, v, vt);
+        else if (filled) write_tile(src, filled, false, h, s0, count, k, v, vt);
+        else __syncthreads();  // src is rewritten by the next item
     }
 }
 
@@ -361,10 +367,11 @@ cudaError_t launch_pack(const uint32_t* ids, size_t kstride, const uint32_t* siz
 
 cudaError_t launch_gather_map(const uint16_t* prefetched, size_t prefetched_rows, const uint16_t* misses,
                               size_t miss_rows, const int32_t* map, size_t count, uint16_t* k, uint16_t* v,
-                              hsb_device_status* status, cudaStream_t stream) {
+                              hsb_device_status* status, cudaStream_t stream, int zero_padding) {
     const size_t items = (count + kSlotTile - 1) / kSlotTile * kHeads;
     gather_map_kernel<<<persistent_grid(items, 8), kThreads, 0, stream>>>(prefetched, prefetched_rows, misses,
-                                                                          miss_rows, map, count, k, v, status);
+                                                                          miss_rows, map, count, k, v, status,
+                                                                          zero_padding);
     return cudaGetLastError();
 }
 

@@ -498,11 +498,13 @@ int hsb_history_select(hsb_history* h, size_t layer, uint64_t position, const ui
  * [32][128][count]; hot rows from the pool, cold rows from d_staged_rows
  * (4096-byte K||V rows of the ascending d_staged_ids, e.g. the cover's cold
  * positions read with hsb_kv_records_verify).  A selected cold ID that was not
- * staged sets HSB_E_MAP_MISS.  Consumes the layer's prepared history. */
+ * staged sets HSB_E_MAP_MISS.  zero_padding != 0 zeroes slots k..count-1
+ * (the reference's packed layout); 0 writes the live slots only, for
+ * attention over sizes = k.  Consumes the layer's prepared history. */
 int hsb_history_fetch(hsb_history* h, size_t layer, const uint32_t* d_ids, size_t kcap,
                       const hsb_selection* d_result, const uint32_t* d_staged_ids, size_t nstaged,
-                      const uint16_t* d_staged_rows, size_t count, uint16_t* d_k, uint16_t* d_v,
-                      hsb_device_status* d_status, void* stream);
+                      const uint16_t* d_staged_rows, size_t count, int zero_padding, uint16_t* d_k,
+                      uint16_t* d_v, hsb_device_status* d_status, void* stream);
 
 /* ------------------------------------------------------ layer executor
  * The model-facing decode step of GQALayerExecutor::prepare
