@@ -50,13 +50,15 @@ def parse():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "kv-sharded", "sweep", "h2o", "records", "history"],
+                    choices=["decode", "kv-sharded", "sweep", "h2o", "records", "history", "executor"],
                     help="decode: configs[1] (the headline); kv-sharded: configs[4], one selected-KV layer "
                          "over --batch sequences with the KV heads split over the ranks; sweep: configs[2], "
                          "the selected-KV layer step per length N; h2o: the H2O group-sum reduction "
                          "(decode and prefill-block shapes) beside the reference's CUDA kernel; records: the "
                          "cold-tier KV record encoder and verifier (FNV-1a) beside the reference's CPU checksum; "
-                         "history: the hot/cold decode history protocol (prepare/select/fetch) per layer")
+                         "history: the hot/cold decode history protocol (prepare/select/fetch) per layer; executor: "
+                         "the model-facing decode step (current-KV append + selection + attention over live slots) "
+                         "beside the reference executor's padded upload")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--h2o-keys", type=int, default=32768, help="h2o workload: keys N")
     ap.add_argument("--h2o-queries", default="1,16,512", help="h2o workload: comma-separated query counts")
@@ -1124,6 +1126,22 @@ def run_history(args, torch):
         assert int(res[2].item()) == 0, res
         launches += 2 * 23 * layers * 10
         graph.reset()
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import binding as ob
+
+        if ob.reference_available():
+            n = prompt + steps + 1
+            host = rows[2][:n].cpu().numpy().view(np.uint16)
+            kc = np.ascontiguousarray(host[:, :1024]).reshape(-1)
+            vc = np.ascontiguousarray(host[:, 1024:]).reshape(-1)
+            q16 = qs[2].cpu().numpy().view(np.uint16).reshape(-1)
+            q32 = q16.view(np.float16).astype(np.float32).reshape(32, 128)
+            threads = min(16, os.cpu_count() or 1)
+            secs, _ = reference_layer_times(kc, vc, q16, q32, n, alpha, threads, True)
+            cpu = {"value": round(secs * 1e6, 1), "unit": "us per layer", "cores": threads, "kind": "reference",
+                   "sample": f"one selected-KV layer at N={n}: FullGqaCpuScorer x{threads}, select_gqa_scores, "
+                             "gqa_physical_union, pack_gqa_workspace (oracle/_ref), attention by the oracle port"}
     hist.close()
     p_us = float(np.median(prep)) * 1e3 / layers
     s_us = float(np.median(self_)) * 1e3 / layers
@@ -1136,7 +1154,91 @@ def run_history(args, torch):
             "host_included_prepare_cover_us_per_layer": round(p_us, 2),
             "host_included_select_fetch_us_per_layer": round(s_us, 2),
             "k_mean": round(float(np.mean(ks)), 2), "cover_cold_rows_mean": round(float(np.mean(colds)), 1),
-            "gpu_launches": launches, "clocks": clocks.summary()}
+            "cpu_baseline": cpu, "gpu_launches": launches, "clocks": clocks.summary()}
+
+
+def run_executor(args, torch):
+    """The model-facing decode step (hsb_executor_decode_layer) for a
+    32-layer step at N = 32768: per layer the model's current K/V tensor is
+    appended to the HBM cache, the rehearsal rounded to F16, and the layer
+    step (or dense attention for layers 0-1) runs over the live slots, one
+    CUDA graph per step.  Beside it, the reference executor's delivery of the
+    same layer (runtime/gqa_executor.cpp:187-207): the padded per-query-head
+    K / V / mask workspace of count slots uploaded from pinned host memory,
+    timed here as that one copy (its CPU selection and packing not counted)."""
+    import hillserve_b200 as hsb
+
+    n, layers = 32768, LAYERS
+    ex = hsb.DecodeExecutor(layers, n + 64, alpha=args.alpha, dense_layers=DENSE)
+    m = Model(hsb, torch, n, layers, args.alpha, seed=3)
+    for l in range(layers):  # the prompt's K/V rows, as prefill leaves them in the cache
+        ex.cache[l][:n, :1024].copy_(m.kc[l].view(n, 1024))
+        ex.cache[l][:n, 1024:].copy_(m.vc[l].view(n, 1024))
+        ex.completed[l] = n
+    g = torch.Generator(device="cuda").manual_seed(4)
+    cur = [torch.empty((1, 8, 256), dtype=torch.float16, device="cuda").normal_(generator=g).view(torch.int16)
+           for _ in range(layers)]
+    reh = [m.q16[l].view(torch.float16).float().reshape(32, 128).contiguous() for l in range(layers)]
+    outs = [torch.empty((32, 128), dtype=torch.float32, device="cuda") for _ in range(layers)]
+    stream = torch.cuda.Stream()
+    lib = hsb._capi.lib()
+    b = ex._buffers()
+    pos = n
+
+    def step():
+        for l in range(layers):
+            rc = lib.hsb_executor_decode_layer(cur[l].data_ptr(), reh[l].data_ptr(), m.q32[l].data_ptr(),
+                                               ex.cache[l].data_ptr(), ex.capacity, pos, int(l < DENSE),
+                                               ctypes.c_float(args.alpha), ctypes.c_float(0.2), ex.count,
+                                               ctypes.byref(b), outs[l].data_ptr(), ex.status.data_ptr(),
+                                               stream.cuda_stream)
+            assert rc == 0, lib.hsb_last_error()
+
+    with torch.cuda.stream(stream):
+        step()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    torch.cuda.synchronize()
+    steps = max(10, min(args.steps, 200))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        e0.record()
+        for _ in range(steps):
+            graph.replay()
+        e1.record()
+        e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    assert not ex.status.any(), ex.status
+    # the reference delivery of one sparse layer: K + V [count][32][128] F16 and
+    # the mask [32][qpad 64][count] F32, uploaded from pinned memory
+    count = ex.count
+    ref_bytes = count * 32 * 128 * 2 * 2 + 32 * 64 * count * 4
+    host = torch.empty(ref_bytes, dtype=torch.uint8).pin_memory()
+    dev = torch.empty(ref_bytes, dtype=torch.uint8, device="cuda")
+    for _ in range(2):
+        dev.copy_(host, non_blocking=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(5):
+        dev.copy_(host, non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    upload_ms = e0.elapsed_time(e1) / 5
+    graph.reset()
+    return {"metric": "model-facing decode step (executor) layer-steps/s at N=32K", "impl": "ours",
+            "workload": "executor", "unit": "layer-steps/s", "value": round(layers / (ms * 1e-3), 1),
+            "ms_per_step": round(ms, 4), "data": "synthetic",
+            "config": {"workload": f"32-layer decode step through hsb_executor_decode_layer, N={n}, "
+                                   f"layers 0-{DENSE - 1} dense", "alpha": args.alpha, "slots": count},
+            "h2d_bytes_per_layer": 0,
+            "reference_delivery": {"bytes_per_layer": ref_bytes, "pinned_upload_ms_per_layer": round(upload_ms, 3),
+                                   "note": "the reference's padded K/V/mask upload alone, per selected-KV layer"},
+            "gpu_launches": (steps + max(3, args.warmup)) * (DENSE * 3 + (layers - DENSE) * 4),
+            "clocks": clocks.summary()}
 
 
 def main():
@@ -1164,6 +1266,8 @@ def main():
         line = run_records(args, torch)
     elif args.workload == "history":
         line = run_history(args, torch)
+    elif args.workload == "executor":
+        line = run_executor(args, torch)
     elif args.workload == "kv-sharded":
         if dist is None:  # one GPU: a world of one, still through the process-group code
             import datetime
