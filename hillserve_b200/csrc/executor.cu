@@ -21,15 +21,31 @@ namespace {
 
 // The model's current KV tensor (ggml_concat(k_cur, v_cur, 0) cast to F16):
 // [token][KV head][K 128 | V 128].  The cache row of a token: K[8][128] then
-// V[8][128] (the payload layout of runtime/gqa_executor.cpp:155).  A block
-// moves one token as 256 16-byte words; a non-finite F16 in the current KV is
-// an error (runtime/gqa_executor.cpp:153).
-__global__ void executor_append_kernel(const uint16_t* __restrict__ current, unsigned long long n,
-                                       uint16_t* __restrict__ cache, unsigned long long first,
-                                       hsb_device_status* status) {
+// V[8][128] (the payload layout of runtime/gqa_executor.cpp:155).  Blocks
+// 0..n-1 move one token each as 256 16-byte words; a non-finite F16 in the
+// current KV is an error (runtime/gqa_executor.cpp:153).  With a rehearsal,
+// block n rounds it to F16 (query_f16, policy/full_gqa_runtime.cpp:61-64: a
+// non-finite input, or an F16 overflow, is an error).  One launch per layer.
+__global__ void __launch_bounds__(256) executor_prepare_kernel(const uint16_t* __restrict__ current,
+                                                               unsigned long long n, uint16_t* __restrict__ cache,
+                                                               unsigned long long first,
+                                                               const float* __restrict__ rehearsal,
+                                                               uint16_t* __restrict__ q16,
+                                                               hsb_device_status* status) {
+    pdl_wait();
+    pdl_trigger();
     const unsigned long long t = blockIdx.x;
-    if (t >= n) return;
-    const int i = threadIdx.x;  // 256 threads
+    const int i = threadIdx.x;
+    if (t == n) {
+        for (int j = i; j < kHeads * kDim; j += blockDim.x) {
+            const float x = rehearsal[j];
+            const uint16_t h = half_bits(x);
+            q16[j] = h;
+            if (!isfinite(x)) raise_status(status, HSB_E_EXECUTOR_REHEARSAL, j);
+            else if (!is_finite_half(h)) raise_status(status, HSB_E_EXECUTOR_REHEARSAL_F16, j);
+        }
+        return;
+    }
     const int head = i >> 5, part = (i >> 4) & 1, c8 = i & 15;
     const uint4 w = reinterpret_cast<const uint4*>(current + t * 2048 + head * 256 + part * 128)[c8];
     reinterpret_cast<uint4*>(cache + (first + t) * 2048 + part * 1024 + head * 128)[c8] = w;
@@ -41,17 +57,11 @@ __global__ void executor_append_kernel(const uint16_t* __restrict__ current, uns
     if (!__syncthreads_and(finite) && i == 0) raise_status(status, HSB_E_EXECUTOR_NONFINITE_KV, (int)t);
 }
 
-// query_f16 (policy/full_gqa_runtime.cpp:61-64): a finite F32 rehearsal
-// rounded to F16 with the reference's rule, which must stay finite.
-__global__ void executor_query_kernel(const float* __restrict__ rehearsal, uint16_t* __restrict__ q16,
-                                     hsb_device_status* status) {
-    for (int i = threadIdx.x; i < kHeads * kDim; i += blockDim.x) {
-        const float x = rehearsal[i];
-        const uint16_t h = half_bits(x);
-        q16[i] = h;
-        if (!isfinite(x)) raise_status(status, HSB_E_EXECUTOR_REHEARSAL, i);
-        else if (!is_finite_half(h)) raise_status(status, HSB_E_EXECUTOR_REHEARSAL_F16, i);
-    }
+cudaError_t launch_prepare(const uint16_t* current, size_t n, uint16_t* cache, size_t first, const float* rehearsal,
+                           uint16_t* q16, hsb_device_status* status, cudaStream_t stream) {
+    const unsigned blocks = (unsigned)(n + (rehearsal ? 1 : 0));
+    return launch_dependent(executor_prepare_kernel, dim3(blocks), dim3(256), 0, stream, false, current,
+                            (unsigned long long)n, cache, (unsigned long long)first, rehearsal, q16, status);
 }
 
 size_t align256(size_t x) { return (x + 255) / 256 * 256; }
@@ -71,9 +81,8 @@ int hsb_executor_append(const uint16_t* d_current, size_t n_tokens, uint16_t* d_
         return record_error(HSB_E_EXECUTOR_SHAPE, "GQA current KV ABI mismatch");
     if ((reinterpret_cast<uintptr_t>(d_current) | reinterpret_cast<uintptr_t>(d_cache)) & 15u)
         return record_error(HSB_E_INVALID, "executor tensors must be 16-byte aligned");
-    executor_append_kernel<<<(unsigned)n_tokens, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        d_current, n_tokens, d_cache, first_position, d_status);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_prepare(d_current, n_tokens, d_cache, first_position, nullptr, nullptr, d_status,
+                                   static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return record_cuda_error(e, "executor append launch");
     record_error(HSB_OK, "");
     return HSB_OK;
@@ -82,8 +91,8 @@ int hsb_executor_append(const uint16_t* d_current, size_t n_tokens, uint16_t* d_
 int hsb_executor_query(const float* d_rehearsal, uint16_t* d_q16, hsb_device_status* d_status, void* stream) {
     if (!d_rehearsal || !d_q16 || !d_status)
         return record_error(HSB_E_EXECUTOR_SHAPE, "full GQA actual rehearsal must be32x128");
-    executor_query_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(d_rehearsal, d_q16, d_status);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_prepare(nullptr, 0, nullptr, 0, d_rehearsal, d_q16, d_status,
+                                   static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return record_cuda_error(e, "executor query launch");
     record_error(HSB_OK, "");
     return HSB_OK;
@@ -105,16 +114,20 @@ int hsb_executor_decode_layer(const uint16_t* d_current, const float* d_rehearsa
     const size_t layer_bytes = align256(std::max(hsb_layer_workspace_bytes(capacity, count),
                                                  hsb_attention_dense_workspace_bytes(capacity)));
     uint16_t* q16 = reinterpret_cast<uint16_t*>(static_cast<unsigned char*>(buffers->workspace) + layer_bytes);
-    int rc = hsb_executor_append(d_current, 1, d_cache, capacity, position, d_status, stream);
-    if (rc) return rc;
+    if (!d_current || !d_cache || !d_status || position >= capacity || (!dense && !d_rehearsal))
+        return record_error(HSB_E_EXECUTOR_SHAPE, "GQA current KV ABI mismatch");
+    if ((reinterpret_cast<uintptr_t>(d_current) | reinterpret_cast<uintptr_t>(d_cache)) & 15u)
+        return record_error(HSB_E_INVALID, "executor tensors must be 16-byte aligned");
+    // the current token's append and (sparse layers) the selection query, one launch
+    cudaError_t e = launch_prepare(d_current, 1, d_cache, position, dense ? nullptr : d_rehearsal, q16, d_status,
+                                   static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return record_cuda_error(e, "executor prepare launch");
     const size_t valid = position + 1;
     if (dense) {
         // the two dense layers (runtime/gqa_executor.cpp:174-176): every position
         return hsb_attention_dense(d_q, d_cache, d_cache + 1024, valid, 2048, d_out, buffers->workspace, layer_bytes,
                                    stream);
     }
-    rc = hsb_executor_query(d_rehearsal, q16, d_status, stream);
-    if (rc) return rc;
     hsb_layer_buffers b = *buffers;
     b.workspace_bytes = layer_bytes;
     return hsb_layer_step(q16, d_q, d_cache, d_cache + 1024, 2048, valid, alpha, ratio, count, &b, d_out, stream);
