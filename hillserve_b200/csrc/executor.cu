@@ -24,8 +24,10 @@ namespace {
 // V[8][128] (the payload layout of runtime/gqa_executor.cpp:155).  Blocks
 // 0..n-1 move one token each as 256 16-byte words; a non-finite F16 in the
 // current KV is an error (runtime/gqa_executor.cpp:153).  With a rehearsal,
-// block n rounds it to F16 (query_f16, policy/full_gqa_runtime.cpp:61-64: a
-// non-finite input, or an F16 overflow, is an error).  One launch per layer.
+// blocks n..n+3 round it to F16 (query_f16, policy/full_gqa_runtime.cpp:
+// 61-64: a non-finite input, or an F16 overflow, is an error).  One launch
+// per layer.
+constexpr int kQueryBlocks = 4;
 __global__ void __launch_bounds__(256) executor_prepare_kernel(const uint16_t* __restrict__ current,
                                                                unsigned long long n, uint16_t* __restrict__ cache,
                                                                unsigned long long first,
@@ -36,8 +38,9 @@ __global__ void __launch_bounds__(256) executor_prepare_kernel(const uint16_t* _
     pdl_trigger();
     const unsigned long long t = blockIdx.x;
     const int i = threadIdx.x;
-    if (t == n) {
-        for (int j = i; j < kHeads * kDim; j += blockDim.x) {
+    if (t >= n) {  // blocks n .. n+3: a quarter of the query each
+        const int q0 = (int)(t - n) * (kHeads * kDim / kQueryBlocks);
+        for (int j = q0 + i; j < q0 + kHeads * kDim / kQueryBlocks; j += blockDim.x) {
             const float x = rehearsal[j];
             const uint16_t h = half_bits(x);
             q16[j] = h;
@@ -59,7 +62,7 @@ __global__ void __launch_bounds__(256) executor_prepare_kernel(const uint16_t* _
 
 cudaError_t launch_prepare(const uint16_t* current, size_t n, uint16_t* cache, size_t first, const float* rehearsal,
                            uint16_t* q16, hsb_device_status* status, cudaStream_t stream) {
-    const unsigned blocks = (unsigned)(n + (rehearsal ? 1 : 0));
+    const unsigned blocks = (unsigned)(n + (rehearsal ? kQueryBlocks : 0));
     return launch_dependent(executor_prepare_kernel, dim3(blocks), dim3(256), 0, stream, false, current,
                             (unsigned long long)n, cache, (unsigned long long)first, rehearsal, q16, status);
 }
