@@ -387,17 +387,22 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
     // ---------------- consumers
     const int kh = warp;
     const float4* qv = qs + kh * kDim;
-    float M[kGroup], L[kGroup], o[kGroup][4];
+    // Accumulators in pairs for the paired FP32 FMA (__ffma2_rn: two
+    // independent fma.rn, the same roundings as fmaf): the scores a01 = heads
+    // {0,1}, a23 = {2,3}; the outputs o2[j][0] = heads {0,1}, o2[j][1] =
+    // {2,3} of channel slot j.
+    float M[kGroup], L[kGroup];
+    float2 o2[4][2];
 #pragma unroll
     for (int g = 0; g < kGroup; ++g) {
         M[g] = -INFINITY;
         L[g] = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) o[g][j] = 0.0f;
     }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o2[j][0] = o2[j][1] = make_float2(0.0f, 0.0f);
     uint32_t it = 0;
     for (unsigned tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
-        float a[kGroup] = {0.f, 0.f, 0.f, 0.f};
+        float2 a01 = make_float2(0.0f, 0.0f), a23 = make_float2(0.0f, 0.0f);
         for (int half = 0; half < 2; ++half, ++it) {
             const uint32_t s = it % kDTSlots;
             if (!mbar_wait(&full[s], (it / kDTSlots) & 1)) {
@@ -413,14 +418,11 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
                 for (int e = 0; e < 4; ++e) {
                     const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&words[e]));
                     const float4 qa = qv[half * 64 + j * 8 + 2 * e], qb = qv[half * 64 + j * 8 + 2 * e + 1];
-                    a[0] = fmaf(qa.x, f.x, a[0]);
-                    a[1] = fmaf(qa.y, f.x, a[1]);
-                    a[2] = fmaf(qa.z, f.x, a[2]);
-                    a[3] = fmaf(qa.w, f.x, a[3]);
-                    a[0] = fmaf(qb.x, f.y, a[0]);
-                    a[1] = fmaf(qb.y, f.y, a[1]);
-                    a[2] = fmaf(qb.z, f.y, a[2]);
-                    a[3] = fmaf(qb.w, f.y, a[3]);
+                    const float2 fx = make_float2(f.x, f.x), fy = make_float2(f.y, f.y);
+                    a01 = __ffma2_rn(make_float2(qa.x, qa.y), fx, a01);
+                    a23 = __ffma2_rn(make_float2(qa.z, qa.w), fx, a23);
+                    a01 = __ffma2_rn(make_float2(qb.x, qb.y), fy, a01);
+                    a23 = __ffma2_rn(make_float2(qb.z, qb.w), fy, a23);
                 }
             }
             __syncwarp();
@@ -428,17 +430,23 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
         }
         // online softmax over this tile (tokens past the end weigh 0)
         const bool valid = tile * 32 + lane < p.tokens;
-        float pr[kGroup];
+        const float a[kGroup] = {a01.x, a01.y, a23.x, a23.y};
+        float pr[kGroup], fg[kGroup];
 #pragma unroll
         for (int g = 0; g < kGroup; ++g) {
             const float sg = valid ? a[g] * p.scale : -INFINITY;
             const float mn = fmaxf(M[g], warp_max(sg));  // finite: the tile has a valid token
-            const float f = expf(M[g] - mn);              // 0 on the first tile
+            fg[g] = expf(M[g] - mn);                      // 0 on the first tile
             pr[g] = valid ? expf(sg - mn) : 0.0f;
-            L[g] = fmaf(L[g], f, warp_sum(pr[g]));
-#pragma unroll
-            for (int j = 0; j < 4; ++j) o[g][j] *= f;
+            L[g] = fmaf(L[g], fg[g], warp_sum(pr[g]));
             M[g] = mn;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            o2[j][0].x *= fg[0];
+            o2[j][0].y *= fg[1];
+            o2[j][1].x *= fg[2];
+            o2[j][1].y *= fg[3];
         }
         // The tile's weights, one float4 per token: P.V reads them by broadcast.
         pw[kh * 32 + lane] = make_float4(pr[0], pr[1], pr[2], pr[3]);
@@ -456,12 +464,12 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
                 const uint32_t w = *reinterpret_cast<const uint32_t*>(base + t * 128 + (((lane >> 2) ^ (t & 7)) << 4));
                 const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
                 const float4 p4 = pt[t];
-                const float pg[kGroup] = {p4.x, p4.y, p4.z, p4.w};
-#pragma unroll
-                for (int g = 0; g < kGroup; ++g) {
-                    o[g][2 * half] = fmaf(pg[g], f.x, o[g][2 * half]);
-                    o[g][2 * half + 1] = fmaf(pg[g], f.y, o[g][2 * half + 1]);
-                }
+                const float2 p01 = make_float2(p4.x, p4.y), p23 = make_float2(p4.z, p4.w);
+                const float2 fx = make_float2(f.x, f.x), fy = make_float2(f.y, f.y);
+                o2[2 * half][0] = __ffma2_rn(p01, fx, o2[2 * half][0]);
+                o2[2 * half][1] = __ffma2_rn(p23, fx, o2[2 * half][1]);
+                o2[2 * half + 1][0] = __ffma2_rn(p01, fy, o2[2 * half + 1][0]);
+                o2[2 * half + 1][1] = __ffma2_rn(p23, fy, o2[2 * half + 1][1]);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
@@ -474,10 +482,12 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
             part[0] = M[g];
             part[1] = L[g];
         }
-        part[2 + 2 * lane] = o[g][0];
-        part[3 + 2 * lane] = o[g][1];
-        part[2 + 64 + 2 * lane] = o[g][2];
-        part[3 + 64 + 2 * lane] = o[g][3];
+        const int pair = g >> 1;
+        const bool second = g & 1;
+        part[2 + 2 * lane] = second ? o2[0][pair].y : o2[0][pair].x;
+        part[3 + 2 * lane] = second ? o2[1][pair].y : o2[1][pair].x;
+        part[2 + 64 + 2 * lane] = second ? o2[2][pair].y : o2[2][pair].x;
+        part[3 + 64 + 2 * lane] = second ? o2[3][pair].y : o2[3][pair].x;
     }
 }
 
