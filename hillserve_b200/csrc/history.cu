@@ -17,15 +17,16 @@
 // (a hot run reads the pool, a cold run the cold K), columns = positions:
 // the same raw F16 scores as the reference's hot + cold merge.
 //
-// Protocol.  prepare() scores the history [0, position) and its payload
-// cover (hsb_prefetch_cover) on the history's own stream, like the
-// reference's async job (cover() then lists the cover's cold positions);
-// select() joins it on the caller's stream, scores
-// the current token, normalises and selects; fetch() builds the gather map
-// of the selected IDs (hot -> pool slot, cold -> the caller's staged rows)
-// and packs K/V with hsb_gather_map's kernel (live slots only, or zero
-// padding up to `count`).  The reference's protocol
-// checks are kept, with its messages.
+// Protocol.  prepare() scores the history [0, position) -- raw scores and
+// the order keys of the normalised ones -- and selects its payload cover
+// (the selector in cover mode, on those keys) on the history's own stream,
+// like the reference's async job; cover() then lists the cover's cold
+// positions.  select() joins the job on the caller's stream, scores the
+// current token and selects on the keys; fetch() builds the gather map of
+// the selected IDs (hot -> pool slot, cold -> the caller's staged rows) and
+// packs K/V with hsb_gather_map's kernel (live slots only, or zero padding
+// up to `count`).  The reference's protocol checks are kept, with its
+// messages.
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -258,6 +259,7 @@ struct hsb_history {
         size_t layer = 0;
         uint64_t position = 0;
         uint16_t* raw = nullptr;   // [32][capacity]
+        uint16_t* keys = nullptr;  // [32][capacity] order keys of the normalised scores
         uint16_t* query = nullptr; // [32][128] F16 of prepare()
         uint32_t* cover = nullptr; // [32][cap]
         size_t cap = 0;
@@ -266,6 +268,7 @@ struct hsb_history {
         cudaEvent_t inputs = nullptr;
     } jobs[2];
     uint16_t* raw_direct = nullptr;  // select() without a prepared history
+    uint16_t* keys_direct = nullptr;
     void* select_ws = nullptr;
     size_t select_ws_bytes = 0;
     void* cover_ws = nullptr;
@@ -425,6 +428,7 @@ int hsb_history_create(const hsb_history_config* cfg, const int64_t* hot_slot_by
     h->select_ws_bytes = select_workspace_bytes(kHeads, c.capacity, h->kcap);
     for (auto& j : h->jobs) {
         j.raw = keep(h.get(), dev_alloc<uint16_t>((size_t)kHeads * c.capacity, &e));
+        j.keys = keep(h.get(), dev_alloc<uint16_t>((size_t)kHeads * c.capacity, &e));
         j.query = keep(h.get(), dev_alloc<uint16_t>((size_t)kHeads * kDim, &e));
         j.cover = keep(h.get(), dev_alloc<uint32_t>((size_t)kHeads * h->cover_cap, &e));
         j.cover_result = keep(h.get(), dev_alloc<hsb_selection>(1, &e));
@@ -432,6 +436,7 @@ int hsb_history_create(const hsb_history_config* cfg, const int64_t* hot_slot_by
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&j.inputs, cudaEventDisableTiming);
     }
     h->raw_direct = keep(h.get(), dev_alloc<uint16_t>((size_t)kHeads * c.capacity, &e));
+    h->keys_direct = keep(h.get(), dev_alloc<uint16_t>((size_t)kHeads * c.capacity, &e));
     h->select_ws = keep(h.get(), dev_alloc<unsigned char>(h->select_ws_bytes, &e));
     h->cover_ws = keep(h.get(), dev_alloc<unsigned char>(h->cover_ws_bytes, &e));
     if (e != cudaSuccess) return record_cuda_error(e, "history allocation");
@@ -491,14 +496,34 @@ int hsb_history_prepare(hsb_history* h, size_t layer, uint64_t position, const u
     if (e == cudaSuccess) e = cudaStreamWaitEvent(h->work, J.inputs, 0);
     if (e == cudaSuccess) e = cudaMemcpyAsync(J.query, d_q16, kHeads * kDim * 2, cudaMemcpyDeviceToDevice, h->work);
     if (e == cudaSuccess)
-        e = score_runs(J.query, L.runs, position, L.pool, kRowWords, L.cold, kKeyWords, J.raw, c.capacity, nullptr,
+        e = score_runs(J.query, L.runs, position, L.pool, kRowWords, L.cold, kKeyWords, J.raw, c.capacity, J.keys,
                        h->work);
     if (e != cudaSuccess) return record_cuda_error(e, "history prepare launch");
-    // The payload cover of the final selection (policy/full_gqa_runtime.cpp:299-344).
+    // The payload cover of the final selection (policy/full_gqa_runtime.cpp:299-344),
+    // from the scorer's order keys: hsb_prefetch_cover's selection on its
+    // normalised scores, without normalising them again.
     const size_t cap = std::min<size_t>(position, (size_t)std::floor(double(position + 1) * double(0.2f)));
-    int rc = hsb_prefetch_cover(J.raw, c.capacity, position, c.alpha, c.fp32_counts, J.cover, cap, J.cover_result,
-                                h->cover_ws, h->cover_ws_bytes, h->work);
-    if (rc) return rc;
+    if (!cap) return history_fail(HSB_E_COVER_RANGE, "payload prefetch historical cap/range mismatch");
+    SelectLaunch sl{};
+    sl.scores = J.keys;
+    sl.keys = 1;
+    sl.tie_raw = J.raw;
+    sl.cover = 1;
+    sl.heads = kHeads;
+    sl.stride = c.capacity;
+    sl.valid = position;
+    sl.alpha = c.alpha;
+    sl.ratio = 1.0f;
+    sl.fp32_counts = c.fp32_counts != 0;
+    sl.ids = J.cover;
+    sl.kcap = cap;
+    sl.counts = nullptr;
+    sl.result = J.cover_result;
+    sl.workspace = h->cover_ws;
+    sl.workspace_bytes = h->cover_ws_bytes;
+    sl.cover_cap = cap;
+    e = launch_select(sl, h->work);
+    if (e != cudaSuccess) return record_cuda_error(e, "history cover launch");
     J.cap = cap;
     e = cudaEventRecord(J.ready, h->work);
     if (e != cudaSuccess) return record_cuda_error(e, "history prepare event");
@@ -544,25 +569,28 @@ int hsb_history_select(hsb_history* h, size_t layer, uint64_t position, const ui
     if (!d_q16 || !d_ids || !d_result) return history_fail(HSB_E_INVALID, "null selector buffer");
     const auto s = static_cast<cudaStream_t>(stream);
     uint16_t* raw = h->raw_direct;
+    uint16_t* keys = h->keys_direct;
     cudaError_t e = cudaSuccess;
     if (L.job >= 0) {
         auto& J = h->jobs[L.job];
         if (J.position != position)
             return history_fail(HSB_E_HISTORY_PROTOCOL, "history Q/position differs from current same-query selection");
         raw = J.raw;
+        keys = J.keys;
         if (e == cudaSuccess) e = cudaStreamWaitEvent(s, J.ready, 0);
         // the current token, an ordinary candidate (full_gqa_runtime.cpp:531-548)
         const Run current{0, 1, true, (uint64_t)L.row_of_position[position]};  // generated: always hot
         if (e == cudaSuccess)
             e = score_runs(d_q16, std::vector<Run>{current}, 1, L.pool, kRowWords, L.cold, kKeyWords, raw + position,
-                           c.capacity, nullptr, s);
+                           c.capacity, keys + position, s);
     } else if (e == cudaSuccess) {
-        e = score_runs(d_q16, L.runs, position + 1, L.pool, kRowWords, L.cold, kKeyWords, raw, c.capacity, nullptr,
-                       s);
+        e = score_runs(d_q16, L.runs, position + 1, L.pool, kRowWords, L.cold, kKeyWords, raw, c.capacity, keys, s);
     }
     if (e != cudaSuccess) return record_cuda_error(e, "history select launch");
-    int rc = hsb_select(raw, 1, kHeads, c.capacity, position + 1, c.alpha, 0.2f, c.fp32_counts, d_ids, kcap,
-                        d_counts, d_result, h->select_ws, h->select_ws_bytes, stream);
+    // select_gqa_scores on the scorer's order keys (the raw scores break a
+    // boundary tie between +0 and -0, as in the layer step)
+    int rc = hsb_select_keys(keys, raw, kHeads, c.capacity, position + 1, c.alpha, 0.2f, c.fp32_counts, d_ids, kcap,
+                             d_counts, d_result, h->select_ws, h->select_ws_bytes, stream);
     if (rc) return rc;
     if (L.job >= 0) {
         history_query_check_kernel<<<1, 256, 0, s>>>(h->jobs[L.job].query, d_q16, d_result);
