@@ -104,6 +104,8 @@ __global__ void history_append_kernel(const uint16_t* __restrict__ rows, unsigne
                                       unsigned long long count, const int32_t* __restrict__ slot,
                                       const int32_t* __restrict__ cold_row, uint16_t* __restrict__ pool,
                                       uint16_t* __restrict__ cold) {
+    pdl_wait();
+    pdl_trigger();
     const unsigned long long t = blockIdx.x;
     if (t >= count) return;
     const unsigned long long pos = first + t;
@@ -133,6 +135,8 @@ __global__ void __launch_bounds__(1024) history_cover_cold_kernel(const uint32_t
                                                                   uint32_t* __restrict__ out_count) {
     __shared__ uint32_t bits[kCoverWords];
     __shared__ uint32_t warp_total[32];
+    pdl_wait();
+    pdl_trigger();
     const unsigned tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const unsigned words = (unsigned)((position + 31) / 32);
     for (unsigned w = tid; w < words; w += blockDim.x) bits[w] = 0;
@@ -176,6 +180,8 @@ __global__ void history_map_kernel(const uint32_t* __restrict__ ids, unsigned lo
                                    unsigned long long completed, const uint32_t* __restrict__ staged,
                                    unsigned long long nstaged, unsigned long long count, int32_t* __restrict__ map,
                                    hsb_device_status* status) {
+    pdl_wait();
+    pdl_trigger();
     const unsigned long long i = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= 32ull * count) return;
     const unsigned h = (unsigned)(i / count);
@@ -215,6 +221,8 @@ __global__ void history_map_kernel(const uint32_t* __restrict__ ids, unsigned lo
 // status the selection left.
 __global__ void history_query_check_kernel(const uint16_t* __restrict__ a, const uint16_t* __restrict__ b,
                                            hsb_selection* result) {
+    pdl_wait();
+    pdl_trigger();
     bool same = true;
     for (int i = threadIdx.x; i < kHeads * kDim; i += blockDim.x) same &= a[i] == b[i];
     if (!__syncthreads_and(same) && threadIdx.x == 0) {
@@ -464,9 +472,10 @@ int hsb_history_append(hsb_history* h, size_t layer, uint64_t first, size_t coun
         return history_fail(HSB_E_HISTORY_PROTOCOL, "prefetched history permits only its current-token append");
     if ((reinterpret_cast<uintptr_t>(d_rows) & 15u) != 0)
         return history_fail(HSB_E_INVALID, "history rows must be 16-byte aligned");
-    history_append_kernel<<<(unsigned)count, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-        d_rows, first, count, L.slot, L.cold_row, L.pool, L.cold);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_dependent(history_append_kernel, dim3((unsigned)count), dim3(128), 0,
+                                     static_cast<cudaStream_t>(stream), false, d_rows, (unsigned long long)first,
+                                     (unsigned long long)count, (const int32_t*)L.slot, (const int32_t*)L.cold_row,
+                                     L.pool, L.cold);
     if (e != cudaSuccess) return record_cuda_error(e, "history append launch");
     L.completed += count;
     record_error(HSB_OK, "");
@@ -544,8 +553,9 @@ int hsb_history_cover(hsb_history* h, size_t layer, uint32_t* d_cold_ids, uint32
     const auto s = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaStreamWaitEvent(s, J.ready, 0);
     if (e == cudaSuccess && d_cold_ids && d_cold_count)
-        history_cover_cold_kernel<<<1, 1024, 0, s>>>(J.cover, J.cap, J.cover_result, L.slot, J.position, d_cold_ids,
-                                                     d_cold_count);
+        e = launch_dependent(history_cover_cold_kernel, dim3(1), dim3(1024), 0, s, false, (const uint32_t*)J.cover,
+                             (unsigned long long)J.cap, (const hsb_selection*)J.cover_result, (const int32_t*)L.slot,
+                             (unsigned long long)J.position, d_cold_ids, d_cold_count);
     if (e == cudaSuccess && d_cover_result)
         e = cudaMemcpyAsync(d_cover_result, J.cover_result, sizeof(hsb_selection), cudaMemcpyDeviceToDevice, s);
     if (e == cudaSuccess) e = cudaGetLastError();
@@ -593,8 +603,8 @@ int hsb_history_select(hsb_history* h, size_t layer, uint64_t position, const ui
                              d_counts, d_result, h->select_ws, h->select_ws_bytes, stream);
     if (rc) return rc;
     if (L.job >= 0) {
-        history_query_check_kernel<<<1, 256, 0, s>>>(h->jobs[L.job].query, d_q16, d_result);
-        e = cudaGetLastError();
+        e = launch_dependent(history_query_check_kernel, dim3(1), dim3(256), 0, s, false,
+                             (const uint16_t*)h->jobs[L.job].query, d_q16, d_result);
         if (e != cudaSuccess) return record_cuda_error(e, "history query check launch");
     }
     L.last_selected = position;
@@ -624,12 +634,13 @@ int hsb_history_fetch(hsb_history* h, size_t layer, const uint32_t* d_ids, size_
         h->map_capacity = 32 * count;
     }
     const unsigned threads = 256;
-    history_map_kernel<<<(unsigned)((32 * count + threads - 1) / threads), threads, 0, s>>>(
-        d_ids, kcap, d_result, L.slot, L.completed, d_staged_ids, nstaged, count, h->map, d_status);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_dependent(history_map_kernel, dim3((unsigned)((32 * count + threads - 1) / threads)),
+                                     dim3(threads), 0, s, false, d_ids, (unsigned long long)kcap, d_result,
+                                     (const int32_t*)L.slot, (unsigned long long)L.completed, d_staged_ids,
+                                     (unsigned long long)nstaged, (unsigned long long)count, h->map, d_status);
     if (e == cudaSuccess)
         e = launch_gather_map(L.pool, h->hot_slots, d_staged_rows ? d_staged_rows : L.pool, nstaged, h->map, count,
-                              d_k, d_v, d_status, s, zero_padding);
+                              d_k, d_v, d_status, s, zero_padding, &d_result->k);
     if (e != cudaSuccess) return record_cuda_error(e, "history fetch launch");
     // The prepared job is consumed (policy/full_gqa_runtime.cpp:620-622).
     if (L.job >= 0) {

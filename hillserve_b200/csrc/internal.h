@@ -157,10 +157,11 @@ cudaError_t launch_pack(const uint32_t* ids, size_t kstride, const uint32_t* siz
                         cudaStream_t stream);
 // zero_padding 0: only each head's leading slots with a source are written
 // (the map must put its sources first); the rest of the layout is untouched.
+// live_k (device, with zero_padding 0): no head has a source at slot >= *live_k.
 cudaError_t launch_gather_map(const uint16_t* prefetched, size_t prefetched_rows,
                               const uint16_t* misses, size_t miss_rows, const int32_t* map,
                               size_t count, uint16_t* k, uint16_t* v, hsb_device_status* status,
-                              cudaStream_t stream, int zero_padding = 1);
+                              cudaStream_t stream, int zero_padding = 1, const uint32_t* live_k = nullptr);
 cudaError_t launch_gather_cache(const uint32_t* ids, size_t kstride, const uint32_t* sizes,
                                 size_t sizes_stride, const uint16_t* kcache,
                                 const uint16_t* vcache, size_t stride_words, size_t visible,

@@ -242,14 +242,18 @@ __global__ void __launch_bounds__(kThreads) gather_map_kernel(const uint16_t* __
                                                               size_t mrows, const int32_t* __restrict__ map,
                                                               size_t count, uint16_t* __restrict__ k,
                                                               uint16_t* __restrict__ v, hsb_device_status* status,
-                                                              int zero_padding) {
+                                                              int zero_padding, const uint32_t* __restrict__ live_k) {
     __shared__ SlotSource src[kSlotTile];
     __shared__ __align__(16) uint16_t vt[kSlotTile][kVPitch];
     const size_t tiles_per_head = (count + kSlotTile - 1) / kSlotTile;
-    const size_t total = tiles_per_head * kHeads;
+    // Live slots only, with their number on the device: walk only the tiles
+    // that can hold one.
+    const size_t live_tiles =
+        (!zero_padding && live_k) ? (std::min<size_t>(*live_k, count) + kSlotTile - 1) / kSlotTile : tiles_per_head;
+    const size_t total = live_tiles * kHeads;
     for (size_t item = blockIdx.x; item < total; item += gridDim.x) {
-        const int h = (int)(item / tiles_per_head);
-        const size_t s0 = (item % tiles_per_head) * kSlotTile;
+        const int h = (int)(item / live_tiles);
+        const size_t s0 = (item % live_tiles) * kSlotTile;
         const int live = (int)std::min<size_t>(kSlotTile, count - s0);
         const int kh = h >> 2;
         if (threadIdx.x < kSlotTile) {
@@ -367,11 +371,12 @@ cudaError_t launch_pack(const uint32_t* ids, size_t kstride, const uint32_t* siz
 
 cudaError_t launch_gather_map(const uint16_t* prefetched, size_t prefetched_rows, const uint16_t* misses,
                               size_t miss_rows, const int32_t* map, size_t count, uint16_t* k, uint16_t* v,
-                              hsb_device_status* status, cudaStream_t stream, int zero_padding) {
+                              hsb_device_status* status, cudaStream_t stream, int zero_padding,
+                              const uint32_t* live_k) {
     const size_t items = (count + kSlotTile - 1) / kSlotTile * kHeads;
     gather_map_kernel<<<persistent_grid(items, 8), kThreads, 0, stream>>>(prefetched, prefetched_rows, misses,
                                                                           miss_rows, map, count, k, v, status,
-                                                                          zero_padding);
+                                                                          zero_padding, live_k);
     return cudaGetLastError();
 }
 
