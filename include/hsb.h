@@ -459,6 +459,8 @@ int hsb_score_history(const uint16_t* d_q, const uint16_t* d_hot_pool, size_t po
 int hsb_history_plan_slots(size_t prompt_tokens, size_t generated_capacity, size_t capacity, double beta,
                            int allow_partial_prompt, int64_t* hot_slot_by_position, size_t* hot_prompt_tokens);
 
+/* A history is one request's state: drive it from one host thread at a time
+ * (its calls check and update host-side protocol state). */
 typedef struct hsb_history hsb_history;
 typedef struct hsb_history_config {
     size_t layers;              /* <= 32 */
