@@ -310,28 +310,21 @@ __global__ void __launch_bounds__(kDThreads) attention_dense_kernel(const __grid
 // ------------------------------------------------------------- dense (TMA)
 // Dense decode attention streamed like the scorer: a ring of 32 KB TMA boxes
 // ({64 channels, 32 tokens, 8 KV heads}, 128-byte swizzle) carries, per
-// 32-token tile, K channels 0-63, K 64-127, V 0-63, V 64-127.  Sixteen
-// consumer warps: warp w is KV head w % 8 and channel half w / 8, so each box
-// is read by the eight warps of its half.  For the logits lane l is token l:
-// a warp forms the dot products over its 64 channels (FP32, paired FMAs) and
-// the two warps of a KV head add their halves through shared memory (a
-// double-buffered exchange, paced by a per-head mbarrier with bounded waits);
-// both then run the same online softmax per query head.  For P.V a warp owns
-// the output channels of its half (lane l: channels 2(l/4)*.. of its box, as
-// the swizzle lays them out), the tile's weights arriving by shared-memory
-// broadcast.  One CTA per SM walks tiles blockIdx.x, +gridDim.x, ... and
-// writes one (max, sum, out[128]) partial per query head;
-// dense_combine_kernel folds them.
+// 32-token tile, K channels 0-63, K 64-127, V 0-63, V 64-127.  Warp w is KV
+// head w.  For the logits lane l is token l (the scorer's dot products, FP32);
+// an online softmax per query head keeps (max, sum) per warp; for P.V lane l
+// owns channels 2l, 2l+1 of each half, the tile's weights arriving by
+// shuffle.  One CTA per SM walks tiles blockIdx.x, +gridDim.x, ... and writes
+// one (max, sum, out[128]) partial per query head; dense_combine_kernel folds
+// them.
 constexpr int kDTBox = 32 * kKvHeads * 64 * 2;  // bytes per box
-constexpr int kDTSlots = 5;
-constexpr int kDTConsumers = 2 * kKvHeads;
+constexpr int kDTSlots = 6;
+constexpr int kDTConsumers = kKvHeads;
 constexpr int kDTThreads = (kDTConsumers + 1) * 32;
 constexpr int kDTQBytes = kKvHeads * kDim * kGroup * 4;  // F32 [kv][c][4 heads]
-constexpr int kDTPBytes = kDTConsumers * 32 * 16;         // per warp: the tile's weights, float4 [token][4 heads]
-constexpr int kDTXBytes = 2 * kDTConsumers * 32 * 16;     // [tile parity][warp]: half-channel logits, float4 [token]
-constexpr int kDTSmem = 1024 + kDTSlots * kDTBox + kDTQBytes + kDTPBytes + kDTXBytes + (2 * kDTSlots + kKvHeads) * 8;
+constexpr int kDTPBytes = kDTConsumers * 32 * 16;  // per warp: the tile's weights, float4 [token][4 heads]
+constexpr int kDTSmem = 1024 + kDTSlots * kDTBox + kDTQBytes + kDTPBytes + 2 * kDTSlots * 8;
 constexpr int kDenseMaxCtas = 256;
-static_assert(kDTSmem <= 227 * 1024, "dense attention shared memory");
 
 struct DenseTmaParams {
     CUtensorMap kmap, vmap;
@@ -350,10 +343,8 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
     unsigned char* slots = smem;
     float4* qs = reinterpret_cast<float4*>(smem + kDTSlots * kDTBox);
     float4* pw = reinterpret_cast<float4*>(smem + kDTSlots * kDTBox + kDTQBytes);
-    float4* xs = reinterpret_cast<float4*>(smem + kDTSlots * kDTBox + kDTQBytes + kDTPBytes);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDTSlots * kDTBox + kDTQBytes + kDTPBytes + kDTXBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDTSlots * kDTBox + kDTQBytes + kDTPBytes);
     uint64_t* empty = full + kDTSlots;
-    uint64_t* pair = empty + kDTSlots;  // [KV head]: both halves' logits written
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < kHeads * kDim; i += blockDim.x) {
         const int h = i >> 7, c = i & 127;
@@ -362,9 +353,8 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
     if (threadIdx.x == 0) {
         for (int s = 0; s < kDTSlots; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kDTConsumers / 2);  // a box is read by one half's eight warps
+            mbar_init(&empty[s], kDTConsumers);
         }
-        for (int k = 0; k < kKvHeads; ++k) mbar_init(&pair[k], 2);
         mbar_fence_init();
     }
     __syncthreads();
@@ -395,26 +385,25 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
     }
 
     // ---------------- consumers
-    const int kh = warp & (kKvHeads - 1), hf = warp / kKvHeads;
-    const float4* qv = qs + kh * kDim + hf * 64;
+    const int kh = warp;
+    const float4* qv = qs + kh * kDim;
     // Accumulators in pairs for the paired FP32 FMA (__ffma2_rn: two
-    // independent fma.rn, the same roundings as fmaf): the logits a01 = query
-    // heads {0,1}, a23 = {2,3}; the outputs o2[j][0] = heads {0,1}, o2[j][1]
-    // = {2,3} of this lane's channel j of the half.
+    // independent fma.rn, the same roundings as fmaf): the scores a01 = heads
+    // {0,1}, a23 = {2,3}; the outputs o2[j][0] = heads {0,1}, o2[j][1] =
+    // {2,3} of channel slot j.
     float M[kGroup], L[kGroup];
-    float2 o2[2][2];
+    float2 o2[4][2];
 #pragma unroll
     for (int g = 0; g < kGroup; ++g) {
         M[g] = -INFINITY;
         L[g] = 0.0f;
     }
 #pragma unroll
-    for (int j = 0; j < 2; ++j) o2[j][0] = o2[j][1] = make_float2(0.0f, 0.0f);
-    uint32_t n = 0;  // tiles done by this CTA
-    for (unsigned tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++n) {
+    for (int j = 0; j < 4; ++j) o2[j][0] = o2[j][1] = make_float2(0.0f, 0.0f);
+    uint32_t it = 0;
+    for (unsigned tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
         float2 a01 = make_float2(0.0f, 0.0f), a23 = make_float2(0.0f, 0.0f);
-        {
-            const uint32_t it = 4 * n + hf;  // this half's K box
+        for (int half = 0; half < 2; ++half, ++it) {
             const uint32_t s = it % kDTSlots;
             if (!mbar_wait(&full[s], (it / kDTSlots) & 1)) {
                 raise_status(p.status, HSB_E_TIMEOUT, blockIdx.x);
@@ -428,7 +417,7 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&words[e]));
-                    const float4 qa = qv[j * 8 + 2 * e], qb = qv[j * 8 + 2 * e + 1];
+                    const float4 qa = qv[half * 64 + j * 8 + 2 * e], qb = qv[half * 64 + j * 8 + 2 * e + 1];
                     const float2 fx = make_float2(f.x, f.x), fy = make_float2(f.y, f.y);
                     a01 = __ffma2_rn(make_float2(qa.x, qa.y), fx, a01);
                     a23 = __ffma2_rn(make_float2(qa.z, qa.w), fx, a23);
@@ -439,22 +428,9 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
-        // The two halves' logits meet: buffer [tile parity][warp], so a warp
-        // never overwrites a value its partner may still be reading (that
-        // happens only two tiles later, after the partner's next arrival).
-        float4* xb = xs + (n & 1) * kDTConsumers * 32;
-        xb[warp * 32 + lane] = make_float4(a01.x, a01.y, a23.x, a23.y);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&pair[kh]);
-        if (!mbar_wait(&pair[kh], n & 1)) {
-            raise_status(p.status, HSB_E_TIMEOUT, blockIdx.x);
-            return;
-        }
-        const float4 x0 = xb[kh * 32 + lane], x1 = xb[(kKvHeads + kh) * 32 + lane];
-        // online softmax over this tile (tokens past the end weigh 0); both
-        // warps of the head compute it alike
+        // online softmax over this tile (tokens past the end weigh 0)
         const bool valid = tile * 32 + lane < p.tokens;
-        const float a[kGroup] = {x0.x + x1.x, x0.y + x1.y, x0.z + x1.z, x0.w + x1.w};
+        const float a[kGroup] = {a01.x, a01.y, a23.x, a23.y};
         float pr[kGroup], fg[kGroup];
 #pragma unroll
         for (int g = 0; g < kGroup; ++g) {
@@ -466,24 +442,23 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
             M[g] = mn;
         }
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
+        for (int j = 0; j < 4; ++j) {
             o2[j][0].x *= fg[0];
             o2[j][0].y *= fg[1];
             o2[j][1].x *= fg[2];
             o2[j][1].y *= fg[3];
         }
         // The tile's weights, one float4 per token: P.V reads them by broadcast.
-        pw[warp * 32 + lane] = make_float4(pr[0], pr[1], pr[2], pr[3]);
+        pw[kh * 32 + lane] = make_float4(pr[0], pr[1], pr[2], pr[3]);
         __syncwarp();
-        {
-            const uint32_t it = 4 * n + 2 + hf;  // this half's V box
+        for (int half = 0; half < 2; ++half, ++it) {
             const uint32_t s = it % kDTSlots;
             if (!mbar_wait(&full[s], (it / kDTSlots) & 1)) {
                 raise_status(p.status, HSB_E_TIMEOUT, blockIdx.x);
                 return;
             }
             const unsigned char* base = slots + s * kDTBox + kh * 32 * 128 + (lane & 3) * 4;
-            const float4* pt = pw + warp * 32;
+            const float4* pt = pw + kh * 32;
 #pragma unroll 8
             for (int t = 0; t < 32; ++t) {
                 const uint32_t w = *reinterpret_cast<const uint32_t*>(base + t * 128 + (((lane >> 2) ^ (t & 7)) << 4));
@@ -491,10 +466,10 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
                 const float4 p4 = pt[t];
                 const float2 p01 = make_float2(p4.x, p4.y), p23 = make_float2(p4.z, p4.w);
                 const float2 fx = make_float2(f.x, f.x), fy = make_float2(f.y, f.y);
-                o2[0][0] = __ffma2_rn(p01, fx, o2[0][0]);
-                o2[0][1] = __ffma2_rn(p23, fx, o2[0][1]);
-                o2[1][0] = __ffma2_rn(p01, fy, o2[1][0]);
-                o2[1][1] = __ffma2_rn(p23, fy, o2[1][1]);
+                o2[2 * half][0] = __ffma2_rn(p01, fx, o2[2 * half][0]);
+                o2[2 * half][1] = __ffma2_rn(p23, fx, o2[2 * half][1]);
+                o2[2 * half + 1][0] = __ffma2_rn(p01, fy, o2[2 * half + 1][0]);
+                o2[2 * half + 1][1] = __ffma2_rn(p23, fy, o2[2 * half + 1][1]);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
@@ -503,14 +478,16 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
 #pragma unroll
     for (int g = 0; g < kGroup; ++g) {
         float* part = p.part + ((size_t)(kh * kGroup + g) * gridDim.x + blockIdx.x) * kPart;
-        if (lane == 0 && hf == 0) {
+        if (lane == 0) {
             part[0] = M[g];
             part[1] = L[g];
         }
-        const int pr_ = g >> 1;
+        const int pair = g >> 1;
         const bool second = g & 1;
-        part[2 + hf * 64 + 2 * lane] = second ? o2[0][pr_].y : o2[0][pr_].x;
-        part[3 + hf * 64 + 2 * lane] = second ? o2[1][pr_].y : o2[1][pr_].x;
+        part[2 + 2 * lane] = second ? o2[0][pair].y : o2[0][pair].x;
+        part[3 + 2 * lane] = second ? o2[1][pair].y : o2[1][pair].x;
+        part[2 + 64 + 2 * lane] = second ? o2[2][pair].y : o2[2][pair].x;
+        part[3 + 64 + 2 * lane] = second ? o2[3][pair].y : o2[3][pair].x;
     }
 }
 
