@@ -166,6 +166,17 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+// Prefetch of one 3-D box into L2 (no shared memory, no barrier, nothing to
+// wait for).  A hint only: L2 is where every SM's global writes land, so a
+// prefetched line never hides a later write to it, and the box may be read
+// before pdl_wait() while the preceding grid still runs.  Same coordinate
+// rule as tma_load_3d.
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int x, int y, int z) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+
 __device__ __forceinline__ uint32_t lanemask_lt() {
     uint32_t m;
     asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
