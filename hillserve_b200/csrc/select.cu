@@ -55,7 +55,10 @@ struct SelectHeader {
     unsigned int pad[31];
     unsigned int err[128];  // bit0 non-finite score, bit1 rounded count overflow
     float rounded[128];
-    unsigned int cnt[128];  // cluster path: per-head threshold counts, summed over the head's CTAs
+    // Cluster path, one word per head, added to once by each of the head's
+    // CTAs: bits 0-7 CTAs arrived, 8-15 CTAs that saw a non-finite key,
+    // 16-63 the threshold count.  The word is both the data and the barrier.
+    unsigned long long hc[128];
 };
 
 struct SelectParams {
@@ -566,14 +569,15 @@ struct ClusterShared {
     unsigned int c_hi;                  // keys of the whole head in the chosen coarse bin
     unsigned int tie_key0, tie_key1;    // direct path, leader: keys at ranks k - 1 and k
     unsigned int last_id, next_id;      // leader: the need_eq-th and next tie of K*
+    unsigned int sel_ids[32];           // leader: the first 32 ordered ids (the one-tile epilogue)
     unsigned int status, status_index;
     unsigned long long k;
     int timeout;
 };
 
-__device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
-    unsigned int v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 // ---- gather + attention epilogue of the cluster kernel (layer step).
@@ -606,13 +610,15 @@ __device__ __forceinline__ void group_sync(int id) {
 }
 
 // One 32-slot tile of head h into the group's running (M, L, acc).
+template <bool kSharedIds>
 __device__ __forceinline__ void epilogue_tile(const SelectEpilogue& e, const uint32_t* ids, int h, unsigned s0,
                                               int live, const float* qs, EpiGroupSmem& gs, int gtid, int bar,
                                               float& M, float& L, float& acc) {
     const int slot = gtid >> 2, qd = gtid & 3, kh = h >> 2;
     uint4 kr[4], vr[4];
     if (slot < live) {
-        const uint32_t id = __ldcg(ids + s0 + slot);  // written by the leader CTA
+        // written by the leader CTA: its own shared copy, or global memory
+        const uint32_t id = kSharedIds ? ids[s0 + slot] : __ldcg(ids + s0 + slot);
         const uint4* ks = reinterpret_cast<const uint4*>(e.kcache + (size_t)id * e.stride_words + kh * kDim) + qd * 4;
         const uint4* vs = reinterpret_cast<const uint4*>(e.vcache + (size_t)id * e.stride_words + kh * kDim) + qd * 4;
 #pragma unroll
@@ -685,9 +691,6 @@ __device__ __forceinline__ void epilogue_tile(const SelectEpilogue& e, const uin
     group_sync(bar);  // vt / wgt / stat are rewritten by the next tile
 }
 
-__device__ __forceinline__ void red_add_release(unsigned int* p, unsigned int v) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 __device__ __forceinline__ void cluster_arrive_release() {
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
@@ -709,6 +712,9 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     const uint16_t* scores = p.scores + seqb * p.seq_scores;
     hsb_selection* result = p.result + seqb;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // The epilogue's query channel, loaded now: its latency hides behind the
+    // selection instead of following it.
+    const float q_own = (p.ga.out && tid < kDim) ? __ldg(p.ga.q + ((size_t)seqb * p.heads + h) * kDim + tid) : 0.0f;
     const unsigned long long n = p.valid;
     const unsigned long long cs = ((n + kCluster - 1) / kCluster + 7) / 8 * 8;
     const unsigned long long b0 = min(n, (unsigned long long)r * cs), b1 = min(n, b0 + cs);
@@ -817,31 +823,39 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     // acquire after the grid barrier.
     cluster_arrive_release();
     if (warp == 0) {
-        // ---- 2. grid barrier (bounded): lane 0 adds this CTA's count, makes a
-        // release-ordered arrival and polls with acquire loads; the warp then
-        // reads every head's record at once (__syncwarp orders its lanes after
-        // lane 0's acquire).
+        // ---- 2. grid barrier (bounded): lane 0 adds this CTA's record to its
+        // head's word (one atomic: count, non-finite flag, arrival); lane j
+        // polls heads 4j .. 4j + 3 until each has all its CTAs' records, and
+        // the words it read are the counts (no second read, no fence: the
+        // data is the atomic itself).
         int timeout = 0;
-        if (!ext && lane == 0) {
-            if (sh.cnt) atomicAdd(&p.header->cnt[h], sh.cnt);
-            if (!p.cover && sh.bad) atomicOr(&p.header->err[h], 1u);
-            red_add_release(&p.header->arrived, 1u);
+        const uint32_t nh = ext ? p.heads_total : p.heads, own_head = ext ? p.head_base + h : h;
+        unsigned long long word[4] = {0, 0, 0, 0};
+        if (!ext) {
+            if (lane == 0)
+                atomicAdd(&p.header->hc[h], ((unsigned long long)sh.cnt << 16) |
+                                                ((!p.cover && sh.bad) ? 256ull : 0ull) | 1ull);
             const unsigned long long start = global_ns();
-            while (ld_acquire(&p.header->arrived) < gridDim.x) {
-                if (global_ns() - start > kWaitLimitNs) {
-                    timeout = 1;
-                    break;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t hh = lane * 4 + j;
+                if (hh >= nh || timeout) continue;
+                unsigned long long w;
+                while (((w = ld_relaxed_u64(&p.header->hc[hh])) & 255ull) < (unsigned long long)kCluster) {
+                    if (global_ns() - start > kWaitLimitNs) {
+                        timeout = 1;
+                        break;
+                    }
                 }
+                word[j] = w;
             }
         }
-        timeout = __shfl_sync(0xffffffffu, timeout, 0);
-        __syncwarp();
+        timeout = __any_sync(0xffffffffu, timeout);
         if (lane == 0) sh.timeout = timeout;
         // Per-head counts (4 heads per lane), F16 rounding, fold in head order.
         unsigned int e[4] = {0, 0, 0, 0};
         float rr[4] = {0.f, 0.f, 0.f, 0.f};
         unsigned long long own = 0;
-        const uint32_t nh = ext ? p.heads_total : p.heads, own_head = ext ? p.head_base + h : h;
         if (!timeout) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -854,8 +868,8 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
                         c = rec & 0x7fffffffu;
                         nonfinite = rec >> 31;
                     } else {
-                        c = __ldcg(&p.header->cnt[hh]);
-                        nonfinite = __ldcg(&p.header->err[hh]) & 1u;
+                        c = word[j] >> 16;
+                        nonfinite = ((word[j] >> 8) & 255ull) ? 1u : 0u;
                     }
                     if (p.cover) c += 1;  // at most one newly appended current token
                     const float rounded = p.fp32_counts ? (float)c : half_value(half_bits((float)c));
@@ -1029,6 +1043,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
                         rk += (ok > ek) || (ok == ek && j < (unsigned)tid);
                     }
                     if (rk < k) out[rk] = (uint32_t)(e & 0xffffffffu);
+                    if (rk < 32) sh.sel_ids[rk] = (uint32_t)(e & 0xffffffffu);
                     if (rk + 1 == k) {
                         sh.last_id = (uint32_t)(e & 0xffffffffu);
                         sh.tie_key0 = ek;
@@ -1042,6 +1057,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
                 sort_pass<kCThreads>(sh.hist, sh.scan, &sh.total, src, bufB, cand, 0);
                 sort_pass<kCThreads>(sh.hist, sh.scan, &sh.total, bufB, src, cand, 8);
                 for (unsigned int j = tid; j < k; j += kCThreads) out[j] = (uint32_t)(src[j] & 0xffffffffu);
+                if ((unsigned)tid < min(k, 32ull)) sh.sel_ids[tid] = (uint32_t)(src[tid] & 0xffffffffu);
                 if (tid == 0) {
                     sh.last_id = (uint32_t)(src[k - 1] & 0xffffffffu);
                     sh.tie_key0 = (uint32_t)(src[k - 1] >> 32);
@@ -1237,11 +1253,13 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
                     rk += (ok > ek) || (ok == ek && j < (unsigned)tid);
                 }
                 if (rk < k) out[rk] = (uint32_t)(e & 0xffffffffu);
+                if (rk < 32) sh.sel_ids[rk] = (uint32_t)(e & 0xffffffffu);
             }
         } else {
             sort_pass<kCThreads>(sh.hist, sh.scan, &sh.total, src, tmp, (unsigned int)k, 0);
             sort_pass<kCThreads>(sh.hist, sh.scan, &sh.total, tmp, src, (unsigned int)k, 8);
             for (unsigned int j = tid; j < k; j += kCThreads) out[j] = (uint32_t)(src[j] & 0xffffffffu);
+            if ((unsigned)tid < min(k, 32ull)) sh.sel_ids[tid] = (uint32_t)(src[tid] & 0xffffffffu);
         }
     }
     }  // radix path
@@ -1263,25 +1281,25 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
         // gathers and attends alone; its peers are done.
         if (r != 0) return;
         __syncthreads();  // the sort's reads of the candidate buffers are over
-        if (tid < kDim) es.q[tid >> 5][tid & 31] = __ldg(ga.q + h * kDim + tid);
-        __syncthreads();  // the ids (written by this CTA) and q are in place
+        if (tid < kDim) es.q[tid >> 5][tid & 31] = q_own;
+        __syncthreads();  // the ids (sel_ids, written by this CTA) and q are in place
         if (grp == 0) {
             float M = -INFINITY, L = 0.0f, acc = 0.0f;
-            epilogue_tile(ga, out, (int)h, 0u, (int)k, &es.q[0][0], es.g[0], gtid, 1, M, L, acc);
+            epilogue_tile<true>(ga, sh.sel_ids, (int)h, 0u, (int)k, &es.q[0][0], es.g[0], gtid, 1, M, L, acc);
             ga.out[h * kDim + gtid] = L > 0.0f ? acc / L : 0.0f;
         }
         return;
     }
     cl.sync();  // the ordered ids are written (cluster-scope release / acquire)
-    if (tid < kDim) es.q[tid >> 5][tid & 31] = __ldg(ga.q + h * kDim + tid);
+    if (tid < kDim) es.q[tid >> 5][tid & 31] = q_own;
     __syncthreads();
     float M = -INFINITY, L = 0.0f, acc = 0.0f;
     const unsigned ntiles = (unsigned)((k + 31) / 32);
     // Tile t goes to CTA t % 4, group (t / 4) % 4: a few tiles spread over SMs first.
     for (unsigned t = grp * kCluster + r; t < ntiles; t += kCluster * kEpiGroups) {
         const unsigned s0 = t * 32;
-        epilogue_tile(ga, out, (int)h, s0, (int)min(32ull, k - s0), &es.q[0][0], es.g[grp], gtid, 1 + grp, M, L,
-                      acc);
+        epilogue_tile<false>(ga, out, (int)h, s0, (int)min(32ull, k - s0), &es.q[0][0], es.g[grp], gtid, 1 + grp, M,
+                             L, acc);
     }
     EpiSmem* lead_es = cl.map_shared_rank(&es, 0);
     float* part = lead_es->part[r * kEpiGroups + grp];
