@@ -177,6 +177,12 @@ __device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int x, i
                  : "memory");
 }
 
+// Named barrier `id` (1..15; 0 is __syncthreads) over `count` threads, a
+// multiple of 32: whole warps take part.
+__device__ __forceinline__ void named_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ uint32_t lanemask_lt() {
     uint32_t m;
     asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));

@@ -277,8 +277,6 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
             tma_prefetch_3d(&p.maps[v], kTHalf, y0 + t0, 0);
         }
     }
-    pdl_wait();
-    pdl_trigger();
     extern __shared__ unsigned char smem_raw[];
     // The 128-byte swizzle pattern repeats every 1024 bytes of shared address:
     // align by offsetting the shared array itself (keeps the pointers in the
@@ -296,28 +294,25 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
     uint16_t* okeys = p.keys ? p.keys + seq * p.out_seq : nullptr;
     ScoreExtras extras = p.extras;
     if (extras.h0) extras.h0 += (size_t)seq * kH0Partials;
-    clear_extras(extras, blockDim.x);
-    for (int i = threadIdx.x; i < G * kGroup * kDim; i += blockDim.x) {
-        const int h = i >> 7, c = i & 127;
-        reinterpret_cast<uint16_t*>(qs)[((h >> 2) * kDim + c) * kGroup + (h & 3)] = qg[i];
-    }
     __shared__ unsigned int h0_max, h0_bad, h0_done;
     if (threadIdx.x == 0) {
         h0_max = 0;
         h0_bad = 0;
         h0_done = 0;
-    }
-    if (threadIdx.x == 0) {
         for (int s = 0; s < kTStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kTConsumerWarps);
         }
         mbar_fence_init();
     }
-    // Q is staged before any K tile is requested: issued after the stream
-    // starts, its loads queue behind the whole grid's first tiles.
-    __syncthreads();
+    __syncthreads();  // the ring's barriers are initialised (no global access yet)
+    pdl_wait();
+    pdl_trigger();
+    constexpr int kConsumerThreads = kTConsumerWarps * 32;
 
+    // The producer starts the ring at once; the consumers stage Q meanwhile
+    // (in the decode step measured 1-2 % faster per step than staging Q
+    // first: the first tiles are L2 hits from the prefetch above).
     if (warp == kTConsumerWarps) {
         if (lane != 0) return;
         // ---------------- producer: two half-channel TMA loads per tile
@@ -344,7 +339,13 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
         return;
     }
 
-    // ---------------- consumers
+    // ---------------- consumers: clear the extras, stage Q, then consume
+    clear_extras(extras, kConsumerThreads);
+    for (int i = threadIdx.x; i < G * kGroup * kDim; i += kConsumerThreads) {
+        const int h = i >> 7, c = i & 127;
+        reinterpret_cast<uint16_t*>(qs)[((h >> 2) * kDim + c) * kGroup + (h & 3)] = qg[i];
+    }
+    named_sync(1, kConsumerThreads);
     const int kh = warp % G, tl = (warp / G) * 32 + lane;  // KV head, token in tile
     const uint4* qv = qs + kh * (kDim / 2);
     uint32_t it = 0, h0max = 0, h0bad = 0;
