@@ -569,6 +569,7 @@ struct ClusterShared {
     unsigned int c_hi;                  // keys of the whole head in the chosen coarse bin
     unsigned int tie_key0, tie_key1;    // direct path, leader: keys at ranks k - 1 and k
     unsigned int last_id, next_id;      // leader: the need_eq-th and next tie of K*
+    unsigned int cand_slots;            // leader: direct-path candidates placed so far
     unsigned int sel_ids[32];           // leader: the first 32 ordered ids (the one-tile epilogue)
     unsigned int status, status_index;
     unsigned long long k;
@@ -736,6 +737,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
         sh.bad = 0;
         sh.last_id = 0xffffffffu;
         sh.next_id = 0xffffffffu;
+        sh.cand_slots = 0;
     }
     for (int i = tid; i < 1024; i += kCThreads) sh.coarse[i] = 0;
     if (tid < 64) sh.fine[tid] = 0;
@@ -993,38 +995,57 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
         if (lane == 0) sh.red[warp][q] = v;
     }
     if (direct) {
-        // ---- 3'. the candidates: every key of bins >= hi, in ID order
-        __syncthreads();
-        unsigned int before = 0;
-        for (unsigned int q = 0; q < r; ++q)
-            for (int w = 0; w < kCWarps; ++w) before += sh.red[w][q];
+        // ---- 3'. the candidates: every key of bins >= hi
         unsigned long long* dst = cl.map_shared_rank(bufA, 0);
-        const unsigned int per = ((m + kCThreads - 1) / kCThreads + 7) / 8 * 8;
-        const unsigned int j0 = min(m, tid * per), j1 = min(m, j0 + per);
-        unsigned int mine = 0;
-        for (unsigned int j = j0; j < j1; j += 8) {  // 16-byte loads: no bank conflicts
-            uint32_t w[4];
-            if (j + 8 <= j1) {
+        if (above_hi + sh.c_hi <= kRankSortMax) {  // the same in every CTA of the cluster
+            // Few candidates: each takes a slot from the leader's counter, in any
+            // order (the leader's rank sort orders by key, then ID).
+            unsigned int* slot = cl.map_shared_rank(&sh.cand_slots, 0);
+            for (unsigned int j = tid * 8; j < m; j += kCThreads * 8) {
+                // keys[] holds a multiple of 8 entries: the 16-byte load stays inside
                 const uint4 v = *reinterpret_cast<const uint4*>(keys + j);
-                w[0] = v.x;
-                w[1] = v.y;
-                w[2] = v.z;
-                w[3] = v.w;
-            } else {
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    w[e] = (j + 2 * e < j1 ? keys[j + 2 * e] : 0u) | ((j + 2 * e + 1 < j1 ? keys[j + 2 * e + 1] : 0u) << 16);
+                for (int e = 0; e < 8; ++e) {
+                    const uint32_t key = (w[e >> 1] >> (16 * (e & 1))) & 0xffffu;
+                    if (j + e < m && (key >> 6) >= hi)
+                        dst[atomicAdd(slot, 1u)] = ((unsigned long long)key << 32) | (unsigned int)(b0 + j + e);
+                }
             }
+        } else {
+            // In ID order: a block scan places each thread's candidates after
+            // those of the cluster's earlier chunks.
+            __syncthreads();
+            unsigned int before = 0;
+            for (unsigned int q = 0; q < r; ++q)
+                for (int w = 0; w < kCWarps; ++w) before += sh.red[w][q];
+            const unsigned int per = ((m + kCThreads - 1) / kCThreads + 7) / 8 * 8;
+            const unsigned int j0 = min(m, tid * per), j1 = min(m, j0 + per);
+            unsigned int mine = 0;
+            for (unsigned int j = j0; j < j1; j += 8) {  // 16-byte loads: no bank conflicts
+                uint32_t w[4];
+                if (j + 8 <= j1) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(keys + j);
+                    w[0] = v.x;
+                    w[1] = v.y;
+                    w[2] = v.z;
+                    w[3] = v.w;
+                } else {
 #pragma unroll
-            for (int e = 0; e < 8; ++e)
-                mine += (j + e < j1 && ((w[e >> 1] >> (16 * (e & 1))) & 0xffffu) >> 6 >= hi) ? 1u : 0u;
-        }
-        unsigned int pos = before + block_exclusive_scan<kCThreads>(mine, sh.scan, &sh.total);
-        if (mine) {
-            for (unsigned int j = j0; j < j1; ++j) {
-                const unsigned int key = keys[j];
-                if ((key >> 6) >= hi && pos < kSmemSortMax)
-                    dst[pos++] = ((unsigned long long)key << 32) | (unsigned int)(b0 + j);
+                    for (int e = 0; e < 4; ++e)
+                        w[e] = (j + 2 * e < j1 ? keys[j + 2 * e] : 0u) | ((j + 2 * e + 1 < j1 ? keys[j + 2 * e + 1] : 0u) << 16);
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    mine += (j + e < j1 && ((w[e >> 1] >> (16 * (e & 1))) & 0xffffu) >> 6 >= hi) ? 1u : 0u;
+            }
+            unsigned int pos = before + block_exclusive_scan<kCThreads>(mine, sh.scan, &sh.total);
+            if (mine) {
+                for (unsigned int j = j0; j < j1; ++j) {
+                    const unsigned int key = keys[j];
+                    if ((key >> 6) >= hi && pos < kSmemSortMax)
+                        dst[pos++] = ((unsigned long long)key << 32) | (unsigned int)(b0 + j);
+                }
             }
         }
         cl.sync();  // every chunk's candidates are in the leader
@@ -1035,12 +1056,14 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
             unsigned long long* src = bufA;
             if (cand <= kRankSortMax) {
                 if ((unsigned)tid < cand) {
+                    // rank by key descending, ID ascending (unique IDs)
                     const unsigned long long e = src[tid];
-                    const unsigned int ek = (unsigned int)(e >> 32);
+                    const unsigned int ek = (unsigned int)(e >> 32), eid = (unsigned int)e;
                     unsigned int rk = 0;
                     for (unsigned int j = 0; j < cand; ++j) {
-                        const unsigned int ok = (unsigned int)(src[j] >> 32);
-                        rk += (ok > ek) || (ok == ek && j < (unsigned)tid);
+                        const unsigned long long o = src[j];
+                        const unsigned int ok = (unsigned int)(o >> 32);
+                        rk += (ok > ek) || (ok == ek && (unsigned int)o < eid);
                     }
                     if (rk < k) out[rk] = (uint32_t)(e & 0xffffffffu);
                     if (rk < 32) sh.sel_ids[rk] = (uint32_t)(e & 0xffffffffu);
