@@ -215,10 +215,10 @@ constexpr int kTThreads = (kTConsumerWarps + 1) * 32;
 constexpr int kTQBytes = kDim * kKvHeads * kGroup * 2;   // 8192
 constexpr int kTSmemBytes = 1024 + kTStages * kTStageBytes + kTQBytes + 64;
 // Key tiles per CTA prefetched into L2 before the grid dependency wait.  In
-// the 32-layer decode step at N 32K: none 0.922 ms, two 0.893 ms, three
-// 0.909 ms, four 0.913 ms per step (deeper prefetches compete with the
-// running selector's gathers).
-constexpr int kTPrefetchTiles = 2;
+// the 32-layer decode step at N 32K (three alternating runs each, one box):
+// none 0.965 ms, one 0.954 ms, two 0.968 ms per step.  A deeper prefetch
+// floods DRAM while the previous selector's epilogue gathers its rows.
+constexpr int kTPrefetchTiles = 1;
 
 struct TmaParams {
     CUtensorMap maps[HSB_MAX_VIEWS];
