@@ -139,6 +139,25 @@ def test_coarse_values_many_ties(cuda, ob):
             same_as_oracle(cuda, ob, sc, H, n, n, alpha, ratio)
 
 
+@pytest.mark.parametrize("n,seed", [(32768, 1), (32768, 2), (20000, 3), (4100, 4)])
+def test_few_candidates_with_equal_top_keys(cuda, ob, n, seed):
+    """Equal top keys spread over the four chunks of a head, few enough that
+    the selector's direct path places them in arrival order (at most 256
+    candidates): the selection must still list equal keys by ascending ID,
+    and heads holding more equal keys than k count as boundary ties."""
+    rng = np.random.default_rng(seed)
+    sc = rng.standard_normal((H, n)).astype(np.float16)
+    for h in range(H):
+        planted = rng.choice(n, size=8 + h % 5, replace=False)  # 8..12 copies of the maximum
+        sc[h, planted] = np.float16(6.0)
+        second = rng.choice(np.setdiff1d(np.arange(n), planted), size=3, replace=False)
+        sc[h, second] = np.float16(5.75)  # a second tier just below
+    bits = sc.view(np.uint16).reshape(-1).copy()
+    for alpha in (0.2, 0.3, 1.0):
+        g = same_as_oracle(cuda, ob, bits, H, n, n, alpha, 0.2)
+        assert g[2] > 0
+
+
 def test_errors_in_reference_order(cuda, ob):
     hb = ob.half_bits
     n = 64
