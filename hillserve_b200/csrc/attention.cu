@@ -494,10 +494,13 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
 // out[h][d] = sum_c exp(M_c - M) o_c[d] / sum_c exp(M_c - M) L_c over the
 // dense kernel's per-CTA partials.  One CTA per query head: the partials'
 // weights go to shared memory once, then 8 groups of 128 threads (thread =
-// channel) each sum every 8th partial with independent loads.
+// channel) each sum every 8th partial.  All loads are issued before any
+// arithmetic (a loop of dependent loads cost ~4 us per dense layer).
 constexpr int kCombineGroups = 8;
 __global__ void __launch_bounds__(kDim * kCombineGroups) dense_combine_kernel(const float* __restrict__ part,
                                                                              int nparts, float* __restrict__ out) {
+    constexpr int kPer = kDenseMaxCtas / kCombineGroups;  // partials per thread
+    constexpr int kPerLane = kDenseMaxCtas / 32;          // partials per lane of warp 0
     pdl_wait();
     pdl_trigger();
     __shared__ float w[kDenseMaxCtas];
@@ -505,23 +508,47 @@ __global__ void __launch_bounds__(kDim * kCombineGroups) dense_combine_kernel(co
     __shared__ float red[2];
     const int h = blockIdx.x, tid = threadIdx.x, d = tid & (kDim - 1), grp = tid / kDim;
     const float* base = part + (size_t)h * nparts * kPart;
+    // Every load is issued up front (one round trip, not one per partial):
+    // this thread's output channel of partials grp, grp + 8, ..., and for
+    // warp 0 the maxima and sums.  The arithmetic keeps its order.
+    float ov[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int c = grp + i * kCombineGroups;
+        ov[i] = c < nparts ? __ldg(base + (size_t)c * kPart + 2 + d) : 0.0f;
+    }
     if (tid < 32) {
+        float mv[kPerLane], lv[kPerLane];
+#pragma unroll
+        for (int i = 0; i < kPerLane; ++i) {
+            const int c = tid + 32 * i;
+            mv[i] = c < nparts ? __ldg(base + (size_t)c * kPart) : -INFINITY;
+            lv[i] = c < nparts ? __ldg(base + (size_t)c * kPart + 1) : 0.0f;
+        }
         float m = -INFINITY;
-        for (int c = tid; c < nparts; c += 32) m = fmaxf(m, __ldg(base + (size_t)c * kPart));
+#pragma unroll
+        for (int i = 0; i < kPerLane; ++i) m = fmaxf(m, mv[i]);
         m = warp_max(m);
         float l = 0.0f;
-        for (int c = tid; c < nparts; c += 32) {
-            const float wc = expf(__ldg(base + (size_t)c * kPart) - m);
-            w[c] = wc;
-            l = fmaf(__ldg(base + (size_t)c * kPart + 1), wc, l);
+#pragma unroll
+        for (int i = 0; i < kPerLane; ++i) {
+            const int c = tid + 32 * i;
+            if (c < nparts) {
+                const float wc = expf(mv[i] - m);
+                w[c] = wc;
+                l = fmaf(lv[i], wc, l);
+            }
         }
         l = warp_sum(l);
         if (tid == 0) red[0] = l;
     }
     __syncthreads();
     float acc = 0.0f;
-#pragma unroll 4
-    for (int c = grp; c < nparts; c += kCombineGroups) acc = fmaf(__ldg(base + (size_t)c * kPart + 2 + d), w[c], acc);
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int c = grp + i * kCombineGroups;
+        if (c < nparts) acc = fmaf(ov[i], w[c], acc);
+    }
     acc_s[grp][d] = acc;
     __syncthreads();
     if (tid < kDim) {
