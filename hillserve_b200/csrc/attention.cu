@@ -346,9 +346,20 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDTSlots * kDTBox + kDTQBytes + kDTPBytes);
     uint64_t* empty = full + kDTSlots;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int i = threadIdx.x; i < kHeads * kDim; i += blockDim.x) {
-        const int h = i >> 7, c = i & 127;
-        reinterpret_cast<float*>(qs)[((h >> 2) * kDim + c) * kGroup + (h & 3)] = p.q[i];
+    {  // Q to shared memory: every load issued before any store (one round trip)
+        constexpr int kPer = (kHeads * kDim + kDTThreads - 1) / kDTThreads;
+        float qv[kPer];
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int i = threadIdx.x + u * kDTThreads;
+            qv[u] = i < kHeads * kDim ? p.q[i] : 0.0f;  // written by the preceding grid: a coherent load
+        }
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int i = threadIdx.x + u * kDTThreads;
+            if (i < kHeads * kDim)
+                reinterpret_cast<float*>(qs)[((i >> 9) * kDim + (i & 127)) * kGroup + ((i >> 7) & 3)] = qv[u];
+        }
     }
     if (threadIdx.x == 0) {
         for (int s = 0; s < kDTSlots; ++s) {

@@ -341,9 +341,16 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
 
     // ---------------- consumers: clear the extras, stage Q, then consume
     clear_extras(extras, kConsumerThreads);
-    for (int i = threadIdx.x; i < G * kGroup * kDim; i += kConsumerThreads) {
-        const int h = i >> 7, c = i & 127;
-        reinterpret_cast<uint16_t*>(qs)[((h >> 2) * kDim + c) * kGroup + (h & 3)] = qg[i];
+    {  // every load issued before any store (one round trip)
+        constexpr int kPer = G * kGroup * kDim / kConsumerThreads;
+        uint16_t qv[kPer];
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) qv[u] = qg[threadIdx.x + u * kConsumerThreads];  // coherent: the preceding grid may write Q
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int i = threadIdx.x + u * kConsumerThreads, h = i >> 7, c = i & 127;
+            reinterpret_cast<uint16_t*>(qs)[((h >> 2) * kDim + c) * kGroup + (h & 3)] = qv[u];
+        }
     }
     named_sync(1, kConsumerThreads);
     const int kh = warp % G, tl = (warp / G) * 32 + lane;  // KV head, token in tile

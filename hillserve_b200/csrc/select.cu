@@ -715,7 +715,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     // The epilogue's query channel, loaded now: its latency hides behind the
     // selection instead of following it.
-    const float q_own = (p.ga.out && tid < kDim) ? __ldg(p.ga.q + ((size_t)seqb * p.heads + h) * kDim + tid) : 0.0f;
+    const float q_own = (p.ga.out && tid < kDim) ? p.ga.q[((size_t)seqb * p.heads + h) * kDim + tid] : 0.0f;
     const unsigned long long n = p.valid;
     const unsigned long long cs = ((n + kCluster - 1) / kCluster + 7) / 8 * 8;
     const unsigned long long b0 = min(n, (unsigned long long)r * cs), b1 = min(n, b0 + cs);
