@@ -39,12 +39,17 @@ __global__ void __launch_bounds__(256) executor_prepare_kernel(const uint16_t* _
     const unsigned long long t = blockIdx.x;
     const int i = threadIdx.x;
     if (t >= n) {  // blocks n .. n+3: a quarter of the query each
+        constexpr int kPer = kHeads * kDim / kQueryBlocks / 256;  // elements per thread
         const int q0 = (int)(t - n) * (kHeads * kDim / kQueryBlocks);
-        for (int j = q0 + i; j < q0 + kHeads * kDim / kQueryBlocks; j += blockDim.x) {
-            const float x = rehearsal[j];
-            const uint16_t h = half_bits(x);
+        float x[kPer];
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) x[u] = rehearsal[q0 + i + u * 256];  // loads first: one round trip
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int j = q0 + i + u * 256;
+            const uint16_t h = half_bits(x[u]);
             q16[j] = h;
-            if (!isfinite(x)) raise_status(status, HSB_E_EXECUTOR_REHEARSAL, j);
+            if (!isfinite(x[u])) raise_status(status, HSB_E_EXECUTOR_REHEARSAL, j);
             else if (!is_finite_half(h)) raise_status(status, HSB_E_EXECUTOR_REHEARSAL_F16, j);
         }
         return;

@@ -111,9 +111,15 @@ __global__ void history_append_kernel(const uint16_t* __restrict__ rows, unsigne
     const unsigned long long pos = first + t;
     const uint4* src = reinterpret_cast<const uint4*>(rows + t * kRowWords);
     const int32_t s = slot[pos];
+    // 128 threads; each thread's loads are issued before its stores.
     if (s >= 0) {
         uint4* dst = reinterpret_cast<uint4*>(pool + (size_t)s * kRowWords);
-        for (int i = threadIdx.x; i < (int)(kRowWords / 8); i += blockDim.x) dst[i] = src[i];
+        constexpr int kPer = (int)(kRowWords / 8) / 128;
+        uint4 w[kPer];
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) w[u] = src[threadIdx.x + u * 128];
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) dst[threadIdx.x + u * 128] = w[u];
     } else if (cold_row[pos] >= 0) {
         uint4* dst = reinterpret_cast<uint4*>(cold + (size_t)cold_row[pos] * kKeyWords);
         for (int i = threadIdx.x; i < (int)(kKeyWords / 8); i += blockDim.x) dst[i] = src[i];
@@ -223,8 +229,17 @@ __global__ void history_query_check_kernel(const uint16_t* __restrict__ a, const
                                            hsb_selection* result) {
     pdl_wait();
     pdl_trigger();
+    // 256 threads: every load issued before any compare (one round trip).
+    constexpr int kPer = kHeads * kDim / 256;
+    uint16_t x[kPer], y[kPer];
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+        x[u] = a[threadIdx.x + u * 256];
+        y[u] = b[threadIdx.x + u * 256];
+    }
     bool same = true;
-    for (int i = threadIdx.x; i < kHeads * kDim; i += blockDim.x) same &= a[i] == b[i];
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) same &= x[u] == y[u];
     if (!__syncthreads_and(same) && threadIdx.x == 0) {
         result->k = 0;
         result->boundary_tied_heads = 0;

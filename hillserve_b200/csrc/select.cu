@@ -747,7 +747,21 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     // chunk's keys to shared memory with the coarse histogram.
     unsigned int mx = 0, bad0 = 0, bad = 0;
     const bool ext = p.ext != nullptr;
-    if (p.h0 && !ext) head0_from_partials<kCThreads>(p.h0, mx, bad0);
+    // Phase 1's global loads go out together, one round trip rather than a
+    // chain: the chunk's first two 16-byte words of keys per thread and, in
+    // the layer step, the two head-0 partials per thread.
+    static_assert(kH0Partials == 2 * kCThreads, "two head-0 partials per thread");
+    uint4 kw[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+        if (tid + u * kCThreads < m8) kw[u] = reinterpret_cast<const uint4*>(row + b0)[tid + u * kCThreads];
+    // Shard steps: the threshold record's status (written by the preceding grid).
+    const int ext_status = ext ? (int)p.ext_thr[2 * seqb + 1] : 0;
+    if (p.h0 && !ext) {
+        const uint32_t v0 = __ldcg(p.h0 + tid), v1 = __ldcg(p.h0 + tid + kCThreads);
+        mx = max(v0 & 0xffffu, v1 & 0xffffu);
+        bad0 = (v0 | v1) >> 16;
+    }
 #pragma unroll 4
     for (unsigned long long g = tid; g < ((p.h0 || ext) ? 0 : n8); g += kCThreads) {
         const uint4 w = reinterpret_cast<const uint4*>(row0)[g];
@@ -764,8 +778,8 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
         bad0 |= key_nonfinite(key);
         mx = key_nan(key) ? mx : max(mx, key);
     }
-    for (unsigned int g = tid; g < m8; g += kCThreads) {
-        const uint4 w = reinterpret_cast<const uint4*>(row + b0)[g];
+    // One 16-byte word of keys: coarse histogram, order keys to shared memory.
+    auto take = [&](const uint4 w, unsigned int g) {
         const uint32_t v[4] = {w.x, w.y, w.z, w.w};
         uint32_t k2[4];
 #pragma unroll
@@ -777,7 +791,12 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
             k2[j >> 1] = a | (b << 16);
         }
         reinterpret_cast<uint4*>(keys)[g] = make_uint4(k2[0], k2[1], k2[2], k2[3]);
-    }
+    };
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+        if (tid + u * kCThreads < m8) take(kw[u], tid + u * kCThreads);
+    for (unsigned int g = tid + 2 * kCThreads; g < m8; g += kCThreads)
+        take(reinterpret_cast<const uint4*>(row + b0)[g], g);
     for (unsigned int i = m8 * 8 + tid; i < m; i += kCThreads) {
         const uint32_t key = to_key(row[b0 + i], p.mode);
         bad |= key_nonfinite(key);
@@ -793,7 +812,6 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     __syncthreads();
     const float maximum = half_value((uint16_t)key_bits(sh.maxkey));
     const float threshold = half_value(half_bits(sh.maxkey ? maximum - p.alpha : -INFINITY));
-    const int ext_status = ext ? (int)__ldg(p.ext_thr + 2 * seqb + 1) : 0;
     const bool head0_bad = !ext && !p.cover && sh.bad0;
     const bool thr_bad = !ext && !isfinite(threshold);
     if (head0_bad || thr_bad || ext_status) {
