@@ -526,15 +526,15 @@ __global__ void __launch_bounds__(kDim * kCombineGroups) dense_combine_kernel(co
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
         const int c = grp + i * kCombineGroups;
-        ov[i] = c < nparts ? __ldg(base + (size_t)c * kPart + 2 + d) : 0.0f;
+        ov[i] = c < nparts ? __ldcg(base + (size_t)c * kPart + 2 + d) : 0.0f;
     }
     if (tid < 32) {
         float mv[kPerLane], lv[kPerLane];
 #pragma unroll
         for (int i = 0; i < kPerLane; ++i) {
             const int c = tid + 32 * i;
-            mv[i] = c < nparts ? __ldg(base + (size_t)c * kPart) : -INFINITY;
-            lv[i] = c < nparts ? __ldg(base + (size_t)c * kPart + 1) : 0.0f;
+            mv[i] = c < nparts ? __ldcg(base + (size_t)c * kPart) : -INFINITY;
+            lv[i] = c < nparts ? __ldcg(base + (size_t)c * kPart + 1) : 0.0f;
         }
         float m = -INFINITY;
 #pragma unroll
@@ -724,8 +724,8 @@ __global__ void __launch_bounds__(kGAThreads) gather_attention_kernel(const __gr
                 const uint4* vs = reinterpret_cast<const uint4*>(p.vcache + (size_t)id * p.stride_words + kh * kDim) + qd * 4;
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
-                    kr[u] = __ldg(ks + u);
-                    vr[u] = __ldg(vs + u);
+                    kr[u] = __ldcg(ks + u);
+                    vr[u] = __ldcg(vs + u);
                 }
             }
         }
@@ -745,7 +745,7 @@ __global__ void __launch_bounds__(kGAThreads) gather_attention_kernel(const __gr
         float dot = 0.0f;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            const float4 qa = __ldg(qv + 2 * u), qb = __ldg(qv + 2 * u + 1);
+            const float4 qa = __ldcg(qv + 2 * u), qb = __ldcg(qv + 2 * u + 1);
             const uint32_t w[4] = {kr[u].x, kr[u].y, kr[u].z, kr[u].w};
             const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&w[0]));
             const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&w[1]));

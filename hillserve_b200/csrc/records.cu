@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(kWarpsMax * 32) records_kernel(const __grid_co
         const unsigned long long c = j * 8 + (lane & 7);
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-            reg[k] = lsrc[k] && c < chunks ? __ldg(reinterpret_cast<const uint4*>(lsrc[k] + j * 128))
+            reg[k] = lsrc[k] && c < chunks ? __ldcg(reinterpret_cast<const uint4*>(lsrc[k] + j * 128))
                                            : make_uint4(0, 0, 0, 0);
     };
     if (vec_mask) {

@@ -1416,7 +1416,7 @@ __global__ void __launch_bounds__(kCountThreads) shard_count_kernel(const uint16
         sbad = 0;
     }
     __syncthreads();
-    const unsigned int thr_key = __ldg(thr);
+    const unsigned int thr_key = __ldcg(thr);
     const uint16_t* row = keys + (unsigned long long)blockIdx.x * tokens;
     const bool vec = tokens % 8 == 0 && (reinterpret_cast<uintptr_t>(keys) & 15) == 0;
     const unsigned long long n8 = vec ? tokens / 8 : 0;
