@@ -39,6 +39,14 @@ LAYERS, DENSE, N, HEADS = 32, 2, 32768, 32
 THETA = 500000.0
 
 
+def layer_seeds(seed: int, layer: int) -> tuple:
+    """Generator streams of one layer's inputs (Q, K, V) for sequence `seed`:
+    the same numbers on the GPU (hsb_synth_*) and on the CPU (the oracle's
+    restatement), so either side can rebuild the other's data."""
+    ls = seed * 1000 + layer
+    return ls * 7 + 1, ls * 7 + 2, ls * 7 + 3
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -60,10 +68,15 @@ def parse():
                          "the model-facing decode step (current-KV append + selection + attention over live slots) "
                          "beside the reference executor's padded upload")
     ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--prefetch-mib", type=float, default=64.0,
+                    help="MiB of the next layer's keys each selected-KV layer pulls into L2 while it selects")
     ap.add_argument("--h2o-keys", type=int, default=32768, help="h2o workload: keys N")
     ap.add_argument("--h2o-queries", default="1,16,512", help="h2o workload: comma-separated query counts")
     ap.add_argument("--records-layers", type=int, default=32, help="records workload: layers of the sequence")
     return ap.parse_args()
+
+
+METRIC = "selected-KV decode layer-steps/s at N=32K (score+select+gather HBM GB/s vs peak)"
 
 
 def peaks():
@@ -145,10 +158,10 @@ class Model:
         self.kc = torch.empty((layers, tokens * 1024), dtype=torch.int16, device=dev)
         self.vc = torch.empty((layers, tokens * 1024), dtype=torch.int16, device=dev)
         for l in range(layers):
-            ls = seed * 1000 + l
-            lib.hsb_synth_normal_f16(self.q16[l].data_ptr(), 4096, ls * 7 + 1, 1.0, s)
-            lib.hsb_synth_keys(self.kc[l].data_ptr(), tokens, 1024, ls * 7 + 2, 0.02, 4.0, 1, THETA, s)
-            lib.hsb_synth_keys(self.vc[l].data_ptr(), tokens, 1024, ls * 7 + 3, 0.0, 1.0, 0, THETA, s)
+            sq, sk, sv = layer_seeds(seed, l)
+            lib.hsb_synth_normal_f16(self.q16[l].data_ptr(), 4096, sq, 1.0, s)
+            lib.hsb_synth_keys(self.kc[l].data_ptr(), tokens, 1024, sk, 0.02, 4.0, 1, THETA, s)
+            lib.hsb_synth_keys(self.vc[l].data_ptr(), tokens, 1024, sv, 0.0, 1.0, 0, THETA, s)
         self.q32.copy_(self.q16.view(torch.float16).float())
         self.k_in.copy_(self.kc[:, -1024:])
         self.v_in.copy_(self.vc[:, -1024:])
@@ -178,6 +191,7 @@ class Model:
         self.ev_layer = [[mk() for _ in range(2)] for _ in range(nsparse)]
         self.ev_dense = [[mk() for _ in range(2)] for _ in range(DENSE)]
         self.lib = lib
+        self.prefetch_bytes = 0  # bytes of the next layer's keys pulled into L2 during a selection
 
     def step(self, stream, mode: str = "timed"):
         """Launches one 32-layer decode step on `stream`.
@@ -208,9 +222,11 @@ class Model:
             if mode in ("timed", "layers"):
                 e = self.ev_layer[l - DENSE]
                 mark(e[0])
-                rc = lib.hsb_layer_step(P(self.q16[l]), P(self.q32[l]), P(self.kc[l]), P(self.vc[l]), 1024, n,
-                                        self.alpha, 0.2, self.count, ctypes.byref(self.buffers[l]),
-                                        P(self.out[l]), s)
+                # While layer l selects, layer l + 1's keys stream into L2.
+                nxt = self.prefetch_bytes if l + 1 < self.layers else 0
+                rc = lib.hsb_layer_step_prefetch(P(self.q16[l]), P(self.q32[l]), P(self.kc[l]), P(self.vc[l]), 1024,
+                                                 n, self.alpha, 0.2, self.count, ctypes.byref(self.buffers[l]),
+                                                 P(self.out[l]), P(self.kc[l + 1]) if nxt else None, nxt, s)
                 mark(e[1])
                 assert rc == 0, lib.hsb_last_error()
                 continue
@@ -244,6 +260,10 @@ class Model:
                 "attention": float(np.mean(at)), "dense_attention": float(np.mean(dn)) if dn else 0.0,
                 "score_select_gather": float(np.mean(np.array(sc) + np.array(se) + np.array(ga)))}
 
+    def dense_ms(self):
+        """Mean duration (ms) of one dense layer in the last 'layers' replay."""
+        return float(np.mean([e[0].elapsed_time(e[1]) for e in self.ev_dense])) if self.ev_dense else 0.0
+
     def layer_ms(self):
         """Mean duration (ms) of one hsb_layer_step in the last 'layers' replay."""
         return float(np.mean([e[0].elapsed_time(e[1]) for e in self.ev_layer])) if self.ev_layer else 0.0
@@ -274,6 +294,7 @@ def run_ours(args, rank, world, torch, dist):
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
     dev_index = torch.cuda.current_device()
     m = Model(hsb, torch, args.tokens, args.layers, args.alpha, seed=rank)
+    m.prefetch_bytes = min(int(args.prefetch_mib * (1 << 20)), 2048 * args.tokens) // 16 * 16
     stream = torch.cuda.Stream()
     torch.cuda.synchronize()
     with torch.cuda.stream(stream):
@@ -320,6 +341,7 @@ def run_ours(args, rank, world, torch, dist):
         layer_graph.replay()
     stream.synchronize()
     stages["layer_step"] = m.layer_ms()
+    dense_in_graph = m.dense_ms()  # the same replay: each dense layer between events
     t = torch.tensor([ms], dtype=torch.float64, device="cuda")
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -338,15 +360,22 @@ def run_ours(args, rank, world, torch, dist):
     b_score = 2048 * n + 8192 + 64 * n
     b_select = 64 * n + 4 * 32 * mean_k
     b_gather = 4096 * mean_u + 16384 * mean_k
+    b_ssg = b_score + b_select + b_gather
     peak, peak_kind = peaks()
     score_gbs = b_score / (stages["score"] / 1e3) / 1e9
-    ssg_gbs = (b_score + b_select + b_gather) / (stages["score_select_gather"] / 1e3) / 1e9
+    ssg_gbs = b_ssg / (stages["score_select_gather"] / 1e3) / 1e9
     b_attn = 16384 * mean_k + 16384
-    layer_gbs = (b_score + b_select + b_gather + b_attn) / (stages["layer_step"] / 1e3) / 1e9
+    layer_gbs = (b_ssg + b_attn) / (stages["layer_step"] / 1e3) / 1e9
+    # The main figure, from the timed graph itself: the step's time less
+    # its dense layers, per selected-KV layer (score + select + gather, with
+    # the fused attention epilogue inside it).
+    sparse_layers = args.layers - DENSE
+    per_layer_ms = (ms_per_step - DENSE * dense_in_graph) / sparse_layers
+    graded_gbs = b_ssg / (per_layer_ms / 1e3) / 1e9
     traffic = ncu_traffic() if n == N else None  # the capture is of the N=32768 launch
 
     line = {
-        "metric": "selected-KV decode layer-steps/s at N=32K (score+select+gather HBM GB/s vs peak)",
+        "metric": METRIC,
         "value": round(value, 1),
         "unit": "layer-steps/s",
         "n_gpus": world,
@@ -358,31 +387,40 @@ def run_ours(args, rank, world, torch, dist):
         "vs_baseline": None,
         "dtype": "f16 in, f32 accumulate (ordered)",
         "data": "synthetic",
-        "config": {"workload": "configs[1]: 32-layer decode step, N=32768, layers 0-1 dense, 2-31 selected-KV",
-                   "tokens": n, "layers": args.layers, "alpha": args.alpha, "cap_ratio": 0.2,
-                   "kv_bytes_per_step": 2 * 2048 * n * args.layers, "l2": "inputs 4.3 GB >> 126 MB L2, no flush",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "launch": "one CUDA graph per 32-layer step"},
+        "config": workload_config(args),
+        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+        "launch": "one CUDA graph per 32-layer step",
+        "l2_prefetch_next_layer_bytes": m.prefetch_bytes,
+        "score_select_gather": {"bytes_per_layer": round(b_ssg), "us_per_layer": round(per_layer_ms * 1e3, 2),
+                                "GB_s": round(graded_gbs, 1), "frac_of_peak": round(graded_gbs / peak, 4),
+                                "peak_GB_s": peak, "peak_kind": peak_kind,
+                                "path": "the timed graph: (ms_per_step - dense layers) / selected-KV layers; "
+                                        "score -> select -> fused gather + attention"},
         "stages_ms": {k: round(v, 5) for k, v in stages.items()},
+        "stages_ms_dense_in_graph": round(dense_in_graph, 5),
         "selection": {"k_mean": mean_k, "k_min": int(min(ks)) if ks else 0, "k_max": int(max(ks)) if ks else 0,
                       "union_mean": mean_u, "zero_selection_layers": zero,
                       "note": "k==0 is the reference's own outcome at this alpha (it throws there); "
                               "attention over an empty selection returns zeros"},
-        "score_select_gather": {"bytes": b_score + b_select + b_gather, "GB_s": round(ssg_gbs, 1),
-                                "frac_of_peak": round(ssg_gbs / peak, 4), "peak_GB_s": peak, "peak_kind": peak_kind,
-                                "path": "separate C-ABI calls (score_with_keys, select_keys, gather_cache)"},
-        "layer_step": {"bytes": b_score + b_select + b_gather + b_attn, "us": round(stages["layer_step"] * 1e3, 2),
+        "separate_calls": {"bytes": round(b_ssg), "GB_s": round(ssg_gbs, 1), "frac_of_peak": round(ssg_gbs / peak, 4),
+                           "path": "separate C-ABI calls (score_with_keys, select_keys, gather_cache), each "
+                                   "between events: not the timed path"},
+        "layer_step": {"bytes": round(b_ssg + b_attn), "us": round(stages["layer_step"] * 1e3, 2),
                        "GB_s": round(layer_gbs, 1), "frac_of_peak": round(layer_gbs / peak, 4),
-                       "path": "hsb_layer_step (score -> select -> fused gather + attention), the timed path"},
+                       "path": "hsb_layer_step alone between two event nodes (carries the launch ramp the timed "
+                               "graph hides)"},
         "roofline": {"kernel": "score_tma_kernel", "bound": "hbm", "achieved": round(score_gbs, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(score_gbs / peak, 4), "traffic": traffic,
+                     "traffic_source": "profiles/score_tma_kernel_n32768_traffic.json (one ncu capture)",
                      "algorithmic_bytes_per_launch": b_score, "peak_kind": peak_kind},
         "e2e": e2e,
         "gpu_launches": kernel_launches_per_step(args.layers) * args.steps,
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(m, torch, args)
+        line["cpu_baseline"], parity = cpu_baseline(m, torch, args)
+        if parity is not None:
+            line["parity"] = parity
     graph.reset()
     prof_graph.reset()
     layer_graph.reset()
@@ -451,78 +489,144 @@ def ncu_traffic():
 
 
 # ---------------------------------------------------------------- reference
-def reference_layer_times(kc, vc, q16, q32, n, alpha, threads, sparse: bool):
+# Both CPU legs -- the repo arm's cpu_baseline and the --impl reference arm --
+# time the same routine, reference_step(), over the same sample: full 32-layer
+# decode steps, every layer on its own data.  Stage 4 (attention) has no
+# reference CPU code (the reference runs it in ggml on the GPU,
+# runtime/gqa_delivery.cpp:15-21), so both time the oracle's threaded float
+# port of that ggml graph for it.
+REF_SAMPLE = ("full 32-layer decode steps at N={n}, every layer on its own data (2 dense + 30 selected-KV): "
+              "reference FullGqaCpuScorer x{t} threads, F16 scaling, select_gqa_scores, gqa_physical_union, "
+              "pack_gqa_workspace from oracle/_ref (built from the reference sources); attention by the oracle's "
+              "float port of the ggml graph, x{t} threads (the reference's attention is ggml on the GPU)")
+
+
+def workload_config(args) -> dict:
+    """The workload both arms measure (identical dicts in both lines)."""
+    n = args.tokens
+    return {"workload": "configs[1]: 32-layer decode step, N=32768, layers 0-1 dense, 2-31 selected-KV",
+            "tokens": n, "layers": args.layers, "alpha": args.alpha, "cap_ratio": 0.2,
+            "kv_bytes_per_step": 2 * 2048 * n * args.layers, "l2": "inputs 4.3 GB >> 126 MB L2, no flush"}
+
+
+def reference_layer(kc, vc, q16, q32, n, alpha, threads, sparse: bool):
     """One layer of the reference CPU path (oracle/_ref) on host arrays.
-    Returns (seconds, k)."""
+    Returns (seconds, result): result holds k, counts and the ordered IDs of
+    a selected-KV layer and the attention output."""
     from oracle import binding as ob
 
     t0 = time.perf_counter()
     if not sparse:
-        ob.attention_dense_fast(kc, vc, n, q32, threads)
-        return time.perf_counter() - t0, n
-    scorer = reference_layer_times.scorers.setdefault(threads, ob.RefScorer(threads, 0))
+        out = ob.attention_dense_fast(kc, vc, n, q32, threads)
+        return time.perf_counter() - t0, {"out": out}
+    scorer = reference_layer.scorers.setdefault(threads, ob.RefScorer(threads, 0))
     raw = scorer.score(q16, [(kc, 0, n, 1024)])
     scaled = ob.ref_scale(raw)
-    ids, counts, k, _ = ob.ref_select(scaled, HEADS, n, n, alpha, 0.2)
+    ids, counts, k, tied = ob.ref_select(scaled, HEADS, n, n, alpha, 0.2)
+    out = np.zeros((HEADS, 128), dtype=np.float32)
     if k:
         sizes = np.full(HEADS, k, dtype=np.uint64)
         physical = ob.ref_union(ids, sizes, n)
         rows = np.empty((len(physical), 2048), dtype=np.uint16)
         rows[:, :1024] = kc.reshape(n, 1024)[physical.astype(np.int64)]
         rows[:, 1024:] = vc.reshape(n, 1024)[physical.astype(np.int64)]
-        count = max(32, (int(math.floor((n) * 0.2)) + 31) // 32 * 32)
+        count = max(32, (int(math.floor(n * 0.2)) + 31) // 32 * 32)
         kp, vp, mask = ob.ref_pack(ids, sizes, [n - 1], physical, rows.reshape(-1).view(np.uint8), count)
-        ob.attention_packed_fast(kp, vp, mask, count, q32, threads)
-    return time.perf_counter() - t0, k
+        out = ob.attention_packed_fast(kp, vp, mask, count, q32, threads)
+    return time.perf_counter() - t0, {"k": int(k), "counts": counts, "ids": ids, "tied": int(tied), "out": out}
 
 
-reference_layer_times.scorers = {}
+reference_layer.scorers = {}
 
 
-def host_layers(torch, tokens, layers, seed):
-    """The same seeded inputs as our arm (generated on the GPU, then held in
-    host memory for the CPU path)."""
-    import hillserve_b200 as hsb
+def reference_step(data, n, alpha, threads):
+    """One decode step of the reference CPU path over every layer of `data`
+    (a list of (K, V, Q16, Q32) host arrays per layer).  Returns (seconds,
+    per-layer results)."""
+    t = 0.0
+    results = []
+    for l, d in enumerate(data):
+        dt, r = reference_layer(*d, n, alpha, threads, l >= DENSE)
+        t += dt
+        results.append(r)
+    return t, results
 
-    m = Model(hsb, torch, tokens, min(layers, 4), 0.1, seed)
-    torch.cuda.synchronize()
+
+def cpu_layers(tokens, layers, seed, threads):
+    """The benchmark's inputs rebuilt on the CPU by the oracle's restatement of
+    the library's generator -- the same bits as the GPU's hsb_synth_* (checked
+    in tests/test_gpu_bench_inputs.py) without loading the library."""
+    from oracle import binding as ob
+
     out = []
-    for l in range(min(layers, 4)):
-        out.append((m.kc[l].cpu().numpy().view(np.uint16), m.vc[l].cpu().numpy().view(np.uint16),
-                    m.q16[l].cpu().numpy().view(np.uint16), m.q32[l].cpu().numpy()))
-    del m
-    torch.cuda.empty_cache()
+    for l in range(layers):
+        sq, sk, sv = layer_seeds(seed, l)
+        q16 = ob.synth_normal(4096, sq, 1.0, threads=threads)
+        kc = ob.synth_keys(tokens, sk, 0.02, 4.0, True, THETA, threads=threads)
+        vc = ob.synth_keys(tokens, sv, 0.0, 1.0, False, THETA, threads=threads)
+        out.append((kc, vc, q16, q16.view(np.float16).astype(np.float32)))
     return out
 
 
-def cpu_baseline(m, torch, args, sample_layers=(0, 2, 3)):
-    """Reference CPU path timed on this host's cores on a bounded sample: one
-    dense and two selected-KV layers, scaled to the 32-layer step."""
+def parity_block(m, ref_results):
+    """The GPU's selections and outputs of the timed step against the
+    reference CPU path's on the same layers: k, counts, boundary ties and the
+    ordered IDs bit for bit; attention relative to the output's largest
+    magnitude (tolerance 2e-3)."""
+    res = m.results.cpu().numpy()
+    counts = m.counts.cpu().numpy().astype(np.uint32)
+    ids = m.ids.cpu().numpy().astype(np.uint64)
+    outs = m.out.cpu().numpy().astype(np.float64)
+    layers, bad, worst = [], [], 0.0
+    for l, r in enumerate(ref_results):
+        want = r["out"].astype(np.float64)
+        scale = float(np.max(np.abs(want))) or 1.0
+        if l >= DENSE:
+            layers.append(l)
+            k = r["k"]
+            ok = int(res[l, 0]) == k and int(res[l, 1]) == r["tied"] and np.array_equal(counts[l], r["counts"])
+            ok = ok and np.array_equal(ids[l, :, :k], r["ids"][:, :k])
+            ok = ok and int(res[l, 2]) == (70 if k == 0 else 0)
+            if not ok:
+                bad.append(l)
+            if k == 0:
+                continue  # the reference throws "zero selection"; the output stays zero
+        worst = max(worst, float(np.max(np.abs(outs[l] - want))) / scale)
+    return {"layers": layers, "bit_exact": not bad, "mismatched_layers": bad,
+            "checked": "k, counts, boundary ties, status and ordered per-head IDs of every selected-KV layer of the "
+                       "timed step vs the reference CPU path on the same data",
+            "attention_max_rel_err": round(worst, 7), "attention_tol": 2e-3,
+            "attention_vs": "the oracle's float port of the ggml attention graph"}
+
+
+def cpu_baseline(m, torch, args):
+    """The reference CPU path timed on this host's cores over full 32-layer
+    steps of the same data as the GPU arm (copied from HBM), and the parity
+    check of the GPU's results against it."""
     from oracle import binding as ob
 
     if not ob.reference_available():
         return {"value": None, "unit": "layer-steps/s", "cores": os.cpu_count(), "kind": "unavailable",
-                "sample": "oracle/_ref was not built (reference sources absent when built)"}
+                "sample": "oracle/_ref was not built (reference sources absent when built)"}, None
     threads = min(128, os.cpu_count() or 1)  # FullGqaCpuScorer accepts 1..128 threads
     n = args.tokens
-    data = {}
-    for l in sample_layers:
-        data[l] = (m.kc[l].cpu().numpy().view(np.uint16), m.vc[l].cpu().numpy().view(np.uint16),
-                   m.q16[l].cpu().numpy().view(np.uint16), m.q32[l].cpu().numpy())
-    reference_layer_times(*data[sample_layers[1]], n, args.alpha, threads, True)  # warm-up
-    dense_t = [reference_layer_times(*data[l], n, args.alpha, threads, l < DENSE)[0] for l in sample_layers
-               if l < DENSE]
-    sparse_t = [reference_layer_times(*data[l], n, args.alpha, threads, False)[0] for l in sample_layers
-                if l >= DENSE]
-    step_s = DENSE * float(np.mean(dense_t)) + (args.layers - DENSE) * float(np.mean(sparse_t))
-    return {"value": round(args.layers / step_s, 3), "unit": "layer-steps/s", "cores": threads, "kind": "reference",
-            "sample": f"1 dense + {len(sparse_t)} selected-KV layers at N={n} (reference FullGqaCpuScorer "
-                      f"x{threads} threads, select_gqa_scores, gqa_physical_union, pack_gqa_workspace; attention "
-                      f"by the oracle port, x{threads} threads), scaled to {args.layers} layers",
-            "dense_layer_s": round(float(np.mean(dense_t)), 4), "sparse_layer_s": round(float(np.mean(sparse_t)), 4)}
+    data = [(m.kc[l].cpu().numpy().view(np.uint16), m.vc[l].cpu().numpy().view(np.uint16),
+             m.q16[l].cpu().numpy().view(np.uint16), m.q32[l].cpu().numpy()) for l in range(args.layers)]
+    reference_layer(*data[DENSE], n, args.alpha, threads, True)  # warm-up
+    times = []
+    for _ in range(2):
+        t, results = reference_step(data, n, args.alpha, threads)
+        times.append(t)
+    step_s = float(np.mean(times))
+    line = {"value": round(args.layers / step_s, 3), "unit": "layer-steps/s", "cores": threads, "kind": "reference",
+            "sample": "2 " + REF_SAMPLE.format(n=n, t=threads), "step_s": round(step_s, 4)}
+    return line, parity_block(m, results)
 
 
 def run_reference(args, rank, world, torch):
+    """The reference arm: the reference's own CPU path (oracle/_ref) timed on
+    this host's cores on the repo arm's workload, its inputs rebuilt on the
+    CPU (no GPU and none of the library's code).  Rank 0 only."""
     from oracle import binding as ob
 
     if rank != 0:
@@ -531,31 +635,27 @@ def run_reference(args, rank, world, torch):
         return {"impl": "reference", "unavailable": "oracle/_ref not built: reference sources were absent at build"}
     threads = min(128, os.cpu_count() or 1)
     n = args.tokens
-    layers = host_layers(torch, n, args.layers, seed=0)
-    for _ in range(max(args.warmup, 3)):
-        reference_layer_times(*layers[2 % len(layers)], n, args.alpha, threads, True)
-    # Each step: the 32-layer decode step with the layers' data cycled from a
-    # 4-layer sample (2 dense + 2 selected-KV).
     t0 = time.perf_counter()
-    ks = []
+    data = cpu_layers(n, args.layers, 0, threads)
+    gen_s = time.perf_counter() - t0
+    warm = max(args.warmup, 3)
+    for _ in range(warm):
+        reference_step(data, n, args.alpha, threads)
+    secs, ks = 0.0, []
     for _ in range(args.steps):
-        for l in range(args.layers):
-            d = layers[l % len(layers)] if l < DENSE else layers[DENSE + (l % 2)]
-            _, k = reference_layer_times(*d, n, args.alpha, threads, l >= DENSE)
-            if l >= DENSE:
-                ks.append(k)
-    secs = time.perf_counter() - t0
+        t, results = reference_step(data, n, args.alpha, threads)
+        secs += t
+        ks = [r["k"] for r in results[DENSE:]]
     value = args.layers * args.steps / secs
-    return {"metric": "selected-KV decode layer-steps/s at N=32K (score+select+gather HBM GB/s vs peak)",
-            "value": round(value, 3), "unit": "layer-steps/s", "n_gpus": world, "steps": args.steps,
-            "warmup": max(args.warmup, 3), "ms_per_step": round(secs * 1e3 / args.steps, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 in, f32 accumulate",
-            "data": "synthetic", "impl": "reference",
-            "config": {"workload": "configs[1]: 32-layer decode step, N=32768, layers 0-1 dense, 2-31 selected-KV",
-                       "tokens": n, "layers": args.layers, "alpha": args.alpha, "cap_ratio": 0.2},
-            "selection": {"k_mean": float(np.mean(ks)) if ks else 0.0},
-            "cpu_baseline": {"value": round(value, 3), "unit": "layer-steps/s", "cores": threads, "kind": "reference",
-                             "sample": "full 32-layer steps, layer data cycled from 2 dense + 2 selected-KV layers"},
+    return {"metric": METRIC, "value": round(value, 3), "unit": "layer-steps/s", "n_gpus": world,
+            "steps": args.steps, "warmup": warm, "ms_per_step": round(secs * 1e3 / args.steps, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 in, f32 accumulate (ordered)", "data": "synthetic", "impl": "reference",
+            "config": workload_config(args),
+            "selection": {"k_mean": float(np.mean(ks)) if ks else 0.0, "k_per_layer": ks},
+            "cpu_baseline": {"value": round(value, 3), "unit": "layer-steps/s", "cores": threads,
+                             "kind": "reference", "sample": REF_SAMPLE.format(n=n, t=threads)},
+            "inputs": f"rebuilt on the CPU by the oracle's restatement of the generator ({gen_s:.1f} s, untimed)",
             "e2e": {"value": round(value, 3), "unit": "layer-steps/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
 
@@ -1146,7 +1246,7 @@ def run_history(args, torch):
             q16 = qs[2].cpu().numpy().view(np.uint16).reshape(-1)
             q32 = q16.view(np.float16).astype(np.float32).reshape(32, 128)
             threads = min(16, os.cpu_count() or 1)
-            secs, _ = reference_layer_times(kc, vc, q16, q32, n, alpha, threads, True)
+            secs, _ = reference_layer(kc, vc, q16, q32, n, alpha, threads, True)
             cpu = {"value": round(secs * 1e6, 1), "unit": "us per layer", "cores": threads, "kind": "reference",
                    "sample": f"one selected-KV layer at N={n}: FullGqaCpuScorer x{threads}, select_gqa_scores, "
                              "gqa_physical_union, pack_gqa_workspace (oracle/_ref), attention by the oracle port"}

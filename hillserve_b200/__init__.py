@@ -327,6 +327,32 @@ def rehearsal_query(x, w, position: int, theta: float = 500000.0, stream=None):
     return q32, q16
 
 
+# ---------------------------------------------------- synthetic inputs
+def synth_normal(count: int, seed: int, stddev: float = 1.0, bf16: bool = False, out=None, device="cuda",
+                 stream=None):
+    """Seeded N(0, stddev) values as F16 (or BF16) bits, int16 [count]
+    (hsb_synth_normal_f16 / _bf16; reproducible on the CPU bit for bit)."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty(int(count), dtype=torch.int16, device=device)
+    fn = lib().hsb_synth_normal_bf16 if bf16 else lib().hsb_synth_normal_f16
+    _raise(fn(_ptr(out), int(count), int(seed), C.c_float(stddev), _stream(stream)))
+    return out
+
+
+def synth_keys(tokens: int, seed: int, heavy_fraction: float = 0.02, heavy_scale: float = 4.0, rope: bool = True,
+               theta: float = 500000.0, stride_words: int = 1024, out=None, device="cuda", stream=None):
+    """Seeded key rows [tokens][stride_words] (1024 words written per row):
+    N(0,1) F16 values, a heavy_fraction of rows times heavy_scale, NORM-mode
+    RoPE by token position (hsb_synth_keys)."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty(int(tokens) * int(stride_words), dtype=torch.int16, device=device)
+    _raise(lib().hsb_synth_keys(_ptr(out), int(tokens), int(stride_words), int(seed), C.c_float(heavy_fraction),
+                                C.c_float(heavy_scale), int(rope), C.c_float(theta), _stream(stream)))
+    return out
+
+
 def attention_slots(position: int, ratio: float = 0.2) -> int:
     """Reference delivery slot count max(32, roundup32(floor(0.2*(pos+1))))
     (runtime/gqa_executor.cpp:145)."""
@@ -788,8 +814,17 @@ class SelectedKVLayer:
                                      self.result.data_ptr(), self.k_packed.data_ptr(), self.v_packed.data_ptr(),
                                      self.workspace.data_ptr(), self.workspace.numel())
 
-    def __call__(self, q16, q32, kcache, vcache, stride_words: int = 1024, out=None, stream=None):
+    def __call__(self, q16, q32, kcache, vcache, stride_words: int = 1024, out=None, stream=None, prefetch=None,
+                 prefetch_bytes: int = 0):
+        """prefetch / prefetch_bytes: a range (the next layer's keys) to pull
+        into L2 while the selection runs (hsb_layer_step_prefetch)."""
         out = self.out if out is None else out
+        if prefetch is not None and prefetch_bytes:
+            _raise(lib().hsb_layer_step_prefetch(_ptr(q16), _ptr(q32), _ptr(kcache), _ptr(vcache), stride_words,
+                                                 self.valid, C.c_float(self.alpha), C.c_float(self.ratio),
+                                                 self.count, C.byref(self._buffers), _ptr(out), _ptr(prefetch),
+                                                 int(prefetch_bytes), _stream(stream)))
+            return out
         _raise(lib().hsb_layer_step(_ptr(q16), _ptr(q32), _ptr(kcache), _ptr(vcache), stride_words, self.valid,
                                     C.c_float(self.alpha), C.c_float(self.ratio), self.count, C.byref(self._buffers),
                                     _ptr(out), _stream(stream)))

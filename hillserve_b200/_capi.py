@@ -69,6 +69,7 @@ _SIGNATURES = {
     "hsb_rehearsal_query": (I, [P, P, U64, F, P, P, P]),
     "hsb_layer_workspace_bytes": (SZ, [SZ, SZ]),
     "hsb_layer_step": (I, [P, P, P, P, SZ, SZ, F, F, SZ, P, P, P]),
+    "hsb_layer_step_prefetch": (I, [P, P, P, P, SZ, SZ, F, F, SZ, P, P, P, SZ, P]),
     "hsb_shard_head0_words": (SZ, []),
     "hsb_shard_score": (I, [P, I, P, SZ, SZ, P, P, P, P]),
     "hsb_shard_threshold": (I, [P, SZ, F, P, P]),

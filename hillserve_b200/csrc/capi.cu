@@ -513,10 +513,13 @@ LayerLayout layer_layout(size_t valid, size_t count) {
 
 size_t hsb_layer_workspace_bytes(size_t valid, size_t count) { return layer_layout(valid, count).total; }
 
-int hsb_layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_kcache, const uint16_t* d_vcache,
-                   size_t stride_words, size_t valid, float alpha, float ratio, size_t count,
-                   const hsb_layer_buffers* b, float* d_out, void* stream) {
+static int layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_kcache, const uint16_t* d_vcache,
+                      size_t stride_words, size_t valid, float alpha, float ratio, size_t count,
+                      const hsb_layer_buffers* b, float* d_out, const void* d_prefetch, size_t prefetch_bytes,
+                      void* stream) {
     if (!b || !d_q16 || !d_q32 || !d_out) return fail(HSB_E_INVALID, "layer step arguments");
+    if (prefetch_bytes && (!d_prefetch || !aligned(d_prefetch, 16)))
+        return fail(HSB_E_INVALID, "layer step: the prefetch range must start on a 16-byte boundary");
     int rc = check_select(HSB_QUERY_HEADS, valid, valid, alpha, ratio);
     if (rc) return rc;
     if (count < select_kmax(valid, ratio) || count == 0)
@@ -581,6 +584,8 @@ int hsb_layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_
     sl.ga.count = count;
     sl.ga.out = d_out;
     sl.ga.scale = 1.0f / sqrtf(128.0f);
+    sl.ga.prefetch = d_prefetch;
+    sl.ga.prefetch_bytes = prefetch_bytes & ~(size_t)15;
     int fused = 0;
     sl.ga_done = &fused;
     if ((e = launch_select(sl, s)) != cudaSuccess) return fail_cuda(e, "select launch");
@@ -591,6 +596,21 @@ int hsb_layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_
         return fail_cuda(e, "gather-attention launch");
     g_last_error.clear();
     return HSB_OK;
+}
+
+int hsb_layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_kcache, const uint16_t* d_vcache,
+                   size_t stride_words, size_t valid, float alpha, float ratio, size_t count,
+                   const hsb_layer_buffers* b, float* d_out, void* stream) {
+    return layer_step(d_q16, d_q32, d_kcache, d_vcache, stride_words, valid, alpha, ratio, count, b, d_out, nullptr,
+                      0, stream);
+}
+
+int hsb_layer_step_prefetch(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_kcache,
+                            const uint16_t* d_vcache, size_t stride_words, size_t valid, float alpha, float ratio,
+                            size_t count, const hsb_layer_buffers* b, float* d_out, const void* d_next,
+                            size_t next_bytes, void* stream) {
+    return layer_step(d_q16, d_q32, d_kcache, d_vcache, stride_words, valid, alpha, ratio, count, b, d_out, d_next,
+                      next_bytes, stream);
 }
 
 // ------------------------------------------------------------ KV-head shards

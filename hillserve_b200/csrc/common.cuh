@@ -177,6 +177,13 @@ __device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int x, i
                  : "memory");
 }
 
+// Untiled bulk prefetch of [src, src + bytes) into L2 (a hint: nothing
+// waits for it and no data can be stale).  src 16-byte aligned, bytes a
+// multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Named barrier `id` (1..15; 0 is __syncthreads) over `count` threads, a
 // multiple of 32: whole warps take part.
 __device__ __forceinline__ void named_sync(int id, int count) {

@@ -98,6 +98,11 @@ struct SelectEpilogue {
     float* out = nullptr;    // null: no epilogue
     float scale = 0.0f;
     unsigned heads = 32;     // query heads per packed K slot (a shard packs its own)
+    // L2 prefetch hint issued as the selector starts: `prefetch_bytes` at
+    // `prefetch` (16-byte aligned, a multiple of 16), split over the grid --
+    // the next layer's key cache, streamed while the selection runs.
+    const void* prefetch = nullptr;
+    unsigned long long prefetch_bytes = 0;
 };
 struct SelectLaunch {
     const uint16_t* scores;

@@ -3,12 +3,10 @@
 // memory of their own.
 //
 // Who needs it: an attention step that runs as an operator inside a host
-// framework's compute graph (a ggml-style backend op, or a decode step being
-// captured into a CUDA graph in global capture mode). Such an operator is
-// handed its input and output tensors and a stream, and nothing else. It has
-// no workspace slot to pass. It may not call cudaMalloc either: the
-// framework's allocator owns device memory, and global-mode capture refuses
-// the call.
+// framework's compute graph (a ggml-style backend op, for instance). Such an
+// operator is handed its input and output tensors and a stream, and nothing
+// else: it has no workspace slot to pass, and it may not call cudaMalloc,
+// because the framework's allocator owns the device memory.
 //
 // What it does instead: the attention's scratch (the per-split partial
 // results and the per-head arrival counters of its last-CTA combine) lives
@@ -24,13 +22,18 @@
 //    Calls whose executions overlap on the GPU (different streams, or
 //    different host threads without ordering) race on the array and give
 //    wrong results. Order them on one stream.
-//  - The first call on each device resolves the array's device address with
-//    cudaGetSymbolAddress (with that device current). Make that first call
-//    before any stream capture begins.
+//  - The first call in each CUDA context (normally once per device: the
+//    device's primary context) resolves the array's device address with
+//    cudaGetSymbolAddress, with that context current. Make that first call
+//    before any stream capture begins. A context created later on the same
+//    device -- after cudaDeviceReset, or a host framework's own driver-API
+//    context made current -- is a new set-up: its first call resolves the
+//    address again (the cache is keyed by the context's unique ID).
 //
 // The entry point allocates nothing: it calls no cudaMalloc / cudaFree and
 // no allocating library routine. It then runs exactly the kernel of
 // hsb_attention_packed.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -47,26 +50,73 @@ namespace {
 constexpr size_t kScratchBytes = 448 * 1024;
 __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
+// The address belongs to the module instance of one CUDA context, so the
+// cache is keyed by the context's unique ID (cuCtxGetId; the handle from
+// cuCtxGetCurrent where the driver lacks it), not by the device ordinal.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+struct ScratchEntry {
+    unsigned long long context = 0;
+    void* address = nullptr;
+};
+constexpr int kScratchEntries = 64;
 std::mutex g_scratch_mutex;
-void* g_scratch_address[64] = {};
+ScratchEntry g_scratch_cache[kScratchEntries];
+int g_scratch_next = 0;
 
-// Device address of g_noalloc_scratch on the current device; resolved once
-// per device.  Returns HSB_OK or an error already recorded.
-int scratch_address(void** out) {
-    int dev = -1;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return record_cuda_error(e, "hsb_attention_packed_noalloc: cudaGetDevice");
-    if (dev < 0 || dev >= 64) return record_error(HSB_E_NO_DEVICE, "hsb_attention_packed_noalloc: device ordinal out of range");
-    std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (g_scratch_address[dev] == nullptr) {
-        void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || p == nullptr)
-            return record_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidSymbol,
-                                     "hsb_attention_packed_noalloc: cudaGetSymbolAddress of the static scratch");
-        g_scratch_address[dev] = p;
+void* driver_entry(const char* name) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint(name, &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+        cudaGetLastError();
+        return nullptr;
     }
-    *out = g_scratch_address[dev];
+    return f;
+}
+
+// Unique key of the calling thread's current context; 0 on failure.
+unsigned long long current_context_key() {
+    static CtxGetCurrentFn get_current = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        get_current = reinterpret_cast<CtxGetCurrentFn>(driver_entry("cuCtxGetCurrent"));
+        get_id = reinterpret_cast<CtxGetIdFn>(driver_entry("cuCtxGetId"));
+    });
+    if (!get_current) return 0;
+    CUcontext ctx = nullptr;
+    if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+    unsigned long long id = 0;
+    if (get_id && get_id(ctx, &id) == CUDA_SUCCESS) return id + 1;  // never 0
+    return reinterpret_cast<unsigned long long>(ctx);
+}
+
+// Device address of g_noalloc_scratch in the current context, resolved once
+// per context.  Returns HSB_OK or an error already recorded.
+int scratch_address(void** out) {
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    unsigned long long key = current_context_key();
+    if (key != 0) {
+        for (const ScratchEntry& entry : g_scratch_cache) {
+            if (entry.context == key) {
+                *out = entry.address;
+                return HSB_OK;
+            }
+        }
+    }
+    // Resolving the symbol also makes the device's primary context current
+    // when the thread had none yet.
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+        return record_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidSymbol,
+                                 "hsb_attention_packed_noalloc: cudaGetSymbolAddress of the static scratch");
+    if (key == 0) key = current_context_key();
+    if (key == 0) return record_error(HSB_E_NO_DEVICE, "hsb_attention_packed_noalloc: no current CUDA context");
+    g_scratch_cache[g_scratch_next] = ScratchEntry{key, p};
+    g_scratch_next = (g_scratch_next + 1) % kScratchEntries;
+    *out = p;
     return HSB_OK;
 }
 

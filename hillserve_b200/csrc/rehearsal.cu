@@ -8,9 +8,6 @@
 // together -- streaming both W rows with 16-byte loads and reducing in FP32.
 // The rotation angle position * theta^(-2i/128) and its sine/cosine are
 // evaluated in FP64 so that large positions keep full accuracy.
-//
-// Also: seeded synthetic inputs for benchmarks (counter-based hash +
-// Box-Muller), which are not part of the reference path.
 #include <algorithm>
 #include <cmath>
 
@@ -76,82 +73,11 @@ __global__ void __launch_bounds__(kRThreads) rehearsal_kernel(const uint16_t* __
     }
 }
 
-// ---------------------------------------------------------------- synthetic
-__device__ __forceinline__ unsigned long long mix64(unsigned long long z) {
-    z += 0x9e3779b97f4a7c15ull;
-    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
-    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
-    return z ^ (z >> 31);
-}
-// One N(0,1) sample per (seed, index): Box-Muller on two 24-bit uniforms.
-__device__ __forceinline__ float normal_sample(unsigned long long seed, unsigned long long i) {
-    const unsigned long long u = mix64(seed ^ mix64(i));
-    const float u1 = ((float)(u >> 40) + 0.5f) * (1.0f / 16777216.0f);
-    const float u2 = ((float)((u >> 16) & 0xffffffull) + 0.5f) * (1.0f / 16777216.0f);
-    return sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
-}
-
-__global__ void synth_normal_kernel(uint16_t* out, unsigned long long count, unsigned long long seed,
-                                    float stddev, int bf16) {
-    for (unsigned long long i = blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x; i < count;
-         i += (unsigned long long)gridDim.x * blockDim.x) {
-        const float v = normal_sample(seed, i) * stddev;
-        out[i] = bf16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v)) : half_bits(v);
-    }
-}
-
-// rows: [tokens][1024 words used] at stride_words; one thread per channel pair.
-__global__ void synth_keys_kernel(uint16_t* rows, unsigned long long tokens, unsigned long long stride,
-                                  unsigned long long seed, float heavy_fraction, float heavy_scale, int rope,
-                                  float theta) {
-    const unsigned long long pairs = tokens * 512ull;
-    const unsigned long long heavy_cut = (unsigned long long)((double)heavy_fraction * 18446744073709551616.0);
-    for (unsigned long long i = blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x; i < pairs;
-         i += (unsigned long long)gridDim.x * blockDim.x) {
-        const unsigned long long t = i / 512, c2 = (i % 512) * 2;  // c2 = kv_head*128 + even channel
-        const float scale = (heavy_fraction > 0.f && mix64(seed * 0x2545f4914f6cdd1dull + t) < heavy_cut)
-                                ? heavy_scale : 1.0f;
-        float a = normal_sample(seed, t * 1024 + c2) * scale;
-        float b = normal_sample(seed, t * 1024 + c2 + 1) * scale;
-        if (rope) {
-            const int ii = (int)((c2 & 127) >> 1);
-            const float inv = powf(theta, -2.0f * (float)ii / 128.0f);
-            float s, c;
-            sincosf((float)t * inv, &s, &c);
-            const float ra = a * c - b * s, rb = a * s + b * c;
-            a = ra;
-            b = rb;
-        }
-        uint16_t* row = rows + t * stride;
-        row[c2] = half_bits(a);
-        row[c2 + 1] = half_bits(b);
-    }
-}
-
-int grid_for(unsigned long long n) {
-    const DeviceInfo& dev = device_info();
-    return (int)std::max<unsigned long long>(1, std::min<unsigned long long>((n + 255) / 256, (unsigned long long)dev.sms * 16));
-}
-
 }  // namespace
 
 cudaError_t launch_rehearsal(const uint16_t* x, const uint16_t* w, uint64_t position, float theta, float* q32,
                              uint16_t* q16, cudaStream_t stream) {
     rehearsal_kernel<<<kHeads * kDim / 16, kRThreads, 0, stream>>>(x, w, position, theta, q32, q16);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_synth_normal(uint16_t* out, size_t count, uint64_t seed, float stddev, int bf16,
-                                cudaStream_t stream) {
-    synth_normal_kernel<<<grid_for(count), 256, 0, stream>>>(out, count, seed, stddev, bf16);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_synth_keys(uint16_t* rows, size_t tokens, size_t stride_words, uint64_t seed,
-                              float heavy_fraction, float heavy_scale, int rope, float theta,
-                              cudaStream_t stream) {
-    synth_keys_kernel<<<grid_for(tokens * 512ull), 256, 0, stream>>>(rows, tokens, stride_words, seed,
-                                                                      heavy_fraction, heavy_scale, rope, theta);
     return cudaGetLastError();
 }
 

@@ -707,6 +707,17 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __maxnreg__(80)
     select_cluster_kernel(const __grid_constant__ SelectParams p) {
     pdl_wait();
     pdl_trigger();
+    // The next layer's keys into L2 while this selection runs (the scorer
+    // has finished, so DRAM would otherwise idle): the last warp of every CTA
+    // issues 64 KB bulk prefetches over the CTA's share of the range.
+    if (p.ga.prefetch_bytes && (threadIdx.x >> 5) == kCWarps - 1) {
+        const unsigned long long share = (p.ga.prefetch_bytes / gridDim.x + 15) & ~15ull;
+        const unsigned long long b0 = min(p.ga.prefetch_bytes, (unsigned long long)blockIdx.x * share);
+        const unsigned long long b1 = min(p.ga.prefetch_bytes, b0 + share);
+        const unsigned char* base = static_cast<const unsigned char*>(p.ga.prefetch);
+        for (unsigned long long o = b0 + (unsigned long long)(threadIdx.x & 31) * 65536; o < b1; o += 32ull * 65536)
+            bulk_prefetch_l2(base + o, (uint32_t)min(65536ull, b1 - o));
+    }
     extern __shared__ __align__(16) unsigned char dyn[];
     __shared__ ClusterShared sh;
     cg::cluster_group cl = cg::this_cluster();

@@ -256,17 +256,18 @@ int hsb_attention_packed(const float* d_q, const uint16_t* d_k, const uint16_t* 
                          void* d_workspace, size_t workspace_bytes, void* stream);
 /* hsb_attention_packed without a workspace argument; it has no counterpart in
  * the reference.  It is meant for callers that cannot provide or allocate any
- * device memory beyond their inputs and outputs: an operator run inside a
- * host framework's compute graph, whose tensors are handed to it and whose
- * allocator owns device memory, or a step captured in global capture mode,
- * where cudaMalloc is refused.  The scratch is a static device array of
- * 448 KiB that every GPU loading this library holds until exit; count must be
- * <= HSB_NOALLOC_MAX_SLOTS (the reference delivery workspace's slot limit),
- * else HSB_E_WORKSPACE.  The call allocates nothing.  The first call on each
- * device resolves the array's address (cudaGetSymbolAddress) and should come
- * before any stream capture.  All calls on a device share the array and its
- * last contents: calls that overlap on the GPU race, so order them on one
- * stream. */
+ * device memory beyond their inputs and outputs, such as an operator run
+ * inside a host framework's compute graph, whose tensors are handed to it and
+ * whose allocator owns the device memory.  The scratch is a static device
+ * array of 448 KiB that every GPU loading this library holds until exit;
+ * count must be <= HSB_NOALLOC_MAX_SLOTS (the reference delivery workspace's
+ * slot limit), else HSB_E_WORKSPACE.  The call allocates nothing.  The first
+ * call in each CUDA context (normally once per device) resolves the array's
+ * address (cudaGetSymbolAddress) and should come before any stream capture;
+ * a new context on the device (after cudaDeviceReset, or another context
+ * made current) resolves it again on its first call.  All calls on a device
+ * share the array and its last contents: calls that overlap on the GPU race,
+ * so order them on one stream. */
 #define HSB_NOALLOC_MAX_SLOTS 6592
 int hsb_attention_packed_noalloc(const float* d_q, const uint16_t* d_k, const uint16_t* d_v,
                                  size_t count, const float* d_mask, size_t qpad,
@@ -313,6 +314,17 @@ int hsb_layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_
                    const uint16_t* d_vcache, size_t stride_words, size_t valid, float alpha,
                    float ratio, size_t count, const hsb_layer_buffers* buffers, float* d_out,
                    void* stream);
+/* hsb_layer_step that also streams the next layer's key cache into L2 while
+ * this layer's selection runs (the scorer has finished and DRAM would
+ * otherwise idle): next_bytes at d_next (16-byte aligned; rounded down to a
+ * multiple of 16) are prefetched as an L2 hint by the selector's CTAs.
+ * Nothing waits for it and nothing can read stale data through it, so the
+ * results are those of hsb_layer_step; a decode step passes layer l + 1's
+ * keys to layer l. */
+int hsb_layer_step_prefetch(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_kcache,
+                            const uint16_t* d_vcache, size_t stride_words, size_t valid, float alpha,
+                            float ratio, size_t count, const hsb_layer_buffers* buffers, float* d_out,
+                            const void* d_next, size_t next_bytes, void* stream);
 
 /* ------------------------------------------------------- KV-head shards
  * One selected-KV layer split across GPUs by KV head (each GPU holds
@@ -538,10 +550,18 @@ int hsb_executor_decode_layer(const uint16_t* d_current, const float* d_rehearsa
                               hsb_device_status* d_status, void* stream);
 
 /* ------------------------------------------------------ synthetic inputs
- * Benchmark inputs, not part of the reference interface: seeded F16 normal
- * values (counter-based hash + Box-Muller).  For K rows, a heavy_fraction of
- * token rows is multiplied by heavy_scale before rounding, and rope != 0
- * rotates adjacent channel pairs by position * theta^(-2i/128). */
+ * Benchmark inputs, not part of the reference interface, defined so that a
+ * CPU program reproduces them bit for bit.  Sample i of stream `seed`:
+ * a = mix64(seed ^ mix64(i)), b = mix64(a) (mix64 = the splitmix64
+ * finaliser), u1 = ((a >> 12) + 0.5) * 2^-52, u2 = ((b >> 12) + 0.5) * 2^-52,
+ * value = sqrt(-2 ln u1) * cos(2 pi u2) * stddev in IEEE double, one rounding
+ * per operation, with ln, e^x and sin/cos of 2 pi x evaluated by fixed series
+ * (the formulas are in csrc/synth.cu), then rounded to F32 and to F16 (or
+ * BF16) with round-to-nearest-even.  Key rows (1024 words each, at
+ * stride_words): token t is heavy when mix64(seed * 0x2545f4914f6cdd1d + t)
+ * < heavy_fraction * 2^64, its values then times heavy_scale; rope != 0
+ * rotates channel pair (2i, 2i+1) of every KV head by t * theta^(-i/64)
+ * (NORM mode), in double, before the rounding. */
 int hsb_synth_normal_f16(uint16_t* d_out, size_t count, uint64_t seed, float stddev,
                          void* stream);
 int hsb_synth_normal_bf16(uint16_t* d_out, size_t count, uint64_t seed, float stddev,

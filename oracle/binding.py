@@ -72,6 +72,10 @@ def oracle() -> C.CDLL:
         lib.orc_kv_records_encode.argtypes = [P, SZ, SZ, SZ, C.c_uint64, C.c_uint32, C.c_uint64, P]
         lib.orc_kv_records_encode.restype = None
         lib.orc_kv_records_verify.argtypes = [P, SZ, P, P, P, SZ, C.c_uint64, C.c_uint32, SZ, P, SZ, P, SZ, P]
+        lib.orc_synth_normal.argtypes = [P, SZ, C.c_uint64, C.c_float, C.c_int, C.c_int]
+        lib.orc_synth_normal.restype = None
+        lib.orc_synth_keys.argtypes = [P, SZ, SZ, C.c_uint64, C.c_float, C.c_float, C.c_int, C.c_float, C.c_int]
+        lib.orc_synth_keys.restype = None
         _oracle = lib
     return _oracle
 
@@ -283,6 +287,23 @@ def rehearsal(x_bf16, w_bf16, position: int, theta: float = 500000.0) -> np.ndar
 
 
 # ------------------------------------------------------------- reference
+def synth_normal(count: int, seed: int, stddev: float = 1.0, bf16: bool = False, threads: int = 8) -> np.ndarray:
+    """The library's seeded normal generator (hsb_synth_normal_f16/_bf16),
+    restated on the CPU: uint16 F16 (or BF16) bits [count]."""
+    out = np.empty(count, dtype=np.uint16)
+    oracle().orc_synth_normal(_p(out), count, seed, stddev, int(bf16), threads)
+    return out
+
+
+def synth_keys(tokens: int, seed: int, heavy_fraction: float = 0.02, heavy_scale: float = 4.0, rope: bool = True,
+               theta: float = 500000.0, stride: int = 1024, threads: int = 8) -> np.ndarray:
+    """The library's key-row generator (hsb_synth_keys), restated on the
+    CPU: uint16 [tokens * stride] with 1024 words per row written."""
+    out = np.zeros(tokens * stride, dtype=np.uint16)
+    oracle().orc_synth_keys(_p(out), tokens, stride, seed, heavy_fraction, heavy_scale, int(rope), theta, threads)
+    return out
+
+
 def _err():
     return C.create_string_buffer(512)
 

@@ -657,3 +657,192 @@ int orc_kv_records_verify(const void* window, size_t window_bytes, const uint64_
     }
     return 0;
 }
+
+/* ---------------------------------------------------------------------
+ * Synthetic benchmark inputs: a restatement of the library's generator
+ * (hsb_synth_normal_f16 / _bf16 / hsb_synth_keys), so that the inputs the
+ * benchmark times can be rebuilt on the CPU and its selections checked
+ * against the reference.  Not a reference algorithm.  Every operation is an
+ * IEEE double operation with one rounding (built with -ffp-contract=off), and
+ * the elementary functions are series in those operations:
+ *   ln m = 2 atanh((m-1)/(m+1)) on m in (1/sqrt2, sqrt2], 12 odd terms;
+ *   e^r after Cody-Waite reduction by ln2 (split in two), Taylor to r^16;
+ *   sin, cos of 2 pi x after folding x to [0, 1/8] turn, Taylor to t^19. */
+static uint64_t syn_mix64(uint64_t z) {
+    z += 0x9e3779b97f4a7c15ull;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
+static double syn_log(double x) {
+    uint64_t bits;
+    memcpy(&bits, &x, 8);
+    int e = (int)((bits >> 52) & 0x7ff) - 1023;
+    const uint64_t mb = (bits & 0x000fffffffffffffull) | 0x3ff0000000000000ull;
+    double m;
+    memcpy(&m, &mb, 8);
+    if (m > 0x1.6a09e667f3bcdp+0) {
+        m = m * 0.5;
+        e += 1;
+    }
+    static const double inv_odd[12] = {
+        1.0, 0x1.5555555555555p-2, 0x1.999999999999ap-3, 0x1.2492492492492p-3,
+        0x1.c71c71c71c71cp-4, 0x1.745d1745d1746p-4, 0x1.3b13b13b13b14p-4, 0x1.1111111111111p-4,
+        0x1.e1e1e1e1e1e1ep-5, 0x1.af286bca1af28p-5, 0x1.8618618618618p-5, 0x1.642c8590b2164p-5};
+    const double s = (m - 1.0) / (m + 1.0);
+    const double z = s * s;
+    double t = inv_odd[11];
+    for (int j = 10; j >= 0; --j) t = t * z + inv_odd[j];
+    return (double)e * 0x1.62e42fefa39efp-1 + (s + s) * t;
+}
+
+/* 1 / n!, n = 0 .. 19 */
+static const double syn_inv_fact[20] = {
+    1.0, 1.0, 0.5, 0x1.5555555555555p-3, 0x1.5555555555555p-5, 0x1.1111111111111p-7,
+    0x1.6c16c16c16c17p-10, 0x1.a01a01a01a01ap-13, 0x1.a01a01a01a01ap-16, 0x1.71de3a556c734p-19,
+    0x1.27e4fb7789f5cp-22, 0x1.ae64567f544e4p-26, 0x1.1eed8eff8d898p-29, 0x1.6124613a86d09p-33,
+    0x1.93974a8c07c9dp-37, 0x1.ae7f3e733b81fp-41, 0x1.ae7f3e733b81fp-45, 0x1.952c77030ad4ap-49,
+    0x1.6827863b97d97p-53, 0x1.2f49b46814157p-57};
+
+static double syn_exp(double x) {
+    const double k = rint(x * 0x1.71547652b82fep+0);
+    const double r = (x - k * 0x1.62e42feep-1) - k * 0x1.a39ef35793c76p-33;
+    double p = syn_inv_fact[16];
+    for (int n = 15; n >= 0; --n) p = p * r + syn_inv_fact[n];
+    const uint64_t tb = (uint64_t)((int)k + 1023) << 52;
+    double two_k;
+    memcpy(&two_k, &tb, 8);
+    return p * two_k;
+}
+
+static void syn_sincos_turns(double x, double* sn, double* cs) {
+    const double y = x - rint(x);
+    const int neg = y < 0.0;
+    double a = neg ? -y : y;
+    int flip_cos = 0, swap = 0;
+    if (a > 0.25) {
+        a = 0.5 - a;
+        flip_cos = 1;
+    }
+    if (a > 0.125) {
+        a = 0.25 - a;
+        swap = 1;
+    }
+    const double t = a * 0x1.921fb54442d18p+2;
+    const double z = t * t;
+    /* alternating signs: odd powers for sin, even for cos */
+    double ps = -syn_inv_fact[19];
+    for (int n = 17, sg = 1; n >= 1; n -= 2, sg = -sg) ps = ps * z + (sg > 0 ? syn_inv_fact[n] : -syn_inv_fact[n]);
+    const double s = t * ps;
+    double pc = -syn_inv_fact[18];
+    for (int n = 16, sg = 1; n >= 0; n -= 2, sg = -sg) pc = pc * z + (sg > 0 ? syn_inv_fact[n] : -syn_inv_fact[n]);
+    double s2 = swap ? pc : s, c2 = swap ? s : pc;
+    if (flip_cos) c2 = -c2;
+    if (neg) s2 = -s2;
+    *sn = s2;
+    *cs = c2;
+}
+
+static double syn_normal(uint64_t seed, uint64_t i) {
+    const uint64_t a = syn_mix64(seed ^ syn_mix64(i));
+    const uint64_t b = syn_mix64(a);
+    const double u1 = ((double)(a >> 12) + 0.5) * 0x1p-52;
+    const double u2 = ((double)(b >> 12) + 0.5) * 0x1p-52;
+    double s, c;
+    syn_sincos_turns(u2, &s, &c);
+    return sqrt(-2.0 * syn_log(u1)) * c;
+}
+
+static uint16_t syn_round16(double v, int bf16) {
+    const float f = (float)v;
+    if (!bf16) return orc_half_bits(f);
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    return (uint16_t)((x + 0x7fffu + ((x >> 16) & 1u)) >> 16); /* RNE; the inputs are finite */
+}
+
+typedef struct {
+    uint16_t* out;
+    size_t begin, end, stride;
+    uint64_t seed, heavy_cut;
+    double stddev, heavy_scale, ln_theta;
+    int bf16, rope, keys;
+} syn_job;
+
+static void* syn_worker(void* arg) {
+    const syn_job* j = (const syn_job*)arg;
+    if (!j->keys) {
+        for (size_t i = j->begin; i < j->end; ++i) j->out[i] = syn_round16(syn_normal(j->seed, i) * j->stddev, j->bf16);
+        return NULL;
+    }
+    for (size_t t = j->begin; t < j->end; ++t) {
+        const double scale = syn_mix64(j->seed * 0x2545f4914f6cdd1dull + t) < j->heavy_cut ? j->heavy_scale : 1.0;
+        uint16_t* row = j->out + t * j->stride;
+        for (size_t c2 = 0; c2 < 1024; c2 += 2) {
+            double a = syn_normal(j->seed, t * 1024 + c2) * scale;
+            double b = syn_normal(j->seed, t * 1024 + c2 + 1) * scale;
+            if (j->rope) {
+                const double pair = (double)((c2 & 127) >> 1);
+                const double inv_freq = syn_exp(-(pair * 0x1p-6) * j->ln_theta);
+                const double turns = ((double)t * inv_freq) * 0x1.45f306dc9c883p-3;
+                double s, c;
+                syn_sincos_turns(turns, &s, &c);
+                const double ra = a * c - b * s;
+                const double rb = a * s + b * c;
+                a = ra;
+                b = rb;
+            }
+            row[c2] = syn_round16(a, 0);
+            row[c2 + 1] = syn_round16(b, 0);
+        }
+    }
+    return NULL;
+}
+
+static void syn_run(syn_job base, size_t total, int threads) {
+    if (threads < 1) threads = 1;
+    if (threads > 128) threads = 128;
+    pthread_t tid[128];
+    syn_job jobs[128];
+    const size_t per = (total + (size_t)threads - 1) / (size_t)threads;
+    for (int i = 0; i < threads; ++i) {
+        jobs[i] = base;
+        jobs[i].begin = (size_t)i * per < total ? (size_t)i * per : total;
+        jobs[i].end = jobs[i].begin + per < total ? jobs[i].begin + per : total;
+        if (i == 0 || pthread_create(&tid[i], NULL, syn_worker, &jobs[i]) != 0) {
+            if (i) syn_worker(&jobs[i]);
+            tid[i] = 0;
+        }
+    }
+    syn_worker(&jobs[0]);
+    for (int i = 1; i < threads; ++i)
+        if (tid[i]) pthread_join(tid[i], NULL);
+}
+
+void orc_synth_normal(uint16_t* out, size_t count, uint64_t seed, float stddev, int bf16, int threads) {
+    syn_job j;
+    memset(&j, 0, sizeof j);
+    j.out = out;
+    j.seed = seed;
+    j.stddev = (double)stddev;
+    j.bf16 = bf16;
+    syn_run(j, count, threads);
+}
+
+void orc_synth_keys(uint16_t* rows, size_t tokens, size_t stride_words, uint64_t seed, float heavy_fraction,
+                    float heavy_scale, int rope, float theta, int threads) {
+    syn_job j;
+    memset(&j, 0, sizeof j);
+    j.out = rows;
+    j.stride = stride_words;
+    j.seed = seed;
+    j.heavy_cut = !(heavy_fraction > 0.0f) ? 0
+                  : heavy_fraction >= 1.0f ? ~0ull
+                                           : (uint64_t)((double)heavy_fraction * 18446744073709551616.0);
+    j.heavy_scale = (double)heavy_scale;
+    j.rope = rope;
+    j.ln_theta = rope ? syn_log((double)theta) : 0.0;
+    j.keys = 1;
+    syn_run(j, tokens, threads);
+}

@@ -154,6 +154,15 @@ int orc_kv_records_verify(const void* window, size_t window_bytes, const uint64_
                           uint32_t layer, size_t record_bytes, void* out, size_t out_stride,
                           const uint32_t* out_rows, size_t out_capacity, uint32_t* error_index);
 
+/* Synthetic benchmark inputs, restating the library's generator
+ * (hsb_synth_normal_f16/_bf16, hsb_synth_keys in include/hsb.h) bit for bit:
+ * splitmix64 counters, Box-Muller in double precision with series for ln,
+ * e^x and sin/cos of 2 pi x, RNE to F32 then F16 / BF16.  Keys: heavy rows
+ * by hash, NORM-mode RoPE by token position.  threads <= 128. */
+void orc_synth_normal(uint16_t* out, size_t count, uint64_t seed, float stddev, int bf16, int threads);
+void orc_synth_keys(uint16_t* rows, size_t tokens, size_t stride_words, uint64_t seed, float heavy_fraction,
+                    float heavy_scale, int rope, float theta, int threads);
+
 #ifdef __cplusplus
 }
 #endif
