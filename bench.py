@@ -68,8 +68,8 @@ def parse():
                          "the model-facing decode step (current-KV append + selection + attention over live slots) "
                          "beside the reference executor's padded upload")
     ap.add_argument("--batch", type=int, default=64)
-    ap.add_argument("--prefetch-mib", type=float, default=64.0,
-                    help="MiB of the next layer's keys each selected-KV layer pulls into L2 while it selects")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="kv-sharded: cross-GPU exchanges over peer memory (own kernels) or NCCL collectives")
     ap.add_argument("--h2o-keys", type=int, default=32768, help="h2o workload: keys N")
     ap.add_argument("--h2o-queries", default="1,16,512", help="h2o workload: comma-separated query counts")
     ap.add_argument("--records-layers", type=int, default=32, help="records workload: layers of the sequence")
@@ -185,26 +185,45 @@ class Model:
                                                self.counts[l].data_ptr(), self.results[l].data_ptr(),
                                                self.kp.data_ptr(), self.vp.data_ptr(), self.ws_layer.data_ptr(),
                                                self.ws_layer.numel()) for l in range(layers)]
+        # The pipelined schedule keeps two score / workspace sets: layer l + 1
+        # prepares into one while layer l selects from the other.
+        self.scores2 = [self.scores, torch.empty_like(self.scores)]
+        self.ws2 = [self.ws_layer, hsb._workspace(self.ws_layer.numel(), dev)]
+        self.pbuffers = [hsb._capi.LayerBuffers(self.scores2[l % 2].data_ptr(), self.ids[l].data_ptr(),
+                                                self.counts[l].data_ptr(), self.results[l].data_ptr(),
+                                                self.kp.data_ptr(), self.vp.data_ptr(), self.ws2[l % 2].data_ptr(),
+                                                self.ws2[l % 2].numel()) for l in range(layers)]
+        self.side = torch.cuda.Stream(priority=0)  # history scoring; selection runs on the caller's stream
+        self.ev_prep = [torch.cuda.Event() for _ in range(layers)]
+        self.ev_sel = [torch.cuda.Event() for _ in range(layers)]
         nsparse = layers - DENSE
         mk = lambda: torch.cuda.Event(enable_timing=True, external=True)  # noqa: E731
         self.ev = [[mk() for _ in range(5)] for _ in range(nsparse)]
         self.ev_layer = [[mk() for _ in range(2)] for _ in range(nsparse)]
         self.ev_dense = [[mk() for _ in range(2)] for _ in range(DENSE)]
         self.lib = lib
-        self.prefetch_bytes = 0  # bytes of the next layer's keys pulled into L2 during a selection
 
     def step(self, stream, mode: str = "timed"):
         """Launches one 32-layer decode step on `stream`.
 
-        timed:  selected-KV layers through hsb_layer_step (score -> select ->
-                fused gather + attention, three kernels), no event nodes;
-        layers: the same with events around each layer step (profiling);
+        timed:  the reference's early-rehearsal order (pipelined): layer l's
+                history is scored (hsb_layer_prepare, on a side stream) as
+                soon as layer l - 2's attention is done -- its selection
+                query comes from layer l - 1's input norm -- so it runs beside
+                layer l - 1's selection; layer l's select (hsb_layer_select:
+                current token, selection, gather, attention) follows its own
+                prepare and layer l - 1's attention, on `stream`;
+        serial: every selected-KV layer through hsb_layer_step (score ->
+                select + fused gather and attention) in layer order;
+        layers: serial with events around each layer step (profiling);
         stages: the four separate C-ABI calls with events between them
                 (profiling: per-stage attribution)."""
         lib, P = self.lib, self.hsb._ptr
         s = stream.cuda_stream
         n = self.n
-        events = mode != "timed"
+        if mode == "timed":
+            return self.step_pipelined(stream)
+        events = mode != "serial"
 
         def mark(e):
             if events:
@@ -219,14 +238,12 @@ class Model:
                 mark(e[1])
                 assert rc == 0, lib.hsb_last_error()
                 continue
-            if mode in ("timed", "layers"):
+            if mode in ("serial", "layers"):
                 e = self.ev_layer[l - DENSE]
                 mark(e[0])
-                # While layer l selects, layer l + 1's keys stream into L2.
-                nxt = self.prefetch_bytes if l + 1 < self.layers else 0
-                rc = lib.hsb_layer_step_prefetch(P(self.q16[l]), P(self.q32[l]), P(self.kc[l]), P(self.vc[l]), 1024,
-                                                 n, self.alpha, 0.2, self.count, ctypes.byref(self.buffers[l]),
-                                                 P(self.out[l]), P(self.kc[l + 1]) if nxt else None, nxt, s)
+                rc = lib.hsb_layer_step(P(self.q16[l]), P(self.q32[l]), P(self.kc[l]), P(self.vc[l]), 1024, n,
+                                        self.alpha, 0.2, self.count, ctypes.byref(self.buffers[l]),
+                                        P(self.out[l]), s)
                 mark(e[1])
                 assert rc == 0, lib.hsb_last_error()
                 continue
@@ -245,6 +262,35 @@ class Model:
                                            P(self.out[l]), P(self.ws_att), self.ws_att.numel(), s)
             mark(e[4])
             assert rc == 0, lib.hsb_last_error()
+
+    def step_pipelined(self, stream):
+        lib, P, torch = self.lib, self.hsb._ptr, self.torch
+        n, side = self.n, self.side
+        start = torch.cuda.Event()
+        start.record(stream)
+        side.wait_event(start)
+        for l in range(self.layers):
+            if l < DENSE:
+                rc = lib.hsb_attention_dense(P(self.q32[l]), P(self.kc[l]), P(self.vc[l]), n, 1024, P(self.out[l]),
+                                             P(self.ws_dense), self.ws_dense.numel(), stream.cuda_stream)
+                assert rc == 0, lib.hsb_last_error()
+                self.ev_sel[l].record(stream)
+                continue
+            # history of layer l: its query exists once layer l - 2 has attended
+            side.wait_event(self.ev_sel[l - 2])
+            rc = lib.hsb_layer_prepare(P(self.q16[l]), P(self.kc[l]), 1024, n, self.alpha, 0.2, self.count,
+                                       ctypes.byref(self.pbuffers[l]), side.cuda_stream)
+            assert rc == 0, lib.hsb_last_error()
+            self.ev_prep[l].record(side)
+            stream.wait_event(self.ev_prep[l])
+            rc = lib.hsb_layer_select(P(self.q16[l]), P(self.q32[l]), P(self.kc[l]), P(self.vc[l]), 1024, n,
+                                      self.alpha, 0.2, self.count, ctypes.byref(self.pbuffers[l]), P(self.out[l]),
+                                      stream.cuda_stream)
+            assert rc == 0, lib.hsb_last_error()
+            self.ev_sel[l].record(stream)
+        done = torch.cuda.Event()
+        done.record(side)
+        stream.wait_event(done)
 
     def stage_ms(self):
         """Per-stage durations (ms) of the last replay, averaged over layers."""
@@ -294,18 +340,18 @@ def run_ours(args, rank, world, torch, dist):
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
     dev_index = torch.cuda.current_device()
     m = Model(hsb, torch, args.tokens, args.layers, args.alpha, seed=rank)
-    m.prefetch_bytes = min(int(args.prefetch_mib * (1 << 20)), 2048 * args.tokens) // 16 * 16
-    stream = torch.cuda.Stream()
+    stream = torch.cuda.Stream(priority=-1)  # selection (the critical path) before history scoring
     torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        m.step(stream)  # eager run: sets kernel attributes before capture
-    stream.synchronize()
-    with torch.cuda.stream(stream):
-        m.step(stream, "stages")  # eager: the separate-call path's attributes too
-    stream.synchronize()
+    for mode in ("timed", "serial", "stages"):  # eager runs set kernel attributes before capture
+        with torch.cuda.stream(stream):
+            m.step(stream, mode)
+        torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         m.step(stream)
+    serial_graph = torch.cuda.CUDAGraph()  # every layer through hsb_layer_step, in order
+    with torch.cuda.graph(serial_graph, stream=stream):
+        m.step(stream, "serial")
     prof_graph = torch.cuda.CUDAGraph()  # separate C-ABI calls with per-stage events
     with torch.cuda.graph(prof_graph, stream=stream):
         m.step(stream, "stages")
@@ -331,6 +377,16 @@ def run_ours(args, rank, world, torch, dist):
     if dist:
         dist.barrier()
     ms = start.elapsed_time(stop)
+    # The serial schedule, for comparison (same work, no overlap between layers).
+    for _ in range(3):
+        serial_graph.replay()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(args.steps):
+            serial_graph.replay()
+        stop.record(stream)
+    stop.synchronize()
+    serial_ms = start.elapsed_time(stop) / args.steps
     # Per-stage breakdown from a separate replay whose graph carries events
     # (event nodes add their own gaps, so the sum exceeds ms_per_step).
     with torch.cuda.stream(stream):
@@ -390,7 +446,11 @@ def run_ours(args, rank, world, torch, dist):
         "config": workload_config(args),
         "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
         "launch": "one CUDA graph per 32-layer step",
-        "l2_prefetch_next_layer_bytes": m.prefetch_bytes,
+        "schedule": "early rehearsal (patches/llama-b6000-early-rehearsal.patch:46-52): layer l's history is "
+                    "scored (hsb_layer_prepare) once layer l-2 has attended, beside layer l-1's selection; layer l's "
+                    "select (current token, selection, gather, attention: hsb_layer_select) follows its prepare and "
+                    "layer l-1's attention",
+        "serial_schedule_ms_per_step": round(serial_ms, 4),
         "score_select_gather": {"bytes_per_layer": round(b_ssg), "us_per_layer": round(per_layer_ms * 1e3, 2),
                                 "GB_s": round(graded_gbs, 1), "frac_of_peak": round(graded_gbs / peak, 4),
                                 "peak_GB_s": peak, "peak_kind": peak_kind,
@@ -422,6 +482,7 @@ def run_ours(args, rank, world, torch, dist):
         if parity is not None:
             line["parity"] = parity
     graph.reset()
+    serial_graph.reset()
     prof_graph.reset()
     layer_graph.reset()
     return line
@@ -662,9 +723,11 @@ def run_reference(args, rank, world, torch):
 
 def run_sharded(args, rank, world, torch, dist):
     """--batch independent sequences of N tokens, one selected-KV
-    layer, KV heads split over the ranks (G = 8 / world per rank), with the
-    threshold broadcast, count-record and output all-gathers over NCCL.  The
-    whole step (kernels and collectives) is captured in one CUDA graph."""
+    layer, KV heads split over the ranks (G = 8 / world per rank).  The
+    exchanges -- thresholds from rank 0, every head's count records, the
+    attention outputs -- go over NVLink peer memory through the library's
+    own kernels (--exchange peer, the default) or through NCCL collectives
+    (--exchange nccl).  The whole step is captured in one CUDA graph."""
     import hillserve_b200 as hsb
     from hillserve_b200 import sharded as sh
 
@@ -677,24 +740,33 @@ def run_sharded(args, rank, world, torch, dist):
     vshard = torch.empty_like(kshard)
     rows = torch.empty((n, 8, 128), dtype=torch.int16, device="cuda")
     for b in range(batch):  # the same sequences on every rank; each keeps its own heads
-        lib.hsb_synth_normal_f16(q16[b].data_ptr(), 4096, 9000 + 7 * b, 1.0, s)
-        lib.hsb_synth_keys(rows.data_ptr(), n, 1024, 9001 + 7 * b, 0.02, 4.0, 1, THETA, s)
+        sq, sk, sv = layer_seeds(9, b)
+        lib.hsb_synth_normal_f16(q16[b].data_ptr(), 4096, sq, 1.0, s)
+        lib.hsb_synth_keys(rows.data_ptr(), n, 1024, sk, 0.02, 4.0, 1, THETA, s)
         kshard[b].copy_(rows[:, g * rank:g * (rank + 1), :])
-        lib.hsb_synth_keys(rows.data_ptr(), n, 1024, 9002 + 7 * b, 0.0, 1.0, 0, THETA, s)
+        lib.hsb_synth_keys(rows.data_ptr(), n, 1024, sv, 0.0, 1.0, 0, THETA, s)
         vshard[b].copy_(rows[:, g * rank:g * (rank + 1), :])
     del rows
     q32 = q16.view(torch.float16).float()
     q16l, q32l = sh.shard_queries(q16, world, rank), sh.shard_queries(q32, world, rank)
     layer = sh.KVHeadShardedLayer(n, batch, world, rank, alpha=args.alpha)
+    peer = args.exchange == "peer"
+    ex = sh.PeerExchange(batch, world, rank) if peer else None
+
+    def step():
+        if peer:
+            return layer.step_peer(q16l, q32l, kshard, vshard, ex)
+        return layer.step(q16l, q32l, kshard, vshard)
+
     stream = torch.cuda.Stream()
     holder = {}
     with torch.cuda.stream(stream):
         for _ in range(2):
-            holder["out"], holder["res"] = layer.step(q16l, q32l, kshard, vshard)
+            holder["out"], holder["res"] = step()
     stream.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
-        holder["out"], holder["res"] = layer.step(q16l, q32l, kshard, vshard)
+        holder["out"], holder["res"] = step()
     for _ in range(max(args.warmup, 3)):
         graph.replay()
     torch.cuda.synchronize()
@@ -713,7 +785,12 @@ def run_sharded(args, rank, world, torch, dist):
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     res = holder["res"].cpu().numpy()
+    exch_status = ex.status.cpu().numpy().tolist() if peer else None
     graph.reset()
+    torch.cuda.synchronize()
+    dist.barrier()  # every rank is done with the peers' mailboxes
+    if peer:
+        ex.close()
     b_layer = 2048 * n + 8192 + 64 * n  # per sequence: K read by the scorer, Q, scores + keys
     return {"metric": "KV-head-sharded selected-KV layer: sequence-layer-steps/s at N=32K",
             "value": round(batch * args.steps / (ms / 1e3), 1), "unit": "sequence-layer-steps/s",
@@ -723,8 +800,12 @@ def run_sharded(args, rank, world, torch, dist):
             "config": {"workload": "configs[4]: one selected-KV layer, KV heads sharded over the GPUs",
                        "sequences": batch, "tokens": n, "alpha": args.alpha, "cap_ratio": 0.2,
                        "kv_heads_per_gpu": g, "parallelism": f"KV-head shards x{world}",
-                       "exchange": "NCCL broadcast of thresholds, all-gather of count records and outputs",
-                       "launch": "one CUDA graph per step (kernels and collectives)"},
+                       "exchange": ("peer memory: the library's kernels store thresholds, count records and "
+                                    "outputs into every rank's mailbox (CUDA IPC) with bounded flag waits"
+                                    if peer else "NCCL broadcast of thresholds, all-gather of count records and "
+                                                 "outputs"),
+                       "launch": "one CUDA graph per step"},
+            "exchange_status": exch_status,
             "score_bytes_per_step": b_layer * batch, "selection": {"k_mean": float(res[:, 0].mean()),
                                                                  "zero_selection": int((res[:, 0] == 0).sum())},
             "clocks": clocks.summary()}
@@ -1351,6 +1432,9 @@ def run_executor(args, torch):
 
 def main():
     args = parse()
+    # NCCL prints its version banner on stdout at INFO/VERSION levels; the
+    # JSON line must be the only stdout line of rank 0.
+    os.environ.setdefault("NCCL_DEBUG", "WARN")
     import torch
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -814,20 +814,25 @@ class SelectedKVLayer:
                                      self.result.data_ptr(), self.k_packed.data_ptr(), self.v_packed.data_ptr(),
                                      self.workspace.data_ptr(), self.workspace.numel())
 
-    def __call__(self, q16, q32, kcache, vcache, stride_words: int = 1024, out=None, stream=None, prefetch=None,
-                 prefetch_bytes: int = 0):
-        """prefetch / prefetch_bytes: a range (the next layer's keys) to pull
-        into L2 while the selection runs (hsb_layer_step_prefetch)."""
+    def __call__(self, q16, q32, kcache, vcache, stride_words: int = 1024, out=None, stream=None):
         out = self.out if out is None else out
-        if prefetch is not None and prefetch_bytes:
-            _raise(lib().hsb_layer_step_prefetch(_ptr(q16), _ptr(q32), _ptr(kcache), _ptr(vcache), stride_words,
-                                                 self.valid, C.c_float(self.alpha), C.c_float(self.ratio),
-                                                 self.count, C.byref(self._buffers), _ptr(out), _ptr(prefetch),
-                                                 int(prefetch_bytes), _stream(stream)))
-            return out
         _raise(lib().hsb_layer_step(_ptr(q16), _ptr(q32), _ptr(kcache), _ptr(vcache), stride_words, self.valid,
                                     C.c_float(self.alpha), C.c_float(self.ratio), self.count, C.byref(self._buffers),
                                     _ptr(out), _stream(stream)))
+        return out
+
+    def prepare(self, q16, kcache, stride_words: int = 1024, stream=None):
+        """The history half (hsb_layer_prepare): scores positions [0, valid - 1)."""
+        _raise(lib().hsb_layer_prepare(_ptr(q16), _ptr(kcache), stride_words, self.valid, C.c_float(self.alpha),
+                                       C.c_float(self.ratio), self.count, C.byref(self._buffers), _stream(stream)))
+
+    def select(self, q16, q32, kcache, vcache, stride_words: int = 1024, out=None, stream=None):
+        """The select half (hsb_layer_select): scores the current position
+        valid - 1, then selects, gathers and attends."""
+        out = self.out if out is None else out
+        _raise(lib().hsb_layer_select(_ptr(q16), _ptr(q32), _ptr(kcache), _ptr(vcache), stride_words, self.valid,
+                                      C.c_float(self.alpha), C.c_float(self.ratio), self.count,
+                                      C.byref(self._buffers), _ptr(out), _stream(stream)))
         return out
 
     def selection(self, stream=None) -> Selection:

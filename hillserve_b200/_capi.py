@@ -27,6 +27,15 @@ class DeviceStatus(C.Structure):
     _fields_ = [("code", C.c_int32), ("index", C.c_int32)]
 
 
+class MailboxLayout(C.Structure):
+    _fields_ = [("thr", SZ), ("records", SZ), ("outputs", SZ), ("results", SZ), ("status", SZ), ("bytes", SZ)]
+
+
+class PeerGroup(C.Structure):
+    _fields_ = [("world", C.c_int), ("rank", C.c_int), ("mailbox", P * 8), ("batch", SZ),
+                ("wait_limit_ns", C.c_uint64)]
+
+
 class Selection(C.Structure):
     _fields_ = [("k", C.c_uint32), ("boundary_tied_heads", C.c_uint32), ("status", DeviceStatus)]
 
@@ -69,13 +78,23 @@ _SIGNATURES = {
     "hsb_rehearsal_query": (I, [P, P, U64, F, P, P, P]),
     "hsb_layer_workspace_bytes": (SZ, [SZ, SZ]),
     "hsb_layer_step": (I, [P, P, P, P, SZ, SZ, F, F, SZ, P, P, P]),
-    "hsb_layer_step_prefetch": (I, [P, P, P, P, SZ, SZ, F, F, SZ, P, P, P, SZ, P]),
+    "hsb_layer_prepare": (I, [P, P, SZ, SZ, F, F, SZ, P, P]),
+    "hsb_layer_select": (I, [P, P, P, P, SZ, SZ, F, F, SZ, P, P, P]),
     "hsb_shard_head0_words": (SZ, []),
     "hsb_shard_score": (I, [P, I, P, SZ, SZ, P, P, P, P]),
     "hsb_shard_threshold": (I, [P, SZ, F, P, P]),
     "hsb_shard_count": (I, [P, SZ, SZ, SZ, P, P, P]),
     "hsb_shard_select_workspace_bytes": (SZ, [I, SZ, SZ, SZ]),
     "hsb_shard_select": (I, [P, P, I, SZ, SZ, P, P, SZ, SZ, F, F, P, SZ, P, P, P, P, P, P, P, P, P, SZ, P]),
+    "hsb_mailbox_bytes": (SZ, [SZ]),
+    "hsb_mailbox_layout_of": (None, [SZ, P]),
+    "hsb_mailbox_create": (I, [SZ, P, P]),
+    "hsb_mailbox_destroy": (I, [P]),
+    "hsb_mailbox_open": (I, [P, P]),
+    "hsb_mailbox_close": (I, [P]),
+    "hsb_exchange_threshold": (I, [P, F, P, P]),
+    "hsb_exchange_count": (I, [P, SZ, SZ, P, P]),
+    "hsb_exchange_finish": (I, [P, P, SZ, P, P]),
     "hsb_h2o_group_sums": (I, [P, P, P, SZ, SZ, P, SZ, P, P]),
     "hsb_segment_extent_bytes": (U64, [SZ, U64, SZ]),
     "hsb_segment_header": (I, [P, U64, SZ, U64, SZ]),

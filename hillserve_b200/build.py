@@ -25,7 +25,7 @@ LIB = LIBDIR / "libhsb.so"
 COMPAT = PKG / "compat"
 COMPAT_LIB = LIBDIR / "libhsb_compat.so"
 CUDA_LIB = "/usr/local/cuda/lib64"
-SOURCES = ["score.cu", "select.cu", "pack.cu", "attention.cu", "rehearsal.cu", "capi.cu", "noalloc.cu", "h2o.cu", "records.cu", "history.cu", "executor.cu", "synth.cu"]
+SOURCES = ["score.cu", "select.cu", "pack.cu", "attention.cu", "rehearsal.cu", "capi.cu", "noalloc.cu", "h2o.cu", "records.cu", "history.cu", "executor.cu", "synth.cu", "exchange.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

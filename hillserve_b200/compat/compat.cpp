@@ -374,42 +374,85 @@ void pack_gqa_workspace(const std::vector<std::vector<std::uint64_t>>& ids, cons
 }
 
 // ------------------------------------------------------------ prefetch
+namespace {
+// Makes `device` current for one scope and restores the caller's device.
+struct DeviceScope {
+    int previous = 0;
+    bool restore = false;
+    explicit DeviceScope(int device) {
+        cuda_check(cudaGetDevice(&previous), "get CUDA device");
+        restore = previous != device;
+        if (restore) cuda_check(cudaSetDevice(device), "set CUDA device");
+    }
+    ~DeviceScope() {
+        if (restore) cudaSetDevice(previous);
+    }
+};
+// Pinned host memory (page-locked, so copies run asynchronously).
+struct PinnedBuffer {
+    unsigned char* ptr = nullptr;
+    explicit PinnedBuffer(std::size_t bytes) {
+        cuda_check(cudaMallocHost(reinterpret_cast<void**>(&ptr), std::max<std::size_t>(bytes, 256)),
+                   "pinned host allocation");
+    }
+    ~PinnedBuffer() {
+        if (ptr) cudaFreeHost(ptr);
+    }
+    PinnedBuffer(const PinnedBuffer&) = delete;
+    PinnedBuffer& operator=(const PinnedBuffer&) = delete;
+};
+struct Event {
+    cudaEvent_t e = nullptr;
+    explicit Event(unsigned flags = cudaEventDefault) {
+        cuda_check(cudaEventCreateWithFlags(&e, flags), "event");
+    }
+    ~Event() {
+        if (e) cudaEventDestroy(e);
+    }
+    Event(const Event&) = delete;
+    Event& operator=(const Event&) = delete;
+};
+// A borrowed stream that may still run work of ours: drained before the
+// buffers that work uses are released.
+struct BorrowedStream {
+    cudaStream_t stream = nullptr;
+    void hold(cudaStream_t s) { stream = s; }
+    void release() { stream = nullptr; }
+    void drain() noexcept {
+        if (stream && cudaStreamSynchronize(stream) == cudaSuccess) stream = nullptr;
+    }
+};
+}  // namespace
+
+// Members are declared so that destruction runs streams and the borrowed
+// consumer first (each drains its work) and frees memory last.
 struct GQAPrefetchCuda::Impl {
     int device = 0;
-    std::size_t rows = 0, bytes = 0;
-    struct Slot {
-        void* host = nullptr;
-        void* gpu = nullptr;
-        cudaStream_t stream = nullptr;
-        cudaEvent_t start = nullptr, ready = nullptr;
-        std::size_t valid = 0;
+    std::size_t rows = 0, slot_bytes = 0;
+    // Both slots' rows: one HBM region and one pinned region, slot s at s * slot_bytes.
+    DeviceBuffer staged;
+    std::unique_ptr<PinnedBuffer> pinned;
+    // A delivery's inputs travel in one copy: [status word | map | miss rows]
+    // (the pinned arena starts with a zero status word); the status comes
+    // back into the last 8 bytes of the pinned arena.
+    std::size_t map_off = 256, miss_off = 0, arena_bytes = 0;
+    DeviceBuffer arena;
+    std::unique_ptr<PinnedBuffer> arena_host;
+    std::unique_ptr<Event> delivered;
+    struct Queue {
+        std::unique_ptr<Stream> stream;
+        std::unique_ptr<Event> start, ready;
+        std::size_t rows = 0;
     };
-    Slot slots[2];
-    void* misses = nullptr;
-    std::int32_t* map = nullptr;
-    hsb_device_status* status = nullptr;
-    cudaEvent_t delivery = nullptr;
-    cudaStream_t consume_stream = nullptr;
-    bool consume_pending = false;
+    Queue queue[2];
+    BorrowedStream consumer;
     ~Impl() {
-        // Drain everything that may still read a slot before freeing it;
-        // cleanup never throws (runtime/gqa_prefetch_cuda.cu:31-41).
-        cudaSetDevice(device);
-        if (consume_pending && consume_stream) cudaStreamSynchronize(consume_stream);
-        if (delivery) cudaEventSynchronize(delivery);
-        for (auto& s : slots)
-            if (s.stream) cudaStreamSynchronize(s.stream);
-        for (auto& s : slots) {
-            if (s.start) cudaEventDestroy(s.start);
-            if (s.ready) cudaEventDestroy(s.ready);
-            if (s.gpu) cudaFree(s.gpu);
-            if (s.host) cudaFreeHost(s.host);
-            if (s.stream) cudaStreamDestroy(s.stream);
+        try {
+            DeviceScope scope(device);
+            consumer.drain();
+            for (auto& q : queue) q.stream.reset();  // synchronises the slot's upload
+        } catch (...) {
         }
-        if (misses) cudaFree(misses);
-        if (map) cudaFree(map);
-        if (status) cudaFree(status);
-        if (delivery) cudaEventDestroy(delivery);
     }
 };
 
@@ -420,49 +463,52 @@ GQAPrefetchCuda::GQAPrefetchCuda(void* pointer, std::size_t max_rows) : impl_(ne
     if (a.type != cudaMemoryTypeDevice) throw std::runtime_error("prefetch target must be CUDA device memory");
     p.device = a.device;
     p.rows = max_rows;
-    p.bytes = max_rows * 4096;
-    cuda_check(cudaSetDevice(p.device), "prefetch set device");
-    for (auto& s : p.slots) {
-        cuda_check(cudaMalloc(&s.gpu, std::max<std::size_t>(p.bytes, 256)), "prefetch slot allocation");
-        cuda_check(cudaMallocHost(&s.host, std::max<std::size_t>(p.bytes, 256)), "prefetch pinned slot allocation");
-        cuda_check(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking), "prefetch private stream");
-        cuda_check(cudaEventCreate(&s.start), "prefetch start event");
-        cuda_check(cudaEventCreate(&s.ready), "prefetch ready event");
+    p.slot_bytes = max_rows * 4096;
+    DeviceScope scope(p.device);
+    p.staged.reserve(2 * p.slot_bytes);
+    p.pinned.reset(new PinnedBuffer(2 * p.slot_bytes));
+    p.miss_off = p.map_off + (max_rows * 32 * 4 + 255) / 256 * 256;
+    p.arena_bytes = p.miss_off + p.slot_bytes;
+    p.arena.reserve(p.arena_bytes);
+    p.arena_host.reset(new PinnedBuffer(p.arena_bytes + 8));
+    std::memset(p.arena_host->ptr, 0, p.map_off);
+    p.delivered.reset(new Event(cudaEventDisableTiming));
+    for (auto& q : p.queue) {
+        q.stream.reset(new Stream);
+        q.start.reset(new Event);
+        q.ready.reset(new Event);
     }
-    cuda_check(cudaMalloc(&p.misses, std::max<std::size_t>(p.bytes, 256)), "prefetch miss allocation");
-    cuda_check(cudaMalloc(reinterpret_cast<void**>(&p.map), std::max<std::size_t>(max_rows * 32 * 4, 256)),
-               "prefetch map allocation");
-    cuda_check(cudaMalloc(reinterpret_cast<void**>(&p.status), sizeof(hsb_device_status)), "prefetch status");
-    cuda_check(cudaEventCreateWithFlags(&p.delivery, cudaEventDisableTiming), "prefetch delivery event");
 }
 GQAPrefetchCuda::~GQAPrefetchCuda() = default;
-std::size_t GQAPrefetchCuda::gpu_bytes() const { return impl_->bytes * 3 + impl_->rows * 32 * 4; }
-std::size_t GQAPrefetchCuda::host_bytes() const { return impl_->bytes * 2; }
+std::size_t GQAPrefetchCuda::gpu_bytes() const { return impl_->slot_bytes * 3 + impl_->rows * 32 * 4; }
+std::size_t GQAPrefetchCuda::host_bytes() const { return impl_->slot_bytes * 2; }
 
 GQAPrefetchCuda::Upload GQAPrefetchCuda::stage(unsigned slot, const std::vector<std::uint8_t>& payload) {
     auto& p = *impl_;
-    if (slot >= 2 || payload.size() > p.bytes || payload.size() % 4096)
+    if (slot >= 2 || payload.size() > p.slot_bytes || payload.size() % 4096)
         throw std::runtime_error("prefetch CUDA slot geometry");
-    auto& s = p.slots[slot];
-    cuda_check(cudaSetDevice(p.device), "prefetch worker device");
+    DeviceScope scope(p.device);
+    auto& q = p.queue[slot];
+    unsigned char* host = p.pinned->ptr + slot * p.slot_bytes;
+    unsigned char* dev = p.staged.as<unsigned char>() + slot * p.slot_bytes;
+    if (!payload.empty()) std::memcpy(host, payload.data(), payload.size());
     Upload out;
-    if (!payload.empty()) std::memcpy(s.host, payload.data(), payload.size());
     out.started_ns = now_ns();
     out.bytes = payload.size();
-    s.valid = payload.size() / 4096;
+    q.rows = payload.size() / 4096;
+    const cudaStream_t s = q.stream->s;
     try {
-        cuda_check(cudaEventRecord(s.start, s.stream), "prefetch upload start");
-        if (!payload.empty())
-            cuda_check(cudaMemcpyAsync(s.gpu, s.host, payload.size(), cudaMemcpyHostToDevice, s.stream), "prefetch H2D");
-        cuda_check(cudaEventRecord(s.ready, s.stream), "prefetch ready record");
-        cuda_check(cudaEventSynchronize(s.ready), "prefetch upload completion");
-        out.ready_observed_ns = now_ns();
-        cuda_check(cudaEventElapsedTime(&out.device_ms, s.start, s.ready), "prefetch upload interval");
-        return out;
+        cuda_check(cudaEventRecord(q.start->e, s), "prefetch upload start");
+        h2d(dev, host, payload.size(), s);
+        cuda_check(cudaEventRecord(q.ready->e, s), "prefetch ready record");
+        cuda_check(cudaEventSynchronize(q.ready->e), "prefetch upload completion");
     } catch (...) {
-        cudaStreamSynchronize(s.stream);  // never release the pinned source mid-copy
+        cudaStreamSynchronize(s);  // the pinned rows stay in use until the copy is over
         throw;
     }
+    out.ready_observed_ns = now_ns();
+    cuda_check(cudaEventElapsedTime(&out.device_ms, q.start->e, q.ready->e), "prefetch upload interval");
+    return out;
 }
 
 GQAPrefetchCuda::Delivery GQAPrefetchCuda::deliver(unsigned slot, const std::vector<std::int32_t>& rows,
@@ -470,56 +516,54 @@ GQAPrefetchCuda::Delivery GQAPrefetchCuda::deliver(unsigned slot, const std::vec
                                                    std::size_t mask_elements, std::size_t count, void* k, void* v,
                                                    void* gpu_mask, void* raw_stream) {
     auto& p = *impl_;
-    // runtime/gqa_prefetch_cuda.cu:217-218
-    if (slot >= 2 || !raw_stream || count > p.rows || rows.size() != count * 32 || misses.size() > p.bytes ||
+    // runtime/gqa_prefetch_cuda.cu:217-218: geometry, then every map entry.
+    if (slot >= 2 || !raw_stream || count > p.rows || rows.size() != count * 32 || misses.size() > p.slot_bytes ||
         misses.size() % 4096)
         throw std::runtime_error("prefetch CUDA delivery geometry/stream");
-    auto& s = p.slots[slot];
-    std::size_t valid_pairs = 0;
-    for (auto row : rows) {
-        if (row >= 0 && std::size_t(row) >= s.valid) throw std::runtime_error("prefetch row outside uploaded payload");
-        if (row <= -2 && std::size_t(-2 - static_cast<long long>(row)) >= misses.size() / 4096)
+    const std::size_t staged_rows = p.queue[slot].rows, miss_rows = misses.size() / 4096;
+    std::size_t live = 0;
+    for (const std::int32_t r : rows) {
+        if (r >= 0 && static_cast<std::size_t>(r) >= staged_rows)
+            throw std::runtime_error("prefetch row outside uploaded payload");
+        if (r <= -2 && static_cast<std::size_t>(-2 - static_cast<long long>(r)) >= miss_rows)
             throw std::runtime_error("prefetch miss row outside payload");
-        if (row != -1) ++valid_pairs;
+        live += r != -1;
     }
-    cuda_check(cudaSetDevice(p.device), "prefetch consumer device");
+    DeviceScope scope(p.device);
     const auto stream = static_cast<cudaStream_t>(raw_stream);
+    unsigned char* host = p.arena_host->ptr;
+    unsigned char* dev = p.arena.as<unsigned char>();
+    std::memcpy(host + p.map_off, rows.data(), rows.size() * 4);
+    if (!misses.empty()) std::memcpy(host + p.miss_off, misses.data(), misses.size());
+    const std::size_t copy_bytes = misses.empty() ? p.map_off + rows.size() * 4 : p.miss_off + misses.size();
+    auto* status = reinterpret_cast<hsb_device_status*>(dev);
+    auto* status_back = reinterpret_cast<hsb_device_status*>(host + p.arena_bytes);
     Delivery out;
     out.started_ns = now_ns();
-    p.consume_stream = stream;
-    p.consume_pending = true;
+    p.consumer.hold(stream);
     try {
-        cuda_check(cudaStreamWaitEvent(stream, s.ready, 0), "attention stream waits for prefetched payload");
-        if (!misses.empty())
-            cuda_check(cudaMemcpyAsync(p.misses, misses.data(), misses.size(), cudaMemcpyHostToDevice, stream),
-                       "prefetch miss H2D");
-        cuda_check(cudaMemcpyAsync(p.map, rows.data(), rows.size() * 4, cudaMemcpyHostToDevice, stream),
-                   "prefetch gather map H2D");
-        if (mask_elements)
-            cuda_check(cudaMemcpyAsync(gpu_mask, mask, mask_elements * 4, cudaMemcpyHostToDevice, stream),
-                       "prefetch attention mask H2D");
-        cuda_check(cudaMemsetAsync(p.status, 0, sizeof(hsb_device_status), stream), "status reset");
-        hsb_check(hsb_gather_map(static_cast<const std::uint16_t*>(s.gpu), s.valid,
-                                 static_cast<const std::uint16_t*>(p.misses), misses.size() / 4096, p.map, count,
-                                 static_cast<std::uint16_t*>(k), static_cast<std::uint16_t*>(v), p.status, stream));
-        cuda_check(cudaEventRecord(p.delivery, stream), "prefetch delivery completion record");
+        cuda_check(cudaStreamWaitEvent(stream, p.queue[slot].ready->e, 0), "attention stream waits for prefetched payload");
+        h2d(dev, host, copy_bytes, stream);  // zero status, map, miss rows
+        if (mask_elements) h2d(gpu_mask, mask, mask_elements * 4, stream);
+        hsb_check(hsb_gather_map(p.staged.as<std::uint16_t>() + slot * p.slot_bytes / 2, staged_rows,
+                                 reinterpret_cast<const std::uint16_t*>(dev + p.miss_off), miss_rows,
+                                 reinterpret_cast<const std::int32_t*>(dev + p.map_off), count,
+                                 static_cast<std::uint16_t*>(k), static_cast<std::uint16_t*>(v), status, stream));
+        d2h(status_back, status, sizeof(hsb_device_status), stream);
+        cuda_check(cudaEventRecord(p.delivered->e, stream), "prefetch delivery completion record");
         const auto wait = Clock::now();
-        cuda_check(cudaEventSynchronize(p.delivery), "prefetch delivery completion");
-        hsb_check(hsb_status_check(p.status, stream));
+        cuda_check(cudaEventSynchronize(p.delivered->e), "prefetch delivery completion");
         out.wait_ms = std::chrono::duration<double, std::milli>(Clock::now() - wait).count();
-        out.ready_observed_ns = now_ns();
-        out.h2d_bytes = misses.size() + rows.size() * 4 + mask_elements * 4;
-        out.d2d_bytes = valid_pairs * 128 * 4;
-        p.consume_pending = false;
-        p.consume_stream = nullptr;
-        return out;
     } catch (...) {
-        if (cudaStreamSynchronize(stream) == cudaSuccess) {
-            p.consume_pending = false;
-            p.consume_stream = nullptr;
-        }
+        p.consumer.drain();
         throw;
     }
+    p.consumer.release();
+    if (status_back->code != HSB_OK) throw_status(status_back->code);
+    out.ready_observed_ns = now_ns();
+    out.h2d_bytes = misses.size() + rows.size() * 4 + mask_elements * 4;
+    out.d2d_bytes = live * 128 * 4;
+    return out;
 }
 
 // ------------------------------------------------------------ delivery
@@ -615,42 +659,26 @@ std::string GQADeliveryWorkspace::verify_and_consume() {
 }
 
 // ------------------------------------------------------- H2O statistics
-// runtime/gqa_h2o_stats.cu:60-173 over hsb_h2o_group_sums.
+// The interface of runtime/gqa_h2o_stats.hpp over hsb_h2o_group_sums: the
+// reduction and the copy of the sums to pinned memory run on the caller's
+// attention stream, bracketed by three timing events.
 struct GQAH2OStatsCuda::Impl {
     int device = 0;
     std::size_t keys = 0, bytes = 0;
-    float* gpu = nullptr;
-    float* host = nullptr;
-    cudaEvent_t begin = nullptr, reduced = nullptr, copied = nullptr;
-    cudaStream_t pending_stream = nullptr;
-    bool pending = false;
+    DeviceBuffer sums;
+    std::unique_ptr<PinnedBuffer> host;
+    std::unique_ptr<Event> begin, reduced, copied;
+    BorrowedStream consumer;
     ~Impl() {
-        // Never throws; a submission that failed before its completion event
-        // may still use the buffers on the borrowed stream, so drain it first.
-        int previous = 0;
-        const bool restore = cudaGetDevice(&previous) == cudaSuccess;
-        cudaSetDevice(device);
-        if (pending && pending_stream) cudaStreamSynchronize(pending_stream);
-        if (begin) cudaEventDestroy(begin);
-        if (reduced) cudaEventDestroy(reduced);
-        if (copied) cudaEventDestroy(copied);
-        if (gpu) cudaFree(gpu);
-        if (host) cudaFreeHost(host);
-        if (restore) cudaSetDevice(previous);
+        // Never throws; a reduction that failed before its completion event
+        // may still use the buffers on the borrowed stream: drain it first.
+        try {
+            DeviceScope scope(device);
+            consumer.drain();
+        } catch (...) {
+        }
     }
 };
-
-namespace {
-// Makes `device` current for one scope and restores the caller's device.
-struct DeviceScope {
-    int previous = 0;
-    explicit DeviceScope(int device) {
-        cuda_check(cudaGetDevice(&previous), "H2O get CUDA device");
-        if (previous != device) cuda_check(cudaSetDevice(device), "H2O set CUDA device");
-    }
-    ~DeviceScope() { cudaSetDevice(previous); }
-};
-}  // namespace
 
 GQAH2OStatsCuda::GQAH2OStatsCuda(const void* reference, std::size_t capacity) : impl_(new Impl) {
     if (!reference || !capacity) throw std::runtime_error("H2O statistics needs CUDA pointer and nonzero capacity");
@@ -664,11 +692,11 @@ GQAH2OStatsCuda::GQAH2OStatsCuda(const void* reference, std::size_t capacity) : 
     if (a.type != cudaMemoryTypeDevice) throw std::runtime_error("H2O attention statistics requires CUDA device memory");
     p.device = a.device;
     DeviceScope scope(p.device);
-    cuda_check(cudaMalloc(reinterpret_cast<void**>(&p.gpu), p.bytes), "H2O reduction allocation");
-    cuda_check(cudaMallocHost(reinterpret_cast<void**>(&p.host), p.bytes), "H2O pinned sums allocation");
-    cuda_check(cudaEventCreate(&p.begin), "H2O begin event");
-    cuda_check(cudaEventCreate(&p.reduced), "H2O reduction event");
-    cuda_check(cudaEventCreate(&p.copied), "H2O D2H completion event");
+    p.sums.reserve(p.bytes);
+    p.host.reset(new PinnedBuffer(p.bytes));
+    p.begin.reset(new Event);
+    p.reduced.reset(new Event);
+    p.copied.reset(new Event);
 }
 GQAH2OStatsCuda::~GQAH2OStatsCuda() = default;
 std::size_t GQAH2OStatsCuda::gpu_bytes() const noexcept { return impl_->bytes; }
@@ -685,40 +713,32 @@ GQAH2OStatsCuda::Result GQAH2OStatsCuda::reduce(const void* probabilities, const
     const auto stream = static_cast<cudaStream_t>(raw_stream);
     Result out;
     out.started_ns = now_ns();
-    p.pending_stream = stream;
-    p.pending = true;
+    float* sums = p.sums.as<float>();
+    cuda_check(cudaEventRecord(p.begin->e, stream), "H2O reduction start record");
+    const int rc = hsb_h2o_group_sums(probabilities, ne.data(), nb.data(), keys, queries, sums, p.keys, nullptr,
+                                      stream);
+    if (rc != HSB_OK) throw_status(rc);  // rejected before any launch: nothing of ours uses the buffers
+    out.elements = keys * 8;
+    out.d2h_bytes = out.elements * sizeof(float);
+    p.consumer.hold(stream);
     try {
-        cuda_check(cudaEventRecord(p.begin, stream), "H2O reduction start record");
-        const int rc = hsb_h2o_group_sums(probabilities, ne.data(), nb.data(), keys, queries, p.gpu, p.keys, nullptr,
-                                          stream);
-        if (rc != HSB_OK) {  // rejected before any launch: nothing of ours is on the stream
-            p.pending = false;
-            p.pending_stream = nullptr;
-            throw_status(rc);
-        }
-        out.elements = keys * 8;
-        out.d2h_bytes = out.elements * sizeof(float);
-        cuda_check(cudaEventRecord(p.reduced, stream), "H2O reduction ready record");
-        cuda_check(cudaMemcpyAsync(p.host, p.gpu, out.d2h_bytes, cudaMemcpyDeviceToHost, stream), "H2O group sums D2H");
-        cuda_check(cudaEventRecord(p.copied, stream), "H2O D2H ready record");
-        cuda_check(cudaEventSynchronize(p.copied), "H2O group sums completion");
-        out.ready_observed_ns = now_ns();
-        p.pending = false;
-        p.pending_stream = nullptr;
-        float reduction_ms = 0, d2h_ms = 0;
-        cuda_check(cudaEventElapsedTime(&reduction_ms, p.begin, p.reduced), "H2O reduction interval");
-        cuda_check(cudaEventElapsedTime(&d2h_ms, p.reduced, p.copied), "H2O D2H interval");
-        out.reduction_ms = reduction_ms;
-        out.d2h_ms = d2h_ms;
-        out.sums = p.host;
-        return out;
+        cuda_check(cudaEventRecord(p.reduced->e, stream), "H2O reduction ready record");
+        d2h(p.host->ptr, sums, out.d2h_bytes, stream);
+        cuda_check(cudaEventRecord(p.copied->e, stream), "H2O D2H ready record");
+        cuda_check(cudaEventSynchronize(p.copied->e), "H2O group sums completion");
     } catch (...) {
-        if (p.pending && cudaStreamSynchronize(stream) == cudaSuccess) {
-            p.pending = false;
-            p.pending_stream = nullptr;
-        }
+        p.consumer.drain();
         throw;
     }
+    p.consumer.release();
+    out.ready_observed_ns = now_ns();
+    float reduction_ms = 0, d2h_ms = 0;
+    cuda_check(cudaEventElapsedTime(&reduction_ms, p.begin->e, p.reduced->e), "H2O reduction interval");
+    cuda_check(cudaEventElapsedTime(&d2h_ms, p.reduced->e, p.copied->e), "H2O D2H interval");
+    out.reduction_ms = reduction_ms;
+    out.d2h_ms = d2h_ms;
+    out.sums = reinterpret_cast<const float*>(p.host->ptr);
+    return out;
 }
 
 }  // namespace hillserve

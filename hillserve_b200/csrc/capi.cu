@@ -513,17 +513,24 @@ LayerLayout layer_layout(size_t valid, size_t count) {
 
 size_t hsb_layer_workspace_bytes(size_t valid, size_t count) { return layer_layout(valid, count).total; }
 
-static int layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_kcache, const uint16_t* d_vcache,
-                      size_t stride_words, size_t valid, float alpha, float ratio, size_t count,
-                      const hsb_layer_buffers* b, float* d_out, const void* d_prefetch, size_t prefetch_bytes,
-                      void* stream) {
-    if (!b || !d_q16 || !d_q32 || !d_out) return fail(HSB_E_INVALID, "layer step arguments");
-    if (prefetch_bytes && (!d_prefetch || !aligned(d_prefetch, 16)))
-        return fail(HSB_E_INVALID, "layer step: the prefetch range must start on a 16-byte boundary");
+// The layer step whole, or split at the reference's prepare / select
+// boundary (policy/full_gqa_runtime.cpp:493-516 scores the history ahead;
+// :531-548 scores the current token inside select): kPrepare scores positions
+// [0, valid - 1); kSelect scores position valid - 1 in the selector and
+// completes the layer.
+enum LayerPhase { kLayerWhole, kLayerPrepare, kLayerSelect };
+
+static int layer_step(LayerPhase phase, const uint16_t* d_q16, const float* d_q32, const uint16_t* d_kcache,
+                      const uint16_t* d_vcache, size_t stride_words, size_t valid, float alpha, float ratio,
+                      size_t count, const hsb_layer_buffers* b, float* d_out, void* stream) {
+    const bool selects = phase != kLayerPrepare;
+    if (!b || !d_q16 || (selects && (!d_q32 || !d_out))) return fail(HSB_E_INVALID, "layer step arguments");
     int rc = check_select(HSB_QUERY_HEADS, valid, valid, alpha, ratio);
     if (rc) return rc;
     if (count < select_kmax(valid, ratio) || count == 0)
         return fail(HSB_E_SEL_CAPACITY, hsb_status_message(HSB_E_SEL_CAPACITY));
+    if (phase != kLayerWhole && valid < 2)
+        return fail(HSB_E_INVALID, "layer prepare / select: at least one history position before the current one");
     const LayerLayout lay = layer_layout(valid, count);
     if (!b->scores || !b->ids || !b->result || !b->k_packed || !b->v_packed || !b->workspace ||
         b->workspace_bytes < lay.total || !aligned(b->workspace, 256))
@@ -533,26 +540,39 @@ static int layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t*
     size_t total = 0;
     if ((rc = check_views(&view, 1, &total))) return rc;
     // 16-byte row and query loads / packed stores.
-    if (!d_vcache || !aligned(d_vcache, 16) || !aligned(d_q32, 16) || !aligned(b->k_packed, 16) ||
-        !aligned(b->v_packed, 16))
+    if (selects && (!d_vcache || !aligned(d_vcache, 16) || !aligned(d_q32, 16) || !aligned(b->k_packed, 16) ||
+                    !aligned(b->v_packed, 16)))
         return fail(HSB_E_INVALID, "layer step: V cache, F32 query and packed buffers must be 16-byte aligned");
+    if (phase == kLayerSelect && (!aligned(d_q16, 16) || !aligned(d_kcache, 16) || (stride_words * 2) % 16))
+        return fail(HSB_E_INVALID, "layer select: the query and the key rows must be 16-byte aligned");
+    if (phase == kLayerSelect && !select_cluster_available(valid))
+        return fail(HSB_E_INVALID, "layer select: needs the cluster selector (at most 65536 positions)");
     unsigned char* ws = static_cast<unsigned char*>(b->workspace);
     uint16_t* keys = reinterpret_cast<uint16_t*>(ws + lay.keys);
     uint32_t* h0 = reinterpret_cast<uint32_t*>(ws + lay.h0);
-    // The scorer clears what the later stages expect at zero (selector
-    // header, result, attention counters) and leaves head-0 partials, so the
-    // step has no memset nodes and the selector no pass over head 0's row.
-    ScoreExtras x{};
-    x.h0 = h0;
-    x.zero[0] = reinterpret_cast<uint32_t*>(ws + lay.sel);
-    x.zero_words[0] = (unsigned)(select_header_bytes() / 4);
-    x.zero[1] = reinterpret_cast<uint32_t*>(b->result);
-    x.zero_words[1] = (unsigned)(sizeof(hsb_selection) / 4);
-    x.zero[2] = reinterpret_cast<uint32_t*>(ws + lay.att);
-    x.zero_words[2] = HSB_QUERY_HEADS;
     cudaError_t e;
-    if ((e = launch_score(d_q16, &view, 1, b->scores, valid, 0, &b->result->status, s, keys, &x)) != cudaSuccess)
-        return fail_cuda(e, "score launch");
+    if (phase != kLayerSelect) {
+        // The scorer clears what the later stages expect at zero (selector
+        // header, result, attention counters) and leaves head-0 partials, so
+        // the step has no memset nodes and the selector no pass over head 0's
+        // row.  Prepare scores the history only: columns [0, valid - 1).
+        ScoreExtras x{};
+        x.h0 = h0;
+        x.zero[0] = reinterpret_cast<uint32_t*>(ws + lay.sel);
+        x.zero_words[0] = (unsigned)(select_header_bytes() / 4);
+        x.zero[1] = reinterpret_cast<uint32_t*>(b->result);
+        x.zero_words[1] = (unsigned)(sizeof(hsb_selection) / 4);
+        x.zero[2] = reinterpret_cast<uint32_t*>(ws + lay.att);
+        x.zero_words[2] = HSB_QUERY_HEADS;
+        const hsb_key_view scored{d_kcache, phase == kLayerPrepare ? valid - 1 : valid, stride_words};
+        if ((e = launch_score(d_q16, &scored, 1, b->scores, valid, 0, &b->result->status, s, keys, &x)) !=
+            cudaSuccess)
+            return fail_cuda(e, "score launch");
+        if (phase == kLayerPrepare) {
+            g_last_error.clear();
+            return HSB_OK;
+        }
+    }
     SelectLaunch sl{};
     sl.scores = keys;
     sl.keys = 1;
@@ -573,6 +593,16 @@ static int layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t*
     sl.reset_header = 0;
     sl.h0 = h0;
     sl.zero_is_error = 1;
+    if (phase == kLayerSelect) {
+        // Beside another layer's history scorer, a cooperative launch would
+        // wait for the whole GPU; the selector's CTAs instead become resident
+        // as that scorer's CTAs retire (which never wait on the selector), so
+        // its bounded grid barrier completes without the attribute.
+        sl.cooperative = 0;
+        sl.cur_q = d_q16;
+        sl.cur_k = d_kcache + (valid - 1) * stride_words;
+        sl.cur_raw = b->scores;
+    }
     // The cluster selector gathers and attends in its epilogue; otherwise a
     // separate gather + attention kernel follows.
     sl.ga.q = d_q32;
@@ -584,8 +614,6 @@ static int layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t*
     sl.ga.count = count;
     sl.ga.out = d_out;
     sl.ga.scale = 1.0f / sqrtf(128.0f);
-    sl.ga.prefetch = d_prefetch;
-    sl.ga.prefetch_bytes = prefetch_bytes & ~(size_t)15;
     int fused = 0;
     sl.ga_done = &fused;
     if ((e = launch_select(sl, s)) != cudaSuccess) return fail_cuda(e, "select launch");
@@ -601,16 +629,21 @@ static int layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t*
 int hsb_layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_kcache, const uint16_t* d_vcache,
                    size_t stride_words, size_t valid, float alpha, float ratio, size_t count,
                    const hsb_layer_buffers* b, float* d_out, void* stream) {
-    return layer_step(d_q16, d_q32, d_kcache, d_vcache, stride_words, valid, alpha, ratio, count, b, d_out, nullptr,
-                      0, stream);
+    return layer_step(kLayerWhole, d_q16, d_q32, d_kcache, d_vcache, stride_words, valid, alpha, ratio, count, b,
+                      d_out, stream);
 }
 
-int hsb_layer_step_prefetch(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_kcache,
-                            const uint16_t* d_vcache, size_t stride_words, size_t valid, float alpha, float ratio,
-                            size_t count, const hsb_layer_buffers* b, float* d_out, const void* d_next,
-                            size_t next_bytes, void* stream) {
-    return layer_step(d_q16, d_q32, d_kcache, d_vcache, stride_words, valid, alpha, ratio, count, b, d_out, d_next,
-                      next_bytes, stream);
+int hsb_layer_prepare(const uint16_t* d_q16, const uint16_t* d_kcache, size_t stride_words, size_t valid,
+                      float alpha, float ratio, size_t count, const hsb_layer_buffers* b, void* stream) {
+    return layer_step(kLayerPrepare, d_q16, nullptr, d_kcache, nullptr, stride_words, valid, alpha, ratio, count, b,
+                      nullptr, stream);
+}
+
+int hsb_layer_select(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_kcache, const uint16_t* d_vcache,
+                     size_t stride_words, size_t valid, float alpha, float ratio, size_t count,
+                     const hsb_layer_buffers* b, float* d_out, void* stream) {
+    return layer_step(kLayerSelect, d_q16, d_q32, d_kcache, d_vcache, stride_words, valid, alpha, ratio, count, b,
+                      d_out, stream);
 }
 
 // ------------------------------------------------------------ KV-head shards
@@ -720,6 +753,95 @@ int hsb_shard_select(const uint16_t* d_order_keys, const uint16_t* d_raw, int kv
     sl.ga.heads = (unsigned)heads;
     e = launch_select(sl, as_stream(stream));
     if (e != cudaSuccess) return fail_cuda(e, "shard select launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+// ------------------------------------------- KV-head shards, peer memory
+size_t hsb_mailbox_bytes(size_t batch) { return mailbox_bytes(batch); }
+
+void hsb_mailbox_layout_of(size_t batch, hsb_mailbox_layout* out) {
+    if (out) mailbox_offsets(batch, out);
+}
+
+int hsb_mailbox_create(size_t batch, void** d_mailbox, void* ipc_handle) {
+    if (!d_mailbox || batch == 0 || batch > 65535) return fail(HSB_E_INVALID, "mailbox arguments");
+    static_assert(sizeof(cudaIpcMemHandle_t) == HSB_IPC_HANDLE_BYTES, "IPC handle size");
+    void* p = nullptr;
+    const size_t bytes = mailbox_bytes(batch);
+    cudaError_t e = cudaMalloc(&p, bytes);  // a base pointer: its IPC handle maps the mailbox itself
+    if (e != cudaSuccess) return fail_cuda(e, "mailbox allocation");
+    e = cudaMemset(p, 0, bytes);
+    if (e == cudaSuccess && ipc_handle) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return fail_cuda(e, "mailbox set-up");
+    }
+    *d_mailbox = p;
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+int hsb_mailbox_destroy(void* d_mailbox) {
+    const cudaError_t e = cudaFree(d_mailbox);
+    return e == cudaSuccess ? HSB_OK : fail_cuda(e, "mailbox release");
+}
+
+int hsb_mailbox_open(const void* ipc_handle, void** d_peer) {
+    if (!ipc_handle || !d_peer) return fail(HSB_E_INVALID, "mailbox open arguments");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, ipc_handle, sizeof h);
+    const cudaError_t e = cudaIpcOpenMemHandle(d_peer, h, cudaIpcMemLazyEnablePeerAccess);
+    return e == cudaSuccess ? HSB_OK : fail_cuda(e, "mailbox open");
+}
+
+int hsb_mailbox_close(void* d_peer) {
+    const cudaError_t e = cudaIpcCloseMemHandle(d_peer);
+    return e == cudaSuccess ? HSB_OK : fail_cuda(e, "mailbox close");
+}
+
+static int check_group(const hsb_peer_group* g) {
+    if (!g || g->world < 1 || g->world > HSB_MAX_PEERS || HSB_KV_HEADS % g->world || g->rank < 0 ||
+        g->rank >= g->world || g->batch == 0 || g->batch > 65535)
+        return fail(HSB_E_INVALID, "peer group: world must divide the 8 KV heads, rank < world, batch 1..65535");
+    for (int w = 0; w < g->world; ++w)
+        if (!g->mailbox[w] || !aligned(g->mailbox[w], 256))
+            return fail(HSB_E_INVALID, "peer group: every rank's mailbox must be mapped (256-byte aligned)");
+    return HSB_OK;
+}
+
+int hsb_exchange_threshold(const uint32_t* d_head0, float alpha, const hsb_peer_group* g, void* stream) {
+    int rc = check_group(g);
+    if (rc) return rc;
+    if (!d_head0) return fail(HSB_E_INVALID, "exchange threshold: head-0 partials");
+    if (g->rank != 0) return fail(HSB_E_INVALID, "exchange threshold: rank 0 holds query head 0");
+    if (!(alpha >= 0.0f) || !std::isfinite(alpha)) return fail(HSB_E_SEL_PARAMS, "GQA selector numeric parameters");
+    const cudaError_t e = launch_exchange_threshold(d_head0, alpha, g, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "exchange threshold launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+int hsb_exchange_count(const uint16_t* d_order_keys, size_t heads, size_t tokens, const hsb_peer_group* g,
+                       void* stream) {
+    int rc = check_group(g);
+    if (rc) return rc;
+    if (!d_order_keys || tokens == 0 || tokens > 0x7fffffffull || heads * (size_t)g->world != HSB_QUERY_HEADS)
+        return fail(HSB_E_INVALID, "exchange count: keys [batch][32 / world][tokens]");
+    const cudaError_t e = launch_exchange_count(d_order_keys, heads, tokens, g, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "exchange count launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
+int hsb_exchange_finish(const float* d_out, const hsb_selection* d_results, size_t heads, const hsb_peer_group* g,
+                        void* stream) {
+    int rc = check_group(g);
+    if (rc) return rc;
+    if (!d_out || !d_results || !aligned(d_out, 16) || heads * (size_t)g->world != HSB_QUERY_HEADS)
+        return fail(HSB_E_INVALID, "exchange finish: outputs [batch][32 / world][128] (16-byte aligned), results");
+    const cudaError_t e = launch_exchange_finish(d_out, d_results, heads, g, as_stream(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "exchange finish launch");
     g_last_error.clear();
     return HSB_OK;
 }

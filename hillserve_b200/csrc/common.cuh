@@ -48,6 +48,14 @@ __device__ __forceinline__ uint16_t scale_half(uint16_t raw) {
     return half_bits(__fdiv_rn(half_value(raw), __fsqrt_rn(128.0f)));
 }
 __device__ __forceinline__ bool is_finite_half(uint16_t h) { return (h & 0x7c00u) != 0x7c00u; }
+// Mixed-precision FMA: F16 x F16 + F32 -> F32 with one rounding.  The F16
+// product is exact in F32, so this equals the reference's rounded multiply
+// followed by a rounded add (kernels/full_gqa_pipeline/ABI.json:31-37).
+__device__ __forceinline__ float fma_f16(uint32_t a16, uint32_t b16, float c) {
+    float d;
+    asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"((unsigned short)a16), "h"((unsigned short)b16), "f"(c));
+    return d;
+}
 
 // ---------------------------------------------------------------- status
 // Order in which the reference would have met two errors: a payload-table
@@ -175,13 +183,6 @@ __device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int x, i
     asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];"
                  ::"l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z)
                  : "memory");
-}
-
-// Untiled bulk prefetch of [src, src + bytes) into L2 (a hint: nothing
-// waits for it and no data can be stale).  src 16-byte aligned, bytes a
-// multiple of 16.
-__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 // Named barrier `id` (1..15; 0 is __syncthreads) over `count` threads, a

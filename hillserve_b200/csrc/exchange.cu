@@ -1,0 +1,322 @@
+// exchange.cu -- the cross-GPU exchanges of a KV-head-sharded selected-KV
+// layer over peer memory (NVLink / NVSwitch P2P loads and stores), replacing
+// the NCCL broadcast and all-gathers of the collective path.
+//
+// The reference couples a sequence's heads twice (policy/gqa_policy.cpp:
+// 49-63): the threshold comes from query head 0's maximum, and k from the F16
+// mean of all 32 heads' F16 counts.  With the heads split over W GPUs, one
+// step of a batch of sequences is, on every rank:
+//   score (score_batch_kernel) -> [rank 0] threshold + push -> count + push,
+//   wait for every rank's records -> select (the cluster selector in record
+//   mode, reading the records from this rank's mailbox) -> finish: push this
+//   rank's attention outputs, wait for every rank's.
+// Every rank owns one mailbox (cudaMalloc'd, exported by CUDA IPC): its
+// header holds one epoch flag per producer (rank 0's thresholds, each rank's
+// records, each rank's outputs) and the rank's own step counter; its body the
+// thresholds, the 32 heads' count records, the 32 heads' outputs and every
+// rank's selection results.  Producers store into every rank's mailbox, fence
+// at system scope, and the last CTA to finish releases the flag (the step's
+// epoch) on every rank; consumers poll their own mailbox's flags with
+// system-scope acquire loads.  Flags only grow (one epoch per step), so
+// nothing is reset between steps.  Every wait is bounded (the group's limit,
+// 2 s by default): a wait that gives up records HSB_E_TIMEOUT in the
+// mailbox's status word and the kernel returns.  After a timeout the group's
+// epochs disagree: the mailboxes must be recreated.  No multicast object and
+// no TMA multicast are used: plain stores to peer memory only.
+#include <algorithm>
+#include <cmath>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace hsb {
+namespace {
+
+struct MailboxHeader {
+    unsigned long long thr_flag;        // epoch of the thresholds (from rank 0)
+    unsigned long long rec_flag[8];     // epoch of rank w's count records
+    unsigned long long out_flag[8];     // epoch of rank w's outputs
+    unsigned long long epoch;           // this rank: the last step completed
+    unsigned int arrive[4];             // this rank: last-CTA counters (threshold, count, finish)
+    hsb_device_status status;           // this rank: first error of the exchange
+    unsigned int pad[(256 - 8 * 18 - 16 - 8) / 4];
+};
+static_assert(sizeof(MailboxHeader) == 256, "mailbox header is 256 bytes");
+
+size_t align256(size_t b) { return (b + 255) / 256 * 256; }
+
+struct Layout {
+    size_t thr, rec, out, res, total;
+};
+Layout layout(size_t batch) {
+    Layout l{};
+    l.thr = sizeof(MailboxHeader);
+    l.rec = l.thr + align256(batch * 2 * 4);
+    l.out = l.rec + align256(batch * kHeads * 4);
+    l.res = l.out + align256(batch * kHeads * kDim * 4);
+    l.total = l.res + align256((size_t)HSB_MAX_PEERS * batch * sizeof(hsb_selection));
+    return l;
+}
+
+struct PeerParams {
+    unsigned char* mb[HSB_MAX_PEERS];  // every rank's mailbox (own: local)
+    int world, rank;
+    unsigned long long batch;
+    unsigned long long limit_ns;
+    Layout lay;
+};
+
+__device__ __forceinline__ MailboxHeader* header(const PeerParams& p, int w) {
+    return reinterpret_cast<MailboxHeader*>(p.mb[w]);
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* a) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned long long* a, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+}
+// Bounded wait until *flag >= epoch; false when the limit ran out.
+__device__ bool wait_flag(const unsigned long long* flag, unsigned long long epoch, unsigned long long limit_ns) {
+    if (ld_acquire_sys(flag) >= epoch) return true;
+    const unsigned long long start = global_ns();
+    while (ld_acquire_sys(flag) < epoch) {
+        if (global_ns() - start > limit_ns) return false;
+        __nanosleep(32);
+    }
+    return true;
+}
+// The step this launch belongs to: one past the last completed one.
+__device__ __forceinline__ unsigned long long step_epoch(const PeerParams& p) {
+    return __ldcg(&header(p, p.rank)->epoch) + 1;
+}
+// Last-CTA election over the grid (after this CTA's stores and a system
+// fence): true in exactly one CTA, which also resets the counter.
+__device__ bool last_cta(unsigned int* counter) {
+    __shared__ bool last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        last = atomicAdd(counter, 1u) == gridDim.x - 1;
+        if (last) {
+            *counter = 0;
+            __threadfence_system();
+        }
+    }
+    __syncthreads();
+    return last;
+}
+// One thread per rank releases `flag` (by offset in the header) = epoch on
+// every rank's mailbox, then the caller waits for its own copies.
+__device__ void release_all(const PeerParams& p, size_t flag_offset, unsigned long long epoch) {
+    if (threadIdx.x < (unsigned)p.world)
+        st_release_sys(reinterpret_cast<unsigned long long*>(p.mb[threadIdx.x] + flag_offset), epoch);
+}
+// Waits (thread w < world) for every rank's flag at flag_offset + 8 w; the
+// first wait that gives up raises HSB_E_TIMEOUT (index = rank waited for).
+__device__ void wait_all(const PeerParams& p, size_t flag_offset, unsigned long long epoch) {
+    if (threadIdx.x < (unsigned)p.world) {
+        const unsigned long long* f =
+            reinterpret_cast<const unsigned long long*>(p.mb[p.rank] + flag_offset) + threadIdx.x;
+        if (!wait_flag(f, epoch, p.limit_ns)) raise_status(&header(p, p.rank)->status, HSB_E_TIMEOUT, threadIdx.x);
+    }
+    __syncthreads();
+}
+
+constexpr int kThrThreads = 256;
+// Rank 0: each sequence's threshold record {order key of F16(max - alpha),
+// status} from the history scorer's head-0 partials (gqa_policy.cpp:50-54),
+// stored into every rank's mailbox; the last CTA releases thr_flag.
+__global__ void __launch_bounds__(kThrThreads) exch_threshold_kernel(const uint32_t* h0, float alpha,
+                                                                     const __grid_constant__ PeerParams p) {
+    pdl_wait();
+    const unsigned long long epoch = step_epoch(p);
+    h0 += (size_t)blockIdx.x * kH0Partials;
+    __shared__ unsigned int smax, sbad;
+    if (threadIdx.x == 0) {
+        smax = 0;
+        sbad = 0;
+    }
+    __syncthreads();
+    unsigned int mx = 0, bad0 = 0;
+    for (unsigned int i = threadIdx.x; i < kH0Partials; i += kThrThreads) {
+        const uint32_t v = __ldcg(h0 + i);
+        mx = max(mx, v & 0xffffu);
+        bad0 |= v >> 16;
+    }
+    mx = __reduce_max_sync(0xffffffffu, mx);
+    bad0 = __reduce_or_sync(0xffffffffu, bad0);
+    if ((threadIdx.x & 31) == 0) {
+        atomicMax(&smax, mx);
+        atomicOr(&sbad, bad0);
+    }
+    __syncthreads();
+    if (threadIdx.x < (unsigned)p.world) {
+        const uint16_t kb = (uint16_t)((smax & 0x8000u) ? (smax ^ 0x8000u) : (~smax & 0xffffu));
+        const float threshold = half_value(half_bits(smax ? half_value(kb) - alpha : -INFINITY));
+        uint32_t status = 0;
+        if (sbad) status = HSB_E_SEL_NONFINITE_HEAD0;
+        else if (!isfinite(threshold)) status = HSB_E_SEL_THRESHOLD;
+        uint32_t* thr = reinterpret_cast<uint32_t*>(p.mb[threadIdx.x] + p.lay.thr) + 2 * blockIdx.x;
+        const uint2 rec = make_uint2(status ? 0u : order_key(half_bits(threshold)), status);
+        *reinterpret_cast<uint2*>(thr) = rec;
+    }
+    if (last_cta(&header(p, p.rank)->arrive[0])) release_all(p, offsetof(MailboxHeader, thr_flag), epoch);
+}
+
+constexpr int kCntThreads = 1024;
+// Every rank, CTA = (sequence, local head): wait for the thresholds, count
+// #{keys >= threshold key} | non-finite << 31 and store the record into
+// every rank's mailbox (column head_base + head); the last CTA releases this
+// rank's rec_flag and then waits for every rank's records.
+__global__ void __launch_bounds__(kCntThreads) exch_count_kernel(const uint16_t* keys, unsigned long long tokens,
+                                                                 unsigned heads, unsigned head_base,
+                                                                 const __grid_constant__ PeerParams p) {
+    pdl_wait();
+    const unsigned long long epoch = step_epoch(p);
+    MailboxHeader* own = header(p, p.rank);
+    __shared__ int ready;
+    if (threadIdx.x == 0) ready = wait_flag(&own->thr_flag, epoch, p.limit_ns);
+    __syncthreads();
+    if (!ready) {
+        if (threadIdx.x == 0) raise_status(&own->status, HSB_E_TIMEOUT, 0);
+        return;  // the group's epochs now disagree: the mailboxes must be recreated
+    }
+    const unsigned seq = blockIdx.x / heads, head = blockIdx.x % heads;
+    const unsigned int thr_key = __ldcg(reinterpret_cast<const uint32_t*>(p.mb[p.rank] + p.lay.thr) + 2 * seq);
+    __shared__ unsigned int scnt, sbad;
+    if (threadIdx.x == 0) {
+        scnt = 0;
+        sbad = 0;
+    }
+    __syncthreads();
+    const uint16_t* row = keys + (unsigned long long)blockIdx.x * tokens;
+    const bool vec = tokens % 8 == 0 && (reinterpret_cast<uintptr_t>(keys) & 15) == 0;
+    const unsigned long long n8 = vec ? tokens / 8 : 0;
+    unsigned int cnt = 0, bad = 0;
+    for (unsigned long long g = threadIdx.x; g < n8; g += kCntThreads) {
+        const uint4 w = reinterpret_cast<const uint4*>(row)[g];
+        const uint32_t v[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t key = (v[j >> 1] >> (16 * (j & 1))) & 0xffffu;
+            bad |= key_nonfinite(key);
+            cnt += (!key_nan(key) && key >= thr_key) ? 1u : 0u;
+        }
+    }
+    for (unsigned long long i = n8 * 8 + threadIdx.x; i < tokens; i += kCntThreads) {
+        const uint32_t key = row[i];
+        bad |= key_nonfinite(key);
+        cnt += (!key_nan(key) && key >= thr_key) ? 1u : 0u;
+    }
+    cnt = __reduce_add_sync(0xffffffffu, cnt);
+    bad = __any_sync(0xffffffffu, bad);
+    if ((threadIdx.x & 31) == 0) {
+        if (cnt) atomicAdd(&scnt, cnt);
+        if (bad) atomicOr(&sbad, 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x < (unsigned)p.world) {
+        uint32_t* rec = reinterpret_cast<uint32_t*>(p.mb[threadIdx.x] + p.lay.rec);
+        rec[(size_t)seq * kHeads + head_base + head] = scnt | (sbad << 31);
+    }
+    if (last_cta(&own->arrive[1])) {
+        release_all(p, offsetof(MailboxHeader, rec_flag) + 8 * p.rank, epoch);
+        wait_all(p, offsetof(MailboxHeader, rec_flag), epoch);
+    }
+}
+
+constexpr int kFinThreads = 256;
+// Every rank: this rank's outputs [batch][heads][128] and selection results
+// [batch] into every rank's mailbox (outputs at heads head_base.., results at
+// slot rank); the last CTA releases out_flag, waits for every rank's, and
+// closes the step (epoch).
+__global__ void __launch_bounds__(kFinThreads) exch_finish_kernel(const float* out, const hsb_selection* results,
+                                                                  unsigned heads, unsigned head_base,
+                                                                  const __grid_constant__ PeerParams p) {
+    pdl_wait();
+    const unsigned long long epoch = step_epoch(p);
+    const unsigned long long n4 = p.batch * heads * (kDim / 4);  // float4 pieces
+    for (unsigned long long i = blockIdx.x * (unsigned long long)kFinThreads + threadIdx.x; i < n4;
+         i += (unsigned long long)gridDim.x * kFinThreads) {
+        const unsigned long long row = i / (kDim / 4), piece = i % (kDim / 4);
+        const unsigned long long seq = row / heads, h = row % heads;
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(out) + i);
+        const unsigned long long at = ((seq * kHeads + head_base + h) * kDim) / 4 + piece;
+        for (int w = 0; w < p.world; ++w) reinterpret_cast<float4*>(p.mb[w] + p.lay.out)[at] = v;
+    }
+    for (unsigned long long i = blockIdx.x * (unsigned long long)kFinThreads + threadIdx.x; i < p.batch;
+         i += (unsigned long long)gridDim.x * kFinThreads) {
+        const hsb_selection r = results[i];
+        for (int w = 0; w < p.world; ++w)
+            reinterpret_cast<hsb_selection*>(p.mb[w] + p.lay.res)[(size_t)p.rank * p.batch + i] = r;
+    }
+    MailboxHeader* own = header(p, p.rank);
+    if (last_cta(&own->arrive[2])) {
+        release_all(p, offsetof(MailboxHeader, out_flag) + 8 * p.rank, epoch);
+        wait_all(p, offsetof(MailboxHeader, out_flag), epoch);
+        if (threadIdx.x == 0) own->epoch = epoch;
+    }
+}
+
+bool peer_params(const hsb_peer_group* g, PeerParams* p) {
+    if (!g || g->world < 1 || g->world > HSB_MAX_PEERS || HSB_KV_HEADS % g->world || g->rank < 0 ||
+        g->rank >= g->world || g->batch == 0)
+        return false;
+    for (int w = 0; w < g->world; ++w) {
+        if (!g->mailbox[w] || (reinterpret_cast<uintptr_t>(g->mailbox[w]) & 255)) return false;
+        p->mb[w] = static_cast<unsigned char*>(g->mailbox[w]);
+    }
+    p->world = g->world;
+    p->rank = g->rank;
+    p->batch = g->batch;
+    p->limit_ns = g->wait_limit_ns ? g->wait_limit_ns : kWaitLimitNs;
+    p->lay = layout(g->batch);
+    return true;
+}
+
+}  // namespace
+
+size_t mailbox_bytes(size_t batch) { return layout(batch).total; }
+
+void mailbox_offsets(size_t batch, hsb_mailbox_layout* out) {
+    const Layout l = layout(batch);
+    out->thr = l.thr;
+    out->records = l.rec;
+    out->outputs = l.out;
+    out->results = l.res;
+    out->status = offsetof(MailboxHeader, status);
+    out->bytes = l.total;
+}
+
+cudaError_t launch_exchange_threshold(const uint32_t* h0, float alpha, const hsb_peer_group* g,
+                                      cudaStream_t stream) {
+    PeerParams p{};
+    if (!peer_params(g, &p)) return cudaErrorInvalidValue;
+    return launch_dependent(exch_threshold_kernel, dim3((unsigned)g->batch), dim3(kThrThreads), 0, stream, false, h0,
+                            alpha, p);
+}
+
+cudaError_t launch_exchange_count(const uint16_t* keys, size_t heads, size_t tokens, const hsb_peer_group* g,
+                                  cudaStream_t stream) {
+    PeerParams p{};
+    if (!peer_params(g, &p) || heads * g->world != kHeads) return cudaErrorInvalidValue;
+    return launch_dependent(exch_count_kernel, dim3((unsigned)(heads * g->batch)), dim3(kCntThreads), 0, stream, false,
+                            keys, (unsigned long long)tokens, (unsigned)heads, (unsigned)(heads * g->rank), p);
+}
+
+cudaError_t launch_exchange_finish(const float* out, const hsb_selection* results, size_t heads,
+                                   const hsb_peer_group* g, cudaStream_t stream) {
+    PeerParams p{};
+    if (!peer_params(g, &p) || heads * g->world != kHeads) return cudaErrorInvalidValue;
+    const DeviceInfo& dev = device_info();
+    const unsigned long long pieces = g->batch * heads * (kDim / 4);
+    const unsigned blocks =
+        (unsigned)std::max<unsigned long long>(1, std::min<unsigned long long>((pieces + kFinThreads - 1) / kFinThreads,
+                                                                               (unsigned long long)dev.sms));
+    return launch_dependent(exch_finish_kernel, dim3(blocks), dim3(kFinThreads), 0, stream, false, out, results,
+                            (unsigned)heads, (unsigned)(heads * g->rank), p);
+}
+
+}  // namespace hsb

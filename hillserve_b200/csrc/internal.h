@@ -98,11 +98,6 @@ struct SelectEpilogue {
     float* out = nullptr;    // null: no epilogue
     float scale = 0.0f;
     unsigned heads = 32;     // query heads per packed K slot (a shard packs its own)
-    // L2 prefetch hint issued as the selector starts: `prefetch_bytes` at
-    // `prefetch` (16-byte aligned, a multiple of 16), split over the grid --
-    // the next layer's key cache, streamed while the selection runs.
-    const void* prefetch = nullptr;
-    unsigned long long prefetch_bytes = 0;
 };
 struct SelectLaunch {
     const uint16_t* scores;
@@ -137,7 +132,24 @@ struct SelectLaunch {
     // and the epilogue's buffers per sequence.
     uint32_t batch = 1;
     unsigned long long seq_scores = 0;
+    // The layer's select after a prepared history (cluster path, batch 1,
+    // keys mode with h0): the scorer covered positions [0, valid - 1), and
+    // the kernel scores the current position valid - 1 itself -- cur_q F16
+    // [heads][128] against its key row cur_k (8 KV heads x 128, 16-byte
+    // aligned) -- writing the raw scores to cur_raw[h * stride + valid - 1].
+    const uint16_t* cur_q = nullptr;
+    const uint16_t* cur_k = nullptr;
+    uint16_t* cur_raw = nullptr;
+    int cooperative = 1;  // launch attribute of the grid-barrier kernels
 };
+// Exchanges over peer memory (exchange.cu); arguments validated there.
+size_t mailbox_bytes(size_t batch);
+void mailbox_offsets(size_t batch, hsb_mailbox_layout* out);
+cudaError_t launch_exchange_threshold(const uint32_t* h0, float alpha, const hsb_peer_group* g, cudaStream_t stream);
+cudaError_t launch_exchange_count(const uint16_t* keys, size_t heads, size_t tokens, const hsb_peer_group* g,
+                                  cudaStream_t stream);
+cudaError_t launch_exchange_finish(const float* out, const hsb_selection* results, size_t heads,
+                                   const hsb_peer_group* g, cudaStream_t stream);
 cudaError_t launch_shard_threshold(const uint32_t* h0, size_t batch, float alpha, uint32_t* thr,
                                    cudaStream_t stream);
 cudaError_t launch_shard_count(const uint16_t* keys, size_t heads, size_t tokens, size_t batch, const uint32_t* thr,

@@ -239,13 +239,9 @@ struct TmaParams {
     // extras.h0 by kH0Partials words.
     unsigned long long seq_tokens, q_seq, out_seq;
     int prefetch_tiles;  // key tiles per CTA pulled into L2 before the grid dependency wait
+    unsigned long long batch;  // score_batch_kernel: sequences (tiles is per sequence)
 };
 
-__device__ __forceinline__ float fma_f16(uint32_t a16, uint32_t b16, float c) {
-    float d;
-    asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"((unsigned short)a16), "h"((unsigned short)b16), "f"(c));
-    return d;
-}
 
 __device__ __forceinline__ int tile_view(const TmaParams& p, unsigned long long tile) {
     int v = 0;
@@ -422,6 +418,179 @@ __global__ void __launch_bounds__(kTThreads, 2) score_tma_kernel(const __grid_co
     }
 }
 
+// ---------------------------------------------------------- batched shards
+// The scorer over a batch of sequences of a KV-head shard: one wave of at
+// most two CTAs per SM, CTA c taking the contiguous run of global tiles
+// [c T / grid, (c + 1) T / grid) of the T = batch x tiles (sequence-major)
+// tiles, so every CTA has the same work within one tile and no second wave
+// trails the first.  A run crosses sequence boundaries: at each crossing the
+// consumers restage Q and close the head-0 partial of the sequence they
+// leave.  Head-0 partials: CTA c writes slot c - first(s) of sequence s,
+// first(s) being the CTA that holds the sequence's first tile, and first(s)
+// also zeroes the slots past the sequence's CTA count.
+__device__ __forceinline__ unsigned long long flat_cta_of(unsigned long long t, unsigned long long total,
+                                                          unsigned long long grid) {
+    // the CTA whose run [floor(c total / grid), floor((c+1) total / grid)) holds tile t
+    return ((t + 1) * grid + total - 1) / total - 1;
+}
+
+template <int G>
+__global__ void __launch_bounds__(kTThreads, 2) score_batch_kernel(const __grid_constant__ TmaParams p) {
+    constexpr int T = 256 / G;
+    const unsigned long long total = p.tiles * p.batch, grid = gridDim.x;
+    const unsigned long long g0 = blockIdx.x * total / grid, g1 = (blockIdx.x + 1) * total / grid;
+    if (threadIdx.x == kTConsumerWarps * 32 && g0 < g1) {  // the first tile into L2 before the dependency wait
+        const int y = (int)((g0 / p.tiles) * p.seq_tokens + (g0 % p.tiles) * T);
+        tma_prefetch_3d(&p.maps[0], 0, y, 0);
+        tma_prefetch_3d(&p.maps[0], kTHalf, y, 0);
+    }
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    unsigned char* stages = smem;
+    uint4* qs = reinterpret_cast<uint4*>(smem + kTStages * kTStageBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTStages * kTStageBytes + kTQBytes);
+    uint64_t* empty = full + kTStages;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ unsigned int h0_max, h0_bad;
+    if (threadIdx.x == 0) {
+        h0_max = 0;
+        h0_bad = 0;
+        for (int s = 0; s < kTStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kTConsumerWarps);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+    pdl_wait();
+    pdl_trigger();
+    constexpr int kConsumerThreads = kTConsumerWarps * 32;
+
+    if (warp == kTConsumerWarps) {
+        if (lane != 0) return;
+        uint32_t it = 0;
+        bool ok = true;
+        for (unsigned long long g = g0; g < g1 && ok; ++g) {
+            const int y = (int)((g / p.tiles) * p.seq_tokens + (g % p.tiles) * T);
+            for (int half = 0; half < 2; ++half, ++it) {
+                const uint32_t s = it % kTStages;
+                if (it >= kTStages && !mbar_wait(&empty[s], ((it / kTStages) - 1) & 1)) {
+                    raise_status(p.status, HSB_E_TIMEOUT, blockIdx.x);
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[s], kTStageBytes);
+                tma_load_3d(stages + s * kTStageBytes, &p.maps[0], half * kTHalf, y, 0, &full[s]);
+            }
+        }
+        if (!ok) {
+            const uint32_t first = it > kTStages ? it - kTStages : 0;
+            for (uint32_t j = first; j < it; ++j) (void)mbar_wait(&full[j % kTStages], (j / kTStages) & 1);
+        }
+        return;
+    }
+
+    const int kh = warp % G, tl = (warp / G) * 32 + lane;
+    const uint4* qv = qs + kh * (kDim / 2);
+    uint32_t it = 0, h0max = 0, h0bad = 0;
+    unsigned long long seq = ~0ull;
+    // A consumer warp whose wait gave up stops consuming but still meets the
+    // consumers' named barriers, so no warp is left waiting at one.
+    bool aborted = false;
+    // Closes sequence s on this CTA: its head-0 partial (slot blockIdx.x -
+    // first(s)), and the zero slots when this CTA holds s's first tile.
+    auto close_seq = [&](unsigned long long s) {
+        if (!p.extras.h0) return;
+        if (kh == 0) {
+            const uint32_t m = __reduce_max_sync(0xffffffffu, h0max);
+            const uint32_t b = __reduce_or_sync(0xffffffffu, h0bad);
+            if (lane == 0) {
+                atomicMax(&h0_max, m);
+                atomicOr(&h0_bad, b);
+            }
+        }
+        h0max = 0;
+        h0bad = 0;
+        named_sync(1, kConsumerThreads);
+        uint32_t* h0 = p.extras.h0 + s * kH0Partials;
+        const unsigned long long first = flat_cta_of(s * p.tiles, total, grid);
+        const unsigned long long last = flat_cta_of(s * p.tiles + p.tiles - 1, total, grid);
+        if (threadIdx.x == 0) {
+            h0[blockIdx.x - first] = (h0_bad << 16) | h0_max;
+            h0_max = 0;
+            h0_bad = 0;
+        }
+        if (blockIdx.x == first)
+            for (unsigned w = (unsigned)(last - first + 1) + threadIdx.x; w < kH0Partials; w += kConsumerThreads)
+                h0[w] = 0u;
+    };
+    for (unsigned long long g = g0; g < g1; ++g) {
+        const unsigned long long s_now = g / p.tiles, t0 = (g % p.tiles) * T;
+        if (s_now != seq) {
+            if (seq != ~0ull) close_seq(seq);
+            named_sync(1, kConsumerThreads);  // every consumer is done with the previous Q
+            constexpr int kPer = G * kGroup * kDim / kConsumerThreads;
+            const uint16_t* qg = p.q + s_now * p.q_seq;
+            uint16_t qv16[kPer];
+#pragma unroll
+            for (int u = 0; u < kPer; ++u) qv16[u] = qg[threadIdx.x + u * kConsumerThreads];
+#pragma unroll
+            for (int u = 0; u < kPer; ++u) {
+                const int i = threadIdx.x + u * kConsumerThreads, h = i >> 7, c = i & 127;
+                reinterpret_cast<uint16_t*>(qs)[((h >> 2) * kDim + c) * kGroup + (h & 3)] = qv16[u];
+            }
+            named_sync(1, kConsumerThreads);
+            seq = s_now;
+        }
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        if (aborted) continue;  // keeps meeting the named barriers at sequence crossings
+        for (int half = 0; half < 2; ++half, ++it) {
+            const uint32_t s = it % kTStages;
+            if (!mbar_wait(&full[s], (it / kTStages) & 1)) {
+                raise_status(p.status, HSB_E_TIMEOUT, blockIdx.x);
+                aborted = true;
+                break;
+            }
+            const unsigned char* row = stages + s * kTStageBytes + (kh * T + tl) * 128;
+            const uint4* qh = qv + half * (kTHalf / 2);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint4 w = *reinterpret_cast<const uint4*>(row + ((j ^ (tl & 7)) << 4));
+                const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int e = 0; e < 8; e += 2) {
+                    const uint4 qq = qh[j * 4 + (e >> 1)];
+                    const uint32_t k0 = words[e >> 1] & 0xffffu, k1 = words[e >> 1] >> 16;
+                    a0 = fma_f16(qq.x & 0xffffu, k0, a0);
+                    a1 = fma_f16(qq.x >> 16, k0, a1);
+                    a2 = fma_f16(qq.y & 0xffffu, k0, a2);
+                    a3 = fma_f16(qq.y >> 16, k0, a3);
+                    a0 = fma_f16(qq.z & 0xffffu, k1, a0);
+                    a1 = fma_f16(qq.z >> 16, k1, a1);
+                    a2 = fma_f16(qq.w & 0xffffu, k1, a2);
+                    a3 = fma_f16(qq.w >> 16, k1, a3);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        if (!aborted && (unsigned long long)tl < p.seq_tokens - t0) {
+            const unsigned long long col = seq * p.out_seq + t0 + tl;
+            const float acc[4] = {a0, a1, a2, a3};
+#pragma unroll
+            for (int gq = 0; gq < kGroup; ++gq) {
+                const uint16_t sc = half_bits(acc[gq]);
+                const unsigned long long at = (unsigned long long)(kh * kGroup + gq) * p.out_stride + col;
+                p.out[at] = sc;
+                const uint32_t key = order_key(scale_half(sc));
+                p.keys[at] = (uint16_t)key;
+                if (kh == 0 && gq == 0) track_head0(key, h0max, h0bad);
+            }
+        }
+    }
+    if (seq != ~0ull) close_seq(seq);
+}
+
 // Token-major keys of one view seen as a 3-D tensor {channel, token, KV head}
 // (strides: token = stride_words words, KV head = 128 words), so that a box
 // lands in shared memory as [KV head][token][channels].
@@ -470,6 +639,14 @@ cudaError_t configure_tma_kernels() {
         e = cudaFuncSetAttribute(score_tma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemBytes);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(score_tma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(score_batch_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(score_batch_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(score_batch_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(score_batch_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmemBytes);
     return e;
 }
 
@@ -581,15 +758,17 @@ cudaError_t launch_score_shard(const uint16_t* q, int kv_heads, const uint16_t* 
     t.status = status;
     if (extras) t.extras = *extras;
     t.prefetch_tiles = kTPrefetchTiles;
-    // CTAs per sequence: the whole batch fills two CTAs per SM.
-    const unsigned long long per_seq =
-        std::max<unsigned long long>(1, ((unsigned long long)dev.sms * 2 + batch - 1) / batch);
-    const dim3 grid((unsigned)std::min<unsigned long long>(t.tiles, per_seq), (unsigned)batch);
+    // One wave: at most two CTAs per SM over the batch's tiles, contiguous
+    // runs across sequences (score_batch_kernel).
+    t.batch = batch;
+    const unsigned long long total = t.tiles * batch;
+    const dim3 grid((unsigned)std::min<unsigned long long>(total, (unsigned long long)dev.sms * 2));
+    if (!keys) return cudaErrorInvalidValue;
     switch (kv_heads) {
-    case 1: return launch_dependent(score_tma_kernel<1>, grid, dim3(kTThreads), kTSmemBytes, stream, false, t);
-    case 2: return launch_dependent(score_tma_kernel<2>, grid, dim3(kTThreads), kTSmemBytes, stream, false, t);
-    case 4: return launch_dependent(score_tma_kernel<4>, grid, dim3(kTThreads), kTSmemBytes, stream, false, t);
-    case 8: return launch_dependent(score_tma_kernel<8>, grid, dim3(kTThreads), kTSmemBytes, stream, false, t);
+    case 1: return launch_dependent(score_batch_kernel<1>, grid, dim3(kTThreads), kTSmemBytes, stream, false, t);
+    case 2: return launch_dependent(score_batch_kernel<2>, grid, dim3(kTThreads), kTSmemBytes, stream, false, t);
+    case 4: return launch_dependent(score_batch_kernel<4>, grid, dim3(kTThreads), kTSmemBytes, stream, false, t);
+    case 8: return launch_dependent(score_batch_kernel<8>, grid, dim3(kTThreads), kTSmemBytes, stream, false, t);
     default: return cudaErrorInvalidValue;
     }
 }

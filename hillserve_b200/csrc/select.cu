@@ -88,6 +88,10 @@ struct SelectParams {
     // seq_scores elements in; every per-head output advances by its own size.
     uint32_t batch;
     unsigned long long seq_scores;
+    // Current position scored here (see SelectLaunch): cur_q, cur_k, cur_raw.
+    const uint16_t* cur_q;
+    const uint16_t* cur_k;
+    uint16_t* cur_raw;
 };
 
 // Head-0 maximum key and non-finite flag from the scorer's per-CTA partials
@@ -574,6 +578,8 @@ struct ClusterShared {
     unsigned int status, status_index;
     unsigned long long k;
     int timeout;
+    // Current position: [head 0 / this head][query row, key row]
+    __align__(16) uint16_t cur_row[2][2][kDim];
 };
 
 __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
@@ -707,17 +713,6 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __maxnreg__(80)
     select_cluster_kernel(const __grid_constant__ SelectParams p) {
     pdl_wait();
     pdl_trigger();
-    // The next layer's keys into L2 while this selection runs (the scorer
-    // has finished, so DRAM would otherwise idle): the last warp of every CTA
-    // issues 64 KB bulk prefetches over the CTA's share of the range.
-    if (p.ga.prefetch_bytes && (threadIdx.x >> 5) == kCWarps - 1) {
-        const unsigned long long share = (p.ga.prefetch_bytes / gridDim.x + 15) & ~15ull;
-        const unsigned long long b0 = min(p.ga.prefetch_bytes, (unsigned long long)blockIdx.x * share);
-        const unsigned long long b1 = min(p.ga.prefetch_bytes, b0 + share);
-        const unsigned char* base = static_cast<const unsigned char*>(p.ga.prefetch);
-        for (unsigned long long o = b0 + (unsigned long long)(threadIdx.x & 31) * 65536; o < b1; o += 32ull * 65536)
-            bulk_prefetch_l2(base + o, (uint32_t)min(65536ull, b1 - o));
-    }
     extern __shared__ __align__(16) unsigned char dyn[];
     __shared__ ClusterShared sh;
     cg::cluster_group cl = cg::this_cluster();
@@ -770,6 +765,35 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __maxnreg__(80)
 #pragma unroll
     for (int u = 0; u < 2; ++u)
         if (tid + u * kCThreads < m8) kw[u] = reinterpret_cast<const uint4*>(row + b0)[tid + u * kCThreads];
+    // Current position (select after a prepared history): two warps stage
+    // a query row and the position's key row, and their lane 0 scores it in
+    // the scorer's order (channels 0..127, F32 from +0, one F16 rounding) --
+    // head 0 for the threshold in every CTA, and this CTA's head in the CTA
+    // whose chunk holds the position.  The key loads above are in flight
+    // meanwhile.
+    const bool cur_mode = p.cur_k != nullptr;
+    const unsigned long long cur = n - 1;
+    const bool own_cur = cur_mode && cur >= b0 && cur < b1;
+    const unsigned int cur_local = own_cur ? (unsigned int)(cur - b0) : 0xffffffffu;
+    const int cur_slot = !cur_mode ? -1 : warp == kCWarps - 1 ? 0 : (warp == kCWarps - 2 && own_cur) ? 1 : -1;
+    uint32_t cur_key = 0;
+    if (cur_slot >= 0) {
+        const uint32_t qh = cur_slot == 0 ? 0u : h;
+        const uint4 v = lane < 16 ? reinterpret_cast<const uint4*>(p.cur_q + (size_t)qh * kDim)[lane]
+                                  : reinterpret_cast<const uint4*>(p.cur_k + (size_t)(qh / kGroup) * kDim)[lane - 16];
+        reinterpret_cast<uint4*>(&sh.cur_row[cur_slot][0][0])[lane] = v;
+        __syncwarp();
+        if (lane == 0) {
+            const uint16_t* qs = sh.cur_row[cur_slot][0];
+            const uint16_t* ks = sh.cur_row[cur_slot][1];
+            float acc = 0.0f;
+#pragma unroll 16
+            for (int c = 0; c < kDim; ++c) acc = fma_f16(qs[c], ks[c], acc);
+            const uint16_t raw = half_bits(acc);
+            cur_key = order_key(scale_half(raw));
+            if (cur_slot == 1) p.cur_raw[(size_t)h * p.stride + cur] = raw;
+        }
+    }
     // Shard steps: the threshold record's status (written by the preceding grid).
     const int ext_status = ext ? (int)p.ext_thr[2 * seqb + 1] : 0;
     if (p.h0 && !ext) {
@@ -794,15 +818,23 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __maxnreg__(80)
         mx = key_nan(key) ? mx : max(mx, key);
     }
     // One 16-byte word of keys: coarse histogram, order keys to shared memory.
+    // The current position's slot (not written by the history scorer) is
+    // skipped here and filled below.
     auto take = [&](const uint4 w, unsigned int g) {
         const uint32_t v[4] = {w.x, w.y, w.z, w.w};
         uint32_t k2[4];
+        const unsigned int skip = (g == (cur_local >> 3)) ? (cur_local & 7u) : 8u;
 #pragma unroll
         for (int j = 0; j < 8; j += 2) {
             const uint32_t a = to_key(v[j >> 1] & 0xffffu, p.mode), b = to_key(v[j >> 1] >> 16, p.mode);
-            bad |= key_nonfinite(a) | key_nonfinite(b);
-            atomicAdd(&sh.coarse[a >> 6], 1u);
-            atomicAdd(&sh.coarse[b >> 6], 1u);
+            if ((unsigned)j != skip) {
+                bad |= key_nonfinite(a);
+                atomicAdd(&sh.coarse[a >> 6], 1u);
+            }
+            if ((unsigned)j + 1 != skip) {
+                bad |= key_nonfinite(b);
+                atomicAdd(&sh.coarse[b >> 6], 1u);
+            }
             k2[j >> 1] = a | (b << 16);
         }
         reinterpret_cast<uint4*>(keys)[g] = make_uint4(k2[0], k2[1], k2[2], k2[3]);
@@ -813,10 +845,15 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __maxnreg__(80)
     for (unsigned int g = tid + 2 * kCThreads; g < m8; g += kCThreads)
         take(reinterpret_cast<const uint4*>(row + b0)[g], g);
     for (unsigned int i = m8 * 8 + tid; i < m; i += kCThreads) {
+        if (i == cur_local) continue;
         const uint32_t key = to_key(row[b0 + i], p.mode);
         bad |= key_nonfinite(key);
         atomicAdd(&sh.coarse[key >> 6], 1u);
         keys[i] = (uint16_t)key;
+    }
+    if (cur_slot == 0 && lane == 0) {  // the current position joins head 0's maximum
+        bad0 |= key_nonfinite(cur_key);
+        mx = key_nan(cur_key) ? mx : max(mx, cur_key);
     }
     mx = __reduce_max_sync(0xffffffffu, mx);
     bad0 = __any_sync(0xffffffffu, bad0);
@@ -842,6 +879,14 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __maxnreg__(80)
         return;  // every CTA of the grid takes this branch; nothing is pending
     }
     const unsigned int thr_key = order_key(half_bits(threshold));
+    if (cur_mode) {  // the current position's key joins this chunk (after every take() store)
+        if (cur_slot == 1 && lane == 0) {
+            bad |= key_nonfinite(cur_key);
+            atomicAdd(&sh.coarse[cur_key >> 6], 1u);
+            keys[cur_local] = (uint16_t)cur_key;
+        }
+        __syncthreads();
+    }
     unsigned int cnt = 0;
     for (unsigned int i = tid; i < (ext ? 0u : m); i += kCThreads) {
         const unsigned int key = keys[i];
@@ -1550,6 +1595,12 @@ cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream) {
     p.heads_total = s.ext ? s.heads_total : s.heads;
     p.batch = s.batch ? s.batch : 1;
     p.seq_scores = s.seq_scores;
+    p.cur_q = s.cur_q;
+    p.cur_k = s.cur_k;
+    p.cur_raw = s.cur_raw;
+    if (s.cur_k && !(s.keys && s.h0 && !s.ext && p.batch == 1 && s.valid >= 2 &&
+                     s.valid <= kClusterKeysMax && s.heads <= (uint32_t)cluster_capacity(dev.ordinal)))
+        return cudaErrorInvalidValue;  // the current position is scored by the cluster kernel only
     if (s.ga_done) *s.ga_done = 0;
     cudaError_t e = cudaSuccess;
     if (s.reset_header) {
@@ -1577,7 +1628,7 @@ cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream) {
         cfg.gridDim = dim3(p.batch * s.heads * kCluster);
         // Shard steps (records from the exchange) have no grid barrier, so a
         // batch of any size needs no co-residency: an ordinary cluster launch.
-        if (s.ext) cfg.numAttrs = 0;
+        if (s.ext || !s.cooperative) cfg.numAttrs = 0;
         cfg.blockDim = dim3(kCThreads);
         cfg.dynamicSmemBytes = ((cs + 7) / 8 * 8 * 2 + 15) / 16 * 16 + 2 * kSmemSortMax * 8;
         if (s.ga.out) cfg.dynamicSmemBytes = std::max(cfg.dynamicSmemBytes, kEpiSmemBytes);

@@ -21,6 +21,13 @@ The sum of F16-rounded integer counts is exact in FP32 in any order, so the
 folded k equals the unsharded selector's (policy/full_gqa_runtime.cpp:307-309
 makes the same argument).  Phases are methods so that a caller (or a test)
 can place the exchanges itself; step() places them with torch.distributed.
+
+PeerExchange does the same exchanges with the library's own kernels over
+NVLink peer memory (hsb_exchange_*): every rank's mailbox is mapped into every
+process by CUDA IPC, producers store into every mailbox and release an epoch
+flag, consumers wait on their own mailbox's flags (bounded waits).  No NCCL
+call sits on the data path; the process group only carries the one-time
+exchange of IPC handles.
 """
 from __future__ import annotations
 
@@ -129,6 +136,35 @@ class KVHeadShardedLayer:
             _ptr(vshard), _ptr(self.k_packed), _ptr(self.v_packed), _ptr(self.out), _ptr(self.workspace),
             self.workspace.numel(), stream), "shard select")
 
+    # ------------------------------------------------------- peer memory
+    def step_peer(self, q16, q32, kshard, vshard, exchange: PeerExchange):
+        """The whole layer with the exchanges over peer memory: five launches
+        on this rank (four on ranks other than 0), no collective.  Returns the
+        mailbox's outputs [batch][32][128] and the combined selection records
+        [batch][4] (k, boundary-tied heads summed over ranks, status code,
+        index); the exchange's own status is in exchange.status."""
+        torch = self.torch
+        stream = torch.cuda.current_stream().cuda_stream
+        g = C.byref(exchange.group)
+        self.score(q16, kshard, stream)
+        if self.geo.rank == 0:
+            self._check(self.lib.hsb_exchange_threshold(_ptr(self.head0), C.c_float(self.alpha), g, stream),
+                        "exchange threshold")
+        self._check(self.lib.hsb_exchange_count(_ptr(self.keys), self.geo.heads, self.tokens, g, stream),
+                    "exchange count")
+        self._check(self.lib.hsb_shard_select(
+            _ptr(self.keys), _ptr(self.scores), self.geo.kv_heads, self.tokens, self.batch, exchange.thr_ptr,
+            exchange.records_ptr, HEADS, self.geo.head_base, C.c_float(self.alpha), C.c_float(self.ratio),
+            _ptr(self.ids), self.count, _ptr(self.counts), _ptr(self.results), _ptr(q32), _ptr(kshard),
+            _ptr(vshard), _ptr(self.k_packed), _ptr(self.v_packed), _ptr(self.out), _ptr(self.workspace),
+            self.workspace.numel(), stream), "shard select")
+        self._check(self.lib.hsb_exchange_finish(_ptr(self.out), _ptr(self.results), self.geo.heads, g, stream),
+                    "exchange finish")
+        res = exchange.results
+        combined = res[0].clone()
+        combined[:, 1] = res[:, :, 1].sum(dim=0)
+        return exchange.outputs, combined
+
     # ------------------------------------------------------------------ step
     def step(self, q16, q32, kshard, vshard, group=None):
         """The whole layer on this rank; returns the all-gathered outputs
@@ -158,6 +194,80 @@ class KVHeadShardedLayer:
         combined = res[0].clone()
         combined[:, 1] = sum(r[:, 1] for r in res)
         return out, combined
+
+
+class _DeviceArray:
+    """A torch view of library-owned device memory (__cuda_array_interface__)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerExchange:
+    """The mailboxes of one KV-head-sharded group over peer memory.
+
+    Every rank creates its mailbox, the IPC handles travel once over the
+    process group (all_gather_object), and every rank maps the others'.  The
+    mailbox of this rank ends each step with all 32 heads' outputs
+    (`outputs`, [batch][32][128] F32) and every rank's selection results."""
+
+    def __init__(self, batch: int, world: int, rank: int, group=None, wait_limit_ns: int = 0):
+        import torch
+
+        self.lib = _capi.lib()
+        self.batch, self.world, self.rank = batch, world, rank
+        self.layout = _capi.MailboxLayout()
+        self.lib.hsb_mailbox_layout_of(batch, C.byref(self.layout))
+        handle = (C.c_ubyte * 64)()
+        own = C.c_void_p()
+        self._check(self.lib.hsb_mailbox_create(batch, C.byref(own), handle), "mailbox create")
+        self.own = own.value
+        self.opened = []
+        ptrs = [0] * world
+        ptrs[rank] = self.own
+        if world > 1:
+            import torch.distributed as dist
+
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            for w in range(world):
+                if w == rank:
+                    continue
+                peer = C.c_void_p()
+                buf = (C.c_ubyte * 64).from_buffer_copy(handles[w])
+                self._check(self.lib.hsb_mailbox_open(buf, C.byref(peer)), f"mailbox open (rank {w})")
+                ptrs[w] = peer.value
+                self.opened.append(peer.value)
+        self.group = _capi.PeerGroup()
+        self.group.world, self.group.rank, self.group.batch = world, rank, batch
+        self.group.wait_limit_ns = int(wait_limit_ns)
+        for w in range(world):
+            self.group.mailbox[w] = ptrs[w]
+        lay = self.layout
+        self.outputs = torch.as_tensor(_DeviceArray(self.own + lay.outputs, (batch, HEADS, DIM), "<f4"),
+                                       device="cuda")
+        self.results = torch.as_tensor(_DeviceArray(self.own + lay.results, (world, batch, 4), "<i4"),
+                                       device="cuda")
+        self.status = torch.as_tensor(_DeviceArray(self.own + lay.status, (2,), "<i4"), device="cuda")
+        self.thr_ptr = self.own + lay.thr
+        self.records_ptr = self.own + lay.records
+
+    def _check(self, rc: int, what: str):
+        if rc != 0:
+            from . import HsbError
+
+            raise HsbError(rc, f"{what}: {self.lib.hsb_last_error().decode()}")
+
+    def close(self):
+        """Unmaps the peers' mailboxes and frees this rank's (after the
+        group's last step; every rank calls it)."""
+        for p in self.opened:
+            self.lib.hsb_mailbox_close(C.c_void_p(p))
+        self.opened = []
+        if self.own:
+            self.lib.hsb_mailbox_destroy(C.c_void_p(self.own))
+            self.own = 0
 
 
 def shard_rows(full, world: int, rank: int):

@@ -42,6 +42,8 @@ extern "C" {
 #define HSB_DIM 128
 #define HSB_ROW_WORDS 2048 /* one interleaved KV row: K[8,128] then V[8,128] */
 #define HSB_MAX_VIEWS 8    /* key views per scoring launch (more are split) */
+#define HSB_MAX_PEERS 8    /* GPUs of one KV-head-sharded group */
+#define HSB_IPC_HANDLE_BYTES 64
 
 typedef enum hsb_status {
     HSB_OK = 0,
@@ -314,17 +316,25 @@ int hsb_layer_step(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_
                    const uint16_t* d_vcache, size_t stride_words, size_t valid, float alpha,
                    float ratio, size_t count, const hsb_layer_buffers* buffers, float* d_out,
                    void* stream);
-/* hsb_layer_step that also streams the next layer's key cache into L2 while
- * this layer's selection runs (the scorer has finished and DRAM would
- * otherwise idle): next_bytes at d_next (16-byte aligned; rounded down to a
- * multiple of 16) are prefetched as an L2 hint by the selector's CTAs.
- * Nothing waits for it and nothing can read stale data through it, so the
- * results are those of hsb_layer_step; a decode step passes layer l + 1's
- * keys to layer l. */
-int hsb_layer_step_prefetch(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_kcache,
-                            const uint16_t* d_vcache, size_t stride_words, size_t valid, float alpha,
-                            float ratio, size_t count, const hsb_layer_buffers* buffers, float* d_out,
-                            const void* d_next, size_t next_bytes, void* stream);
+/* The layer step split where the reference splits it
+ * (FullGqaRuntimePolicy::prepare_history, policy/full_gqa_runtime.cpp:493-516,
+ * scores the history ahead of the layer; select, :549-585, adds the current
+ * token's scores, :531-548, and selects).  hsb_layer_prepare scores positions
+ * [0, valid - 1) with the selection query (the early rehearsal,
+ * patches/llama-b6000-early-rehearsal.patch:46-52) and needs only the history
+ * rows; hsb_layer_select scores the current position valid - 1 -- whose K row
+ * must be in the cache by then -- normalises, selects, gathers and attends.
+ * Together they give hsb_layer_step's results bit for bit.  valid >= 2; the
+ * select needs the cluster selector (valid <= 65536) and 16-byte aligned
+ * d_q16 / key rows.  Order: select after its prepare (same buffers), and the
+ * next prepare on those buffers after that select; a decode step runs
+ * layer l + 1's prepare beside layer l's select on two buffer sets. */
+int hsb_layer_prepare(const uint16_t* d_q16, const uint16_t* d_kcache, size_t stride_words, size_t valid,
+                      float alpha, float ratio, size_t count, const hsb_layer_buffers* buffers, void* stream);
+int hsb_layer_select(const uint16_t* d_q16, const float* d_q32, const uint16_t* d_kcache,
+                     const uint16_t* d_vcache, size_t stride_words, size_t valid, float alpha,
+                     float ratio, size_t count, const hsb_layer_buffers* buffers, float* d_out,
+                     void* stream);
 
 /* ------------------------------------------------------- KV-head shards
  * One selected-KV layer split across GPUs by KV head (each GPU holds
@@ -366,6 +376,60 @@ int hsb_shard_select(const uint16_t* d_order_keys, const uint16_t* d_raw, int kv
                      const uint16_t* d_kshard, const uint16_t* d_vshard, uint16_t* d_k_packed,
                      uint16_t* d_v_packed, float* d_out, void* d_workspace, size_t workspace_bytes,
                      void* stream);
+
+/* ------------------------------------- KV-head shards over peer memory
+ * The same step with the exchanges done by this library's kernels over
+ * NVLink peer memory instead of NCCL collectives (the reference has no
+ * multi-GPU code; the coupling reproduced is that of policy/gqa_policy.cpp:
+ * 49-63).  Every rank owns a mailbox -- device memory exported by CUDA IPC
+ * and opened by every other rank of the node -- and one step is, on every
+ * rank, in stream order:
+ *   hsb_shard_score (head-0 partials on rank 0)
+ *   -> rank 0: hsb_exchange_threshold   (stores the thresholds into every
+ *      mailbox, releases a flag)
+ *   -> hsb_exchange_count               (waits for the thresholds, stores
+ *      its heads' count records into every mailbox, waits for every rank's)
+ *   -> hsb_shard_select with d_thr / d_records in this rank's mailbox
+ *   -> hsb_exchange_finish              (stores its outputs and selection
+ *      results into every mailbox, waits for every rank's).
+ * Afterwards this rank's mailbox holds all 32 heads' outputs [batch][32][128]
+ * F32 and every rank's results [world][batch].  Flags carry a step epoch
+ * kept in the mailbox, so no reset is needed between steps (CUDA graphs
+ * replay the step as is).  Every wait is bounded by wait_limit_ns (0: 2 s);
+ * one that gives up writes HSB_E_TIMEOUT (index = the rank waited for) to the
+ * mailbox's status word and the kernel returns -- the mailboxes must then be
+ * recreated.  Plain peer loads and stores only: no multicast. */
+typedef struct hsb_mailbox_layout {
+    size_t thr;      /* uint32 [batch][2]: threshold order key, status */
+    size_t records;  /* uint32 [batch][32]: count | non-finite << 31 */
+    size_t outputs;  /* float [batch][32][128] */
+    size_t results;  /* hsb_selection [world][batch] */
+    size_t status;   /* hsb_device_status of the exchange */
+    size_t bytes;
+} hsb_mailbox_layout;
+typedef struct hsb_peer_group {
+    int world;                        /* 1, 2, 4 or 8 */
+    int rank;
+    void* mailbox[HSB_MAX_PEERS];     /* every rank's mailbox as mapped in this process (own: local) */
+    size_t batch;                     /* sequences per step */
+    uint64_t wait_limit_ns;           /* bound of every cross-GPU wait; 0 = 2 s */
+} hsb_peer_group;
+size_t hsb_mailbox_bytes(size_t batch);
+void hsb_mailbox_layout_of(size_t batch, hsb_mailbox_layout* out);
+/* Set-up (allocates): a zeroed mailbox for `batch` sequences on the current
+ * device and, when ipc_handle != NULL, its HSB_IPC_HANDLE_BYTES CUDA IPC
+ * handle for the other ranks. */
+int hsb_mailbox_create(size_t batch, void** d_mailbox, void* ipc_handle);
+int hsb_mailbox_destroy(void* d_mailbox);
+/* Maps another process's mailbox (cudaIpcOpenMemHandle, peer access enabled
+ * on demand) / unmaps it. */
+int hsb_mailbox_open(const void* ipc_handle, void** d_peer);
+int hsb_mailbox_close(void* d_peer);
+int hsb_exchange_threshold(const uint32_t* d_head0, float alpha, const hsb_peer_group* group, void* stream);
+int hsb_exchange_count(const uint16_t* d_order_keys, size_t heads, size_t tokens, const hsb_peer_group* group,
+                       void* stream);
+int hsb_exchange_finish(const float* d_out, const hsb_selection* d_results, size_t heads,
+                        const hsb_peer_group* group, void* stream);
 
 /* ---------------------------------------------- H2O residency statistics
  * The device work of GQAH2OStatsCuda::reduce (runtime/gqa_h2o_stats.cu:

@@ -165,3 +165,65 @@ def test_rehearsal_prefetch_step(cuda, ob, alpha):
     wkp, wvp, wmask = ob.pack(wids, np.full(32, wk), [n], wphys, payload, count)
     assert np.array_equal(host_u16(kp), wkp) and np.array_equal(host_u16(vp), wvp)
     assert np.array_equal(mask.cpu().numpy(), wmask)
+
+
+@pytest.mark.parametrize("n,alpha,seed", [(4096, 10.0, 5), (4096, 0.1, 6), (2000, 50.0, 7), (4103, 5.0, 8),
+                                          (32768, 10.0, 9), (64, 50.0, 10)])
+def test_prepare_select_equals_layer_step(cuda, ob, n, alpha, seed):
+    """The split layer (hsb_layer_prepare scores the history [0, n-1);
+    hsb_layer_select scores the current position n-1 in the selector) gives
+    hsb_layer_step's bits: scores, k, ties, counts, IDs, packed K/V, output.
+    The split's buffers start poisoned (0xff), so a read of the unscored
+    current column would show; the whole result is also checked against the
+    oracle.  Odd n puts the current position in the selector's tail loop."""
+    import torch
+
+    q16, k, _ = inputs.config1(n, seed=seed)
+    v = inputs.values(seed, n)
+    q32 = np.frombuffer(q16.astype(np.uint16).tobytes(), dtype=np.float16).astype(np.float32)
+    qd, q32d, kd, vd = dev_u16(q16), _t(q32, torch.float32), dev_u16(k), dev_u16(v)
+    whole = cuda.SelectedKVLayer(n, alpha)
+    out_w = whole(qd, q32d, kd, vd).clone()
+    sel_w = whole.selection()
+    split = cuda.SelectedKVLayer(n, alpha)
+    for t in (split.scores, split.workspace, split.ids, split.counts, split.k_packed, split.v_packed):
+        t.view(torch.uint8).fill_(0xFF)
+    split.prepare(qd, kd)
+    out_s = split.select(qd, q32d, kd, vd)
+    sel_s = split.selection()
+    assert (sel_s.k, sel_s.boundary_tied_heads, sel_s.status.code) == (sel_w.k, sel_w.boundary_tied_heads,
+                                                                        sel_w.status.code)
+    assert torch.equal(split.scores, whole.scores)
+    assert torch.equal(split.counts, whole.counts)
+    kk = sel_w.k
+    assert torch.equal(split.ids[:, :kk], whole.ids[:, :kk])
+    count = whole.count
+    assert torch.equal(split.k_packed.view(count, 32, 128)[:kk], whole.k_packed.view(count, 32, 128)[:kk])
+    assert torch.equal(split.v_packed.view(32, 128, count)[:, :, :kk], whole.v_packed.view(32, 128, count)[:, :, :kk])
+    assert torch.equal(out_s, out_w)
+    raw, ids, counts, wk = oracle_layer(ob, q16, q32, k, v, n, alpha)
+    assert np.array_equal(host_u16(split.scores), raw) and kk == wk
+
+
+@pytest.mark.parametrize("where", ["head0", "other"])
+def test_select_current_nonfinite(cuda, where):
+    """A non-finite score at the current position raises the reference's
+    error in the split as in the whole step: head 0 -> nonfinite head0 score
+    (22), any other head -> nonfinite GQA score (24)."""
+    import torch
+
+    n = 4096
+    q16, k, _ = inputs.config1(n, seed=12)
+    v = inputs.values(12, n)
+    kk = k.copy().reshape(n, 8, 128)
+    kk[n - 1, 0 if where == "head0" else 5, 3] = 0x7C00  # +inf in the current position's key row
+    q32 = np.frombuffer(q16.astype(np.uint16).tobytes(), dtype=np.float16).astype(np.float32)
+    qd, q32d, kd, vd = dev_u16(q16), _t(q32, torch.float32), dev_u16(kk.reshape(-1)), dev_u16(v)
+    whole = cuda.SelectedKVLayer(n, 5.0)
+    whole(qd, q32d, kd, vd)
+    split = cuda.SelectedKVLayer(n, 5.0)
+    split.prepare(qd, kd)
+    split.select(qd, q32d, kd, vd)
+    a, b = whole.selection(), split.selection()
+    assert a.status.code == b.status.code == (22 if where == "head0" else 24)
+    assert a.status.index == b.status.index
