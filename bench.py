@@ -57,10 +57,12 @@ def parse():
     ap.add_argument("--tokens", type=int, default=N)
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode",
+    ap.add_argument("--no-configs1", action="store_true", help="kv-sharded at N=1: skip the configs[1] block")
+    ap.add_argument("--workload", default="kv-sharded",
                     choices=["decode", "kv-sharded", "sweep", "h2o", "records", "history", "executor"],
-                    help="decode: configs[1] (the headline); kv-sharded: configs[4], one selected-KV layer "
-                         "over --batch sequences with the KV heads split over the ranks; sweep: configs[2], "
+                    help="kv-sharded (the headline at every N): configs[4], one selected-KV layer over --batch "
+                         "sequences with the KV heads split over the ranks, plus (N=1) a configs[1] block; decode: "
+                         "configs[1] alone, the 32-layer decode step; sweep: configs[2], "
                          "the selected-KV layer step per length N; h2o: the H2O group-sum reduction "
                          "(decode and prefill-block shapes) beside the reference's CUDA kernel; records: the "
                          "cold-tier KV record encoder and verifier (FNV-1a) beside the reference's CPU checksum; "
@@ -721,42 +723,98 @@ def run_reference(args, rank, world, torch):
                     "d2h_bytes_per_step": 0}}
 
 
+# ---------------------------------------------------------- configs[4]
+SHARD_SEED = 9        # generator streams of sequence b: layer_seeds(SHARD_SEED, b)
+SHARD_SAMPLE = 8      # sequences of the CPU legs' bounded sample (of the batch)
+
+
+def shard_config(args, world) -> dict:
+    """The configs[4] workload both arms measure (identical dicts)."""
+    return {"workload": "configs[4]: 64 independent sequences x N=32768, one selected-KV layer each, the 8 KV "
+                        "heads split over the GPUs; a layer-step = one sequence's layer",
+            "sequences": args.batch, "tokens": args.tokens, "alpha": args.alpha, "cap_ratio": 0.2,
+            "kv_heads_per_gpu": 8 // world, "l2": "K/V shards 8.6 GB >> 126 MB L2, no flush"}
+
+
+def shard_cpu_sequences(tokens, count, threads):
+    """The first `count` sequences of the configs[4] batch rebuilt on the CPU
+    (the oracle's restatement of the generator, bit-identical to the GPU's)."""
+    from oracle import binding as ob
+
+    out = []
+    for b in range(count):
+        sq, sk, sv = layer_seeds(SHARD_SEED, b)
+        q16 = ob.synth_normal(4096, sq, 1.0, threads=threads)
+        kc = ob.synth_keys(tokens, sk, 0.02, 4.0, True, THETA, threads=threads)
+        vc = ob.synth_keys(tokens, sv, 0.0, 1.0, False, THETA, threads=threads)
+        out.append((kc, vc, q16, q16.view(np.float16).astype(np.float32)))
+    return out
+
+
+def shard_reference_step(data, n, alpha, threads):
+    """One selected-KV layer of every sampled sequence through the reference
+    CPU path (the same per-layer routine as configs[1]'s)."""
+    t, results = 0.0, []
+    for d in data:
+        dt, r = reference_layer(*d, n, alpha, threads, True)
+        t += dt
+        results.append(r)
+    return t, results
+
+
+SHARD_REF_SAMPLE = ("{m} of the {b} sequences per step, one selected-KV layer each at N={n}: reference "
+                    "FullGqaCpuScorer x{t} threads, F16 scaling, select_gqa_scores, gqa_physical_union, "
+                    "pack_gqa_workspace from oracle/_ref; attention by the oracle's float port of the ggml graph "
+                    "(x{t} threads)")
+
+
 def run_sharded(args, rank, world, torch, dist):
-    """--batch independent sequences of N tokens, one selected-KV
-    layer, KV heads split over the ranks (G = 8 / world per rank).  The
-    exchanges -- thresholds from rank 0, every head's count records, the
-    attention outputs -- go over NVLink peer memory through the library's
-    own kernels (--exchange peer, the default) or through NCCL collectives
-    (--exchange nccl).  The whole step is captured in one CUDA graph."""
+    """configs[4], the headline at every N: --batch independent sequences of
+    N tokens, one selected-KV layer, the KV heads split over the ranks
+    (G = 8 / world per rank).  The exchanges -- thresholds from rank 0, every
+    head's count records, the attention outputs -- go over NVLink peer memory
+    through the library's own kernels (--exchange peer, the default) or NCCL
+    collectives (--exchange nccl).  The step is one CUDA graph; a second
+    graph with event nodes between the phases gives the per-phase timeline."""
     import hillserve_b200 as hsb
     from hillserve_b200 import sharded as sh
 
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+    dev_index = torch.cuda.current_device()
     lib = hsb._capi.lib()
     n, batch, g = args.tokens, args.batch, 8 // world
     s = torch.cuda.current_stream().cuda_stream
-    q16 = torch.empty((batch, HEADS, 128), dtype=torch.int16, device="cuda")
+    # The step's queries of this rank's heads, F16 then F32, in one buffer
+    # (one host copy per step end to end).
+    hq = g * 4
+    inbuf = torch.empty(batch * hq * 128 * 6, dtype=torch.uint8, device="cuda")
+    q16l = inbuf[:batch * hq * 256].view(torch.int16).view(batch, hq, 128)
+    q32l = inbuf[batch * hq * 256:].view(torch.float32).view(batch, hq, 128)
     kshard = torch.empty((batch, n, g, 128), dtype=torch.int16, device="cuda")
     vshard = torch.empty_like(kshard)
     rows = torch.empty((n, 8, 128), dtype=torch.int16, device="cuda")
+    qfull = torch.empty((HEADS, 128), dtype=torch.int16, device="cuda")
     for b in range(batch):  # the same sequences on every rank; each keeps its own heads
-        sq, sk, sv = layer_seeds(9, b)
-        lib.hsb_synth_normal_f16(q16[b].data_ptr(), 4096, sq, 1.0, s)
+        sq, sk, sv = layer_seeds(SHARD_SEED, b)
+        lib.hsb_synth_normal_f16(qfull.data_ptr(), 4096, sq, 1.0, s)
+        q16l[b].copy_(qfull[hq * rank:hq * (rank + 1)])
         lib.hsb_synth_keys(rows.data_ptr(), n, 1024, sk, 0.02, 4.0, 1, THETA, s)
         kshard[b].copy_(rows[:, g * rank:g * (rank + 1), :])
         lib.hsb_synth_keys(rows.data_ptr(), n, 1024, sv, 0.0, 1.0, 0, THETA, s)
         vshard[b].copy_(rows[:, g * rank:g * (rank + 1), :])
     del rows
-    q32 = q16.view(torch.float16).float()
-    q16l, q32l = sh.shard_queries(q16, world, rank), sh.shard_queries(q32, world, rank)
+    q32l.copy_(q16l.view(torch.float16).float())
     layer = sh.KVHeadShardedLayer(n, batch, world, rank, alpha=args.alpha)
     peer = args.exchange == "peer"
     ex = sh.PeerExchange(batch, world, rank) if peer else None
+    phase_ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(6)]
 
-    def step():
-        if peer:
+    def step(events=False):
+        if not peer:
+            return layer.step(q16l, q32l, kshard, vshard)
+        if not events:
             return layer.step_peer(q16l, q32l, kshard, vshard, ex)
-        return layer.step(q16l, q32l, kshard, vshard)
+        return layer.step_peer(q16l, q32l, kshard, vshard, ex, marks=[e.record for e in phase_ev])
 
     stream = torch.cuda.Stream()
     holder = {}
@@ -767,12 +825,17 @@ def run_sharded(args, rank, world, torch, dist):
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         holder["out"], holder["res"] = step()
+    prof = None
+    if peer:
+        prof = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(prof, stream=stream):
+            step(events=True)
     for _ in range(max(args.warmup, 3)):
         graph.replay()
     torch.cuda.synchronize()
     dist.barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(torch.cuda.current_device()) as clocks:
+    with ClockSampler(dev_index) as clocks:
         with torch.cuda.stream(stream):
             start.record(stream)
             for _ in range(args.steps):
@@ -784,31 +847,181 @@ def run_sharded(args, rank, world, torch, dist):
     t = torch.tensor([start.elapsed_time(stop)], dtype=torch.float64, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
+    value = batch * args.steps / (ms / 1e3)
+
+    # ---- per-phase timeline (graph with event nodes; max over ranks)
+    phases = None
+    if prof is not None:
+        with torch.cuda.stream(stream):
+            prof.replay()
+        stream.synchronize()
+        names = ["score", "threshold_push", "count_exchange", "select", "finish_exchange"]
+        dur = torch.tensor([phase_ev[i].elapsed_time(phase_ev[i + 1]) for i in range(5)], dtype=torch.float64,
+                           device="cuda")
+        dist.all_reduce(dur, op=dist.ReduceOp.MAX)
+        phases = {k: round(float(v), 5) for k, v in zip(names, dur.tolist())}
+
+    # ---- end to end: queries in from pinned host memory, outputs back
+    e2e = None
+    if peer:
+        hin = inbuf.cpu().pin_memory()
+        hout = torch.empty((batch, HEADS, 128), dtype=torch.float32).pin_memory()
+
+        def one():
+            inbuf.copy_(hin, non_blocking=True)
+            graph.replay()
+            if rank == 0:
+                hout.copy_(ex.outputs, non_blocking=True)
+
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                one()
+            stream.synchronize()
+            dist.barrier()
+            start.record(stream)
+            for _ in range(args.steps):
+                one()
+            stop.record(stream)
+        stop.synchronize()
+        te = torch.tensor([start.elapsed_time(stop)], dtype=torch.float64, device="cuda")
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(batch * args.steps / (float(te.item()) / 1e3), 1), "unit": "layer-steps/s",
+               "h2d_bytes_per_step": int(hin.numel()), "d2h_bytes_per_step": int(hout.numel() * 4) if rank == 0 else 0,
+               "note": "per rank: its heads' F16 + F32 queries in from pinned memory; rank 0 reads back the "
+                       "all-gathered outputs [64][32][128] F32; K/V shards stay resident in HBM"}
+
     res = holder["res"].cpu().numpy()
-    exch_status = ex.status.cpu().numpy().tolist() if peer else None
+    peak, peak_kind = peaks()
+    # The dominant kernel: the batched shard scorer (algorithmic bytes: this
+    # rank's K of every sequence, its Q, scores and order keys written).
+    b_score = batch * (n * g * 256 + hq * 256 + hq * n * 4)
+    roofline = None
+    if phases:
+        achieved = b_score / (phases["score"] / 1e3) / 1e9
+        roofline = {"kernel": "score_batch_kernel", "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                    "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": shard_traffic(world),
+                    "traffic_source": "profiles/score_batch_kernel_configs4_traffic.json (one ncu capture)",
+                    "algorithmic_bytes_per_launch": b_score, "peak_kind": peak_kind,
+                    "duration": "the score phase of the event-marked replay, max over ranks"}
+    b_ssg = batch * (2048 * n + 8192 + 64 * n + 64 * n)  # whole job: K, Q, scores + keys, keys again (select)
+    graded = b_ssg / (ms / args.steps / 1e3) / 1e9
+    line = {"metric": METRIC, "value": round(value, 1), "unit": "layer-steps/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f16 in, f32 accumulate (ordered)", "data": "synthetic",
+            "config": shard_config(args, world),
+            "exchange": ("peer memory: the library's kernels store thresholds, count records and outputs into "
+                         "every rank's CUDA-IPC-mapped mailbox, epoch flags, bounded waits; no collective on the "
+                         "data path" if peer else "NCCL broadcast of thresholds, all-gather of records and outputs"),
+            "launch": "one CUDA graph per step",
+            "phases_ms": phases,
+            "score_select_gather": {"bytes_per_step_all_gpus": b_ssg, "GB_s": round(graded, 1),
+                                    "frac_of_peak_x_gpus": round(graded / (peak * world), 4), "peak_GB_s": peak,
+                                    "peak_kind": peak_kind, "path": "the timed graph, whole step"},
+            "roofline": roofline, "e2e": e2e,
+            "gpu_launches": (5 if rank == 0 else 4) * args.steps if peer else None,
+            "exchange_status": ex.status.cpu().numpy().tolist() if peer else None,
+            "selection": {"k_mean": float(res[:, 0].mean()), "zero_selection": int((res[:, 0] == 0).sum())},
+            "clocks": clocks.summary()}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"], line["parity"] = shard_cpu_baseline(layer, kshard, vshard, q16l, q32l, holder, args)
     graph.reset()
+    if prof is not None:
+        prof.reset()
     torch.cuda.synchronize()
     dist.barrier()  # every rank is done with the peers' mailboxes
     if peer:
         ex.close()
-    b_layer = 2048 * n + 8192 + 64 * n  # per sequence: K read by the scorer, Q, scores + keys
-    return {"metric": "KV-head-sharded selected-KV layer: sequence-layer-steps/s at N=32K",
-            "value": round(batch * args.steps / (ms / 1e3), 1), "unit": "sequence-layer-steps/s",
-            "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
-            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f16 in, f32 accumulate (ordered)", "data": "synthetic",
-            "config": {"workload": "configs[4]: one selected-KV layer, KV heads sharded over the GPUs",
-                       "sequences": batch, "tokens": n, "alpha": args.alpha, "cap_ratio": 0.2,
-                       "kv_heads_per_gpu": g, "parallelism": f"KV-head shards x{world}",
-                       "exchange": ("peer memory: the library's kernels store thresholds, count records and "
-                                    "outputs into every rank's mailbox (CUDA IPC) with bounded flag waits"
-                                    if peer else "NCCL broadcast of thresholds, all-gather of count records and "
-                                                 "outputs"),
-                       "launch": "one CUDA graph per step"},
-            "exchange_status": exch_status,
-            "score_bytes_per_step": b_layer * batch, "selection": {"k_mean": float(res[:, 0].mean()),
-                                                                 "zero_selection": int((res[:, 0] == 0).sum())},
-            "clocks": clocks.summary()}
+    return line
+
+
+def shard_traffic(world):
+    p = ROOT / "profiles" / "score_batch_kernel_configs4_traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get(f"dram_bytes_per_launch_w{world}")
+        except (ValueError, OSError):
+            return None
+    return None
+
+
+def shard_cpu_baseline(layer, kshard, vshard, q16l, q32l, holder, args):
+    """configs[4]'s reference CPU path on the first SHARD_SAMPLE sequences of
+    the same data (copied from HBM), and the GPU's selections against it."""
+    from oracle import binding as ob
+
+    if not ob.reference_available():
+        return {"value": None, "unit": "layer-steps/s", "kind": "unavailable",
+                "sample": "oracle/_ref was not built"}, None
+    threads = min(128, os.cpu_count() or 1)
+    n, m = args.tokens, min(SHARD_SAMPLE, args.batch)
+    data = [(kshard[b].cpu().numpy().view(np.uint16).reshape(-1), vshard[b].cpu().numpy().view(np.uint16).reshape(-1),
+             q16l[b].cpu().numpy().view(np.uint16).reshape(-1), q32l[b].cpu().numpy().reshape(-1)) for b in range(m)]
+    shard_reference_step(data[:1], n, args.alpha, threads)  # warm-up
+    times = []
+    for _ in range(2):
+        t, results = shard_reference_step(data, n, args.alpha, threads)
+        times.append(t)
+    secs = float(np.mean(times))
+    base = {"value": round(m / secs, 3), "unit": "layer-steps/s", "cores": threads, "kind": "reference",
+            "sample": "2 steps of " + SHARD_REF_SAMPLE.format(m=m, b=args.batch, n=n, t=threads)}
+    res = holder["res"].cpu().numpy()
+    counts = layer.counts.cpu().numpy().astype(np.uint32)
+    ids = layer.ids.cpu().numpy().astype(np.uint64)
+    outs = holder["out"].cpu().numpy().astype(np.float64)
+    bad, worst = [], 0.0
+    for b, r in enumerate(results):
+        k = r["k"]
+        ok = int(res[b, 0]) == k and int(res[b, 1]) == r["tied"] and np.array_equal(counts[b], r["counts"])
+        ok = ok and np.array_equal(ids[b, :, :k], r["ids"][:, :k]) and int(res[b, 2]) == (70 if k == 0 else 0)
+        if not ok:
+            bad.append(b)
+        if k:
+            want = r["out"].astype(np.float64)
+            worst = max(worst, float(np.max(np.abs(outs[b] - want)) / (float(np.max(np.abs(want))) or 1.0)))
+    parity = {"sequences": list(range(m)), "bit_exact": not bad, "mismatched_sequences": bad,
+              "checked": "k, counts, boundary ties, status and ordered per-head IDs of the timed step's sequences "
+                         "vs the reference CPU path on the same data",
+              "attention_max_rel_err": round(worst, 7), "attention_tol": 2e-3,
+              "attention_vs": "the oracle's float port of the ggml attention graph"}
+    return base, parity
+
+
+def run_reference_sharded(args, rank, world, torch):
+    """The reference arm of configs[4]: the reference CPU path on a bounded
+    sample of the batch, its inputs rebuilt on the CPU.  Rank 0 only."""
+    from oracle import binding as ob
+
+    if rank != 0:
+        return None
+    if not ob.reference_available():
+        return {"impl": "reference", "unavailable": "oracle/_ref not built: reference sources were absent at build"}
+    threads = min(128, os.cpu_count() or 1)
+    n, m = args.tokens, min(SHARD_SAMPLE, args.batch)
+    t0 = time.perf_counter()
+    data = shard_cpu_sequences(n, m, threads)
+    gen_s = time.perf_counter() - t0
+    warm = max(args.warmup, 3)
+    for _ in range(warm):
+        shard_reference_step(data, n, args.alpha, threads)
+    secs, ks = 0.0, []
+    for _ in range(args.steps):
+        t, results = shard_reference_step(data, n, args.alpha, threads)
+        secs += t
+        ks = [r["k"] for r in results]
+    value = m * args.steps / secs
+    sample = SHARD_REF_SAMPLE.format(m=m, b=args.batch, n=n, t=threads)
+    return {"metric": METRIC, "value": round(value, 3), "unit": "layer-steps/s", "n_gpus": world,
+            "steps": args.steps, "warmup": warm, "ms_per_step": round(secs * 1e3 / args.steps, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f16 in, f32 accumulate (ordered)", "data": "synthetic", "impl": "reference",
+            "config": shard_config(args, world),
+            "selection": {"k_per_sequence": ks},
+            "cpu_baseline": {"value": round(value, 3), "unit": "layer-steps/s", "cores": threads, "kind": "reference",
+                             "sample": sample},
+            "inputs": f"rebuilt on the CPU by the oracle's restatement of the generator ({gen_s:.1f} s, untimed)",
+            "e2e": {"value": round(value, 3), "unit": "layer-steps/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
 
 
 def run_sweep(args, torch):
@@ -1449,7 +1662,10 @@ def main():
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
         dist = tdist
     if args.impl == "reference":
-        line = run_reference(args, rank, world, torch)
+        if args.workload == "kv-sharded":
+            line = run_reference_sharded(args, rank, world, torch)
+        else:
+            line = run_reference(args, rank, world, torch)
     elif args.workload == "sweep":
         line = run_sweep(args, torch)
     elif args.workload == "h2o":
@@ -1471,6 +1687,9 @@ def main():
             tdist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=120))
             dist = tdist
         line = run_sharded(args, rank, world, torch, dist)
+        if rank == 0 and world == 1 and not args.no_configs1:
+            # configs[1], the 32-layer decode step, as a second block of the line
+            line["configs1"] = run_ours(args, rank, world, torch, None)
     else:
         line = run_ours(args, rank, world, torch, dist)
     if rank == 0 and line is not None:

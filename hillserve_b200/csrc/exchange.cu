@@ -21,8 +21,8 @@
 // nothing is reset between steps.  Every wait is bounded (the group's limit,
 // 2 s by default): a wait that gives up records HSB_E_TIMEOUT in the
 // mailbox's status word and the kernel returns.  After a timeout the group's
-// epochs disagree: the mailboxes must be recreated.  No multicast object and
-// no TMA multicast are used: plain stores to peer memory only.
+// epochs disagree: the mailboxes must be recreated.  Every transfer is a
+// plain store by a thread into peer memory.
 #include <algorithm>
 #include <cmath>
 

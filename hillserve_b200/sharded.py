@@ -137,29 +137,38 @@ class KVHeadShardedLayer:
             self.workspace.numel(), stream), "shard select")
 
     # ------------------------------------------------------- peer memory
-    def step_peer(self, q16, q32, kshard, vshard, exchange: PeerExchange):
+    def step_peer(self, q16, q32, kshard, vshard, exchange: PeerExchange, marks=None):
         """The whole layer with the exchanges over peer memory: five launches
         on this rank (four on ranks other than 0), no collective.  Returns the
         mailbox's outputs [batch][32][128] and the combined selection records
         [batch][4] (k, boundary-tied heads summed over ranks, status code,
-        index); the exchange's own status is in exchange.status."""
+        index); the exchange's own status is in exchange.status.  marks: six
+        callables run on the current stream around the five phases (event
+        records, for a timeline)."""
         torch = self.torch
         stream = torch.cuda.current_stream().cuda_stream
         g = C.byref(exchange.group)
+        mark = (lambda i: marks[i]()) if marks else (lambda i: None)
+        mark(0)
         self.score(q16, kshard, stream)
+        mark(1)
         if self.geo.rank == 0:
             self._check(self.lib.hsb_exchange_threshold(_ptr(self.head0), C.c_float(self.alpha), g, stream),
                         "exchange threshold")
+        mark(2)
         self._check(self.lib.hsb_exchange_count(_ptr(self.keys), self.geo.heads, self.tokens, g, stream),
                     "exchange count")
+        mark(3)
         self._check(self.lib.hsb_shard_select(
             _ptr(self.keys), _ptr(self.scores), self.geo.kv_heads, self.tokens, self.batch, exchange.thr_ptr,
             exchange.records_ptr, HEADS, self.geo.head_base, C.c_float(self.alpha), C.c_float(self.ratio),
             _ptr(self.ids), self.count, _ptr(self.counts), _ptr(self.results), _ptr(q32), _ptr(kshard),
             _ptr(vshard), _ptr(self.k_packed), _ptr(self.v_packed), _ptr(self.out), _ptr(self.workspace),
             self.workspace.numel(), stream), "shard select")
+        mark(4)
         self._check(self.lib.hsb_exchange_finish(_ptr(self.out), _ptr(self.results), self.geo.heads, g, stream),
                     "exchange finish")
+        mark(5)
         res = exchange.results
         combined = res[0].clone()
         combined[:, 1] = res[:, :, 1].sum(dim=0)

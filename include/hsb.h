@@ -398,7 +398,7 @@ int hsb_shard_select(const uint16_t* d_order_keys, const uint16_t* d_raw, int kv
  * replay the step as is).  Every wait is bounded by wait_limit_ns (0: 2 s);
  * one that gives up writes HSB_E_TIMEOUT (index = the rank waited for) to the
  * mailbox's status word and the kernel returns -- the mailboxes must then be
- * recreated.  Plain peer loads and stores only: no multicast. */
+ * recreated.  Plain peer stores by threads only. */
 typedef struct hsb_mailbox_layout {
     size_t thr;      /* uint32 [batch][2]: threshold order key, status */
     size_t records;  /* uint32 [batch][32]: count | non-finite << 31 */

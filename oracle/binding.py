@@ -13,6 +13,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "_build" / "libhs_oracle.so"
 REF_SO = HERE / "_ref" / "libhs_ref.so"
+REF_RUNTIME_SO = HERE / "_ref" / "libhs_ref_runtime.so"
 
 P = C.c_void_p
 SZ = C.c_size_t
@@ -302,6 +303,47 @@ def synth_keys(tokens: int, seed: int, heavy_fraction: float = 0.02, heavy_scale
     out = np.zeros(tokens * stride, dtype=np.uint16)
     oracle().orc_synth_keys(_p(out), tokens, stride, seed, heavy_fraction, heavy_scale, int(rope), theta, threads)
     return out
+
+
+_ref_runtime = None
+
+
+def ref_runtime_available() -> bool:
+    return REF_RUNTIME_SO.exists()
+
+
+def ref_runtime_decode(rows: np.ndarray, capacity: int, prompt: int, steps: int, layer: int, beta: float,
+                       alpha: float, rehearsal: np.ndarray, workdir: str) -> dict:
+    """Drives the reference FullGqaRuntimePolicy (oracle/_ref, compiled from
+    its sources) through `steps` decode steps of one layer after a prompt of
+    `prompt` positions: per step the payload cover its prepare_history
+    publishes (full_gqa_runtime.cpp:299-344) and its final selection
+    (:549-585).  rows: [capacity][2048] K||V F16 bits; rehearsal: [steps][4096]
+    F32 selection queries."""
+    global _ref_runtime
+    if _ref_runtime is None:
+        lib = C.CDLL(str(REF_RUNTIME_SO))
+        lib.ref_runtime_decode.argtypes = [C.c_char_p, SZ, SZ, SZ, C.c_int, C.c_double, C.c_float, P, P, P, P, SZ, P,
+                                           P, P, SZ, P, P, SZ, C.c_char_p, SZ]
+        _ref_runtime = lib
+    cap_max = max(1, int(np.floor((prompt + steps + 1) * 0.2)) + 1)
+    phys_max, k_max = prompt + steps + 1, cap_max
+    rows = np.ascontiguousarray(rows, dtype=np.uint16)
+    q = np.ascontiguousarray(rehearsal, dtype=np.float32)
+    bound = np.zeros(steps, dtype=np.uint64)
+    cover = np.zeros((steps, 32, cap_max), dtype=np.uint64)
+    phys = np.zeros((steps, phys_max), dtype=np.uint64)
+    nphys = np.zeros(steps, dtype=np.uint64)
+    cold = np.zeros((steps, phys_max), dtype=np.uint8)
+    k = np.zeros(steps, dtype=np.uint64)
+    final = np.zeros((steps, 32, k_max), dtype=np.uint64)
+    e = _err()
+    if _ref_runtime.ref_runtime_decode(workdir.encode(), capacity, prompt, steps, layer, beta, alpha, _p(rows),
+                                       _p(q), _p(bound), _p(cover), cap_max, _p(phys), _p(nphys), _p(cold), phys_max,
+                                       _p(k), _p(final), k_max, e, 512):
+        raise ReferenceError_(e.value.decode())
+    return {"bound": bound, "cover": cover, "physical": phys, "nphysical": nphys, "cold": cold, "k": k,
+            "final": final}
 
 
 def _err():

@@ -3,7 +3,7 @@ own CPU code (oracle/_ref/libhs_ref.so, compiled from the HillServe sources by
 oracle/Makefile) on seeded inputs.  Run here, where the reference sources
 exist:
 
-    make -C oracle && python tests/golden/make_golden.py [--only h2o|records|history]
+    make -C oracle && python tests/golden/make_golden.py [--only h2o|records|history|runtime]
 
 Inputs are regenerated bit-exactly from their seeds by tests/inputs.py, so
 the fixtures hold only input digests and the reference's outputs.
@@ -148,8 +148,62 @@ def history_plans() -> None:
     np.savez_compressed(OUT / "history_plans.npz", slots_digest=np.array(digests), hot_tokens=np.array(hots))
 
 
+# Decode cases run through the reference's own FullGqaRuntimePolicy:
+# (seed, capacity, prompt, steps, layer, beta, alpha).  Alphas are chosen so
+# that no step selects nothing (the runtime throws there) and some steps stay
+# below the 20 % cap.
+RUNTIME_CASES = ((5, 192, 128, 3, 3, 1.0, 4.0), (6, 1088, 1024, 4, 2, 0.25, 3.0), (7, 4160, 4096, 2, 7, 1.0, 3.0),
+                 (8, 640, 576, 3, 5, 0.5, 4.0), (9, 2112, 2048, 3, 4, 1.0, 6.0))
+
+
+def runtime_rows(seed: int, capacity: int) -> np.ndarray:
+    """K||V rows [capacity][2048] (F16 bits) of a runtime case: K ~ N(0,1)
+    with heavy rows x4, V ~ N(0,1) (tests/inputs.py streams)."""
+    k = inputs.normals(seed, capacity * 1024, stream=2).reshape(capacity, 1024)
+    k[inputs.heavy_rows(seed, capacity)] *= 4.0
+    rows = np.empty((capacity, 2048), dtype=np.uint16)
+    rows[:, :1024] = inputs.f16_bits(k)
+    rows[:, 1024:] = inputs.values(seed, capacity).reshape(capacity, 1024)
+    return rows
+
+
+def runtime_queries(seed: int, steps: int) -> np.ndarray:
+    """F16-exact F32 rehearsal queries [steps][4096] of a runtime case."""
+    return np.stack([inputs.f16_bits(inputs.normals(seed * 100 + s, 4096, stream=1)).view(np.float16)
+                     .astype(np.float32) for s in range(steps)])
+
+
+def runtime_vectors() -> None:
+    import tempfile
+
+    assert ob.ref_runtime_available(), "build oracle/_ref/libhs_ref_runtime.so first (make -C oracle)"
+    fields = {"cases": np.array(RUNTIME_CASES, dtype=np.float64)}
+    for i, (seed, cap, prompt, steps, layer, beta, alpha) in enumerate(RUNTIME_CASES):
+        rows = runtime_rows(seed, cap)
+        q = runtime_queries(seed, steps)
+        with tempfile.TemporaryDirectory() as d:
+            r = ob.ref_runtime_decode(rows, cap, prompt, steps, layer, beta, alpha, q, d)
+        b = int(r["bound"].max())
+        kmax = int(r["k"].max())
+        fields[f"c{i}_input_digest"] = np.array(inputs.digest(rows, q))
+        fields[f"c{i}_bound"] = r["bound"]
+        fields[f"c{i}_cover"] = r["cover"][:, :, :b].astype(np.uint32)
+        fields[f"c{i}_nphysical"] = r["nphysical"]
+        fields[f"c{i}_physical"] = r["physical"][:, :int(r["nphysical"].max())].astype(np.uint32)
+        fields[f"c{i}_cold"] = r["cold"][:, :int(r["nphysical"].max())]
+        fields[f"c{i}_k"] = r["k"]
+        fields[f"c{i}_final"] = r["final"][:, :, :kmax].astype(np.uint32)
+        print("runtime case", i, "bound", r["bound"].tolist(), "k", r["k"].tolist(), "physical",
+              r["nphysical"].tolist())
+    np.savez_compressed(OUT / "runtime_decode.npz", **fields)
+
+
 def main() -> None:
     assert ob.reference_available(), "build oracle/_ref first (make -C oracle)"
+    if sys.argv[1:] == ["--only", "runtime"]:
+        runtime_vectors()
+        print("runtime fixture written to", OUT)
+        return
     if sys.argv[1:] == ["--only", "history"]:
         history_plans()
         print("history fixture written to", OUT)
@@ -164,6 +218,8 @@ def main() -> None:
         return
     records_vectors()
     history_plans()
+    if ob.ref_runtime_available():
+        runtime_vectors()
     # ---- 0. H2O group sums through the reference's CPU policy
     h2o_vectors()
     # ---- 1. reference scorer test vectors

@@ -172,3 +172,48 @@ def test_history_protocol_rejections(cuda):
         torch.cuda.synchronize()
         assert int(st[0].item()) == 52  # HSB_E_MAP_MISS
     hist.close()
+
+
+@pytest.mark.parametrize("i", [0, 1, 2, 3, 4])
+def test_history_matches_reference_runtime(cuda, i):
+    """The GPU decode history against the reference's own runtime outputs
+    (tests/golden/runtime_decode.npz, made by running FullGqaRuntimePolicy
+    from the reference sources): per step the cover's bound and its cold
+    positions (the rows the runtime reads from the cold tier) after
+    prepare, and the final per-head selection after the current token's
+    append -- bit for bit."""
+    import sys
+    from pathlib import Path
+
+    import torch
+    import hillserve_b200 as hsb
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
+    import make_golden as mg
+
+    fx = np.load(Path(__file__).resolve().parent / "golden" / "runtime_decode.npz", allow_pickle=False)
+    seed, cap, prompt, steps, layer, beta, alpha = [t(x) for t, x in zip((int,) * 5 + (float, float),
+                                                                          mg.RUNTIME_CASES[i])]
+    rows = mg.runtime_rows(seed, cap)
+    q = mg.runtime_queries(seed, steps)
+    hist = hsb.History(layer + 1, cap, prompt, steps, beta=beta, alpha=alpha)
+    hist.append(layer, 0, _dev(rows[:prompt], torch.int16))
+    for s in range(steps):
+        pos = prompt + s
+        qd = _dev(q[s].astype(np.float16).view(np.uint16).reshape(32, 128), torch.int16)
+        hist.prepare_history(layer, pos, qd)
+        got_cold, got_bound = hist.cover(layer)
+        assert got_bound == int(fx[f"c{i}_bound"][s])
+        n = int(fx[f"c{i}_nphysical"][s])
+        phys = fx[f"c{i}_physical"][s][:n].astype(np.int64)
+        want_cold = phys[fx[f"c{i}_cold"][s][:n].astype(bool)]
+        assert np.array_equal(got_cold.cpu().numpy().astype(np.int64), want_cold)
+        hist.append(layer, pos, _dev(rows[pos:pos + 1], torch.int16))
+        gids, _, res = hist.select(layer, pos, qd)
+        k = int(fx[f"c{i}_k"][s])
+        r = res.cpu().numpy()
+        assert r[0] == k and r[2] == 0, r
+        assert np.array_equal(gids[:, :k].cpu().numpy().astype(np.uint32), fx[f"c{i}_final"][s][:, :k])
+        staged = got_cold.cpu().numpy().astype(np.int64)
+        hist.fetch(layer, gids, res, got_cold, _dev(rows[staged], torch.int16), (k + 31) // 32 * 32)
+    hist.close()
