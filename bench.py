@@ -59,7 +59,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-configs1", action="store_true", help="kv-sharded at N=1: skip the configs[1] block")
     ap.add_argument("--workload", default="kv-sharded",
-                    choices=["decode", "kv-sharded", "sweep", "h2o", "records", "history", "executor"],
+                    choices=["decode", "kv-sharded", "sweep", "h2o", "records", "history", "executor", "rehearsal"],
                     help="kv-sharded (the headline at every N): configs[4], one selected-KV layer over --batch "
                          "sequences with the KV heads split over the ranks, plus (N=1) a configs[1] block; decode: "
                          "configs[1] alone, the 32-layer decode step; sweep: configs[2], "
@@ -68,7 +68,7 @@ def parse():
                          "cold-tier KV record encoder and verifier (FNV-1a) beside the reference's CPU checksum; "
                          "history: the hot/cold decode history protocol (prepare/select/fetch) per layer; executor: "
                          "the model-facing decode step (current-KV append + selection + attention over live slots) "
-                         "beside the reference executor's padded upload")
+                         "beside the reference executor's padded upload; rehearsal: configs[3], the rehearsal prefetch step")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="kv-sharded: cross-GPU exchanges over peer memory (own kernels) or NCCL collectives")
@@ -1024,6 +1024,139 @@ def run_reference_sharded(args, rank, world, torch):
                     "d2h_bytes_per_step": 0}}
 
 
+def run_rehearsal(args, torch):
+    """configs[3], the rehearsal prefetch step at N = 32768: the rehearsal
+    query q = RoPE_N(W_q x) (x bf16 [4096] ~ N(0,1), W_q bf16 [4096][4096] ~
+    N(0, 0.02): 32 MiB, hsb_rehearsal_query) cast to F16, scored against the
+    HBM keys (hsb_score_with_keys), selected (hsb_select_keys, alpha 5: the
+    reference runtime's default, so that rows move), the physical union
+    (hsb_union), and the union's K||V rows staged from a pinned-host cold
+    tier into HBM (hsb_stage_rows, one device-side count, no host round
+    trip).  One CUDA graph per step; events between the stages."""
+    import hillserve_b200 as hsb
+
+    lib = hsb._capi.lib()
+    P = hsb._ptr
+    dev = torch.device("cuda")
+    n, alpha = args.tokens, 5.0
+    s0 = torch.cuda.current_stream().cuda_stream
+    x = torch.empty(4096, dtype=torch.int16, device=dev)
+    w = torch.empty(4096 * 4096, dtype=torch.int16, device=dev)
+    lib.hsb_synth_normal_bf16(x.data_ptr(), 4096, 31, 1.0, s0)
+    lib.hsb_synth_normal_bf16(w.data_ptr(), 4096 * 4096, 32, 0.02, s0)
+    kc = torch.empty(n * 1024, dtype=torch.int16, device=dev)
+    vc = torch.empty(n * 1024, dtype=torch.int16, device=dev)
+    lib.hsb_synth_keys(kc.data_ptr(), n, 1024, 33, 0.02, 4.0, 1, THETA, s0)
+    lib.hsb_synth_keys(vc.data_ptr(), n, 1024, 34, 0.0, 1.0, 0, THETA, s0)
+    rows = torch.empty((n, 2048), dtype=torch.int16, device=dev)
+    rows[:, :1024].copy_(kc.view(n, 1024))
+    rows[:, 1024:].copy_(vc.view(n, 1024))
+    cold = rows.cpu().pin_memory()  # the pinned-host cold tier: K||V rows, 4096 B each
+    del rows
+    q32 = torch.empty(4096, dtype=torch.float32, device=dev)
+    q16 = torch.empty(4096, dtype=torch.int16, device=dev)
+    scores = torch.empty((HEADS, n), dtype=torch.int16, device=dev)
+    keys = torch.empty((HEADS, n), dtype=torch.int16, device=dev)
+    kcap = hsb.select_kmax(n, 0.2)
+    ids = torch.empty((HEADS, kcap), dtype=torch.int32, device=dev)
+    counts = torch.zeros(HEADS, dtype=torch.int32, device=dev)
+    res = torch.zeros(4, dtype=torch.int32, device=dev)
+    ws_sel = hsb._workspace(lib.hsb_select_workspace_bytes(HEADS, n, n, kcap), dev)
+    ws_uni = hsb._workspace(lib.hsb_union_workspace_bytes(n), dev)
+    physical = torch.empty(n, dtype=torch.int32, device=dev)
+    nphys = torch.zeros(1, dtype=torch.int32, device=dev)
+    st = torch.zeros(2, dtype=torch.int32, device=dev)
+    staged = torch.empty(n * 4096, dtype=torch.uint8, device=dev)
+    ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(6)]
+
+    def body(stream, marks):
+        sp = stream.cuda_stream
+        mark = (lambda i: ev[i].record(stream)) if marks else (lambda i: None)
+        mark(0)
+        rc = lib.hsb_rehearsal_query(P(x), P(w), n, ctypes.c_float(THETA), P(q32), P(q16), sp)
+        mark(1)
+        rc |= lib.hsb_score_with_keys(P(q16), P(kc), n, 1024, P(scores), P(keys), sp)
+        mark(2)
+        rc |= lib.hsb_select_keys(P(keys), P(scores), HEADS, n, n, ctypes.c_float(alpha), ctypes.c_float(0.2), 0,
+                                  P(ids), kcap, P(counts), P(res), P(ws_sel), ws_sel.numel(), sp)
+        mark(3)
+        rc |= lib.hsb_union(P(ids), kcap, P(res), 0, n, P(physical), P(nphys), P(st), P(ws_uni), ws_uni.numel(), sp)
+        mark(4)
+        rc |= lib.hsb_stage_rows(ctypes.c_void_p(cold.data_ptr()), P(physical), P(nphys), n, P(staged), sp)
+        mark(5)
+        assert rc == 0, lib.hsb_last_error()
+
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        body(stream, False)
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        body(stream, False)
+    gp = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gp, stream=stream):
+        body(stream, True)
+    for _ in range(max(3, args.warmup)):
+        g.replay()
+    torch.cuda.synchronize()
+    steps = max(10, min(args.steps, 200))
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        with torch.cuda.stream(stream):
+            a.record(stream)
+            for _ in range(steps):
+                g.replay()
+            b.record(stream)
+        b.synchronize()
+    ms = a.elapsed_time(b) / steps
+    reps = []
+    for _ in range(5):
+        with torch.cuda.stream(stream):
+            gp.replay()
+        stream.synchronize()
+        reps.append([ev[i].elapsed_time(ev[i + 1]) for i in range(5)])
+    stage = np.median(np.array(reps), axis=0)
+    names = ["rehearsal_gemv", "score", "select", "union", "stage_rows_from_pinned_host"]
+    k, u = int(res[0].item()), int(nphys.item())
+    peak, peak_kind = peaks()
+    b_gemv = 4096 * 4096 * 2 + 4096 * 2 + 4096 * 6  # W_q, x, q F32 + F16 out
+    gemv_gbs = b_gemv / (stage[0] / 1e3) / 1e9
+    pcie_gbs = 4096 * u / (stage[4] / 1e3) / 1e9 if stage[4] > 0 else None
+    line = {"metric": "configs[3] rehearsal prefetch step at N=32K", "impl": "ours", "workload": "rehearsal",
+            "unit": "us per step", "value": round(ms * 1e3, 2), "higher_is_better": False, "data": "synthetic",
+            "config": {"workload": "configs[3]: rehearsal q = RoPE_N(W_q x), F16 -> score K[32768,8,128] -> "
+                                   "select (alpha 5) -> union -> stage the union's rows from pinned host memory",
+                       "tokens": n, "alpha": alpha},
+            "stages_us": {nm: round(float(v) * 1e3, 2) for nm, v in zip(names, stage)},
+            "selection": {"k": k, "union_rows": u, "pcie_bytes": 4096 * u},
+            "rehearsal_gemv": {"bytes": b_gemv, "GB_s": round(gemv_gbs, 1), "frac_of_peak": round(gemv_gbs / peak, 4),
+                               "peak_GB_s": peak, "peak_kind": peak_kind},
+            "stage_rows_GB_s_over_pcie": round(pcie_gbs, 1) if pcie_gbs else None,
+            "gpu_launches": 5 * steps, "clocks": clocks.summary()}
+    if not args.no_cpu_baseline:
+        from oracle import binding as ob
+
+        if ob.reference_available():
+            threads = min(128, os.cpu_count() or 1)
+            xh, wh = x.cpu().numpy().view(np.uint16), w.cpu().numpy().view(np.uint16)
+            kh, vh = kc.cpu().numpy().view(np.uint16), vc.cpu().numpy().view(np.uint16)
+            t0 = time.perf_counter()
+            qd = ob.rehearsal(xh, wh, n, THETA)
+            t1 = time.perf_counter()
+            q16h = qd.astype(np.float32).astype(np.float16).view(np.uint16)
+            dt, r = reference_layer(kh, vh, q16h, qd.astype(np.float32), n, alpha, threads, True)
+            line["cpu_baseline"] = {"value": round(((t1 - t0) + dt) * 1e6, 1), "unit": "us per step",
+                                    "cores": threads, "kind": "reference",
+                                    "sample": "one step: the oracle's FP64 rehearsal GEMV + RoPE (1 core; the "
+                                              "reference's is ggml on the GPU), then the reference CPU path "
+                                              "(FullGqaCpuScorer, select_gqa_scores, union, pack; oracle/_ref) "
+                                              "and the oracle's attention port",
+                                    "rehearsal_s": round(t1 - t0, 4), "select_path_s": round(dt, 4)}
+    g.reset()
+    gp.reset()
+    return line
+
+
 def run_sweep(args, torch):
     """latency and HBM GB/s of one selected-KV layer step
     (score -> select -> gather + attention) per length N, the configs[0]
@@ -1668,6 +1801,8 @@ def main():
             line = run_reference(args, rank, world, torch)
     elif args.workload == "sweep":
         line = run_sweep(args, torch)
+    elif args.workload == "rehearsal":
+        line = run_rehearsal(args, torch)
     elif args.workload == "h2o":
         line = run_h2o(args, torch)
     elif args.workload == "records":

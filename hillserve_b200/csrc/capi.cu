@@ -484,7 +484,8 @@ int hsb_rehearsal_query(const uint16_t* d_x, const uint16_t* d_w, uint64_t posit
                         uint16_t* d_q_f16, void* stream) {
     if (!d_x || !d_w || (!d_q_f32 && !d_q_f16) || !(theta > 0.0f) || !std::isfinite(theta))
         return fail(HSB_E_INVALID, "rehearsal arguments");
-    if (!aligned(d_w, 16)) return fail(HSB_E_INVALID, "rehearsal weights must be 16-byte aligned");
+    if (!aligned(d_w, 16) || !aligned(d_x, 16))
+        return fail(HSB_E_INVALID, "rehearsal weights and activation must be 16-byte aligned");
     cudaError_t e = launch_rehearsal(d_x, d_w, position, theta, d_q_f32, d_q_f16, as_stream(stream));
     if (e != cudaSuccess) return fail_cuda(e, "rehearsal launch");
     g_last_error.clear();

@@ -166,10 +166,12 @@ __global__ void __launch_bounds__(kThrThreads) exch_threshold_kernel(const uint3
 }
 
 constexpr int kCntThreads = 1024;
-// Every rank, CTA = (sequence, local head): wait for the thresholds, count
-// #{keys >= threshold key} | non-finite << 31 and store the record into
-// every rank's mailbox (column head_base + head); the last CTA releases this
-// rank's rec_flag and then waits for every rank's records.
+// Every rank: wait for the thresholds, then for each (sequence, local head)
+// item count #{keys >= threshold key} | non-finite << 31 and store the record
+// into every rank's mailbox (column head_base + head).  A persistent grid (at
+// most two CTAs per SM) walks the items, so the flag wait and the
+// system-scope fence are paid once per CTA, not once per item; the last CTA
+// releases this rank's rec_flag and waits for every rank's records.
 __global__ void __launch_bounds__(kCntThreads) exch_count_kernel(const uint16_t* keys, unsigned long long tokens,
                                                                  unsigned heads, unsigned head_base,
                                                                  const __grid_constant__ PeerParams p) {
@@ -177,49 +179,54 @@ __global__ void __launch_bounds__(kCntThreads) exch_count_kernel(const uint16_t*
     const unsigned long long epoch = step_epoch(p);
     MailboxHeader* own = header(p, p.rank);
     __shared__ int ready;
+    __shared__ unsigned int scnt, sbad;
     if (threadIdx.x == 0) ready = wait_flag(&own->thr_flag, epoch, p.limit_ns);
     __syncthreads();
     if (!ready) {
         if (threadIdx.x == 0) raise_status(&own->status, HSB_E_TIMEOUT, 0);
         return;  // the group's epochs now disagree: the mailboxes must be recreated
     }
-    const unsigned seq = blockIdx.x / heads, head = blockIdx.x % heads;
-    const unsigned int thr_key = __ldcg(reinterpret_cast<const uint32_t*>(p.mb[p.rank] + p.lay.thr) + 2 * seq);
-    __shared__ unsigned int scnt, sbad;
-    if (threadIdx.x == 0) {
-        scnt = 0;
-        sbad = 0;
-    }
-    __syncthreads();
-    const uint16_t* row = keys + (unsigned long long)blockIdx.x * tokens;
     const bool vec = tokens % 8 == 0 && (reinterpret_cast<uintptr_t>(keys) & 15) == 0;
     const unsigned long long n8 = vec ? tokens / 8 : 0;
-    unsigned int cnt = 0, bad = 0;
-    for (unsigned long long g = threadIdx.x; g < n8; g += kCntThreads) {
-        const uint4 w = reinterpret_cast<const uint4*>(row)[g];
-        const uint32_t v[4] = {w.x, w.y, w.z, w.w};
+    const uint32_t* thr = reinterpret_cast<const uint32_t*>(p.mb[p.rank] + p.lay.thr);
+    const unsigned long long items = p.batch * heads;
+    for (unsigned long long item = blockIdx.x; item < items; item += gridDim.x) {
+        const unsigned seq = (unsigned)(item / heads), head = (unsigned)(item % heads);
+        const unsigned int thr_key = __ldcg(thr + 2 * seq);
+        if (threadIdx.x == 0) {
+            scnt = 0;
+            sbad = 0;
+        }
+        __syncthreads();
+        const uint16_t* row = keys + item * tokens;
+        unsigned int cnt = 0, bad = 0;
+        for (unsigned long long g = threadIdx.x; g < n8; g += kCntThreads) {
+            const uint4 w = reinterpret_cast<const uint4*>(row)[g];
+            const uint32_t v[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const uint32_t key = (v[j >> 1] >> (16 * (j & 1))) & 0xffffu;
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t key = (v[j >> 1] >> (16 * (j & 1))) & 0xffffu;
+                bad |= key_nonfinite(key);
+                cnt += (!key_nan(key) && key >= thr_key) ? 1u : 0u;
+            }
+        }
+        for (unsigned long long i = n8 * 8 + threadIdx.x; i < tokens; i += kCntThreads) {
+            const uint32_t key = row[i];
             bad |= key_nonfinite(key);
             cnt += (!key_nan(key) && key >= thr_key) ? 1u : 0u;
         }
-    }
-    for (unsigned long long i = n8 * 8 + threadIdx.x; i < tokens; i += kCntThreads) {
-        const uint32_t key = row[i];
-        bad |= key_nonfinite(key);
-        cnt += (!key_nan(key) && key >= thr_key) ? 1u : 0u;
-    }
-    cnt = __reduce_add_sync(0xffffffffu, cnt);
-    bad = __any_sync(0xffffffffu, bad);
-    if ((threadIdx.x & 31) == 0) {
-        if (cnt) atomicAdd(&scnt, cnt);
-        if (bad) atomicOr(&sbad, 1u);
-    }
-    __syncthreads();
-    if (threadIdx.x < (unsigned)p.world) {
-        uint32_t* rec = reinterpret_cast<uint32_t*>(p.mb[threadIdx.x] + p.lay.rec);
-        rec[(size_t)seq * kHeads + head_base + head] = scnt | (sbad << 31);
+        cnt = __reduce_add_sync(0xffffffffu, cnt);
+        bad = __any_sync(0xffffffffu, bad);
+        if ((threadIdx.x & 31) == 0) {
+            if (cnt) atomicAdd(&scnt, cnt);
+            if (bad) atomicOr(&sbad, 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x < (unsigned)p.world) {
+            uint32_t* rec = reinterpret_cast<uint32_t*>(p.mb[threadIdx.x] + p.lay.rec);
+            rec[(size_t)seq * kHeads + head_base + head] = scnt | (sbad << 31);
+        }
+        __syncthreads();  // scnt / sbad are reset for the next item
     }
     if (last_cta(&own->arrive[1])) {
         release_all(p, offsetof(MailboxHeader, rec_flag) + 8 * p.rank, epoch);
@@ -302,8 +309,10 @@ cudaError_t launch_exchange_count(const uint16_t* keys, size_t heads, size_t tok
                                   cudaStream_t stream) {
     PeerParams p{};
     if (!peer_params(g, &p) || heads * g->world != kHeads) return cudaErrorInvalidValue;
-    return launch_dependent(exch_count_kernel, dim3((unsigned)(heads * g->batch)), dim3(kCntThreads), 0, stream, false,
-                            keys, (unsigned long long)tokens, (unsigned)heads, (unsigned)(heads * g->rank), p);
+    const DeviceInfo& dev = device_info();
+    const unsigned grid = (unsigned)std::min<unsigned long long>(heads * g->batch, (unsigned long long)dev.sms * 2);
+    return launch_dependent(exch_count_kernel, dim3(grid), dim3(kCntThreads), 0, stream, false, keys,
+                            (unsigned long long)tokens, (unsigned)heads, (unsigned)(heads * g->rank), p);
 }
 
 cudaError_t launch_exchange_finish(const float* out, const hsb_selection* results, size_t heads,

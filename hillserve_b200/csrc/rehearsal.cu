@@ -28,7 +28,22 @@ __global__ void __launch_bounds__(kRThreads) rehearsal_kernel(const uint16_t* __
                                                               float* __restrict__ q32,
                                                               uint16_t* __restrict__ q16) {
     __shared__ __align__(16) float xs[kEmbed];
-    for (int i = threadIdx.x; i < kEmbed; i += kRThreads) xs[i] = bf16_value(x[i]);
+    {  // x in one round trip: every thread's 16-byte loads first, then the stores
+        constexpr int kPer = kEmbed / 8 / kRThreads;  // 16-byte pieces per thread
+        uint4 xv[kPer];
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) xv[u] = reinterpret_cast<const uint4*>(x)[threadIdx.x + u * kRThreads];
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int e = (threadIdx.x + u * kRThreads) * 8;
+            const uint32_t w[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                xs[e + 2 * j] = bf16_value(w[j] & 0xffffu);
+                xs[e + 2 * j + 1] = bf16_value(w[j] >> 16);
+            }
+        }
+    }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pair = blockIdx.x * 8 + warp;  // 0..2047

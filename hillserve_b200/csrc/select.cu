@@ -705,12 +705,89 @@ __device__ __forceinline__ void cluster_wait_acquire() {
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// 80 registers, no spills (a two-CTAs-per-SM bound forced 64 and spilled).
-// One selector CTA per SM is all the grid needs (32 heads x 4 CTAs <= 148
-// SMs), and 512 x 80 registers still leave room for one early-resident CTA
-// of the next layer's scorer (288 x 72).  Measured 0.7638 -> 0.7543 ms.
-__global__ void __cluster_dims__(kCluster, 1, 1) __maxnreg__(80)
-    select_cluster_kernel(const __grid_constant__ SelectParams p) {
+// The fold of warp 0 of a selector CTA: the per-head counts (4 heads per
+// lane; from the grid barrier's words, or from the exchanged records in
+// record mode), each rounded to F16 (or kept in F32), the first failing head
+// in head order (non-finite before count overflow within a head), and k from
+// the F16 mean and the ratio cap.  The rounded counts are integers below
+// 2^16 and there are at most 128 of them, so every partial sum is an integer
+// below 2^24 and exact in FP32: the tree sum equals the reference's
+// sequential FP32 sum (gqa_policy.cpp:60) bit for bit.
+struct CountFold {
+    unsigned long long k;
+    unsigned int status, index;
+    uint32_t own;  // this CTA's head's count
+};
+__device__ __forceinline__ CountFold fold_counts(const SelectParams& p, uint32_t seqb, uint32_t h,
+                                                 unsigned long long n, const unsigned long long word[4],
+                                                 int timeout) {
+    const int lane = threadIdx.x & 31;
+    const bool ext = p.ext != nullptr;
+    const uint32_t nh = ext ? p.heads_total : p.heads, own_head = ext ? p.head_base + h : h;
+    unsigned int e[4] = {0, 0, 0, 0};
+    float rr[4] = {0.f, 0.f, 0.f, 0.f};
+    unsigned long long own = 0;
+    if (!timeout) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t hh = lane * 4 + j;
+            if (hh < nh) {
+                unsigned long long c;
+                uint32_t nonfinite;
+                if (ext) {
+                    const uint32_t rec = __ldg(p.ext + seqb * p.heads_total + hh);
+                    c = rec & 0x7fffffffu;
+                    nonfinite = rec >> 31;
+                } else {
+                    c = word[j] >> 16;
+                    nonfinite = ((word[j] >> 8) & 255ull) ? 1u : 0u;
+                }
+                if (p.cover) c += 1;  // at most one newly appended current token
+                const float rounded = p.fp32_counts ? (float)c : half_value(half_bits((float)c));
+                e[j] = nonfinite | (isfinite(rounded) ? 0u : 2u);
+                rr[j] = rounded;
+                if (hh == own_head) own = c;
+            }
+        }
+    }
+    CountFold f{};
+    f.own = __reduce_max_sync(0xffffffffu, (unsigned int)own);
+    unsigned int my_status = 0, my_index = 0;
+#pragma unroll
+    for (int j = 3; j >= 0; --j) {
+        if (e[j]) {
+            my_status = (e[j] & 1u) ? HSB_E_SEL_NONFINITE : (p.cover ? HSB_E_COVER_COUNT : HSB_E_SEL_COUNT_F16);
+            my_index = lane * 4 + j;
+        }
+    }
+    const unsigned int failing = __ballot_sync(0xffffffffu, my_status != 0);
+    if (failing) {
+        const int src = __ffs(failing) - 1;
+        f.status = __shfl_sync(0xffffffffu, my_status, src);
+        f.index = __shfl_sync(0xffffffffu, my_index, src);
+    }
+    float total = (rr[0] + rr[1]) + (rr[2] + rr[3]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+    if (!timeout && !f.status) {
+        const float mean = p.fp32_counts ? __fdiv_rn(total, (float)nh)
+                                         : half_value(half_bits(__fdiv_rn(total, (float)nh)));
+        if (p.cover) {
+            if (!(isfinite(mean) && mean >= 1.0f)) f.status = HSB_E_COVER_MEAN;
+            else f.k = min(p.cover_cap, (unsigned long long)mean);
+        } else {
+            if (!isfinite(mean)) f.status = HSB_E_SEL_MEAN_F16;
+            else {
+                const unsigned long long cap = (unsigned long long)floor((double)n * (double)p.ratio);
+                f.k = min((unsigned long long)mean, min(cap, n));
+            }
+        }
+    }
+    return f;
+}
+
+// The cluster selector's body, shared by its two launch shapes below.
+__device__ __forceinline__ void select_cluster_body(const SelectParams& p) {
     pdl_wait();
     pdl_trigger();
     extern __shared__ __align__(16) unsigned char dyn[];
@@ -751,6 +828,42 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __maxnreg__(80)
     }
     for (int i = tid; i < 1024; i += kCThreads) sh.coarse[i] = 0;
     if (tid < 64) sh.fine[tid] = 0;
+    // Record mode (shard steps): k follows from the exchanged records alone,
+    // so a sequence whose threshold record carries an error, or which
+    // selects nothing, is settled before any of its keys is loaded -- with
+    // the same outputs as the full path below.
+    if (p.ext != nullptr) {
+        const int status0 = (int)p.ext_thr[2 * seqb + 1];
+        if (warp == 0 && !status0) {
+            const unsigned long long none[4] = {0, 0, 0, 0};
+            const CountFold f = fold_counts(p, seqb, h, p.valid, none, 0);
+            unsigned int status = f.status;
+            if (!status && f.k == 0 && p.zero_is_error) status = HSB_E_ZERO_SELECTION;
+            if (lane == 0) {
+                sh.k = status ? 0 : f.k;
+                sh.status = status;
+                sh.status_index = f.index;
+                sh.cnt = f.own;
+            }
+        }
+        __syncthreads();
+        if (status0 || sh.k == 0) {
+            if (status0) {
+                if (seq_first && tid == 0) {
+                    result->k = 0;
+                    result->status.code = status0;
+                    result->status.index = 0;
+                }
+            } else if (tid == 0) {
+                if (r == 0 && p.counts) p.counts[seqb * p.heads + h] = sh.cnt;
+                if (seq_first && sh.status) raise_status(&result->status, (int)sh.status, (int)sh.status_index);
+            }
+            if (p.ga.out && r == 0)
+                for (int d = tid; d < kDim; d += kCThreads) p.ga.out[(seqb * p.heads + h) * kDim + d] = 0.0f;
+            return;  // the whole cluster takes this branch (one k per sequence)
+        }
+        if (tid == 0) sh.cnt = 0;
+    }
     __syncthreads();
 
     // ---- 1. head-0 maximum over the whole row (every CTA, from L2), own
@@ -909,7 +1022,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __maxnreg__(80)
         // the words it read are the counts (no second read, no fence: the
         // data is the atomic itself).
         int timeout = 0;
-        const uint32_t nh = ext ? p.heads_total : p.heads, own_head = ext ? p.head_base + h : h;
+        const uint32_t nh = ext ? p.heads_total : p.heads;
         unsigned long long word[4] = {0, 0, 0, 0};
         if (!ext) {
             if (lane == 0)
@@ -932,74 +1045,10 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __maxnreg__(80)
         }
         timeout = __any_sync(0xffffffffu, timeout);
         if (lane == 0) sh.timeout = timeout;
-        // Per-head counts (4 heads per lane), F16 rounding, fold in head order.
-        unsigned int e[4] = {0, 0, 0, 0};
-        float rr[4] = {0.f, 0.f, 0.f, 0.f};
-        unsigned long long own = 0;
-        if (!timeout) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const uint32_t hh = lane * 4 + j;
-                if (hh < nh) {
-                    unsigned long long c;
-                    uint32_t nonfinite;
-                    if (ext) {
-                        const uint32_t rec = __ldg(p.ext + seqb * p.heads_total + hh);
-                        c = rec & 0x7fffffffu;
-                        nonfinite = rec >> 31;
-                    } else {
-                        c = word[j] >> 16;
-                        nonfinite = ((word[j] >> 8) & 255ull) ? 1u : 0u;
-                    }
-                    if (p.cover) c += 1;  // at most one newly appended current token
-                    const float rounded = p.fp32_counts ? (float)c : half_value(half_bits((float)c));
-                    e[j] = nonfinite | (isfinite(rounded) ? 0u : 2u);
-                    rr[j] = rounded;
-                    if (hh == own_head) own = c;
-                }
-            }
-        }
-        own = __reduce_max_sync(0xffffffffu, (unsigned int)own);
+        const CountFold f = fold_counts(p, seqb, h, n, word, timeout);
+        const unsigned long long own = f.own, k = f.k;
+        unsigned int status = f.status, index = f.index;
         if (r == 0 && lane == 0 && p.counts && !timeout) p.counts[seqb * p.heads + h] = (uint32_t)own;
-        // First failing head in head order (non-finite before count overflow
-        // within a head), found by ballot.  The rounded counts are integers
-        // below 2^16 and there are at most 128 of them, so every partial sum
-        // is an integer below 2^24 and exact in FP32: the tree sum equals the
-        // reference's sequential FP32 sum (gqa_policy.cpp:60) bit for bit.
-        unsigned int my_status = 0, my_index = 0;
-#pragma unroll
-        for (int j = 3; j >= 0; --j) {
-            if (e[j]) {
-                my_status = (e[j] & 1u) ? HSB_E_SEL_NONFINITE : (p.cover ? HSB_E_COVER_COUNT : HSB_E_SEL_COUNT_F16);
-                my_index = lane * 4 + j;
-            }
-        }
-        const unsigned int failing = __ballot_sync(0xffffffffu, my_status != 0);
-        unsigned int status = 0, index = 0;
-        if (failing) {
-            const int src = __ffs(failing) - 1;
-            status = __shfl_sync(0xffffffffu, my_status, src);
-            index = __shfl_sync(0xffffffffu, my_index, src);
-        }
-        float total = (rr[0] + rr[1]) + (rr[2] + rr[3]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-        unsigned long long k = 0;
-        if (!timeout && !status) {
-            const float mean = p.fp32_counts ? __fdiv_rn(total, (float)nh)
-                                             : half_value(half_bits(__fdiv_rn(total, (float)nh)));
-            if (p.cover) {
-                if (!(isfinite(mean) && mean >= 1.0f)) status = HSB_E_COVER_MEAN;
-                else k = min(p.cover_cap, (unsigned long long)mean);
-            } else {
-                if (!isfinite(mean)) status = HSB_E_SEL_MEAN_F16;
-                else {
-                    k = (unsigned long long)mean;
-                    const unsigned long long cap = (unsigned long long)floor((double)n * (double)p.ratio);
-                    k = min(k, min(cap, n));
-                }
-            }
-        }
         if (timeout) status = HSB_E_TIMEOUT;
         if (!status && k == 0 && p.zero_is_error) status = HSB_E_ZERO_SELECTION;
         if (lane == 0) {
@@ -1424,6 +1473,24 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __maxnreg__(80)
     }
 }
 
+// The layer step's selector: one launch of 32 heads (128 CTAs, one per
+// SM), so one CTA's latency sets the pace.  80 registers, no spills (a
+// two-CTAs-per-SM bound forced 64 and spilled); 512 x 80 registers still
+// leave room for one early-resident CTA of the next layer's scorer
+// (288 x 72).  Measured 0.7638 -> 0.7543 ms per decode step.
+__global__ void __cluster_dims__(kCluster, 1, 1) __maxnreg__(80)
+    select_cluster_kernel(const __grid_constant__ SelectParams p) {
+    select_cluster_body(p);
+}
+
+// Record mode over a batch of sequences (shard steps): no grid barrier and
+// many clusters per launch (64 sequences x 32 / W heads x 4 CTAs), so
+// occupancy sets the pace: at most 64 registers give two CTAs per SM.
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
+    select_cluster_batch_kernel(const __grid_constant__ SelectParams p) {
+    select_cluster_body(p);
+}
+
 // ------------------------------------------------------------- shard steps
 // The threshold record of a KV-head-sharded step, on the shard that holds
 // query head 0: {order key of F16(max - alpha), status}, the status being the
@@ -1519,7 +1586,9 @@ int cluster_capacity(int device) {
         int c = 0;
         const int smem = (int)(kCChunkMax * 2 + 2 * kSmemSortMax * 8);
         if (cudaFuncSetAttribute(select_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) ==
-            cudaSuccess) {
+                cudaSuccess &&
+            cudaFuncSetAttribute(select_cluster_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) ==
+                cudaSuccess) {
             cudaLaunchConfig_t cfg{};
             cfg.gridDim = dim3(kCluster * 32);
             cfg.blockDim = dim3(kCThreads);
@@ -1632,7 +1701,8 @@ cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream) {
         cfg.blockDim = dim3(kCThreads);
         cfg.dynamicSmemBytes = ((cs + 7) / 8 * 8 * 2 + 15) / 16 * 16 + 2 * kSmemSortMax * 8;
         if (s.ga.out) cfg.dynamicSmemBytes = std::max(cfg.dynamicSmemBytes, kEpiSmemBytes);
-        const cudaError_t le = cudaLaunchKernelEx(&cfg, select_cluster_kernel, p);
+        const cudaError_t le = s.ext ? cudaLaunchKernelEx(&cfg, select_cluster_batch_kernel, p)
+                                     : cudaLaunchKernelEx(&cfg, select_cluster_kernel, p);
         if (le == cudaSuccess && s.ga_done) *s.ga_done = s.ga.out != nullptr;
         return le;
     }

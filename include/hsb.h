@@ -285,7 +285,8 @@ int hsb_attention_dense(const float* d_q, const uint16_t* d_kcache, const uint16
 /* ------------------------------------------------------- rehearsal query
  * The rehearsal query producer (patches/llama-b6000-round2.patch:303-317 and
  * the F16 cast of policy/full_gqa_runtime.cpp:61-64): q = RoPE_position(W x),
- * x bf16 [4096], W bf16 [4096 out][4096 in], NORM-mode RoPE with base theta.
+ * x bf16 [4096], W bf16 [4096 out][4096 in] (both 16-byte aligned), NORM-mode
+ * RoPE with base theta.
  * Writes d_q_f32 [32][128] and/or d_q_f16 (either may be NULL). */
 int hsb_rehearsal_query(const uint16_t* d_x, const uint16_t* d_w, uint64_t position,
                         float theta, float* d_q_f32, uint16_t* d_q_f16, void* stream);
