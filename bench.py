@@ -774,8 +774,9 @@ def run_sharded(args, rank, world, torch, dist):
     (G = 8 / world per rank).  The exchanges -- thresholds from rank 0, every
     head's count records, the attention outputs -- go over NVLink peer memory
     through the library's own kernels (--exchange peer, the default) or NCCL
-    collectives (--exchange nccl).  The step is one CUDA graph; a second
-    graph with event nodes between the phases gives the per-phase timeline."""
+    collectives (--exchange nccl).  The step is one CUDA graph of four
+    launches per rank (rank 0's scorer pushes the thresholds); a second graph
+    with event nodes between the phases gives the per-phase timeline."""
     import hillserve_b200 as hsb
     from hillserve_b200 import sharded as sh
 
@@ -807,7 +808,7 @@ def run_sharded(args, rank, world, torch, dist):
     layer = sh.KVHeadShardedLayer(n, batch, world, rank, alpha=args.alpha)
     peer = args.exchange == "peer"
     ex = sh.PeerExchange(batch, world, rank) if peer else None
-    phase_ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(6)]
+    phase_ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(5)]
 
     def step(events=False):
         if not peer:
@@ -855,8 +856,8 @@ def run_sharded(args, rank, world, torch, dist):
         with torch.cuda.stream(stream):
             prof.replay()
         stream.synchronize()
-        names = ["score", "threshold_push", "count_exchange", "select", "finish_exchange"]
-        dur = torch.tensor([phase_ev[i].elapsed_time(phase_ev[i + 1]) for i in range(5)], dtype=torch.float64,
+        names = ["score", "count_exchange", "select", "finish_exchange"]  # rank 0's scorer pushes thresholds
+        dur = torch.tensor([phase_ev[i].elapsed_time(phase_ev[i + 1]) for i in range(4)], dtype=torch.float64,
                            device="cuda")
         dist.all_reduce(dur, op=dist.ReduceOp.MAX)
         phases = {k: round(float(v), 5) for k, v in zip(names, dur.tolist())}
@@ -919,7 +920,7 @@ def run_sharded(args, rank, world, torch, dist):
                                     "frac_of_peak_x_gpus": round(graded / (peak * world), 4), "peak_GB_s": peak,
                                     "peak_kind": peak_kind, "path": "the timed graph, whole step"},
             "roofline": roofline, "e2e": e2e,
-            "gpu_launches": (5 if rank == 0 else 4) * args.steps if peer else None,
+            "gpu_launches": 4 * args.steps if peer else None,
             "exchange_status": ex.status.cpu().numpy().tolist() if peer else None,
             "selection": {"k_mean": float(res[:, 0].mean()), "zero_selection": int((res[:, 0] == 0).sum())},
             "clocks": clocks.summary()}

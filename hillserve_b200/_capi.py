@@ -93,6 +93,7 @@ _SIGNATURES = {
     "hsb_mailbox_open": (I, [P, P]),
     "hsb_mailbox_close": (I, [P]),
     "hsb_exchange_threshold": (I, [P, F, P, P]),
+    "hsb_shard_score_push": (I, [P, I, P, SZ, SZ, P, P, P, F, P, P]),
     "hsb_exchange_count": (I, [P, SZ, SZ, P, P]),
     "hsb_exchange_finish": (I, [P, P, SZ, P, P]),
     "hsb_h2o_group_sums": (I, [P, P, P, SZ, SZ, P, SZ, P, P]),

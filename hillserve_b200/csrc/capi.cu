@@ -667,6 +667,31 @@ int hsb_shard_score(const uint16_t* d_q, int kv_heads, const uint16_t* d_kshard,
     return HSB_OK;
 }
 
+static int check_group(const hsb_peer_group* g);
+
+int hsb_shard_score_push(const uint16_t* d_q, int kv_heads, const uint16_t* d_kshard, size_t tokens, size_t batch,
+                         uint16_t* d_scores, uint16_t* d_order_keys, uint32_t* d_head0, float alpha,
+                         const hsb_peer_group* group, void* stream) {
+    if (!d_q || !d_kshard || !d_scores || !d_order_keys || !d_head0 || !valid_kv_heads(kv_heads) || tokens == 0 ||
+        batch == 0 || batch > 65535 || tokens * batch > 0x7fffffffull)
+        return fail(HSB_E_INVALID, "shard score arguments");
+    if (!aligned(d_kshard, 16)) return fail(HSB_E_INVALID, "key shard must be 16-byte aligned");
+    if (!(alpha >= 0.0f) || !std::isfinite(alpha)) return fail(HSB_E_SEL_PARAMS, "GQA selector numeric parameters");
+    int rc = check_group(group);
+    if (rc) return rc;
+    if (group->rank != 0 || group->batch != batch || group->world * kv_heads != HSB_KV_HEADS)
+        return fail(HSB_E_INVALID, "shard score push: rank 0 of a group of this batch, holding 8 / world KV heads");
+    ThresholdPush push{};
+    if (!threshold_push_params(group, alpha, &push)) return fail(HSB_E_INVALID, "shard score push: peer group");
+    ScoreExtras x{};
+    x.h0 = d_head0;
+    const cudaError_t e = launch_score_shard(d_q, kv_heads, d_kshard, tokens, (size_t)kv_heads * HSB_DIM, d_scores,
+                                             d_order_keys, nullptr, &x, as_stream(stream), batch, &push);
+    if (e != cudaSuccess) return fail_cuda(e, "shard score launch");
+    g_last_error.clear();
+    return HSB_OK;
+}
+
 int hsb_shard_threshold(const uint32_t* d_head0, size_t batch, float alpha, uint32_t* d_thr, void* stream) {
     if (!d_head0 || !d_thr || batch == 0 || batch > 65535) return fail(HSB_E_INVALID, "shard threshold arguments");
     if (!(alpha >= 0.0f) || !std::isfinite(alpha)) return fail(HSB_E_SEL_PARAMS, "GQA selector numeric parameters");

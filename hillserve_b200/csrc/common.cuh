@@ -83,6 +83,28 @@ __device__ __forceinline__ void raise_status(hsb_device_status* st, int code, in
     }
 }
 
+// System-scope acquire load / release store of a 64-bit flag (flags that
+// other GPUs write or read through peer memory).
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* a) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned long long* a, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+}
+// The threshold record of a sequence from its head-0 maximum key and
+// non-finite flag (policy/gqa_policy.cpp:50-54): {order key of
+// F16(max - alpha), status}.
+__device__ __forceinline__ uint2 threshold_record(uint32_t maxkey, uint32_t bad0, float alpha) {
+    const uint16_t kb = (uint16_t)((maxkey & 0x8000u) ? (maxkey ^ 0x8000u) : (~maxkey & 0xffffu));
+    const float threshold = half_value(half_bits(maxkey ? half_value(kb) - alpha : -INFINITY));
+    uint32_t status = 0;
+    if (bad0) status = HSB_E_SEL_NONFINITE_HEAD0;
+    else if (!isfinite(threshold)) status = HSB_E_SEL_THRESHOLD;
+    return make_uint2(status ? 0u : order_key(half_bits(threshold)), status);
+}
+
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -46,7 +46,7 @@ static_assert(sizeof(MailboxHeader) == 256, "mailbox header is 256 bytes");
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
 
 struct Layout {
-    size_t thr, rec, out, res, total;
+    size_t thr, rec, out, res, ctr, total;
 };
 Layout layout(size_t batch) {
     Layout l{};
@@ -54,7 +54,10 @@ Layout layout(size_t batch) {
     l.rec = l.thr + align256(batch * 2 * 4);
     l.out = l.rec + align256(batch * kHeads * 4);
     l.res = l.out + align256(batch * kHeads * kDim * 4);
-    l.total = l.res + align256((size_t)HSB_MAX_PEERS * batch * sizeof(hsb_selection));
+    // this rank's counters of the scorer's threshold push: [batch] CTAs per
+    // sequence done, then sequences done
+    l.ctr = l.res + align256((size_t)HSB_MAX_PEERS * batch * sizeof(hsb_selection));
+    l.total = l.ctr + align256((batch + 1) * 4);
     return l;
 }
 
@@ -68,14 +71,6 @@ struct PeerParams {
 
 __device__ __forceinline__ MailboxHeader* header(const PeerParams& p, int w) {
     return reinterpret_cast<MailboxHeader*>(p.mb[w]);
-}
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* a) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release_sys(unsigned long long* a, unsigned long long v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
 }
 // Bounded wait until *flag >= epoch; false when the limit ran out.
 __device__ bool wait_flag(const unsigned long long* flag, unsigned long long epoch, unsigned long long limit_ns) {
@@ -153,14 +148,8 @@ __global__ void __launch_bounds__(kThrThreads) exch_threshold_kernel(const uint3
     }
     __syncthreads();
     if (threadIdx.x < (unsigned)p.world) {
-        const uint16_t kb = (uint16_t)((smax & 0x8000u) ? (smax ^ 0x8000u) : (~smax & 0xffffu));
-        const float threshold = half_value(half_bits(smax ? half_value(kb) - alpha : -INFINITY));
-        uint32_t status = 0;
-        if (sbad) status = HSB_E_SEL_NONFINITE_HEAD0;
-        else if (!isfinite(threshold)) status = HSB_E_SEL_THRESHOLD;
         uint32_t* thr = reinterpret_cast<uint32_t*>(p.mb[threadIdx.x] + p.lay.thr) + 2 * blockIdx.x;
-        const uint2 rec = make_uint2(status ? 0u : order_key(half_bits(threshold)), status);
-        *reinterpret_cast<uint2*>(thr) = rec;
+        *reinterpret_cast<uint2*>(thr) = threshold_record(smax, sbad, alpha);
     }
     if (last_cta(&header(p, p.rank)->arrive[0])) release_all(p, offsetof(MailboxHeader, thr_flag), epoch);
 }
@@ -284,6 +273,21 @@ bool peer_params(const hsb_peer_group* g, PeerParams* p) {
 }
 
 }  // namespace
+
+bool threshold_push_params(const hsb_peer_group* g, float alpha, ThresholdPush* out) {
+    PeerParams p{};
+    if (!peer_params(g, &p) || g->rank != 0) return false;
+    *out = ThresholdPush{};
+    for (int w = 0; w < g->world; ++w) out->mb[w] = p.mb[w];
+    out->world = g->world;
+    out->thr_off = p.lay.thr;
+    out->flag_off = offsetof(MailboxHeader, thr_flag);
+    out->epoch = &reinterpret_cast<MailboxHeader*>(p.mb[0])->epoch;
+    out->seq_done = reinterpret_cast<unsigned int*>(p.mb[0] + p.lay.ctr);
+    out->all_done = out->seq_done + g->batch;
+    out->alpha = alpha;
+    return true;
+}
 
 size_t mailbox_bytes(size_t batch) { return layout(batch).total; }
 

@@ -69,9 +69,11 @@ cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nv
 // batch > 1: that many sequences back to back (keys_cache [batch][tokens],
 // q [batch][4 kv_heads][128], out / keys [batch][4 kv_heads][tokens],
 // extras->h0 [batch][kH0Partials]).
+struct ThresholdPush;
 cudaError_t launch_score_shard(const uint16_t* q, int kv_heads, const uint16_t* keys_cache, size_t tokens,
                                size_t stride_words, uint16_t* out, uint16_t* keys, hsb_device_status* status,
-                               const ScoreExtras* extras, cudaStream_t stream, size_t batch = 1);
+                               const ScoreExtras* extras, cudaStream_t stream, size_t batch = 1,
+                               const ThresholdPush* push = nullptr);
 cudaError_t launch_scale(const uint16_t* raw, size_t count, uint16_t* out, cudaStream_t stream);
 // Tensor map of a token-major [tokens][8][128] F16 cache seen as {channel,
 // token, KV head} with 64 x 32 x 8 boxes and the 128-byte swizzle (the
@@ -143,6 +145,20 @@ struct SelectLaunch {
     int cooperative = 1;  // launch attribute of the grid-barrier kernels
 };
 // Exchanges over peer memory (exchange.cu); arguments validated there.
+// The scorer's threshold push (rank 0 of a peer group): the CTA that closes a
+// sequence's last head-0 partial stores its threshold record into every
+// rank's mailbox; the one that closes the batch's last sequence resets the
+// counters and releases the threshold flag.
+struct ThresholdPush {
+    unsigned char* mb[HSB_MAX_PEERS] = {};
+    int world = 0;  // 0: no push
+    unsigned long long thr_off = 0, flag_off = 0;
+    const unsigned long long* epoch = nullptr;  // rank 0's step counter
+    unsigned int* seq_done = nullptr;           // [batch], zero between steps
+    unsigned int* all_done = nullptr;           // zero between steps
+    float alpha = 0.0f;
+};
+bool threshold_push_params(const hsb_peer_group* g, float alpha, ThresholdPush* out);
 size_t mailbox_bytes(size_t batch);
 void mailbox_offsets(size_t batch, hsb_mailbox_layout* out);
 cudaError_t launch_exchange_threshold(const uint32_t* h0, float alpha, const hsb_peer_group* g, cudaStream_t stream);

@@ -22,6 +22,15 @@ constexpr int kRThreads = 256;  // 8 warps, 8 output pairs per CTA
 
 __device__ __forceinline__ float bf16_value(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
 
+// A 16-byte load of weights, which nothing writes while the kernel runs.
+__device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
 __global__ void __launch_bounds__(kRThreads) rehearsal_kernel(const uint16_t* __restrict__ x,
                                                               const uint16_t* __restrict__ w,
                                                               unsigned long long position, float theta,
@@ -51,20 +60,39 @@ __global__ void __launch_bounds__(kRThreads) rehearsal_kernel(const uint16_t* __
     const uint4* w0 = reinterpret_cast<const uint4*>(w + (size_t)r0 * kEmbed);
     const uint4* w1 = reinterpret_cast<const uint4*>(w + (size_t)(r0 + 1) * kEmbed);
     float a0 = 0.f, a1 = 0.f;
-#pragma unroll 4
-    for (int c = 0; c < kEmbed / 256; ++c) {
-        const int idx = c * 32 + lane;  // 16-byte piece: elements idx*8 .. idx*8+7
-        const uint4 u = w0[idx], v = w1[idx];
-        const float4 xa = reinterpret_cast<const float4*>(xs)[idx * 2];
-        const float4 xb = reinterpret_cast<const float4*>(xs)[idx * 2 + 1];
-        const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-        const uint32_t uw[4] = {u.x, u.y, u.z, u.w}, vw[4] = {v.x, v.y, v.z, v.w};
+    // The GEMV is a pure 32 MiB stream: each lane issues the 16-byte loads of
+    // half its columns of both rows before any arithmetic (16 loads in flight
+    // per lane), twice.
+    constexpr int kPieces = kEmbed / 256;  // 16-byte pieces per lane per row
+    constexpr int kBatch = kPieces / 2;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            a0 = fmaf(bf16_value(uw[j] & 0xffffu), xv[2 * j], a0);
-            a0 = fmaf(bf16_value(uw[j] >> 16), xv[2 * j + 1], a0);
-            a1 = fmaf(bf16_value(vw[j] & 0xffffu), xv[2 * j], a1);
-            a1 = fmaf(bf16_value(vw[j] >> 16), xv[2 * j + 1], a1);
+    for (int c0 = 0; c0 < kPieces; c0 += kBatch) {
+        uint4 u[kBatch], v[kBatch];
+#pragma unroll
+        for (int c = 0; c < kBatch; ++c) {  // volatile asm: issued here, in order, before any use
+            u[c] = ldg_stream(w0 + (c0 + c) * 32 + lane);
+            v[c] = ldg_stream(w1 + (c0 + c) * 32 + lane);
+        }
+        // The arithmetic below reads the loaded words through these (empty,
+        // ordered) statements, so it cannot be scheduled between the loads.
+#pragma unroll
+        for (int c = 0; c < kBatch; ++c)
+            asm volatile("" : "+r"(u[c].x), "+r"(u[c].y), "+r"(u[c].z), "+r"(u[c].w), "+r"(v[c].x), "+r"(v[c].y),
+                         "+r"(v[c].z), "+r"(v[c].w));
+#pragma unroll
+        for (int c = 0; c < kBatch; ++c) {
+            const int idx = (c0 + c) * 32 + lane;  // 16-byte piece: elements idx*8 .. idx*8+7
+            const float4 xa = reinterpret_cast<const float4*>(xs)[idx * 2];
+            const float4 xb = reinterpret_cast<const float4*>(xs)[idx * 2 + 1];
+            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+            const uint32_t uw[4] = {u[c].x, u[c].y, u[c].z, u[c].w}, vw[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                a0 = fmaf(bf16_value(uw[j] & 0xffffu), xv[2 * j], a0);
+                a0 = fmaf(bf16_value(uw[j] >> 16), xv[2 * j + 1], a0);
+                a1 = fmaf(bf16_value(vw[j] & 0xffffu), xv[2 * j], a1);
+                a1 = fmaf(bf16_value(vw[j] >> 16), xv[2 * j + 1], a1);
+            }
         }
     }
     a0 = warp_sum(a0);

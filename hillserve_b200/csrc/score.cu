@@ -240,7 +240,36 @@ struct TmaParams {
     unsigned long long seq_tokens, q_seq, out_seq;
     int prefetch_tiles;  // key tiles per CTA pulled into L2 before the grid dependency wait
     unsigned long long batch;  // score_batch_kernel: sequences (tiles is per sequence)
+    ThresholdPush push;        // score_batch_kernel on rank 0 of a peer group
 };
+
+// Thread 0 of a CTA that has just written its head-0 partial of sequence s
+// (one of the sequence's ncta slots): the CTA that completes the sequence
+// derives its threshold record from the ncta partials and stores it into
+// every rank's mailbox; the CTA that completes the batch's last sequence
+// resets the counters and releases the threshold flag (the step's epoch).
+__device__ void push_threshold(const ThresholdPush& x, unsigned long long batch, unsigned long long s,
+                               const uint32_t* h0, unsigned ncta) {
+    __threadfence();
+    if (atomicAdd(x.seq_done + s, 1u) + 1 != ncta) return;
+    __threadfence();
+    uint32_t mx = 0, bad = 0;
+    for (unsigned i = 0; i < ncta; ++i) {
+        const uint32_t v = __ldcg(h0 + i);
+        mx = max(mx, v & 0xffffu);
+        bad |= v >> 16;
+    }
+    const uint2 rec = threshold_record(mx, bad, x.alpha);
+    for (int w = 0; w < x.world; ++w) *reinterpret_cast<uint2*>(x.mb[w] + x.thr_off + 8 * s) = rec;
+    __threadfence_system();
+    if (atomicAdd(x.all_done, 1u) + 1 != (unsigned)batch) return;
+    for (unsigned long long b = 0; b < batch; ++b) x.seq_done[b] = 0;
+    *x.all_done = 0;
+    __threadfence_system();
+    const unsigned long long epoch = __ldcg(x.epoch) + 1;
+    for (int w = 0; w < x.world; ++w)
+        st_release_sys(reinterpret_cast<unsigned long long*>(x.mb[w] + x.flag_off), epoch);
+}
 
 
 __device__ __forceinline__ int tile_view(const TmaParams& p, unsigned long long tile) {
@@ -519,6 +548,7 @@ __global__ void __launch_bounds__(kTThreads, 2) score_batch_kernel(const __grid_
             h0[blockIdx.x - first] = (h0_bad << 16) | h0_max;
             h0_max = 0;
             h0_bad = 0;
+            if (p.push.world) push_threshold(p.push, p.batch, s, h0, (unsigned)(last - first + 1));
         }
         if (blockIdx.x == first)
             for (unsigned w = (unsigned)(last - first + 1) + threadIdx.x; w < kH0Partials; w += kConsumerThreads)
@@ -729,7 +759,8 @@ cudaError_t launch_score(const uint16_t* q, const hsb_key_view* views, size_t nv
 
 cudaError_t launch_score_shard(const uint16_t* q, int kv_heads, const uint16_t* keys_cache, size_t tokens,
                                size_t stride_words, uint16_t* out, uint16_t* keys, hsb_device_status* status,
-                               const ScoreExtras* extras, cudaStream_t stream, size_t batch) {
+                               const ScoreExtras* extras, cudaStream_t stream, size_t batch,
+                               const ThresholdPush* push) {
     const DeviceInfo& dev = device_info();
     static thread_local int configured_device = -1;
     if (configured_device != dev.ordinal) {
@@ -761,6 +792,10 @@ cudaError_t launch_score_shard(const uint16_t* q, int kv_heads, const uint16_t* 
     // One wave: at most two CTAs per SM over the batch's tiles, contiguous
     // runs across sequences (score_batch_kernel).
     t.batch = batch;
+    if (push) {
+        if (!extras || !extras->h0) return cudaErrorInvalidValue;  // the push derives from the head-0 partials
+        t.push = *push;
+    }
     const unsigned long long total = t.tiles * batch;
     const dim3 grid((unsigned)std::min<unsigned long long>(total, (unsigned long long)dev.sms * 2));
     if (!keys) return cudaErrorInvalidValue;

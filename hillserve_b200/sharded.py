@@ -138,37 +138,38 @@ class KVHeadShardedLayer:
 
     # ------------------------------------------------------- peer memory
     def step_peer(self, q16, q32, kshard, vshard, exchange: PeerExchange, marks=None):
-        """The whole layer with the exchanges over peer memory: five launches
-        on this rank (four on ranks other than 0), no collective.  Returns the
+        """The whole layer with the exchanges over peer memory: four launches
+        on every rank (rank 0's scorer pushes the thresholds), no collective.  Returns the
         mailbox's outputs [batch][32][128] and the combined selection records
         [batch][4] (k, boundary-tied heads summed over ranks, status code,
-        index); the exchange's own status is in exchange.status.  marks: six
-        callables run on the current stream around the five phases (event
+        index); the exchange's own status is in exchange.status.  marks: five
+        callables run on the current stream around the four phases (event
         records, for a timeline)."""
         torch = self.torch
         stream = torch.cuda.current_stream().cuda_stream
         g = C.byref(exchange.group)
         mark = (lambda i: marks[i]()) if marks else (lambda i: None)
         mark(0)
-        self.score(q16, kshard, stream)
+        if self.geo.rank == 0:  # the scorer pushes the thresholds itself
+            self._check(self.lib.hsb_shard_score_push(
+                _ptr(q16), self.geo.kv_heads, _ptr(kshard), self.tokens, self.batch, _ptr(self.scores),
+                _ptr(self.keys), _ptr(self.head0), C.c_float(self.alpha), g, stream), "shard score push")
+        else:
+            self.score(q16, kshard, stream)
         mark(1)
-        if self.geo.rank == 0:
-            self._check(self.lib.hsb_exchange_threshold(_ptr(self.head0), C.c_float(self.alpha), g, stream),
-                        "exchange threshold")
-        mark(2)
         self._check(self.lib.hsb_exchange_count(_ptr(self.keys), self.geo.heads, self.tokens, g, stream),
                     "exchange count")
-        mark(3)
+        mark(2)
         self._check(self.lib.hsb_shard_select(
             _ptr(self.keys), _ptr(self.scores), self.geo.kv_heads, self.tokens, self.batch, exchange.thr_ptr,
             exchange.records_ptr, HEADS, self.geo.head_base, C.c_float(self.alpha), C.c_float(self.ratio),
             _ptr(self.ids), self.count, _ptr(self.counts), _ptr(self.results), _ptr(q32), _ptr(kshard),
             _ptr(vshard), _ptr(self.k_packed), _ptr(self.v_packed), _ptr(self.out), _ptr(self.workspace),
             self.workspace.numel(), stream), "shard select")
-        mark(4)
+        mark(3)
         self._check(self.lib.hsb_exchange_finish(_ptr(self.out), _ptr(self.results), self.geo.heads, g, stream),
                     "exchange finish")
-        mark(5)
+        mark(4)
         res = exchange.results
         combined = res[0].clone()
         combined[:, 1] = res[:, :, 1].sum(dim=0)

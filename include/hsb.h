@@ -427,6 +427,13 @@ int hsb_mailbox_destroy(void* d_mailbox);
 int hsb_mailbox_open(const void* ipc_handle, void** d_peer);
 int hsb_mailbox_close(void* d_peer);
 int hsb_exchange_threshold(const uint32_t* d_head0, float alpha, const hsb_peer_group* group, void* stream);
+/* hsb_shard_score and hsb_exchange_threshold in one launch, on rank 0: the
+ * scorer CTA that completes a sequence's head-0 partials stores its
+ * threshold record into every mailbox, and the one that completes the
+ * batch's last sequence releases the threshold flag. */
+int hsb_shard_score_push(const uint16_t* d_q, int kv_heads, const uint16_t* d_kshard, size_t tokens, size_t batch,
+                         uint16_t* d_scores, uint16_t* d_order_keys, uint32_t* d_head0, float alpha,
+                         const hsb_peer_group* group, void* stream);
 int hsb_exchange_count(const uint16_t* d_order_keys, size_t heads, size_t tokens, const hsb_peer_group* group,
                        void* stream);
 int hsb_exchange_finish(const float* d_out, const hsb_selection* d_results, size_t heads,
