@@ -311,19 +311,32 @@ __global__ void __launch_bounds__(kDThreads) attention_dense_kernel(const __grid
 // Dense decode attention streamed like the scorer: a ring of 32 KB TMA boxes
 // ({64 channels, 32 tokens, 8 KV heads}, 128-byte swizzle) carries, per
 // 32-token tile, K channels 0-63, K 64-127, V 0-63, V 64-127.  Warp w is KV
-// head w.  For the logits lane l is token l (the scorer's dot products, FP32);
-// an online softmax per query head keeps (max, sum) per warp; for P.V lane l
-// owns channels 2l, 2l+1 of each half, the tile's weights arriving by
-// shuffle.  One CTA per SM walks tiles blockIdx.x, +gridDim.x, ... and writes
-// one (max, sum, out[128]) partial per query head; dense_combine_kernel folds
-// them.
+// head w and runs both contractions of its four query heads on the tensor
+// cores with mma.sync.m16n8k16 (F16 operands, F32 accumulate):
+//
+//   logits  S^T[token][col] = K[token][ch] . Qx^T[ch][col]
+//   output  O^T[ch][col]    = V^T[ch][token] . Px^T[token][col]
+//
+// Decode has four query heads per KV head, so the MMA's eight columns carry
+// each head twice: column h holds the F16 rounding of head h's F32 value
+// (x_hi = f16(x)) and column h + 4 its remainder (x_lo = f16(x - x_hi)).
+// Summing the two columns gives products of the F32 value to ~2^-22
+// relative, near FP32, at no extra MMA cost.  Q is first scaled by a power
+// of two per KV head (max |q| in [2^14, 2^15)) so that neither half
+// overflows or leaves the F16 normal range; the logit scale undoes it
+// exactly.  K and V are F16 already and enter unchanged (ldmatrix from the
+// swizzled boxes, .trans for V^T).  An online softmax per query head keeps
+// (max, sum); the tile's weights go through a per-warp shared array into the
+// B fragments of the P.V product.  One CTA per SM walks tiles blockIdx.x,
+// +gridDim.x, ... and writes one (max, sum, out[128]) partial per query
+// head; dense_combine_kernel folds them.
 constexpr int kDTBox = 32 * kKvHeads * 64 * 2;  // bytes per box
 constexpr int kDTSlots = 6;
 constexpr int kDTConsumers = kKvHeads;
 constexpr int kDTThreads = (kDTConsumers + 1) * 32;
-constexpr int kDTQBytes = kKvHeads * kDim * kGroup * 4;  // F32 [kv][c][4 heads]
-constexpr int kDTPBytes = kDTConsumers * 32 * 16;  // per warp: the tile's weights, float4 [token][4 heads]
-constexpr int kDTSmem = 1024 + kDTSlots * kDTBox + kDTQBytes + kDTPBytes + 2 * kDTSlots * 8;
+constexpr int kDTPStride = 40;  // halves per weight row (32 tokens + pad: conflict-free B-fragment loads)
+constexpr int kDTPBytes = kDTConsumers * 8 * kDTPStride * 2;  // per warp: [8 columns][kDTPStride] F16
+constexpr int kDTSmem = 1024 + kDTSlots * kDTBox + kDTPBytes + 2 * kDTSlots * 8;
 constexpr int kDenseMaxCtas = 256;
 
 struct DenseTmaParams {
@@ -335,32 +348,43 @@ struct DenseTmaParams {
     float scale;
 };
 
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+// D += A . B, m16n8k16, A row-major F16, B column-major F16, D F32.
+__device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// The F16 half of x that column `lo` of a hi/lo pair carries.
+__device__ __forceinline__ __half split_half(float x, bool lo) {
+    const __half hi = __float2half_rn(x);
+    return lo ? __float2half_rn(x - __half2float(hi)) : hi;
+}
+__device__ __forceinline__ uint32_t pack_halves(__half a, __half b) {
+    return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+}
+
 __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(const __grid_constant__ DenseTmaParams p) {
     pdl_wait();
     pdl_trigger();
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     unsigned char* slots = smem;
-    float4* qs = reinterpret_cast<float4*>(smem + kDTSlots * kDTBox);
-    float4* pw = reinterpret_cast<float4*>(smem + kDTSlots * kDTBox + kDTQBytes);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDTSlots * kDTBox + kDTQBytes + kDTPBytes);
+    __half* pw = reinterpret_cast<__half*>(smem + kDTSlots * kDTBox);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDTSlots * kDTBox + kDTPBytes);
     uint64_t* empty = full + kDTSlots;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    {  // Q to shared memory: every load issued before any store (one round trip)
-        constexpr int kPer = (kHeads * kDim + kDTThreads - 1) / kDTThreads;
-        float qv[kPer];
-#pragma unroll
-        for (int u = 0; u < kPer; ++u) {
-            const int i = threadIdx.x + u * kDTThreads;
-            qv[u] = i < kHeads * kDim ? p.q[i] : 0.0f;  // written by the preceding grid: a coherent load
-        }
-#pragma unroll
-        for (int u = 0; u < kPer; ++u) {
-            const int i = threadIdx.x + u * kDTThreads;
-            if (i < kHeads * kDim)
-                reinterpret_cast<float*>(qs)[((i >> 9) * kDim + (i & 127)) * kGroup + ((i >> 7) & 3)] = qv[u];
-        }
-    }
     if (threadIdx.x == 0) {
         for (int s = 0; s < kDTSlots; ++s) {
             mbar_init(&full[s], 1);
@@ -395,110 +419,172 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
         return;
     }
 
-    // ---------------- consumers
+    // ---------------- consumers: warp kh = KV head kh, query heads 4kh .. 4kh+3
     const int kh = warp;
-    const float4* qv = qs + kh * kDim;
-    // Accumulators in pairs for the paired FP32 FMA (__ffma2_rn: two
-    // independent fma.rn, the same roundings as fmaf): the scores a01 = heads
-    // {0,1}, a23 = {2,3}; the outputs o2[j][0] = heads {0,1}, o2[j][1] =
-    // {2,3} of channel slot j.
-    float M[kGroup], L[kGroup];
-    float2 o2[4][2];
+    const int g = lane >> 2, t = lane & 3;  // MMA fragment row group and thread-in-group
+    // Q^T B fragments (column g = head g & 3, half g >> 2) for the 8 channel
+    // steps, every load issued first (the preceding grid wrote Q: coherent).
+    float2 qv[8][2];
+    {
+        const float* qh = p.q + (size_t)(kh * kGroup + (g & 3)) * kDim + 2 * t;
 #pragma unroll
-    for (int g = 0; g < kGroup; ++g) {
-        M[g] = -INFINITY;
-        L[g] = 0.0f;
+        for (int ks = 0; ks < 8; ++ks) {
+            qv[ks][0] = make_float2(qh[16 * ks], qh[16 * ks + 1]);  // q needs only 4-byte alignment
+            qv[ks][1] = make_float2(qh[16 * ks + 8], qh[16 * ks + 9]);
+        }
     }
+    float qmax = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) o2[j][0] = o2[j][1] = make_float2(0.0f, 0.0f);
+    for (int ks = 0; ks < 8; ++ks)
+        qmax = fmaxf(qmax, fmaxf(fmaxf(fabsf(qv[ks][0].x), fabsf(qv[ks][0].y)),
+                                 fmaxf(fabsf(qv[ks][1].x), fabsf(qv[ks][1].y))));
+    qmax = warp_max(qmax);
+    // 2^e with max |q| 2^e in [2^14, 2^15); e = 0 for a zero, subnormal or non-finite maximum.
+    const int qexp = (int)((__float_as_uint(qmax) >> 23) & 0xffu);
+    const int e = (qexp == 0 || qexp == 0xff) ? 0 : max(-100, min(100, 141 - qexp));
+    const float up = __uint_as_float((uint32_t)(127 + e) << 23);
+    const float sw = p.scale * __uint_as_float((uint32_t)(127 - e) << 23);  // the logit scale, 2^e undone
+    const bool lo_col = g >= 4;
+    uint32_t bq[8][2];
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks)
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+            bq[ks][j] = pack_halves(split_half(qv[ks][j].x * up, lo_col), split_half(qv[ks][j].y * up, lo_col));
+
+    // Lane state: heads h0 = 2 (t & 1) and h0 + 1 -- the same two heads for
+    // the logits it holds and for its output columns (2t, 2t + 1 mod 4).
+    float M[2] = {-INFINITY, -INFINITY}, L[2] = {0.0f, 0.0f};
+    float o[8][4];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) o[m][0] = o[m][1] = o[m][2] = o[m][3] = 0.0f;
+    __half* pwarp = pw + kh * 8 * kDTPStride;
+    const bool lo_half = t >= 2;
+    const int h0 = 2 * (t & 1);
+    // ldmatrix row addresses: lane i serves matrix i >> 3, row i & 7.
+    const int mi = lane >> 3, mr = lane & 7;
     uint32_t it = 0;
     for (unsigned tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
-        float2 a01 = make_float2(0.0f, 0.0f), a23 = make_float2(0.0f, 0.0f);
+        float acc[2][4];
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.0f;
         for (int half = 0; half < 2; ++half, ++it) {
             const uint32_t s = it % kDTSlots;
             if (!mbar_wait(&full[s], (it / kDTSlots) & 1)) {
                 raise_status(p.status, HSB_E_TIMEOUT, blockIdx.x);
                 return;
             }
-            const unsigned char* row = slots + s * kDTBox + (kh * 32 + lane) * 128;
+            const uint32_t base = smem_addr(slots + s * kDTBox + kh * 32 * 128);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const uint4 w = *reinterpret_cast<const uint4*>(row + ((j ^ (lane & 7)) << 4));
-                const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+            for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&words[e]));
-                    const float4 qa = qv[half * 64 + j * 8 + 2 * e], qb = qv[half * 64 + j * 8 + 2 * e + 1];
-                    const float2 fx = make_float2(f.x, f.x), fy = make_float2(f.y, f.y);
-                    a01 = __ffma2_rn(make_float2(qa.x, qa.y), fx, a01);
-                    a23 = __ffma2_rn(make_float2(qa.z, qa.w), fx, a23);
-                    a01 = __ffma2_rn(make_float2(qb.x, qb.y), fy, a01);
-                    a23 = __ffma2_rn(make_float2(qb.z, qb.w), fy, a23);
+                for (int mt = 0; mt < 2; ++mt) {
+                    // A = K rows: matrices {tokens +0/+8} x {channels +0/+8}
+                    const int tok = mt * 16 + mr + ((mi & 1) << 3);
+                    const int chunk = 2 * kk + (mi >> 1);
+                    uint32_t a[4];
+                    ldsm_x4(base + tok * 128 + ((chunk ^ (tok & 7)) << 4), a);
+                    mma_f16(acc[mt], a, bq[half * 4 + kk][0], bq[half * 4 + kk][1]);
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
-        // online softmax over this tile (tokens past the end weigh 0)
-        const bool valid = tile * 32 + lane < p.tokens;
-        const float a[kGroup] = {a01.x, a01.y, a23.x, a23.y};
-        float pr[kGroup], fg[kGroup];
+        // Logits of heads h0, h0 + 1 for tokens g, g + 8, 16 + g, 24 + g: the
+        // hi column plus the lo column (lane t ^ 2), then the scale.
+        float sc[2][4];
 #pragma unroll
-        for (int g = 0; g < kGroup; ++g) {
-            const float sg = valid ? a[g] * p.scale : -INFINITY;
-            const float mn = fmaxf(M[g], warp_max(sg));  // finite: the tile has a valid token
-            fg[g] = expf(M[g] - mn);                      // 0 on the first tile
-            pr[g] = valid ? expf(sg - mn) : 0.0f;
-            L[g] = fmaf(L[g], fg[g], warp_sum(pr[g]));
-            M[g] = mn;
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const float x = acc[mt][r] + __shfl_xor_sync(0xffffffffu, acc[mt][r], 2);
+                const int tok = mt * 16 + g + ((r >> 1) << 3);
+                sc[mt][r] = tile * 32 + tok < p.tokens ? x * sw : -INFINITY;
+            }
+        float fg[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {  // head h0 + j: registers r = j, j + 2
+            float mx = fmaxf(fmaxf(sc[0][j], sc[0][j + 2]), fmaxf(sc[1][j], sc[1][j + 2]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const float mn = fmaxf(M[j], mx);  // finite: the tile has a valid token
+            fg[j] = expf(M[j] - mn);           // 0 on the first tile
+            float sum = 0.0f;
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int r = j; r < 4; r += 2) {
+                    const float pr = expf(sc[mt][r] - mn);  // 0 for a masked token
+                    sum += pr;
+                    const int tok = mt * 16 + g + ((r >> 1) << 3);
+                    pwarp[(h0 + j + (lo_half ? 4 : 0)) * kDTPStride + tok] = split_half(pr, lo_half);
+                }
+            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+            L[j] = fmaf(L[j], fg[j], sum);
+            M[j] = mn;
         }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            o2[j][0].x *= fg[0];
-            o2[j][0].y *= fg[1];
-            o2[j][1].x *= fg[2];
-            o2[j][1].y *= fg[3];
+        for (int m = 0; m < 8; ++m) {
+            o[m][0] *= fg[0];
+            o[m][1] *= fg[1];
+            o[m][2] *= fg[0];
+            o[m][3] *= fg[1];
         }
-        // The tile's weights, one float4 per token: P.V reads them by broadcast.
-        pw[kh * 32 + lane] = make_float4(pr[0], pr[1], pr[2], pr[3]);
         __syncwarp();
+        // P^T B fragments: column g, tokens 16 kt + 2t (+1) and + 8.
+        uint32_t bp[2][2];
+#pragma unroll
+        for (int kt = 0; kt < 2; ++kt) {
+            const uint32_t* row = reinterpret_cast<const uint32_t*>(pwarp + g * kDTPStride + kt * 16);
+            bp[kt][0] = row[t];
+            bp[kt][1] = row[4 + t];
+        }
         for (int half = 0; half < 2; ++half, ++it) {
             const uint32_t s = it % kDTSlots;
             if (!mbar_wait(&full[s], (it / kDTSlots) & 1)) {
                 raise_status(p.status, HSB_E_TIMEOUT, blockIdx.x);
                 return;
             }
-            const unsigned char* base = slots + s * kDTBox + kh * 32 * 128 + (lane & 3) * 4;
-            const float4* pt = pw + kh * 32;
-#pragma unroll 8
-            for (int t = 0; t < 32; ++t) {
-                const uint32_t w = *reinterpret_cast<const uint32_t*>(base + t * 128 + (((lane >> 2) ^ (t & 7)) << 4));
-                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
-                const float4 p4 = pt[t];
-                const float2 p01 = make_float2(p4.x, p4.y), p23 = make_float2(p4.z, p4.w);
-                const float2 fx = make_float2(f.x, f.x), fy = make_float2(f.y, f.y);
-                o2[2 * half][0] = __ffma2_rn(p01, fx, o2[2 * half][0]);
-                o2[2 * half][1] = __ffma2_rn(p23, fx, o2[2 * half][1]);
-                o2[2 * half + 1][0] = __ffma2_rn(p01, fy, o2[2 * half + 1][0]);
-                o2[2 * half + 1][1] = __ffma2_rn(p23, fy, o2[2 * half + 1][1]);
+            const uint32_t base = smem_addr(slots + s * kDTBox + kh * 32 * 128);
+#pragma unroll
+            for (int kt = 0; kt < 2; ++kt) {
+#pragma unroll
+                for (int mc = 0; mc < 4; ++mc) {
+                    // A = V^T: matrices {channels +0/+8} x {tokens +0/+8}, transposed on load
+                    const int tok = kt * 16 + mr + ((mi >> 1) << 3);
+                    const int chunk = 2 * mc + (mi & 1);
+                    uint32_t a[4];
+                    ldsm_x4_trans(base + tok * 128 + ((chunk ^ (tok & 7)) << 4), a);
+                    mma_f16(o[half * 4 + mc], a, bp[kt][0], bp[kt][1]);
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
+        __syncwarp();  // the weights are read before the next tile overwrites them
     }
+    // O^T: lane holds channels 16m + g (+8) of columns 2t, 2t + 1; hi + lo.
 #pragma unroll
-    for (int g = 0; g < kGroup; ++g) {
-        float* part = p.part + ((size_t)(kh * kGroup + g) * gridDim.x + blockIdx.x) * kPart;
-        if (lane == 0) {
-            part[0] = M[g];
-            part[1] = L[g];
+    for (int m = 0; m < 8; ++m)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) o[m][r] += __shfl_xor_sync(0xffffffffu, o[m][r], 2);
+    if (t < 2) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            float* part = p.part + ((size_t)(kh * kGroup + h0 + j) * gridDim.x + blockIdx.x) * kPart;
+            if (g == 0) {
+                part[0] = M[j];
+                part[1] = L[j];
+            }
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+                part[2 + 16 * m + g] = o[m][j];
+                part[2 + 16 * m + g + 8] = o[m][j + 2];
+            }
         }
-        const int pair = g >> 1;
-        const bool second = g & 1;
-        part[2 + 2 * lane] = second ? o2[0][pair].y : o2[0][pair].x;
-        part[3 + 2 * lane] = second ? o2[1][pair].y : o2[1][pair].x;
-        part[2 + 64 + 2 * lane] = second ? o2[2][pair].y : o2[2][pair].x;
-        part[3 + 64 + 2 * lane] = second ? o2[3][pair].y : o2[3][pair].x;
     }
 }
 

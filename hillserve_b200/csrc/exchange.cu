@@ -167,6 +167,22 @@ __global__ void __launch_bounds__(kCntThreads) exch_count_kernel(const uint16_t*
     pdl_wait();
     const unsigned long long epoch = step_epoch(p);
     MailboxHeader* own = header(p, p.rank);
+    const bool vec = tokens % 8 == 0 && (reinterpret_cast<uintptr_t>(keys) & 15) == 0;
+    const unsigned long long n8 = vec ? tokens / 8 : 0;
+    // The first item's keys (up to kPre 16-byte words per thread) are loaded
+    // while thread 0 waits for the thresholds: the count then starts from
+    // registers the moment they arrive.
+    constexpr int kPre = 4;
+    uint4 pre[kPre];
+    const bool prefetch = n8 <= (unsigned long long)kPre * kCntThreads && blockIdx.x < p.batch * heads;
+    if (prefetch) {
+        const uint4* row = reinterpret_cast<const uint4*>(keys + (unsigned long long)blockIdx.x * tokens);
+#pragma unroll
+        for (int u = 0; u < kPre; ++u) {
+            const unsigned long long g = threadIdx.x + (unsigned long long)u * kCntThreads;
+            pre[u] = g < n8 ? row[g] : make_uint4(0, 0, 0, 0);
+        }
+    }
     __shared__ int ready;
     __shared__ unsigned int scnt, sbad;
     if (threadIdx.x == 0) ready = wait_flag(&own->thr_flag, epoch, p.limit_ns);
@@ -175,8 +191,6 @@ __global__ void __launch_bounds__(kCntThreads) exch_count_kernel(const uint16_t*
         if (threadIdx.x == 0) raise_status(&own->status, HSB_E_TIMEOUT, 0);
         return;  // the group's epochs now disagree: the mailboxes must be recreated
     }
-    const bool vec = tokens % 8 == 0 && (reinterpret_cast<uintptr_t>(keys) & 15) == 0;
-    const unsigned long long n8 = vec ? tokens / 8 : 0;
     const uint32_t* thr = reinterpret_cast<const uint32_t*>(p.mb[p.rank] + p.lay.thr);
     const unsigned long long items = p.batch * heads;
     for (unsigned long long item = blockIdx.x; item < items; item += gridDim.x) {
@@ -189,7 +203,21 @@ __global__ void __launch_bounds__(kCntThreads) exch_count_kernel(const uint16_t*
         __syncthreads();
         const uint16_t* row = keys + item * tokens;
         unsigned int cnt = 0, bad = 0;
-        for (unsigned long long g = threadIdx.x; g < n8; g += kCntThreads) {
+        const bool from_regs = prefetch && item == blockIdx.x;
+        if (from_regs) {
+#pragma unroll
+            for (int u = 0; u < kPre; ++u) {
+                if (threadIdx.x + (unsigned long long)u * kCntThreads >= n8) continue;
+                const uint32_t v[4] = {pre[u].x, pre[u].y, pre[u].z, pre[u].w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t key = (v[j >> 1] >> (16 * (j & 1))) & 0xffffu;
+                    bad |= key_nonfinite(key);
+                    cnt += (!key_nan(key) && key >= thr_key) ? 1u : 0u;
+                }
+            }
+        }
+        for (unsigned long long g = threadIdx.x; g < (from_regs ? 0 : n8); g += kCntThreads) {
             const uint4 w = reinterpret_cast<const uint4*>(row)[g];
             const uint32_t v[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll

@@ -84,3 +84,24 @@ def test_dense(cuda, ob, n, stride):
     out = cuda.attention_dense(_t(q32, torch.float32), kd, vd, n, stride)
     torch.cuda.synchronize()
     assert rel_err(out.cpu().numpy().astype(np.float64), want) < TOL
+
+
+@pytest.mark.parametrize("factor,tol", [(1.0, 1e-4), (30.0, TOL), (1e5, TOL), (1e-4, TOL)])
+def test_dense_query_range(cuda, ob, factor, tol):
+    """The dense kernel's tensor-core path carries Q as F16 hi/lo halves after
+    a power-of-two scale per KV head: queries far outside the F16 range (1e5)
+    or near its subnormals (1e-4) keep their accuracy, and at unit scale the
+    result stays near FP32 (1e-4, twenty times inside the stage tolerance)."""
+    import torch
+
+    n = 4096
+    _, k, _ = inputs.config1(n, seed=23)
+    v = inputs.values(23, n)
+    q32 = (inputs.normals(23, 4096, stream=9) * factor).astype(np.float32)
+    q32[5 * 128 + 17] *= 8.0  # one channel of one head well above the rest of its KV group
+    want = ob.attention_dense(k, v, n, 1024, q32)
+    out = cuda.attention_dense(_t(q32, torch.float32), dev_u16(k), dev_u16(v), n, 1024)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().astype(np.float64)
+    assert np.all(np.isfinite(got))
+    assert rel_err(got, want) < tol
