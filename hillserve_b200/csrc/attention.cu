@@ -9,9 +9,14 @@
 // contraction to give the tensor cores; the kernel is a bandwidth-bound
 // GEMV pair on the CUDA cores.
 //
-// attention_dense_kernel: dense decode attention over a token-major cache
-// (the two dense layers): a CTA owns (KV head, 512 tokens) and serves the
-// four query heads of the group from one read of each K and V row.
+// attention_dense_tma_kernel: dense decode attention over a token-major
+// cache (the two dense layers).  Every query head reads every row, so the
+// four heads of a KV group share one contraction per tile: the kernel streams
+// K/V through TMA and runs logits and P.V on the tensor cores (below).
+//
+// attention_dense_kernel: the fallback when no tensor map can be encoded: a
+// CTA owns (KV head, 512 tokens) and serves the four query heads of the group
+// from one read of each K and V row on the CUDA cores.
 #include <algorithm>
 #include <cmath>
 
@@ -376,6 +381,15 @@ __device__ __forceinline__ uint32_t pack_halves(__half a, __half b) {
 }
 
 __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(const __grid_constant__ DenseTmaParams p) {
+    if (threadIdx.x == kDTConsumers * 32) {
+        // The ring's first fill (tile blockIdx.x, then the K boxes of the
+        // next) into L2 before the dependency wait: the history rows are not
+        // the preceding grid's output, and L2 is the point of coherence for
+        // any row it does write.
+        for (unsigned j = 0, tile = blockIdx.x; j < 2 && tile < p.tiles; ++j, tile += gridDim.x)
+            for (int box = 0; box < (j ? 2 : 4); ++box)
+                tma_prefetch_3d(box < 2 ? &p.kmap : &p.vmap, (box & 1) * 64, (int)(tile * 32), 0);
+    }
     pdl_wait();
     pdl_trigger();
     extern __shared__ unsigned char smem_raw[];
@@ -590,13 +604,18 @@ __global__ void __launch_bounds__(kDTThreads, 1) attention_dense_tma_kernel(cons
 
 // out[h][d] = sum_c exp(M_c - M) o_c[d] / sum_c exp(M_c - M) L_c over the
 // dense kernel's per-CTA partials.  One CTA per query head: the partials'
-// weights go to shared memory once, then 8 groups of 128 threads (thread =
-// channel) each sum every 8th partial.  All loads are issued before any
-// arithmetic (a loop of dependent loads cost ~4 us per dense layer).
-constexpr int kCombineGroups = 8;
-__global__ void __launch_bounds__(kDim * kCombineGroups) dense_combine_kernel(const float* __restrict__ part,
-                                                                             int nparts, float* __restrict__ out) {
-    constexpr int kPer = kDenseMaxCtas / kCombineGroups;  // partials per thread
+// weights go to shared memory once, then 4 groups of 128 threads (thread =
+// channel) each sum every 4th partial.  Loads are issued in batches of 20
+// before any arithmetic (a loop of dependent loads cost ~4 us per dense
+// layer).  512 threads at <= 56 registers fit beside a resident dense CTA
+// (288 threads, 120 registers, ~200 KB shared memory), so the programmatic
+// launch makes the combine's CTAs resident while the dense kernel still runs
+// and they start the moment it completes.
+constexpr int kCombineGroups = 4;
+constexpr int kCombineBatch = 20;
+__global__ void __maxnreg__(56) dense_combine_kernel(const float* __restrict__ part, int nparts,
+                                                     float* __restrict__ out) {
+    constexpr int kPer = kDenseMaxCtas / kCombineGroups;  // partials per thread, at most
     constexpr int kPerLane = kDenseMaxCtas / 32;          // partials per lane of warp 0
     pdl_wait();
     pdl_trigger();
@@ -605,12 +624,11 @@ __global__ void __launch_bounds__(kDim * kCombineGroups) dense_combine_kernel(co
     __shared__ float red[2];
     const int h = blockIdx.x, tid = threadIdx.x, d = tid & (kDim - 1), grp = tid / kDim;
     const float* base = part + (size_t)h * nparts * kPart;
-    // Every load is issued up front (one round trip, not one per partial):
-    // this thread's output channel of partials grp, grp + 8, ..., and for
-    // warp 0 the maxima and sums.  The arithmetic keeps its order.
-    float ov[kPer];
+    // The first batch of this thread's output channel (partials grp, grp + 4,
+    // ...) and, for warp 0, the maxima and sums are all in flight at once.
+    float ov[kCombineBatch];
 #pragma unroll
-    for (int i = 0; i < kPer; ++i) {
+    for (int i = 0; i < kCombineBatch; ++i) {
         const int c = grp + i * kCombineGroups;
         ov[i] = c < nparts ? __ldcg(base + (size_t)c * kPart + 2 + d) : 0.0f;
     }
@@ -642,9 +660,21 @@ __global__ void __launch_bounds__(kDim * kCombineGroups) dense_combine_kernel(co
     __syncthreads();
     float acc = 0.0f;
 #pragma unroll
-    for (int i = 0; i < kPer; ++i) {
+    for (int i = 0; i < kCombineBatch; ++i) {
         const int c = grp + i * kCombineGroups;
         if (c < nparts) acc = fmaf(ov[i], w[c], acc);
+    }
+    for (int b = kCombineBatch; b < kPer && grp + b * kCombineGroups < nparts; b += kCombineBatch) {
+#pragma unroll
+        for (int i = 0; i < kCombineBatch; ++i) {
+            const int c = grp + (b + i) * kCombineGroups;
+            ov[i] = c < nparts ? __ldcg(base + (size_t)c * kPart + 2 + d) : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < kCombineBatch; ++i) {
+            const int c = grp + (b + i) * kCombineGroups;
+            if (c < nparts) acc = fmaf(ov[i], w[c], acc);
+        }
     }
     acc_s[grp][d] = acc;
     __syncthreads();
