@@ -18,7 +18,7 @@ namespace hsb {
 namespace {
 
 constexpr int kEmbed = 4096;
-constexpr int kRThreads = 256;  // 8 warps, 8 output pairs per CTA
+constexpr int kRThreads = 128;  // 4 warps, 4 output pairs per CTA: 512 CTAs, ~3.5 per SM
 
 __device__ __forceinline__ float bf16_value(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
 
@@ -37,41 +37,60 @@ __global__ void __launch_bounds__(kRThreads) rehearsal_kernel(const uint16_t* __
                                                               float* __restrict__ q32,
                                                               uint16_t* __restrict__ q16) {
     __shared__ __align__(16) float xs[kEmbed];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pair = blockIdx.x * (kRThreads / 32) + warp;  // 0..2047
+    const int r0 = pair * 2;
+    const uint4* w0 = reinterpret_cast<const uint4*>(w + (size_t)r0 * kEmbed);
+    const uint4* w1 = reinterpret_cast<const uint4*>(w + (size_t)(r0 + 1) * kEmbed);
+    // The GEMV is a pure 32 MiB stream: each lane issues the 16-byte loads of
+    // half its columns of both rows before any arithmetic (16 loads in flight
+    // per lane), twice.  The first half is issued before x is staged, so the
+    // stream starts at the kernel's first instruction.
+    constexpr int kPieces = kEmbed / 256;  // 16-byte pieces per lane per row
+    constexpr int kBatch = kPieces / 2;
+    uint4 u[kBatch], v[kBatch];
+#pragma unroll
+    for (int c = 0; c < kBatch; ++c) {  // volatile asm: issued here, in order, before any use
+        u[c] = ldg_stream(w0 + c * 32 + lane);
+        v[c] = ldg_stream(w1 + c * 32 + lane);
+    }
     {  // x in one round trip: every thread's 16-byte loads first, then the stores
         constexpr int kPer = kEmbed / 8 / kRThreads;  // 16-byte pieces per thread
         uint4 xv[kPer];
 #pragma unroll
-        for (int u = 0; u < kPer; ++u) xv[u] = reinterpret_cast<const uint4*>(x)[threadIdx.x + u * kRThreads];
+        for (int k = 0; k < kPer; ++k) xv[k] = reinterpret_cast<const uint4*>(x)[threadIdx.x + k * kRThreads];
 #pragma unroll
-        for (int u = 0; u < kPer; ++u) {
-            const int e = (threadIdx.x + u * kRThreads) * 8;
-            const uint32_t w[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
+        for (int k = 0; k < kPer; ++k) {
+            const int e = (threadIdx.x + k * kRThreads) * 8;
+            const uint32_t xw[4] = {xv[k].x, xv[k].y, xv[k].z, xv[k].w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                xs[e + 2 * j] = bf16_value(w[j] & 0xffffu);
-                xs[e + 2 * j + 1] = bf16_value(w[j] >> 16);
+                xs[e + 2 * j] = bf16_value(xw[j] & 0xffffu);
+                xs[e + 2 * j + 1] = bf16_value(xw[j] >> 16);
             }
         }
     }
+    // The rotation of this pair depends on no loaded data: lane 0 evaluates
+    // it while the loads are in flight.
+    float cs = 1.0f, sn = 0.0f;
+    if (lane == 0) {
+        const int i = (r0 & (kDim - 1)) >> 1;  // pair index inside the head
+        const double angle = (double)position * pow((double)theta, -2.0 * (double)i / (double)kDim);
+        double sd, cd;
+        sincos(angle, &sd, &cd);
+        cs = (float)cd;
+        sn = (float)sd;
+    }
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pair = blockIdx.x * 8 + warp;  // 0..2047
-    const int r0 = pair * 2;
-    const uint4* w0 = reinterpret_cast<const uint4*>(w + (size_t)r0 * kEmbed);
-    const uint4* w1 = reinterpret_cast<const uint4*>(w + (size_t)(r0 + 1) * kEmbed);
     float a0 = 0.f, a1 = 0.f;
-    // The GEMV is a pure 32 MiB stream: each lane issues the 16-byte loads of
-    // half its columns of both rows before any arithmetic (16 loads in flight
-    // per lane), twice.
-    constexpr int kPieces = kEmbed / 256;  // 16-byte pieces per lane per row
-    constexpr int kBatch = kPieces / 2;
 #pragma unroll
     for (int c0 = 0; c0 < kPieces; c0 += kBatch) {
-        uint4 u[kBatch], v[kBatch];
+        if (c0 > 0) {
 #pragma unroll
-        for (int c = 0; c < kBatch; ++c) {  // volatile asm: issued here, in order, before any use
-            u[c] = ldg_stream(w0 + (c0 + c) * 32 + lane);
-            v[c] = ldg_stream(w1 + (c0 + c) * 32 + lane);
+            for (int c = 0; c < kBatch; ++c) {
+                u[c] = ldg_stream(w0 + (c0 + c) * 32 + lane);
+                v[c] = ldg_stream(w1 + (c0 + c) * 32 + lane);
+            }
         }
         // The arithmetic below reads the loaded words through these (empty,
         // ordered) statements, so it cannot be scheduled between the loads.
@@ -98,11 +117,6 @@ __global__ void __launch_bounds__(kRThreads) rehearsal_kernel(const uint16_t* __
     a0 = warp_sum(a0);
     a1 = warp_sum(a1);
     if (lane == 0) {
-        const int i = (r0 & (kDim - 1)) >> 1;  // pair index inside the head
-        const double angle = (double)position * pow((double)theta, -2.0 * (double)i / (double)kDim);
-        double s, c;
-        sincos(angle, &s, &c);
-        const float cs = (float)c, sn = (float)s;
         const float o0 = a0 * cs - a1 * sn;
         const float o1 = a0 * sn + a1 * cs;
         if (q32) {
@@ -120,7 +134,7 @@ __global__ void __launch_bounds__(kRThreads) rehearsal_kernel(const uint16_t* __
 
 cudaError_t launch_rehearsal(const uint16_t* x, const uint16_t* w, uint64_t position, float theta, float* q32,
                              uint16_t* q16, cudaStream_t stream) {
-    rehearsal_kernel<<<kHeads * kDim / 16, kRThreads, 0, stream>>>(x, w, position, theta, q32, q16);
+    rehearsal_kernel<<<kHeads * kDim / 2 / (kRThreads / 32), kRThreads, 0, stream>>>(x, w, position, theta, q32, q16);
     return cudaGetLastError();
 }
 
