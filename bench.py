@@ -851,7 +851,7 @@ def run_sharded(args, rank, world, torch, dist):
     value = batch * args.steps / (ms / 1e3)
 
     # ---- per-phase timeline (graph with event nodes; max over ranks)
-    phases = None
+    phases = timeline = None
     if prof is not None:
         with torch.cuda.stream(stream):
             prof.replay()
@@ -859,8 +859,15 @@ def run_sharded(args, rank, world, torch, dist):
         names = ["score", "count_exchange", "select", "finish_exchange"]  # rank 0's scorer pushes thresholds
         dur = torch.tensor([phase_ev[i].elapsed_time(phase_ev[i + 1]) for i in range(4)], dtype=torch.float64,
                            device="cuda")
+        # Each rank's phase ends, µs after its own step start (the previous
+        # step's finish exchange lines the ranks up, so the rows compare).
+        ends = torch.tensor([phase_ev[0].elapsed_time(phase_ev[i + 1]) * 1e3 for i in range(4)],
+                            dtype=torch.float64, device="cuda")
         dist.all_reduce(dur, op=dist.ReduceOp.MAX)
         phases = {k: round(float(v), 5) for k, v in zip(names, dur.tolist())}
+        rows = [torch.empty_like(ends) for _ in range(world)]
+        dist.all_gather(rows, ends)
+        timeline = {k: [round(float(r[i]), 1) for r in rows] for i, k in enumerate(names)}
 
     # ---- end to end: queries in from pinned host memory, outputs back
     e2e = None
@@ -916,6 +923,7 @@ def run_sharded(args, rank, world, torch, dist):
                          "data path" if peer else "NCCL broadcast of thresholds, all-gather of records and outputs"),
             "launch": "one CUDA graph per step",
             "phases_ms": phases,
+            "phase_ends_us_per_rank": timeline,
             "score_select_gather": {"bytes_per_step_all_gpus": b_ssg, "GB_s": round(graded, 1),
                                     "frac_of_peak_x_gpus": round(graded / (peak * world), 4), "peak_GB_s": peak,
                                     "peak_kind": peak_kind, "path": "the timed graph, whole step"},
