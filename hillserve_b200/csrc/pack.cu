@@ -158,6 +158,70 @@ __global__ void __launch_bounds__(1024) union_compact_kernel(const uint32_t* __r
     }
 }
 
+// The whole union in one CTA when the membership words fit in shared memory
+// (visible <= kUnionSmemWords): the words are cleared, marked by one warp
+// per head and compacted there, so the step is one launch with no global
+// workspace traffic (the three-node path -- clear, mark, compact -- spends
+// most of its time between launches).  Same marks, statuses and sorted
+// output as the path above.
+constexpr size_t kUnionSmemWords = 49152;  // 192 KB
+__global__ void __launch_bounds__(1024) union_smem_kernel(const uint32_t* __restrict__ ids, size_t kstride,
+                                                          const uint32_t* __restrict__ sizes, size_t sizes_stride,
+                                                          size_t visible, uint32_t* __restrict__ physical,
+                                                          uint32_t* __restrict__ count, hsb_device_status* status) {
+    extern __shared__ __align__(16) uint32_t seen_s[];
+    __shared__ uint32_t warp_tot[32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const size_t words4 = (visible + 3) / 4;
+    for (size_t i = tid; i < words4; i += 1024) reinterpret_cast<uint4*>(seen_s)[i] = make_uint4(0, 0, 0, 0);
+    __syncthreads();
+    {  // warp h marks head h
+        const int h = warp;
+        const uint32_t size = head_size(sizes, sizes_stride, h);
+        if (size > kstride) {
+            if (lane == 0) raise_status(status, HSB_E_INVALID, h);
+        } else {
+            const uint32_t bit = 1u << h;
+            for (uint32_t s = lane; s < size; s += 32) {
+                const uint32_t id = ids[h * kstride + s];
+                if (id >= visible) {
+                    raise_status(status, HSB_E_UNION_DUPLICATE, h);
+                    continue;
+                }
+                if (atomicOr(&seen_s[id], bit) & bit) raise_status(status, HSB_E_UNION_DUPLICATE, h);
+            }
+        }
+    }
+    __syncthreads();
+    const size_t seg = ((visible + 1023) / 1024 + 3) / 4 * 4;
+    const size_t b0 = std::min(visible, tid * seg), b1 = std::min(visible, b0 + seg);
+    uint32_t c = 0;
+    for (size_t i = b0; i < b1; ++i) c += seen_s[i] != 0;
+    uint32_t x = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        const uint32_t t = warp_tot[lane];
+        uint32_t sum = t;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, sum, o);
+            if (lane >= o) sum += y;
+        }
+        warp_tot[lane] = sum - t;
+        if (lane == 31) *count = sum;
+    }
+    __syncthreads();
+    uint32_t pos = warp_tot[warp] + x - c;
+    for (size_t i = b0; c && i < b1; ++i)
+        if (seen_s[i]) physical[pos++] = (uint32_t)i;
+}
+
 // ------------------------------------------------------------------ pack
 __global__ void pack_offsets_kernel(const uint32_t* __restrict__ physical, size_t nphysical,
                                     uint64_t last_position, int32_t* __restrict__ offsets,
@@ -350,6 +414,20 @@ size_t union_workspace_bytes(size_t visible) { return (visible * 4 + 255) / 256 
 cudaError_t launch_union(const uint32_t* ids, size_t kstride, const uint32_t* sizes, size_t sizes_stride,
                          size_t visible, uint32_t* physical, uint32_t* physical_count,
                          hsb_device_status* status, void* workspace, cudaStream_t stream) {
+    if (visible <= kUnionSmemWords) {
+        const size_t smem = (visible + 3) / 4 * 16;
+        const DeviceInfo& dev = device_info();
+        static thread_local int configured_device = -1;
+        if (configured_device != dev.ordinal) {
+            cudaError_t e = cudaFuncSetAttribute(union_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)(kUnionSmemWords * 4));
+            if (e != cudaSuccess) return e;
+            configured_device = dev.ordinal;
+        }
+        union_smem_kernel<<<1, 1024, smem, stream>>>(ids, kstride, sizes, sizes_stride, visible, physical,
+                                                     physical_count, status);
+        return cudaGetLastError();
+    }
     uint32_t* seen = static_cast<uint32_t*>(workspace);
     cudaError_t e = cudaMemsetAsync(seen, 0, visible * 4, stream);
     if (e != cudaSuccess) return e;

@@ -103,6 +103,24 @@ def test_union_duplicates(cuda):
         cuda.gqa_physical_union(_t(ids, torch.int32), _t(np.full(32, 2), torch.int32), 2)
 
 
+@pytest.mark.parametrize("visible", [5, 32768, 49152, 49153, 70000])
+def test_union_paths(cuda, visible):
+    """Both union shapes (membership words in shared memory up to 49152
+    positions, in the global workspace past that) give the sorted set of
+    every head's IDs."""
+    import torch
+
+    rng = np.random.default_rng(visible)
+    k = min(visible, 700)
+    sizes = rng.integers(0, k + 1, 32)
+    ids = np.zeros((32, k), dtype=np.int64)
+    for h in range(32):
+        ids[h, :sizes[h]] = rng.choice(visible, sizes[h], replace=False)
+    want = np.unique(np.concatenate([ids[h, :sizes[h]] for h in range(32)]))
+    u = cuda.gqa_physical_union(_t(ids, torch.int32), _t(sizes, torch.int32), visible)
+    assert u.cpu().numpy().astype(np.int64).tolist() == want.tolist()
+
+
 @pytest.mark.parametrize("count", [32, 37, 200])
 def test_gather_map_vs_oracle(cuda, ob, count):
     import torch
