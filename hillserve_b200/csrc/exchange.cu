@@ -171,7 +171,8 @@ __global__ void __launch_bounds__(kCntThreads) exch_count_kernel(const uint16_t*
     const unsigned long long n8 = vec ? tokens / 8 : 0;
     // The first item's keys (up to kPre 16-byte words per thread) are loaded
     // while thread 0 waits for the thresholds: the count then starts from
-    // registers the moment they arrive.
+    // registers the moment they arrive.  Rows longer than kPre words per
+    // thread take the plain loop below instead.
     constexpr int kPre = 4;
     uint4 pre[kPre];
     const bool prefetch = n8 <= (unsigned long long)kPre * kCntThreads && blockIdx.x < p.batch * heads;
@@ -203,7 +204,19 @@ __global__ void __launch_bounds__(kCntThreads) exch_count_kernel(const uint16_t*
         __syncthreads();
         const uint16_t* row = keys + item * tokens;
         unsigned int cnt = 0, bad = 0;
-        const bool from_regs = prefetch && item == blockIdx.x;
+        const bool from_regs = prefetch;
+        // The next item's keys go out before this item is counted, so each
+        // CTA keeps one item's loads in flight while it counts the previous.
+        uint4 nxt[kPre];
+        const unsigned long long next = item + gridDim.x;
+        if (prefetch && next < items) {
+            const uint4* nrow = reinterpret_cast<const uint4*>(keys + next * tokens);
+#pragma unroll
+            for (int u = 0; u < kPre; ++u) {
+                const unsigned long long g = threadIdx.x + (unsigned long long)u * kCntThreads;
+                nxt[u] = g < n8 ? nrow[g] : make_uint4(0, 0, 0, 0);
+            }
+        }
         if (from_regs) {
 #pragma unroll
             for (int u = 0; u < kPre; ++u) {
@@ -231,6 +244,10 @@ __global__ void __launch_bounds__(kCntThreads) exch_count_kernel(const uint16_t*
             const uint32_t key = row[i];
             bad |= key_nonfinite(key);
             cnt += (!key_nan(key) && key >= thr_key) ? 1u : 0u;
+        }
+        if (prefetch && next < items) {
+#pragma unroll
+            for (int u = 0; u < kPre; ++u) pre[u] = nxt[u];
         }
         cnt = __reduce_add_sync(0xffffffffu, cnt);
         bad = __any_sync(0xffffffffu, bad);

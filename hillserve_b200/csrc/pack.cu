@@ -193,17 +193,17 @@ __global__ void __launch_bounds__(1024) union_smem_kernel(const uint32_t* __rest
         }
     }
     __syncthreads();
-    const size_t seg = ((visible + 1023) / 1024 + 3) / 4 * 4;
-    const size_t b0 = std::min(visible, tid * seg), b1 = std::min(visible, b0 + seg);
+    // Compaction: warp w owns a contiguous run of 32-word rows; lane l reads
+    // word l of each row (consecutive words: no bank conflicts), and a
+    // ballot gives the row's members in ID order.
+    const size_t rows = (visible + 31) / 32, rows_w = (rows + 31) / 32;
+    const size_t r0 = std::min(rows, warp * rows_w), r1 = std::min(rows, r0 + rows_w);
     uint32_t c = 0;
-    for (size_t i = b0; i < b1; ++i) c += seen_s[i] != 0;
-    uint32_t x = c;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
+    for (size_t r = r0; r < r1; ++r) {
+        const size_t i = r * 32 + lane;
+        c += __popc(__ballot_sync(0xffffffffu, i < visible && seen_s[i] != 0));
     }
-    if (lane == 31) warp_tot[warp] = x;
+    if (lane == 0) warp_tot[warp] = c;
     __syncthreads();
     if (warp == 0) {
         const uint32_t t = warp_tot[lane];
@@ -217,9 +217,14 @@ __global__ void __launch_bounds__(1024) union_smem_kernel(const uint32_t* __rest
         if (lane == 31) *count = sum;
     }
     __syncthreads();
-    uint32_t pos = warp_tot[warp] + x - c;
-    for (size_t i = b0; c && i < b1; ++i)
-        if (seen_s[i]) physical[pos++] = (uint32_t)i;
+    uint32_t pos = warp_tot[warp];
+    for (size_t r = r0; c && r < r1; ++r) {
+        const size_t i = r * 32 + lane;
+        const bool member = i < visible && seen_s[i] != 0;
+        const uint32_t bits = __ballot_sync(0xffffffffu, member);
+        if (member) physical[pos + __popc(bits & ((1u << lane) - 1u))] = (uint32_t)i;
+        pos += __popc(bits);
+    }
 }
 
 // ------------------------------------------------------------------ pack

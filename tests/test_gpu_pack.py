@@ -103,11 +103,11 @@ def test_union_duplicates(cuda):
         cuda.gqa_physical_union(_t(ids, torch.int32), _t(np.full(32, 2), torch.int32), 2)
 
 
-@pytest.mark.parametrize("visible", [5, 32768, 49152, 49153, 70000])
+@pytest.mark.parametrize("visible", [5, 32768, 49152, 49153, 66048])
 def test_union_paths(cuda, visible):
     """Both union shapes (membership words in shared memory up to 49152
-    positions, in the global workspace past that) give the sorted set of
-    every head's IDs."""
+    positions, in the global workspace past that, up to the reference's
+    66048-position bound) give the sorted set of every head's IDs."""
     import torch
 
     rng = np.random.default_rng(visible)
