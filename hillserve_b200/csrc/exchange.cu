@@ -328,8 +328,7 @@ bool threshold_push_params(const hsb_peer_group* g, float alpha, ThresholdPush* 
     out->thr_off = p.lay.thr;
     out->flag_off = offsetof(MailboxHeader, thr_flag);
     out->epoch = &reinterpret_cast<MailboxHeader*>(p.mb[0])->epoch;
-    out->seq_done = reinterpret_cast<unsigned int*>(p.mb[0] + p.lay.ctr);
-    out->all_done = out->seq_done + g->batch;
+    out->cta_done = reinterpret_cast<unsigned int*>(p.mb[0] + p.lay.ctr);
     out->alpha = alpha;
     return true;
 }

@@ -154,8 +154,7 @@ struct ThresholdPush {
     int world = 0;  // 0: no push
     unsigned long long thr_off = 0, flag_off = 0;
     const unsigned long long* epoch = nullptr;  // rank 0's step counter
-    unsigned int* seq_done = nullptr;           // [batch], zero between steps
-    unsigned int* all_done = nullptr;           // zero between steps
+    unsigned int* cta_done = nullptr;           // CTAs finished, zero between steps
     float alpha = 0.0f;
 };
 bool threshold_push_params(const hsb_peer_group* g, float alpha, ThresholdPush* out);

@@ -243,35 +243,6 @@ struct TmaParams {
     ThresholdPush push;        // score_batch_kernel on rank 0 of a peer group
 };
 
-// Thread 0 of a CTA that has just written its head-0 partial of sequence s
-// (one of the sequence's ncta slots): the CTA that completes the sequence
-// derives its threshold record from the ncta partials and stores it into
-// every rank's mailbox; the CTA that completes the batch's last sequence
-// resets the counters and releases the threshold flag (the step's epoch).
-__device__ void push_threshold(const ThresholdPush& x, unsigned long long batch, unsigned long long s,
-                               const uint32_t* h0, unsigned ncta) {
-    __threadfence();
-    if (atomicAdd(x.seq_done + s, 1u) + 1 != ncta) return;
-    __threadfence();
-    uint32_t mx = 0, bad = 0;
-    for (unsigned i = 0; i < ncta; ++i) {
-        const uint32_t v = __ldcg(h0 + i);
-        mx = max(mx, v & 0xffffu);
-        bad |= v >> 16;
-    }
-    const uint2 rec = threshold_record(mx, bad, x.alpha);
-    for (int w = 0; w < x.world; ++w) *reinterpret_cast<uint2*>(x.mb[w] + x.thr_off + 8 * s) = rec;
-    __threadfence_system();
-    if (atomicAdd(x.all_done, 1u) + 1 != (unsigned)batch) return;
-    for (unsigned long long b = 0; b < batch; ++b) x.seq_done[b] = 0;
-    *x.all_done = 0;
-    __threadfence_system();
-    const unsigned long long epoch = __ldcg(x.epoch) + 1;
-    for (int w = 0; w < x.world; ++w)
-        st_release_sys(reinterpret_cast<unsigned long long*>(x.mb[w] + x.flag_off), epoch);
-}
-
-
 __device__ __forceinline__ int tile_view(const TmaParams& p, unsigned long long tile) {
     int v = 0;
 #pragma unroll 1
@@ -463,6 +434,39 @@ __device__ __forceinline__ unsigned long long flat_cta_of(unsigned long long t, 
     return ((t + 1) * grid + total - 1) / total - 1;
 }
 
+// The threshold push of rank 0's shard scorer, run by the consumer threads
+// of the CTA that finishes last (every head-0 partial is written by then):
+// thread t folds sequences t, t + threads, ... -- their ncta partials, loads
+// issued together -- into {threshold key, status} records stored into every
+// rank's mailbox; then one system-scope fence, the counter reset, and the
+// threshold flag (the step's epoch) released on every rank.  Done once at
+// the end rather than as each sequence closes, the push never stalls a CTA
+// that still has tiles to score.
+__device__ void push_thresholds(const ThresholdPush& x, unsigned long long batch, unsigned long long tiles,
+                                unsigned long long total, unsigned long long grid, const uint32_t* h0_all,
+                                int tid, int threads) {
+    for (unsigned long long s = tid; s < batch; s += threads) {
+        const unsigned long long first = flat_cta_of(s * tiles, total, grid);
+        const unsigned long long last = flat_cta_of(s * tiles + tiles - 1, total, grid);
+        const unsigned ncta = (unsigned)(last - first + 1);
+        const uint32_t* h0 = h0_all + s * kH0Partials;
+        uint32_t mx = 0, bad = 0;
+        constexpr int kBatchLoads = 8;
+        for (unsigned i0 = 0; i0 < ncta; i0 += kBatchLoads) {
+            uint32_t v[kBatchLoads];
+#pragma unroll
+            for (int j = 0; j < kBatchLoads; ++j) v[j] = i0 + j < ncta ? __ldcg(h0 + i0 + j) : 0u;
+#pragma unroll
+            for (int j = 0; j < kBatchLoads; ++j) {
+                mx = max(mx, v[j] & 0xffffu);
+                bad |= v[j] >> 16;
+            }
+        }
+        const uint2 rec = threshold_record(mx, bad, x.alpha);
+        for (int w = 0; w < x.world; ++w) *reinterpret_cast<uint2*>(x.mb[w] + x.thr_off + 8 * s) = rec;
+    }
+}
+
 template <int G>
 __global__ void __launch_bounds__(kTThreads, 2) score_batch_kernel(const __grid_constant__ TmaParams p) {
     constexpr int T = 256 / G;
@@ -548,7 +552,6 @@ __global__ void __launch_bounds__(kTThreads, 2) score_batch_kernel(const __grid_
             h0[blockIdx.x - first] = (h0_bad << 16) | h0_max;
             h0_max = 0;
             h0_bad = 0;
-            if (p.push.world) push_threshold(p.push, p.batch, s, h0, (unsigned)(last - first + 1));
         }
         if (blockIdx.x == first)
             for (unsigned w = (unsigned)(last - first + 1) + threadIdx.x; w < kH0Partials; w += kConsumerThreads)
@@ -619,6 +622,28 @@ __global__ void __launch_bounds__(kTThreads, 2) score_batch_kernel(const __grid_
         }
     }
     if (seq != ~0ull) close_seq(seq);
+    if (p.push.world) {
+        // Rank 0 of a peer group: the CTA that finishes last pushes every
+        // sequence's threshold record (its partials are all written now).
+        __shared__ int last_cta;
+        named_sync(1, kConsumerThreads);
+        if (threadIdx.x == 0) {
+            __threadfence();
+            last_cta = atomicAdd(p.push.cta_done, 1u) + 1 == (unsigned)grid;
+        }
+        named_sync(1, kConsumerThreads);
+        if (!last_cta) return;
+        __threadfence();
+        push_thresholds(p.push, p.batch, p.tiles, total, grid, p.extras.h0, threadIdx.x, kConsumerThreads);
+        named_sync(1, kConsumerThreads);
+        if (threadIdx.x == 0) {
+            __threadfence_system();
+            *p.push.cta_done = 0;
+            const unsigned long long epoch = __ldcg(p.push.epoch) + 1;
+            for (int w = 0; w < p.push.world; ++w)
+                st_release_sys(reinterpret_cast<unsigned long long*>(p.push.mb[w] + p.push.flag_off), epoch);
+        }
+    }
 }
 
 // Token-major keys of one view seen as a 3-D tensor {channel, token, KV head}

@@ -84,7 +84,7 @@ struct SelectParams {
     const uint32_t* ext_thr;
     uint32_t head_base, heads_total;
     // Batch of sequences (shard steps; 1 otherwise): blockIdx.x covers
-    // batch x heads x kCluster.  Sequence b's scores / keys start b *
+    // batch x heads x the cluster size (kBatchCluster in record mode).  Sequence b's scores / keys start b *
     // seq_scores elements in; every per-head output advances by its own size.
     uint32_t batch;
     unsigned long long seq_scores;
@@ -555,18 +555,20 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(const __grid_consta
 // grid barrier (the cross-head count exchange, with the cluster barrier's
 // release/acquire split around it) and two cluster barriers.
 namespace cg = cooperative_groups;
-constexpr int kCluster = 4;
+constexpr int kCluster = 4;       // CTAs per head in the layer step's selector
+constexpr int kBatchCluster = 2;  // CTAs per head in record mode (shard steps), see the batch kernel
 constexpr int kCThreads = 512;
 constexpr int kCWarps = kCThreads / 32;
 constexpr unsigned long long kClusterKeysMax = 65536;           // valid tokens per head on this path
 constexpr unsigned long long kCChunkMax = kClusterKeysMax / kCluster;
 
+template <int C>
 struct ClusterShared {
     unsigned int hist[kCWarps][256];  // leader: LSD sort offsets
     unsigned int coarse[1024];        // histogram of key >> 6 over this CTA's chunk
     unsigned int fine[64];            // key & 63 inside the chosen coarse bin, this chunk
     unsigned int scan[32];
-    unsigned int red[kCWarps][kCluster];
+    unsigned int red[kCWarps][C];
     unsigned int maxkey, bad0, cnt, bad;
     unsigned int b_bin, b_above, b_eqtotal, total;
     unsigned int gt_before, eq_before;  // survivors of the cluster's earlier chunks
@@ -604,13 +606,17 @@ struct __align__(16) EpiGroupSmem {
     float stat[4];
 };
 static_assert(sizeof(EpiGroupSmem) % 16 == 0 && (kEpiPitch * 2) % 16 == 0, "16-byte aligned V staging");
+template <int C>
 struct __align__(16) EpiSmem {
     EpiGroupSmem g[kEpiGroups];
     __align__(16) float q[4][36];  // the head's query, channel quarters padded apart (distinct banks)
-    float part[kCluster * kEpiGroups][kDim + 2];  // leader: every group's (max, sum, out[128])
+    float part[C * kEpiGroups][kDim + 2];  // leader: every group's (max, sum, out[128])
 };
-static_assert(offsetof(EpiSmem, q) % 16 == 0, "16-byte aligned query");
-constexpr size_t kEpiSmemBytes = (sizeof(EpiSmem) + 15) / 16 * 16;
+static_assert(offsetof(EpiSmem<kCluster>, q) % 16 == 0, "16-byte aligned query");
+template <int C>
+constexpr size_t epi_smem_bytes() {
+    return (sizeof(EpiSmem<C>) + 15) / 16 * 16;
+}
 
 __device__ __forceinline__ void group_sync(int id) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(kEpiThreads) : "memory");
@@ -786,17 +792,19 @@ __device__ __forceinline__ CountFold fold_counts(const SelectParams& p, uint32_t
     return f;
 }
 
-// The cluster selector's body, shared by its two launch shapes below.
+// The cluster selector's body, shared by its two launch shapes below; C is
+// the cluster size (CTAs per head).
+template <int C>
 __device__ __forceinline__ void select_cluster_body(const SelectParams& p) {
     pdl_wait();
     pdl_trigger();
     extern __shared__ __align__(16) unsigned char dyn[];
-    __shared__ ClusterShared sh;
+    __shared__ ClusterShared<C> sh;
     cg::cluster_group cl = cg::this_cluster();
     const unsigned int r = cl.block_rank();
-    const uint32_t h = (blockIdx.x / kCluster) % p.heads;
-    const uint32_t seqb = blockIdx.x / (kCluster * p.heads);  // sequence of the batch
-    const bool seq_first = blockIdx.x % (kCluster * p.heads) == 0;  // first CTA of the sequence
+    const uint32_t h = (blockIdx.x / C) % p.heads;
+    const uint32_t seqb = blockIdx.x / (C * p.heads);  // sequence of the batch
+    const bool seq_first = blockIdx.x % (C * p.heads) == 0;  // first CTA of the sequence
     const uint16_t* scores = p.scores + seqb * p.seq_scores;
     hsb_selection* result = p.result + seqb;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -804,7 +812,7 @@ __device__ __forceinline__ void select_cluster_body(const SelectParams& p) {
     // selection instead of following it.
     const float q_own = (p.ga.out && tid < kDim) ? p.ga.q[((size_t)seqb * p.heads + h) * kDim + tid] : 0.0f;
     const unsigned long long n = p.valid;
-    const unsigned long long cs = ((n + kCluster - 1) / kCluster + 7) / 8 * 8;
+    const unsigned long long cs = ((n + C - 1) / C + 7) / 8 * 8;
     const unsigned long long b0 = min(n, (unsigned long long)r * cs), b1 = min(n, b0 + cs);
     const unsigned int m = (unsigned int)(b1 - b0);
     uint16_t* keys = reinterpret_cast<uint16_t*>(dyn);  // [cs] this chunk's keys
@@ -871,12 +879,16 @@ __device__ __forceinline__ void select_cluster_body(const SelectParams& p) {
     unsigned int mx = 0, bad0 = 0, bad = 0;
     const bool ext = p.ext != nullptr;
     // Phase 1's global loads go out together, one round trip rather than a
-    // chain: the chunk's first two 16-byte words of keys per thread and, in
+    // chain: the chunk's first kPreW 16-byte words of keys per thread and, in
     // the layer step, the two head-0 partials per thread.
     static_assert(kH0Partials == 2 * kCThreads, "two head-0 partials per thread");
-    uint4 kw[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+    // Words of keys per thread loaded up front: a 32768-key row's whole chunk.
+    constexpr int kPreW = 8 / C;
+    uint4 kw[kPreW];
 #pragma unroll
-    for (int u = 0; u < 2; ++u)
+    for (int u = 0; u < kPreW; ++u) kw[u] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int u = 0; u < kPreW; ++u)
         if (tid + u * kCThreads < m8) kw[u] = reinterpret_cast<const uint4*>(row + b0)[tid + u * kCThreads];
     // Current position (select after a prepared history): two warps stage
     // a query row and the position's key row, and their lane 0 scores it in
@@ -953,9 +965,9 @@ __device__ __forceinline__ void select_cluster_body(const SelectParams& p) {
         reinterpret_cast<uint4*>(keys)[g] = make_uint4(k2[0], k2[1], k2[2], k2[3]);
     };
 #pragma unroll
-    for (int u = 0; u < 2; ++u)
+    for (int u = 0; u < kPreW; ++u)
         if (tid + u * kCThreads < m8) take(kw[u], tid + u * kCThreads);
-    for (unsigned int g = tid + 2 * kCThreads; g < m8; g += kCThreads)
+    for (unsigned int g = tid + kPreW * kCThreads; g < m8; g += kCThreads)
         take(reinterpret_cast<const uint4*>(row + b0)[g], g);
     for (unsigned int i = m8 * 8 + tid; i < m; i += kCThreads) {
         if (i == cur_local) continue;
@@ -1034,7 +1046,7 @@ __device__ __forceinline__ void select_cluster_body(const SelectParams& p) {
                 const uint32_t hh = lane * 4 + j;
                 if (hh >= nh || timeout) continue;
                 unsigned long long w;
-                while (((w = ld_relaxed_u64(&p.header->hc[hh])) & 255ull) < (unsigned long long)kCluster) {
+                while (((w = ld_relaxed_u64(&p.header->hc[hh])) & 255ull) < (unsigned long long)C) {
                     if (global_ns() - start > kWaitLimitNs) {
                         timeout = 1;
                         break;
@@ -1082,16 +1094,16 @@ __device__ __forceinline__ void select_cluster_body(const SelectParams& p) {
     // ---- 3. radix select over the cluster's histograms.  Thread t owns
     // coarse bins 1023 - 2t and 1022 - 2t (descending).
     const unsigned int bin0 = 1023u - 2u * tid, bin1 = bin0 - 1u;
-    unsigned int cq0[kCluster], cq1[kCluster];
+    unsigned int cq0[C], cq1[C];
 #pragma unroll
-    for (int q = 0; q < kCluster; ++q) {
+    for (int q = 0; q < C; ++q) {
         const unsigned int* rc = cl.map_shared_rank(&sh.coarse[0], q);
         cq0[q] = rc[bin0];
         cq1[q] = rc[bin1];
     }
     unsigned int c0 = 0, c1 = 0;
 #pragma unroll
-    for (int q = 0; q < kCluster; ++q) {
+    for (int q = 0; q < C; ++q) {
         c0 += cq0[q];
         c1 += cq1[q];
     }
@@ -1115,7 +1127,7 @@ __device__ __forceinline__ void select_cluster_body(const SelectParams& p) {
     // Per-chunk counts of bins > hi (radix path) or >= hi (direct path):
     // the cluster prefix of each chunk.
 #pragma unroll
-    for (int q = 0; q < kCluster; ++q) {
+    for (int q = 0; q < C; ++q) {
         const unsigned int lo_bin = direct ? hi : hi + 1;
         unsigned int v = (bin0 >= lo_bin ? cq0[q] : 0u) + (bin1 >= lo_bin ? cq1[q] : 0u);
         v = __reduce_add_sync(0xffffffffu, v);
@@ -1251,9 +1263,9 @@ __device__ __forceinline__ void select_cluster_body(const SelectParams& p) {
     }
     cl.sync();  // every chunk's fine histogram is complete
     if (warp == 0) {  // 64 fine bins, two per lane, descending
-        unsigned int f0[kCluster], f1[kCluster], s0 = 0, s1 = 0;
+        unsigned int f0[C], f1[C], s0 = 0, s1 = 0;
 #pragma unroll
-        for (int q = 0; q < kCluster; ++q) {
+        for (int q = 0; q < C; ++q) {
             const unsigned int* rf = cl.map_shared_rank(&sh.fine[0], q);
             f0[q] = rf[63 - 2 * lane];
             f1[q] = rf[62 - 2 * lane];
@@ -1288,7 +1300,7 @@ __device__ __forceinline__ void select_cluster_body(const SelectParams& p) {
         // the chunks before this CTA.
         unsigned int gt_before = 0, eq_before = 0;
 #pragma unroll
-        for (int q = 0; q < kCluster; ++q) {
+        for (int q = 0; q < C; ++q) {
             unsigned int g = ((63 - 2 * lane) > b2 ? f0[q] : 0u) + ((62 - 2 * lane) > b2 ? f1[q] : 0u);
             unsigned int eq = ((63 - 2 * lane) == b2 ? f0[q] : 0u) + ((62 - 2 * lane) == b2 ? f1[q] : 0u);
             g = __reduce_add_sync(0xffffffffu, g);
@@ -1319,7 +1331,7 @@ __device__ __forceinline__ void select_cluster_body(const SelectParams& p) {
     const bool small = k <= kSmemSortMax;
     unsigned long long* sortbuf = p.sortbuf + ((unsigned long long)seqb * p.heads + h) * 2 * p.kcap;
     unsigned long long* dst = small ? cl.map_shared_rank(bufA, 0) : sortbuf;
-    ClusterShared* lead = cl.map_shared_rank(&sh, 0);
+    ClusterShared<C>* lead = cl.map_shared_rank(&sh, 0);
     // Thread t owns keys [t*per, t*per + per) of the chunk (ID order follows
     // thread order); one block scan of (gt << 16 | eq) places its survivors.
     const unsigned int per = ((m + kCThreads - 1) / kCThreads + 7) / 8 * 8;
@@ -1416,7 +1428,7 @@ __device__ __forceinline__ void select_cluster_body(const SelectParams& p) {
     if (!fused) return;
 
     // ---- epilogue: gather the head's selected rows and attend over them
-    EpiSmem& es = *reinterpret_cast<EpiSmem*>(dyn);  // keys and sort buffers are no longer needed
+    EpiSmem<C>& es = *reinterpret_cast<EpiSmem<C>*>(dyn);  // keys and sort buffers are no longer needed
     const int grp = tid / kEpiThreads, gtid = tid % kEpiThreads;
     // This sequence's view of the epilogue's buffers.
     SelectEpilogue ga = p.ga;
@@ -1445,13 +1457,13 @@ __device__ __forceinline__ void select_cluster_body(const SelectParams& p) {
     __syncthreads();
     float M = -INFINITY, L = 0.0f, acc = 0.0f;
     const unsigned ntiles = (unsigned)((k + 31) / 32);
-    // Tile t goes to CTA t % 4, group (t / 4) % 4: a few tiles spread over SMs first.
-    for (unsigned t = grp * kCluster + r; t < ntiles; t += kCluster * kEpiGroups) {
+    // Tile t goes to CTA t % C, group (t / C) % 4: a few tiles spread over SMs first.
+    for (unsigned t = grp * C + r; t < ntiles; t += C * kEpiGroups) {
         const unsigned s0 = t * 32;
         epilogue_tile<false>(ga, out, (int)h, s0, (int)min(32ull, k - s0), &es.q[0][0], es.g[grp], gtid, 1 + grp, M,
                              L, acc);
     }
-    EpiSmem* lead_es = cl.map_shared_rank(&es, 0);
+    EpiSmem<C>* lead_es = cl.map_shared_rank(&es, 0);
     float* part = lead_es->part[r * kEpiGroups + grp];
     if (gtid == 0) {
         part[0] = M;
@@ -1462,9 +1474,9 @@ __device__ __forceinline__ void select_cluster_body(const SelectParams& p) {
     if (r != 0) return;
     if (tid < kDim) {
         float mx = -INFINITY;
-        for (int i = 0; i < kCluster * kEpiGroups; ++i) mx = fmaxf(mx, es.part[i][0]);
+        for (int i = 0; i < C * kEpiGroups; ++i) mx = fmaxf(mx, es.part[i][0]);
         float lsum = 0.0f, o = 0.0f;
-        for (int i = 0; i < kCluster * kEpiGroups; ++i) {
+        for (int i = 0; i < C * kEpiGroups; ++i) {
             const float w = es.part[i][0] == -INFINITY ? 0.0f : expf(es.part[i][0] - mx);
             lsum = fmaf(es.part[i][1], w, lsum);
             o = fmaf(es.part[i][2 + tid], w, o);
@@ -1480,15 +1492,17 @@ __device__ __forceinline__ void select_cluster_body(const SelectParams& p) {
 // (288 x 72).  Measured 0.7638 -> 0.7543 ms per decode step.
 __global__ void __cluster_dims__(kCluster, 1, 1) __maxnreg__(80)
     select_cluster_kernel(const __grid_constant__ SelectParams p) {
-    select_cluster_body(p);
+    select_cluster_body<kCluster>(p);
 }
 
 // Record mode over a batch of sequences (shard steps): no grid barrier and
-// many clusters per launch (64 sequences x 32 / W heads x 4 CTAs), so
-// occupancy sets the pace: at most 64 registers give two CTAs per SM.
-__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kCThreads, 2)
+// many clusters per launch (64 sequences x 32 / W heads x kBatchCluster
+// CTAs), so throughput, not one head's latency, sets the pace: two CTAs per
+// head instead of four halve the CTAs and cluster barriers per head, and at
+// most 64 registers with a 16384-key chunk still give two CTAs per SM.
+__global__ void __cluster_dims__(kBatchCluster, 1, 1) __launch_bounds__(kCThreads, 2)
     select_cluster_batch_kernel(const __grid_constant__ SelectParams p) {
-    select_cluster_body(p);
+    select_cluster_body<kBatchCluster>(p);
 }
 
 // ------------------------------------------------------------- shard steps
@@ -1585,10 +1599,11 @@ int cluster_capacity(int device) {
     if (!known[device]) {
         int c = 0;
         const int smem = (int)(kCChunkMax * 2 + 2 * kSmemSortMax * 8);
+        const int smem_batch = (int)(kClusterKeysMax / kBatchCluster * 2 + 2 * kSmemSortMax * 8);
         if (cudaFuncSetAttribute(select_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) ==
                 cudaSuccess &&
-            cudaFuncSetAttribute(select_cluster_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) ==
-                cudaSuccess) {
+            cudaFuncSetAttribute(select_cluster_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 smem_batch) == cudaSuccess) {
             cudaLaunchConfig_t cfg{};
             cfg.gridDim = dim3(kCluster * 32);
             cfg.blockDim = dim3(kCThreads);
@@ -1693,14 +1708,17 @@ cudaError_t launch_select(const SelectLaunch& s, cudaStream_t stream) {
     cfg.numAttrs = 1;
     const int capacity = cluster_capacity(dev.ordinal);  // also configures the cluster kernel
     if (s.valid <= kClusterKeysMax && (s.ext || s.heads <= (uint32_t)capacity)) {
-        const size_t cs = ((size_t)s.valid + kCluster - 1) / kCluster;
-        cfg.gridDim = dim3(p.batch * s.heads * kCluster);
+        const int csize = s.ext ? kBatchCluster : kCluster;
+        const size_t cs = ((size_t)s.valid + csize - 1) / csize;
+        cfg.gridDim = dim3(p.batch * s.heads * csize);
         // Shard steps (records from the exchange) have no grid barrier, so a
         // batch of any size needs no co-residency: an ordinary cluster launch.
         if (s.ext || !s.cooperative) cfg.numAttrs = 0;
         cfg.blockDim = dim3(kCThreads);
         cfg.dynamicSmemBytes = ((cs + 7) / 8 * 8 * 2 + 15) / 16 * 16 + 2 * kSmemSortMax * 8;
-        if (s.ga.out) cfg.dynamicSmemBytes = std::max(cfg.dynamicSmemBytes, kEpiSmemBytes);
+        if (s.ga.out)
+            cfg.dynamicSmemBytes = std::max(cfg.dynamicSmemBytes,
+                                            s.ext ? epi_smem_bytes<kBatchCluster>() : epi_smem_bytes<kCluster>());
         const cudaError_t le = s.ext ? cudaLaunchKernelEx(&cfg, select_cluster_batch_kernel, p)
                                      : cudaLaunchKernelEx(&cfg, select_cluster_kernel, p);
         if (le == cudaSuccess && s.ga_done) *s.ga_done = s.ga.out != nullptr;

@@ -428,9 +428,9 @@ int hsb_mailbox_open(const void* ipc_handle, void** d_peer);
 int hsb_mailbox_close(void* d_peer);
 int hsb_exchange_threshold(const uint32_t* d_head0, float alpha, const hsb_peer_group* group, void* stream);
 /* hsb_shard_score and hsb_exchange_threshold in one launch, on rank 0: the
- * scorer CTA that completes a sequence's head-0 partials stores its
- * threshold record into every mailbox, and the one that completes the
- * batch's last sequence releases the threshold flag. */
+ * scorer CTA that finishes last folds every sequence's head-0 partials into
+ * its threshold record, stores the records into every mailbox and releases
+ * the threshold flag. */
 int hsb_shard_score_push(const uint16_t* d_q, int kv_heads, const uint16_t* d_kshard, size_t tokens, size_t batch,
                          uint16_t* d_scores, uint16_t* d_order_keys, uint32_t* d_head0, float alpha,
                          const hsb_peer_group* group, void* stream);
