@@ -853,8 +853,12 @@ def run_sharded(args, rank, world, torch, dist):
     # ---- per-phase timeline (graph with event nodes; max over ranks)
     phases = timeline = None
     if prof is not None:
+        # Three replays back to back: the ranks' host launches are skewed, but
+        # each step's finish exchange lines them up for the next, so the last
+        # replay (whose events are read) starts together on every rank.
         with torch.cuda.stream(stream):
-            prof.replay()
+            for _ in range(3):
+                prof.replay()
         stream.synchronize()
         names = ["score", "count_exchange", "select", "finish_exchange"]  # rank 0's scorer pushes thresholds
         dur = torch.tensor([phase_ev[i].elapsed_time(phase_ev[i + 1]) for i in range(4)], dtype=torch.float64,
