@@ -157,8 +157,8 @@ __global__ void __launch_bounds__(kThrThreads) exch_threshold_kernel(const uint3
 constexpr int kCntThreads = 1024;
 // Every rank: wait for the thresholds, then for each (sequence, local head)
 // item count #{keys >= threshold key} | non-finite << 31 and store the record
-// into every rank's mailbox (column head_base + head).  A persistent grid (at
-// most two CTAs per SM) walks the items, so the flag wait and the
+// into every rank's mailbox (column head_base + head).  A persistent grid (the
+// CTAs that fit resident at once) walks the items, so the flag wait and the
 // system-scope fence are paid once per CTA, not once per item; the last CTA
 // releases this rank's rec_flag and waits for every rank's records.
 __global__ void __launch_bounds__(kCntThreads) exch_count_kernel(const uint16_t* keys, unsigned long long tokens,
@@ -358,7 +358,21 @@ cudaError_t launch_exchange_count(const uint16_t* keys, size_t heads, size_t tok
     PeerParams p{};
     if (!peer_params(g, &p) || heads * g->world != kHeads) return cudaErrorInvalidValue;
     const DeviceInfo& dev = device_info();
-    const unsigned grid = (unsigned)std::min<unsigned long long>(heads * g->batch, (unsigned long long)dev.sms * 2);
+    // The persistent grid is what stays resident (one 1024-thread CTA per SM
+    // at this register count): CTAs beyond it would wait for the first ones
+    // to exit and run their items as a second, serial wave.
+    static thread_local int resident_device = -1, resident = 1;
+    if (resident_device != dev.ordinal) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, exch_count_kernel, kCntThreads, 0) != cudaSuccess ||
+            n < 1)
+            n = 1;
+        (void)cudaGetLastError();
+        resident = n;
+        resident_device = dev.ordinal;
+    }
+    const unsigned grid =
+        (unsigned)std::min<unsigned long long>(heads * g->batch, (unsigned long long)dev.sms * resident);
     return launch_dependent(exch_count_kernel, dim3(grid), dim3(kCntThreads), 0, stream, false, keys,
                             (unsigned long long)tokens, (unsigned)heads, (unsigned)(heads * g->rank), p);
 }
