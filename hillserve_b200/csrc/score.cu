@@ -635,14 +635,19 @@ __global__ void __launch_bounds__(kTThreads, 2) score_batch_kernel(const __grid_
         if (!last_cta) return;
         __threadfence();
         push_thresholds(p.push, p.batch, p.tiles, total, grid, p.extras.h0, threadIdx.x, kConsumerThreads);
+        __shared__ unsigned long long push_epoch;
         named_sync(1, kConsumerThreads);
         if (threadIdx.x == 0) {
             __threadfence_system();
             *p.push.cta_done = 0;
-            const unsigned long long epoch = __ldcg(p.push.epoch) + 1;
-            for (int w = 0; w < p.push.world; ++w)
-                st_release_sys(reinterpret_cast<unsigned long long*>(p.push.mb[w] + p.push.flag_off), epoch);
+            push_epoch = __ldcg(p.push.epoch) + 1;
         }
+        named_sync(1, kConsumerThreads);
+        // One release per rank, from as many threads at once: a single thread
+        // looping over the ranks would pay one system-scope fence per rank.
+        if (threadIdx.x < (unsigned)p.push.world)
+            st_release_sys(reinterpret_cast<unsigned long long*>(p.push.mb[threadIdx.x] + p.push.flag_off),
+                           push_epoch);
     }
 }
 
