@@ -268,6 +268,107 @@ __global__ void __launch_bounds__(kCntThreads) exch_count_kernel(const uint16_t*
     }
 }
 
+// The same exchange with the items staged in shared memory by the bulk-copy
+// engine: up to kCntStages items (64 KB each at 32768 keys) per CTA are in
+// flight at once, so the key stream does not stall on one item's round
+// trip; the count then reads shared memory.  Chosen by the host when the
+// rows are 16-byte aligned and at least two items fit.  Every wait is
+// bounded; a CTA that gives up waits (bounded) for its own copies still in
+// flight before it returns.
+constexpr int kCntStages = 3;
+constexpr size_t kCntStageSmem = 200 * 1024;  // dynamic shared memory the stages may take
+__global__ void __launch_bounds__(kCntThreads, 1) exch_count_staged_kernel(const uint16_t* keys,
+                                                                           unsigned long long tokens, unsigned heads,
+                                                                           unsigned head_base, int stages,
+                                                                           const __grid_constant__ PeerParams p) {
+    pdl_wait();
+    extern __shared__ __align__(128) unsigned char stage_buf[];
+    __shared__ uint64_t bar[kCntStages];
+    __shared__ int ready;
+    __shared__ unsigned int scnt, sbad;
+    const unsigned long long epoch = step_epoch(p);
+    MailboxHeader* own = header(p, p.rank);
+    const unsigned long long items = p.batch * heads;
+    const uint32_t item_bytes = (uint32_t)(tokens * 2);
+    const unsigned long long mine = blockIdx.x < items ? (items - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+    const unsigned long long issued0 = mine < (unsigned long long)stages ? mine : (unsigned long long)stages;
+    auto issue = [&](unsigned long long j) {  // this CTA's j-th item into stage j % stages
+        uint64_t* b = &bar[j % stages];
+        mbar_arrive_expect_tx(b, item_bytes);
+        bulk_copy_g2s(stage_buf + (j % stages) * item_bytes, keys + (blockIdx.x + j * gridDim.x) * tokens, item_bytes,
+                      b);
+    };
+    // Copies issued and not yet consumed [from, to): waited for before any exit.
+    auto drain = [&](unsigned long long from, unsigned long long to) {
+        for (unsigned long long j = from; j < to; ++j) (void)mbar_wait(&bar[j % stages], (uint32_t)((j / stages) & 1));
+    };
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) mbar_init(&bar[s], 1);
+        mbar_fence_init();
+        for (unsigned long long j = 0; j < issued0; ++j) issue(j);
+        ready = wait_flag(&own->thr_flag, epoch, p.limit_ns);
+        scnt = 0;
+        sbad = 0;
+    }
+    __syncthreads();
+    if (!ready) {
+        if (threadIdx.x == 0) {
+            raise_status(&own->status, HSB_E_TIMEOUT, 0);
+            drain(0, issued0);
+        }
+        return;  // the group's epochs now disagree: the mailboxes must be recreated
+    }
+    const uint32_t* thr = reinterpret_cast<const uint32_t*>(p.mb[p.rank] + p.lay.thr);
+    const unsigned long long n8 = tokens / 8;
+    for (unsigned long long j = 0; j < mine; ++j) {
+        const unsigned long long item = blockIdx.x + j * gridDim.x;
+        const unsigned seq = (unsigned)(item / heads), head = (unsigned)(item % heads);
+        const unsigned int thr_key = __ldcg(thr + 2 * seq);
+        const int landed = __syncthreads_and(mbar_wait(&bar[j % stages], (uint32_t)((j / stages) & 1)) ? 1 : 0);
+        if (!landed) {
+            if (threadIdx.x == 0) {
+                raise_status(&own->status, HSB_E_TIMEOUT, (int)blockIdx.x);
+                const unsigned long long issued = j + stages < mine ? j + stages : mine;
+                drain(j, issued);  // item j's own copy included
+            }
+            return;
+        }
+        const uint4* row = reinterpret_cast<const uint4*>(stage_buf + (j % stages) * item_bytes);
+        unsigned int cnt = 0, bad = 0;
+        for (unsigned long long g = threadIdx.x; g < n8; g += kCntThreads) {
+            const uint4 w = row[g];
+            const uint32_t v[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const uint32_t key = (v[e >> 1] >> (16 * (e & 1))) & 0xffffu;
+                bad |= key_nonfinite(key);
+                cnt += (!key_nan(key) && key >= thr_key) ? 1u : 0u;
+            }
+        }
+        cnt = __reduce_add_sync(0xffffffffu, cnt);
+        bad = __any_sync(0xffffffffu, bad);
+        if ((threadIdx.x & 31) == 0) {
+            if (cnt) atomicAdd(&scnt, cnt);
+            if (bad) atomicOr(&sbad, 1u);
+        }
+        __syncthreads();  // the stage is read and the item's count is complete
+        if (threadIdx.x == 0 && j + stages < mine) issue(j + stages);
+        if (threadIdx.x < (unsigned)p.world) {
+            uint32_t* rec = reinterpret_cast<uint32_t*>(p.mb[threadIdx.x] + p.lay.rec);
+            rec[(size_t)seq * kHeads + head_base + head] = scnt | (sbad << 31);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            scnt = 0;
+            sbad = 0;
+        }
+    }
+    if (last_cta(&own->arrive[1])) {
+        release_all(p, offsetof(MailboxHeader, rec_flag) + 8 * p.rank, epoch);
+        wait_all(p, offsetof(MailboxHeader, rec_flag), epoch);
+    }
+}
+
 constexpr int kFinThreads = 256;
 // Every rank: this rank's outputs [batch][heads][128] and selection results
 // [batch] into every rank's mailbox (outputs at heads head_base.., results at
@@ -370,6 +471,24 @@ cudaError_t launch_exchange_count(const uint16_t* keys, size_t heads, size_t tok
         (void)cudaGetLastError();
         resident = n;
         resident_device = dev.ordinal;
+    }
+    // Staged path: rows 16-byte aligned and at least two 64 KB-class items
+    // in shared memory (one CTA per SM).
+    const size_t item_bytes = tokens * 2;
+    const int stages = (int)std::min<size_t>(kCntStages, item_bytes ? kCntStageSmem / item_bytes : 0);
+    if (tokens % 8 == 0 && (reinterpret_cast<uintptr_t>(keys) & 15) == 0 && stages >= 2 &&
+        item_bytes <= 0xffffffffull) {
+        static thread_local int staged_device = -1;
+        if (staged_device != dev.ordinal) {
+            const cudaError_t e = cudaFuncSetAttribute(exch_count_staged_kernel,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kCntStageSmem);
+            if (e != cudaSuccess) return e;
+            staged_device = dev.ordinal;
+        }
+        const unsigned sgrid = (unsigned)std::min<unsigned long long>(heads * g->batch, (unsigned long long)dev.sms);
+        return launch_dependent(exch_count_staged_kernel, dim3(sgrid), dim3(kCntThreads), (size_t)stages * item_bytes,
+                                stream, false, keys, (unsigned long long)tokens, (unsigned)heads,
+                                (unsigned)(heads * g->rank), stages, p);
     }
     const unsigned grid =
         (unsigned)std::min<unsigned long long>(heads * g->batch, (unsigned long long)dev.sms * resident);
