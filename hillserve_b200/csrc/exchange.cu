@@ -285,7 +285,6 @@ __global__ void __launch_bounds__(kCntThreads, 1) exch_count_staged_kernel(const
     extern __shared__ __align__(128) unsigned char stage_buf[];
     __shared__ uint64_t bar[kCntStages];
     __shared__ int ready;
-    __shared__ unsigned int scnt, sbad;
     const unsigned long long epoch = step_epoch(p);
     MailboxHeader* own = header(p, p.rank);
     const unsigned long long items = p.batch * heads;
@@ -307,8 +306,6 @@ __global__ void __launch_bounds__(kCntThreads, 1) exch_count_staged_kernel(const
         mbar_fence_init();
         for (unsigned long long j = 0; j < issued0; ++j) issue(j);
         ready = wait_flag(&own->thr_flag, epoch, p.limit_ns);
-        scnt = 0;
-        sbad = 0;
     }
     __syncthreads();
     if (!ready) {
@@ -320,12 +317,48 @@ __global__ void __launch_bounds__(kCntThreads, 1) exch_count_staged_kernel(const
     }
     const uint32_t* thr = reinterpret_cast<const uint32_t*>(p.mb[p.rank] + p.lay.thr);
     const unsigned long long n8 = tokens / 8;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // Per-warp partials of the last two items (double-buffered by item
+    // parity): one CTA barrier per item.  Warp 0 reduces item j's partials
+    // after barrier j and before it reaches barrier j + 1, so item j + 2
+    // (same slot) cannot overwrite them early.
+    __shared__ unsigned int wcnt[2][kCntThreads / 32], wbad[2][kCntThreads / 32];
     for (unsigned long long j = 0; j < mine; ++j) {
         const unsigned long long item = blockIdx.x + j * gridDim.x;
         const unsigned seq = (unsigned)(item / heads), head = (unsigned)(item % heads);
         const unsigned int thr_key = __ldcg(thr + 2 * seq);
-        const int landed = __syncthreads_and(mbar_wait(&bar[j % stages], (uint32_t)((j / stages) & 1)) ? 1 : 0);
-        if (!landed) {
+        // Counted: not NaN and >= threshold, i.e. key in [max(thr, 0x03ff), 0xfc00];
+        // non-finite: key <= 0x03ff or key >= 0xfc00 (from the running min / max).
+        const uint32_t lo = max(thr_key, 0x03ffu);
+        const uint32_t span = lo <= 0xfc00u ? 0xfc00u - lo : 0u;
+        const bool none = lo > 0xfc00u;
+        bool ok = mbar_wait(&bar[j % stages], (uint32_t)((j / stages) & 1));
+        unsigned int cnt = 0;
+        uint32_t kmin = 0xffffu, kmax = 0u;
+        if (ok) {
+            const uint4* row = reinterpret_cast<const uint4*>(stage_buf + (j % stages) * item_bytes);
+            for (unsigned long long g = threadIdx.x; g < n8; g += kCntThreads) {
+                const uint4 w = row[g];
+                const uint32_t v[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const uint32_t k0 = v[e] & 0xffffu, k1 = v[e] >> 16;
+                    kmin = min(kmin, min(k0, k1));
+                    kmax = max(kmax, max(k0, k1));
+                    cnt += (k0 - lo <= span) ? 1u : 0u;
+                    cnt += (k1 - lo <= span) ? 1u : 0u;
+                }
+            }
+        }
+        if (none) cnt = 0;
+        cnt = __reduce_add_sync(0xffffffffu, cnt);
+        kmin = __reduce_min_sync(0xffffffffu, kmin);
+        kmax = __reduce_max_sync(0xffffffffu, kmax);
+        if (lane == 0) {
+            wcnt[j & 1][warp] = cnt;
+            wbad[j & 1][warp] = (kmin <= 0x03ffu || kmax >= 0xfc00u) ? 1u : 0u;
+        }
+        if (__syncthreads_or(!ok)) {  // the stage is read by every warp (or a copy never landed)
             if (threadIdx.x == 0) {
                 raise_status(&own->status, HSB_E_TIMEOUT, (int)blockIdx.x);
                 const unsigned long long issued = j + stages < mine ? j + stages : mine;
@@ -333,34 +366,15 @@ __global__ void __launch_bounds__(kCntThreads, 1) exch_count_staged_kernel(const
             }
             return;
         }
-        const uint4* row = reinterpret_cast<const uint4*>(stage_buf + (j % stages) * item_bytes);
-        unsigned int cnt = 0, bad = 0;
-        for (unsigned long long g = threadIdx.x; g < n8; g += kCntThreads) {
-            const uint4 w = row[g];
-            const uint32_t v[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const uint32_t key = (v[e >> 1] >> (16 * (e & 1))) & 0xffffu;
-                bad |= key_nonfinite(key);
-                cnt += (!key_nan(key) && key >= thr_key) ? 1u : 0u;
-            }
-        }
-        cnt = __reduce_add_sync(0xffffffffu, cnt);
-        bad = __any_sync(0xffffffffu, bad);
-        if ((threadIdx.x & 31) == 0) {
-            if (cnt) atomicAdd(&scnt, cnt);
-            if (bad) atomicOr(&sbad, 1u);
-        }
-        __syncthreads();  // the stage is read and the item's count is complete
         if (threadIdx.x == 0 && j + stages < mine) issue(j + stages);
-        if (threadIdx.x < (unsigned)p.world) {
-            uint32_t* rec = reinterpret_cast<uint32_t*>(p.mb[threadIdx.x] + p.lay.rec);
-            rec[(size_t)seq * kHeads + head_base + head] = scnt | (sbad << 31);
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            scnt = 0;
-            sbad = 0;
+        if (warp == 0) {
+            unsigned int c = wcnt[j & 1][lane], bd = wbad[j & 1][lane];
+            c = __reduce_add_sync(0xffffffffu, c);
+            bd = __reduce_or_sync(0xffffffffu, bd);
+            if (lane < p.world) {
+                uint32_t* rec = reinterpret_cast<uint32_t*>(p.mb[lane] + p.lay.rec);
+                rec[(size_t)seq * kHeads + head_base + head] = c | (bd << 31);
+            }
         }
     }
     if (last_cta(&own->arrive[1])) {
