@@ -730,10 +730,13 @@ SHARD_SAMPLE = 8      # sequences of the CPU legs' bounded sample (of the batch)
 
 def shard_config(args, world) -> dict:
     """The configs[4] workload both arms measure (identical dicts)."""
-    return {"workload": "configs[4]: 64 independent sequences x N=32768, one selected-KV layer each, the 8 KV "
-                        "heads split over the GPUs; a layer-step = one sequence's layer",
+    kv = args.batch * args.tokens * 8 * 128 * 2 * 2  # K and V, F16, every sequence
+    l2 = (f"K/V shards {kv / 1e9:.1f} GB >> 126 MB L2, no flush" if kv > 4 * 126e6 else
+          f"K/V {kv / 1e6:.0f} MB, within 4x the 126 MB L2 and no flush: not an HBM figure")
+    return {"workload": f"configs[4]: {args.batch} independent sequences x N={args.tokens}, one selected-KV layer "
+                        "each, the 8 KV heads split over the GPUs; a layer-step = one sequence's layer",
             "sequences": args.batch, "tokens": args.tokens, "alpha": args.alpha, "cap_ratio": 0.2,
-            "kv_heads_per_gpu": 8 // world, "l2": "K/V shards 8.6 GB >> 126 MB L2, no flush"}
+            "kv_heads_per_gpu": 8 // world, "l2": l2}
 
 
 def shard_cpu_sequences(tokens, count, threads):
