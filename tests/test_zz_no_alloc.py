@@ -75,3 +75,27 @@ def test_matches_workspace_entry_on_two_calls_in_a_row():
         w, g = want.cpu().numpy().astype(np.float64), got.cpu().numpy().astype(np.float64)
         assert np.all(np.isfinite(g))
         assert rel_err(g, w) <= TOL, (seed, count)
+
+
+@pytest.mark.gpu
+def test_calls_leave_device_memory_unchanged():
+    """The promise itself: once the first call has resolved the scratch
+    address, further calls take no device memory (a cudaMalloc of any size
+    moves the device's free-memory figure by at least one 2 MiB page)."""
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    lib = _lib()
+    s = torch.cuda.current_stream().cuda_stream
+    q, k, v, sizes = _case(torch, 13, MAX_SLOTS)
+    out = torch.empty(4096, dtype=torch.float32, device="cuda")
+    call = lambda: lib.hsb_attention_packed_noalloc(q.data_ptr(), k.data_ptr(), v.data_ptr(), MAX_SLOTS,  # noqa: E731
+                                                    None, 0, sizes.data_ptr(), 1, out.data_ptr(), s)
+    assert call() == 0, lib.hsb_last_error()  # set-up: the scratch address of this context
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        assert call() == 0, lib.hsb_last_error()
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free_before
+    assert np.all(np.isfinite(out.cpu().numpy()))
