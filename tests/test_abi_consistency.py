@@ -5,9 +5,9 @@ ctypes does not read the header: an argtypes list with one entry too few, a
 size_t bound as int, or a float bound as double passes garbage to the
 library without any error.  So the header's prototypes are parsed here and
 compared with hillserve_b200/_capi.py's table -- count, and the C type class
-of every parameter and of the return value.  The C snippets of INTEGRATION.md
-are checked the same way for their argument counts, so the integration guide
-cannot drift from the header either.  CPU only."""
+of every parameter and of the return value.  The C snippets of the
+integration guide are checked the same way for their argument counts, so
+the guide cannot drift from the header either.  CPU only."""
 from __future__ import annotations
 
 import ctypes as C
@@ -139,11 +139,11 @@ def test_integration_snippets_match_header():
 
 
 def test_names_in_docs_exist():
-    """Every hsb_ function the guide and the design notes name is declared."""
+    """Every hsb_ function the integration guide and the README name is declared."""
     protos = header_prototypes()
     headers = "".join((ROOT / "include" / h).read_text() for h in ("hsb.h", "hsb_compat.h"))
     libraries = {"hsb_compat"}  # the C++ drop-in's link target (libhsb_compat.so)
-    for doc in ("INTEGRATION.md", "DESIGN.md", "README.md"):
+    for doc in ("INTEGRATION.md", "README.md"):
         for name in set(re.findall(r"`(hsb_\w+)", (ROOT / doc).read_text())):
             if name.endswith("_"):  # a family, written `hsb_history_*`
                 assert any(p.startswith(name) for p in protos), (doc, name)
