@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cfenv>
 #include <cmath>
 #include <cstdio>
@@ -33,6 +34,9 @@ cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
 std::mutex g_dev_mutex;
 DeviceInfo g_devices[64];
+// Set (release) once a device's entry is filled; a reader that sees it set
+// (acquire) sees the whole entry.
+std::atomic<bool> g_device_ready[64];
 }  // namespace
 
 int record_error(int status, const char* message) { return fail(status, message); }
@@ -43,9 +47,9 @@ const DeviceInfo& device_info() {
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
     DeviceInfo& d = g_devices[dev];
-    if (d.ordinal != dev) {
+    if (!g_device_ready[dev].load(std::memory_order_acquire)) {
         std::lock_guard<std::mutex> lock(g_dev_mutex);
-        if (d.ordinal != dev) {
+        if (!g_device_ready[dev].load(std::memory_order_relaxed)) {
             cudaDeviceProp prop{};
             if (cudaGetDeviceProperties(&prop, dev) == cudaSuccess) {
                 d.sms = prop.multiProcessorCount;
@@ -56,6 +60,7 @@ const DeviceInfo& device_info() {
                 d.sms = 148;
             }
             d.ordinal = dev;
+            g_device_ready[dev].store(true, std::memory_order_release);
         }
     }
     return d;
