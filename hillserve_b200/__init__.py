@@ -68,7 +68,14 @@ def _stream(stream=None):
 
 
 def _ptr(t) -> C.c_void_p:
-    return C.c_void_p(0 if t is None else t.data_ptr())
+    """The address a kernel will read or write.  Device tensors and pinned
+    host tensors (mapped into the GPU's address space) qualify; a pageable
+    host tensor would make the kernel fault, so it is refused here."""
+    if t is None:
+        return C.c_void_p(0)
+    if t.device.type == "cpu" and not t.is_pinned():
+        raise InvalidArgument(10, "a pageable host tensor cannot be read by the GPU: pass a device or pinned tensor")
+    return C.c_void_p(t.data_ptr())
 
 
 def _status_buffer(device):

@@ -175,3 +175,15 @@ def test_workspace_queries_are_pure(lib):
 def test_ctypes_byref_is_accepted_for_pointer_arguments():
     x = C.c_uint32(0)
     assert C.c_void_p.from_param(C.byref(x)) is not None
+
+
+def test_python_mirror_refuses_pageable_host_tensors():
+    """A kernel given a pageable host address faults the GPU; the Python
+    mirror refuses such a tensor before any call reaches the library."""
+    torch = pytest.importorskip("torch")
+    import hillserve_b200 as hsb
+
+    q = torch.zeros(4096, dtype=torch.int16)  # pageable host memory
+    with pytest.raises(hsb.InvalidArgument, match="pageable host tensor"):
+        hsb.score_pipeline_v3(q, q, 64, out=q)
+    assert hsb._ptr(None).value is None
