@@ -8,6 +8,13 @@
 #include <cstddef>
 #include <cstdint>
 #include <vector>
+// The reference header defines these functions inline and so brings in the
+// following standard headers; translation units written against it may rely
+// on them.
+#include <algorithm>
+#include <cstring>
+#include <limits>
+#include <stdexcept>
 
 namespace hillserve {
 std::vector<std::uint64_t> gqa_physical_union(const std::vector<std::vector<std::uint64_t>>& ids,
