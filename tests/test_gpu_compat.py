@@ -35,3 +35,19 @@ def test_reference_interfaces_on_b200(cuda):
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr + r.stdout
     assert '"status":"passed"' in r.stdout
+
+
+@pytest.mark.parametrize("program", ["full_gqa_cpu_tests", "gqa_pack_tests"])
+def test_reference_unit_test_program_on_b200(cuda, program):
+    """The reference's own tests/full_gqa_cpu_tests.cpp and
+    tests/gqa_pack_tests.cpp, compiled unmodified against the drop-in headers
+    and linked to libhsb_compat (oracle/Makefile): the scorer's bit-exact
+    checks against the test's independent oracle (ragged and non-contiguous
+    views, subnormals, overflow, signed zero, the rounding-mode rejection) and
+    the union / pack layout checks, all run on the library's kernels."""
+    exe = ROOT / "oracle" / "_ref" / f"{program}_b200"
+    if not exe.exists():
+        pytest.skip("built only where the reference sources were present")
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr + r.stdout
+    assert "passed" in r.stdout
