@@ -24,9 +24,9 @@ def _strip_comments(text: str) -> str:
     return re.sub(r"//[^\n]*", " ", text)
 
 
-def header_prototypes() -> dict[str, tuple[str, list[str]]]:
+def header_prototypes(header: str = "hsb.h") -> dict[str, tuple[str, list[str]]]:
     """name -> (return type, [parameter declarations]) of every hsb_ function."""
-    text = _strip_comments((ROOT / "include" / "hsb.h").read_text())
+    text = _strip_comments((ROOT / "include" / header).read_text())
     text = re.sub(r"^\s*#[^\n]*", " ", text, flags=re.M)
     out: dict[str, tuple[str, list[str]]] = {}
     for m in re.finditer(r"([A-Za-z_][\w\s\*]*?)\b(hsb_\w+)\s*\(([^;{}]*?)\)\s*;", text):
@@ -149,3 +149,27 @@ def test_names_in_docs_exist():
                 assert any(p.startswith(name) for p in protos), (doc, name)
                 continue
             assert name in protos or name in libraries or re.search(rf"\b{name}\b", headers), (doc, name)
+
+
+def test_integration_ctypes_snippets_match_headers():
+    """The guide's ctypes examples declare argtypes / restype that agree with
+    include/hsb.h and include/hsb_compat.h (char* may be bound as c_char_p)."""
+    protos = {**header_prototypes("hsb.h"), **header_prototypes("hsb_compat.h")}
+    text = (ROOT / "INTEGRATION.md").read_text()
+    blocks = re.findall(r"```python\n(.*?)```", text, flags=re.S)
+    seen = 0
+    for block in blocks:
+        for name, expr in re.findall(r"\w+\.(hsb_\w+)\.argtypes\s*=\s*(.+)", block):
+            argtypes = eval(expr, {"C": C})  # noqa: S307 - the guide's own list expression
+            params = protos[name][1]
+            assert len(argtypes) == len(params), (name, len(argtypes), params)
+            for decl, t in zip(params, argtypes):
+                want, got = c_class(decl), ctypes_class(t)
+                assert _same(want, got) or (want == "char_p" and got == "pointer") or \
+                    (want == "pointer" and got == "char_p" and "char" in decl), (name, decl, t)
+            seen += 1
+        for name, expr in re.findall(r"\w+\.(hsb_\w+)\.restype\s*=\s*(.+)", block):
+            restype = eval(expr, {"C": C})  # noqa: S307
+            want = c_class(protos[name][0])
+            assert _same(want, ctypes_class(restype)), (name, protos[name][0], restype)
+    assert seen >= 3
