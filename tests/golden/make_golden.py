@@ -3,7 +3,7 @@ own CPU code (oracle/_ref/libhs_ref.so, compiled from the HillServe sources by
 oracle/Makefile) on seeded inputs.  Run here, where the reference sources
 exist:
 
-    make -C oracle && python tests/golden/make_golden.py [--only h2o|records|history|runtime]
+    make -C oracle && python tests/golden/make_golden.py [--only h2o|records|history|runtime|host_checks]
 
 Inputs are regenerated bit-exactly from their seeds by tests/inputs.py, so
 the fixtures hold only input digests and the reference's outputs.
@@ -198,8 +198,47 @@ def runtime_vectors() -> None:
     np.savez_compressed(OUT / "runtime_decode.npz", **fields)
 
 
+REFERENCE = Path(__import__("os").environ.get("HILLSERVE_REFERENCE", "/root/reference"))
+HOST_CHECKS = ROOT / "tests" / "cpp" / "host_checks.cpp"
+
+
+def build_host_checks(out: Path, against: str) -> Path:
+    """tests/cpp/host_checks.cpp built against the reference's own headers and
+    sources (against="reference") or against the drop-in headers and
+    libhsb_compat (against="dropin")."""
+    import subprocess
+
+    cmd = ["g++", "-std=c++17", "-O1", "-ffp-contract=off", "-pthread"]
+    if against == "reference":
+        srcs = [REFERENCE / f for f in ("policy/full_gqa_cpu.cpp", "policy/gqa_policy.cpp", "policy/host_policy.cpp",
+                                        "smartssd/adapter.cpp")]
+        cmd += [f"-I{REFERENCE}", str(HOST_CHECKS), *map(str, srcs)]
+    else:
+        lib = ROOT / "hillserve_b200" / "_lib"
+        cmd += [f"-I{ROOT / 'hillserve_b200' / 'compat'}", f"-I{ROOT / 'include'}", str(HOST_CHECKS), f"-L{lib}",
+                "-lhsb_compat", "-lhsb", f"-Wl,-rpath,{lib}"]
+    subprocess.run([*cmd, "-o", str(out)], check=True)
+    return out
+
+
+def host_checks() -> None:
+    """The reference's exception class and message for each rejected call of
+    tests/cpp/host_checks.cpp (host_checks_reference.txt)."""
+    import subprocess
+    import tempfile
+
+    with tempfile.TemporaryDirectory() as d:
+        exe = build_host_checks(Path(d) / "host_checks_ref", "reference")
+        text = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout
+    (OUT / "host_checks_reference.txt").write_text(text)
+
+
 def main() -> None:
     assert ob.reference_available(), "build oracle/_ref first (make -C oracle)"
+    if sys.argv[1:] == ["--only", "host_checks"]:
+        host_checks()
+        print("host-check fixture written to", OUT)
+        return
     if sys.argv[1:] == ["--only", "runtime"]:
         runtime_vectors()
         print("runtime fixture written to", OUT)
@@ -218,6 +257,7 @@ def main() -> None:
         return
     records_vectors()
     history_plans()
+    host_checks()
     if ob.ref_runtime_available():
         runtime_vectors()
     # ---- 0. H2O group sums through the reference's CPU policy
