@@ -3,7 +3,8 @@
 Its output must equal hsb_attention_packed's (same kernel, scratch in a static
 device array instead of a caller workspace) within the attention tolerance,
 on two calls in a row with different inputs -- the second call reuses the
-scratch the first one left behind.  Counts beyond the static scratch's slot
+scratch the first one left behind -- and the oracle's double-precision
+attention over the same live slots.  Counts beyond the static scratch's slot
 limit are rejected before any GPU work."""
 from __future__ import annotations
 
@@ -52,7 +53,7 @@ def test_rejects_counts_beyond_the_static_scratch():
 
 
 @pytest.mark.gpu
-def test_matches_workspace_entry_on_two_calls_in_a_row():
+def test_matches_workspace_entry_on_two_calls_in_a_row(ob):
     torch = pytest.importorskip("torch")
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
@@ -75,6 +76,10 @@ def test_matches_workspace_entry_on_two_calls_in_a_row():
         w, g = want.cpu().numpy().astype(np.float64), got.cpu().numpy().astype(np.float64)
         assert np.all(np.isfinite(g))
         assert rel_err(g, w) <= TOL, (seed, count)
+        # and the oracle's double-precision attention over the same live slots
+        exact = ob.attention_compact(k.cpu().numpy().view(np.uint16), v.cpu().numpy().view(np.uint16), count,
+                                     sizes.cpu().numpy().astype(np.uint32), q.cpu().numpy()).reshape(-1)
+        assert rel_err(g, exact) <= TOL, (seed, count)
 
 
 @pytest.mark.gpu
