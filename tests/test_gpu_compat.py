@@ -37,14 +37,22 @@ def test_reference_interfaces_on_b200(cuda):
     assert '"status":"passed"' in r.stdout
 
 
-@pytest.mark.parametrize("program", ["full_gqa_cpu_tests", "gqa_pack_tests"])
+@pytest.mark.parametrize("program", ["full_gqa_cpu_tests", "gqa_pack_tests", "quality_alpha_tests",
+                                     "full_gqa_prefetch_tests"])
 def test_reference_unit_test_program_on_b200(cuda, program):
-    """The reference's own tests/full_gqa_cpu_tests.cpp and
-    tests/gqa_pack_tests.cpp, compiled unmodified against the drop-in headers
-    and linked to libhsb_compat (oracle/Makefile): the scorer's bit-exact
-    checks against the test's independent oracle (ragged and non-contiguous
-    views, subnormals, overflow, signed zero, the rounding-mode rejection) and
-    the union / pack layout checks, all run on the library's kernels."""
+    """The reference's own test programs, compiled unmodified against the
+    drop-in headers and linked to libhsb_compat (oracle/Makefile), run on the
+    library's kernels:
+
+    - tests/full_gqa_cpu_tests.cpp: the scorer, bit-exact against the test's
+      independent oracle (ragged and non-contiguous views, subnormals,
+      overflow, signed zero, the rounding-mode rejection);
+    - tests/gqa_pack_tests.cpp: union and pack layout;
+    - tests/quality_alpha_tests.cpp and tests/full_gqa_prefetch_tests.cpp:
+      the reference's FullGqaRuntimePolicy (built from its own sources) with
+      its scorer and selector taken from the drop-in -- exact k and counts per
+      alpha, the live runtime against its scalar oracle, and the payload
+      cover containing the final selections."""
     exe = ROOT / "oracle" / "_ref" / f"{program}_b200"
     if not exe.exists():
         pytest.skip("built only where the reference sources were present")
